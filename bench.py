@@ -1,0 +1,481 @@
+"""Benchmark: soft Smith-Waterman forward + backward GCUPS on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...
+
+Metric: GCUPS = valid DP cells per second for one forward that
+produces value + marginals plus ``value.sum().backward()``.  Default workload is
+soft_sw, fp32 scores [256, 512, 512] ~ N(0,1) (seed 0), gap -1,
+temperature 1, no masks.  Weak scaling: every rank runs its own 256-problem batch
+(seeded from the global seed and its rank) and the per-sequence values are
+gathered with NCCL every step -- the only collective on the path.
+
+``value`` is measured with the inputs resident in HBM (scores 268 MB > L2 126 MB,
+so every step streams from DRAM; no extra L2 flush).  ``e2e`` is the same step
+through the public API with the scores copied from pinned host memory at the
+start of every step and the values copied back at the end.
+``--impl reference`` times the reference's own CPU kernels (oracle/_ref, built
+from the reference sources) on the host cores, on the same config.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "soft_sw fwd+bwd GCUPS (DP cells/s) at 1/2/4/8 B200; % of HBM/MUFU roofline"
+
+# BASELINE.json configs (C1..C5)
+CONFIGS = {
+    "c1": dict(family="linear", B=2, L1=100, L2=120, gap=-1.0, T=1.0, scale=1.0, lengths=False,
+               dtype="f32", desc="soft_sw [2,100,120] fp32, gap -1, T 1"),
+    "c2": dict(family="linear", B=256, L1=512, L2=512, gap=-1.0, T=1.0, scale=1.0, lengths=False,
+               dtype="f32", desc="soft_sw [256,512,512] fp32, gap -1, T 1, no masks"),
+    "c3": dict(family="linear", B=1024, L1=512, L2=512, gap=-0.5, T=0.5, scale=1.0, lengths=True,
+               dtype="f32", desc="soft_sw [1024,512,512] fp32, lengths U[64,512] (seed 1), gap -0.5, T 0.5"),
+    "c4": dict(family="affine", B=64, L1=1024, L2=1024, gap=(-2.0, -0.5), T=1.0, scale=1.0, lengths=False,
+               dtype="bf16", desc="soft_sw_affine [64,1024,1024] bf16 -> fp32, open -2, ext -0.5, T 1"),
+    "c5": dict(family="linear", B=32, L1=4096, L2=4096, gap=-1.0, T=1.0, scale=0.5, lengths=False,
+               dtype="f32", desc="soft_sw [32,4096,4096] fp32 0.5*N(0,1), gap -1, T 1"),
+}
+
+# Algorithmic cost per valid cell (fixed convention):
+#   fused DP kernel (value + marginals): read scores 4 B (bf16: 2 B) + write marginals 4 B;
+#     MUFU 10 (forward LSE 4 ex2 + 1 lg2, reverse 1 ex2 beta_init + 4 ex2 weights);
+#     affine: 22 MUFU.
+#   value backward kernel: read marginals 4 B + write grad 4 B.
+MUFU_PER_CELL = {"linear": 10, "affine": 22}
+MUFU_PER_SM_CLK = 16
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), float(d.get("sm_max_mhz", 1965.0)), "measured"
+    except Exception:
+        return 6650.0, 1965.0, "fallback"
+
+
+# ----------------------------------------------------------------------------
+# clocks sampler (nvidia-smi during the timed region)
+# ----------------------------------------------------------------------------
+class ClockSampler:
+    """nvidia-smi sampler: lines are timestamped on arrival by a reader thread;
+    the summary keeps the samples taken within 0.15 s of the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.rows = []
+        self.t0 = self.t1 = None
+
+    def start(self):
+        import threading
+
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+            return
+
+        def reader():
+            for line in self.proc.stdout:
+                self.rows.append((time.monotonic(), [p.strip() for p in line.split(",")]))
+
+        self.thread = threading.Thread(target=reader, daemon=True)
+        self.thread.start()
+        t_end = time.monotonic() + 5.0
+        while not self.rows and time.monotonic() < t_end:   # wait until it is emitting
+            time.sleep(0.02)
+
+    def mark_start(self):
+        self.t0 = time.monotonic()
+
+    def mark_end(self):
+        self.t1 = time.monotonic()
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.2)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        t0 = (self.t0 or 0) - 0.15
+        t1 = (self.t1 or time.monotonic()) + 0.15
+        rows = [r for (t, r) in self.rows if t0 <= t <= t1 and len(r) >= 9]
+        if not rows:
+            return None
+
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+        sm = [v for v in (num(r[1]) for r in rows) if v is not None]
+        mx = [v for v in (num(r[2]) for r in rows) if v is not None]
+        pw = [v for v in (num(r[3]) for r in rows) if v is not None]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[k] for r in rows for k in range(4) if r[5 + k].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "power_w_max": max(pw) if pw else None, "reasons": reasons, "samples": len(rows)}
+
+
+# ----------------------------------------------------------------------------
+# inputs
+# ----------------------------------------------------------------------------
+def make_inputs(cfg, rank: int):
+    import torch
+
+    g = torch.Generator().manual_seed(0 + 7919 * rank)
+    s = torch.randn(cfg["B"], cfg["L1"], cfg["L2"], generator=g) * cfg["scale"]
+    if cfg["dtype"] == "bf16":
+        s = s.to(torch.bfloat16)
+    lengths = None
+    if cfg["lengths"]:
+        g1 = torch.Generator().manual_seed(1 + 7919 * rank)
+        lengths = torch.randint(64, 513, (cfg["B"], 2), generator=g1, dtype=torch.int32)
+    return s, lengths
+
+
+def valid_cells(cfg, lengths) -> int:
+    if lengths is None:
+        return cfg["B"] * cfg["L1"] * cfg["L2"]
+    l = lengths.to(dtype=__import__("torch").int64)
+    return int((l[:, 0] * l[:, 1]).sum().item())
+
+
+# ----------------------------------------------------------------------------
+# our implementation
+# ----------------------------------------------------------------------------
+def run_ours(args, cfg):
+    import torch
+    import torch.distributed as dist
+
+    import d2p_b200 as d2p
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+
+    s_host, lengths = make_inputs(cfg, rank)
+    cells = valid_cells(cfg, lengths)
+    fam = cfg["family"]
+    gap = cfg["gap"]
+    T = cfg["T"]
+    s_dev = s_host.to(dev).requires_grad_(True)
+    len_dev = lengths.to(dev) if lengths is not None else None
+    vals_all = torch.empty(world * cfg["B"], device=dev)
+
+    def fwd(scores):
+        if fam == "linear":
+            return d2p.soft_sw(scores, gap=gap, temperature=T, lengths=len_dev)
+        return d2p.soft_sw_affine(scores, gap_open=gap[0], gap_ext=gap[1], temperature=T, lengths=len_dev)
+
+    def step(scores):
+        res = fwd(scores)
+        (grad,) = torch.autograd.grad(res.value.sum(), scores)
+        v = res.value.detach()
+        if world > 1:
+            dist.all_gather_into_tensor(vals_all, v)
+        return v, grad
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+            torch.cuda.synchronize()
+
+    # ---------------- device-resident timing ----------------
+    for _ in range(args.warmup):
+        step(s_dev)
+    barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    clocks.mark_start()
+    e0.record()
+    for _ in range(args.steps):
+        step(s_dev)
+    e1.record()
+    barrier()
+    clocks.mark_end()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+
+    # ---------------- dominant kernel alone (same stream, CUDA events) ----------------
+    nk = max(3, args.steps)
+    with torch.no_grad():
+        def kern():
+            if fam == "linear":
+                return torch.ops.d2p.soft_sw_with_grads(s_dev, gap, T, len_dev)
+            return torch.ops.d2p.soft_sw_affine_with_grads(s_dev, gap[0], gap[1], T, len_dev)
+        for _ in range(2):
+            kern()
+        torch.cuda.synchronize()
+        k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        k0.record()
+        for _ in range(nk):
+            kern()
+        k1.record()
+        torch.cuda.synchronize()
+        k_ms = k0.elapsed_time(k1) / nk
+
+    # ---------------- end to end from pinned host memory ----------------
+    s_pin = s_host.pin_memory()
+    v_host = torch.empty(cfg["B"], pin_memory=True)
+    buf = torch.empty_like(s_dev, requires_grad=False)
+
+    def e2e_step():
+        buf.copy_(s_pin, non_blocking=True)
+        x = buf.requires_grad_(True)
+        v, grad = step(x)
+        v_host.copy_(v, non_blocking=True)
+        x.requires_grad_(False)
+        return grad
+
+    for _ in range(max(1, min(args.warmup, 2))):
+        e2e_step()
+    barrier()
+    x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    x0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    x1.record()
+    barrier()
+    e2e_ms = x0.elapsed_time(x1) / args.steps
+    te = torch.tensor([e2e_ms], device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_ms = float(te.item())
+
+    total_cells = cells * world
+    gcups = total_cells / (ms_max * 1e-3) / 1e9
+    e2e_gcups = total_cells / (e2e_ms * 1e-3) / 1e9
+
+    hbm_gbs, sm_max_mhz, peak_src = load_peaks()
+    sm_clock_mhz = (clk or {}).get("sm_mhz") or sm_max_mhz
+    sm_count = torch.cuda.get_device_properties(dev).multi_processor_count
+    score_bytes = 2 if cfg["dtype"] == "bf16" else 4
+    padded = cfg["B"] * cfg["L1"] * cfg["L2"]
+    # fused DP kernel algorithmic traffic: scores read + marginals write (padding
+    # cells of the marginals are zero-filled: 4 B each)
+    k_bytes = cells * score_bytes + padded * 4
+    k_mufu = cells * MUFU_PER_CELL[fam]
+    mufu_peak = sm_count * MUFU_PER_SM_CLK * sm_max_mhz * 1e6  # ops/s at max SM clock
+    t_hbm = k_bytes / (hbm_gbs * 1e9)
+    t_mufu = k_mufu / mufu_peak
+    bound = "mufu" if t_mufu >= t_hbm else "hbm"
+    k_s = k_ms * 1e-3
+    if bound == "mufu":
+        achieved, peak, unit = k_mufu / k_s / 1e12, mufu_peak / 1e12, "Tops/s (MUFU)"
+    else:
+        achieved, peak, unit = k_bytes / k_s / 1e9, hbm_gbs, "GB/s"
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", f"traffic_{args.config}.json")
+    if os.path.exists(tp):
+        try:
+            traffic = json.load(open(tp)).get("bytes_per_launch")
+        except Exception:
+            traffic = None
+    roofline = {
+        "bound": bound, "achieved": round(achieved, 4), "peak": round(peak, 4), "unit": unit,
+        "frac": round(achieved / peak, 4), "traffic": traffic,
+        "kernel": "sw fused value+marginals (d2p_sw_forward_backward)",
+        "kernel_ms": round(k_ms, 4), "time_bound_ms": round(max(t_hbm, t_mufu) * 1e3, 4),
+        "hbm_gbs_achieved": round(k_bytes / k_s / 1e9, 2), "hbm_peak_gbs": hbm_gbs,
+        "mufu_tops_achieved": round(k_mufu / k_s / 1e12, 3), "mufu_peak_tops": round(mufu_peak / 1e12, 3),
+        "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs; MUFU = {sm_count} SM x 16/clk x {sm_max_mhz:.0f} MHz)",
+        "step_frac": round((max(t_hbm, t_mufu) + (8.0 * padded) / (hbm_gbs * 1e9)) / (ms_max * 1e-3), 4),
+    }
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(cfg, args.cpu_seconds)
+
+    if world > 1:
+        dist.barrier()
+    if rank == 0:
+        h2d = s_host.numel() * s_host.element_size()
+        line = {
+            "metric": METRIC, "value": round(gcups, 3), "unit": "GCUPS", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_max, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32" if cfg["dtype"] == "f32" else "bf16-in/f32",
+            "data": "synthetic (seeded N(0,1) scores, BASELINE shapes)",
+            "config": {"workload": f"{args.config}: {cfg['desc']}", "per_rank_batch": cfg["B"],
+                       "global_batch": cfg["B"] * world, "L1": cfg["L1"], "L2": cfg["L2"],
+                       "valid_cells_per_rank": cells, "step": "forward (value+marginals) + value.sum().backward()",
+                       "l2": "inputs larger than L2 (scores+marginals stream from DRAM every step)",
+                       "parallelism": f"batch x{world} (one process per GPU), NCCL all_gather of values"},
+            "e2e": {"value": round(e2e_gcups, 3), "unit": "GCUPS", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": cfg["B"] * 4, "ms_per_step": round(e2e_ms, 4)},
+            "gpu_launches": args.steps * 2,
+            "roofline": roofline,
+            "clocks": clk,
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+# ----------------------------------------------------------------------------
+# reference CPU (oracle/_ref = the reference's own CPU kernels)
+# ----------------------------------------------------------------------------
+def _ref_step(cfg, s_np, len_np):
+    import oracle
+
+    if cfg["family"] == "linear":
+        r = oracle.sw_linear(s_np, len_np, cfg["gap"], cfg["T"], "ref")
+    else:
+        r = oracle.sw_affine(s_np, len_np, cfg["gap"][0], cfg["gap"][1], cfg["T"], "ref")
+    # value.sum().backward(): grad = 1 * marginals (the reference recomputes the
+    # reverse DP here; timing the elementwise product is the cheaper variant)
+    _ = r["marginals"] * 1.0
+    return r
+
+
+def cpu_baseline(cfg, seconds: float, cores=None):
+    import numpy as np
+    import oracle
+
+    kind = "reference" if oracle.ref_available() else "port"
+    ncores = cores or os.cpu_count() or 1
+    oracle.set_threads(ncores)
+    s_host, lengths = make_inputs(cfg, 0)
+    s_np = s_host.float().numpy()
+    len_np = lengths.numpy() if lengths is not None else None
+    impl = "ref" if kind == "reference" else "f32"
+    # bounded sample: grow the number of problems until one call takes >= ~0.5 s
+    nb = min(cfg["B"], max(1, ncores))
+    while True:
+        sub = s_np[:nb]
+        ln = len_np[:nb] if len_np is not None else None
+        t0 = time.perf_counter()
+        if impl == "ref":
+            _ref_step(cfg, sub, ln)
+        else:
+            oracle.sw_linear(sub, ln, cfg["gap"], cfg["T"], "f32")
+        dt = time.perf_counter() - t0
+        if dt >= 0.5 or nb >= cfg["B"]:
+            break
+        nb = min(cfg["B"], nb * 2)
+    reps = max(1, int(seconds / max(dt, 1e-3)))
+    best = dt
+    for _ in range(reps - 1):
+        t0 = time.perf_counter()
+        if impl == "ref":
+            _ref_step(cfg, sub, ln)
+        else:
+            oracle.sw_linear(sub, ln, cfg["gap"], cfg["T"], "f32")
+        best = min(best, time.perf_counter() - t0)
+    c = int(np.sum(ln[:, 0].astype(np.int64) * ln[:, 1])) if ln is not None else nb * cfg["L1"] * cfg["L2"]
+    return {"value": round(c / best / 1e9, 5), "unit": "GCUPS", "cores": ncores, "kind": kind,
+            "sample": f"{nb} problems of {cfg['L1']}x{cfg['L2']} ({args_config_name(cfg)}), fwd+bwd, best of {reps}"}
+
+
+def args_config_name(cfg):
+    for k, v in CONFIGS.items():
+        if v is cfg:
+            return k
+    return "custom"
+
+
+def run_reference(args, cfg):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import numpy as np
+    import oracle
+
+    kind = "reference" if oracle.ref_available() else "port"
+    ncores = os.cpu_count() or 1
+    oracle.set_threads(ncores)
+    s_host, lengths = make_inputs(cfg, 0)
+    s_np = s_host.float().numpy()
+    len_np = lengths.numpy() if lengths is not None else None
+    # bounded per-step sample sized so the whole run stays within a few minutes
+    nb = min(cfg["B"], max(1, ncores))
+    budget = args.ref_step_seconds
+    while True:
+        t0 = time.perf_counter()
+        _ref_step(cfg, s_np[:nb], len_np[:nb] if len_np is not None else None)
+        dt = time.perf_counter() - t0
+        if dt * 2 > budget or nb >= cfg["B"]:
+            break
+        nb = min(cfg["B"], nb * 2)
+    sub = s_np[:nb]
+    ln = len_np[:nb] if len_np is not None else None
+    for _ in range(args.warmup):
+        _ref_step(cfg, sub, ln)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        _ref_step(cfg, sub, ln)
+    dt = (time.perf_counter() - t0) / args.steps
+    c = int(np.sum(ln[:, 0].astype(np.int64) * ln[:, 1])) if ln is not None else nb * cfg["L1"] * cfg["L2"]
+    g = c / dt / 1e9
+    sample = f"{nb} of {cfg['B']} problems of {cfg['L1']}x{cfg['L2']} per step, fwd+bwd"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(g, 5), "unit": "GCUPS", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1))",
+        "config": {"workload": f"{args.config}: {cfg['desc']}", "sample": sample},
+        "cpu_baseline": {"value": round(g, 5), "unit": "GCUPS", "cores": ncores, "kind": kind, "sample": sample},
+        "e2e": {"value": round(g, 5), "unit": "GCUPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=8.0)
+    ap.add_argument("--ref-step-seconds", type=float, default=6.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    cfg = CONFIGS[args.config]
+    if args.impl == "reference":
+        run_reference(args, cfg)
+    else:
+        run_ours(args, cfg)
+
+
+if __name__ == "__main__":
+    main()

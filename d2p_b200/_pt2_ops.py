@@ -1,0 +1,294 @@
+"""PT2-safe custom ops (``d2p_py::*``) used while compiling or on fake tensors.
+
+Mirrors the soft Smith-Waterman part of d2p/_pt2_ops.py:72-487: each op wraps
+the dispatcher op, carries a fake implementation, and the differentiable ones
+(``soft_sw``, ``soft_sw_float``, affine analogues) register an autograd formula
+built from the saved marginals (value branch) and ``*_backward_full`` (marginal
+branch).
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+from torch.library import custom_op
+
+from ._pt2_utils import _is_fake_tensor
+
+
+def _scalar(value, default: float = 0.0) -> float:
+    if isinstance(value, (int, float)):
+        return float(value)
+    if isinstance(value, torch.Tensor):
+        if _is_fake_tensor(value):
+            return default
+        return float(value.item())
+    return float(value)
+
+
+def _add(a, b):
+    if a is None:
+        return b
+    if b is None:
+        return a
+    return a + b
+
+
+def _expand_batch(g: Optional[torch.Tensor], marg: torch.Tensor):
+    if g is None:
+        return None
+    return g.view([marg.size(0)] + [1] * (marg.dim() - 1)) * marg
+
+
+def _batch_dot(g: Optional[torch.Tensor], per_batch: torch.Tensor):
+    if g is None:
+        return None
+    return (g * per_batch).sum().reshape([1])
+
+
+def _like(scores, *kinds):
+    B, L1, L2 = scores.shape
+    out = []
+    for k in kinds:
+        shape = {"B": [B], "P": [B, L1, L2], "1": [1]}[k]
+        out.append(scores.new_empty(shape, dtype=torch.float32))
+    return tuple(out) if len(out) > 1 else out[0]
+
+
+# --------------------------------------------------------------------------- linear
+@custom_op("d2p_py::soft_sw_with_grads", mutates_args=())
+def soft_sw_with_grads(scores: torch.Tensor, gap: float, temperature: float,
+                       lengths: Optional[torch.Tensor]) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    v, m, gg, gt = torch.ops.d2p.soft_sw_with_grads(scores, gap, temperature, lengths)
+    return v, m, gg, gt
+
+
+@soft_sw_with_grads.register_fake
+def _(scores, gap, temperature, lengths):
+    return _like(scores, "B", "P", "B", "B")
+
+
+@custom_op("d2p_py::soft_sw_hvp", mutates_args=())
+def soft_sw_hvp(scores: torch.Tensor, tangent: torch.Tensor, gap: float, temperature: float,
+                lengths: Optional[torch.Tensor]) -> torch.Tensor:
+    return torch.ops.d2p.soft_sw_hvp(scores, tangent, gap, temperature, lengths)
+
+
+@soft_sw_hvp.register_fake
+def _(scores, tangent, gap, temperature, lengths):
+    return _like(scores, "P")
+
+
+@custom_op("d2p_py::soft_sw_param_jacobian", mutates_args=())
+def soft_sw_param_jacobian(scores: torch.Tensor, param_type: int, gap: float, temperature: float,
+                           lengths: Optional[torch.Tensor]) -> torch.Tensor:
+    return torch.ops.d2p.soft_sw_param_jacobian(scores, param_type, gap, temperature, lengths)
+
+
+@soft_sw_param_jacobian.register_fake
+def _(scores, param_type, gap, temperature, lengths):
+    return _like(scores, "P")
+
+
+@custom_op("d2p_py::soft_sw_backward_full", mutates_args=())
+def soft_sw_backward_full(scores: torch.Tensor, grad_alignment: torch.Tensor, gap: float,
+                          temperature: float, lengths: Optional[torch.Tensor]) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    a, b, c = torch.ops.d2p.soft_sw_backward_full(scores, grad_alignment, gap, temperature, lengths)
+    return a, b, c
+
+
+@soft_sw_backward_full.register_fake
+def _(scores, grad_alignment, gap, temperature, lengths):
+    return _like(scores, "P", "1", "1")
+
+
+@custom_op("d2p_py::soft_sw", mutates_args=())
+def soft_sw(scores: torch.Tensor, gap: torch.Tensor, temperature: torch.Tensor,
+            lengths: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    v, m = torch.ops.d2p.soft_sw(scores, gap, temperature, lengths)
+    return v, m
+
+
+@soft_sw.register_fake
+def _(scores, gap, temperature, lengths):
+    return _like(scores, "B", "P")
+
+
+def _soft_sw_setup(ctx, inputs, output):
+    scores, gap, temperature, lengths = inputs
+    ctx.save_for_backward(scores, output[1])
+    ctx.gap = _scalar(gap)
+    ctx.temperature = _scalar(temperature)
+    ctx.lengths = lengths
+
+
+def _soft_sw_backward(ctx, grad_value, grad_marg):
+    scores, marg = ctx.saved_tensors
+    grad_scores = _expand_batch(grad_value, marg)
+    need_gap, need_t = ctx.needs_input_grad[1], ctx.needs_input_grad[2]
+    g_gap = g_t = None
+    if grad_value is not None and (need_gap or need_t):
+        _, _, dgap, dt = soft_sw_with_grads(scores, ctx.gap, ctx.temperature, ctx.lengths)
+        g_gap = _batch_dot(grad_value, dgap) if need_gap else None
+        g_t = _batch_dot(grad_value, dt) if need_t else None
+    if grad_marg is not None:
+        gs, gg, gt = soft_sw_backward_full(scores, grad_marg, ctx.gap, ctx.temperature, ctx.lengths)
+        grad_scores = _add(grad_scores, gs)
+        g_gap = _add(g_gap, gg) if need_gap else None
+        g_t = _add(g_t, gt) if need_t else None
+    return grad_scores, g_gap, g_t, None
+
+
+soft_sw.register_autograd(_soft_sw_backward, setup_context=_soft_sw_setup)
+
+
+@custom_op("d2p_py::soft_sw_float", mutates_args=())
+def soft_sw_float(scores: torch.Tensor, gap: float, temperature: float,
+                  lengths: Optional[torch.Tensor]) -> tuple[torch.Tensor, torch.Tensor]:
+    v, m = torch.ops.d2p.soft_sw_float(scores, gap, temperature, lengths)
+    return v, m
+
+
+@soft_sw_float.register_fake
+def _(scores, gap, temperature, lengths):
+    return _like(scores, "B", "P")
+
+
+def _soft_sw_float_setup(ctx, inputs, output):
+    scores, gap, temperature, lengths = inputs
+    ctx.save_for_backward(scores, output[1])
+    ctx.gap, ctx.temperature, ctx.lengths = gap, temperature, lengths
+
+
+def _soft_sw_float_backward(ctx, grad_value, grad_marg):
+    scores, marg = ctx.saved_tensors
+    grad_scores = _expand_batch(grad_value, marg)
+    if grad_marg is not None:
+        gs, _, _ = soft_sw_backward_full(scores, grad_marg, ctx.gap, ctx.temperature, ctx.lengths)
+        grad_scores = _add(grad_scores, gs)
+    return grad_scores, None, None, None
+
+
+soft_sw_float.register_autograd(_soft_sw_float_backward, setup_context=_soft_sw_float_setup)
+
+
+# --------------------------------------------------------------------------- affine
+@custom_op("d2p_py::soft_sw_affine_with_grads", mutates_args=())
+def soft_sw_affine_with_grads(scores: torch.Tensor, gap_open: float, gap_ext: float, temperature: float,
+                              lengths: Optional[torch.Tensor]) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    v, m, a, b, c = torch.ops.d2p.soft_sw_affine_with_grads(scores, gap_open, gap_ext, temperature, lengths)
+    return v, m, a, b, c
+
+
+@soft_sw_affine_with_grads.register_fake
+def _(scores, gap_open, gap_ext, temperature, lengths):
+    return _like(scores, "B", "P", "B", "B", "B")
+
+
+@custom_op("d2p_py::soft_sw_affine_hvp", mutates_args=())
+def soft_sw_affine_hvp(scores: torch.Tensor, tangent: torch.Tensor, gap_open: float, gap_ext: float,
+                       temperature: float, lengths: Optional[torch.Tensor]) -> torch.Tensor:
+    return torch.ops.d2p.soft_sw_affine_hvp(scores, tangent, gap_open, gap_ext, temperature, lengths)
+
+
+@soft_sw_affine_hvp.register_fake
+def _(scores, tangent, gap_open, gap_ext, temperature, lengths):
+    return _like(scores, "P")
+
+
+@custom_op("d2p_py::soft_sw_affine_param_jacobian", mutates_args=())
+def soft_sw_affine_param_jacobian(scores: torch.Tensor, param_type: int, gap_open: float, gap_ext: float,
+                                  temperature: float, lengths: Optional[torch.Tensor]) -> torch.Tensor:
+    return torch.ops.d2p.soft_sw_affine_param_jacobian(scores, param_type, gap_open, gap_ext, temperature,
+                                                       lengths)
+
+
+@soft_sw_affine_param_jacobian.register_fake
+def _(scores, param_type, gap_open, gap_ext, temperature, lengths):
+    return _like(scores, "P")
+
+
+@custom_op("d2p_py::soft_sw_affine_backward_full", mutates_args=())
+def soft_sw_affine_backward_full(scores: torch.Tensor, grad_alignment: torch.Tensor, gap_open: float,
+                                 gap_ext: float, temperature: float,
+                                 lengths: Optional[torch.Tensor]) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    a, b, c, d = torch.ops.d2p.soft_sw_affine_backward_full(scores, grad_alignment, gap_open, gap_ext,
+                                                            temperature, lengths)
+    return a, b, c, d
+
+
+@soft_sw_affine_backward_full.register_fake
+def _(scores, grad_alignment, gap_open, gap_ext, temperature, lengths):
+    return _like(scores, "P", "1", "1", "1")
+
+
+@custom_op("d2p_py::soft_sw_affine", mutates_args=())
+def soft_sw_affine(scores: torch.Tensor, gap_open: torch.Tensor, gap_ext: torch.Tensor,
+                   temperature: torch.Tensor, lengths: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    v, m = torch.ops.d2p.soft_sw_affine(scores, gap_open, gap_ext, temperature, lengths)
+    return v, m
+
+
+@soft_sw_affine.register_fake
+def _(scores, gap_open, gap_ext, temperature, lengths):
+    return _like(scores, "B", "P")
+
+
+def _soft_sw_affine_setup(ctx, inputs, output):
+    scores, go, ge, temperature, lengths = inputs
+    ctx.save_for_backward(scores, output[1])
+    ctx.go, ctx.ge, ctx.temperature = _scalar(go), _scalar(ge), _scalar(temperature)
+    ctx.lengths = lengths
+
+
+def _soft_sw_affine_backward(ctx, grad_value, grad_marg):
+    scores, marg = ctx.saved_tensors
+    grad_scores = _expand_batch(grad_value, marg)
+    need = ctx.needs_input_grad[1:4]
+    grads = [None, None, None]
+    if grad_value is not None and any(need):
+        fwd = soft_sw_affine_with_grads(scores, ctx.go, ctx.ge, ctx.temperature, ctx.lengths)
+        for k in range(3):
+            if need[k]:
+                grads[k] = _batch_dot(grad_value, fwd[2 + k])
+    if grad_marg is not None:
+        r = soft_sw_affine_backward_full(scores, grad_marg, ctx.go, ctx.ge, ctx.temperature, ctx.lengths)
+        grad_scores = _add(grad_scores, r[0])
+        for k in range(3):
+            if need[k]:
+                grads[k] = _add(grads[k], r[1 + k])
+    return grad_scores, grads[0], grads[1], grads[2], None
+
+
+soft_sw_affine.register_autograd(_soft_sw_affine_backward, setup_context=_soft_sw_affine_setup)
+
+
+@custom_op("d2p_py::soft_sw_affine_float", mutates_args=())
+def soft_sw_affine_float(scores: torch.Tensor, gap_open: float, gap_ext: float, temperature: float,
+                         lengths: Optional[torch.Tensor]) -> tuple[torch.Tensor, torch.Tensor]:
+    v, m = torch.ops.d2p.soft_sw_affine_float(scores, gap_open, gap_ext, temperature, lengths)
+    return v, m
+
+
+@soft_sw_affine_float.register_fake
+def _(scores, gap_open, gap_ext, temperature, lengths):
+    return _like(scores, "B", "P")
+
+
+def _soft_sw_affine_float_setup(ctx, inputs, output):
+    scores, go, ge, temperature, lengths = inputs
+    ctx.save_for_backward(scores, output[1])
+    ctx.go, ctx.ge, ctx.temperature, ctx.lengths = go, ge, temperature, lengths
+
+
+def _soft_sw_affine_float_backward(ctx, grad_value, grad_marg):
+    scores, marg = ctx.saved_tensors
+    grad_scores = _expand_batch(grad_value, marg)
+    if grad_marg is not None:
+        r = soft_sw_affine_backward_full(scores, grad_marg, ctx.go, ctx.ge, ctx.temperature, ctx.lengths)
+        grad_scores = _add(grad_scores, r[0])
+    return grad_scores, None, None, None, None
+
+
+soft_sw_affine_float.register_autograd(_soft_sw_affine_float_backward,
+                                       setup_context=_soft_sw_affine_float_setup)

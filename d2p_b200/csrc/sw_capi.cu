@@ -1,0 +1,333 @@
+// sw_capi.cu -- extern "C" entry points of libd2p_b200.so (declared in include/d2p_b200.h).
+//
+// Argument checking, workspace carving and kernel selection live here; the
+// kernels themselves are in sw_plane.cu (general engine), sw_wavefront.cu (fast
+// value+marginals path) and sw_elementwise.cu.
+#include <limits.h>
+#include <stdint.h>
+
+#include "../../include/d2p_b200.h"
+#include "sw_internal.h"
+
+namespace d2pb {
+
+// fast path hooks (sw_wavefront.cu); return kNotHandled when the shape is not
+// covered so that the plane engine runs instead.
+size_t wavefront_workspace_bytes(int family, int B, int L1, int L2);
+int launch_wavefront(const SwArgs& a, int family, size_t ws_bytes, cudaStream_t st);
+constexpr int kNotHandled = -1;
+
+static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+static bool dims_ok(int B, int L1, int L2) {
+    if (B < 0 || L1 < 0 || L2 < 0) return false;
+    // per-problem cell indices are 32-bit inside the kernels (the reference's
+    // "(L1 + 1) * (L2 + 1) <= INT_MAX" rule, src/sw/torch_cuda.cpp:49-65)
+    if ((long long)(L1 + 1) * (long long)(L2 + 1) > (long long)INT_MAX) return false;
+    return true;
+}
+
+static size_t plane_bytes(int family, int mode, int B, int L1, int L2) {
+    const size_t plane = (size_t)L1 * (size_t)L2;
+    const int np = family == D2P_FAMILY_AFFINE ? aff_planes(mode) : lin_planes(mode);
+    return align256((size_t)B * plane * np * sizeof(float));
+}
+
+static size_t op_bytes(int family, int op, int B, int L1, int L2) {
+    switch (op) {
+        case D2P_OP_FORWARD_BACKWARD: {
+            size_t pe = plane_bytes(family, MODE_MARG, B, L1, L2);
+            size_t wf = wavefront_workspace_bytes(family, B, L1, L2);
+            return pe > wf ? pe : wf;
+        }
+        case D2P_OP_HVP:
+            return plane_bytes(family, MODE_HVP, B, L1, L2);
+        case D2P_OP_PARAM_JACOBIAN:
+            return plane_bytes(family, MODE_PT, B, L1, L2);
+        case D2P_OP_BACKWARD_FULL:
+            return plane_bytes(family, MODE_PT, B, L1, L2) + align256((size_t)4 * (B > 0 ? B : 1) * sizeof(float));
+        default:
+            return (size_t)-1;
+    }
+}
+
+static SwArgs base_args(const float* scores, const int* lengths, int B, int L1, int L2) {
+    SwArgs a{};
+    a.scores = scores;
+    a.lengths = lengths;
+    a.B = B;
+    a.L1 = L1;
+    a.L2 = L2;
+    return a;
+}
+
+}  // namespace d2pb
+
+using namespace d2pb;
+
+extern "C" {
+
+int d2p_version(void) { return 100; }
+
+const char* d2p_error_string(int code) {
+    switch (code) {
+        case D2P_OK: return "success";
+        case D2P_ERR_INVALID_ARGUMENT: return "d2p_b200: invalid argument";
+        case D2P_ERR_WORKSPACE_TOO_SMALL: return "d2p_b200: workspace too small";
+        case D2P_ERR_TOO_LARGE: return "d2p_b200: problem too large for 32-bit cell indexing";
+        case D2P_ERR_DEVICE_STATUS: return "d2p_b200: device-side status error";
+        default: break;
+    }
+    if (code > 0 && code < 1000) return cudaGetErrorString((cudaError_t)code);
+    return "d2p_b200: unknown error";
+}
+
+size_t d2p_sw_workspace_bytes(int family, int op, int B, int L1, int L2) {
+    if (family != D2P_FAMILY_LINEAR && family != D2P_FAMILY_AFFINE) return (size_t)-1;
+    if (!dims_ok(B, L1, L2)) return (size_t)-1;
+    return op_bytes(family, op, B, L1, L2);
+}
+
+// ---------------------------------------------------------------- linear
+int d2p_sw_forward_backward(const float* scores, const int* lengths, int B, int L1, int L2,
+                            float gap, float temperature, const float* gap_dev,
+                            const float* temperature_dev, float* value, float* marginals,
+                            float* grad_gap, float* grad_temperature, void* workspace,
+                            size_t workspace_bytes, void* stream) {
+    if (!dims_ok(B, L1, L2)) return D2P_ERR_TOO_LARGE;
+    if (B == 0) return D2P_OK;
+    if (!scores && L1 > 0 && L2 > 0) return D2P_ERR_INVALID_ARGUMENT;
+    const size_t need = op_bytes(D2P_FAMILY_LINEAR, D2P_OP_FORWARD_BACKWARD, B, L1, L2);
+    if (need > 0 && (!workspace || workspace_bytes < need)) return D2P_ERR_WORKSPACE_TOO_SMALL;
+    cudaStream_t st = (cudaStream_t)stream;
+    SwArgs a = base_args(scores, lengths, B, L1, L2);
+    a.gap = gap;
+    a.temp = temperature;
+    a.gap_dev = gap_dev;
+    a.temp_dev = temperature_dev;
+    a.mode = MODE_MARG;
+    a.value = value;
+    a.out = marginals;
+    a.grad_gap = grad_gap;
+    a.grad_T = grad_temperature;
+    a.ws = (float*)workspace;
+    int rc = launch_wavefront(a, D2P_FAMILY_LINEAR, workspace_bytes, st);
+    if (rc != kNotHandled) return rc;
+    return launch_lin_plane(a, st);
+}
+
+int d2p_sw_hvp(const float* scores, const float* tangent, const int* lengths, int B, int L1,
+               int L2, float gap, float temperature, float* hvp, void* workspace,
+               size_t workspace_bytes, void* stream) {
+    if (!dims_ok(B, L1, L2)) return D2P_ERR_TOO_LARGE;
+    if (B == 0) return D2P_OK;
+    if ((!scores || !tangent || !hvp) && L1 > 0 && L2 > 0) return D2P_ERR_INVALID_ARGUMENT;
+    const size_t need = op_bytes(D2P_FAMILY_LINEAR, D2P_OP_HVP, B, L1, L2);
+    if (need > 0 && (!workspace || workspace_bytes < need)) return D2P_ERR_WORKSPACE_TOO_SMALL;
+    SwArgs a = base_args(scores, lengths, B, L1, L2);
+    a.tangent = tangent;
+    a.gap = gap;
+    a.temp = temperature;
+    a.mode = MODE_HVP;
+    a.out = hvp;
+    a.ws = (float*)workspace;
+    return launch_lin_plane(a, (cudaStream_t)stream);
+}
+
+int d2p_sw_param_jacobian(const float* scores, const int* lengths, int B, int L1, int L2,
+                          int param_type, float gap, float temperature, float* jacobian,
+                          void* workspace, size_t workspace_bytes, void* stream) {
+    if (param_type != 0 && param_type != 1) return D2P_ERR_INVALID_ARGUMENT;
+    if (!dims_ok(B, L1, L2)) return D2P_ERR_TOO_LARGE;
+    if (B == 0) return D2P_OK;
+    if ((!scores || !jacobian) && L1 > 0 && L2 > 0) return D2P_ERR_INVALID_ARGUMENT;
+    const size_t need = op_bytes(D2P_FAMILY_LINEAR, D2P_OP_PARAM_JACOBIAN, B, L1, L2);
+    if (need > 0 && (!workspace || workspace_bytes < need)) return D2P_ERR_WORKSPACE_TOO_SMALL;
+    SwArgs a = base_args(scores, lengths, B, L1, L2);
+    a.gap = gap;
+    a.temp = temperature;
+    a.mode = param_type == 0 ? MODE_PGAP : MODE_PT;
+    a.out = jacobian;
+    a.ws = (float*)workspace;
+    return launch_lin_plane(a, (cudaStream_t)stream);
+}
+
+int d2p_sw_backward_full(const float* scores, const float* grad_marginals, const int* lengths,
+                         int B, int L1, int L2, float gap, float temperature, float* grad_scores,
+                         float* grad_gap, float* grad_temperature, void* workspace,
+                         size_t workspace_bytes, void* stream) {
+    if (!dims_ok(B, L1, L2)) return D2P_ERR_TOO_LARGE;
+    if (!grad_scores || !grad_gap || !grad_temperature) return D2P_ERR_INVALID_ARGUMENT;
+    const size_t need = op_bytes(D2P_FAMILY_LINEAR, D2P_OP_BACKWARD_FULL, B, L1, L2);
+    if (!workspace || workspace_bytes < need) return D2P_ERR_WORKSPACE_TOO_SMALL;
+    cudaStream_t st = (cudaStream_t)stream;
+    if (B == 0) {
+        cudaError_t e1 = cudaMemsetAsync(grad_gap, 0, sizeof(float), st);
+        cudaError_t e2 = cudaMemsetAsync(grad_temperature, 0, sizeof(float), st);
+        return (int)(e1 != cudaSuccess ? e1 : e2);
+    }
+    float* planes = (float*)workspace;
+    float* partials = (float*)((char*)workspace + plane_bytes(D2P_FAMILY_LINEAR, MODE_PT, B, L1, L2));
+    SwArgs a = base_args(scores, lengths, B, L1, L2);
+    a.gap = gap;
+    a.temp = temperature;
+    a.ws = planes;
+    a.tangent = grad_marginals;
+    a.mode = MODE_HVP;
+    a.out = grad_scores;
+    int rc = launch_lin_plane(a, st);
+    if (rc) return rc;
+    a.tangent = nullptr;
+    a.out = nullptr;
+    a.dot_with = grad_marginals;
+    a.mode = MODE_PGAP;
+    a.dot_out = partials;
+    rc = launch_lin_plane(a, st);
+    if (rc) return rc;
+    a.mode = MODE_PT;
+    a.dot_out = partials + B;
+    rc = launch_lin_plane(a, st);
+    if (rc) return rc;
+    rc = launch_sum_batches(partials, 1, B, grad_gap, 0, st);
+    if (rc) return rc;
+    return launch_sum_batches(partials + B, 1, B, grad_temperature, 0, st);
+}
+
+int d2p_sw_value_backward(const float* grad_value, const float* marginals,
+                          const float* dvalue_dparams, int n_params, int B, int L1, int L2,
+                          float* grad_scores, float* grad_params, void* stream) {
+    if (B < 0 || L1 < 0 || L2 < 0 || n_params < 0) return D2P_ERR_INVALID_ARGUMENT;
+    if (B == 0) {
+        if (n_params > 0 && grad_params)
+            return (int)cudaMemsetAsync(grad_params, 0, sizeof(float) * n_params, (cudaStream_t)stream);
+        return D2P_OK;
+    }
+    if (!grad_value || (!marginals && L1 > 0 && L2 > 0) || (!grad_scores && L1 > 0 && L2 > 0))
+        return D2P_ERR_INVALID_ARGUMENT;
+    if (n_params > 0 && (!dvalue_dparams || !grad_params)) return D2P_ERR_INVALID_ARGUMENT;
+    return launch_value_backward(grad_value, marginals, dvalue_dparams, n_params, B, L1, L2,
+                                 grad_scores, grad_params, (cudaStream_t)stream);
+}
+
+// ---------------------------------------------------------------- affine
+int d2p_sw_affine_forward_backward(const void* scores, int scores_dtype, const int* lengths,
+                                   int B, int L1, int L2, float gap_open, float gap_ext,
+                                   float temperature, const float* gap_open_dev,
+                                   const float* gap_ext_dev, const float* temperature_dev,
+                                   float* value, float* marginals, float* grad_gap_open,
+                                   float* grad_gap_ext, float* grad_temperature, void* workspace,
+                                   size_t workspace_bytes, void* stream) {
+    if (scores_dtype != D2P_DTYPE_F32 && scores_dtype != D2P_DTYPE_BF16) return D2P_ERR_INVALID_ARGUMENT;
+    if (!dims_ok(B, L1, L2)) return D2P_ERR_TOO_LARGE;
+    if (B == 0) return D2P_OK;
+    if (!scores && L1 > 0 && L2 > 0) return D2P_ERR_INVALID_ARGUMENT;
+    const size_t need = op_bytes(D2P_FAMILY_AFFINE, D2P_OP_FORWARD_BACKWARD, B, L1, L2);
+    if (need > 0 && (!workspace || workspace_bytes < need)) return D2P_ERR_WORKSPACE_TOO_SMALL;
+    cudaStream_t st = (cudaStream_t)stream;
+    SwArgs a = base_args(scores_dtype == D2P_DTYPE_F32 ? (const float*)scores : nullptr, lengths, B, L1, L2);
+    a.scores_bf16 = scores_dtype == D2P_DTYPE_BF16 ? (const __nv_bfloat16*)scores : nullptr;
+    a.gap = gap_open;
+    a.gap2 = gap_ext;
+    a.temp = temperature;
+    a.gap_dev = gap_open_dev;
+    a.gap2_dev = gap_ext_dev;
+    a.temp_dev = temperature_dev;
+    a.mode = MODE_MARG;
+    a.value = value;
+    a.out = marginals;
+    a.grad_gap = grad_gap_open;
+    a.grad_gap2 = grad_gap_ext;
+    a.grad_T = grad_temperature;
+    a.ws = (float*)workspace;
+    int rc = launch_wavefront(a, D2P_FAMILY_AFFINE, workspace_bytes, st);
+    if (rc != kNotHandled) return rc;
+    return launch_aff_plane(a, st);
+}
+
+int d2p_sw_affine_hvp(const float* scores, const float* tangent, const int* lengths, int B,
+                      int L1, int L2, float gap_open, float gap_ext, float temperature,
+                      float* hvp, void* workspace, size_t workspace_bytes, void* stream) {
+    if (!dims_ok(B, L1, L2)) return D2P_ERR_TOO_LARGE;
+    if (B == 0) return D2P_OK;
+    if ((!scores || !tangent || !hvp) && L1 > 0 && L2 > 0) return D2P_ERR_INVALID_ARGUMENT;
+    const size_t need = op_bytes(D2P_FAMILY_AFFINE, D2P_OP_HVP, B, L1, L2);
+    if (need > 0 && (!workspace || workspace_bytes < need)) return D2P_ERR_WORKSPACE_TOO_SMALL;
+    SwArgs a = base_args(scores, lengths, B, L1, L2);
+    a.tangent = tangent;
+    a.gap = gap_open;
+    a.gap2 = gap_ext;
+    a.temp = temperature;
+    a.mode = MODE_HVP;
+    a.out = hvp;
+    a.ws = (float*)workspace;
+    return launch_aff_plane(a, (cudaStream_t)stream);
+}
+
+int d2p_sw_affine_param_jacobian(const float* scores, const int* lengths, int B, int L1, int L2,
+                                 int param_type, float gap_open, float gap_ext,
+                                 float temperature, float* jacobian, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
+    if (param_type < 0 || param_type > 2) return D2P_ERR_INVALID_ARGUMENT;
+    if (!dims_ok(B, L1, L2)) return D2P_ERR_TOO_LARGE;
+    if (B == 0) return D2P_OK;
+    if ((!scores || !jacobian) && L1 > 0 && L2 > 0) return D2P_ERR_INVALID_ARGUMENT;
+    const size_t need = op_bytes(D2P_FAMILY_AFFINE, D2P_OP_PARAM_JACOBIAN, B, L1, L2);
+    if (need > 0 && (!workspace || workspace_bytes < need)) return D2P_ERR_WORKSPACE_TOO_SMALL;
+    SwArgs a = base_args(scores, lengths, B, L1, L2);
+    a.gap = gap_open;
+    a.gap2 = gap_ext;
+    a.temp = temperature;
+    a.mode = param_type == 0 ? MODE_PGAP : (param_type == 1 ? MODE_PGE : MODE_PT);
+    a.out = jacobian;
+    a.ws = (float*)workspace;
+    return launch_aff_plane(a, (cudaStream_t)stream);
+}
+
+int d2p_sw_affine_backward_full(const float* scores, const float* grad_marginals,
+                                const int* lengths, int B, int L1, int L2, float gap_open,
+                                float gap_ext, float temperature, float* grad_scores,
+                                float* grad_gap_open, float* grad_gap_ext,
+                                float* grad_temperature, void* workspace,
+                                size_t workspace_bytes, void* stream) {
+    if (!dims_ok(B, L1, L2)) return D2P_ERR_TOO_LARGE;
+    if (!grad_scores || !grad_gap_open || !grad_gap_ext || !grad_temperature) return D2P_ERR_INVALID_ARGUMENT;
+    const size_t need = op_bytes(D2P_FAMILY_AFFINE, D2P_OP_BACKWARD_FULL, B, L1, L2);
+    if (!workspace || workspace_bytes < need) return D2P_ERR_WORKSPACE_TOO_SMALL;
+    cudaStream_t st = (cudaStream_t)stream;
+    if (B == 0) {
+        float* outs[3] = {grad_gap_open, grad_gap_ext, grad_temperature};
+        for (float* o : outs) {
+            cudaError_t e = cudaMemsetAsync(o, 0, sizeof(float), st);
+            if (e != cudaSuccess) return (int)e;
+        }
+        return D2P_OK;
+    }
+    float* planes = (float*)workspace;
+    float* partials = (float*)((char*)workspace + plane_bytes(D2P_FAMILY_AFFINE, MODE_PT, B, L1, L2));
+    SwArgs a = base_args(scores, lengths, B, L1, L2);
+    a.gap = gap_open;
+    a.gap2 = gap_ext;
+    a.temp = temperature;
+    a.ws = planes;
+    a.tangent = grad_marginals;
+    a.mode = MODE_HVP;
+    a.out = grad_scores;
+    int rc = launch_aff_plane(a, st);
+    if (rc) return rc;
+    a.tangent = nullptr;
+    a.out = nullptr;
+    a.dot_with = grad_marginals;
+    const int modes[3] = {MODE_PGAP, MODE_PGE, MODE_PT};
+    float* outs[3] = {grad_gap_open, grad_gap_ext, grad_temperature};
+    for (int q = 0; q < 3; ++q) {
+        a.mode = modes[q];
+        a.dot_out = partials + (size_t)q * B;
+        rc = launch_aff_plane(a, st);
+        if (rc) return rc;
+        rc = launch_sum_batches(partials + (size_t)q * B, 1, B, outs[q], 0, st);
+        if (rc) return rc;
+    }
+    return D2P_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,93 @@
+// sw_elementwise.cu -- the value-branch backward and small deterministic reductions.
+//
+// value backward (replaces the torch ops in the reference's
+// SoftSWRegularCUDAFunction::backward value branch, src/sw/torch_cuda.cpp:292-321,
+// which re-ran the whole reverse DP; d2p/_pt2_ops.py:180 shows that reusing the
+// saved marginals is the same gradient):
+//     grad_scores[b,i,j] = grad_value[b] * marginals[b,i,j]
+//     grad_param[p]      = sum_b grad_value[b] * dvalue_dparam[p,b]
+// HBM-bound: 8 bytes per cell (read marginals, write grad), 128-bit accesses,
+// grid sized to a multiple of the SM count.
+#include "sw_common.cuh"
+#include "sw_internal.h"
+
+namespace d2pb {
+
+__global__ void __launch_bounds__(256) value_backward_kernel(const float* __restrict__ g,
+                                                             const float* __restrict__ marg,
+                                                             const float* __restrict__ dparams,
+                                                             int n_params, int B, size_t plane,
+                                                             float* __restrict__ out,
+                                                             float* __restrict__ gparams) {
+    const size_t total = (size_t)B * plane;
+    const size_t tid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    const bool vec = ((plane & 3) == 0) && ((((uintptr_t)marg) | ((uintptr_t)out)) & 15) == 0;
+    if (vec) {
+        const size_t n4 = total >> 2;
+        const float4* __restrict__ m4 = reinterpret_cast<const float4*>(marg);
+        float4* __restrict__ o4 = reinterpret_cast<float4*>(out);
+        for (size_t q = tid; q < n4; q += stride) {
+            const size_t b = (q << 2) / plane;
+            const float gb = __ldg(g + b);
+            float4 v = __ldcs(m4 + q);  // streamed: read once
+            v.x *= gb; v.y *= gb; v.z *= gb; v.w *= gb;
+            __stcs(o4 + q, v);
+        }
+    } else {
+        for (size_t q = tid; q < total; q += stride) out[q] = __ldg(g + q / plane) * marg[q];
+    }
+    if (blockIdx.x == 0 && threadIdx.x < 32 && n_params > 0 && gparams) {
+        // fixed-order reduction: lane-strided partial sums, then a shuffle tree
+        for (int pi = 0; pi < n_params; ++pi) {
+            float acc = 0.f;
+            for (int b = threadIdx.x; b < B; b += 32) acc += g[b] * dparams[(size_t)pi * B + b];
+            acc = warp_sum(acc);
+            if (threadIdx.x == 0) gparams[pi] = acc;
+        }
+    }
+}
+
+// out[p] (+)= sum_b partials[p*B + b], deterministic (one warp).
+__global__ void sum_batches_kernel(const float* __restrict__ partials, int P, int B,
+                                   float* __restrict__ out, int accumulate) {
+    for (int pi = 0; pi < P; ++pi) {
+        float acc = 0.f;
+        for (int b = threadIdx.x; b < B; b += 32) acc += partials[(size_t)pi * B + b];
+        acc = warp_sum(acc);
+        if (threadIdx.x == 0) out[pi] = accumulate ? out[pi] + acc : acc;
+    }
+}
+
+static int grid_for(size_t work_items) {
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) {
+        int v = 0;
+        if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0) sms = v;
+    }
+    size_t want = (work_items + 255) / 256;
+    size_t cap = (size_t)sms * 8;  // 8 resident CTAs of 256 threads per SM
+    if (want > cap) want = cap;
+    if (want < 1) want = 1;
+    return (int)want;
+}
+
+int launch_value_backward(const float* grad_value, const float* marginals, const float* dparams,
+                          int n_params, int B, int L1, int L2, float* grad_scores,
+                          float* grad_params, cudaStream_t st) {
+    const size_t plane = (size_t)L1 * L2;
+    const size_t total = (size_t)B * plane;
+    if (total == 0 && n_params == 0) return 0;
+    const int grid = grid_for(total / 4 + 1);
+    value_backward_kernel<<<grid, 256, 0, st>>>(grad_value, marginals, dparams, n_params, B,
+                                                plane > 0 ? plane : 1, grad_scores, grad_params);
+    return (int)cudaGetLastError();
+}
+
+int launch_sum_batches(const float* partials, int P, int B, float* out, int accumulate,
+                       cudaStream_t st) {
+    sum_batches_kernel<<<1, 32, 0, st>>>(partials, P, B, out, accumulate);
+    return (int)cudaGetLastError();
+}
+
+}  // namespace d2pb

@@ -1,0 +1,66 @@
+// sw_internal.h -- internal launch descriptors shared by the d2p_b200 CUDA sources.
+// Not part of the public C ABI (that is include/d2p_b200.h).
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+
+namespace d2pb {
+
+// operator modes (one kernel instantiation each)
+enum SwMode : int {
+    MODE_MARG = 0,  // value + marginals (+ dS/dgap, dS/dT)
+    MODE_HVP = 1,   // Hessian-vector product  H = d(marginals)/d(scores) . V
+    MODE_PGAP = 2,  // dP/d(gap)          (affine: dP/d(gap_open))
+    MODE_PGE = 3,   // affine only: dP/d(gap_ext)
+    MODE_PT = 4,    // dP/d(temperature)
+};
+
+// DP planes (each B*L1*L2 floats) the plane engine needs per mode; planes are
+// ordered so that a mode uses a prefix of the full layout.
+__host__ __device__ constexpr int lin_planes(int mode) {
+    return mode == MODE_MARG ? 2 : (mode == MODE_PT ? 5 : 4);
+}
+__host__ __device__ constexpr int aff_planes(int mode) {
+    return mode == MODE_MARG ? 6 : (mode == MODE_PT ? 15 : 12);
+}
+
+// library error codes (cudaError_t values are passed through unchanged)
+constexpr int kErrInvalid = 1001;
+constexpr int kErrWorkspace = 1002;
+constexpr int kErrTooLarge = 1003;
+constexpr int kErrDeviceStatus = 1004;
+
+struct SwArgs {
+    const float* scores;                // [B, L1, L2] fp32 (may be null if scores_bf16 set)
+    const __nv_bfloat16* scores_bf16;   // [B, L1, L2] bf16 (affine fast/plane paths)
+    const float* tangent;               // [B, L1, L2] HVP direction
+    const int* lengths;                 // [B, 2] or null (full lengths)
+    int B, L1, L2;                      // padded dims
+    float gap, gap2, temp;              // linear: gap; affine: gap=open, gap2=ext
+    const float* gap_dev;               // optional device scalars (override host values)
+    const float* gap2_dev;
+    const float* temp_dev;
+    int mode;
+    float* value;                       // [B]
+    float* out;                         // [B, L1, L2]: marginals / H / dP
+    float* grad_gap;                    // [B]  (affine: d/d gap_open)
+    float* grad_gap2;                   // [B]  (affine: d/d gap_ext)
+    float* grad_T;                      // [B]
+    float* ws;                          // workspace
+    int* status;                        // device status word (optional)
+    const float* dot_with;              // [B, L1, L2] optional: param modes accumulate
+    float* dot_out;                     //   dot_out[b] = sum_ij dot_with[b,i,j] * dP[b,i,j]
+};
+
+int launch_lin_plane(const SwArgs& a, cudaStream_t st);
+int launch_aff_plane(const SwArgs& a, cudaStream_t st);
+
+// elementwise / reduction kernels (sw_elementwise.cu)
+int launch_value_backward(const float* grad_value, const float* marginals, const float* dparams,
+                          int n_params, int B, int L1, int L2, float* grad_scores,
+                          float* grad_params, cudaStream_t st);
+int launch_sum_batches(const float* partials, int P, int B, float* out, int accumulate,
+                       cudaStream_t st);
+
+}  // namespace d2pb

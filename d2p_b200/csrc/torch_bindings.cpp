@@ -1,0 +1,714 @@
+// torch_bindings.cpp -- the reference's dispatcher surface (torch.ops.d2p.*) for the
+// soft Smith-Waterman family, implemented on top of the C ABI in
+// include/d2p_b200.h (libd2p_b200.so).
+//
+// Schemas are the reference's, verbatim (src/sw/registry.cpp:30-44,
+// src/sw_affine/registry.cpp:27-42), so code written against d2p's ops binds
+// unchanged.  CUDA and AutogradCUDA keys are registered exactly as the reference
+// does (src/sw/torch_cuda.cpp:857-883, src/sw_affine/torch_cuda.cpp:914-948);
+// there is no CPU kernel and no fallback: CPU tensors are rejected with the
+// reference's "must be a CUDA tensor" message.
+//
+// Differences from the reference host glue, all behaviour-preserving:
+//  * no cudaStreamSynchronize after launches, no DP planes cloned into the
+//    autograd context (the value backward reuses the saved marginals, as the
+//    reference's PT2 path does, d2p/_pt2_ops.py:178-206);
+//  * tensor gap/temperature on the scores' device are read on the device
+//    (no .item() host sync on the forward path);
+//  * lengths=None is passed down as "full lengths" instead of materialising a
+//    [B,2] tensor with a host->device copy.
+#include <ATen/ATen.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/csrc/autograd/custom_function.h>
+#include <torch/library.h>
+#include <torch/types.h>
+
+#include <limits>
+#include <vector>
+
+#include "../../include/d2p_b200.h"
+
+namespace {
+
+using torch::Tensor;
+using torch::autograd::AutogradContext;
+using torch::autograd::tensor_list;
+
+#define D2PB_CHECK_CUDA(x) TORCH_CHECK((x).is_cuda(), #x " must be a CUDA tensor")
+#define D2PB_CHECK_CONTIGUOUS(x) TORCH_CHECK((x).is_contiguous(), #x " must be contiguous")
+#define D2PB_CHECK_FLOAT(x) \
+    TORCH_CHECK((x).scalar_type() == torch::kFloat32, #x " must be float32, got ", (x).scalar_type())
+#define D2PB_CHECK_INPUT(x) \
+    D2PB_CHECK_CUDA(x);     \
+    D2PB_CHECK_CONTIGUOUS(x); \
+    D2PB_CHECK_FLOAT(x)
+
+inline void check_rc(int rc, const char* what) {
+    TORCH_CHECK(rc == 0, what, " failed: ", d2p_error_string(rc), " (code ", rc, ")");
+}
+
+inline void* cur_stream() { return (void*)at::cuda::getCurrentCUDAStream().stream(); }
+
+struct Shape {
+    int B, L1, L2;
+};
+
+// src/sw/torch_cuda.cpp:41-65 (messages kept)
+int checked_dim(int64_t value, const char* name) {
+    TORCH_CHECK(value >= 0 && value <= static_cast<int64_t>(std::numeric_limits<int>::max()),
+                name, " must fit int32 CUDA kernel indexing, got ", value);
+    return static_cast<int>(value);
+}
+
+Shape checked_shape(const Tensor& scores) {
+    TORCH_CHECK(scores.dim() == 3, "scores must be 3D (B, L1, L2)");
+    Shape s{checked_dim(scores.size(0), "scores batch dimension"),
+            checked_dim(scores.size(1), "scores L1 dimension"),
+            checked_dim(scores.size(2), "scores L2 dimension")};
+    const int64_t cells = (static_cast<int64_t>(s.L1) + 1) * (static_cast<int64_t>(s.L2) + 1);
+    TORCH_CHECK(cells <= static_cast<int64_t>(std::numeric_limits<int>::max()),
+                "SW CUDA DP table is too large for 32-bit kernel indexing: ",
+                "(L1 + 1) * (L2 + 1) = ", cells, " exceeds ", std::numeric_limits<int>::max());
+    return s;
+}
+
+// src/sw/torch_cuda.cpp:67-97: same checks and messages.  The range check needs
+// the values on the host (one small device->host copy), as in the reference.
+void validate_lengths(const Tensor& lengths, const Shape& s, const torch::Device& device) {
+    D2PB_CHECK_CUDA(lengths);
+    D2PB_CHECK_CONTIGUOUS(lengths);
+    TORCH_CHECK(lengths.dim() == 2 && lengths.size(0) == s.B && lengths.size(1) == 2);
+    TORCH_CHECK(lengths.dtype() == torch::kInt32, "lengths must be int32");
+    TORCH_CHECK(lengths.device() == device, "lengths must be on same device as scores, got ",
+                lengths.device(), " vs ", device);
+    auto h = lengths.to(torch::kCPU);
+    auto acc = h.accessor<int32_t, 2>();
+    for (int b = 0; b < s.B; ++b) {
+        const int l1 = acc[b][0], l2 = acc[b][1];
+        TORCH_CHECK(l1 >= 0 && l1 <= s.L1, "lengths[", b, ",0] must be between 0 and ", s.L1, ", got ", l1);
+        TORCH_CHECK(l2 >= 0 && l2 <= s.L2, "lengths[", b, ",1] must be between 0 and ", s.L2, ", got ", l2);
+    }
+}
+
+// Returns an undefined tensor for "full lengths".
+Tensor resolve_lengths(const c10::optional<Tensor>& lengths, const Shape& s, const torch::Device& dev) {
+    if (!lengths.has_value() || !lengths->defined()) return Tensor();
+    validate_lengths(*lengths, s, dev);
+    return *lengths;
+}
+
+inline const int* len_ptr(const Tensor& t) { return t.defined() ? t.data_ptr<int>() : nullptr; }
+
+Tensor workspace(int family, int op, const Shape& s, const torch::Device& dev, size_t* bytes) {
+    size_t n = d2p_sw_workspace_bytes(family, op, s.B, s.L1, s.L2);
+    TORCH_CHECK(n != static_cast<size_t>(-1), "SW CUDA problem size not supported");
+    *bytes = n;
+    return torch::empty({static_cast<int64_t>(n > 0 ? n : 1)},
+                        torch::TensorOptions().dtype(torch::kUInt8).device(dev));
+}
+
+// A scalar parameter either as a device pointer (no sync) or a host float.
+struct Param {
+    float host = 0.f;
+    const float* dev = nullptr;
+    Tensor keep;
+};
+
+Param read_param(const Tensor& t, const Tensor& scores, const char* name) {
+    TORCH_CHECK(t.numel() == 1, name, " must be a scalar tensor");
+    Param p;
+    if (t.is_cuda() && t.device() == scores.device()) {
+        p.keep = t.to(torch::kFloat32).contiguous();
+        p.dev = p.keep.data_ptr<float>();
+    } else {
+        p.host = t.to(torch::kCPU).to(torch::kFloat32).item<float>();
+    }
+    return p;
+}
+
+float host_value(const Tensor& t) { return t.to(torch::kCPU).to(torch::kFloat32).item<float>(); }
+
+Tensor prep_grad(Tensor g, const Tensor& scores, const char* what) {
+    TORCH_CHECK(g.sizes() == scores.sizes(), what, " shape mismatch: expected ", scores.sizes(),
+                " but got ", g.sizes());
+    TORCH_CHECK(g.is_cuda(), what, " must be on CUDA, got ", g.device());
+    if (g.scalar_type() != torch::kFloat32) g = g.to(torch::kFloat32);
+    if (g.device() != scores.device()) g = g.to(scores.device());
+    return g.contiguous();
+}
+
+// =============================================================================
+// linear gap: raw computations
+// =============================================================================
+struct LinFwd {
+    Tensor value, marginals, dparams;  // dparams [2,B]: dS/dgap, dS/dT
+};
+
+LinFwd lin_forward(const Tensor& scores, const Param& gap, const Param& T, const Tensor& lengths,
+                   const Shape& s) {
+    auto opt = scores.options();
+    LinFwd r;
+    r.value = torch::empty({s.B}, opt);
+    r.marginals = torch::empty({s.B, s.L1, s.L2}, opt);
+    r.dparams = torch::empty({2, s.B}, opt);
+    size_t wb = 0;
+    Tensor ws = workspace(D2P_FAMILY_LINEAR, D2P_OP_FORWARD_BACKWARD, s, scores.device(), &wb);
+    check_rc(d2p_sw_forward_backward(scores.data_ptr<float>(), len_ptr(lengths), s.B, s.L1, s.L2,
+                                     gap.host, T.host, gap.dev, T.dev, r.value.data_ptr<float>(),
+                                     r.marginals.data_ptr<float>(), r.dparams.data_ptr<float>(),
+                                     r.dparams.data_ptr<float>() + s.B, ws.data_ptr(), wb, cur_stream()),
+             "d2p_sw_forward_backward");
+    return r;
+}
+
+Tensor lin_hvp_raw(const Tensor& scores, const Tensor& tangent, float gap, float T,
+                   const Tensor& lengths, const Shape& s) {
+    Tensor H = torch::empty({s.B, s.L1, s.L2}, scores.options());
+    size_t wb = 0;
+    Tensor ws = workspace(D2P_FAMILY_LINEAR, D2P_OP_HVP, s, scores.device(), &wb);
+    check_rc(d2p_sw_hvp(scores.data_ptr<float>(), tangent.data_ptr<float>(), len_ptr(lengths), s.B,
+                        s.L1, s.L2, gap, T, H.data_ptr<float>(), ws.data_ptr(), wb, cur_stream()),
+             "d2p_sw_hvp");
+    return H;
+}
+
+Tensor lin_jac_raw(const Tensor& scores, int param_type, float gap, float T, const Tensor& lengths,
+                   const Shape& s) {
+    Tensor J = torch::empty({s.B, s.L1, s.L2}, scores.options());
+    size_t wb = 0;
+    Tensor ws = workspace(D2P_FAMILY_LINEAR, D2P_OP_PARAM_JACOBIAN, s, scores.device(), &wb);
+    check_rc(d2p_sw_param_jacobian(scores.data_ptr<float>(), len_ptr(lengths), s.B, s.L1, s.L2,
+                                   param_type, gap, T, J.data_ptr<float>(), ws.data_ptr(), wb,
+                                   cur_stream()),
+             "d2p_sw_param_jacobian");
+    return J;
+}
+
+std::tuple<Tensor, Tensor, Tensor> lin_backward_full_raw(const Tensor& scores, const Tensor& G,
+                                                         float gap, float T, const Tensor& lengths,
+                                                         const Shape& s) {
+    auto opt = scores.options();
+    Tensor gs = torch::empty({s.B, s.L1, s.L2}, opt);
+    Tensor gg = torch::empty({1}, opt), gT = torch::empty({1}, opt);
+    size_t wb = 0;
+    Tensor ws = workspace(D2P_FAMILY_LINEAR, D2P_OP_BACKWARD_FULL, s, scores.device(), &wb);
+    check_rc(d2p_sw_backward_full(scores.data_ptr<float>(), G.data_ptr<float>(), len_ptr(lengths),
+                                  s.B, s.L1, s.L2, gap, T, gs.data_ptr<float>(), gg.data_ptr<float>(),
+                                  gT.data_ptr<float>(), ws.data_ptr(), wb, cur_stream()),
+             "d2p_sw_backward_full");
+    return {gs, gg, gT};
+}
+
+// =============================================================================
+// linear gap: autograd function (reference SoftSWRegularCUDAFunction,
+// src/sw/torch_cuda.cpp:178-411)
+// =============================================================================
+class SoftSWFunction : public torch::autograd::Function<SoftSWFunction> {
+   public:
+    // lengths travels as an optional non-variable argument: autograd records
+    // metadata (device, dtype) for every Tensor input, which an undefined
+    // "full lengths" tensor does not have.
+    static tensor_list forward(AutogradContext* ctx, Tensor scores, Tensor gap, Tensor temperature,
+                               c10::optional<Tensor> lengths_opt) {
+        Tensor lengths = lengths_opt.has_value() ? *lengths_opt : Tensor();
+        ctx->set_materialize_grads(false);
+        D2PB_CHECK_INPUT(scores);
+        const Shape s = checked_shape(scores);
+        c10::cuda::CUDAGuard guard(scores.device());
+        Param pg = read_param(gap, scores, "gap");
+        Param pT = read_param(temperature, scores, "temperature");
+        if (lengths.defined()) validate_lengths(lengths, s, scores.device());
+        LinFwd r = lin_forward(scores, pg, pT, lengths, s);
+        ctx->save_for_backward({scores, r.marginals, r.dparams, gap, temperature});
+        ctx->saved_data["lengths"] = lengths.defined() ? c10::IValue(lengths) : c10::IValue();
+        return {r.value, r.marginals};
+    }
+
+    static tensor_list backward(AutogradContext* ctx, tensor_list grad_outputs) {
+        auto saved = ctx->get_saved_variables();
+        Tensor scores = saved[0], marginals = saved[1], dparams = saved[2];
+        Tensor gap = saved[3], temperature = saved[4];
+        Tensor lengths;
+        if (!ctx->saved_data["lengths"].isNone()) lengths = ctx->saved_data["lengths"].toTensor();
+        const Shape s = checked_shape(scores);
+        c10::cuda::CUDAGuard guard(scores.device());
+        auto opt = scores.options();
+        Tensor gv = grad_outputs[0], gm = grad_outputs[1];
+        Tensor grad_scores, grad_gap = torch::zeros({1}, opt), grad_T = torch::zeros({1}, opt);
+        bool have = false;
+        if (gv.defined() && gv.numel() > 0) {
+            Tensor g = gv.to(torch::kFloat32).contiguous();
+            if (g.device() != scores.device()) g = g.to(scores.device());
+            grad_scores = torch::empty({s.B, s.L1, s.L2}, opt);
+            Tensor gp = torch::empty({2}, opt);
+            check_rc(d2p_sw_value_backward(g.data_ptr<float>(), marginals.data_ptr<float>(),
+                                           dparams.data_ptr<float>(), 2, s.B, s.L1, s.L2,
+                                           grad_scores.data_ptr<float>(), gp.data_ptr<float>(),
+                                           cur_stream()),
+                     "d2p_sw_value_backward");
+            grad_gap = gp.narrow(0, 0, 1);
+            grad_T = gp.narrow(0, 1, 1);
+            have = true;
+        }
+        if (gm.defined() && gm.numel() > 0) {
+            Tensor G = prep_grad(gm, scores, "grad_posteriors");
+            auto r = lin_backward_full_raw(scores, G, host_value(gap), host_value(temperature), lengths, s);
+            grad_scores = have ? grad_scores + std::get<0>(r) : std::get<0>(r);
+            grad_gap = grad_gap + std::get<1>(r);
+            grad_T = grad_T + std::get<2>(r);
+            have = true;
+        }
+        if (!have) grad_scores = torch::zeros({s.B, s.L1, s.L2}, opt);
+        return {grad_scores, grad_gap, grad_T, Tensor()};
+    }
+};
+
+std::vector<Tensor> soft_sw_cuda(Tensor scores, Tensor gap, Tensor temperature, Tensor lengths) {
+    return SoftSWFunction::apply(scores, gap, temperature, c10::optional<Tensor>(lengths));
+}
+
+std::vector<Tensor> soft_sw_float_cuda(Tensor scores, double gap, double temperature,
+                                       c10::optional<Tensor> lengths) {
+    D2PB_CHECK_INPUT(scores);
+    const Shape s = checked_shape(scores);
+    c10::cuda::CUDAGuard guard(scores.device());
+    Tensor len = resolve_lengths(lengths, s, scores.device());
+    auto cpu = torch::TensorOptions().dtype(torch::kFloat32);
+    return SoftSWFunction::apply(scores, torch::full({1}, (float)gap, cpu),
+                                 torch::full({1}, (float)temperature, cpu),
+                                 len.defined() ? c10::optional<Tensor>(len) : c10::nullopt);
+}
+
+std::tuple<Tensor, Tensor, Tensor, Tensor> soft_sw_with_grads_cuda(Tensor scores, double gap,
+                                                                   double temperature,
+                                                                   c10::optional<Tensor> lengths) {
+    D2PB_CHECK_INPUT(scores);
+    const Shape s = checked_shape(scores);
+    c10::cuda::CUDAGuard guard(scores.device());
+    Tensor len = resolve_lengths(lengths, s, scores.device());
+    Param pg, pT;
+    pg.host = (float)gap;
+    pT.host = (float)temperature;
+    LinFwd r = lin_forward(scores, pg, pT, len, s);
+    return {r.value, r.marginals, r.dparams[0], r.dparams[1]};
+}
+
+Tensor soft_sw_hvp_cuda(Tensor scores, Tensor tangent, double gap, double temperature,
+                        c10::optional<Tensor> lengths) {
+    D2PB_CHECK_INPUT(scores);
+    D2PB_CHECK_INPUT(tangent);
+    TORCH_CHECK(scores.dim() == 3, "scores must be 3D");
+    TORCH_CHECK(scores.sizes() == tangent.sizes(), "scores and tangent must have same shape");
+    TORCH_CHECK(tangent.device() == scores.device(), "tangent must be on same device as scores, got ",
+                tangent.device(), " vs ", scores.device());
+    const Shape s = checked_shape(scores);
+    c10::cuda::CUDAGuard guard(scores.device());
+    Tensor len = resolve_lengths(lengths, s, scores.device());
+    return lin_hvp_raw(scores, tangent, (float)gap, (float)temperature, len, s);
+}
+
+Tensor soft_sw_param_jacobian_cuda(Tensor scores, int64_t param_type, double gap, double temperature,
+                                   c10::optional<Tensor> lengths) {
+    D2PB_CHECK_INPUT(scores);
+    TORCH_CHECK(scores.dim() == 3, "scores must be 3D");
+    TORCH_CHECK(param_type >= 0 && param_type <= 1, "param_type must be 0 or 1");
+    const Shape s = checked_shape(scores);
+    c10::cuda::CUDAGuard guard(scores.device());
+    Tensor len = resolve_lengths(lengths, s, scores.device());
+    return lin_jac_raw(scores, (int)param_type, (float)gap, (float)temperature, len, s);
+}
+
+std::tuple<Tensor, Tensor, Tensor> soft_sw_backward_full_cuda(Tensor scores, Tensor grad_alignment,
+                                                              double gap, double temperature,
+                                                              c10::optional<Tensor> lengths) {
+    D2PB_CHECK_INPUT(scores);
+    TORCH_CHECK(scores.dim() == 3, "scores must be 3D (B, L1, L2)");
+    TORCH_CHECK(grad_alignment.sizes() == scores.sizes(), "grad_alignment must have same shape as scores");
+    TORCH_CHECK(grad_alignment.is_cuda(), "grad_alignment must be a CUDA tensor");
+    TORCH_CHECK(grad_alignment.device() == scores.device(),
+                "grad_alignment must be on same device as scores, got ", grad_alignment.device(), " vs ",
+                scores.device());
+    const Shape s = checked_shape(scores);
+    c10::cuda::CUDAGuard guard(scores.device());
+    Tensor len = resolve_lengths(lengths, s, scores.device());
+    Tensor G = grad_alignment.contiguous();
+    if (G.scalar_type() != torch::kFloat32) G = G.to(torch::kFloat32);
+    return lin_backward_full_raw(scores, G, (float)gap, (float)temperature, len, s);
+}
+
+// namespaced aliases (src/sw/torch_cuda.cpp:778-848)
+std::vector<Tensor> sw_forward_cuda(Tensor scores, double gap, double temp, c10::optional<Tensor> lengths) {
+    return soft_sw_float_cuda(scores, gap, temp, lengths);
+}
+std::vector<Tensor> sw_forward_t_cuda(Tensor scores, Tensor gap, Tensor temp, Tensor lengths) {
+    return soft_sw_cuda(scores, gap, temp, lengths);
+}
+std::tuple<Tensor, Tensor> sw_value_grad_params_cuda(Tensor scores, double gap, double temp,
+                                                     c10::optional<Tensor> lengths) {
+    auto r = soft_sw_with_grads_cuda(scores, gap, temp, lengths);
+    return {std::get<2>(r), std::get<3>(r)};
+}
+std::tuple<Tensor, Tensor, Tensor> sw_marginals_backward_cuda(Tensor scores, Tensor grad_marginals,
+                                                              double gap, double temp,
+                                                              c10::optional<Tensor> lengths) {
+    return soft_sw_backward_full_cuda(scores, grad_marginals, gap, temp, lengths);
+}
+Tensor sw_marginals_hvp_cuda(Tensor scores, Tensor v, double gap, double temp, c10::optional<Tensor> lengths) {
+    return soft_sw_hvp_cuda(scores, v, gap, temp, lengths);
+}
+Tensor sw_marginals_grad_gap_cuda(Tensor scores, double gap, double temp, c10::optional<Tensor> lengths) {
+    return soft_sw_param_jacobian_cuda(scores, 0, gap, temp, lengths);
+}
+Tensor sw_marginals_grad_temp_cuda(Tensor scores, double gap, double temp, c10::optional<Tensor> lengths) {
+    return soft_sw_param_jacobian_cuda(scores, 1, gap, temp, lengths);
+}
+
+// =============================================================================
+// affine gap
+// =============================================================================
+// The affine forward accepts bf16 scores directly (read as bf16, upcast in
+// registers).  The reference requires fp32 (bf16 only via autocast,
+// d2p/_compile.py:886-891); accepting bf16 is an extension that halves the
+// score bytes of the bf16 workload and changes no fp32 behaviour.
+#define D2PB_CHECK_AFF_SCORES(x)                                                        \
+    D2PB_CHECK_CUDA(x);                                                                 \
+    D2PB_CHECK_CONTIGUOUS(x);                                                           \
+    TORCH_CHECK((x).scalar_type() == torch::kFloat32 || (x).scalar_type() == torch::kBFloat16, \
+                #x " must be float32, got ", (x).scalar_type())
+
+struct AffFwd {
+    Tensor value, marginals, dparams;  // dparams [3,B]: dS/dgap_open, dS/dgap_ext, dS/dT
+};
+
+AffFwd aff_forward(const Tensor& scores, const Param& go, const Param& ge, const Param& T,
+                   const Tensor& lengths, const Shape& s) {
+    auto opt = scores.options().dtype(torch::kFloat32);
+    AffFwd r;
+    r.value = torch::empty({s.B}, opt);
+    r.marginals = torch::empty({s.B, s.L1, s.L2}, opt);
+    r.dparams = torch::empty({3, s.B}, opt);
+    size_t wb = 0;
+    Tensor ws = workspace(D2P_FAMILY_AFFINE, D2P_OP_FORWARD_BACKWARD, s, scores.device(), &wb);
+    const int dt = scores.scalar_type() == torch::kBFloat16 ? D2P_DTYPE_BF16 : D2P_DTYPE_F32;
+    float* dp = r.dparams.data_ptr<float>();
+    check_rc(d2p_sw_affine_forward_backward(scores.data_ptr(), dt, len_ptr(lengths), s.B, s.L1, s.L2,
+                                            go.host, ge.host, T.host, go.dev, ge.dev, T.dev,
+                                            r.value.data_ptr<float>(), r.marginals.data_ptr<float>(), dp,
+                                            dp + s.B, dp + 2 * s.B, ws.data_ptr(), wb, cur_stream()),
+             "d2p_sw_affine_forward_backward");
+    return r;
+}
+
+Tensor aff_hvp_raw(const Tensor& scores, const Tensor& tangent, float go, float ge, float T,
+                   const Tensor& lengths, const Shape& s) {
+    Tensor H = torch::empty({s.B, s.L1, s.L2}, scores.options());
+    size_t wb = 0;
+    Tensor ws = workspace(D2P_FAMILY_AFFINE, D2P_OP_HVP, s, scores.device(), &wb);
+    check_rc(d2p_sw_affine_hvp(scores.data_ptr<float>(), tangent.data_ptr<float>(), len_ptr(lengths), s.B,
+                               s.L1, s.L2, go, ge, T, H.data_ptr<float>(), ws.data_ptr(), wb, cur_stream()),
+             "d2p_sw_affine_hvp");
+    return H;
+}
+
+Tensor aff_jac_raw(const Tensor& scores, int param_type, float go, float ge, float T,
+                   const Tensor& lengths, const Shape& s) {
+    Tensor J = torch::empty({s.B, s.L1, s.L2}, scores.options());
+    size_t wb = 0;
+    Tensor ws = workspace(D2P_FAMILY_AFFINE, D2P_OP_PARAM_JACOBIAN, s, scores.device(), &wb);
+    check_rc(d2p_sw_affine_param_jacobian(scores.data_ptr<float>(), len_ptr(lengths), s.B, s.L1, s.L2,
+                                          param_type, go, ge, T, J.data_ptr<float>(), ws.data_ptr(), wb,
+                                          cur_stream()),
+             "d2p_sw_affine_param_jacobian");
+    return J;
+}
+
+std::tuple<Tensor, Tensor, Tensor, Tensor> aff_backward_full_raw(const Tensor& scores, const Tensor& G,
+                                                                 float go, float ge, float T,
+                                                                 const Tensor& lengths, const Shape& s) {
+    auto opt = scores.options();
+    Tensor gs = torch::empty({s.B, s.L1, s.L2}, opt);
+    Tensor a = torch::empty({1}, opt), b = torch::empty({1}, opt), c = torch::empty({1}, opt);
+    size_t wb = 0;
+    Tensor ws = workspace(D2P_FAMILY_AFFINE, D2P_OP_BACKWARD_FULL, s, scores.device(), &wb);
+    check_rc(d2p_sw_affine_backward_full(scores.data_ptr<float>(), G.data_ptr<float>(), len_ptr(lengths),
+                                         s.B, s.L1, s.L2, go, ge, T, gs.data_ptr<float>(), a.data_ptr<float>(),
+                                         b.data_ptr<float>(), c.data_ptr<float>(), ws.data_ptr(), wb,
+                                         cur_stream()),
+             "d2p_sw_affine_backward_full");
+    return {gs, a, b, c};
+}
+
+// reference SoftSWAffineCUDAFunction (src/sw_affine/torch_cuda.cpp:126-400)
+class SoftSWAffineFunction : public torch::autograd::Function<SoftSWAffineFunction> {
+   public:
+    static tensor_list forward(AutogradContext* ctx, Tensor scores, Tensor gap_open, Tensor gap_ext,
+                               Tensor temperature, c10::optional<Tensor> lengths_opt) {
+        Tensor lengths = lengths_opt.has_value() ? *lengths_opt : Tensor();
+        ctx->set_materialize_grads(false);
+        D2PB_CHECK_AFF_SCORES(scores);
+        const Shape s = checked_shape(scores);
+        c10::cuda::CUDAGuard guard(scores.device());
+        Param po = read_param(gap_open, scores, "gap_open");
+        Param pe = read_param(gap_ext, scores, "gap_ext");
+        Param pT = read_param(temperature, scores, "temperature");
+        if (lengths.defined()) validate_lengths(lengths, s, scores.device());
+        AffFwd r = aff_forward(scores, po, pe, pT, lengths, s);
+        ctx->save_for_backward({scores, r.marginals, r.dparams, gap_open, gap_ext, temperature});
+        ctx->saved_data["lengths"] = lengths.defined() ? c10::IValue(lengths) : c10::IValue();
+        return {r.value, r.marginals};
+    }
+
+    static tensor_list backward(AutogradContext* ctx, tensor_list grad_outputs) {
+        auto saved = ctx->get_saved_variables();
+        Tensor scores = saved[0], marginals = saved[1], dparams = saved[2];
+        Tensor go = saved[3], ge = saved[4], temperature = saved[5];
+        Tensor lengths;
+        if (!ctx->saved_data["lengths"].isNone()) lengths = ctx->saved_data["lengths"].toTensor();
+        const Shape s = checked_shape(scores);
+        c10::cuda::CUDAGuard guard(scores.device());
+        auto opt = scores.options().dtype(torch::kFloat32);
+        Tensor gv = grad_outputs[0], gm = grad_outputs[1];
+        Tensor grad_scores, g_o = torch::zeros({1}, opt), g_e = torch::zeros({1}, opt),
+                            g_T = torch::zeros({1}, opt);
+        bool have = false;
+        if (gv.defined() && gv.numel() > 0) {
+            Tensor g = gv.to(torch::kFloat32).contiguous();
+            if (g.device() != scores.device()) g = g.to(scores.device());
+            grad_scores = torch::empty({s.B, s.L1, s.L2}, opt);
+            Tensor gp = torch::empty({3}, opt);
+            check_rc(d2p_sw_value_backward(g.data_ptr<float>(), marginals.data_ptr<float>(),
+                                           dparams.data_ptr<float>(), 3, s.B, s.L1, s.L2,
+                                           grad_scores.data_ptr<float>(), gp.data_ptr<float>(), cur_stream()),
+                     "d2p_sw_value_backward");
+            g_o = gp.narrow(0, 0, 1);
+            g_e = gp.narrow(0, 1, 1);
+            g_T = gp.narrow(0, 2, 1);
+            have = true;
+        }
+        if (gm.defined() && gm.numel() > 0) {
+            Tensor G = prep_grad(gm, scores, "grad_posteriors");
+            Tensor sf = scores.scalar_type() == torch::kFloat32 ? scores : scores.to(torch::kFloat32);
+            auto r = aff_backward_full_raw(sf, G, host_value(go), host_value(ge), host_value(temperature),
+                                           lengths, s);
+            grad_scores = have ? grad_scores + std::get<0>(r) : std::get<0>(r);
+            g_o = g_o + std::get<1>(r);
+            g_e = g_e + std::get<2>(r);
+            g_T = g_T + std::get<3>(r);
+            have = true;
+        }
+        if (!have) grad_scores = torch::zeros({s.B, s.L1, s.L2}, opt);
+        return {grad_scores, g_o, g_e, g_T, Tensor()};
+    }
+};
+
+std::vector<Tensor> soft_sw_affine_cuda(Tensor scores, Tensor gap_open, Tensor gap_ext, Tensor temperature,
+                                        Tensor lengths) {
+    return SoftSWAffineFunction::apply(scores, gap_open, gap_ext, temperature, c10::optional<Tensor>(lengths));
+}
+
+std::vector<Tensor> soft_sw_affine_float_cuda(Tensor scores, double gap_open, double gap_ext,
+                                              double temperature, c10::optional<Tensor> lengths) {
+    D2PB_CHECK_AFF_SCORES(scores);
+    const Shape s = checked_shape(scores);
+    c10::cuda::CUDAGuard guard(scores.device());
+    Tensor len = resolve_lengths(lengths, s, scores.device());
+    auto cpu = torch::TensorOptions().dtype(torch::kFloat32);
+    return SoftSWAffineFunction::apply(scores, torch::full({1}, (float)gap_open, cpu),
+                                       torch::full({1}, (float)gap_ext, cpu),
+                                       torch::full({1}, (float)temperature, cpu),
+                                       len.defined() ? c10::optional<Tensor>(len) : c10::nullopt);
+}
+
+std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor> soft_sw_affine_with_grads_cuda(
+    Tensor scores, double gap_open, double gap_ext, double temperature, c10::optional<Tensor> lengths) {
+    D2PB_CHECK_AFF_SCORES(scores);
+    const Shape s = checked_shape(scores);
+    c10::cuda::CUDAGuard guard(scores.device());
+    Tensor len = resolve_lengths(lengths, s, scores.device());
+    Param po, pe, pT;
+    po.host = (float)gap_open;
+    pe.host = (float)gap_ext;
+    pT.host = (float)temperature;
+    AffFwd r = aff_forward(scores, po, pe, pT, len, s);
+    return {r.value, r.marginals, r.dparams[0], r.dparams[1], r.dparams[2]};
+}
+
+Tensor soft_sw_affine_hvp_cuda(Tensor scores, Tensor tangent, double gap_open, double gap_ext,
+                               double temperature, c10::optional<Tensor> lengths) {
+    D2PB_CHECK_INPUT(scores);
+    D2PB_CHECK_INPUT(tangent);
+    TORCH_CHECK(scores.dim() == 3, "scores must be 3D");
+    TORCH_CHECK(scores.sizes() == tangent.sizes(), "scores and tangent must have same shape");
+    TORCH_CHECK(tangent.device() == scores.device(), "tangent must be on same device as scores, got ",
+                tangent.device(), " vs ", scores.device());
+    const Shape s = checked_shape(scores);
+    c10::cuda::CUDAGuard guard(scores.device());
+    Tensor len = resolve_lengths(lengths, s, scores.device());
+    return aff_hvp_raw(scores, tangent, (float)gap_open, (float)gap_ext, (float)temperature, len, s);
+}
+
+Tensor soft_sw_affine_param_jacobian_cuda(Tensor scores, int64_t param_type, double gap_open,
+                                          double gap_ext, double temperature,
+                                          c10::optional<Tensor> lengths) {
+    D2PB_CHECK_INPUT(scores);
+    TORCH_CHECK(scores.dim() == 3, "scores must be 3D");
+    TORCH_CHECK(param_type >= 0 && param_type <= 2, "param_type must be 0, 1, or 2");
+    const Shape s = checked_shape(scores);
+    c10::cuda::CUDAGuard guard(scores.device());
+    Tensor len = resolve_lengths(lengths, s, scores.device());
+    return aff_jac_raw(scores, (int)param_type, (float)gap_open, (float)gap_ext, (float)temperature, len, s);
+}
+
+std::tuple<Tensor, Tensor, Tensor, Tensor> soft_sw_affine_backward_full_cuda(
+    Tensor scores, Tensor grad_alignment, double gap_open, double gap_ext, double temperature,
+    c10::optional<Tensor> lengths) {
+    D2PB_CHECK_INPUT(scores);
+    TORCH_CHECK(scores.dim() == 3, "scores must be 3D (B, L1, L2)");
+    TORCH_CHECK(grad_alignment.sizes() == scores.sizes(), "grad_alignment must have same shape as scores");
+    TORCH_CHECK(grad_alignment.is_cuda(), "grad_alignment must be a CUDA tensor");
+    TORCH_CHECK(grad_alignment.device() == scores.device(),
+                "grad_alignment must be on same device as scores, got ", grad_alignment.device(), " vs ",
+                scores.device());
+    const Shape s = checked_shape(scores);
+    c10::cuda::CUDAGuard guard(scores.device());
+    Tensor len = resolve_lengths(lengths, s, scores.device());
+    Tensor G = grad_alignment.contiguous();
+    if (G.scalar_type() != torch::kFloat32) G = G.to(torch::kFloat32);
+    return aff_backward_full_raw(scores, G, (float)gap_open, (float)gap_ext, (float)temperature, len, s);
+}
+
+// namespaced aliases (src/sw_affine/torch_cuda.cpp:820-911)
+std::vector<Tensor> sw_affine_forward_cuda(Tensor scores, double go, double ge, double temp,
+                                           c10::optional<Tensor> lengths) {
+    return soft_sw_affine_float_cuda(scores, go, ge, temp, lengths);
+}
+std::vector<Tensor> sw_affine_forward_t_cuda(Tensor scores, Tensor go, Tensor ge, Tensor temp, Tensor lengths) {
+    return soft_sw_affine_cuda(scores, go, ge, temp, lengths);
+}
+std::tuple<Tensor, Tensor, Tensor> sw_affine_value_grad_params_cuda(Tensor scores, double go, double ge,
+                                                                    double temp, c10::optional<Tensor> lengths) {
+    auto r = soft_sw_affine_with_grads_cuda(scores, go, ge, temp, lengths);
+    return {std::get<2>(r), std::get<3>(r), std::get<4>(r)};
+}
+std::tuple<Tensor, Tensor, Tensor, Tensor> sw_affine_marginals_backward_cuda(Tensor scores, Tensor g,
+                                                                             double go, double ge,
+                                                                             double temp,
+                                                                             c10::optional<Tensor> lengths) {
+    return soft_sw_affine_backward_full_cuda(scores, g, go, ge, temp, lengths);
+}
+Tensor sw_affine_marginals_hvp_cuda(Tensor scores, Tensor v, double go, double ge, double temp,
+                                    c10::optional<Tensor> lengths) {
+    return soft_sw_affine_hvp_cuda(scores, v, go, ge, temp, lengths);
+}
+Tensor sw_affine_marginals_grad_gap_open_cuda(Tensor scores, double go, double ge, double temp,
+                                              c10::optional<Tensor> lengths) {
+    return soft_sw_affine_param_jacobian_cuda(scores, 0, go, ge, temp, lengths);
+}
+Tensor sw_affine_marginals_grad_gap_ext_cuda(Tensor scores, double go, double ge, double temp,
+                                             c10::optional<Tensor> lengths) {
+    return soft_sw_affine_param_jacobian_cuda(scores, 1, go, ge, temp, lengths);
+}
+Tensor sw_affine_marginals_grad_temp_cuda(Tensor scores, double go, double ge, double temp,
+                                          c10::optional<Tensor> lengths) {
+    return soft_sw_affine_param_jacobian_cuda(scores, 2, go, ge, temp, lengths);
+}
+
+}  // namespace
+
+// =============================================================================
+// schemas (verbatim from the reference registries) and implementations
+// =============================================================================
+TORCH_LIBRARY_FRAGMENT(d2p, m) {
+    // src/sw/registry.cpp:30-44
+    m.def("soft_sw(Tensor scores, Tensor gap, Tensor temperature, Tensor lengths) -> Tensor[]");
+    m.def("soft_sw_float(Tensor scores, float gap, float temperature, Tensor? lengths) -> Tensor[]");
+    m.def("soft_sw_with_grads(Tensor scores, float gap, float temperature, Tensor? lengths) -> (Tensor, Tensor, Tensor, Tensor)");
+    m.def("soft_sw_hvp(Tensor scores, Tensor tangent, float gap, float temperature, Tensor? lengths) -> Tensor");
+    m.def("soft_sw_param_jacobian(Tensor scores, int param_type, float gap, float temperature, Tensor? lengths) -> Tensor");
+    m.def("soft_sw_backward_full(Tensor scores, Tensor grad_alignment, float gap, float temperature, Tensor? lengths) -> (Tensor, Tensor, Tensor)");
+    m.def("sw_forward(Tensor scores, float gap, float temp, Tensor? lengths) -> Tensor[]");
+    m.def("sw_forward_t(Tensor scores, Tensor gap, Tensor temp, Tensor lengths) -> Tensor[]");
+    m.def("sw_value_grad_params(Tensor scores, float gap, float temp, Tensor? lengths) -> (Tensor, Tensor)");
+    m.def("sw_marginals_backward(Tensor scores, Tensor grad_marginals, float gap, float temp, Tensor? lengths) -> (Tensor, Tensor, Tensor)");
+    m.def("sw_marginals_hvp(Tensor scores, Tensor v, float gap, float temp, Tensor? lengths) -> Tensor");
+    m.def("sw_marginals_grad_gap(Tensor scores, float gap, float temp, Tensor? lengths) -> Tensor");
+    m.def("sw_marginals_grad_temp(Tensor scores, float gap, float temp, Tensor? lengths) -> Tensor");
+    // src/sw_affine/registry.cpp:27-42
+    m.def("soft_sw_affine(Tensor scores, Tensor gap_open, Tensor gap_ext, Tensor temperature, Tensor lengths) -> Tensor[]");
+    m.def("soft_sw_affine_float(Tensor scores, float gap_open, float gap_ext, float temperature, Tensor? lengths) -> Tensor[]");
+    m.def("soft_sw_affine_with_grads(Tensor scores, float gap_open, float gap_ext, float temperature, Tensor? lengths) -> (Tensor, Tensor, Tensor, Tensor, Tensor)");
+    m.def("soft_sw_affine_hvp(Tensor scores, Tensor tangent, float gap_open, float gap_ext, float temperature, Tensor? lengths) -> Tensor");
+    m.def("soft_sw_affine_param_jacobian(Tensor scores, int param_type, float gap_open, float gap_ext, float temperature, Tensor? lengths) -> Tensor");
+    m.def("soft_sw_affine_backward_full(Tensor scores, Tensor grad_alignment, float gap_open, float gap_ext, float temperature, Tensor? lengths) -> (Tensor, Tensor, Tensor, Tensor)");
+    m.def("sw_affine_forward(Tensor scores, float gap_open, float gap_ext, float temp, Tensor? lengths) -> Tensor[]");
+    m.def("sw_affine_forward_t(Tensor scores, Tensor gap_open, Tensor gap_ext, Tensor temp, Tensor lengths) -> Tensor[]");
+    m.def("sw_affine_value_grad_params(Tensor scores, float gap_open, float gap_ext, float temp, Tensor? lengths) -> (Tensor, Tensor, Tensor)");
+    m.def("sw_affine_marginals_backward(Tensor scores, Tensor grad_marginals, float gap_open, float gap_ext, float temp, Tensor? lengths) -> (Tensor, Tensor, Tensor, Tensor)");
+    m.def("sw_affine_marginals_hvp(Tensor scores, Tensor v, float gap_open, float gap_ext, float temp, Tensor? lengths) -> Tensor");
+    m.def("sw_affine_marginals_grad_gap_open(Tensor scores, float gap_open, float gap_ext, float temp, Tensor? lengths) -> Tensor");
+    m.def("sw_affine_marginals_grad_gap_ext(Tensor scores, float gap_open, float gap_ext, float temp, Tensor? lengths) -> Tensor");
+    m.def("sw_affine_marginals_grad_temp(Tensor scores, float gap_open, float gap_ext, float temp, Tensor? lengths) -> Tensor");
+}
+
+TORCH_LIBRARY_IMPL(d2p, CUDA, m) {
+    m.impl("soft_sw", soft_sw_cuda);
+    m.impl("soft_sw_float", soft_sw_float_cuda);
+    m.impl("soft_sw_with_grads", soft_sw_with_grads_cuda);
+    m.impl("soft_sw_hvp", soft_sw_hvp_cuda);
+    m.impl("soft_sw_param_jacobian", soft_sw_param_jacobian_cuda);
+    m.impl("soft_sw_backward_full", soft_sw_backward_full_cuda);
+    m.impl("sw_forward", sw_forward_cuda);
+    m.impl("sw_forward_t", sw_forward_t_cuda);
+    m.impl("sw_value_grad_params", sw_value_grad_params_cuda);
+    m.impl("sw_marginals_backward", sw_marginals_backward_cuda);
+    m.impl("sw_marginals_hvp", sw_marginals_hvp_cuda);
+    m.impl("sw_marginals_grad_gap", sw_marginals_grad_gap_cuda);
+    m.impl("sw_marginals_grad_temp", sw_marginals_grad_temp_cuda);
+    m.impl("soft_sw_affine", soft_sw_affine_cuda);
+    m.impl("soft_sw_affine_float", soft_sw_affine_float_cuda);
+    m.impl("soft_sw_affine_with_grads", soft_sw_affine_with_grads_cuda);
+    m.impl("soft_sw_affine_hvp", soft_sw_affine_hvp_cuda);
+    m.impl("soft_sw_affine_param_jacobian", soft_sw_affine_param_jacobian_cuda);
+    m.impl("soft_sw_affine_backward_full", soft_sw_affine_backward_full_cuda);
+    m.impl("sw_affine_forward", sw_affine_forward_cuda);
+    m.impl("sw_affine_forward_t", sw_affine_forward_t_cuda);
+    m.impl("sw_affine_value_grad_params", sw_affine_value_grad_params_cuda);
+    m.impl("sw_affine_marginals_backward", sw_affine_marginals_backward_cuda);
+    m.impl("sw_affine_marginals_hvp", sw_affine_marginals_hvp_cuda);
+    m.impl("sw_affine_marginals_grad_gap_open", sw_affine_marginals_grad_gap_open_cuda);
+    m.impl("sw_affine_marginals_grad_gap_ext", sw_affine_marginals_grad_gap_ext_cuda);
+    m.impl("sw_affine_marginals_grad_temp", sw_affine_marginals_grad_temp_cuda);
+}
+
+// No CPU kernels by design: CPU tensors get a clear error instead of a silent
+// fallback (the reference's CPU path is used only as the test oracle).
+void reject_cpu(const c10::OperatorHandle& op, torch::jit::Stack*) {
+    TORCH_CHECK(false, op.schema().name(),
+                ": scores must be a CUDA tensor (d2p_b200 implements the soft Smith-Waterman "
+                "operators for CUDA devices only)");
+}
+
+TORCH_LIBRARY_IMPL(d2p, CPU, m) {
+    static const char* kOps[] = {
+        "soft_sw", "soft_sw_float", "soft_sw_with_grads", "soft_sw_hvp", "soft_sw_param_jacobian",
+        "soft_sw_backward_full", "sw_forward", "sw_forward_t", "sw_value_grad_params",
+        "sw_marginals_backward", "sw_marginals_hvp", "sw_marginals_grad_gap", "sw_marginals_grad_temp",
+        "soft_sw_affine", "soft_sw_affine_float", "soft_sw_affine_with_grads", "soft_sw_affine_hvp",
+        "soft_sw_affine_param_jacobian", "soft_sw_affine_backward_full", "sw_affine_forward",
+        "sw_affine_forward_t", "sw_affine_value_grad_params", "sw_affine_marginals_backward",
+        "sw_affine_marginals_hvp", "sw_affine_marginals_grad_gap_open", "sw_affine_marginals_grad_gap_ext",
+        "sw_affine_marginals_grad_temp"};
+    for (const char* name : kOps) m.impl(name, torch::CppFunction::makeFromBoxedFunction<&reject_cpu>());
+}
+
+TORCH_LIBRARY_IMPL(d2p, AutogradCUDA, m) {
+    m.impl("soft_sw", soft_sw_cuda);
+    m.impl("soft_sw_float", soft_sw_float_cuda);
+    m.impl("sw_forward", sw_forward_cuda);
+    m.impl("sw_forward_t", sw_forward_t_cuda);
+    m.impl("soft_sw_affine", soft_sw_affine_cuda);
+    m.impl("soft_sw_affine_float", soft_sw_affine_float_cuda);
+    m.impl("sw_affine_forward", sw_affine_forward_cuda);
+    m.impl("sw_affine_forward_t", sw_affine_forward_t_cuda);
+}

@@ -1,0 +1,27 @@
+"""Low-level operator access (d2p/ops/__init__.py): ``ops.sw``, ``ops.sw_affine`` and
+the flat op wrappers of the soft Smith-Waterman family."""
+from . import sw, sw_affine
+from .._ops import (  # noqa: F401
+    d2p,
+    soft_sw, soft_sw_float, soft_sw_with_grads, soft_sw_hvp, soft_sw_param_jacobian, soft_sw_backward_full,
+    soft_sw_affine, soft_sw_affine_float, soft_sw_affine_with_grads, soft_sw_affine_hvp,
+    soft_sw_affine_param_jacobian, soft_sw_affine_backward_full,
+    sw_forward, sw_forward_t, sw_value_grad_params, sw_marginals_backward, sw_marginals_hvp,
+    sw_marginals_grad_gap, sw_marginals_grad_temp,
+    sw_affine_forward, sw_affine_forward_t, sw_affine_value_grad_params, sw_affine_marginals_backward,
+    sw_affine_marginals_hvp, sw_affine_marginals_grad_gap_open, sw_affine_marginals_grad_gap_ext,
+    sw_affine_marginals_grad_temp,
+)
+
+__all__ = [
+    "sw", "sw_affine", "d2p",
+    "soft_sw", "soft_sw_float", "soft_sw_with_grads", "soft_sw_hvp", "soft_sw_param_jacobian",
+    "soft_sw_backward_full",
+    "soft_sw_affine", "soft_sw_affine_float", "soft_sw_affine_with_grads", "soft_sw_affine_hvp",
+    "soft_sw_affine_param_jacobian", "soft_sw_affine_backward_full",
+    "sw_forward", "sw_forward_t", "sw_value_grad_params", "sw_marginals_backward", "sw_marginals_hvp",
+    "sw_marginals_grad_gap", "sw_marginals_grad_temp",
+    "sw_affine_forward", "sw_affine_forward_t", "sw_affine_value_grad_params", "sw_affine_marginals_backward",
+    "sw_affine_marginals_hvp", "sw_affine_marginals_grad_gap_open", "sw_affine_marginals_grad_gap_ext",
+    "sw_affine_marginals_grad_temp",
+]

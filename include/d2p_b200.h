@@ -1,0 +1,163 @@
+/*
+ * d2p_b200.h -- C ABI of the B200-native soft Smith-Waterman operator family.
+ *
+ * Plain pointers and sizes only (no torch types).  Every pointer argument is a
+ * device pointer on the current CUDA device unless stated otherwise; `stream`
+ * is a cudaStream_t passed as void* (NULL = legacy default stream).  All entry
+ * points are asynchronous with respect to the host (no stream synchronisation)
+ * and capturable in a CUDA graph once the workspace is allocated.
+ *
+ * Layouts follow the reference operators (d2p, src/sw/registry.cpp:30-44):
+ *   scores, tangent, marginals, hvp, jacobian, grad_* planes : [B, L1, L2] row-major
+ *   lengths : [B, 2] int32 (L1_b, L2_b) with 0 <= L1_b <= L1, 0 <= L2_b <= L2,
+ *             or NULL for full lengths.  Out-of-range lengths are clamped on the
+ *             device; callers wanting the reference's error messages validate
+ *             on the host first (the torch binding does).
+ *   value, grad_gap, grad_temperature, ... (per problem) : [B] fp32
+ * Padded cells (i >= L1_b or j >= L2_b) of every [B,L1,L2] output are written
+ * as exact zeros.
+ *
+ * Return value: 0 on success; a cudaError_t value (1..999) when a CUDA call
+ * fails; or one of the D2P_ERR_* codes below.  d2p_error_string() describes a code.
+ *
+ * Workspace: each operator needs a device scratch buffer of at least
+ * d2p_sw_workspace_bytes(family, op, B, L1, L2) bytes (256-byte aligned).
+ */
+#ifndef D2P_B200_H
+#define D2P_B200_H
+
+#include <stddef.h>
+
+#if defined(__GNUC__)
+#define D2P_API __attribute__((visibility("default")))
+#else
+#define D2P_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define D2P_OK 0
+#define D2P_ERR_INVALID_ARGUMENT 1001
+#define D2P_ERR_WORKSPACE_TOO_SMALL 1002
+#define D2P_ERR_TOO_LARGE 1003
+#define D2P_ERR_DEVICE_STATUS 1004
+
+#define D2P_DTYPE_F32 0
+#define D2P_DTYPE_BF16 1
+
+#define D2P_FAMILY_LINEAR 0
+#define D2P_FAMILY_AFFINE 1
+
+#define D2P_OP_FORWARD_BACKWARD 0
+#define D2P_OP_HVP 1
+#define D2P_OP_PARAM_JACOBIAN 2
+#define D2P_OP_BACKWARD_FULL 3
+
+/* Library version (major*10000 + minor*100 + patch). */
+D2P_API int d2p_version(void);
+
+/* Human-readable description of a return code (static storage). */
+D2P_API const char* d2p_error_string(int code);
+
+/* Scratch bytes needed by operator `op` of `family` at this problem size
+ * (0 if none).  Returns (size_t)-1 when the size is not supported. */
+D2P_API size_t d2p_sw_workspace_bytes(int family, int op, int B, int L1, int L2);
+
+/* ------------------------------------------------------------------------
+ * Linear gap (reference family src/sw)
+ * --------------------------------------------------------------------- */
+
+/* value[b] = S_b (log partition), marginals = dS/dscores, grad_gap[b] = dS/dgap,
+ * grad_temperature[b] = dS/dT.  Any output pointer may be NULL.  gap_dev /
+ * temperature_dev, when non-NULL, are device scalars that override the host
+ * values (graph-capturable learnable parameters).
+ * Replaces: sw_regular_forward / sw_regular_forward_warp + sw_regular_backward /
+ * sw_regular_backward_warp (reference src/sw/kernels.cuh:139-235) as driven by
+ * soft_sw_regular_cuda_with_grads (src/sw/torch_cuda.cpp:450-504). */
+D2P_API int d2p_sw_forward_backward(const float* scores, const int* lengths, int B, int L1, int L2,
+                            float gap, float temperature, const float* gap_dev,
+                            const float* temperature_dev, float* value, float* marginals,
+                            float* grad_gap, float* grad_temperature, void* workspace,
+                            size_t workspace_bytes, void* stream);
+
+/* hvp = d(marginals)/d(scores) . tangent.
+ * Replaces: sw_regular_forward + sw_regular_hvp (src/sw/kernels.cuh:237-270) as
+ * driven by soft_sw_regular_hvp_cuda (src/sw/torch_cuda.cpp:507-570). */
+D2P_API int d2p_sw_hvp(const float* scores, const float* tangent, const int* lengths, int B, int L1,
+               int L2, float gap, float temperature, float* hvp, void* workspace,
+               size_t workspace_bytes, void* stream);
+
+/* jacobian = d(marginals)/d(theta), theta = gap (param_type 0) or temperature (1).
+ * Replaces: sw_regular_forward + sw_regular_backward + sw_regular_param_grad
+ * (src/sw/kernels.cuh:272-285) as driven by soft_sw_regular_param_jacobian_cuda
+ * (src/sw/torch_cuda.cpp:573-662). */
+D2P_API int d2p_sw_param_jacobian(const float* scores, const int* lengths, int B, int L1, int L2,
+                          int param_type, float gap, float temperature, float* jacobian,
+                          void* workspace, size_t workspace_bytes, void* stream);
+
+/* Gradient of <grad_marginals, marginals> w.r.t. scores, gap and temperature:
+ * grad_scores [B,L1,L2], grad_gap [1], grad_temperature [1] (device).
+ * Replaces: soft_sw_backward_full_cuda (src/sw/torch_cuda.cpp:665-771). */
+D2P_API int d2p_sw_backward_full(const float* scores, const float* grad_marginals, const int* lengths,
+                         int B, int L1, int L2, float gap, float temperature, float* grad_scores,
+                         float* grad_gap, float* grad_temperature, void* workspace,
+                         size_t workspace_bytes, void* stream);
+
+/* Value-branch backward shared by both families:
+ * grad_scores[b,i,j] = grad_value[b] * marginals[b,i,j];
+ * grad_params[p] = sum_b grad_value[b] * dvalue_dparams[p*B + b], p < n_params.
+ * grad_params / dvalue_dparams may be NULL when n_params == 0.
+ * Replaces: the value branch of SoftSWRegularCUDAFunction::backward
+ * (src/sw/torch_cuda.cpp:292-321) and SoftSWAffineCUDAFunction::backward
+ * (src/sw_affine/torch_cuda.cpp:250-290). */
+D2P_API int d2p_sw_value_backward(const float* grad_value, const float* marginals,
+                          const float* dvalue_dparams, int n_params, int B, int L1, int L2,
+                          float* grad_scores, float* grad_params, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Affine gap (reference family src/sw_affine); parameters (gap_open, gap_ext, T)
+ * --------------------------------------------------------------------- */
+
+/* scores_dtype: D2P_DTYPE_F32 or D2P_DTYPE_BF16 (bf16 scores are upcast in
+ * registers; all arithmetic is fp32).
+ * Replaces: sw_affine_forward + sw_affine_backward (src/sw_affine/kernels.cuh:165-223)
+ * as driven by soft_sw_affine_cuda_with_grads (src/sw_affine/torch_cuda.cpp:445-505). */
+D2P_API int d2p_sw_affine_forward_backward(const void* scores, int scores_dtype, const int* lengths,
+                                   int B, int L1, int L2, float gap_open, float gap_ext,
+                                   float temperature, const float* gap_open_dev,
+                                   const float* gap_ext_dev, const float* temperature_dev,
+                                   float* value, float* marginals, float* grad_gap_open,
+                                   float* grad_gap_ext, float* grad_temperature, void* workspace,
+                                   size_t workspace_bytes, void* stream);
+
+/* Replaces: sw_affine_forward + sw_affine_hvp (src/sw_affine/kernels.cuh:225-254) as
+ * driven by soft_sw_affine_hvp_cuda (src/sw_affine/torch_cuda.cpp:508-577). */
+D2P_API int d2p_sw_affine_hvp(const float* scores, const float* tangent, const int* lengths, int B,
+                      int L1, int L2, float gap_open, float gap_ext, float temperature,
+                      float* hvp, void* workspace, size_t workspace_bytes, void* stream);
+
+/* param_type 0 = gap_open, 1 = gap_ext, 2 = temperature.
+ * Replaces: sw_affine_forward + sw_affine_backward + sw_affine_param_grad
+ * (src/sw_affine/kernels.cuh:256-269) as driven by soft_sw_affine_param_jacobian_cuda
+ * (src/sw_affine/torch_cuda.cpp:580-677). */
+D2P_API int d2p_sw_affine_param_jacobian(const float* scores, const int* lengths, int B, int L1, int L2,
+                                 int param_type, float gap_open, float gap_ext,
+                                 float temperature, float* jacobian, void* workspace,
+                                 size_t workspace_bytes, void* stream);
+
+/* grad_scores [B,L1,L2], grad_gap_open [1], grad_gap_ext [1], grad_temperature [1].
+ * Replaces: soft_sw_affine_backward_full_cuda (src/sw_affine/torch_cuda.cpp:680-817). */
+D2P_API int d2p_sw_affine_backward_full(const float* scores, const float* grad_marginals,
+                                const int* lengths, int B, int L1, int L2, float gap_open,
+                                float gap_ext, float temperature, float* grad_scores,
+                                float* grad_gap_open, float* grad_gap_ext,
+                                float* grad_temperature, void* workspace,
+                                size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* D2P_B200_H */

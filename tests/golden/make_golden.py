@@ -1,0 +1,68 @@
+"""Generate the golden fixtures in tests/golden/ from the REFERENCE's own CPU
+kernels (src/sw/kernels_cpu.cpp, src/sw_affine/kernels_cpu.cpp compiled from the
+reference sources into oracle/_ref/libref_sw_cpu.so by oracle/Makefile).
+
+Run in a container where the reference sources are present:
+    make -C oracle && python tests/golden/make_golden.py
+Inputs are seeded (torch.Generator) so the fixtures are reproducible; each .npz
+holds the inputs and the reference outputs of every operator mode.
+"""
+import os
+import sys
+
+import zlib
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+import oracle  # noqa: E402
+
+CASES = [
+    # name, B, L1, L2, T, linear gap, (affine open, ext), with_lengths
+    ("small_t1", 2, 7, 9, 1.0, -1.0, (-2.0, -0.5), False),
+    ("ragged_t05", 3, 12, 10, 0.5, -0.5, (-1.7, -0.4), True),
+    ("sharp_t01", 2, 6, 11, 0.1, -1.0, (-2.0, -0.5), False),
+    ("row1", 2, 1, 8, 1.0, -1.0, (-2.0, -0.5), False),
+]
+
+
+def main():
+    assert oracle.ref_available(), "reference CPU build missing: run `make -C oracle` with the reference present"
+    oracle.set_threads(1)
+    for name, B, L1, L2, T, gap, (go, ge), with_len in CASES:
+        g = torch.Generator().manual_seed(zlib.crc32(name.encode()))
+        s = torch.randn(B, L1, L2, generator=g).numpy()
+        V = torch.randn(B, L1, L2, generator=g).numpy()
+        G = torch.randn(B, L1, L2, generator=g).numpy()
+        ln = None
+        if with_len:
+            l1 = torch.randint(1, L1 + 1, (B,), generator=g)
+            l2 = torch.randint(1, L2 + 1, (B,), generator=g)
+            ln = torch.stack([l1, l2], 1).to(torch.int32).numpy()
+        out = dict(scores=s, tangent=V, grad_marginals=G, T=np.float32(T), gap=np.float32(gap),
+                   gap_open=np.float32(go), gap_ext=np.float32(ge),
+                   lengths=ln if ln is not None else np.zeros((0, 2), np.int32))
+        r = oracle.sw_linear(s, ln, gap, T, "ref")
+        for k in ("value", "marginals", "grad_gap", "grad_T"):
+            out["lin_" + k] = r[k]
+        out["lin_hvp"] = oracle.sw_linear_hvp(s, V, ln, gap, T, "ref")
+        out["lin_jac0"] = oracle.sw_linear_param_jacobian(s, 0, ln, gap, T, "ref")
+        out["lin_jac1"] = oracle.sw_linear_param_jacobian(s, 1, ln, gap, T, "ref")
+        bf = oracle.sw_linear_backward_full(s, G, ln, gap, T, "ref")
+        out["lin_bf_scores"], out["lin_bf_gap"], out["lin_bf_T"] = bf
+        r = oracle.sw_affine(s, ln, go, ge, T, "ref")
+        for k in ("value", "marginals", "grad_open", "grad_ext", "grad_T"):
+            out["aff_" + k] = r[k]
+        out["aff_hvp"] = oracle.sw_affine_hvp(s, V, ln, go, ge, T, "ref")
+        for p in range(3):
+            out[f"aff_jac{p}"] = oracle.sw_affine_param_jacobian(s, p, ln, go, ge, T, "ref")
+        bf = oracle.sw_affine_backward_full(s, G, ln, go, ge, T, "ref")
+        out["aff_bf_scores"], out["aff_bf_open"], out["aff_bf_ext"], out["aff_bf_T"] = bf
+        np.savez_compressed(os.path.join(HERE, name + ".npz"), **out)
+        print("wrote", name)
+
+
+if __name__ == "__main__":
+    main()

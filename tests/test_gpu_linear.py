@@ -1,0 +1,135 @@
+"""GPU parity of the linear-gap soft Smith-Waterman ops against the CPU oracle.
+
+Every case calls the product through torch.ops.d2p (which calls the C ABI in
+libd2p_b200.so) and compares with oracle/ (fp64 restatement of the reference
+algorithm; the fp32 restatement is bit-identical to the reference's own CPU
+kernels, see tests/test_oracle_golden.py).
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from tests._parity import check, lengths_for, scores
+
+pytestmark = pytest.mark.gpu
+
+CASES = [  # (B, L1, L2, T, gap)
+    (1, 8, 10, 1.0, -1.0),
+    (4, 16, 16, 0.1, -1.0),
+    (2, 5, 20, 2.0, -1.0),
+    (3, 33, 47, 0.5, -0.5),
+    (2, 100, 120, 1.0, -1.0),   # BASELINE config 1 shape
+    (2, 1, 7, 1.0, -1.0),
+    (2, 9, 1, 0.7, -1.3),
+]
+
+
+@pytest.fixture(scope="module")
+def d2p():
+    import d2p_b200
+
+    return d2p_b200
+
+
+@pytest.mark.parametrize("B,L1,L2,T,gap", CASES)
+def test_forward_backward(d2p, cuda_device, B, L1, L2, T, gap):
+    s = scores(B, L1, L2, seed=B * 1000 + L1)
+    v, m, gg, gt = torch.ops.d2p.soft_sw_with_grads(s.to(cuda_device), gap, T, None)
+    r64 = oracle.sw_linear(s.numpy(), None, gap, T, "f64")
+    r32 = oracle.sw_linear(s.numpy(), None, gap, T, "f32")
+    check("value", v, r64["value"], r32["value"])
+    check("marginals", m, r64["marginals"], r32["marginals"])
+    check("grad_gap", gg, r64["grad_gap"], r32["grad_gap"], rtol=1e-4, atol=1e-5)
+    check("grad_T", gt, r64["grad_T"], r32["grad_T"], rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.parametrize("B,L1,L2,T,gap", CASES[:5])
+def test_variable_lengths_and_padding(d2p, cuda_device, B, L1, L2, T, gap):
+    s = scores(B, L1, L2, seed=7)
+    ln = lengths_for(B, L1, L2, seed=11)
+    v, m, gg, gt = torch.ops.d2p.soft_sw_with_grads(s.to(cuda_device), gap, T, ln.to(cuda_device))
+    r64 = oracle.sw_linear(s.numpy(), ln.numpy(), gap, T, "f64")
+    r32 = oracle.sw_linear(s.numpy(), ln.numpy(), gap, T, "f32")
+    check("value", v, r64["value"], r32["value"])
+    check("marginals", m, r64["marginals"], r32["marginals"])
+    mc = m.cpu()
+    for b, (l1, l2) in enumerate(ln.tolist()):
+        assert torch.count_nonzero(mc[b, l1:, :]) == 0
+        assert torch.count_nonzero(mc[b, :, l2:]) == 0
+
+
+@pytest.mark.parametrize("B,L1,L2,T,gap", CASES[:5])
+def test_hvp(d2p, cuda_device, B, L1, L2, T, gap):
+    s = scores(B, L1, L2, seed=3)
+    V = scores(B, L1, L2, seed=4)
+    H = torch.ops.d2p.soft_sw_hvp(s.to(cuda_device), V.to(cuda_device), gap, T, None)
+    h64 = oracle.sw_linear_hvp(s.numpy(), V.numpy(), None, gap, T, "f64")
+    h32 = oracle.sw_linear_hvp(s.numpy(), V.numpy(), None, gap, T, "f32")
+    check("hvp", H, h64, h32, rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.parametrize("param_type", [0, 1])
+@pytest.mark.parametrize("B,L1,L2,T,gap", CASES[:5])
+def test_param_jacobian(d2p, cuda_device, B, L1, L2, T, gap, param_type):
+    s = scores(B, L1, L2, seed=5)
+    J = torch.ops.d2p.soft_sw_param_jacobian(s.to(cuda_device), param_type, gap, T, None)
+    j64 = oracle.sw_linear_param_jacobian(s.numpy(), param_type, None, gap, T, "f64")
+    j32 = oracle.sw_linear_param_jacobian(s.numpy(), param_type, None, gap, T, "f32")
+    check(f"jac{param_type}", J, j64, j32, rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.parametrize("B,L1,L2,T,gap", CASES[:4])
+def test_backward_full(d2p, cuda_device, B, L1, L2, T, gap):
+    s = scores(B, L1, L2, seed=8)
+    G = scores(B, L1, L2, seed=9)
+    gs, gg, gt = torch.ops.d2p.soft_sw_backward_full(s.to(cuda_device), G.to(cuda_device), gap, T, None)
+    r64 = oracle.sw_linear_backward_full(s.numpy(), G.numpy(), None, gap, T, "f64")
+    r32 = oracle.sw_linear_backward_full(s.numpy(), G.numpy(), None, gap, T, "f32")
+    check("grad_scores", gs, r64[0], r32[0], rtol=1e-4, atol=1e-5)
+    check("grad_gap", gg, r64[1], r32[1], rtol=1e-4, atol=1e-4)
+    check("grad_T", gt, r64[2], r32[2], rtol=1e-4, atol=1e-4)
+
+
+def test_autograd_value_sum(d2p, cuda_device):
+    s = scores(4, 30, 41, seed=21).to(cuda_device).requires_grad_(True)
+    res = d2p.soft_sw(s, gap=-1.0, temperature=1.0)
+    res.value.sum().backward()
+    assert torch.equal(s.grad, res.marginals.detach())
+
+
+def test_autograd_tensor_params(d2p, cuda_device):
+    s0 = scores(3, 12, 17, seed=22)
+    s = s0.to(cuda_device).requires_grad_(True)
+    gap = torch.tensor([-1.0], device=cuda_device, requires_grad=True)
+    T = torch.tensor([0.8], device=cuda_device, requires_grad=True)
+    res = d2p.soft_sw(s, gap=gap, temperature=T)
+    w = torch.linspace(0.5, 1.5, 3, device=cuda_device)
+    (res.value * w).sum().backward()
+    r64 = oracle.sw_linear(s0.numpy(), None, -1.0, 0.8, "f64")
+    wn = w.cpu().numpy().astype(np.float64)
+    check("dgap", gap.grad, np.array([(wn * r64["grad_gap"]).sum()]), rtol=1e-4, atol=1e-5)
+    check("dT", T.grad, np.array([(wn * r64["grad_T"]).sum()]), rtol=1e-4, atol=1e-5)
+    check("dscores", s.grad, wn[:, None, None] * r64["marginals"])
+
+
+def test_autograd_through_marginals(d2p, cuda_device):
+    s0 = scores(2, 10, 13, seed=23)
+    G = scores(2, 10, 13, seed=24)
+    s = s0.to(cuda_device).requires_grad_(True)
+    gap = torch.tensor([-1.0], device=cuda_device, requires_grad=True)
+    T = torch.tensor([1.0], device=cuda_device, requires_grad=True)
+    res = d2p.soft_sw(s, gap=gap, temperature=T)
+    (res.marginals * G.to(cuda_device)).sum().backward()
+    r64 = oracle.sw_linear_backward_full(s0.numpy(), G.numpy(), None, -1.0, 1.0, "f64")
+    check("dscores", s.grad, r64[0], rtol=1e-4, atol=1e-5)
+    check("dgap", gap.grad, r64[1], rtol=1e-4, atol=1e-4)
+    check("dT", T.grad, r64[2], rtol=1e-4, atol=1e-4)
+
+
+def test_repeatable_bitwise(d2p, cuda_device):
+    s = scores(8, 40, 37, seed=30).to(cuda_device)
+    a = torch.ops.d2p.soft_sw_with_grads(s, -1.0, 1.0, None)
+    b = torch.ops.d2p.soft_sw_with_grads(s, -1.0, 1.0, None)
+    for x, y in zip(a, b):
+        assert torch.equal(x, y)
