@@ -407,7 +407,7 @@ def cpu_baseline(cfg, seconds: float, cores=None):
 
 def args_config_name(cfg):
     for k, v in CONFIGS.items():
-        if v is cfg:
+        if v["desc"] == cfg["desc"]:
             return k
     return "custom"
 
@@ -467,10 +467,14 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     ap.add_argument("--ref-step-seconds", type=float, default=6.0)
+    ap.add_argument("--batch", type=int, default=0, help="override the per-rank batch (profiling on a small case)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    cfg = CONFIGS[args.config]
+    cfg = dict(CONFIGS[args.config])
+    if args.batch > 0:
+        cfg["B"] = args.batch
+        cfg["desc"] = cfg["desc"] + f" (batch overridden to {args.batch})"
     if args.impl == "reference":
         run_reference(args, cfg)
     else:

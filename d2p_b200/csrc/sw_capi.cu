@@ -5,6 +5,8 @@
 // value+marginals path) and sw_elementwise.cu.
 #include <limits.h>
 #include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
 
 #include "../../include/d2p_b200.h"
 #include "sw_internal.h"
@@ -18,6 +20,15 @@ int launch_wavefront(const SwArgs& a, int family, size_t ws_bytes, cudaStream_t 
 constexpr int kNotHandled = -1;
 
 static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+bool engine_forced_plane() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("D2P_B200_ENGINE");
+        v = (e && strcmp(e, "plane") == 0) ? 1 : 0;
+    }
+    return v == 1;
+}
 
 static bool dims_ok(int B, int L1, int L2) {
     if (B < 0 || L1 < 0 || L2 < 0) return false;

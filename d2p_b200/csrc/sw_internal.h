@@ -54,6 +54,10 @@ struct SwArgs {
 };
 
 int launch_lin_plane(const SwArgs& a, cudaStream_t st);
+
+// D2P_B200_ENGINE=plane selects the general plane engine for every operator
+// (both engines compute the same results; used to cross-check them in tests).
+bool engine_forced_plane();
 int launch_aff_plane(const SwArgs& a, cudaStream_t st);
 
 // elementwise / reduction kernels (sw_elementwise.cu)

@@ -133,3 +133,66 @@ def test_repeatable_bitwise(d2p, cuda_device):
     b = torch.ops.d2p.soft_sw_with_grads(s, -1.0, 1.0, None)
     for x, y in zip(a, b):
         assert torch.equal(x, y)
+
+
+# Shapes routed to the register/shared-memory wavefront kernel (L2 % 4 == 0):
+# partial and multiple row-blocks, L2 below/around/above the 16-column chunk.
+FAST = [  # (B, L1, L2, T)
+    (2, 1, 4, 1.0), (3, 31, 16, 1.0), (2, 32, 20, 0.5), (2, 33, 64, 1.0), (4, 64, 100, 2.0),
+    (2, 65, 132, 1.0), (3, 100, 36, 0.3), (2, 130, 260, 1.0), (1, 7, 512, 1.0), (1, 200, 8, 1.0),
+]
+
+
+@pytest.mark.parametrize("B,L1,L2,T", FAST)
+def test_wavefront_shapes(d2p, cuda_device, B, L1, L2, T):
+    s = scores(B, L1, L2, seed=L1 * 7 + L2)
+    v, m, gg, gt = torch.ops.d2p.soft_sw_with_grads(s.to(cuda_device), -1.0, T, None)
+    r64 = oracle.sw_linear(s.numpy(), None, -1.0, T, "f64")
+    r32 = oracle.sw_linear(s.numpy(), None, -1.0, T, "f32")
+    check("value", v, r64["value"], r32["value"])
+    check("marginals", m, r64["marginals"], r32["marginals"])
+    check("grad_gap", gg, r64["grad_gap"], r32["grad_gap"], rtol=1e-4, atol=1e-5)
+    check("grad_T", gt, r64["grad_T"], r32["grad_T"], rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.parametrize("B,L1,L2,T", [(6, 70, 96, 1.0), (5, 130, 200, 0.5), (8, 33, 36, 1.0)])
+def test_wavefront_ragged(d2p, cuda_device, B, L1, L2, T):
+    s = scores(B, L1, L2, seed=99)
+    ln = lengths_for(B, L1, L2, seed=L1)
+    ln[0] = torch.tensor([L1, L2], dtype=torch.int32)
+    ln[1] = torch.tensor([1, 1], dtype=torch.int32)
+    v, m, gg, gt = torch.ops.d2p.soft_sw_with_grads(s.to(cuda_device), -0.5, T, ln.to(cuda_device))
+    r64 = oracle.sw_linear(s.numpy(), ln.numpy(), -0.5, T, "f64")
+    r32 = oracle.sw_linear(s.numpy(), ln.numpy(), -0.5, T, "f32")
+    check("value", v, r64["value"], r32["value"])
+    check("marginals", m, r64["marginals"], r32["marginals"])
+    check("grad_gap", gg, r64["grad_gap"], r32["grad_gap"], rtol=1e-4, atol=1e-5)
+    check("grad_T", gt, r64["grad_T"], r32["grad_T"], rtol=1e-4, atol=1e-5)
+    mc = m.cpu()
+    for b, (l1, l2) in enumerate(ln.tolist()):
+        assert torch.count_nonzero(mc[b, l1:, :]) == 0
+        assert torch.count_nonzero(mc[b, :, l2:]) == 0
+
+
+def test_wavefront_empty_problem(d2p, cuda_device):
+    s = scores(3, 8, 8, seed=1)
+    ln = torch.tensor([[0, 8], [8, 0], [8, 8]], dtype=torch.int32)
+    v, m, gg, gt = torch.ops.d2p.soft_sw_with_grads(s.to(cuda_device), -1.0, 1.0, ln.to(cuda_device))
+    r64 = oracle.sw_linear(s.numpy(), ln.numpy(), -1.0, 1.0, "f64")
+    check("value", v, r64["value"])
+    check("marginals", m, r64["marginals"])
+    assert v[0].item() == 0.0 and v[1].item() == 0.0
+
+
+def test_fp64_error_not_worse_than_reference_512(d2p, cuda_device):
+    """At BASELINE config-2 size the reference's own fp32 marginals are ~2.5e-5 away
+    from fp64 (above the 1e-6 tolerance for any fp32 kernel); ours must be no worse."""
+    s = scores(1, 512, 512, seed=0)
+    v, m, gg, gt = torch.ops.d2p.soft_sw_with_grads(s.to(cuda_device), -1.0, 1.0, None)
+    r64 = oracle.sw_linear(s.numpy(), None, -1.0, 1.0, "f64")
+    r32 = oracle.sw_linear(s.numpy(), None, -1.0, 1.0, "f32")
+    e_ours = float(np.abs(m.cpu().numpy() - r64["marginals"]).max())
+    e_ref = float(np.abs(r32["marginals"] - r64["marginals"]).max())
+    print(f"512x512 marginal max|err| vs fp64: ours {e_ours:.3e}  reference fp32 {e_ref:.3e}")
+    assert e_ours <= e_ref
+    check("value", v, r64["value"], r32["value"])
