@@ -41,7 +41,8 @@ static bool dims_ok(int B, int L1, int L2) {
 static size_t plane_bytes(int family, int mode, int B, int L1, int L2) {
     const size_t plane = (size_t)L1 * (size_t)L2;
     const int np = family == D2P_FAMILY_AFFINE ? aff_planes(mode) : lin_planes(mode);
-    return align256((size_t)B * plane * np * sizeof(float));
+    // planes, then one frame per anti-diagonal per problem
+    return align256(((size_t)B * plane * np + (size_t)B * frame_stride(L1, L2)) * sizeof(float));
 }
 
 static size_t op_bytes(int family, int op, int B, int L1, int L2) {

@@ -25,6 +25,10 @@ __host__ __device__ constexpr int aff_planes(int mode) {
     return mode == MODE_MARG ? 6 : (mode == MODE_PT ? 15 : 12);
 }
 
+// The plane engine keeps one integer frame per anti-diagonal (k = i + j, k in
+// [0, L1 + L2 + 2]) per problem after its planes.
+__host__ __device__ inline size_t frame_stride(int L1, int L2) { return (size_t)L1 + (size_t)L2 + 4; }
+
 // library error codes (cudaError_t values are passed through unchanged)
 constexpr int kErrInvalid = 1001;
 constexpr int kErrWorkspace = 1002;

@@ -19,8 +19,15 @@
 //            D = LSE(M_l+go, D_l+ge) [j>1]
 //   value  : S = LSE over all valid cells and states, including alpha[0,0] = 0.
 //
-// The fast path for value+marginals (sw_wavefront.cu) supersedes this engine for
-// MODE_MARG when shapes allow; this engine remains the general implementation.
+// Frames.  Log-domain values grow along the matrix (alpha ~ 10^3 after a few
+// hundred anti-diagonals); stored raw in fp32 they lose absolute precision, and
+// every exponential of a difference inherits that loss.  Each anti-diagonal k
+// therefore has an integer frame F[k] (chosen from the middle cell of diagonal
+// k-1) and the planes store a - F[k].  Differences of frames are exact, so every
+// weight 2^(v - a) is formed from small numbers.  S is kept as integer + fraction.
+//
+// The fast path for linear value+marginals (sw_wavefront.cu) supersedes this
+// engine when shapes allow; this engine remains the general implementation.
 #include "sw_common.cuh"
 #include "sw_internal.h"
 
@@ -47,16 +54,125 @@ __device__ void zero_padding(float* out, int L1max, int L2max, int L1, int L2) {
     }
 }
 
+// Online log-sum-exp over framed values with an integer base R:
+//   sum_k 2^(R + m) * s  with companion sums
+//   y1 = sum e_k * ya_k,   y2 = sum e_k * (v_k - m)        (e_k = 2^(v_k - m))
+// y2 gives E_p[v] - m without forming differences of large numbers.
+struct FrameLse {
+    float R, m, s, y1, y2;
+    bool any;
+    __device__ __forceinline__ void init() { R = 0.f; m = 0.f; s = 0.f; y1 = 0.f; y2 = 0.f; any = false; }
+    __device__ __forceinline__ void add(float at, float F, float ya = 0.f) {
+        if (at <= kNegThresh) return;
+        if (!any) {
+            R = F;
+            m = at;
+            s = 1.f;
+            y1 = ya;
+            y2 = 0.f;
+            any = true;
+            return;
+        }
+        const float v = at + (F - R);
+        if (v > m) {
+            const float d = m - v, f = ex2f(d);
+            y2 = f * (y2 + s * d);
+            s = s * f + 1.f;
+            y1 = y1 * f + ya;
+            m = v;
+        } else {
+            const float d = v - m, e = ex2f(d);
+            s += e;
+            y1 += e * ya;
+            y2 += e * d;
+        }
+        if (m > 64.f) {  // keep m small: move its integer part into R (exact)
+            const float fl = floorf(m);
+            R += fl;
+            m -= fl;
+        }
+    }
+    __device__ __forceinline__ void merge(const FrameLse& o) {
+        if (!o.any) return;
+        if (!any) {
+            *this = o;
+            return;
+        }
+        const float Rn = fmaxf(R, o.R);
+        const float ma = m + (R - Rn), mb = o.m + (o.R - Rn);
+        if (mb > ma) {
+            const float d = ma - mb, f = ex2f(d);
+            y2 = f * (y2 + s * d) + o.y2;
+            s = s * f + o.s;
+            y1 = y1 * f + o.y1;
+            m = mb;
+        } else {
+            const float d = mb - ma, f = ex2f(d);
+            y2 += f * (o.y2 + o.s * d);
+            s += o.s * f;
+            y1 += o.y1 * f;
+            m = ma;
+        }
+        R = Rn;
+    }
+};
+
+__device__ FrameLse block_frame_lse(FrameLse v, float* scratch) {
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        FrameLse q;
+        q.R = __shfl_xor_sync(0xffffffffu, v.R, o);
+        q.m = __shfl_xor_sync(0xffffffffu, v.m, o);
+        q.s = __shfl_xor_sync(0xffffffffu, v.s, o);
+        q.y1 = __shfl_xor_sync(0xffffffffu, v.y1, o);
+        q.y2 = __shfl_xor_sync(0xffffffffu, v.y2, o);
+        q.any = __shfl_xor_sync(0xffffffffu, (int)v.any, o) != 0;
+        v.merge(q);
+    }
+    if (lane == 0) {
+        scratch[6 * wid + 0] = v.R;
+        scratch[6 * wid + 1] = v.m;
+        scratch[6 * wid + 2] = v.s;
+        scratch[6 * wid + 3] = v.y1;
+        scratch[6 * wid + 4] = v.y2;
+        scratch[6 * wid + 5] = v.any ? 1.f : 0.f;
+    }
+    __syncthreads();
+    FrameLse r;
+    r.init();
+    for (int w = 0; w < nw; ++w) {
+        FrameLse q;
+        q.R = scratch[6 * w + 0];
+        q.m = scratch[6 * w + 1];
+        q.s = scratch[6 * w + 2];
+        q.y1 = scratch[6 * w + 3];
+        q.y2 = scratch[6 * w + 4];
+        q.any = scratch[6 * w + 5] != 0.f;
+        r.merge(q);
+    }
+    __syncthreads();
+    return r;
+}
+
+// Forward bookkeeping shared by both families: at the start of diagonal k the
+// frame F[k] is read from the double-buffered shared slot written by the middle
+// cell of diagonal k-1.
+struct FrameWin {
+    float Fk, Fk1, Fk2;  // F[k], F[k-1], F[k-2]
+};
+
 // ==========================================================================
 // LINEAR GAP
 // ==========================================================================
 // workspace planes per problem (each L1max*L2max floats):
-//   0: a (scaled alpha)  1: beta  2: tangent forward (dalpha or U)
+//   0: a - F (framed scaled alpha)  1: beta  2: tangent forward (dalpha or U)
 //   3: tangent backward (dbeta or W)  4: R = (alpha - E[v]) / T  (PT mode)
 template <int MODE>
 __global__ void __launch_bounds__(kPlaneThreads) lin_plane_kernel(SwArgs p) {
-    __shared__ __align__(16) float red[4 * 32];
-    __shared__ float sh_aS, sh_dS;
+    __shared__ __align__(16) float red[6 * 32];
+    __shared__ float sh_F[2];
+    __shared__ float sh_Sint, sh_Sfrac, sh_dS;
 
     const int b = blockIdx.x;
     const int L1m = p.L1, L2m = p.L2;
@@ -80,83 +196,101 @@ __global__ void __launch_bounds__(kPlaneThreads) lin_plane_kernel(SwArgs p) {
     float* __restrict__ TG = ws + 2 * plane;
     float* __restrict__ TB = ws + 3 * plane;
     float* __restrict__ RR = ws + 4 * plane;
+    float* __restrict__ Fg = p.ws + (size_t)p.B * plane * lin_planes(MODE) + (size_t)b * frame_stride(L1m, L2m);
     float* __restrict__ out = p.out ? p.out + (size_t)b * plane : nullptr;
 
     zero_padding(out, L1m, L2m, L1, L2);
     const int W = L2m;  // row stride
 
     // ---------------- forward sweep ----------------
-    OnlineLse acc;
+    FrameLse acc;
     acc.init();
-    if (threadIdx.x == 0) acc.add(0.f, 0.f, 0.f);  // alpha[0,0] = 0 (d alpha = 0)
+    if (threadIdx.x == 0) {
+        acc.add(0.f, 0.f, 0.f);  // alpha[0,0] = 0 (d alpha = 0)
+        sh_F[0] = 0.f;           // F[2]
+        sh_F[1] = 0.f;           // F[3] if diagonal 2 is empty
+        Fg[0] = Fg[1] = 0.f;
+    }
+    __syncthreads();
+    FrameWin fw{0.f, 0.f, 0.f};
     for (int k = 2; k <= L1 + L2; ++k) {
+        fw.Fk2 = fw.Fk1;
+        fw.Fk1 = fw.Fk;
+        fw.Fk = sh_F[k & 1];
+        const float d1 = fw.Fk - fw.Fk1, d2 = fw.Fk - fw.Fk2;
         const int ilo = max(1, k - L2), ihi = min(L1, k - 1);
+        const int imid = (ilo + ihi) >> 1;
+        if (threadIdx.x == 0) Fg[k] = fw.Fk;
         for (int i = ilo + threadIdx.x; i <= ihi; i += blockDim.x) {
             const int j = k - i;
             const size_t q = (size_t)(i - 1) * W + (j - 1);
             const float x = s[q] * c;
             const bool up = i > 1, lf = j > 1, dg = up && lf;
-            const float v0 = dg ? A[q - W - 1] + x : kNeg;
-            const float v1 = up ? A[q - W] + g : kNeg;
-            const float v2 = lf ? A[q - 1] + g : kNeg;
-            const Lse4 r = lse4(v0, v1, v2, x);
+            const float v0 = dg ? A[q - W - 1] + x - d2 : kNeg;
+            const float v1 = up ? A[q - W] + g - d1 : kNeg;
+            const float v2 = lf ? A[q - 1] + g - d1 : kNeg;
+            const float v3 = x - fw.Fk;
+            const Lse4 r = lse4(v0, v1, v2, v3);
             A[q] = r.a;
-            float ya = 0.f, yb = 0.f;
+            if (i == imid) sh_F[(k + 1) & 1] = fw.Fk + rintf(r.a);
+            float ya = 0.f;
             if (MODE != MODE_MARG) {
                 const float inv = 1.f / r.sum;
                 const float w0 = r.t0 * inv, w1 = r.t1 * inv, w2 = r.t2 * inv, w3 = r.t3 * inv;
                 float tg;
                 if (MODE == MODE_HVP) {
                     const float vv = V[q];
-                    const float d0 = dg ? TG[q - W - 1] + vv : 0.f;
-                    const float d1 = up ? TG[q - W] : 0.f;
-                    const float d2 = lf ? TG[q - 1] : 0.f;
-                    tg = w0 * d0 + w1 * d1 + w2 * d2 + w3 * vv;
+                    const float e0 = dg ? TG[q - W - 1] + vv : 0.f;
+                    const float e1 = up ? TG[q - W] : 0.f;
+                    const float e2 = lf ? TG[q - 1] : 0.f;
+                    tg = w0 * e0 + w1 * e1 + w2 * e2 + w3 * vv;
                 } else {
                     const float pg = (MODE == MODE_PGAP) ? 1.f : 0.f;
-                    const float d0 = dg ? TG[q - W - 1] : 0.f;
-                    const float d1 = (up ? TG[q - W] : 0.f) + pg;
-                    const float d2 = (lf ? TG[q - 1] : 0.f) + pg;
-                    tg = w0 * d0 + w1 * d1 + w2 * d2;
+                    const float e0 = dg ? TG[q - W - 1] : 0.f;
+                    const float e1 = (up ? TG[q - W] : 0.f) + pg;
+                    const float e2 = (lf ? TG[q - 1] : 0.f) + pg;
+                    tg = w0 * e0 + w1 * e1 + w2 * e2;
                     if (MODE == MODE_PT) {
-                        // (alpha - E[v]) / T, E[v] over the four logits (natural units)
-                        const float ev = (w0 * (dg ? v0 : 0.f) + w1 * (up ? v1 : 0.f) +
-                                          w2 * (lf ? v2 : 0.f) + w3 * x);
-                        const float rt = (r.a - ev) * ic * iT;
+                        // (alpha - E[v]) / T with E[v] over the four logits (framed, exact differences)
+                        const float dv = w0 * (dg ? r.a - v0 : 0.f) + w1 * (up ? r.a - v1 : 0.f) +
+                                         w2 * (lf ? r.a - v2 : 0.f) + w3 * (r.a - v3);
+                        const float rt = dv * ic * iT;
                         RR[q] = rt;
                         tg += rt;
-                        yb = r.a * ic;  // alpha (natural), for sum p*alpha
                     }
                 }
                 TG[q] = tg;
                 ya = tg;
             }
-            acc.add(r.a, ya, yb);
+            acc.add(r.a, fw.Fk, ya);
         }
         __syncthreads();
     }
-    const OnlineLse tot = block_lse(acc, red);
     if (threadIdx.x == 0) {
-        const float aS = tot.m + lg2f(tot.s);
-        sh_aS = aS;
+        Fg[L1 + L2 + 1] = sh_F[(L1 + L2 + 1) & 1];
+        Fg[L1 + L2 + 2] = Fg[L1 + L2 + 1];
+    }
+    const FrameLse tot = block_frame_lse(acc, red);
+    if (threadIdx.x == 0) {
+        const float l2 = tot.m + lg2f(tot.s);
+        const float fl = floorf(l2);
+        sh_Sint = tot.R + fl;
+        sh_Sfrac = l2 - fl;
         float dS = 0.f;
         if (MODE == MODE_HVP || MODE == MODE_PGAP) dS = tot.y1 / tot.s;
-        if (MODE == MODE_PT) {
-            const float Snat = aS * ic;
-            dS = tot.y1 / tot.s + (Snat - tot.y2 / tot.s) * iT;
-        }
+        if (MODE == MODE_PT) dS = tot.y1 / tot.s + (lg2f(tot.s) - tot.y2 / tot.s) * ic * iT;
         sh_dS = dS;
-        if (p.value) p.value[b] = aS * ic;
+        if (p.value) p.value[b] = (sh_Sint + sh_Sfrac) * ic;
     }
     __syncthreads();
-    const float aS = sh_aS;
+    const float Sint = sh_Sint, Sfrac = sh_Sfrac;
     const float dS = sh_dS;
-    const float Snat = aS * ic;
 
     // ---------------- reverse sweep (gather form) ----------------
-    double gsum = 0.0, msum = 0.0;
+    double gsum = 0.0, hsum = 0.0;
     float dsum = 0.f;
     for (int k = L1 + L2; k >= 2; --k) {
+        const float F0 = Fg[k], Fm1 = Fg[k - 1], Fm2 = Fg[k - 2], Fp1 = Fg[k + 1], Fp2 = Fg[k + 2];
         const int ilo = max(1, k - L2), ihi = min(L1, k - 1);
         for (int i = ilo + threadIdx.x; i <= ihi; i += blockDim.x) {
             const int j = k - i;
@@ -166,31 +300,32 @@ __global__ void __launch_bounds__(kPlaneThreads) lin_plane_kernel(SwArgs p) {
             const float x = sc * c;
             const bool up = i > 1, lf = j > 1, dg = up && lf;
             const bool hasD = (i < L1) && (j < L2), hasU = i < L1, hasL = j < L2;
-            const float binit = ex2f(fminf(a - aS, 0.f));
+            const float lp = fminf((a - Sfrac) + (F0 - Sint), 0.f);
+            const float binit = ex2f(lp);
             float beta = binit;
-            // successor weights: transitions (i,j) -> succ
+            // successor weights: transitions (i,j) -> succ (exponents from framed differences)
             float wD = 0.f, wU = 0.f, wL = 0.f;
-            if (hasD) { wD = ex2f(a + s[q + W + 1] * c - A[q + W + 1]); beta += Bt[q + W + 1] * wD; }
-            if (hasU) { wU = ex2f(a + g - A[q + W]); beta += Bt[q + W] * wU; }
-            if (hasL) { wL = ex2f(a + g - A[q + 1]); beta += Bt[q + 1] * wL; }
+            if (hasD) { wD = ex2f(a - A[q + W + 1] + s[q + W + 1] * c + (F0 - Fp2)); beta += Bt[q + W + 1] * wD; }
+            if (hasU) { wU = ex2f(a - A[q + W] + g + (F0 - Fp1)); beta += Bt[q + W] * wU; }
+            if (hasL) { wL = ex2f(a - A[q + 1] + g + (F0 - Fp1)); beta += Bt[q + 1] * wL; }
             Bt[q] = beta;
-            // own incoming weights
-            const float wa = dg ? ex2f(A[q - W - 1] + x - a) : 0.f;
-            const float wsk = ex2f(x - a);
+            // own incoming weights, exponents ea = v - a
+            const float ea = dg ? A[q - W - 1] + x + (Fm2 - F0) - a : kNeg;
+            const float es = x - F0 - a;
+            const float wa = dg ? ex2f(ea) : 0.f;
+            const float wsk = ex2f(es);
             if (MODE == MODE_MARG) {
-                const float vu = up ? A[q - W] + g : kNeg, vl = lf ? A[q - 1] + g : kNeg;
-                const float va = dg ? A[q - W - 1] + x : kNeg;
-                const float wu = up ? ex2f(vu - a) : 0.f;
-                const float wl = lf ? ex2f(vl - a) : 0.f;
+                const float eu = up ? A[q - W] + g + (Fm1 - F0) - a : kNeg;
+                const float el = lf ? A[q - 1] + g + (Fm1 - F0) - a : kNeg;
+                const float wu = up ? ex2f(eu) : 0.f;
+                const float wl = lf ? ex2f(el) : 0.f;
                 const float mu = beta * (wa + wsk);
                 if (out) out[q] = mu;
                 gsum += (double)(beta * (wu + wl));
-                // dS/dT = entropy of the path distribution (see the note at the
-                // end of the kernel): visit probability x local choice entropy
-                // + end-cell entropy; all terms are >= 0 (no cancellation).
-                const float hloc = (dg ? wa * (a - va) : 0.f) + (up ? wu * (a - vu) : 0.f) +
-                                   (lf ? wl * (a - vl) : 0.f) + wsk * (a - x);
-                msum += (double)beta * (double)hloc + (double)binit * (double)(aS - a);
+                // dS/dT = entropy of the path distribution: visit probability x
+                // local choice entropy + end-cell entropy (non-negative terms).
+                const float hloc = (dg ? -wa * ea : 0.f) + (up ? -wu * eu : 0.f) + (lf ? -wl * el : 0.f) - wsk * es;
+                hsum += (double)beta * (double)hloc - (double)binit * (double)lp;
             } else if (MODE == MODE_HVP) {
                 const float da = TG[q];
                 const float vv = V[q];
@@ -220,40 +355,27 @@ __global__ void __launch_bounds__(kPlaneThreads) lin_plane_kernel(SwArgs p) {
                 const float pg = (MODE == MODE_PGAP) ? 1.f : 0.f;
                 const float u = TG[q];
                 float Wv = binit * (u - dS) * iT;
-                if (PT) Wv -= binit * ((a - aS) * ic) * iT * iT;
-                const float an = a * ic;  // alpha (natural)
+                if (PT) Wv -= binit * (((a - Sfrac) + (F0 - Sint)) * ic) * iT * iT;
                 if (hasD) {
                     const size_t qs = q + W + 1;
                     const float rs = PT ? RR[qs] : 0.f;
-                    const float Edu = TG[qs] - rs;
-                    float dw = wD * (u - Edu) * iT;
-                    if (PT) {
-                        const float Ev = A[qs] * ic - T * rs;
-                        const float vtr = an + s[qs];  // logit of the align transition (natural)
-                        dw += wD * (Ev - vtr) * iT * iT;
-                    }
+                    float dw = wD * (u - (TG[qs] - rs)) * iT;
+                    // E[v](succ) - logit(ij -> succ) = (alpha_s - T R_s) - (alpha + s_s)
+                    if (PT) dw += wD * ((A[qs] - a + (Fp2 - F0)) * ic - T * rs - s[qs]) * iT * iT;
                     Wv += TB[qs] * wD + Bt[qs] * dw;
                 }
                 if (hasU) {
                     const size_t qs = q + W;
                     const float rs = PT ? RR[qs] : 0.f;
-                    const float Edu = TG[qs] - rs;
-                    float dw = wU * (u + pg - Edu) * iT;
-                    if (PT) {
-                        const float Ev = A[qs] * ic - T * rs;
-                        dw += wU * (Ev - (an + gapn)) * iT * iT;
-                    }
+                    float dw = wU * (u + pg - (TG[qs] - rs)) * iT;
+                    if (PT) dw += wU * ((A[qs] - a + (Fp1 - F0)) * ic - T * rs - gapn) * iT * iT;
                     Wv += TB[qs] * wU + Bt[qs] * dw;
                 }
                 if (hasL) {
                     const size_t qs = q + 1;
                     const float rs = PT ? RR[qs] : 0.f;
-                    const float Edu = TG[qs] - rs;
-                    float dw = wL * (u + pg - Edu) * iT;
-                    if (PT) {
-                        const float Ev = A[qs] * ic - T * rs;
-                        dw += wL * (Ev - (an + gapn)) * iT * iT;
-                    }
+                    float dw = wL * (u + pg - (TG[qs] - rs)) * iT;
+                    if (PT) dw += wL * ((A[qs] - a + (Fp1 - F0)) * ic - T * rs - gapn) * iT * iT;
                     Wv += TB[qs] * wL + Bt[qs] * dw;
                 }
                 TB[q] = Wv;
@@ -263,10 +385,9 @@ __global__ void __launch_bounds__(kPlaneThreads) lin_plane_kernel(SwArgs p) {
                 float dwa = wa * (dua - Edu) * iT;
                 float dws = wsk * (0.f - Edu) * iT;
                 if (PT) {
-                    const float Ev = an - T * r0;
-                    const float va = dg ? A[q - W - 1] * ic + sc : 0.f;
-                    dwa += wa * (Ev - va) * iT * iT;
-                    dws += wsk * (Ev - sc) * iT * iT;
+                    // E[v] - v_align = (alpha - T r0) - (alpha_diag + s);  E[v] - v_sky = alpha - T r0 - s
+                    if (dg) dwa += wa * ((a - A[q - W - 1] + (F0 - Fm2)) * ic - T * r0 - sc) * iT * iT;
+                    dws += wsk * ((a + F0) * ic - T * r0 - sc) * iT * iT;
                 }
                 const float dPv = Wv * (wa + wsk) + beta * (dwa + dws);
                 if (out) out[q] = dPv;
@@ -280,15 +401,17 @@ __global__ void __launch_bounds__(kPlaneThreads) lin_plane_kernel(SwArgs p) {
         if (threadIdx.x == 0) p.dot_out[b] = D;
     }
     if (MODE == MODE_MARG && (p.grad_gap || p.grad_T)) {
-        // The origin alpha[0,0] = 0 is a possible end state (empty alignment).
-        if (threadIdx.x == 0) msum += (double)ex2f(-aS) * (double)aS;
+        // the origin alpha[0,0] = 0 is a possible end state (empty alignment)
+        if (threadIdx.x == 0) {
+            const float lp0 = fminf(-Sfrac - Sint, 0.f);
+            hsum += (double)ex2f(lp0) * (double)(-lp0);
+        }
         const double G = block_sum_d(gsum, reinterpret_cast<double*>(red));
-        const double H = block_sum_d(msum, reinterpret_cast<double*>(red));
+        const double H = block_sum_d(hsum, reinterpret_cast<double*>(red));
         if (threadIdx.x == 0) {
             if (p.grad_gap) p.grad_gap[b] = (float)G;
             // dS/dT = (S - E[path score]) / T  (reference kernels_cpu.cpp:274-276)
-            //       = H[path]  (entropy of the Gibbs path distribution, nats),
-            // evaluated as a sum of non-negative terms in base-2 units.
+            //       = entropy of the Gibbs path distribution (nats)
             if (p.grad_T) p.grad_T[b] = (float)(H * (double)kLn2);
         }
     }
@@ -297,17 +420,16 @@ __global__ void __launch_bounds__(kPlaneThreads) lin_plane_kernel(SwArgs p) {
 // ==========================================================================
 // AFFINE GAP
 // ==========================================================================
-// planes per problem: alpha M,I,D (0-2), beta M,I,D (3-5), tangent fwd M,I,D
-// (6-8), tangent bwd M,I,D (9-11), R M,I,D (12-14).
+// planes per problem: alpha M,I,D (0-2, framed), beta M,I,D (3-5), tangent fwd
+// M,I,D (6-8), tangent bwd M,I,D (9-11), R M,I,D (12-14).
 template <int MODE>
 __global__ void __launch_bounds__(kPlaneThreads) aff_plane_kernel(SwArgs p) {
-    __shared__ __align__(16) float red[4 * 32];
-    __shared__ float sh_aS, sh_dS;
+    __shared__ __align__(16) float red[6 * 32];
+    __shared__ float sh_F[2];
+    __shared__ float sh_Sint, sh_Sfrac, sh_dS;
 
     const int b = blockIdx.x;
     const int L1m = p.L1, L2m = p.L2;
-    // lengths are validated by the caller; clamp so a bad value can never index
-    // outside the padded problem
     const int L1 = p.lengths ? min(max(p.lengths[2 * b], 0), L1m) : L1m;
     const int L2 = p.lengths ? min(max(p.lengths[2 * b + 1], 0), L2m) : L2m;
     const float gon = read_param(p.gap_dev, p.gap);
@@ -336,43 +458,59 @@ __global__ void __launch_bounds__(kPlaneThreads) aff_plane_kernel(SwArgs p) {
     float* RM = ws + 12 * plane;
     float* RI = ws + 13 * plane;
     float* RD = ws + 14 * plane;
+    float* __restrict__ Fg = p.ws + (size_t)p.B * plane * aff_planes(MODE) + (size_t)b * frame_stride(L1m, L2m);
     float* __restrict__ out = p.out ? p.out + (size_t)b * plane : nullptr;
     zero_padding(out, L1m, L2m, L1, L2);
     const int W = L2m;
     auto score = [&](size_t q) -> float { return sbf ? __bfloat162float(sbf[q]) : s[q]; };
 
-    OnlineLse acc;
+    FrameLse acc;
     acc.init();
-    if (threadIdx.x == 0) acc.add(0.f, 0.f, 0.f);
+    if (threadIdx.x == 0) {
+        acc.add(0.f, 0.f, 0.f);
+        sh_F[0] = 0.f;
+        sh_F[1] = 0.f;
+        Fg[0] = Fg[1] = 0.f;
+    }
+    __syncthreads();
     const float pgo = (MODE == MODE_PGAP) ? 1.f : 0.f;   // param 0: gap_open
     const float pge = (MODE == MODE_PGE) ? 1.f : 0.f;    // param 1: gap_ext
     const bool PT = (MODE == MODE_PT);
 
+    FrameWin fw{0.f, 0.f, 0.f};
     for (int k = 2; k <= L1 + L2; ++k) {
+        fw.Fk2 = fw.Fk1;
+        fw.Fk1 = fw.Fk;
+        fw.Fk = sh_F[k & 1];
+        const float d1 = fw.Fk - fw.Fk1, d2 = fw.Fk - fw.Fk2;
         const int ilo = max(1, k - L2), ihi = min(L1, k - 1);
+        const int imid = (ilo + ihi) >> 1;
+        if (threadIdx.x == 0) Fg[k] = fw.Fk;
         for (int i = ilo + threadIdx.x; i <= ihi; i += blockDim.x) {
             const int j = k - i;
             const size_t q = (size_t)(i - 1) * W + (j - 1);
             const float sc = score(q);
             const float x = sc * c;
             const bool up = i > 1, lf = j > 1, dg = up && lf;
-            const float m0 = dg ? AM[q - W - 1] + x : kNeg;
-            const float m1 = dg ? AI[q - W - 1] + x : kNeg;
-            const float m2 = dg ? AD[q - W - 1] + x : kNeg;
-            const Lse4 rm = lse4(m0, m1, m2, x);
-            const float i0 = up ? AM[q - W] + go : kNeg;
-            const float i1 = up ? AI[q - W] + ge : kNeg;
+            const float m0 = dg ? AM[q - W - 1] + x - d2 : kNeg;
+            const float m1 = dg ? AI[q - W - 1] + x - d2 : kNeg;
+            const float m2 = dg ? AD[q - W - 1] + x - d2 : kNeg;
+            const float m3 = x - fw.Fk;
+            const Lse4 rm = lse4(m0, m1, m2, m3);
+            const float i0 = up ? AM[q - W] + go - d1 : kNeg;
+            const float i1 = up ? AI[q - W] + ge - d1 : kNeg;
             const Lse2 ri = lse2(i0, i1);
-            const float d0 = lf ? AM[q - 1] + go : kNeg;
-            const float d1 = lf ? AD[q - 1] + ge : kNeg;
-            const Lse2 rd = lse2(d0, d1);
+            const float e0 = lf ? AM[q - 1] + go - d1 : kNeg;
+            const float e1 = lf ? AD[q - 1] + ge - d1 : kNeg;
+            const Lse2 rd = lse2(e0, e1);
             AM[q] = rm.a;
             AI[q] = ri.a;
             AD[q] = rd.a;
+            if (i == imid) sh_F[(k + 1) & 1] = fw.Fk + rintf(rm.a);
             if (MODE == MODE_MARG) {
-                acc.add(rm.a);
-                acc.add(ri.a);
-                acc.add(rd.a);
+                acc.add(rm.a, fw.Fk);
+                acc.add(ri.a, fw.Fk);
+                acc.add(rd.a, fw.Fk);
             } else {
                 const float im = 1.f / rm.sum, ii = 1.f / ri.sum, id = 1.f / rd.sum;
                 const float wm0 = rm.t0 * im, wm1 = rm.t1 * im, wm2 = rm.t2 * im, wm3 = rm.t3 * im;
@@ -390,12 +528,12 @@ __global__ void __launch_bounds__(kPlaneThreads) aff_plane_kernel(SwArgs p) {
                     ti = wi0 * ((up ? TM[q - W] : 0.f) + pgo) + wi1 * ((up ? TI[q - W] : 0.f) + pge);
                     td = wd0 * ((lf ? TM[q - 1] : 0.f) + pgo) + wd1 * ((lf ? TD[q - 1] : 0.f) + pge);
                     if (PT) {
-                        const float evm = wm0 * (dg ? m0 : 0.f) + wm1 * (dg ? m1 : 0.f) +
-                                          wm2 * (dg ? m2 : 0.f) + wm3 * x;
-                        const float rmv = (rm.a - evm) * ic * iT;
+                        const float dvm = wm0 * (dg ? rm.a - m0 : 0.f) + wm1 * (dg ? rm.a - m1 : 0.f) +
+                                          wm2 * (dg ? rm.a - m2 : 0.f) + wm3 * (rm.a - m3);
+                        const float rmv = dvm * ic * iT;
                         float riv = 0.f, rdv = 0.f;
-                        if (ri.a > kNegThresh) riv = (ri.a - (wi0 * i0 + wi1 * i1)) * ic * iT;
-                        if (rd.a > kNegThresh) rdv = (rd.a - (wd0 * d0 + wd1 * d1)) * ic * iT;
+                        if (ri.a > kNegThresh) riv = (wi0 * (ri.a - i0) + wi1 * (ri.a - i1)) * ic * iT;
+                        if (rd.a > kNegThresh) rdv = (wd0 * (rd.a - e0) + wd1 * (rd.a - e1)) * ic * iT;
                         RM[q] = rmv;
                         RI[q] = riv;
                         RD[q] = rdv;
@@ -407,67 +545,76 @@ __global__ void __launch_bounds__(kPlaneThreads) aff_plane_kernel(SwArgs p) {
                 TM[q] = tm;
                 TI[q] = ti;
                 TD[q] = td;
-                acc.add(rm.a, tm, PT ? rm.a * ic : 0.f);
-                acc.add(ri.a, ti, PT ? ri.a * ic : 0.f);
-                acc.add(rd.a, td, PT ? rd.a * ic : 0.f);
+                acc.add(rm.a, fw.Fk, tm);
+                acc.add(ri.a, fw.Fk, ti);
+                acc.add(rd.a, fw.Fk, td);
             }
         }
         __syncthreads();
     }
-    const OnlineLse tot = block_lse(acc, red);
     if (threadIdx.x == 0) {
-        const float aS = tot.m + lg2f(tot.s);
-        sh_aS = aS;
+        Fg[L1 + L2 + 1] = sh_F[(L1 + L2 + 1) & 1];
+        Fg[L1 + L2 + 2] = Fg[L1 + L2 + 1];
+    }
+    const FrameLse tot = block_frame_lse(acc, red);
+    if (threadIdx.x == 0) {
+        const float l2 = tot.m + lg2f(tot.s);
+        const float fl = floorf(l2);
+        sh_Sint = tot.R + fl;
+        sh_Sfrac = l2 - fl;
         float dS = 0.f;
         if (MODE == MODE_HVP || MODE == MODE_PGAP || MODE == MODE_PGE) dS = tot.y1 / tot.s;
-        if (PT) dS = tot.y1 / tot.s + (aS * ic - tot.y2 / tot.s) * iT;
+        if (PT) dS = tot.y1 / tot.s + (lg2f(tot.s) - tot.y2 / tot.s) * ic * iT;
         sh_dS = dS;
-        if (p.value) p.value[b] = aS * ic;
+        if (p.value) p.value[b] = (sh_Sint + sh_Sfrac) * ic;
     }
     __syncthreads();
-    const float aS = sh_aS, dS = sh_dS, Snat = aS * ic;
+    const float Sint = sh_Sint, Sfrac = sh_Sfrac, dS = sh_dS;
 
-    double so = 0.0, se = 0.0, msum = 0.0;
+    double so = 0.0, se = 0.0, hsum = 0.0;
     float dsum = 0.f;
     for (int k = L1 + L2; k >= 2; --k) {
+        const float F0 = Fg[k], Fm1 = Fg[k - 1], Fm2 = Fg[k - 2], Fp1 = Fg[k + 1], Fp2 = Fg[k + 2];
         const int ilo = max(1, k - L2), ihi = min(L1, k - 1);
         for (int i = ilo + threadIdx.x; i <= ihi; i += blockDim.x) {
             const int j = k - i;
             const size_t q = (size_t)(i - 1) * W + (j - 1);
             const float sc = score(q);
-            const bool up = i > 1, lf = j > 1;
+            const float x = sc * c;
+            const bool up = i > 1, lf = j > 1, dg = up && lf;
             const bool hasD = (i < L1) && (j < L2), hasU = i < L1, hasL = j < L2;
             const float am = AM[q], ai = AI[q], ad = AD[q];
-            const float bim = ex2f(fminf(am - aS, 0.f));
-            const float bii = ex2f(fminf(ai - aS, 0.f));
-            const float bid = ex2f(fminf(ad - aS, 0.f));
+            const float lpm = fminf((am - Sfrac) + (F0 - Sint), 0.f);
+            const float lpi = fminf((ai - Sfrac) + (F0 - Sint), 0.f);
+            const float lpd = fminf((ad - Sfrac) + (F0 - Sint), 0.f);
+            const float bim = ex2f(lpm), bii = ex2f(lpi), bid = ex2f(lpd);
             float bm = bim, bi = bii, bd = bid;
-            // successor transition weights
+            // successor transition weights (framed exponents)
             float xs = 0.f, wMM = 0.f, wIM = 0.f, wDM = 0.f, wMI = 0.f, wII = 0.f, wMD = 0.f, wDD = 0.f;
-            size_t qD = q + W + 1, qU = q + W, qL = q + 1;
+            const size_t qD = q + W + 1, qU = q + W, qL = q + 1;
             if (hasD) {
                 xs = score(qD) * c;
-                const float amD = AM[qD];
-                wMM = ex2f(am + xs - amD);   // M(ij) -> M(D)
-                wIM = ex2f(ai + xs - amD);   // I(ij) -> M(D)
-                wDM = ex2f(ad + xs - amD);   // D(ij) -> M(D)
+                const float base = xs - AM[qD] + (F0 - Fp2);
+                wMM = ex2f(am + base);   // M(ij) -> M(D)
+                wIM = ex2f(ai + base);   // I(ij) -> M(D)
+                wDM = ex2f(ad + base);   // D(ij) -> M(D)
                 const float bMD = BM[qD];
                 bm += bMD * wMM;
                 bi += bMD * wIM;
                 bd += bMD * wDM;
             }
             if (hasU) {
-                const float aiU = AI[qU];
-                wMI = ex2f(am + go - aiU);   // M(ij) -> I(U)
-                wII = ex2f(ai + ge - aiU);   // I(ij) -> I(U)
+                const float base = -AI[qU] + (F0 - Fp1);
+                wMI = ex2f(am + go + base);   // M(ij) -> I(U)
+                wII = ex2f(ai + ge + base);   // I(ij) -> I(U)
                 const float bIU = BI[qU];
                 bm += bIU * wMI;
                 bi += bIU * wII;
             }
             if (hasL) {
-                const float adL = AD[qL];
-                wMD = ex2f(am + go - adL);   // M(ij) -> D(L)
-                wDD = ex2f(ad + ge - adL);   // D(ij) -> D(L)
+                const float base = -AD[qL] + (F0 - Fp1);
+                wMD = ex2f(am + go + base);   // M(ij) -> D(L)
+                wDD = ex2f(ad + ge + base);   // D(ij) -> D(L)
                 const float bDL = BD[qL];
                 bm += bDL * wMD;
                 bd += bDL * wDD;
@@ -477,43 +624,42 @@ __global__ void __launch_bounds__(kPlaneThreads) aff_plane_kernel(SwArgs p) {
             BD[q] = bd;
             if (MODE == MODE_MARG) {
                 if (out) out[q] = bm;
-                // path entropy (dS/dT): end-state terms for M, I, D ...
-                double hs = (double)bim * (double)(aS - am);
-                if (ai > kNegThresh) hs += (double)bii * (double)(aS - ai);
-                if (ad > kNegThresh) hs += (double)bid * (double)(aS - ad);
+                // path entropy (dS/dT): end-state terms ...
+                double hs = -(double)bim * (double)lpm;
+                if (ai > kNegThresh) hs -= (double)bii * (double)lpi;
+                if (ad > kNegThresh) hs -= (double)bid * (double)lpd;
                 // ... plus visit probability x local choice entropy
                 {
-                    const bool dg = up && lf;
-                    const float x = sc * c;
-                    float hm = ex2f(x - am) * (am - x);
+                    const float es = x - F0 - am;
+                    float hm = -ex2f(es) * es;
                     if (dg) {
-                        const float v0 = AM[q - W - 1] + x, v1 = AI[q - W - 1] + x, v2 = AD[q - W - 1] + x;
-                        hm += ex2f(v0 - am) * (am - v0);
-                        if (v1 > kNegThresh) hm += ex2f(v1 - am) * (am - v1);
-                        if (v2 > kNegThresh) hm += ex2f(v2 - am) * (am - v2);
+                        const float base = x + (Fm2 - F0) - am;
+                        const float q0 = AM[q - W - 1] + base, q1 = AI[q - W - 1] + base, q2 = AD[q - W - 1] + base;
+                        hm -= ex2f(q0) * q0;
+                        if (AI[q - W - 1] > kNegThresh) hm -= ex2f(q1) * q1;
+                        if (AD[q - W - 1] > kNegThresh) hm -= ex2f(q2) * q2;
                     }
                     hs += (double)bm * (double)hm;
                 }
-                // incoming gap transitions of I(ij), D(ij)
-                if (up) {
-                    const float v0 = AM[q - W] + go, v1 = AI[q - W] + ge;
-                    const float w0 = ex2f(v0 - ai), w1 = ex2f(v1 - ai);
+                if (up) {  // incoming gap transitions of I(ij)
+                    const float q0 = AM[q - W] + go + (Fm1 - F0) - ai, q1 = AI[q - W] + ge + (Fm1 - F0) - ai;
+                    const float w0 = ex2f(q0), w1 = ex2f(q1);
                     so += (double)(bi * w0);
                     se += (double)(bi * w1);
-                    float hi = w0 * (ai - v0);
-                    if (v1 > kNegThresh) hi += w1 * (ai - v1);
+                    float hi = -w0 * q0;
+                    if (AI[q - W] > kNegThresh) hi -= w1 * q1;
                     hs += (double)bi * (double)hi;
                 }
-                if (lf) {
-                    const float v0 = AM[q - 1] + go, v1 = AD[q - 1] + ge;
-                    const float w0 = ex2f(v0 - ad), w1 = ex2f(v1 - ad);
+                if (lf) {  // incoming gap transitions of D(ij)
+                    const float q0 = AM[q - 1] + go + (Fm1 - F0) - ad, q1 = AD[q - 1] + ge + (Fm1 - F0) - ad;
+                    const float w0 = ex2f(q0), w1 = ex2f(q1);
                     so += (double)(bd * w0);
                     se += (double)(bd * w1);
-                    float hd = w0 * (ad - v0);
-                    if (v1 > kNegThresh) hd += w1 * (ad - v1);
+                    float hd = -w0 * q0;
+                    if (AD[q - 1] > kNegThresh) hd -= w1 * q1;
                     hs += (double)bd * (double)hd;
                 }
-                msum += hs;
+                hsum += hs;
             } else if (MODE == MODE_HVP) {
                 const float dm = TM[q], di = TI[q], dd = TD[q];
                 float dbm = bim * (dm - dS) * iT;
@@ -543,45 +689,44 @@ __global__ void __launch_bounds__(kPlaneThreads) aff_plane_kernel(SwArgs p) {
                 const float um = TM[q], ui = TI[q], ud = TD[q];
                 float Wm = bim * (um - dS) * iT, Wi = bii * (ui - dS) * iT, Wd = bid * (ud - dS) * iT;
                 if (PT) {
-                    if (am > kNegThresh) Wm -= bim * ((am - aS) * ic) * iT * iT;
-                    if (ai > kNegThresh) Wi -= bii * ((ai - aS) * ic) * iT * iT;
-                    if (ad > kNegThresh) Wd -= bid * ((ad - aS) * ic) * iT * iT;
+                    if (am > kNegThresh) Wm -= bim * (((am - Sfrac) + (F0 - Sint)) * ic) * iT * iT;
+                    if (ai > kNegThresh) Wi -= bii * (((ai - Sfrac) + (F0 - Sint)) * ic) * iT * iT;
+                    if (ad > kNegThresh) Wd -= bid * (((ad - Sfrac) + (F0 - Sint)) * ic) * iT * iT;
                 }
-                const float amn = am * ic, ain = ai * ic, adn = ad * ic;
                 if (hasD) {
                     const float rs = PT ? RM[qD] : 0.f;
                     const float Edu = TM[qD] - rs;
-                    const float Ev = AM[qD] * ic - T * rs;
-                    const float scD = xs * ic;
+                    // E[v](succ) - logit: (alpha_s - T R_s) - (alpha_state + s_s), framed differences
+                    const float dEv = (AM[qD] + (Fp2 - F0)) * ic - T * rs - xs * ic;
                     const float xbD = XM[qD], bMD = BM[qD];
                     float dw;
-                    dw = wMM * (um - Edu) * iT + (PT ? wMM * (Ev - (amn + scD)) * iT * iT : 0.f);
+                    dw = wMM * (um - Edu) * iT + (PT ? wMM * (dEv - am * ic) * iT * iT : 0.f);
                     Wm += xbD * wMM + bMD * dw;
-                    dw = wIM * (ui - Edu) * iT + (PT ? wIM * (Ev - (ain + scD)) * iT * iT : 0.f);
+                    dw = wIM * (ui - Edu) * iT + (PT ? wIM * (dEv - ai * ic) * iT * iT : 0.f);
                     Wi += xbD * wIM + bMD * dw;
-                    dw = wDM * (ud - Edu) * iT + (PT ? wDM * (Ev - (adn + scD)) * iT * iT : 0.f);
+                    dw = wDM * (ud - Edu) * iT + (PT ? wDM * (dEv - ad * ic) * iT * iT : 0.f);
                     Wd += xbD * wDM + bMD * dw;
                 }
                 if (hasU) {
                     const float rs = PT ? RI[qU] : 0.f;
                     const float Edu = TI[qU] - rs;
-                    const float Ev = AI[qU] * ic - T * rs;
+                    const float dEv = (AI[qU] + (Fp1 - F0)) * ic - T * rs;
                     const float xbU = XI[qU], bIU = BI[qU];
                     float dw;
-                    dw = wMI * (um + pgo - Edu) * iT + (PT ? wMI * (Ev - (amn + gon)) * iT * iT : 0.f);
+                    dw = wMI * (um + pgo - Edu) * iT + (PT ? wMI * (dEv - (am * ic + gon)) * iT * iT : 0.f);
                     Wm += xbU * wMI + bIU * dw;
-                    dw = wII * (ui + pge - Edu) * iT + (PT ? wII * (Ev - (ain + gen)) * iT * iT : 0.f);
+                    dw = wII * (ui + pge - Edu) * iT + (PT ? wII * (dEv - (ai * ic + gen)) * iT * iT : 0.f);
                     Wi += xbU * wII + bIU * dw;
                 }
                 if (hasL) {
                     const float rs = PT ? RD[qL] : 0.f;
                     const float Edu = TD[qL] - rs;
-                    const float Ev = AD[qL] * ic - T * rs;
+                    const float dEv = (AD[qL] + (Fp1 - F0)) * ic - T * rs;
                     const float xbL = XD[qL], bDL = BD[qL];
                     float dw;
-                    dw = wMD * (um + pgo - Edu) * iT + (PT ? wMD * (Ev - (amn + gon)) * iT * iT : 0.f);
+                    dw = wMD * (um + pgo - Edu) * iT + (PT ? wMD * (dEv - (am * ic + gon)) * iT * iT : 0.f);
                     Wm += xbL * wMD + bDL * dw;
-                    dw = wDD * (ud + pge - Edu) * iT + (PT ? wDD * (Ev - (adn + gen)) * iT * iT : 0.f);
+                    dw = wDD * (ud + pge - Edu) * iT + (PT ? wDD * (dEv - (ad * ic + gen)) * iT * iT : 0.f);
                     Wd += xbL * wDD + bDL * dw;
                 }
                 XM[q] = Wm;
@@ -598,10 +743,13 @@ __global__ void __launch_bounds__(kPlaneThreads) aff_plane_kernel(SwArgs p) {
         if (threadIdx.x == 0) p.dot_out[b] = D;
     }
     if (MODE == MODE_MARG && (p.grad_gap || p.grad_gap2 || p.grad_T)) {
-        if (threadIdx.x == 0) msum += (double)ex2f(-aS) * (double)aS;  // origin M[0,0] = 0
+        if (threadIdx.x == 0) {  // origin M[0,0] = 0
+            const float lp0 = fminf(-Sfrac - Sint, 0.f);
+            hsum += (double)ex2f(lp0) * (double)(-lp0);
+        }
         const double O = block_sum_d(so, reinterpret_cast<double*>(red));
         const double E = block_sum_d(se, reinterpret_cast<double*>(red));
-        const double H = block_sum_d(msum, reinterpret_cast<double*>(red));
+        const double H = block_sum_d(hsum, reinterpret_cast<double*>(red));
         if (threadIdx.x == 0) {
             if (p.grad_gap) p.grad_gap[b] = (float)O;
             if (p.grad_gap2) p.grad_gap2[b] = (float)E;
