@@ -82,6 +82,29 @@ D2P_API int d2p_sw_forward_backward(const float* scores, const int* lengths, int
                             float* grad_gap, float* grad_temperature, void* workspace,
                             size_t workspace_bytes, void* stream);
 
+/* Size of the library-owned device scratch behind d2p_sw_forward_backward_static
+ * (one array per device). */
+#define D2P_STATIC_SCRATCH_BYTES (64u * 1024u * 1024u)
+
+/* Same results as d2p_sw_forward_backward, but the call allocates nothing and
+ * takes no workspace: it runs in a fixed scratch array built into the library.
+ * For callers that cannot allocate device memory per call -- a host with no
+ * device allocator of its own (C, cgo, FFI), where cudaMalloc/cudaFree around
+ * each call would synchronize the device, or a process whose device memory is
+ * already handed out to a fixed pool.
+ * Limits: problems whose d2p_sw_workspace_bytes(D2P_FAMILY_LINEAR,
+ * D2P_OP_FORWARD_BACKWARD, B, L1, L2) exceeds D2P_STATIC_SCRATCH_BYTES return
+ * D2P_ERR_WORKSPACE_TOO_SMALL.  The scratch is shared by all calls on a device:
+ * calls that overlap on the GPU (different streams or host threads) race on it.
+ * The first call on a device looks up the scratch address with that device
+ * current; make it before any stream capture.
+ * No counterpart in the reference (its CUDA path allocates through torch). */
+D2P_API int d2p_sw_forward_backward_static(const float* scores, const int* lengths, int B, int L1,
+                                           int L2, float gap, float temperature,
+                                           const float* gap_dev, const float* temperature_dev,
+                                           float* value, float* marginals, float* grad_gap,
+                                           float* grad_temperature, void* stream);
+
 /* hvp = d(marginals)/d(scores) . tangent.
  * Replaces: sw_regular_forward + sw_regular_hvp (src/sw/kernels.cuh:237-270) as
  * driven by soft_sw_regular_hvp_cuda (src/sw/torch_cuda.cpp:507-570). */
