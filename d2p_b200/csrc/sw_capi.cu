@@ -48,9 +48,12 @@ static size_t plane_bytes(int family, int mode, int B, int L1, int L2) {
 static size_t op_bytes(int family, int op, int B, int L1, int L2) {
     switch (op) {
         case D2P_OP_FORWARD_BACKWARD: {
-            size_t pe = plane_bytes(family, MODE_MARG, B, L1, L2);
-            size_t wf = wavefront_workspace_bytes(family, B, L1, L2);
-            return pe > wf ? pe : wf;
+            // the fast path's workspace, or the plane engine's (which also serves as
+            // the fix-up for problems the fast path flags), then one flag per problem
+            const size_t pe = plane_bytes(family, MODE_MARG, B, L1, L2);
+            const size_t wf = wavefront_workspace_bytes(family, B, L1, L2);
+            if (wf == 0) return pe;
+            return align256(pe > wf ? pe : wf) + align256((size_t)(B > 0 ? B : 1) * sizeof(int));
         }
         case D2P_OP_HVP:
             return plane_bytes(family, MODE_HVP, B, L1, L2);
@@ -123,8 +126,17 @@ int d2p_sw_forward_backward(const float* scores, const int* lengths, int B, int 
     a.grad_gap = grad_gap;
     a.grad_T = grad_temperature;
     a.ws = (float*)workspace;
-    int rc = launch_wavefront(a, D2P_FAMILY_LINEAR, workspace_bytes, st);
-    if (rc != kNotHandled) return rc;
+    const size_t pe = plane_bytes(D2P_FAMILY_LINEAR, MODE_MARG, B, L1, L2);
+    const size_t wf = wavefront_workspace_bytes(D2P_FAMILY_LINEAR, B, L1, L2);
+    if (wf > 0) {
+        // fast path; problems it flags (a cell sum outside its exponent window, or
+        // a dependency wait that gave up) are recomputed by the plane engine
+        a.redo = (int*)((char*)workspace + align256(pe > wf ? pe : wf));
+        int rc = launch_wavefront(a, D2P_FAMILY_LINEAR, workspace_bytes, st);
+        if (rc == D2P_OK) return launch_lin_plane(a, st);
+        if (rc != kNotHandled) return rc;
+        a.redo = nullptr;
+    }
     return launch_lin_plane(a, st);
 }
 

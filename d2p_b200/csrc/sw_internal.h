@@ -55,6 +55,8 @@ struct SwArgs {
     int* status;                        // device status word (optional)
     const float* dot_with;              // [B, L1, L2] optional: param modes accumulate
     float* dot_out;                     //   dot_out[b] = sum_ij dot_with[b,i,j] * dP[b,i,j]
+    int* redo;                          // [B] fast path: out, set for problems it could not finish;
+                                        // plane engine: in, if set only those problems run
 };
 
 int launch_lin_plane(const SwArgs& a, cudaStream_t st);

@@ -3,31 +3,36 @@
 // One CTA per problem; warps own row-blocks of 32 rows (lane = row) and sweep
 // them left-to-right (forward) and right-to-left (reverse), one cell per lane
 // per step, so the 32 lanes of a warp always sit on one anti-diagonal.
-// Cross-lane dependencies move by warp shuffles; cross-warp dependencies (the
-// last row of a row-block feeding the first row of the next) move through small
-// global boundary rows (L2-resident) prefetched with cp.async, with a CTA barrier
-// every kSync steps and a fixed minimum skew between consecutive row-blocks.
+// Cross-lane dependencies move by warp shuffles.  Cross-warp dependencies (the
+// last row of a row-block feeding the first row of the next) move through
+// small L2-resident boundary rows in the workspace, prefetched with cp.async;
+// consumers wait on per-warp progress counters in shared memory (release /
+// acquire at CTA scope, bounded spins), so no CTA-wide barrier sits on the
+// sweep and every warp runs as soon as its inputs exist.
 //
 // Numerics.  Everything is base-2 scaled (a = alpha*log2(e)/T, one MUFU
-// ex2/lg2 per exponential/logarithm) and every warp keeps its own integer
-// "frame" O per anti-diagonal: a cell stores a - O, so stored magnitudes stay
-// small even when alpha grows to 10^3 along the matrix (the reference carries
-// raw alpha in fp32 and loses absolute precision there).  Frame differences are
-// exact integers; the value S is kept as (integer part, fraction).
+// ex2/lg2 per exponential/logarithm).  Every warp keeps an integer "frame" O
+// per anti-diagonal: a cell stores a - O, so stored magnitudes stay small even
+// when alpha grows to 10^3 along the matrix (the reference carries raw alpha
+// in fp32 and loses absolute precision there).  The frame is re-anchored on
+// the middle lane every 4 steps and advanced by a predicted integer drift in
+// between.  Frame differences are exact integers; the value S is kept as
+// (integer part, fraction).  The forward log-sum-exp is max-shifted, so any
+// spread of values along an anti-diagonal is exact; every reverse exponent is
+// <= 0 by construction (alpha_ij >= alpha_pred + transition).
 //
-// Memory.  The forward writes the framed alpha plane (4 B/cell) and the per-step
-// frames; the reverse pass reads them back, so each cell costs: scores 4 B read
-// twice, alpha 4 B written + read, marginals 4 B written = 20 B/cell.  Every
-// global access is a coalesced 16-byte cp.async (loads) or 16-byte store
-// (write-back of 16-column tiles staged in shared memory).  Per-warp shared
-// rings are [rows][64] floats: lane l touches column j = c - l of row l, so the
-// bank (64 l + j) mod 32 = (c - l) mod 32 differs across the warp -- the
+// Memory.  The forward writes the framed alpha plane (4 B/cell) and the frames;
+// the reverse reads them back, so each cell costs: scores 4 B read twice, alpha
+// 4 B written + read, marginals 4 B written = 20 B/cell.  Every global access
+// is a coalesced 16-byte cp.async (loads) or 16-byte store (write-back of
+// 16-column tiles staged in shared memory).  Per-warp shared rings are
+// [rows][64] floats: lane l touches column j = c - l of row l, so the bank
+// (64 l + j) mod 32 = (c - l) mod 32 differs across the warp -- the
 // anti-diagonal access pattern is bank-conflict free.  A cell's score slot is
-// reused for its output (alpha in the forward, the marginal in the reverse),
-// so the forward needs one ring per warp and the reverse two.
+// reused for its output (alpha in the forward, the marginal in the reverse).
 //
-// Reverse pass: beta is propagated in gather/push form through registers and
-// shuffles (no atomics, deterministic):
+// Reverse pass: beta is propagated in push form through registers and shuffles
+// (no atomics, deterministic):
 //   beta_ij = 2^min(a_ij - S, 0) + sum over successors of beta_succ * w(succ <- ij)
 //   marginal_ij = beta_ij * (w_align + w_sky),  dS/dgap = sum beta*(w_up + w_left),
 //   dS/dT = path entropy (sum of non-negative terms).
@@ -40,12 +45,14 @@
 namespace d2pb {
 namespace wf {
 
-constexpr int kCW = 16;                 // chunk width (columns): unit of loads, write-backs and stages
-constexpr int kRW = 64;                 // ring width (columns) = row stride of the rings (4 chunks)
-constexpr int kSync = 16;               // steps between CTA barriers (= one stage)
-constexpr int kSkew = 80;               // minimum step skew between consecutive row-blocks (> 63, multiple of 16)
-constexpr int kMaxRB = 512;             // row-blocks per problem (L1 <= 16384)
-constexpr int kNW = 6;                  // warps per CTA
+constexpr int kCW = 16;                  // chunk width (columns) = steps per stage
+constexpr int kRW = 64;                  // ring width (columns) = row stride of the rings (4 chunks)
+constexpr int kMaxRB = 512;              // row-blocks per problem (L1 <= 16384)
+constexpr int kNW = 6;                   // warps per CTA
+constexpr int kRebase = 32;              // partition: rebase when the frame runs this far above R
+constexpr int kStageMask = 0xffff;       // progress word = (row-block ordinal << 16) | stages done
+constexpr int kSpinLimit = 1 << 20;      // bounded waits (polls of ~40 ns)
+constexpr unsigned kAll = 0xffffffffu;
 
 struct WarpSmem {
     float ringS[32 * kRW];        // scores; forward: alpha written in place; reverse: marginals in place
@@ -57,17 +64,18 @@ struct WarpSmem {
 
 struct Layout {  // per-problem workspace
     float* aplane;   // [nRB][33][L2m]: row 0 = row above (in this block's frames), rows 1..32 = alpha - O
-    float* frames;   // [nRB][L2m + 32] per-step frame O (exact integers stored as float)
+    float* frames;   // [nRB][L2m + 64] per-step frame O (exact integers stored as float)
     float2* bnd;     // [nRB][L2m] last row of each row-block: (a - O, O)
     float* bb;       // [nRB][L2m] reverse pushes into the row above
 };
 
 __host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+__host__ __device__ inline size_t frame_row(int L2m) { return (size_t)L2m + 64; }
 
 __host__ __device__ inline size_t per_problem_bytes(int L1m, int L2m) {
     const size_t nrb = (size_t)(L1m + 31) / 32;
     size_t b = align_up(nrb * 33 * (size_t)L2m * 4, 256);
-    b += align_up(nrb * (size_t)(L2m + 32) * 4, 256);
+    b += align_up(nrb * frame_row(L2m) * 4, 256);
     b += align_up(nrb * (size_t)L2m * 8, 256);
     b += align_up(nrb * (size_t)L2m * 4, 256);
     return b;
@@ -80,7 +88,7 @@ __device__ inline Layout carve(float* ws, int b, int L1m, int L2m) {
     L.aplane = (float*)base;
     base += align_up(nrb * 33 * (size_t)L2m * 4, 256);
     L.frames = (float*)base;
-    base += align_up(nrb * (size_t)(L2m + 32) * 4, 256);
+    base += align_up(nrb * frame_row(L2m) * 4, 256);
     L.bnd = (float2*)base;
     base += align_up(nrb * (size_t)L2m * 8, 256);
     L.bb = (float*)base;
@@ -96,37 +104,104 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 __device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;\n" ::); }
 __device__ __forceinline__ void cp_async_wait0() { asm volatile("cp.async.wait_group 0;\n" ::); }
 
-__device__ __forceinline__ float exp2i(int k) {  // exact 2^k (0 below 2^-126)
-    return k < -126 ? 0.f : __int_as_float((127 + min(k, 127)) << 23);
+// ---------------------------------------------------------------- progress flags
+__device__ __forceinline__ int ld_acquire(const int* p) {
+    int v;
+    asm volatile("ld.acquire.cta.shared::cta.b32 %0, [%1];\n"
+                 : "=r"(v)
+                 : "r"((unsigned)__cvta_generic_to_shared(p))
+                 : "memory");
+    return v;
 }
-
-// Load chunk `ch` (0-based columns [16ch, 16ch+16)) of `nrows` rows of a
-// row-major fp32 plane (row stride ld) into a [rows][64] ring; columns >= ncols
-// are zero-filled without being read.
-__device__ __forceinline__ void load_chunk(float* ring, const float* plane, int ld, int nrows, int ncols,
-                                           int ch, int lane) {
-    const int col0 = ch * kCW;
-    const int rc = col0 & (kRW - 1);
-    for (int p = lane; p < nrows * 4; p += 32) {
-        const int row = p >> 2, pc = p & 3;
-        const int c = col0 + pc * 4;
-        const bool in = c < ncols;
-        cp_async16(ring + row * kRW + rc + pc * 4, plane + (size_t)row * ld + (in ? c : 0), in ? 16 : 0);
+__device__ __forceinline__ void st_release(int* p, int v) {
+    asm volatile("st.release.cta.shared::cta.b32 [%0], %1;\n" ::"r"((unsigned)__cvta_generic_to_shared(p)), "r"(v)
+                 : "memory");
+}
+// Wait (all lanes) until *flag >= need.  Gives up after kSpinLimit polls and
+// records the failure in *err, so a broken dependency can never hang the GPU.
+__device__ __forceinline__ void wait_flag(const int* flag, int need, int* err) {
+    int it = 0;
+    if (*(volatile int*)err) {  // an earlier wait already gave up: do not stall again
+        __syncwarp();
+        return;
     }
+    while (ld_acquire(flag) < need) {
+        if (++it > kSpinLimit) {
+            *err = 1;
+            break;
+        }
+        __nanosleep(40);
+    }
+    __syncwarp();
 }
 
-// Write back chunk `ch` of a ring (rows < nrows, columns < ncols) to a plane.
-__device__ __forceinline__ void store_chunk(const float* ring, float* plane, int ld, int nrows, int ncols,
-                                            int ch, int lane) {
-    const int col0 = ch * kCW;
-    const int rc = col0 & (kRW - 1);
-    for (int p = lane; p < nrows * 4; p += 32) {
-        const int row = p >> 2, pc = p & 3;
-        const int c = col0 + pc * 4;
-        if (c < ncols) {
-            const float4 v = *reinterpret_cast<const float4*>(ring + row * kRW + rc + pc * 4);
-            float* dst = plane + (size_t)row * ld + c;
-            if (c + 4 <= ncols) {
+// log2 of a positive normal float, with the exponent split off exactly so that
+// lg2.approx only sees the mantissa in [1, 2), where its error is absolute.
+__device__ __forceinline__ float lg2_rr(float s) {
+    const int bits = __float_as_int(s);
+    const float m = __int_as_float((bits & 0x007fffff) | 0x3f800000);
+    return (float)((bits >> 23) - 127) + lg2f(m);
+}
+
+__device__ __forceinline__ float exp2i(int k) {  // exact 2^k for k in [-126, 127]; 0 below
+    return __int_as_float((127 + min(max(k, -127), 127)) << 23);
+}
+
+// A lane's share of copying a [rows][16] chunk between a row-major plane and a
+// [rows][64] ring: rows lane/4 + 8i (i < nit), columns 4*(lane%4) .. +3.
+// Addresses are set up once per row-block; a chunk copy is then a few
+// cp.async / vector loads and stores at immediate offsets.
+struct Tile {
+    const char* g0;   // plane element (row lane/4, column 4*(lane%4))
+    size_t g8;        // bytes from row r to row r + 8
+    unsigned s0;      // shared address of ring element (row lane/4, column 4*(lane%4))
+    int c0;           // 4*(lane%4)
+    int nit;          // rows lane/4 + 8i exist for i < nit
+};
+
+__device__ __forceinline__ Tile make_tile(const float* plane, int ld, const float* ring, int nrows, int lane) {
+    Tile t;
+    const int r0 = lane >> 2;
+    t.c0 = 4 * (lane & 3);
+    t.g0 = reinterpret_cast<const char*>(plane + (size_t)r0 * ld + t.c0);
+    t.g8 = (size_t)8 * ld * sizeof(float);
+    t.s0 = (unsigned)__cvta_generic_to_shared(ring + r0 * kRW + t.c0);
+    t.nit = nrows > r0 ? (nrows - r0 + 7) / 8 : 0;
+    return t;
+}
+
+__device__ __forceinline__ void cp_async16_s(unsigned s, const void* g, int src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(g), "r"(src_bytes));
+}
+
+// chunk ch (columns [16ch, 16ch+16)) plane -> ring; columns >= ncols zero-filled, not read
+template <int NI>
+__device__ __forceinline__ void tile_load(const Tile& t, int ch, int ncols) {
+    const bool in = kCW * ch + t.c0 < ncols;
+    const char* g = t.g0 + (in ? (size_t)(kCW * ch) * sizeof(float) : 0);
+    const unsigned s = t.s0 + (unsigned)(((kCW * ch) & (kRW - 1)) * sizeof(float));
+    const int nb = in ? 16 : 0;
+#pragma unroll
+    for (int i = 0; i < NI; ++i)
+        if (i < t.nit) cp_async16_s(s + i * 8 * kRW * sizeof(float), g + i * t.g8, nb);
+}
+
+// chunk ch ring -> plane (columns < ncols only)
+__device__ __forceinline__ void tile_store(const Tile& t, int ch, int ncols) {
+    const int c = kCW * ch + t.c0;
+    if (c >= ncols) return;
+    char* g = const_cast<char*>(t.g0) + (size_t)(kCW * ch) * sizeof(float);
+    const unsigned s = t.s0 + (unsigned)(((kCW * ch) & (kRW - 1)) * sizeof(float));
+    const bool whole = c + 4 <= ncols;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        if (i < t.nit) {
+            float4 v;
+            asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];\n"
+                         : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                         : "r"(s + i * 8 * kRW * (unsigned)sizeof(float)));
+            float* dst = reinterpret_cast<float*>(g + i * t.g8);
+            if (whole) {
                 __stcs(reinterpret_cast<float4*>(dst), v);
             } else {
                 const int rem = ncols - c;
@@ -154,50 +229,340 @@ __device__ __forceinline__ void load_row_chunk8(float2* ring, const float2* row,
     }
 }
 
-__device__ __forceinline__ int round16(int x) { return (x + 15) & ~15; }
+// ==========================================================================
+// forward sweep of one row-block
+// ==========================================================================
+struct FwdVars {
+    float left, uprev, uprecv;  // own previous output, previous "up", shuffled neighbour output
+    float O, pv;                // frame of the current step, middle-lane probe
+    float J, inc;               // group: frame jump at its first step, per-step increment
+    float gA, gB, dA, dB, dC;   // group offsets: g - J, g - inc, J + inc_prev, inc + J, 2 inc
+    float acc, R;               // partition of this lane's cells: sum 2^a = acc * 2^R
+};
 
-// Start step of each row-block in processing order q (multiples of 16 so that
-// every row-block stage coincides with one barrier interval):
-//   S(q) = max(S(q-1) + kSkew, S(q-NW) + dur16(q-NW));  sched[nRB] = total steps.
-__device__ void build_schedule(int* sched, int nRB, int L1, int dur_base, bool reverse) {
-    if (threadIdx.x == 0) {
-        int prev = -kSkew, total = 0;
-        for (int q = 0; q < nRB; ++q) {
-            int s = prev + kSkew;
-            if (q >= kNW) {
-                const int qq = q - kNW;
-                const int rr = reverse ? nRB - 1 - qq : qq;
-                s = max(s, sched[qq] + round16(dur_base + min(32, L1 - 32 * rr)));
-            }
-            sched[q] = s;
-            prev = s;
-            const int r = reverse ? nRB - 1 - q : q;
-            total = max(total, s + round16(dur_base + min(32, L1 - 32 * r)));
-        }
-        sched[nRB] = total;
+struct FwdCtx {
+    float* ring;             // this lane's ring row (ringS + lane*kRW)
+    const float2* bndring;   // last row of the row-block above, (a - O, O); (kNeg, 0) for row-block 0
+    float* arow0;            // aplane tile row 0 (row above, kept for the reverse)
+    float2* bout;            // boundary row for the next row-block
+    float* frow;             // frames of this row-block
+    float c, g;
+    int lane, nv, L2;
+    bool lane0, st31;        // lane == 0; lane == 31 and a row-block follows
+};
+
+// Start of a group of 4 steps: move the frame by the rounded middle-lane value
+// of the previous step (J), and predict the per-step drift of the next 3 steps
+// from the average over the last group (inc), so that stored values a - O stay
+// small between probes.  Frames stay exact integers.  pf: frames of the group.
+template <bool FULL>
+__device__ __forceinline__ void frame_group_start(const FwdCtx& C, FwdVars& V, float* pf) {
+    const float J = FULL ? rintf(V.pv) : (V.pv > kNegThresh ? rintf(V.pv) : 0.f);
+    const float incp = V.inc;
+    V.O += J;
+    V.J = J;
+    V.inc = fminf(fmaxf(rintf((J + 3.f * incp) * 0.25f), -16.f), 16.f);
+    V.gA = C.g - J;
+    V.gB = C.g - V.inc;
+    V.dA = J + incp;
+    V.dB = V.inc + J;
+    V.dC = 2.f * V.inc;
+    // partition base: keep O - R <= kRebase over the whole group (selects, no branch)
+    const float Dg = V.O - V.R;
+    const bool reb = Dg + 3.f * fmaxf(V.inc, 0.f) > (float)kRebase;
+    V.acc = reb ? V.acc * exp2i(-(int)fminf(Dg, 1.0e6f)) : V.acc;
+    V.R = reb ? V.O : V.R;
+    if (C.lane0) *reinterpret_cast<float4*>(pf) = make_float4(V.O, V.O + V.inc, V.O + 2.f * V.inc, V.O + 3.f * V.inc);
+}
+
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+
+// One forward cell: a = LSE(v0..v3) in max-shifted form (lg2 sees [1, 4],
+// where lg2.approx is accurate to an absolute 2^-22), and, for active lanes,
+// the cell's term of the partition function added to acc * 2^R.  A lane whose
+// term would leave the float range moves its base R up (rare, warp-uniform
+// branch).  Must be called by all 32 lanes together (it votes).
+__device__ __forceinline__ float fwd_cell(FwdVars& V, float v0, float v1, float v2, float v3, bool act) {
+    const float m = fmaxf(max3f(v0, v1, v2), v3);
+    const float s = (ex2f(v0 - m) + ex2f(v1 - m)) + (ex2f(v2 - m) + ex2f(v3 - m));
+    float t = m + (V.O - V.R);
+    const bool big = act && t > 64.f;
+    if (__any_sync(kAll, big)) {  // warp-uniform, rarely taken
+        const int kk = big ? (int)t - 16 : 0;
+        V.acc *= exp2i(-kk);
+        V.R += (float)kk;
+        t -= (float)kk;
     }
-    __syncthreads();
+    const float term = ex2f(t);
+    V.acc = act ? fmaf(s, term, V.acc) : V.acc;
+    return m + lg2f(s);
+}
+
+// 16 forward steps with every lane active (nv == 32, all columns inside
+// [0, L2)): per-stage base pointers, immediate offsets per step.
+__device__ __forceinline__ void fwd_stage_full(const FwdCtx& C, FwdVars& V, int k) {
+    const int c0 = (kCW * k - C.lane) & (kRW - 1);      // this lane's ring column at u = 0
+    float* const pA = C.ring + c0;                       // columns c0 .. 63
+    float* const pB = pA - kRW;                          // after the wrap past column 63
+    const float2* const pbnd = C.bndring + ((kCW * k) & (kRW - 1));  // lane 0: column 16k + u
+    float2* const pout = C.bout + (kCW * k - 31);        // lane 31: column 16k + u - 31
+    float* const prow0 = C.arow0 + kCW * k;              // lane 0: column 16k + u
+    float* const pfr = C.frow + kCW * k;
+    // the stage's scores, read before any of its alpha stores so that no load
+    // waits behind a store to the same ring
+    float scv[kCW];
+#pragma unroll
+    for (int u = 0; u < kCW; ++u) scv[u] = ((u < kRW - c0) ? pA : pB)[u];
+    float2 bvg[4];
+#pragma unroll
+    for (int u = 0; u < kCW; ++u) {
+        float* const p = ((u < kRW - c0) ? pA : pB) + u;
+        if ((u & 3) == 0) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) bvg[i] = pbnd[u + i];
+        }
+        if ((u & 3) == 0)
+            frame_group_start<true>(C, V, pfr + u);
+        else
+            V.O += V.inc;
+        const float dlt = ((u & 3) == 0) ? V.J : V.inc;
+        const float dd = ((u & 3) == 0) ? V.dA : (((u & 3) == 1) ? V.dB : V.dC);
+        const float g1 = ((u & 3) == 0) ? V.gA : V.gB;
+        const float2 bv = bvg[u & 3];
+        const float up = C.lane0 ? bv.x + (bv.y - (V.O - dlt)) : V.uprecv;
+        const float sc = scv[u];
+        const float v0 = fmaf(sc, C.c, V.uprev - dd);
+        const float v1 = up + g1;
+        const float v2 = V.left + g1;
+        const float v3 = fmaf(sc, C.c, -V.O);
+        const float aout = fwd_cell(V, v0, v1, v2, v3, true);
+        *p = aout;
+        if (C.st31) pout[u] = make_float2(aout, V.O);
+        if (C.lane0) prow0[u] = up;
+        V.left = aout;
+        V.uprev = up;
+        V.uprecv = __shfl_up_sync(kAll, aout, 1);
+        if ((u & 3) == 3) V.pv = __shfl_sync(kAll, aout, 16);
+    }
+}
+
+// 16 forward steps at the edges of a row-block (lanes not yet started, already
+// finished, or beyond nv), with per-lane activity masks.
+__device__ __forceinline__ void fwd_stage_part(const FwdCtx& C, FwdVars& V, int k) {
+#pragma unroll
+    for (int u = 0; u < kCW; ++u) {
+        const int tau = kCW * k + u;
+        const int j0 = tau - C.lane;
+        const bool act = (C.lane < C.nv) & (j0 >= 0) & (j0 < C.L2);
+        if ((u & 3) == 0)
+            frame_group_start<false>(C, V, C.frow + tau);
+        else
+            V.O += V.inc;
+        const float dlt = ((u & 3) == 0) ? V.J : V.inc;
+        const float dd = ((u & 3) == 0) ? V.dA : (((u & 3) == 1) ? V.dB : V.dC);
+        const float g1 = ((u & 3) == 0) ? V.gA : V.gB;
+        const float2 bv = C.bndring[tau & (kRW - 1)];
+        const float up = C.lane0 ? bv.x + (bv.y - (V.O - dlt)) : V.uprecv;
+        const int ix = j0 & (kRW - 1);
+        const float sc = C.ring[ix];
+        const float v0 = fmaf(sc, C.c, V.uprev - dd);
+        const float v1 = up + g1;
+        const float v2 = V.left + g1;
+        const float v3 = fmaf(sc, C.c, -V.O);
+        float aout = fwd_cell(V, v0, v1, v2, v3, act);  // all lanes: it votes
+        aout = act ? aout : kNeg;
+        if (act) {
+            C.ring[ix] = aout;
+            if (C.st31) C.bout[j0] = make_float2(aout, V.O);
+            if (C.lane0) C.arow0[j0] = up;
+        }
+        V.left = aout;
+        V.uprev = up;
+        V.uprecv = __shfl_up_sync(kAll, aout, 1);
+        if ((u & 3) == 3) {
+            const int mid = (max(0, tau - C.L2 + 1) + min(C.nv - 1, tau)) >> 1;
+            V.pv = __shfl_sync(kAll, aout, mid);
+        }
+    }
+}
+
+// ==========================================================================
+// reverse sweep of one row-block
+// ==========================================================================
+struct RevVars {
+    float anext, adnext;     // own alpha and row-above alpha at this step's column (loaded last step)
+    float pleft, pdiag, precv;
+    float gs, hs;            // per-stage partial sums (flushed into doubles)
+    float f0, f1;            // forward frames of anti-diagonals tf and tf-1
+};
+
+struct RevCtx {
+    float* ring;             // ringS + lane*kRW; ringA rows sit at fixed offsets from it
+    const float* bbring;     // pushes from the row-block below (zeros for the last row-block)
+    const float* fr;
+    float* bbout;            // pushes into the row above (row-block r-1), or null
+    float c, g, Sint, Sfrac;
+    int lane, nv, L2, P;
+    bool lastLane, push0;    // lane == nv-1; lane 0 of a row-block with a row-block above
+};
+
+// ringA rows relative to this lane's ringS row (WarpSmem layout: ringS, then ringA)
+constexpr int kUpOff = 32 * kRW;         // ringA row `lane`      (row above)
+constexpr int kOwnOff = 33 * kRW;        // ringA row `lane + 1`  (own row)
+
+// one reverse cell; shared by the full and the edge stages
+struct RevCell {
+    float wsum, send, pd, pl, gs, hs;
+};
+
+__device__ __forceinline__ RevCell rev_cell(const RevCtx& C, const RevVars& V, float a, float au, float al,
+                                            float ad, float sc, float f0, float d1, float d2, float inc) {
+    const float c0 = (f0 - C.Sint) - C.Sfrac;
+    const float gg = C.g + d1;
+    const float eu = (au - a) + gg;
+    const float el = (al - a) + gg;
+    const float ea = fmaf(sc, C.c, (ad - a) + d2);
+    const float es = fmaf(sc, C.c, -(a + f0));
+    const float wu = ex2f(eu), wl = ex2f(el), wa = ex2f(ea), wsk = ex2f(es);
+    const float lp = fminf(a + c0, 0.f);
+    const float binit = ex2f(lp);
+    const float beta = binit + (V.pleft + inc);
+    RevCell r;
+    const float pu = beta * wu;
+    r.pd = beta * wa;
+    r.pl = beta * wl;
+    r.send = pu + V.pdiag;
+    r.gs = pu + r.pl;
+    const float h = -fmaf(wu, eu, fmaf(wl, el, fmaf(wa, ea, wsk * es)));
+    r.hs = fmaf(beta, h, -binit * lp);
+    r.wsum = beta * (wa + wsk);
+    return r;
+}
+
+// 16 reverse steps with every lane active (nv == 32, columns in [1, L2)).
+// Here tf = P + 31 - 16k - u = 15 - u (mod 16): the stage reads frames
+// 16m-2 .. 16m+15 (tfs = 16m+15) once into registers.
+__device__ __forceinline__ void rev_stage_full(const RevCtx& C, RevVars& V, int k) {
+    const int m16 = (C.P + 16 - kCW * k) & (kRW - 1);  // 16m mod 64
+    const float4 q0 = *reinterpret_cast<const float4*>(C.fr + m16);
+    const float4 q1 = *reinterpret_cast<const float4*>(C.fr + m16 + 4);
+    const float4 q2 = *reinterpret_cast<const float4*>(C.fr + m16 + 8);
+    const float4 q3 = *reinterpret_cast<const float4*>(C.fr + m16 + 12);
+    const float2 qm = *reinterpret_cast<const float2*>(C.fr + ((m16 - 2) & (kRW - 1)));
+    const float F[18] = {qm.x, qm.y, q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z,
+                         q1.w, q2.x, q2.y, q2.z, q2.w, q3.x, q3.y, q3.z, q3.w};
+    const int cb = (C.P - kCW * k + 31 - C.lane) & (kRW - 1);  // this lane's column at u = 0
+    float* const qA = C.ring + cb;
+    float* const qB = qA + kRW;                                  // after the wrap below column 0
+    const int b0 = (C.P - kCW * k) & (kRW - 1);                  // lane 31's column at u = 0 (mult. of 16)
+    const float* const pb0 = C.bbring + b0;
+    const float* const pb1 = C.bbring + (b0 == 0 ? kRW : b0);
+    float* const pbo = C.bbout + (C.P - kCW * k + 31);           // lane 0's column at u = 0
+    float gs = 0.f, hs = 0.f;
+    // per group of 4 steps, every ring value the group reads is loaded before
+    // the group's marginal stores
+    // this lane's ring column at step u (u = 16: the first of the next stage)
+    auto pcol = [&](int u) { return ((u <= cb) ? qA : qB) - u; };
+    float alg[4], adg[4], scg[4], bbg[4];
+#pragma unroll
+    for (int u = 0; u < kCW; ++u) {
+        if ((u & 3) == 0) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                alg[i] = pcol(u + i + 1)[kOwnOff];
+                adg[i] = pcol(u + i + 1)[kUpOff];
+                scg[i] = pcol(u + i)[0];
+                bbg[i] = (u + i == 0) ? pb0[0] : pb1[-(u + i)];
+            }
+        }
+        float* const pcj = pcol(u);
+        const float f0 = F[17 - u];
+        const float a = V.anext, au = V.adnext;
+        const float al = alg[u & 3], ad = adg[u & 3];
+        const float inc = C.lastLane ? bbg[u & 3] : V.precv;
+        const RevCell r = rev_cell(C, V, a, au, al, ad, scg[u & 3], f0, F[16 - u] - f0, F[15 - u] - f0, inc);
+        *pcj = r.wsum;
+        if (C.push0) pbo[-u] = r.send;
+        gs += r.gs;
+        hs += r.hs;
+        V.precv = __shfl_down_sync(kAll, r.send, 1);
+        V.pdiag = r.pd;
+        V.pleft = r.pl;
+        V.anext = al;
+        V.adnext = ad;
+    }
+    V.gs += gs;
+    V.hs += hs;
+    V.f0 = F[1];
+    V.f1 = F[0];
+}
+
+// 16 reverse steps at the edges of a row-block, with per-lane activity masks.
+__device__ __forceinline__ void rev_stage_part(const RevCtx& C, RevVars& V, int k) {
+#pragma unroll
+    for (int u = 0; u < kCW; ++u) {
+        const int tau = kCW * k + u;
+        const int tf = C.P + C.nv - 1 - tau;            // forward step (anti-diagonal) of this step
+        const int j0 = C.P - tau + (C.nv - 1 - C.lane);
+        const bool act = (C.lane < C.nv) & (j0 >= 0) & (j0 < C.L2);
+        // frames of anti-diagonals tf, tf-1, tf-2 (rotated through registers).
+        // The forward's lane 0 stores the row above at column 0 in the frame of
+        // step 0, so frame indices below 0 read frame 0.
+        const float f2 = C.fr[max(tf - 2, 0) & (kRW - 1)];
+        const float f0 = V.f0;
+        const int cj = j0 & (kRW - 1), cl = (j0 - 1) & (kRW - 1);
+        const float a = V.anext;
+        const float au = V.adnext;
+        const bool hasLeft = j0 >= 1;
+        const float al = hasLeft ? C.ring[kOwnOff + cl] : kNeg;
+        const float ad = hasLeft ? C.ring[kUpOff + cl] : kNeg;
+        const float sc = C.ring[cj];
+        const float inc = C.lastLane ? C.bbring[cj] : V.precv;
+        const RevCell r = rev_cell(C, V, a, au, al, ad, sc, f0, V.f1 - f0, f2 - f0, inc);
+        // inactive lanes push nothing (their inputs may be garbage)
+        V.gs += act ? r.gs : 0.f;
+        V.hs += act ? r.hs : 0.f;
+        const float send = act ? r.send : 0.f;
+        if (act) {
+            C.ring[cj] = r.wsum;
+            if (C.push0) C.bbout[j0] = send;
+        }
+        V.precv = __shfl_down_sync(kAll, send, 1);
+        V.pdiag = act ? r.pd : 0.f;
+        V.pleft = act ? r.pl : 0.f;
+        V.anext = al;
+        V.adnext = ad;
+        V.f0 = V.f1;
+        V.f1 = f2;
+    }
 }
 
 // ==========================================================================
 // linear gap, value + marginals
 // ==========================================================================
 // Forward, row-block r (rows 32r .. 32r+nv-1, 0-based), local step tau:
-//   lane l works on column j = tau - l; all lanes share the frame O[tau].
-//   Stage k (tau = 16k..16k+15): lane 0 is in chunk k, the trailing lane in
-//   chunk >= k-2.  At its start chunk k-3 (finished) is written back as alpha
-//   and chunk k+1 of the scores is prefetched into the same ring slot.
+//   lane l works on column j = tau - l.  Stage k (tau = 16k..16k+15): lane 0 is
+//   in chunk k, the trailing lane in chunk >= k-2.  At its start chunk k-3
+//   (finished) is written back as alpha and chunk k+1 of the scores is
+//   prefetched into the same ring slot.
 // Reverse, row-block r, local step tau, P = 16*ceil((L2-1)/16):
 //   lane l works on column j = P - tau + (nv-1-l) (real work only for j <= L2-1);
 //   forward frame index tf = P + nv - 1 - tau.  At stage k the leading lane
 //   enters chunk n = P/16 - k - 1; chunks n..n+2 are read, chunk n+3 (finished)
 //   is written back as marginals and chunk n-1 is prefetched.
+// Progress: warp w publishes (ordinal << 16 | stages done) after every stage of
+// its current row-block (ordinal = r forward, nRB-1-r reverse), and
+// (ordinal << 16 | kStageMask) when the row-block is complete.
 __global__ void __launch_bounds__(kNW * 32) lin_marg_kernel(SwArgs p) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     WarpSmem& W = reinterpret_cast<WarpSmem*>(smem_raw)[threadIdx.x >> 5];
-    __shared__ int sched[kMaxRB + 1];
+    __shared__ int progF[kNW], progR[kNW];
     __shared__ __align__(16) float red[4 * 32];
-    __shared__ int sh_Sint;
+    __shared__ int sh_Sint, sh_err;
     __shared__ float sh_Sfrac;
 
     const int b = blockIdx.x;
@@ -216,7 +581,7 @@ __global__ void __launch_bounds__(kNW * 32) lin_marg_kernel(SwArgs p) {
     const int nRB = (L1 + 31) / 32;
     const int nch = (L2 + kCW - 1) / kCW;
     const size_t abs_ = (size_t)33 * L2m;       // aplane row-block stride
-    const size_t fst = (size_t)L2m + 32;        // frames row stride
+    const size_t fst = frame_row(L2m);          // frames row stride
 
     if (out && (L1 < L1m || L2 < L2m)) {  // zero the padded part of the marginals
         for (int i = warp; i < L1m; i += kNW) {
@@ -229,126 +594,118 @@ __global__ void __launch_bounds__(kNW * 32) lin_marg_kernel(SwArgs p) {
             if (p.value) p.value[b] = 0.f;
             if (p.grad_gap) p.grad_gap[b] = 0.f;
             if (p.grad_T) p.grad_T[b] = 0.f;
+            if (p.redo) p.redo[b] = 0;
         }
         return;
     }
+    if (threadIdx.x < kNW) {
+        progF[threadIdx.x] = -1;
+        progR[threadIdx.x] = -1;
+    }
+    if (threadIdx.x == 0) sh_err = 0;
+    __syncthreads();
 
     // ============================== forward ==============================
-    build_schedule(sched, nRB, L1, L2 - 1, false);
-    float acc = 0.f, R = 0.f;   // per-lane partition: sum 2^a = acc * 2^R
+    FwdVars V;
+    V.acc = 0.f;
+    V.R = 0.f;
     bool haveR = false;
-    {
-        const int Tf = sched[nRB];
-        int q = warp, nv = 0, ld = 0, sta = 0;
-        float O = 0.f, dlt = 0.f, dltp = 0.f;
-        float left = kNeg, uprev = kNeg, uprecv = kNeg;
-        for (int T0 = 0; T0 < Tf; T0 += kSync) {
-            if (q < nRB && T0 >= sched[q]) {
-                const int r = q;
-                const int k = (T0 - sched[q]) >> 4;
-                const float* srow = S + (size_t)(32 * r) * L2m;
-                const float2* brow = LY.bnd + (size_t)(r - 1) * L2m;
-                float* arow = LY.aplane + (size_t)r * abs_;
-                if (k == 0) {  // row-block prologue
-                    nv = min(32, L1 - 32 * r);
-                    O = dlt = dltp = 0.f;
-                    left = uprev = uprecv = kNeg;
-                    ld = sta = 0;
-                    __syncwarp();
-                    for (; ld < 2 && ld < nch; ++ld) {
-                        load_chunk(W.ringS, srow, L2m, nv, L2, ld, lane);
-                        if (r > 0) load_row_chunk8(W.bnd, brow, L2, ld, lane);
-                        cp_async_commit();
-                    }
-                    if (r > 0) {  // start the frame at the row above, column 0
-                        cp_async_wait0();
-                        __syncwarp();
-                        const float2 bv = W.bnd[0];
-                        O = bv.y + rintf(bv.x);
-                    }
-                } else {
-                    __syncwarp();
-                    // alpha write-back of finished chunks (rows 1..nv of this row-block's tile)
-                    while (sta < nch && (sta + 1) * kCW <= 16 * k - (nv - 1)) {
-                        store_chunk(W.ringS, arow + L2m, L2m, nv, L2, sta, lane);
-                        ++sta;
-                    }
+    for (int r = warp; r < nRB; r += kNW) {
+        const int nv = min(32, L1 - 32 * r);
+        const int nst = (L2 + nv - 1 + kCW - 1) / kCW;
+        const float* srow = S + (size_t)(32 * r) * L2m;
+        const float2* brow = LY.bnd + (size_t)(r - 1) * L2m;
+        float* arow = LY.aplane + (size_t)r * abs_;
+        const bool hasB = r > 0, hasD = r + 1 < nRB;
+        FwdCtx C;
+        C.ring = W.ringS + lane * kRW;
+        C.bndring = W.bnd;
+        C.arow0 = arow;
+        C.bout = LY.bnd + (size_t)r * L2m;
+        C.frow = LY.frames + (size_t)r * fst;
+        C.c = c;
+        C.g = g;
+        C.lane = lane;
+        C.nv = nv;
+        C.L2 = L2;
+        C.lane0 = lane == 0;
+        C.st31 = (lane == 31) && hasD;
+        const int* upflag = &progF[(warp + kNW - 1) % kNW];
+        const int upbase = (r - 1) << 16;
+
+        const Tile tS = make_tile(srow, L2m, W.ringS, nv, lane);        // scores -> ring
+        const Tile tA = make_tile(arow + L2m, L2m, W.ringS, nv, lane);  // ring (alpha) -> plane
+        __syncwarp();
+        if (!hasB) {  // no row above: the boundary ring reads as -inf
+            W.bnd[lane] = make_float2(kNeg, 0.f);
+            W.bnd[lane + 32] = make_float2(kNeg, 0.f);
+        }
+        int ld = 0, sta = 0;
+        for (; ld < 2 && ld < nch; ++ld) {
+            if (hasB) wait_flag(upflag, upbase + min(ld + 3, kStageMask), &sh_err);
+            tile_load<4>(tS, ld, L2);
+            if (hasB) load_row_chunk8(W.bnd, brow, L2, ld, lane);
+            cp_async_commit();
+        }
+        V.O = 0.f;
+        if (hasB) {  // start the frame at the row above, column 0
+            cp_async_wait0();
+            __syncwarp();
+            const float2 bv = W.bnd[0];
+            V.O = bv.y + rintf(bv.x);
+        }
+        if (!haveR) {
+            V.R = V.O;
+            haveR = true;
+        }
+        V.inc = 0.f;  // the first group start sets J, inc and the offsets
+        V.left = V.uprev = V.uprecv = kNeg;
+        V.pv = kNeg;
+
+        for (int k = 0; k < nst; ++k) {
+            if (k > 0) {
+                __syncwarp();
+                // alpha write-back of finished chunks (rows 1..nv of this row-block's tile)
+                while (sta < nch && (sta + 1) * kCW <= kCW * k - (nv - 1)) {
+                    tile_store(tA, sta, L2);
+                    ++sta;
                 }
                 if (ld <= k + 1 && ld < nch) {
-                    load_chunk(W.ringS, srow, L2m, nv, L2, ld, lane);
-                    if (r > 0) load_row_chunk8(W.bnd, brow, L2, ld, lane);
+                    if (hasB) wait_flag(upflag, upbase + min(ld + 3, kStageMask), &sh_err);
+                    tile_load<4>(tS, ld, L2);
+                    if (hasB) load_row_chunk8(W.bnd, brow, L2, ld, lane);
                     ++ld;
                 }
-                cp_async_commit();
-                cp_async_wait1();
-                __syncwarp();
-
-                const bool hasB = r > 0, hasD = r + 1 < nRB;
-                float* frow = LY.frames + (size_t)r * fst;
-#pragma unroll
-                for (int u = 0; u < kCW; ++u) {
-                    const int tau = 16 * k + u;
-                    const int j0 = tau - lane;
-                    const bool act = (lane < nv) & (j0 >= 0) & (j0 < L2);
-                    const int ix = lane * kRW + (j0 & (kRW - 1));
-                    const float Oprev = O - dlt;
-                    float up = uprecv;
-                    if (lane == 0) {
-                        const float2 bv = W.bnd[j0 & (kRW - 1)];
-                        up = hasB ? bv.x + (bv.y - Oprev) : kNeg;  // into frame O[tau-1]
-                        if (act) arow[j0] = up;                     // row above, kept for the reverse
-                    }
-                    const float x = W.ringS[ix] * c;
-                    const Lse4 rr = lse4(uprev + x - (dlt + dltp), up + g - dlt, left + g - dlt, x - O);
-                    const float aout = act ? rr.a : kNeg;
-                    if (act) {
-                        W.ringS[ix] = aout;
-                        if (!haveR) {
-                            R = O;
-                            haveR = true;
-                        }
-                        acc += ex2f(aout + (O - R));
-                        if (lane == 31 && hasD) LY.bnd[(size_t)r * L2m + j0] = make_float2(aout, O);
-                    }
-                    if (lane == 0 && tau < L2 + nv - 1) frow[tau] = O;
-                    left = aout;
-                    uprev = up;
-                    uprecv = __shfl_up_sync(0xffffffffu, aout, 1);
-                    // next frame: round the value of the middle active lane
-                    const int lo = max(0, tau - L2 + 1), hi = min(nv - 1, tau);
-                    const float pv = __shfl_sync(0xffffffffu, aout, (lo + hi) >> 1);
-                    const float nd = (pv > kNegThresh) ? rintf(pv) : 0.f;
-                    dltp = dlt;
-                    dlt = nd;
-                    O += nd;
-                    if (haveR && O - R > 32.f) {
-                        acc *= exp2i((int)(R - O));
-                        R = O;
-                    }
-                }
-                if (16 * (k + 1) >= L2 + nv - 1) {  // last stage of this row-block
-                    __syncwarp();
-                    while (sta < nch) {
-                        store_chunk(W.ringS, arow + L2m, L2m, nv, L2, sta, lane);
-                        ++sta;
-                    }
-                    cp_async_wait0();
-                    __syncwarp();
-                    q += kNW;
-                }
             }
-            __syncthreads();
+            cp_async_commit();
+            cp_async_wait1();
+            __syncwarp();
+            if ((nv == 32) && (kCW * k >= 31) && (kCW * k + kCW - 1 <= L2 - 1))
+                fwd_stage_full(C, V, k);
+            else
+                fwd_stage_part(C, V, k);
+            // lane 31 wrote this stage's boundary cells: publish them
+            if (C.st31) st_release(&progF[warp], (r << 16) | min(k + 1, kStageMask - 1));
         }
+        __syncwarp();
+        while (sta < nch) {
+            tile_store(tA, sta, L2);
+            ++sta;
+        }
+        cp_async_wait0();
+        __syncwarp();
+        if (lane == 31) st_release(&progF[warp], (r << 16) | kStageMask);
     }
 
     // ---- S = log2(sum_lanes acc*2^R + 2^0), kept as integer + fraction
     {
-        const int Rm = (int)block_max(haveR ? fmaxf(R, 0.f) : 0.f, red);
-        float part = haveR ? acc * exp2i((int)R - Rm) : 0.f;
+        const bool has = haveR && V.acc > 0.f;
+        const int Rm = (int)block_max(has ? fmaxf(V.R, 0.f) : 0.f, red);
+        float part = has ? V.acc * exp2i((int)V.R - Rm) : 0.f;
         if (threadIdx.x == 0) part += exp2i(-Rm);  // alpha[0,0] = 0
         const float tot = block_sum(part, red);
         if (threadIdx.x == 0) {
-            const float l2 = lg2f(tot);
+            const float l2 = lg2_rr(tot);
             const float fl = floorf(l2);
             sh_Sint = Rm + (int)fl;
             sh_Sfrac = l2 - fl;
@@ -356,59 +713,91 @@ __global__ void __launch_bounds__(kNW * 32) lin_marg_kernel(SwArgs p) {
         }
         __syncthreads();
     }
-    const float Sint = (float)sh_Sint;
-    const float Sfrac = sh_Sfrac;
 
     // ============================== reverse ==============================
     const int P = kCW * ((L2 - 1 + kCW - 1) / kCW);
-    build_schedule(sched, nRB, L1, P + 1, true);
     double gsum = 0.0, hsum = 0.0;
     {
-        const int Tb = sched[nRB];
-        int q = warp, nv = 0, ldn = 0, ldf = 0, stm = 0;
-        float pleft = 0.f, pdiag = 0.f, precv = 0.f;
-        float f0 = 0.f, f1 = 0.f;
-        for (int T0 = 0; T0 < Tb; T0 += kSync) {
-            if (q < nRB && T0 >= sched[q]) {
-                const int r = nRB - 1 - q;
-                const int k = (T0 - sched[q]) >> 4;
-                if (k == 0) nv = min(32, L1 - 32 * r);
+        RevVars RV;
+        for (int q = warp; q < nRB; q += kNW) {
+            const int r = nRB - 1 - q;
+            const int nv = min(32, L1 - 32 * r);
+            const int nst = (P + nv + kCW - 1) / kCW;
+            const int nfr = L2 + nv - 1;           // frames recorded for this row-block
+            const float* atile = LY.aplane + (size_t)r * abs_;
+            const float* srow = S + (size_t)(32 * r) * L2m;
+            const float* frow = LY.frames + (size_t)r * fst;
+            const float* bbrow = LY.bb + (size_t)(r + 1) * L2m;
+            const bool hasBelow = r + 1 < nRB;
+            RevCtx C;
+            C.ring = W.ringS + lane * kRW;
+            C.bbring = W.bb;
+            C.fr = W.fr;
+            C.bbout = r > 0 ? LY.bb + (size_t)r * L2m : LY.bb;
+            C.c = c;
+            C.g = g;
+            C.Sint = (float)sh_Sint;
+            C.Sfrac = sh_Sfrac;
+            C.lane = lane;
+            C.nv = nv;
+            C.L2 = L2;
+            C.P = P;
+            C.lastLane = lane == nv - 1;
+            C.push0 = (lane == 0) && (r > 0);
+            const int nvB = hasBelow ? min(32, L1 - 32 * (r + 1)) : 0;
+            const int* dnflag = &progR[(warp + kNW - 1) % kNW];
+            const int dnbase = (q - 1) << 16;
+            // stages of row-block r+1 that must be complete before bb chunk ch is
+            // read: its lane 0 pushes into column j at its step P + nvB - 1 - j
+            auto bb_need = [&](int ch) {
+                return dnbase + min(max(P + nvB - 1 - kCW * ch, 0) / kCW + 1, kStageMask);
+            };
+
+            const Tile tA = make_tile(atile, L2m, W.ringA, nv + 1, lane);  // alpha tile -> ringA
+            const Tile tS = make_tile(srow, L2m, W.ringS, nv, lane);       // scores -> ringS
+            const Tile tM = make_tile(out ? out + (size_t)(32 * r) * L2m : S, L2m, W.ringS, nv, lane);
+            __syncwarp();
+            if (!hasBelow) {  // no row-block below: its pushes read as zero
+                W.bb[lane] = 0.f;
+                W.bb[lane + 32] = 0.f;
+            }
+            int ldn = nch, stm = nch - 1;
+            int ldf = (min(P + nv - 1, nfr - 1) >> 4) + 1;
+            const int n0 = P / kCW - 1;
+            while (ldn > max(n0, 0)) {  // chunks n..n+2 for stage 0
+                --ldn;
+                tile_load<5>(tA, ldn, L2);
+                tile_load<4>(tS, ldn, L2);
+                if (hasBelow) {
+                    wait_flag(dnflag, bb_need(ldn), &sh_err);
+                    load_row_chunk4(W.bb, bbrow, L2, ldn, lane);
+                }
+            }
+            while (ldf > (max(P + nv - 1 - 17, 0) >> 4)) {
+                --ldf;
+                load_row_chunk4(W.fr, frow, nfr, ldf, lane);
+            }
+            cp_async_commit();
+            RV.pleft = RV.pdiag = RV.precv = 0.f;
+
+            for (int k = 0; k < nst; ++k) {
                 const int n = P / kCW - k - 1;       // chunk the leading lane enters
-                const int tfs = P + nv - 1 - 16 * k; // frame index at the stage start
-                const int nfr = L2 + nv - 1;         // frames recorded for this row-block
-                const float* atile = LY.aplane + (size_t)r * abs_;
-                const float* srow = S + (size_t)(32 * r) * L2m;
-                const float* frow = LY.frames + (size_t)r * fst;
-                const float* bbrow = LY.bb + (size_t)(r + 1) * L2m;
-                const bool hasBelow = r + 1 < nRB;
+                const int tfs = P + nv - 1 - kCW * k; // frame index at the stage start
                 __syncwarp();
-                if (k == 0) {
-                    pleft = pdiag = precv = 0.f;
-                    ldn = nch;
-                    ldf = (min(tfs, nfr - 1) >> 4) + 1;
-                    stm = nch - 1;
-                    while (ldn > max(n, 0)) {  // chunks n..n+2 for this stage
-                        --ldn;
-                        load_chunk(W.ringA, atile, L2m, nv + 1, L2, ldn, lane);
-                        load_chunk(W.ringS, srow, L2m, nv, L2, ldn, lane);
-                        if (hasBelow) load_row_chunk4(W.bb, bbrow, L2, ldn, lane);
-                    }
-                    while (ldf > (max(tfs - 17, 0) >> 4)) {
-                        --ldf;
-                        load_row_chunk4(W.fr, frow, nfr, ldf, lane);
-                    }
-                    cp_async_commit();
-                } else {
+                if (k > 0) {
                     while (stm >= 0 && stm >= n + 3) {  // finished marginal chunks
-                        if (out) store_chunk(W.ringS, out + (size_t)(32 * r) * L2m, L2m, nv, L2, stm, lane);
+                        if (out) tile_store(tM, stm, L2);
                         --stm;
                     }
                 }
                 while (ldn > max(n - 1, 0)) {  // prefetch for the next stage
                     --ldn;
-                    load_chunk(W.ringA, atile, L2m, nv + 1, L2, ldn, lane);
-                    load_chunk(W.ringS, srow, L2m, nv, L2, ldn, lane);
-                    if (hasBelow) load_row_chunk4(W.bb, bbrow, L2, ldn, lane);
+                    tile_load<5>(tA, ldn, L2);
+                    tile_load<4>(tS, ldn, L2);
+                    if (hasBelow) {
+                        wait_flag(dnflag, bb_need(ldn), &sh_err);
+                        load_row_chunk4(W.bb, bbrow, L2, ldn, lane);
+                    }
                 }
                 while (ldf > (max(tfs - 33, 0) >> 4)) {
                     --ldf;
@@ -417,79 +806,47 @@ __global__ void __launch_bounds__(kNW * 32) lin_marg_kernel(SwArgs p) {
                 cp_async_commit();
                 cp_async_wait1();
                 __syncwarp();
-                if (k == 0) {
-                    f0 = W.fr[max(tfs, 0) & (kRW - 1)];
-                    f1 = W.fr[max(tfs - 1, 0) & (kRW - 1)];
+                if (k == 0) {  // own alpha, row-above alpha and frames at the first step
+                    const int j0 = P + nv - 1 - lane;
+                    RV.anext = C.ring[kOwnOff + (j0 & (kRW - 1))];
+                    RV.adnext = C.ring[kUpOff + (j0 & (kRW - 1))];
+                    RV.f0 = W.fr[(P + nv - 1) & (kRW - 1)];
+                    RV.f1 = W.fr[max(P + nv - 2, 0) & (kRW - 1)];
                 }
-
-                float gs = 0.f, hs = 0.f;
-#pragma unroll
-                for (int u = 0; u < kCW; ++u) {
-                    const int tau = 16 * k + u;
-                    const int tf = tfs - u;
-                    const float f2 = W.fr[max(tf - 2, 0) & (kRW - 1)];
-                    const int j0 = P - tau + (nv - 1 - lane);
-                    const bool act = (lane < nv) & (j0 >= 0) & (j0 < L2);
-                    const int cj = j0 & (kRW - 1), cl = (j0 - 1) & (kRW - 1);
-                    const float a = W.ringA[(lane + 1) * kRW + cj];
-                    const float al = j0 >= 1 ? W.ringA[(lane + 1) * kRW + cl] : kNeg;
-                    const float au = W.ringA[lane * kRW + cj];
-                    const float ad = j0 >= 1 ? W.ringA[lane * kRW + cl] : kNeg;
-                    const float sc = W.ringS[lane * kRW + cj];
-                    const float x = sc * c;
-                    const float vs = x - f0, vu = au + (f1 - f0) + g, vl = al + (f1 - f0) + g;
-                    const float va = ad + (f2 - f0) + x;
-                    const float wu = ex2f(vu - a), wl = ex2f(vl - a), wa = ex2f(va - a), wsk = ex2f(vs - a);
-                    const float lp = fminf((a - Sfrac) + (f0 - Sint), 0.f);
-                    const float binit = ex2f(lp);
-                    float incoming = pleft + precv;
-                    if (lane == nv - 1) incoming = pleft + (hasBelow ? W.bb[cj] : 0.f);
-                    const float beta = binit + incoming;
-                    float send = 0.f, pushdiag = 0.f, pushleft = 0.f;
-                    if (act) {
-                        W.ringS[lane * kRW + cj] = beta * (wa + wsk);
-                        const float pushup = beta * wu;
-                        pushdiag = beta * wa;
-                        pushleft = beta * wl;
-                        send = pushup + pdiag;
-                        gs += pushup + pushleft;
-                        float h = wsk * (a - vs);
-                        if (va > kNegThresh) h += wa * (a - va);
-                        if (vu > kNegThresh) h += wu * (a - vu);
-                        if (vl > kNegThresh) h += wl * (a - vl);
-                        hs += beta * h - binit * lp;
-                        if (lane == 0 && r > 0) LY.bb[(size_t)r * L2m + j0] = send;
-                    }
-                    precv = __shfl_down_sync(0xffffffffu, send, 1);
-                    pdiag = pushdiag;
-                    pleft = pushleft;
-                    f0 = f1;
-                    f1 = f2;
-                }
-                gsum += (double)gs;
-                hsum += (double)hs;
-                if (16 * (k + 1) >= P + nv) {  // last stage of this row-block
-                    __syncwarp();
-                    while (stm >= 0) {
-                        if (out) store_chunk(W.ringS, out + (size_t)(32 * r) * L2m, L2m, nv, L2, stm, lane);
-                        --stm;
-                    }
-                    cp_async_wait0();
-                    __syncwarp();
-                    q += kNW;
-                }
+                RV.gs = 0.f;
+                RV.hs = 0.f;
+                if ((nv == 32) && (kCW * k >= P + 32 - L2) && (kCW * k + kCW - 1 <= P - 1))
+                    rev_stage_full(C, RV, k);
+                else
+                    rev_stage_part(C, RV, k);
+                gsum += (double)RV.gs;
+                hsum += (double)RV.hs;
+                // lane 0 wrote this stage's pushes into the row above: publish them
+                if (C.push0) st_release(&progR[warp], (q << 16) | min(k + 1, kStageMask - 1));
             }
-            __syncthreads();
+            __syncwarp();
+            while (stm >= 0) {
+                if (out) tile_store(tM, stm, L2);
+                --stm;
+            }
+            cp_async_wait0();
+            __syncwarp();
+            if (lane == 0) st_release(&progR[warp], (q << 16) | kStageMask);
         }
     }
 
     if (threadIdx.x == 0) {  // origin alpha[0,0] = 0 as an end state
-        const float lp0 = fminf(-Sfrac - Sint, 0.f);
+        const float lp0 = fminf(-sh_Sfrac - (float)sh_Sint, 0.f);
         hsum += (double)ex2f(lp0) * (double)(-lp0);
     }
     const double G = block_sum_d(gsum, reinterpret_cast<double*>(red));
     const double H = block_sum_d(hsum, reinterpret_cast<double*>(red));
+    // a dependency wait that gave up: the general engine recomputes this problem
+    // (the caller launches it)
+    const int redo = __syncthreads_or(sh_err);
     if (threadIdx.x == 0) {
+        if (p.redo) p.redo[b] = redo;
+        if (sh_err && p.status) atomicOr(p.status, 1);
         if (p.grad_gap) p.grad_gap[b] = (float)G;
         if (p.grad_T) p.grad_T[b] = (float)(H * (double)kLn2);
     }
@@ -505,7 +862,7 @@ size_t wavefront_workspace_bytes(int family, int B, int L1, int L2) {
 }
 
 int launch_wavefront(const SwArgs& a, int family, size_t ws_bytes, cudaStream_t st) {
-    if (family != 0 || a.mode != MODE_MARG) return -1;
+    if (family != 0 || a.mode != MODE_MARG || !a.redo) return -1;
     if (engine_forced_plane()) return -1;
     if (a.L2 % 4 != 0 || a.L1 > 32 * wf::kMaxRB || a.L1 == 0 || a.L2 == 0) return -1;
     if ((((uintptr_t)a.scores) & 15) != 0 || (a.out && (((uintptr_t)a.out) & 15) != 0)) return -1;
