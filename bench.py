@@ -172,6 +172,7 @@ def run_ours(args, cfg):
     import torch.distributed as dist
 
     import d2p_b200 as d2p
+    from d2p_b200.shard import gather_values
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -201,8 +202,8 @@ def run_ours(args, cfg):
         res = fwd(scores)
         (grad,) = torch.autograd.grad(res.value.sum(), scores)
         v = res.value.detach()
-        if world > 1:
-            dist.all_gather_into_tensor(vals_all, v)
+        if world > 1:  # rank r owns problems [r*B, (r+1)*B) of the global batch
+            vals_all.copy_(gather_values(v, world * cfg["B"]))
         return v, grad
 
     def barrier():
