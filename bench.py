@@ -340,7 +340,7 @@ def run_ours(args, cfg):
                        "parallelism": f"batch x{world} (one process per GPU), NCCL all_gather of values"},
             "e2e": {"value": round(e2e_gcups, 3), "unit": "GCUPS", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": cfg["B"] * 4, "ms_per_step": round(e2e_ms, 4)},
-            "gpu_launches": args.steps * 3,
+            "gpu_launches": args.steps * 4,
             "roofline": roofline,
             "clocks": clk,
         }

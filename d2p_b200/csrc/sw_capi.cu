@@ -50,10 +50,13 @@ static size_t op_bytes(int family, int op, int B, int L1, int L2) {
         case D2P_OP_FORWARD_BACKWARD: {
             // the fast path's workspace, or the plane engine's (which also serves as
             // the fix-up for problems the fast path flags), then one flag per problem
-            const size_t pe = plane_bytes(family, MODE_MARG, B, L1, L2);
+            size_t pe = plane_bytes(family, MODE_MARG, B, L1, L2);
             const size_t wf = wavefront_workspace_bytes(family, B, L1, L2);
             if (wf == 0) return pe;
-            return align256(pe > wf ? pe : wf) + align256((size_t)(B > 0 ? B : 1) * sizeof(int));
+            const size_t lf = family == D2P_FAMILY_LINEAR ? lin_fast_workspace_bytes(B, L1, L2) : 0;
+            pe = pe > wf ? pe : wf;
+            pe = pe > lf ? pe : lf;
+            return align256(pe) + align256((size_t)(B > 0 ? B : 1) * sizeof(int));
         }
         case D2P_OP_HVP:
             return plane_bytes(family, MODE_HVP, B, L1, L2);
@@ -126,16 +129,30 @@ int d2p_sw_forward_backward(const float* scores, const int* lengths, int B, int 
     a.grad_gap = grad_gap;
     a.grad_T = grad_temperature;
     a.ws = (float*)workspace;
-    const size_t pe = plane_bytes(D2P_FAMILY_LINEAR, MODE_MARG, B, L1, L2);
+    size_t pe = plane_bytes(D2P_FAMILY_LINEAR, MODE_MARG, B, L1, L2);
     const size_t wf = wavefront_workspace_bytes(D2P_FAMILY_LINEAR, B, L1, L2);
+    const size_t lf = lin_fast_workspace_bytes(B, L1, L2);
     if (wf > 0) {
-        // fast path; problems it flags (a cell sum outside its exponent window, or
-        // a dependency wait that gave up) are recomputed by the plane engine
-        a.redo = (int*)((char*)workspace + align256(pe > wf ? pe : wf));
-        int rc = launch_wavefront(a, D2P_FAMILY_LINEAR, workspace_bytes, st);
-        if (rc == D2P_OK) return launch_lin_plane(a, st);
+        // Fast paths, each recomputing what the previous one flagged:
+        //   linear-domain kernel (no parameter gradients requested) ->
+        //   log-domain wavefront kernel -> plane engine.
+        pe = pe > wf ? pe : wf;
+        pe = pe > lf ? pe : lf;
+        int* flags = (int*)((char*)workspace + align256(pe));
+        a.redo = flags;
+        a.only = nullptr;
+        int rc = launch_lin_fast(a, workspace_bytes, st);
+        if (rc == D2P_OK) a.only = flags;
+        else if (rc != kNotHandled) return rc;
+        rc = launch_wavefront(a, D2P_FAMILY_LINEAR, workspace_bytes, st);
+        if (rc == D2P_OK) {
+            a.only = flags;
+            a.redo = nullptr;
+            return launch_lin_plane(a, st);
+        }
         if (rc != kNotHandled) return rc;
         a.redo = nullptr;
+        a.only = nullptr;
     }
     return launch_lin_plane(a, st);
 }

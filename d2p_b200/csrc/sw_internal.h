@@ -55,9 +55,14 @@ struct SwArgs {
     int* status;                        // device status word (optional)
     const float* dot_with;              // [B, L1, L2] optional: param modes accumulate
     float* dot_out;                     //   dot_out[b] = sum_ij dot_with[b,i,j] * dP[b,i,j]
-    int* redo;                          // [B] fast path: out, set for problems it could not finish;
-                                        // plane engine: in, if set only those problems run
+    int* redo;                          // [B] out: set for problems the kernel could not finish
+    const int* only;                    // [B] in, optional: run only the problems whose entry is set
 };
+
+// linear-domain fast path (sw_linear.cu): value + marginals without parameter
+// gradients; returns -1 when the shape or arguments are not covered
+size_t lin_fast_workspace_bytes(int B, int L1, int L2);
+int launch_lin_fast(const SwArgs& a, size_t ws_bytes, cudaStream_t st);
 
 int launch_lin_plane(const SwArgs& a, cudaStream_t st);
 

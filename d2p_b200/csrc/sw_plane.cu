@@ -175,7 +175,7 @@ __global__ void __launch_bounds__(kPlaneThreads) lin_plane_kernel(SwArgs p) {
     __shared__ float sh_Sint, sh_Sfrac, sh_dS;
 
     const int b = blockIdx.x;
-    if (p.redo && p.redo[b] == 0) return;  // fix-up launch: only problems the fast path flagged
+    if (p.only && p.only[b] == 0) return;  // fix-up launch: only problems a fast path flagged
     const int L1m = p.L1, L2m = p.L2;
     // lengths are validated by the caller; clamp so a bad value can never index
     // outside the padded problem

@@ -41,18 +41,16 @@
 
 #include "sw_common.cuh"
 #include "sw_internal.h"
+#include "sw_ring.cuh"
 
 namespace d2pb {
 namespace wf {
 
-constexpr int kCW = 16;                  // chunk width (columns) = steps per stage
-constexpr int kRW = 64;                  // ring width (columns) = row stride of the rings (4 chunks)
+using namespace ring;
+
 constexpr int kMaxRB = 512;              // row-blocks per problem (L1 <= 16384)
 constexpr int kNW = 6;                   // warps per CTA
 constexpr int kRebase = 32;              // partition: rebase when the frame runs this far above R
-constexpr int kStageMask = 0xffff;       // progress word = (row-block ordinal << 16) | stages done
-constexpr int kSpinLimit = 1 << 20;      // bounded waits (polls of ~40 ns)
-constexpr unsigned kAll = 0xffffffffu;
 
 struct WarpSmem {
     float ringS[32 * kRW];        // scores; forward: alpha written in place; reverse: marginals in place
@@ -69,7 +67,6 @@ struct Layout {  // per-problem workspace
     float* bb;       // [nRB][L2m] reverse pushes into the row above
 };
 
-__host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 __host__ __device__ inline size_t frame_row(int L2m) { return (size_t)L2m + 64; }
 
 __host__ __device__ inline size_t per_problem_bytes(int L1m, int L2m) {
@@ -93,140 +90,6 @@ __device__ inline Layout carve(float* ws, int b, int L1m, int L2m) {
     base += align_up(nrb * (size_t)L2m * 8, 256);
     L.bb = (float*)base;
     return L;
-}
-
-// ---------------------------------------------------------------- cp.async
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, int src_bytes) {
-    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem), "r"(src_bytes));
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
-__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;\n" ::); }
-__device__ __forceinline__ void cp_async_wait0() { asm volatile("cp.async.wait_group 0;\n" ::); }
-
-// ---------------------------------------------------------------- progress flags
-__device__ __forceinline__ int ld_acquire(const int* p) {
-    int v;
-    asm volatile("ld.acquire.cta.shared::cta.b32 %0, [%1];\n"
-                 : "=r"(v)
-                 : "r"((unsigned)__cvta_generic_to_shared(p))
-                 : "memory");
-    return v;
-}
-__device__ __forceinline__ void st_release(int* p, int v) {
-    asm volatile("st.release.cta.shared::cta.b32 [%0], %1;\n" ::"r"((unsigned)__cvta_generic_to_shared(p)), "r"(v)
-                 : "memory");
-}
-// Wait (all lanes) until *flag >= need.  Gives up after kSpinLimit polls and
-// records the failure in *err, so a broken dependency can never hang the GPU.
-__device__ __forceinline__ void wait_flag(const int* flag, int need, int* err) {
-    int it = 0;
-    if (*(volatile int*)err) {  // an earlier wait already gave up: do not stall again
-        __syncwarp();
-        return;
-    }
-    while (ld_acquire(flag) < need) {
-        if (++it > kSpinLimit) {
-            *err = 1;
-            break;
-        }
-        __nanosleep(40);
-    }
-    __syncwarp();
-}
-
-// log2 of a positive normal float, with the exponent split off exactly so that
-// lg2.approx only sees the mantissa in [1, 2), where its error is absolute.
-__device__ __forceinline__ float lg2_rr(float s) {
-    const int bits = __float_as_int(s);
-    const float m = __int_as_float((bits & 0x007fffff) | 0x3f800000);
-    return (float)((bits >> 23) - 127) + lg2f(m);
-}
-
-__device__ __forceinline__ float exp2i(int k) {  // exact 2^k for k in [-126, 127]; 0 below
-    return __int_as_float((127 + min(max(k, -127), 127)) << 23);
-}
-
-// A lane's share of copying a [rows][16] chunk between a row-major plane and a
-// [rows][64] ring: rows lane/4 + 8i (i < nit), columns 4*(lane%4) .. +3.
-// Addresses are set up once per row-block; a chunk copy is then a few
-// cp.async / vector loads and stores at immediate offsets.
-struct Tile {
-    const char* g0;   // plane element (row lane/4, column 4*(lane%4))
-    size_t g8;        // bytes from row r to row r + 8
-    unsigned s0;      // shared address of ring element (row lane/4, column 4*(lane%4))
-    int c0;           // 4*(lane%4)
-    int nit;          // rows lane/4 + 8i exist for i < nit
-};
-
-__device__ __forceinline__ Tile make_tile(const float* plane, int ld, const float* ring, int nrows, int lane) {
-    Tile t;
-    const int r0 = lane >> 2;
-    t.c0 = 4 * (lane & 3);
-    t.g0 = reinterpret_cast<const char*>(plane + (size_t)r0 * ld + t.c0);
-    t.g8 = (size_t)8 * ld * sizeof(float);
-    t.s0 = (unsigned)__cvta_generic_to_shared(ring + r0 * kRW + t.c0);
-    t.nit = nrows > r0 ? (nrows - r0 + 7) / 8 : 0;
-    return t;
-}
-
-__device__ __forceinline__ void cp_async16_s(unsigned s, const void* g, int src_bytes) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(g), "r"(src_bytes));
-}
-
-// chunk ch (columns [16ch, 16ch+16)) plane -> ring; columns >= ncols zero-filled, not read
-template <int NI>
-__device__ __forceinline__ void tile_load(const Tile& t, int ch, int ncols) {
-    const bool in = kCW * ch + t.c0 < ncols;
-    const char* g = t.g0 + (in ? (size_t)(kCW * ch) * sizeof(float) : 0);
-    const unsigned s = t.s0 + (unsigned)(((kCW * ch) & (kRW - 1)) * sizeof(float));
-    const int nb = in ? 16 : 0;
-#pragma unroll
-    for (int i = 0; i < NI; ++i)
-        if (i < t.nit) cp_async16_s(s + i * 8 * kRW * sizeof(float), g + i * t.g8, nb);
-}
-
-// chunk ch ring -> plane (columns < ncols only)
-__device__ __forceinline__ void tile_store(const Tile& t, int ch, int ncols) {
-    const int c = kCW * ch + t.c0;
-    if (c >= ncols) return;
-    char* g = const_cast<char*>(t.g0) + (size_t)(kCW * ch) * sizeof(float);
-    const unsigned s = t.s0 + (unsigned)(((kCW * ch) & (kRW - 1)) * sizeof(float));
-    const bool whole = c + 4 <= ncols;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        if (i < t.nit) {
-            float4 v;
-            asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];\n"
-                         : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-                         : "r"(s + i * 8 * kRW * (unsigned)sizeof(float)));
-            float* dst = reinterpret_cast<float*>(g + i * t.g8);
-            if (whole) {
-                __stcs(reinterpret_cast<float4*>(dst), v);
-            } else {
-                const int rem = ncols - c;
-                dst[0] = v.x;
-                if (rem > 1) dst[1] = v.y;
-                if (rem > 2) dst[2] = v.z;
-            }
-        }
-    }
-}
-
-// one row, one chunk: 16 elements of 4 or 8 bytes
-__device__ __forceinline__ void load_row_chunk4(float* ring, const float* row, int ncols, int ch, int lane) {
-    if (lane < 4) {
-        const int c = ch * kCW + lane * 4;
-        const bool in = c < ncols;
-        cp_async16(ring + ((ch * kCW) & (kRW - 1)) + lane * 4, row + (in ? c : 0), in ? 16 : 0);
-    }
-}
-__device__ __forceinline__ void load_row_chunk8(float2* ring, const float2* row, int ncols, int ch, int lane) {
-    if (lane < 8) {
-        const int c = ch * kCW + lane * 2;
-        const bool in = c < ncols;
-        cp_async16(ring + ((ch * kCW) & (kRW - 1)) + lane * 2, row + (in ? c : 0), in ? 16 : 0);
-    }
 }
 
 // ==========================================================================
@@ -566,6 +429,7 @@ __global__ void __launch_bounds__(kNW * 32) lin_marg_kernel(SwArgs p) {
     __shared__ float sh_Sfrac;
 
     const int b = blockIdx.x;
+    if (p.only && p.only[b] == 0) return;  // fallback launch: only problems the fast path flagged
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int L1m = p.L1, L2m = p.L2;
     const int L1 = p.lengths ? min(max(p.lengths[2 * b], 0), L1m) : L1m;

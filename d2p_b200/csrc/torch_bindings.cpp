@@ -142,22 +142,30 @@ Tensor prep_grad(Tensor g, const Tensor& scores, const char* what) {
 // linear gap: raw computations
 // =============================================================================
 struct LinFwd {
-    Tensor value, marginals, dparams;  // dparams [2,B]: dS/dgap, dS/dT
+    Tensor value, marginals, dparams;  // dparams [2,B]: dS/dgap, dS/dT (undefined if not requested)
 };
 
+// want_params: also compute dS/dgap and dS/dT (needed by soft_sw_with_grads and
+// when gap or temperature require grad); without them the linear-domain fast
+// path can run.
 LinFwd lin_forward(const Tensor& scores, const Param& gap, const Param& T, const Tensor& lengths,
-                   const Shape& s) {
+                   const Shape& s, bool want_params) {
     auto opt = scores.options();
     LinFwd r;
     r.value = torch::empty({s.B}, opt);
     r.marginals = torch::empty({s.B, s.L1, s.L2}, opt);
-    r.dparams = torch::empty({2, s.B}, opt);
+    float* gg = nullptr;
+    float* gt = nullptr;
+    if (want_params) {
+        r.dparams = torch::empty({2, s.B}, opt);
+        gg = r.dparams.data_ptr<float>();
+        gt = gg + s.B;
+    }
     size_t wb = 0;
     Tensor ws = workspace(D2P_FAMILY_LINEAR, D2P_OP_FORWARD_BACKWARD, s, scores.device(), &wb);
     check_rc(d2p_sw_forward_backward(scores.data_ptr<float>(), len_ptr(lengths), s.B, s.L1, s.L2,
                                      gap.host, T.host, gap.dev, T.dev, r.value.data_ptr<float>(),
-                                     r.marginals.data_ptr<float>(), r.dparams.data_ptr<float>(),
-                                     r.dparams.data_ptr<float>() + s.B, ws.data_ptr(), wb, cur_stream()),
+                                     r.marginals.data_ptr<float>(), gg, gt, ws.data_ptr(), wb, cur_stream()),
              "d2p_sw_forward_backward");
     return r;
 }
@@ -219,7 +227,7 @@ class SoftSWFunction : public torch::autograd::Function<SoftSWFunction> {
         Param pg = read_param(gap, scores, "gap");
         Param pT = read_param(temperature, scores, "temperature");
         if (lengths.defined()) validate_lengths(lengths, s, scores.device());
-        LinFwd r = lin_forward(scores, pg, pT, lengths, s);
+        LinFwd r = lin_forward(scores, pg, pT, lengths, s, gap.requires_grad() || temperature.requires_grad());
         ctx->save_for_backward({scores, r.marginals, r.dparams, gap, temperature});
         ctx->saved_data["lengths"] = lengths.defined() ? c10::IValue(lengths) : c10::IValue();
         return {r.value, r.marginals};
@@ -241,14 +249,17 @@ class SoftSWFunction : public torch::autograd::Function<SoftSWFunction> {
             Tensor g = gv.to(torch::kFloat32).contiguous();
             if (g.device() != scores.device()) g = g.to(scores.device());
             grad_scores = torch::empty({s.B, s.L1, s.L2}, opt);
-            Tensor gp = torch::empty({2}, opt);
+            const bool params = dparams.defined();
+            Tensor gp = params ? torch::empty({2}, opt) : Tensor();
             check_rc(d2p_sw_value_backward(g.data_ptr<float>(), marginals.data_ptr<float>(),
-                                           dparams.data_ptr<float>(), 2, s.B, s.L1, s.L2,
-                                           grad_scores.data_ptr<float>(), gp.data_ptr<float>(),
-                                           cur_stream()),
+                                           params ? dparams.data_ptr<float>() : nullptr, params ? 2 : 0,
+                                           s.B, s.L1, s.L2, grad_scores.data_ptr<float>(),
+                                           params ? gp.data_ptr<float>() : nullptr, cur_stream()),
                      "d2p_sw_value_backward");
-            grad_gap = gp.narrow(0, 0, 1);
-            grad_T = gp.narrow(0, 1, 1);
+            if (params) {
+                grad_gap = gp.narrow(0, 0, 1);
+                grad_T = gp.narrow(0, 1, 1);
+            }
             have = true;
         }
         if (gm.defined() && gm.numel() > 0) {
@@ -290,7 +301,7 @@ std::tuple<Tensor, Tensor, Tensor, Tensor> soft_sw_with_grads_cuda(Tensor scores
     Param pg, pT;
     pg.host = (float)gap;
     pT.host = (float)temperature;
-    LinFwd r = lin_forward(scores, pg, pT, len, s);
+    LinFwd r = lin_forward(scores, pg, pT, len, s, true);
     return {r.value, r.marginals, r.dparams[0], r.dparams[1]};
 }
 

@@ -184,6 +184,46 @@ def test_wavefront_empty_problem(d2p, cuda_device):
     assert v[0].item() == 0.0 and v[1].item() == 0.0
 
 
+FASTLIN = [  # (B, L1, L2, T, gap, ragged): value + marginals without parameter gradients
+    (2, 1, 4, 1.0, -1.0, False), (3, 31, 16, 1.0, -1.0, False), (2, 32, 20, 0.5, -1.0, False),
+    (2, 33, 64, 1.0, -1.0, False), (4, 64, 100, 2.0, -1.0, False), (2, 65, 132, 1.0, -0.5, False),
+    (3, 100, 36, 0.3, -1.0, False), (2, 130, 260, 1.0, -1.0, False), (1, 7, 512, 1.0, -1.0, False),
+    (1, 200, 8, 1.0, -1.0, False), (2, 100, 120, 1.0, -1.0, False), (6, 70, 96, 1.0, -0.5, True),
+    (5, 130, 200, 0.5, -0.5, True), (4, 96, 96, 0.1, -1.0, False),
+]
+
+
+@pytest.mark.parametrize("B,L1,L2,T,gap,ragged", FASTLIN)
+def test_value_marginals_without_param_grads(d2p, cuda_device, B, L1, L2, T, gap, ragged):
+    """soft_sw_float with gap / T that need no gradient runs the linear-domain
+    path (the log-domain kernel recomputes whatever it flags)."""
+    s = scores(B, L1, L2, seed=L1 * 13 + L2 + B)
+    ln = lengths_for(B, L1, L2, seed=L2) if ragged else None
+    if ln is not None:
+        ln[0] = torch.tensor([L1, L2], dtype=torch.int32)
+    v, m = torch.ops.d2p.soft_sw_float(s.to(cuda_device), gap, T, None if ln is None else ln.to(cuda_device))
+    lnp = None if ln is None else ln.numpy()
+    r64 = oracle.sw_linear(s.numpy(), lnp, gap, T, "f64")
+    r32 = oracle.sw_linear(s.numpy(), lnp, gap, T, "f32")
+    check("value", v, r64["value"], r32["value"])
+    check("marginals", m, r64["marginals"], r32["marginals"])
+    if ln is not None:
+        mc = m.cpu()
+        for b, (l1, l2) in enumerate(ln.tolist()):
+            assert torch.count_nonzero(mc[b, l1:, :]) == 0
+            assert torch.count_nonzero(mc[b, :, l2:]) == 0
+
+
+def test_fast_paths_agree_512(d2p, cuda_device):
+    """The linear-domain path (no parameter gradients) and the log-domain path
+    (with them) give the same value and marginals at BASELINE config-2 size."""
+    s = scores(2, 512, 512, seed=5).to(cuda_device)
+    v1, m1 = torch.ops.d2p.soft_sw_float(s, -1.0, 1.0, None)
+    v2, m2, _, _ = torch.ops.d2p.soft_sw_with_grads(s, -1.0, 1.0, None)
+    torch.testing.assert_close(v1, v2, rtol=1e-5, atol=1e-4)
+    torch.testing.assert_close(m1, m2, rtol=0, atol=5e-5)
+
+
 @pytest.mark.parametrize("scale,T", [(40.0, 0.5), (8.0, 0.1)])
 def test_wavefront_extreme_scores(d2p, cuda_device, scale, T):
     """Large score magnitudes (alpha jumps of ~100 log2 units per cell) in one
@@ -202,6 +242,9 @@ def test_wavefront_extreme_scores(d2p, cuda_device, scale, T):
     check("marginals", m, r64["marginals"], r32["marginals"], noise=2.0)
     check("grad_gap", gg, r64["grad_gap"], r32["grad_gap"], rtol=1e-4, atol=1e-5, noise=2.0)
     check("grad_T", gt, r64["grad_T"], r32["grad_T"], rtol=1e-4, atol=1e-5, noise=2.0)
+    v2, m2 = torch.ops.d2p.soft_sw_float(s.to(cuda_device), -1.0, T, None)
+    check("value (no param grads)", v2, r64["value"], r32["value"])
+    check("marginals (no param grads)", m2, r64["marginals"], r32["marginals"], noise=2.0)
 
 
 def test_fp64_error_not_worse_than_reference_512(d2p, cuda_device):
