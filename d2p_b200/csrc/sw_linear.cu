@@ -5,27 +5,37 @@
 // logarithm.  In that domain the reference's log-sum-exp recurrence
 // (src/sw/kernels_cpu.cpp:70-150)
 //   Z_ij = P_ij (Z_{i-1,j-1} + 1) + G (Z_{i-1,j} + Z_{i,j-1}),   P = 2^(s c), G = 2^(gap c)
-// costs one exponential (P) and four FP operations per cell, and the reverse
-// pass (src/sw/kernels_cpu.cpp:156-279) becomes the outside recurrence
+// costs one exponential (P) and a handful of FP operations per cell, and the
+// reverse pass (src/sw/kernels_cpu.cpp:156-279) becomes the outside recurrence
 //   B_ij = 1 + P_{i+1,j+1} B_{i+1,j+1} + G (B_{i+1,j} + B_{i,j+1}),
 //   marginal_ij = B_ij P_ij (Z_{i-1,j-1} + 1) / Z_total,
 // with Z_total = 2^S = 1 + sum_ij Z_ij.  Cells outside the problem are 0.
 //
 // Range.  Every lane (row) keeps its own power-of-two frame, Z = z 2^E and
-// B = b 2^Q, re-anchored every 4 steps on the lane's own last value, so z and
-// b stay near 1; values from a neighbour lane or from the next row-block are
-// converted by exact 2^k factors, and a lane that starts inherits its
-// neighbour's frame.  If a value of a problem still leaves [2^-60, 2^60]
-// (score magnitudes far beyond the usual ones), the problem is flagged and the
-// caller recomputes it with the log-domain kernel (sw_wavefront.cu).
+// B = b 2^Q, one frame per group of 4 steps.  The frame of the next group is
+// decided one step early, from the lane's value of the step before (so the
+// integer work never sits on the dependency chain), and every factor that
+// converts a neighbour's value into the lane's frame is prepared with it.
+// Values from the row-block above or below come with their own frames.  If a
+// frame step leaves [2^-60, 2^60] (score magnitudes far beyond the usual ones,
+// or a temperature far below 1), the problem is flagged and the caller
+// recomputes it with the log-domain kernel (sw_wavefront.cu).
+//
+// Dependency chain.  A lane's new value depends on its neighbour's value of
+// the previous step through a warp shuffle and ONE fused multiply-add: the
+// neighbour's frame conversion is folded into the multiplier (G 2^(E'-E)).
 //
 // Structure (shared with sw_wavefront.cu): one CTA per problem; warps own
 // row-blocks of 32 rows (lane = row) and sweep them along anti-diagonals;
-// consecutive row-blocks hand their boundary rows over through L2-resident
-// workspace rows guarded by release/acquire progress words.  The forward
-// stores z in a diagonal-major plane (row = forward step + 2, 32 lanes per
-// row) so that both passes move it with one coalesced 128-byte access per
-// step; the reverse stages it 16 rows (2 KB) at a time through shared memory.
+// consecutive row-blocks are ordered by release/acquire progress words.  The
+// forward stores z in a diagonal-major plane (row = forward step + 2, 32 lanes
+// per row) with one coalesced 128-byte store per step, and each lane's frame
+// once per group; the reverse stages the plane 16 rows at a time through
+// shared memory.  Values that cross to the next row-block inside a pass (the
+// forward's last lane down, the reverse's lane-0 messages up) go through a
+// small shared-memory ring of the producing warp, one 16-byte store per group
+// by the boundary lane: reading a global line another warp has just written
+// costs about a microsecond, an order of magnitude more than the step it feeds.
 //
 // Reverse indexing: reverse step tau of a row-block works on forward
 // anti-diagonal tf = P + 31 - tau (P = 16 ceil((L2-1)/16)); lane l is at
@@ -44,39 +54,41 @@ using namespace ring;
 constexpr int kMaxRB = 512;              // row-blocks per problem (L1 <= 16384)
 constexpr int kNW = 6;                   // warps per CTA
 constexpr int kRebase = 32;              // partition: rebase when the frame runs this far above R
-constexpr float kWinLo = 8.673617380e-19f;   // 2^-60
-constexpr float kWinHi = 1.152921505e18f;    // 2^60
+constexpr int kJMax = 60;                // largest frame step (log2) a problem may take
+constexpr int kZC = 36;                  // row stride of the reverse's z / frame blocks
+constexpr int kHR = 128;                 // handoff ring: steps per parity
+constexpr int kBack = 8;                 // a producer overwrites ring steps its consumer read 8+ stages ago
 
+// Reverse z / frame blocks: column 3 holds lane 0's diagonal input (the row
+// above's last lane), columns 4..35 the row-block's own lanes 0..31, so lane l
+// reads column 3 + l for every l.
 struct WarpSmem {
-    float ringS[32 * kRW];   // scores [rows][64]; reverse: marginals written in place
-    float zr[2][16 * 32];    // reverse: z plane, one 16-step block per slot
-    int er[16 * 32];         // reverse: forward frames, 16 group slots (4 blocks of 4 groups)
-    float rr[kRW];           // reverse: row above the row-block (lane 0's diagonal input)
-    float2 bnd[kRW];         // forward: last row of the row-block above (z, frame bits)
-    float2 bbr[kRW];         // reverse: pushes from the row-block below (value, frame bits)
+    float ringS[32 * kRW];    // scores [rows][64]; reverse: marginals written in place
+    float zr[2][16 * kZC];    // reverse: z of 16 anti-diagonals, two slots
+    int er[16 * kZC];         // reverse: forward frames, 16 group slots
+    // handoff ring, written by this warp's boundary lane for the neighbouring
+    // row-block, by step (values) and by group (frames); two parities so that a
+    // warp's next row-block never overwrites what the neighbour still reads.
+    // Forward: lane 31's z; reverse: lane 0's messages to the row above.
+    float hv[2][kHR];
+    int hf[2][kHR / 4];
 };
+static_assert(sizeof(WarpSmem) % 16 == 0, "per-warp shared blocks must stay 16-byte aligned");
 
 struct Layout {  // per-problem workspace
     float* zpl;      // [nRB][ZT][32]   z of forward step t at row t + 2 (rows 0, 1: zeros)
     int* efr;        // [nRB][GT][32]   frame of each lane for each group of 4 forward steps
-    float* rab;      // [nRB][L2m + 64] lane 0's up input (row above) of column j at j + 1
-    float2* bnd;     // [nRB][L2m]      last row of each row-block: (z, frame bits)
-    float2* bbv;     // [nRB][L2m + 64] reverse pushes of lane 0 into the row above, at column + 15
 };
 
-// Row lengths leave room for the reverse's 16-entry staging blocks, which run
-// up to 31 entries past the last column.
-__host__ __device__ inline int zt_rows(int L2m) { return L2m + 64; }
-__host__ __device__ inline int gt_rows(int L2m) { return (L2m + 64) / 4; }
-__host__ __device__ inline int rb_len(int L2m) { return L2m + 64; }
+// Row counts cover every row the reverse's staging reaches past the last
+// step (the row above's z up to 78 rows past L2, its frames up to 20 groups).
+__host__ __device__ inline int zt_rows(int L2m) { return L2m + 96; }
+__host__ __device__ inline int gt_rows(int L2m) { return (L2m + 96) / 4; }
 
 __host__ __device__ inline size_t per_problem_bytes(int L1m, int L2m) {
     const size_t nrb = (size_t)(L1m + 31) / 32;
     size_t b = align_up(nrb * zt_rows(L2m) * 32 * 4, 256);
     b += align_up(nrb * gt_rows(L2m) * 32 * 4, 256);
-    b += align_up(nrb * (size_t)rb_len(L2m) * 4, 256);
-    b += align_up(nrb * (size_t)L2m * 8, 256);
-    b += align_up(nrb * (size_t)rb_len(L2m) * 8, 256);
     return b;
 }
 
@@ -87,80 +99,125 @@ __device__ inline Layout carve(float* ws, int b, int L1m, int L2m) {
     L.zpl = (float*)base;
     base += align_up(nrb * zt_rows(L2m) * 32 * 4, 256);
     L.efr = (int*)base;
-    base += align_up(nrb * gt_rows(L2m) * 32 * 4, 256);
-    L.rab = (float*)base;
-    base += align_up(nrb * (size_t)rb_len(L2m) * 4, 256);
-    L.bnd = (float2*)base;
-    base += align_up(nrb * (size_t)L2m * 8, 256);
-    L.bbv = (float2*)base;
     return L;
 }
 
 // 2^k for integer k, exact; 0 below 2^-126, clamped at 2^127
 __device__ __forceinline__ float p2(int k) { return exp2i(k); }
-// exponent of a positive normal float (0 for zero)
-__device__ __forceinline__ int expo(float v) { return v > 0.f ? (__float_as_int(v) >> 23) - 127 : 0; }
+// binary exponent of a non-negative value (0 for zero; 128 for inf / NaN)
+__device__ __forceinline__ int expo(float v) {
+    const int bits = __float_as_int(v);
+    return bits > 0 ? (bits >> 23) - 127 : 0;
+}
+
+// partition base after a frame change: sum Z = acc 2^R, contributions scaled by ps = 2^(E - R)
+__device__ __forceinline__ void part_factors(int E, int R, float& accsc, int& nR, float& ps) {
+    const int D = E - R;
+    const bool reb = D > kRebase;
+    accsc = reb ? p2(-D) : 1.f;
+    nR = reb ? E : R;
+    ps = p2(reb ? 0 : D);
+}
 
 // ==========================================================================
 // forward sweep of one row-block
 // ==========================================================================
-struct FwdVars {
-    float zl, zu, zd;   // own previous output, up input (as received), diag input (this lane's frame)
-    int E;              // this lane's frame
-    int Eup_last;       // lane l-1's frame when it produced the up input received next
-    float d0, d1;       // 2^(E_{l-1} - E) for outputs lane l-1 sent in the previous / this group
+struct FwdF {           // one group of 4 forward steps, for frame E
+    float d0, d1;       // 2^(E_{l-1} - E) for the up input of the first / other steps (lane 0: 0)
+    float Gd0, Gd1;     // G d0, G d1
     float fs;           // 2^-E: the +1 start term in this frame
+    float za[4];        // lane 0: the row above's value for each step, in frame E (other lanes: 0)
+};
+
+struct FwdVars {
+    float zl, zd, zsh;  // own z of the previous step; diagonal input of this step; lane l-1's last z
+    int E, Eup;         // own frame; lane l-1's frame in this group
+    int Esent;          // edge stages: lane l-1's frame of the value in zsh
+    FwdF f;
+    int nE, nEup;       // the next group, decided one step early
+    float nfJ;
+    FwdF nf;
     float acc, ps;      // partition of this lane's cells: sum Z = acc 2^R; ps = 2^(E - R)
     int R;
-    float mn, mx;       // range of this lane's outputs
+    float naccsc, nps;
+    int nR;
+    int jmax;           // largest |frame step|
 };
 
 struct FwdCtx {
-    const float* ring;   // this lane's ring row
-    const float2* bndring;
-    float* zrow;         // zpl row 2 (forward step 0) of this row-block, this lane
-    int* erow;           // efr group 0 of this row-block, this lane
-    float* rab;          // rab of this row-block
-    float2* bout;        // bnd of this row-block
+    const float* ring;  // this lane's ring row
+    const float* av;    // handoff ring of the row above (its lane 31's z, by its step); zeros for r = 0
+    const int* af;      //   and its frames, by its group
+    float* ov;          // this row-block's handoff ring for the row-block below
+    int* of;
+    float* zrow;        // zpl row 2 (forward step 0) of this row-block, this lane
+    int* erow;          // efr group 0 of this row-block, this lane
     float c, G;
+    float notl0, isl0;  // lane != 0, lane == 0 as 1 / 0
     int lane, nv, L2;
-    bool lane0, st31;
+    bool l31;           // lane 31: hands its values to the row-block below
 };
 
-// partition base and start term after a change of E
-__device__ __forceinline__ void fwd_frame_factors(FwdVars& V) {
-    int D = V.E - V.R;
-    const bool reb = D > kRebase;
-    V.acc = reb ? V.acc * p2(-D) : V.acc;
-    V.R = reb ? V.E : V.R;
-    D = reb ? 0 : D;
-    V.ps = p2(D);
-    V.fs = p2(-V.E);
+// Factors of group g in frame E; eup0 / eup1: lane l-1's frames of the values
+// lane l receives in the group's first / other steps.  Lane 0's up input is
+// the row above's last lane at forward step t + 31: step 4g + 31 (its group
+// g + 7) for the group's first step, 4g + 32 .. 4g + 34 (group g + 8) for the
+// others.
+__device__ __forceinline__ FwdF fwd_factors(const FwdCtx& C, int E, int eup0, int eup1, int g) {
+    FwdF f;
+    f.d0 = p2(eup0 - E) * C.notl0;
+    f.d1 = p2(eup1 - E) * C.notl0;
+    f.Gd0 = C.G * f.d0;
+    f.Gd1 = C.G * f.d1;
+    f.fs = p2(-E);
+    const float a0 = C.av[(4 * g + 31) & (kHR - 1)];
+    const float4 a = *reinterpret_cast<const float4*>(C.av + ((4 * g + 32) & (kHR - 1)));
+    const float f0 = p2(C.af[(g + 7) & (kHR / 4 - 1)] - E) * C.isl0;
+    const float f1 = p2(C.af[(g + 8) & (kHR / 4 - 1)] - E) * C.isl0;
+    f.za[0] = a0 * f0;
+    f.za[1] = a.x * f1;
+    f.za[2] = a.y * f1;
+    f.za[3] = a.z * f1;
+    return f;
 }
 
-// group start (every 4 steps): re-anchor this lane's frame on its last output
-// and set the conversion factors for lane l-1's outputs (d0: the one it sent
-// in the previous step, d1: those it sends in this group).  Returns lane
-// l-1's frame of the previous step (needed by a lane that starts right now).
-__device__ __forceinline__ int fwd_group_start(FwdVars& V) {
+// At the last step of a group (before its cell): the next group's frame from
+// the lane's previous value, and every factor of group g (the next one).  In
+// edge stages lane l-1 may have changed frame inside the group (it started),
+// so its current frame is read again.
+template <bool FULL>
+__device__ __forceinline__ void fwd_lookahead(const FwdCtx& C, FwdVars& V, int g) {
     const int J = expo(V.zl);
-    V.E += J;
-    const float fJ = p2(-J);
-    V.zl *= fJ;
-    V.zd *= fJ;
-    const int Eup = __shfl_up_sync(kAll, V.E, 1);
-    const int before = V.Eup_last;
-    V.d0 = p2(V.Eup_last - V.E);
-    V.d1 = p2(Eup - V.E);
-    V.Eup_last = Eup;
-    fwd_frame_factors(V);
-    return before;
+    V.jmax = max(V.jmax, abs(J));
+    V.nE = V.E + J;
+    V.nEup = __shfl_up_sync(kAll, V.nE, 1);
+    const int eup_now = FULL ? V.Eup : __shfl_up_sync(kAll, V.E, 1);
+    V.nfJ = p2(-J);
+    V.nf = fwd_factors(C, V.nE, eup_now, V.nEup, g);
+    part_factors(V.nE, V.R, V.naccsc, V.nR, V.nps);
 }
 
-// lane 0's up input: the row-block above's last row, (z, frame) -> frame E
-__device__ __forceinline__ float from_above(float2 bv, int E) { return bv.x * p2(__float_as_int(bv.y) - E); }
+__device__ __forceinline__ void fwd_apply(FwdVars& V) {
+    V.zl *= V.nfJ;
+    V.zd *= V.nfJ;
+    V.E = V.nE;
+    V.Eup = V.nEup;
+    V.f = V.nf;
+    V.acc *= V.naccsc;
+    V.R = V.nR;
+    V.ps = V.nps;
+}
 
-// 16 forward steps with every lane active: per-stage pointers, immediate offsets
+// one cell, step i of its group; returns z, and the up input in this frame
+// (the next step's diagonal input)
+__device__ __forceinline__ float fwd_cell(const FwdCtx& C, const FwdVars& V, int i, float sc, float& zuin) {
+    const float P = ex2f(sc * C.c);
+    const float rest = fmaf(C.G, V.zl + V.f.za[i], P * (V.zd + V.f.fs));
+    zuin = fmaf(V.zsh, i == 0 ? V.f.d0 : V.f.d1, V.f.za[i]);
+    return fmaf(i == 0 ? V.f.Gd0 : V.f.Gd1, V.zsh, rest);
+}
+
+// 16 forward steps with every lane active
 __device__ __forceinline__ void fwd_stage_full(const FwdCtx& C, FwdVars& V, int k) {
     const int c0 = (kCW * k - C.lane) & (kRW - 1);   // this lane's ring column at u = 0
     const float* const pA = C.ring + c0;
@@ -168,215 +225,243 @@ __device__ __forceinline__ void fwd_stage_full(const FwdCtx& C, FwdVars& V, int 
     float scv[kCW];  // the stage's scores, read before anything else happens
 #pragma unroll
     for (int u = 0; u < kCW; ++u) scv[u] = ((u < kRW - c0) ? pA : pB)[u];
-    const float2* const pbnd = C.bndring + ((kCW * k) & (kRW - 1));  // lane 0: column 16k + u
     float* const pz = C.zrow + (size_t)(kCW * k) * 32;
-    float2* const pout = C.bout + (kCW * k - 31);                     // lane 31: column 16k + u - 31
-    float* const prab = C.rab + kCW * k + 1;
     int* const pe = C.erow + (size_t)(kCW * k / 4) * 32;
+    float zq[4];
 #pragma unroll
     for (int u = 0; u < kCW; ++u) {
-        if ((u & 3) == 0) fwd_group_start(V);
-        const float zu_n = V.zu * (((u & 3) == 0) ? V.d0 : V.d1);
-        const float zu_in = C.lane0 ? from_above(pbnd[u], V.E) : zu_n;
-        const float P = ex2f(scv[u] * C.c);
-        const float z = fmaf(C.G, zu_in + V.zl, P * (V.zd + V.fs));
+        const int i = u & 3;
+        if (i == 0) fwd_apply(V);
+        if (i == 3) fwd_lookahead<true>(C, V, 4 * k + (u >> 2) + 1);
+        float zuin;
+        const float z = fwd_cell(C, V, i, scv[u], zuin);
         V.acc = fmaf(z, V.ps, V.acc);
-        V.mn = fminf(V.mn, z);
-        V.mx = fmaxf(V.mx, z);
         pz[(size_t)u * 32] = z;
-        if (C.st31) pout[u] = make_float2(z, __int_as_float(V.E));
-        if (C.lane0) prab[u] = zu_in;
-        if ((u & 3) == 3) pe[(u >> 2) * 32] = V.E;
-        V.zd = zu_in;
+        zq[i] = z;
+        if (i == 3) {
+            const int g = 4 * k + (u >> 2);
+            pe[(u >> 2) * 32] = V.E;
+            sts_group_pred(C.ov + ((4 * g) & (kHR - 1)), C.of + (g & (kHR / 4 - 1)),
+                           make_float4(zq[0], zq[1], zq[2], zq[3]), V.E, C.l31);
+        }
+        V.zd = zuin;
         V.zl = z;
-        V.zu = __shfl_up_sync(kAll, z, 1);
+        V.zsh = __shfl_up_sync(kAll, z, 1);
     }
 }
 
-// edge stages: per-lane activity masks; a lane that starts (column 0) takes
-// lane l-1's frame (lane 0: the frame of the row above) so that its first
-// value is near 1
+// edge stages: per-lane activity; a lane that starts (column 0) takes the
+// frame of the value it receives (lane 0 starts in the frame of the row above)
 __device__ __forceinline__ void fwd_stage_part(const FwdCtx& C, FwdVars& V, int k) {
-#pragma unroll 4
-    for (int u = 0; u < kCW; ++u) {
-        const int tau = kCW * k + u;
-        const int j0 = tau - C.lane;
-        const bool act = (C.lane < C.nv) & (j0 >= 0) & (j0 < C.L2);
-        int Eup_before = V.Eup_last;  // lane l-1's frame at the previous step
-        if ((u & 3) == 0) Eup_before = fwd_group_start(V);
-        const int Eup = __shfl_up_sync(kAll, V.E, 1);
-        const float2 bv = C.bndring[tau & (kRW - 1)];
-        if ((C.lane < C.nv) && j0 == 0) {  // this lane starts: adopt the neighbour's frame
-            V.E = C.lane0 ? __float_as_int(bv.y) : Eup;
-            V.d0 = p2(Eup_before - V.E);
-            V.d1 = 1.f;
-            V.zl = V.zd = 0.f;
-            fwd_frame_factors(V);
+    const bool live = C.lane < C.nv;
+    float zq[4];
+#pragma unroll 1
+    for (int q = 0; q < 4; ++q) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int t = kCW * k + 4 * q + i;
+            const int j0 = t - C.lane;
+            const bool act = live & (j0 >= 0) & (j0 < C.L2);
+            if (i == 0) fwd_apply(V);
+            if (live && j0 == 0 && C.lane > 0) {
+                V.E = V.Esent;
+                V.f = fwd_factors(C, V.E, V.Esent, i == 0 ? V.Eup : V.Esent, 4 * k + q);
+                float accsc, ps;
+                int R;
+                part_factors(V.E, V.R, accsc, R, ps);
+                V.acc *= accsc;
+                V.R = R;
+                V.ps = ps;
+            }
+            if (i == 3) fwd_lookahead<false>(C, V, 4 * k + q + 1);
+            float zuin;
+            float z = fwd_cell(C, V, i, C.ring[j0 & (kRW - 1)], zuin);
+            z = act ? z : 0.f;
+            V.acc = fmaf(z, V.ps, V.acc);
+            C.zrow[(size_t)t * 32] = z;
+            zq[i] = z;
+            if (i == 3) {
+                const int g = t >> 2;
+                C.erow[(size_t)g * 32] = V.E;
+                sts_group_pred(C.ov + ((4 * g) & (kHR - 1)), C.of + (g & (kHR / 4 - 1)),
+                               make_float4(zq[0], zq[1], zq[2], zq[3]), V.E, C.l31);
+            }
+            V.zd = act ? zuin : 0.f;
+            V.zl = z;
+            V.zsh = __shfl_up_sync(kAll, z, 1);
+            V.Esent = __shfl_up_sync(kAll, V.E, 1);
         }
-        const float zu_n = V.zu * (((u & 3) == 0) ? V.d0 : V.d1);
-        const float zu_in = C.lane0 ? from_above(bv, V.E) : zu_n;
-        const float P = ex2f(C.ring[j0 & (kRW - 1)] * C.c);
-        float z = fmaf(C.G, zu_in + V.zl, P * (V.zd + V.fs));
-        z = act ? z : 0.f;
-        V.acc = fmaf(z, V.ps, V.acc);
-        V.mn = act ? fminf(V.mn, z) : V.mn;
-        V.mx = act ? fmaxf(V.mx, z) : V.mx;
-        C.zrow[(size_t)tau * 32] = z;
-        if (act && C.st31) C.bout[j0] = make_float2(z, __int_as_float(V.E));
-        if (act && C.lane0) C.rab[j0 + 1] = zu_in;
-        if ((u & 3) == 3) C.erow[(size_t)(tau >> 2) * 32] = V.E;
-        V.zd = act ? zu_in : 0.f;
-        V.zl = z;
-        V.zu = __shfl_up_sync(kAll, z, 1);
-        // lane l-1's frame for the output just received (it may have started this step)
-        V.Eup_last = __shfl_up_sync(kAll, V.E, 1);
     }
 }
 
 // ==========================================================================
 // reverse sweep of one row-block
 // ==========================================================================
+struct RevF {           // one group of 4 reverse steps, for frame Q
+    float d0, d1;       // 2^(Q_{l+1} - Q) for the message of the first / other steps (bottom lane: 0)
+    float Gd0, Gd1;
+    float fb[4];        // 2^-Q, plus for the bottom lane the push from below (frame Q)
+    float kA, kB, k2;   // 2^(Q + E_diag - S) for the group's two forward frame groups; 2^(Q - S)
+};
+
 struct RevVars {
-    float br, recv, pbp;  // own b of column j+1, message from lane l+1, own P*b of column j+1
-    int Q;                // this lane's reverse frame
-    int Qdn_last;         // lane l+1's frame when it sent the message received next
-    float d0, d1;         // 2^(Q_{l+1} - Q) for messages lane l+1 sent in the previous / this group
-    float fsq;            // 2^-Q: the +1 end term in this frame
-    float k2;             // 2^(Q - S)
-    float kA, kB;         // 2^(Q + E_diag - S) for the two forward groups a reverse group reads
-    float mn, mx;
+    float br, pbp, rsh; // own b and P*b of column j+1; message from lane l+1
+    int Q, Qdn;         // own frame; lane l+1's frame in this group
+    int Qsent;          // edge stages: lane l+1's frame of the message in rsh
+    RevF f;
+    int nQ, nQdn;
+    float nfJ;
+    RevF nf;
+    int jmax;
 };
 
 struct RevCtx {
     float* ring;          // ringS row of this lane
     const float* zr;      // WarpSmem::zr
     const int* er;        // WarpSmem::er
-    const float* rr;      // WarpSmem::rr
-    const float2* bbr;    // WarpSmem::bbr
-    float2* bbout;        // bbv of this row-block (pushes into the row above), index column + 15
+    const float* bv;      // handoff ring of the row-block below (its lane 0's messages, by its step); zeros for the last
+    const int* bf;        //   and its frames, by its group
+    float* ov;            // this row-block's handoff ring for the row-block above
+    int* of;
     float c, G, cS;       // cS = 2^-Sfrac
+    float notBot, isBot;  // lane != nv-1, lane == nv-1 as 1 / 0
     int Sint, lane, nv, L2, P;
-    int ecol;             // er column of this lane's diagonal input: lane l-1 (lane 0: 0)
-    bool lane0, lastLane, push0;
+    bool l0;              // lane 0: hands its messages to the row-block above
 };
 
-// k factors of the reverse group starting at anti-diagonal tf0 (tf0 = 3 mod 4).
-// The diagonal input of lane l at anti-diagonal tf is lane l-1's z of forward
-// group (tf-2)/4 (lane 0: the row above, kept in lane 0's frame of group
-// (tf-1)/4); over tf0, tf0-1, tf0-2, tf0-3 that is group A = (tf0-3)/4 + ... :
-//   lanes >= 1: A for the first two steps, B = A - 1 for the last two;
-//   lane 0:     A for the first three steps, B for the last.
-__device__ __forceinline__ void rev_k_factors(const RevCtx& C, RevVars& V, int tf0) {
-    const int gA = (tf0 - 3) >> 2;
-    const int EA = C.er[(gA & 15) * 32 + C.ecol];
-    const int EB = C.er[((gA - 1) & 15) * 32 + C.ecol];
-    V.kA = p2(V.Q + EA - C.Sint) * C.cS;
-    V.kB = p2(V.Q + EB - C.Sint) * C.cS;
-    V.fsq = p2(-V.Q);
-    V.k2 = p2(V.Q - C.Sint) * C.cS;
+// Factors of reverse group h (anti-diagonals tf0 = P + 31 - 4h down to tf0 - 3)
+// in frame Q; qdn0 / qdn1: lane l+1's frames of the messages received in the
+// group's first / other steps.  The diagonal input of lane l at anti-diagonal
+// tf is forward group (tf - 2) / 4 of lane l-1 (lane 0: group + 8 of the row
+// above's last lane): group gA for tf0 and tf0 - 1, gA - 1 for the rest.  The
+// bottom lane's message from below at step tau is the one lane 0 of the
+// row-block below sent at its step tau + 31 (same column): step 4h + 31 (its
+// group h + 7) for the group's first step, 4h + 32 .. 4h + 34 (group h + 8)
+// for the others.
+__device__ __forceinline__ RevF rev_factors(const RevCtx& C, int Q, int qdn0, int qdn1, int h) {
+    RevF f;
+    f.d0 = p2(qdn0 - Q) * C.notBot;
+    f.d1 = p2(qdn1 - Q) * C.notBot;
+    f.Gd0 = C.G * f.d0;
+    f.Gd1 = C.G * f.d1;
+    const float fsq = p2(-Q);
+    const float e0 = C.bv[(4 * h + 31) & (kHR - 1)];
+    const float4 e = *reinterpret_cast<const float4*>(C.bv + ((4 * h + 32) & (kHR - 1)));
+    const float g0 = p2(C.bf[(h + 7) & (kHR / 4 - 1)] - Q) * C.isBot;
+    const float g1 = p2(C.bf[(h + 8) & (kHR / 4 - 1)] - Q) * C.isBot;
+    f.fb[0] = fmaf(e0, g0, fsq);
+    f.fb[1] = fmaf(e.x, g1, fsq);
+    f.fb[2] = fmaf(e.y, g1, fsq);
+    f.fb[3] = fmaf(e.z, g1, fsq);
+    const int gA = C.P / 4 + 7 - h;
+    const int EA = C.er[(gA & 15) * kZC + 3 + C.lane];
+    const int EB = C.er[((gA - 1) & 15) * kZC + 3 + C.lane];
+    f.kA = p2(Q + EA - C.Sint) * C.cS;
+    f.kB = p2(Q + EB - C.Sint) * C.cS;
+    f.k2 = p2(Q - C.Sint) * C.cS;
+    return f;
 }
 
-__device__ __forceinline__ int rev_group_start(const RevCtx& C, RevVars& V, int tf0) {
+template <bool FULL>
+__device__ __forceinline__ void rev_lookahead(const RevCtx& C, RevVars& V, int h) {
     const int J = expo(V.br);
-    V.Q += J;
-    const float fJ = p2(-J);
-    V.br *= fJ;
-    V.pbp *= fJ;
-    const int Qdn = __shfl_down_sync(kAll, V.Q, 1);
-    const int before = V.Qdn_last;
-    V.d0 = p2(V.Qdn_last - V.Q);
-    V.d1 = p2(Qdn - V.Q);
-    V.Qdn_last = Qdn;
-    rev_k_factors(C, V, tf0);
-    return before;
+    V.jmax = max(V.jmax, abs(J));
+    V.nQ = V.Q + J;
+    V.nQdn = __shfl_down_sync(kAll, V.nQ, 1);
+    const int qdn_now = FULL ? V.Qdn : __shfl_down_sync(kAll, V.Q, 1);
+    V.nfJ = p2(-J);
+    V.nf = rev_factors(C, V.nQ, qdn_now, V.nQdn, h);
 }
 
-__device__ __forceinline__ float kdiag(const RevCtx& C, const RevVars& V, int w) {
-    if (w < 2) return V.kA;
-    if (w == 3) return V.kB;
-    return C.lane0 ? V.kA : V.kB;
+__device__ __forceinline__ void rev_apply(RevVars& V) {
+    V.br *= V.nfJ;
+    V.pbp *= V.nfJ;
+    V.Q = V.nQ;
+    V.Qdn = V.nQdn;
+    V.f = V.nf;
 }
 
-__device__ __forceinline__ float from_below(float2 bv, int Q) { return bv.x * p2(__float_as_int(bv.y) - Q); }
+// one cell, step i of its group: b, P*b, the message to lane l-1 and the marginal
+struct RevOut {
+    float b, pb, msg, mu;
+};
+__device__ __forceinline__ RevOut rev_cell(const RevCtx& C, const RevVars& V, int i, float sc, float ad) {
+    RevOut o;
+    const float P = ex2f(sc * C.c);
+    const float rest = fmaf(C.G, V.br, V.f.fb[i]);
+    o.b = fmaf(i == 0 ? V.f.d0 : V.f.d1, V.rsh, rest);
+    o.msg = fmaf(i == 0 ? V.f.Gd0 : V.f.Gd1, V.rsh, fmaf(C.G, rest, V.pbp));
+    o.pb = P * o.b;
+    o.mu = o.pb * fmaf(ad, i < 2 ? V.f.kA : V.f.kB, V.f.k2);
+    return o;
+}
 
 // 16 reverse steps with every lane active
 __device__ __forceinline__ void rev_stage_full(const RevCtx& C, RevVars& V, int k) {
-    const int m16 = C.P + 16 - kCW * k;                              // tf = m16 + 15 - u
-    const float* const zb = C.zr + ((m16 >> 4) & 1) * (16 * 32) + C.ecol;   // lane l-1's column
-    const int cb = (C.P + 31 - kCW * k - C.lane) & (kRW - 1);       // ring column at u = 0
+    const int m16 = C.P + 16 - kCW * k;                                   // tf = m16 + 15 - u
+    const float* const zb = C.zr + ((m16 >> 4) & 1) * (16 * kZC) + 3 + C.lane;
+    const int cb = (C.P + 31 - kCW * k - C.lane) & (kRW - 1);            // ring column at u = 0
     float* const qA = C.ring + cb;
-    float* const qB = qA + kRW;                                       // after the wrap below column 0
+    float* const qB = qA + kRW;                                            // after the wrap below column 0
     float scv[kCW];
 #pragma unroll
     for (int u = 0; u < kCW; ++u) scv[u] = (((u <= cb) ? qA : qB) - u)[0];
-    const int b0 = (C.P - kCW * k + 15) & (kRW - 1);                 // bbr index of lane 31 at u = 0
-    float2* const pbo = C.bbout + (C.P - kCW * k + 31 + 15);          // lane 0: column P - 16k + 31 - u
+    float mq[4];
 #pragma unroll
     for (int u = 0; u < kCW; ++u) {
-        const int tf = m16 + 15 - u;
-        if ((u & 3) == 0) rev_group_start(C, V, tf);
-        const float ad = C.lane0 ? C.rr[tf & (kRW - 1)] : zb[(15 - u) * 32];
-        const float rc = V.recv * (((u & 3) == 0) ? V.d0 : V.d1);
-        const float inc = C.lastLane ? from_below(C.bbr[(b0 - u) & (kRW - 1)], V.Q) : rc;
-        const float P = ex2f(scv[u] * C.c);
-        const float b = fmaf(C.G, V.br, inc) + V.fsq;
-        const float pb = P * b;
-        const float msg = fmaf(C.G, b, V.pbp);
-        const float mu = P * fmaf(b * ad, kdiag(C, V, u & 3), b * V.k2);
-        (((u <= cb) ? qA : qB) - u)[0] = mu;
-        if (C.push0) pbo[-u] = make_float2(msg, __int_as_float(V.Q));
-        V.mn = fminf(V.mn, b);
-        V.mx = fmaxf(V.mx, b);
-        V.recv = __shfl_down_sync(kAll, msg, 1);
-        V.br = b;
-        V.pbp = pb;
+        const int i = u & 3;
+        if (i == 0) rev_apply(V);
+        if (i == 3) rev_lookahead<true>(C, V, 4 * k + (u >> 2) + 1);
+        const RevOut o = rev_cell(C, V, i, scv[u], zb[(15 - u) * kZC]);
+        (((u <= cb) ? qA : qB) - u)[0] = o.mu;
+        mq[i] = o.msg;
+        if (i == 3) {
+            const int h = 4 * k + (u >> 2);
+            sts_group_pred(C.ov + ((4 * h) & (kHR - 1)), C.of + (h & (kHR / 4 - 1)),
+                           make_float4(mq[0], mq[1], mq[2], mq[3]), V.Q, C.l0);
+        }
+        V.rsh = __shfl_down_sync(kAll, o.msg, 1);
+        V.br = o.b;
+        V.pbp = o.pb;
     }
 }
 
-// edge stages: per-lane activity; a lane that starts (column L2-1) takes lane
-// l+1's frame (the bottom lane: the frame of the pushes from below)
+// edge stages: per-lane activity; a lane that starts (column L2-1, where
+// B = 1 + G B_{i+1,j} stays near 1) starts in frame 0
 __device__ __forceinline__ void rev_stage_part(const RevCtx& C, RevVars& V, int k) {
     const int m16 = C.P + 16 - kCW * k;
-    const float* const zb = C.zr + ((m16 >> 4) & 1) * (16 * 32) + C.ecol;
-#pragma unroll 4
-    for (int u = 0; u < kCW; ++u) {
-        const int tf = m16 + 15 - u;
-        const int j0 = tf - C.lane;
-        const bool act = (C.lane < C.nv) & (j0 >= 0) & (j0 < C.L2);
-        int Qdn_before = V.Qdn_last;
-        if ((u & 3) == 0) Qdn_before = rev_group_start(C, V, tf);
-        const int Qdn = __shfl_down_sync(kAll, V.Q, 1);
-        const float2 bv = C.bbr[(j0 + 15) & (kRW - 1)];
-        if ((C.lane < C.nv) && j0 == C.L2 - 1) {  // this lane starts: adopt the neighbour's frame
-            V.Q = C.lastLane ? __float_as_int(bv.y) : Qdn;
-            V.d0 = p2(Qdn_before - V.Q);
-            V.d1 = 1.f;
-            V.br = V.pbp = 0.f;
-            rev_k_factors(C, V, m16 + 15 - (u & ~3));
+    const float* const zb = C.zr + ((m16 >> 4) & 1) * (16 * kZC) + 3 + C.lane;
+    const bool live = C.lane < C.nv;
+    float mq[4];
+#pragma unroll 1
+    for (int q = 0; q < 4; ++q) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int u = 4 * q + i;
+            const int tf = m16 + 15 - u;
+            const int j0 = tf - C.lane;
+            const bool act = live & (j0 >= 0) & (j0 < C.L2);
+            if (i == 0) rev_apply(V);
+            if (live && j0 == C.L2 - 1) {
+                V.Q = 0;
+                V.f = rev_factors(C, 0, V.Qsent, i == 0 ? V.Qdn : V.Qsent, 4 * k + q);
+            }
+            if (i == 3) rev_lookahead<false>(C, V, 4 * k + q + 1);
+            const int ci = j0 & (kRW - 1);
+            const RevOut o = rev_cell(C, V, i, C.ring[ci], zb[(15 - u) * kZC]);
+            if (act) C.ring[ci] = o.mu;
+            const float msg = act ? o.msg : 0.f;
+            mq[i] = msg;
+            if (i == 3) {
+                const int h = 4 * k + q;
+                sts_group_pred(C.ov + ((4 * h) & (kHR - 1)), C.of + (h & (kHR / 4 - 1)),
+                               make_float4(mq[0], mq[1], mq[2], mq[3]), V.Q, C.l0);
+            }
+            V.rsh = __shfl_down_sync(kAll, msg, 1);
+            V.br = act ? o.b : 0.f;
+            V.pbp = act ? o.pb : 0.f;
+            V.Qsent = __shfl_down_sync(kAll, V.Q, 1);
         }
-        const float adz = (C.lane0 ? C.rr[tf & (kRW - 1)] : zb[(15 - u) * 32]);
-        const float ad = (j0 >= 1) ? adz : 0.f;
-        const float rc = V.recv * (((u & 3) == 0) ? V.d0 : V.d1);
-        const float inc = C.lastLane ? from_below(bv, V.Q) : rc;
-        const int ci = j0 & (kRW - 1);
-        const float P = ex2f(C.ring[ci] * C.c);
-        float b = fmaf(C.G, V.br, inc) + V.fsq;
-        const float mu = P * fmaf(b * ad, kdiag(C, V, u & 3), b * V.k2);
-        b = act ? b : 0.f;
-        const float pb = P * b;
-        float msg = fmaf(C.G, b, V.pbp);
-        msg = act ? msg : 0.f;
-        if (act) {
-            C.ring[ci] = mu;
-            if (C.push0) C.bbout[j0 + 15] = make_float2(msg, __int_as_float(V.Q));
-            V.mn = fminf(V.mn, b);
-            V.mx = fmaxf(V.mx, b);
-        }
-        V.recv = __shfl_down_sync(kAll, msg, 1);
-        V.br = b;
-        V.pbp = act ? pb : 0.f;
-        // lane l+1's frame for the message just received (it may have started this step)
-        V.Qdn_last = __shfl_down_sync(kAll, V.Q, 1);
     }
 }
 
@@ -385,14 +470,18 @@ __device__ __forceinline__ void rev_stage_part(const RevCtx& C, RevVars& V, int 
 // ==========================================================================
 // Progress words: warp w publishes (ordinal << 16 | stages done) for its
 // current row-block (ordinal = r forward, nRB-1-r reverse), and
-// (ordinal << 16 | kStageMask) when the row-block is complete.
-__global__ void __launch_bounds__(kNW * 32) lin_fast_kernel(SwArgs p) {
+// (ordinal << 16 | kStageMask) when the row-block is complete.  The staging
+// for stage k reads the neighbouring row-block up to its stage k + 3, so it
+// waits for k + 4 stages there.
+__global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     WarpSmem& W = reinterpret_cast<WarpSmem*>(smem_raw)[threadIdx.x >> 5];
     __shared__ int progF[kNW], progR[kNW];
     __shared__ __align__(16) float red[4 * 32];
-    __shared__ int sh_Sint, sh_err;
+    __shared__ int sh_Sint, sh_err, sh_bad;
     __shared__ float sh_Sfrac;
+    __shared__ __align__(16) float zv[kHR];   // handoff ring of a missing neighbour: zeros
+    __shared__ int zf[kHR / 4];
 
     const int b = blockIdx.x;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -429,90 +518,84 @@ __global__ void __launch_bounds__(kNW * 32) lin_fast_kernel(SwArgs p) {
         progF[threadIdx.x] = -1;
         progR[threadIdx.x] = -1;
     }
-    if (threadIdx.x == 0) sh_err = 0;
+    if (threadIdx.x < kHR) zv[threadIdx.x] = 0.f;
+    if (threadIdx.x < kHR / 4) zf[threadIdx.x] = 0;
+    if (threadIdx.x == 0) {
+        sh_err = 0;
+        sh_bad = 0;
+    }
     __syncthreads();
-
-    float wmn = 1.f, wmx = 1.f;  // range of every z and b this lane produced
+    // the neighbouring warps: the one that produces this warp's inputs and the
+    // one that consumes its outputs (row-block r-1 / r+1 forward, r+1 / r-1 reverse)
+    const int wprev = (warp + kNW - 1) % kNW, wnext = (warp + 1) % kNW;
+    WarpSmem& Wp = reinterpret_cast<WarpSmem*>(smem_raw)[wprev];
 
     // ============================== forward ==============================
     FwdVars V;
     V.acc = 0.f;
     V.R = 0;
+    V.E = 0;
+    V.jmax = 0;
     for (int r = warp; r < nRB; r += kNW) {
         const int nv = min(32, L1 - 32 * r);
         const int nst = (L2 + nv - 1 + kCW - 1) / kCW;
         const float* srow = S + (size_t)(32 * r) * L2m;
-        const float2* brow = LY.bnd + (size_t)(r - 1) * L2m;
         const bool hasB = r > 0, hasD = r + 1 < nRB;
         float* const zblk = LY.zpl + (size_t)r * zst;
         FwdCtx C;
         C.ring = W.ringS + lane * kRW;
-        C.bndring = W.bnd;
+        C.av = hasB ? Wp.hv[((r - 1) / kNW) & 1] : zv;
+        C.af = hasB ? Wp.hf[((r - 1) / kNW) & 1] : zf;
+        C.ov = W.hv[(r / kNW) & 1];
+        C.of = W.hf[(r / kNW) & 1];
         C.zrow = zblk + 2 * 32 + lane;
         C.erow = LY.efr + (size_t)r * est + lane;
-        C.rab = LY.rab + (size_t)r * rb_len(L2m);
-        C.bout = LY.bnd + (size_t)r * L2m;
         C.c = c;
         C.G = G;
+        C.notl0 = lane == 0 ? 0.f : 1.f;
+        C.isl0 = lane == 0 ? 1.f : 0.f;
         C.lane = lane;
         C.nv = nv;
         C.L2 = L2;
-        C.lane0 = lane == 0;
-        C.st31 = (lane == 31) && hasD;
-        const int* upflag = &progF[(warp + kNW - 1) % kNW];
-        const int upbase = (r - 1) << 16;
+        C.l31 = lane == 31;
         const Tile tS = make_tile(srow, L2m, W.ringS, nv, lane);
 
+        // this ring parity was last written for row-block r - 2kNW: its reader
+        // (row-block r - 2kNW + 1) must be complete before it is reused
+        if (r >= 2 * kNW) wait_flag(&progF[wnext], ((r - 2 * kNW + 1) << 16) | kStageMask, &sh_err);
         __syncwarp();
-        if (!hasB) {  // no row above: its values are zero
-            W.bnd[lane] = make_float2(0.f, __int_as_float(0));
-            W.bnd[lane + 32] = make_float2(0.f, __int_as_float(0));
-        }
-        // rows 0, 1 of the z plane (steps -2, -1) and the row above at column -1 are zero
+        // rows 0, 1 of the z plane (steps -2, -1) are zero
         zblk[lane] = 0.f;
         zblk[32 + lane] = 0.f;
-        if (lane == 0) C.rab[0] = 0.f;
-        int ld = 0;
-        for (; ld < 2 && ld < nch; ++ld) {
-            if (hasB) wait_flag(upflag, upbase + min(ld + 3, kStageMask), &sh_err);
-            tile_load<4>(tS, ld, L2);
-            if (hasB) load_row_chunk8(W.bnd, brow, L2, ld, lane);
-            cp_async_commit();
-        }
-        V.E = 0;
-        if (hasB) {
-            cp_async_wait0();
-            __syncwarp();
-            V.E = __float_as_int(W.bnd[0].y);
-        }
-        V.Eup_last = V.E;
-        V.zl = V.zu = V.zd = 0.f;
-        V.d0 = V.d1 = 1.f;
-        V.mn = V.mx = 1.f;
-        fwd_frame_factors(V);
-
+        if (0 < nch) tile_load<4>(tS, 0, L2);
+        cp_async_commit();
+        V.zl = V.zd = V.zsh = 0.f;
         for (int k = 0; k < nst; ++k) {
-            if (k > 0 && ld <= k + 1 && ld < nch) {
-                __syncwarp();
-                if (hasB) wait_flag(upflag, upbase + min(ld + 3, kStageMask), &sh_err);
-                tile_load<4>(tS, ld, L2);
-                if (hasB) load_row_chunk8(W.bnd, brow, L2, ld, lane);
-                ++ld;
-            }
+            __syncwarp();
+            if (k + 1 < nch) tile_load<4>(tS, k + 1, L2);
             cp_async_commit();
+            // this stage's look-aheads read the row above up to its stage k + 3;
+            // this stage overwrites ring steps that the row-block below read in
+            // its stage k - kBack or earlier
+            if (hasB) wait_flag(&progF[wprev], ((r - 1) << 16) + min(k + 4, kStageMask), &sh_err);
+            if (hasD && k >= kBack) wait_flag(&progF[wnext], ((r + 1) << 16) + (k - kBack + 1), &sh_err);
             cp_async_wait1();
             __syncwarp();
+            if (k == 0) {  // lane 0 starts in the frame of the row above; group 0's factors
+                if (lane == 0) V.E = C.af[7];
+                V.Esent = __shfl_up_sync(kAll, V.E, 1);
+                fwd_lookahead<false>(C, V, 0);
+            }
             if ((nv == 32) && (kCW * k >= 31) && (kCW * k + kCW - 1 <= L2 - 1))
                 fwd_stage_full(C, V, k);
             else
                 fwd_stage_part(C, V, k);
-            if (C.st31) st_release(&progF[warp], (r << 16) | min(k + 1, kStageMask - 1));
+            __syncwarp();  // every lane's reads of the row above's ring come before the release
+            if (lane == 31) st_release(&progF[warp], (r << 16) | min(k + 1, kStageMask - 1));
         }
         cp_async_wait0();
         __syncwarp();
         if (lane == 31) st_release(&progF[warp], (r << 16) | kStageMask);
-        wmn = fminf(wmn, V.mn);
-        wmx = fmaxf(wmx, V.mx);
     }
 
     // ---- S = log2(1 + sum_lanes acc 2^R), kept as integer + fraction
@@ -523,135 +606,132 @@ __global__ void __launch_bounds__(kNW * 32) lin_fast_kernel(SwArgs p) {
         if (threadIdx.x == 0) part += exp2i(-Rm);  // alpha[0,0] = 0
         const float tot = block_sum(part, red);
         if (threadIdx.x == 0) {
-            const float l2 = lg2_rr(tot);
+            const bool fin = tot > 0.f && tot < 3.0e38f;
+            const float l2 = lg2_rr(fin ? tot : 1.f);
             const float fl = floorf(l2);
             sh_Sint = Rm + (int)fl;
             sh_Sfrac = l2 - fl;
+            if (!fin) sh_bad = 1;
             if (p.value) p.value[b] = ((float)sh_Sint + sh_Sfrac) / c;
         }
-        __syncthreads();
+        __syncthreads();  // also: every forward read of the handoff rings is done
     }
 
     // ============================== reverse ==============================
     const int P = kCW * ((L2 - 1 + kCW - 1) / kCW);
     const int nstR = P / kCW + 2;  // lane 0 reaches column 0 at step P + 31
+    RevVars RV;
+    RV.jmax = 0;
     for (int q = warp; q < nRB; q += kNW) {
         const int r = nRB - 1 - q;
         const int nv = min(32, L1 - 32 * r);
         const float* srow = S + (size_t)(32 * r) * L2m;
-        const bool hasBelow = r + 1 < nRB;
-        const float* zblk = LY.zpl + (size_t)r * zst;
-        const int* eblk = LY.efr + (size_t)r * est;
-        const float* rblk = LY.rab + (size_t)r * rb_len(L2m);
-        const float2* bbrow = LY.bbv + (size_t)(r + 1) * rb_len(L2m);
+        const bool hasBelow = r + 1 < nRB, hasAbove = r > 0;
+        const float* const zblk = LY.zpl + (size_t)r * zst;
+        const int* const eblk = LY.efr + (size_t)r * est;
+        const float* const zab = LY.zpl + (size_t)(r - 1) * zst + 31;
+        const int* const eab = LY.efr + (size_t)(r - 1) * est + 31;
         RevCtx C;
         C.ring = W.ringS + lane * kRW;
         C.zr = &W.zr[0][0];
         C.er = W.er;
-        C.rr = W.rr;
-        C.bbr = W.bbr;
-        C.bbout = LY.bbv + (size_t)r * rb_len(L2m);
+        C.bv = hasBelow ? Wp.hv[((q - 1) / kNW) & 1] : zv;
+        C.bf = hasBelow ? Wp.hf[((q - 1) / kNW) & 1] : zf;
+        C.ov = W.hv[(q / kNW) & 1];
+        C.of = W.hf[(q / kNW) & 1];
         C.c = c;
         C.G = G;
         C.cS = ex2f(-sh_Sfrac);
+        C.notBot = lane == nv - 1 ? 0.f : 1.f;
+        C.isBot = lane == nv - 1 ? 1.f : 0.f;
         C.Sint = sh_Sint;
         C.lane = lane;
         C.nv = nv;
         C.L2 = L2;
         C.P = P;
-        C.ecol = lane > 0 ? lane - 1 : 0;
-        C.lane0 = lane == 0;
-        C.lastLane = lane == nv - 1;
-        C.push0 = (lane == 0) && (r > 0);
-        const int* dnflag = &progR[(warp + kNW - 1) % kNW];
-        const int dnbase = (q - 1) << 16;
+        C.l0 = lane == 0;
         const Tile tS = make_tile(srow, L2m, W.ringS, nv, lane);
         const Tile tM = make_tile(out ? out + (size_t)(32 * r) * L2m : srow, L2m, W.ringS, nv, lane);
 
-        // staging for stage kk (M = P/16 + 1 - kk, anti-diagonals 16M .. 16M+15)
-        auto stage_z = [&](int kk) {  // z plane rows 16M .. 16M+15 (lane l-1's diagonal inputs)
-            const int M = P / kCW + 1 - kk;
-            if (kk >= nstR || M < 0) return;
-            const float* src = zblk + (size_t)(16 * M) * 32;
-            float* dst = &W.zr[M & 1][0];
-            for (int i = lane; i < 16 * 32 / 4; i += 32) cp_async16(dst + 4 * i, src + 4 * i, 16);
-        };
-        auto stage_e = [&](int kk) {  // forward frames of groups 4M .. 4M+3
-            const int M = P / kCW + 1 - kk;
-            if (kk >= nstR || M < 0) return;
-            const int g0 = 4 * M;
-            cp_async16(W.er + (g0 & 15) * 32 + 4 * lane, eblk + (size_t)g0 * 32 + 4 * lane, 16);
-        };
-        auto stage_r = [&](int kk) {  // row above (lane 0) and pushes from below (bottom lane)
-            const int M = P / kCW + 1 - kk;
-            if (kk >= nstR || M < 0) return;
-            if (lane < 4) cp_async16(W.rr + ((16 * M + 4 * lane) & (kRW - 1)), rblk + 16 * M + 4 * lane, 16);
-            if (hasBelow && M >= 1) {
-                // bbv indices 16M-16 .. 16M-1 = columns 16M-31 .. 16M-16, pushed by row-block
-                // r+1's lane 0 at its steps P + 31 - column
-                wait_flag(dnflag, dnbase + min((P + 31 - (16 * M - 31)) / kCW + 1, kStageMask), &sh_err);
-                if (lane < 8)
-                    cp_async16(W.bbr + ((16 * M - 16 + 2 * lane) & (kRW - 1)), bbrow + 16 * M - 16 + 2 * lane, 16);
+        // staging for stage kb (M = P/16 + 1 - kb): z rows 16M .. 16M+15 and
+        // the row above's at 16M+32 .. 16M+47; frames of groups 4M-2 .. 4M+3
+        // (the row above's: +8), read by the stage's cells and look-aheads
+        auto batch = [&](int kb) {
+            const int M = P / kCW + 1 - kb;
+            float* const zd = &W.zr[M & 1][0];
+            const float* const zs = zblk + (size_t)(16 * M) * 32;
+#pragma unroll
+            for (int it = 0; it < 4; ++it) {
+                const int cc = lane + 32 * it, row = cc >> 3, c4 = cc & 7;
+                cp_async16(zd + row * kZC + 4 + 4 * c4, zs + row * 32 + 4 * c4, 16);
+            }
+            if (hasAbove && lane < 16) cp_async4(zd + lane * kZC + 3, zab + (size_t)(16 * M + 32 + lane) * 32);
+            const int gl = 4 * M - 2;
+#pragma unroll
+            for (int it = 0; it < 2; ++it) {
+                const int cc = lane + 32 * it, g = gl + (cc >> 3), c4 = cc & 7;
+                if (cc < 48 && g >= 0)
+                    cp_async16(W.er + (g & 15) * kZC + 4 + 4 * c4, eblk + (size_t)g * 32 + 4 * c4, 16);
+            }
+            if (hasAbove && lane >= 16 && lane < 22) {  // slot g holds the row above's group g + 8 (g >= -2)
+                const int g = gl + lane - 16;
+                cp_async4(W.er + (g & 15) * kZC + 3, eab + (size_t)(g + 8) * 32);
             }
         };
 
+        if (q >= 2 * kNW) wait_flag(&progR[wnext], ((q - 2 * kNW + 1) << 16) | kStageMask, &sh_err);
         __syncwarp();
-        if (!hasBelow) {  // no row-block below: its pushes are zero
-            W.bbr[lane] = make_float2(0.f, __int_as_float(0));
-            W.bbr[lane + 32] = make_float2(0.f, __int_as_float(0));
+        if (!hasAbove && lane < 16) {  // no row above: lane 0's diagonal inputs are zero
+            W.zr[0][lane * kZC + 3] = 0.f;
+            W.zr[1][lane * kZC + 3] = 0.f;
+            W.er[lane * kZC + 3] = 0;
         }
         {   // stage 0 reads score chunks M0-2 .. M0 (M0 = P/16 + 1)
             const int M0 = P / kCW + 1;
             for (int ch = M0; ch >= M0 - 2; --ch)
                 if (ch >= 0 && ch < nch) tile_load<4>(tS, ch, L2);
         }
-        stage_z(0);
-        stage_e(0);
-        stage_e(1);
-        stage_r(0);
+        batch(0);
         cp_async_commit();
 
-        RevVars RV;
-        RV.recv = RV.pbp = RV.br = 0.f;
-        RV.mn = RV.mx = 1.f;
-        bool started = false;
+        RV.br = RV.pbp = RV.rsh = 0.f;
+        RV.Q = 0;
+        RV.Qdn = 0;
+        RV.Qsent = 0;
         for (int k = 0; k < nstR; ++k) {
             const int M = P / kCW + 1 - k;
             __syncwarp();
             if (out && M + 1 < nch && M + 1 >= 0) tile_store(tM, M + 1, L2);  // no lane touches it any more
             if (M - 3 >= 0 && M - 3 < nch) tile_load<4>(tS, M - 3, L2);       // for stage k + 1
-            stage_z(k + 1);
-            stage_e(k + 2);
-            stage_r(k + 1);
+            if (k + 1 < nstR) batch(k + 1);
             cp_async_commit();
+            // this stage's look-aheads read the row-block below up to its stage
+            // k + 3; this stage overwrites ring steps the row above read in its
+            // stage k - kBack or earlier
+            if (hasBelow) wait_flag(&progR[wprev], ((q - 1) << 16) + min(k + 4, kStageMask), &sh_err);
+            if (hasAbove && k >= kBack) wait_flag(&progR[wnext], ((q + 1) << 16) + (k - kBack + 1), &sh_err);
             cp_async_wait1();
             __syncwarp();
-            if (!started) {  // lanes adopt a neighbour's frame when they start
-                RV.Q = 0;
-                RV.Qdn_last = 0;
-                RV.d0 = RV.d1 = 1.f;
-                rev_k_factors(C, RV, P + 31);
-                started = true;
-            }
+            if (k == 0) rev_lookahead<false>(C, RV, 0);
             if ((nv == 32) && (kCW * k >= P + 32 - L2) && (kCW * k + kCW - 1 <= P - 1))
                 rev_stage_full(C, RV, k);
             else
                 rev_stage_part(C, RV, k);
-            if (C.push0) st_release(&progR[warp], (q << 16) | min(k + 1, kStageMask - 1));
+            __syncwarp();  // every lane's reads of the row-block below's ring come before the release
+            if (lane == 0) st_release(&progR[warp], (q << 16) | min(k + 1, kStageMask - 1));
         }
         __syncwarp();
         if (out && nch > 0) tile_store(tM, 0, L2);  // the last stage had M = 0
         cp_async_wait0();
         __syncwarp();
         if (lane == 0) st_release(&progR[warp], (q << 16) | kStageMask);
-        wmn = fminf(wmn, RV.mn);
-        wmx = fmaxf(wmx, RV.mx);
     }
 
-    // a value outside the frame window, or a dependency wait that gave up: the
-    // caller recomputes this problem with the log-domain kernel
-    const bool outside = !(wmn >= kWinLo && wmx <= kWinHi);
-    const int redo = __syncthreads_or(outside ? 1 : 0) || sh_err;
+    // a frame step outside the window, a partition that overflowed, or a
+    // dependency wait that gave up: the caller recomputes this problem with
+    // the log-domain kernel
+    const bool outside = max(V.jmax, RV.jmax) > kJMax;
+    const int redo = __syncthreads_or(outside ? 1 : 0) || sh_err || sh_bad;
     if (threadIdx.x == 0 && p.redo) p.redo[b] = redo;
 }
 
@@ -678,6 +758,9 @@ int launch_lin_fast(const SwArgs& a, size_t ws_bytes, cudaStream_t st) {
     static bool attr_set[64] = {false};
     if (dev < 64 && !attr_set[dev]) {
         e = cudaFuncSetAttribute(lin::lin_fast_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return (int)e;
+        e = cudaFuncSetAttribute(lin::lin_fast_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                 (int)cudaSharedmemCarveoutMaxShared);
         if (e != cudaSuccess) return (int)e;
         attr_set[dev] = true;
     }

@@ -26,6 +26,14 @@ __device__ __forceinline__ void cp_async16(void* smem, const void* gmem, int src
     const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem), "r"(src_bytes));
 }
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
+    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(s), "l"(gmem));
+}
+// bring a 128-byte line into L2 ahead of a cp.async that will read it
+__device__ __forceinline__ void prefetch_l2(const void* gmem) {
+    asm volatile("prefetch.global.L2 [%0];\n" ::"l"(gmem));
+}
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
 __device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;\n" ::); }
 __device__ __forceinline__ void cp_async_wait0() { asm volatile("cp.async.wait_group 0;\n" ::); }
@@ -59,6 +67,18 @@ __device__ __forceinline__ void wait_flag(const int* flag, int need, int* err) {
         __nanosleep(40);
     }
     __syncwarp();
+}
+
+// One lane's group handoff into shared memory: four values and a frame word,
+// stored under a predicate (no branch) so the other lanes only pay one issue.
+__device__ __forceinline__ void sts_group_pred(float* v4, int* f, float4 v, int fr, bool pr) {
+    const unsigned a = (unsigned)__cvta_generic_to_shared(v4);
+    const unsigned b = (unsigned)__cvta_generic_to_shared(f);
+    asm volatile(
+        "{\n .reg .pred q;\n setp.ne.b32 q, %6, 0;\n"
+        " @q st.shared.v4.f32 [%0], {%2, %3, %4, %5};\n"
+        " @q st.shared.b32 [%1], %7;\n}\n" ::"r"(a),
+        "r"(b), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"((int)pr), "r"(fr));
 }
 
 // log2 of a positive normal float, with the exponent split off exactly so that
