@@ -53,7 +53,6 @@ using namespace ring;
 
 constexpr int kMaxRB = 512;              // row-blocks per problem (L1 <= 16384)
 constexpr int kNW = 6;                   // warps per CTA
-constexpr int kRebase = 32;              // partition: rebase when the frame runs this far above R
 constexpr int kJMax = 60;                // largest frame step (log2) a problem may take
 constexpr int kZC = 36;                  // row stride of the reverse's z / frame blocks
 constexpr int kHR = 128;                 // handoff ring: steps per parity
@@ -110,14 +109,17 @@ __device__ __forceinline__ int expo(float v) {
     return bits > 0 ? (bits >> 23) - 127 : 0;
 }
 
-// partition base after a frame change: sum Z = acc 2^R, contributions scaled by ps = 2^(E - R)
-__device__ __forceinline__ void part_factors(int E, int R, float& accsc, int& nR, float& ps) {
-    const int D = E - R;
-    const bool reb = D > kRebase;
-    accsc = reb ? p2(-D) : 1.f;
-    nR = reb ? E : R;
-    ps = p2(reb ? 0 : D);
+// Frame steps come from the exponent field of the lane's previous value: for
+// v = m 2^J (m in [1, 2)) the field is the bit pattern of 2^J, so 2^J, 2^-J
+// and J cost one integer operation each.  Zero (a lane that has not started)
+// reads as J = 0.
+__device__ __forceinline__ int efield(float v) {
+    const int b = __float_as_int(v) & 0x7f800000;
+    return b ? b : 0x3f800000;
 }
+__device__ __forceinline__ float inv_p2(float w) { return __int_as_float(0x7f000000 - __float_as_int(w)); }
+// 2^E as a double (|E| <= 1022; larger frames flag the problem)
+__device__ __forceinline__ double p2d(int E) { return __hiloint2double((min(max(E, -1022), 1023) + 1023) << 20, 0); }
 
 // ==========================================================================
 // forward sweep of one row-block
@@ -131,81 +133,85 @@ struct FwdF {           // one group of 4 forward steps, for frame E
 
 struct FwdVars {
     float zl, zd, zsh;  // own z of the previous step; diagonal input of this step; lane l-1's last z
-    int E, Eup;         // own frame; lane l-1's frame in this group
+    int E;              // own frame
     int Esent;          // edge stages: lane l-1's frame of the value in zsh
     FwdF f;
-    int nE, nEup;       // the next group, decided one step early
-    float nfJ;
+    int nE;             // the next group, decided one step early
+    float nfJ;          // 2^(E - nE)
     FwdF nf;
-    float acc, ps;      // partition of this lane's cells: sum Z = acc 2^R; ps = 2^(E - R)
-    int R;
-    float naccsc, nps;
-    int nR;
-    int jmax;           // largest |frame step|
+    float gsum;         // this group's sum of z (frame E)
+    double acc;         // partition of this lane's cells so far: sum Z
+    int ebmin, ebmax;   // range of the frame steps (exponent fields)
+    int emax;           // largest |E|
 };
 
 struct FwdCtx {
     const float* ring;  // this lane's ring row
-    const float* av;    // handoff ring of the row above (its lane 31's z, by its step); zeros for r = 0
-    const int* af;      //   and its frames, by its group
+    const float* av;    // lane 0: handoff ring of the row above (its lane 31's z, by its step);
+    const int* af;      //   and its frames, by its group.  Other lanes (and r = 0): zeros
     float* ov;          // this row-block's handoff ring for the row-block below
     int* of;
     float* zrow;        // zpl row 2 (forward step 0) of this row-block, this lane
     int* erow;          // efr group 0 of this row-block, this lane
     float c, G;
-    float notl0, isl0;  // lane != 0, lane == 0 as 1 / 0
+    float notl0;        // lane != 0 as 1 / 0
     int lane, nv, L2;
-    bool l31;           // lane 31: hands its values to the row-block below
+    bool l0, l31;       // lane 0 follows the row above's frames; lane 31 hands its values down
 };
 
-// Factors of group g in frame E; eup0 / eup1: lane l-1's frames of the values
-// lane l receives in the group's first / other steps.  Lane 0's up input is
-// the row above's last lane at forward step t + 31: step 4g + 31 (its group
-// g + 7) for the group's first step, 4g + 32 .. 4g + 34 (group g + 8) for the
-// others.
-__device__ __forceinline__ FwdF fwd_factors(const FwdCtx& C, int E, int eup0, int eup1, int g) {
+// Factors of group g for a lane (not lane 0) that starts in frame E; eup0 /
+// eup1: lane l-1's frames of the values it receives in the group's first /
+// other steps.
+__device__ __forceinline__ FwdF fwd_factors(const FwdCtx& C, int E, int eup0, int eup1) {
     FwdF f;
     f.d0 = p2(eup0 - E) * C.notl0;
     f.d1 = p2(eup1 - E) * C.notl0;
     f.Gd0 = C.G * f.d0;
     f.Gd1 = C.G * f.d1;
     f.fs = p2(-E);
-    const float a0 = C.av[(4 * g + 31) & (kHR - 1)];
-    const float4 a = *reinterpret_cast<const float4*>(C.av + ((4 * g + 32) & (kHR - 1)));
-    const float f0 = p2(C.af[(g + 7) & (kHR / 4 - 1)] - E) * C.isl0;
-    const float f1 = p2(C.af[(g + 8) & (kHR / 4 - 1)] - E) * C.isl0;
-    f.za[0] = a0 * f0;
-    f.za[1] = a.x * f1;
-    f.za[2] = a.y * f1;
-    f.za[3] = a.z * f1;
+    f.za[0] = f.za[1] = f.za[2] = f.za[3] = 0.f;
     return f;
 }
 
-// At the last step of a group (before its cell): the next group's frame from
-// the lane's previous value, and every factor of group g (the next one).  In
-// edge stages lane l-1 may have changed frame inside the group (it started),
-// so its current frame is read again.
-template <bool FULL>
+// At the last step of a group (before its cell): the next group's frame and
+// every factor of group g (the next one).  A lane re-anchors on its previous
+// value; lane 0 instead takes the frame of the row above's last lane for the
+// steps it receives (its group g + 8: the steps 4g+32 .. 4g+34 of that lane
+// are lane 0's inputs 2..4; input 1, step 4g + 31, is converted from group
+// g + 7, lane 0's previous frame).  Lane l-1's factors follow by exact
+// products: d0' = d1 2^(E - E'), d1' = d0' 2^(E'_{l-1} - E_{l-1}).
 __device__ __forceinline__ void fwd_lookahead(const FwdCtx& C, FwdVars& V, int g) {
-    const int J = expo(V.zl);
-    V.jmax = max(V.jmax, abs(J));
-    V.nE = V.E + J;
-    V.nEup = __shfl_up_sync(kAll, V.nE, 1);
-    const int eup_now = FULL ? V.Eup : __shfl_up_sync(kAll, V.E, 1);
-    V.nfJ = p2(-J);
-    V.nf = fwd_factors(C, V.nE, eup_now, V.nEup, g);
-    part_factors(V.nE, V.R, V.naccsc, V.nR, V.nps);
+    const int eb = efield(V.zl);
+    V.ebmin = min(V.ebmin, eb);
+    V.ebmax = max(V.ebmax, eb);
+    const int ea0 = C.af[(g + 7) & (kHR / 4 - 1)], ea1 = C.af[(g + 8) & (kHR / 4 - 1)];
+    const float w = p2(ea0 - ea1);
+    V.nE = C.l0 ? ea1 : V.E + (eb >> 23) - 127;
+    V.nfJ = C.l0 ? w : __int_as_float(0x7f000000 - eb);
+    const float p2J = C.l0 ? inv_p2(w) : __int_as_float(eb);
+    const float p2Jup = __shfl_up_sync(kAll, p2J, 1);
+    V.nf.d0 = V.f.d1 * V.nfJ;
+    V.nf.d1 = V.nf.d0 * p2Jup;
+    V.nf.Gd0 = C.G * V.nf.d0;
+    V.nf.Gd1 = C.G * V.nf.d1;
+    V.nf.fs = p2(-V.nE);
+    const float a0 = C.av[(4 * g + 31) & (kHR - 1)];
+    const float4 a = *reinterpret_cast<const float4*>(C.av + ((4 * g + 32) & (kHR - 1)));
+    V.nf.za[0] = a0 * w;
+    V.nf.za[1] = a.x;
+    V.nf.za[2] = a.y;
+    V.nf.za[3] = a.z;
 }
 
+// group boundary: the finished group's partition in absolute terms, then the new frame
 __device__ __forceinline__ void fwd_apply(FwdVars& V) {
+    V.acc = fma((double)V.gsum, p2d(V.E), V.acc);
+    V.gsum = 0.f;
     V.zl *= V.nfJ;
     V.zd *= V.nfJ;
     V.E = V.nE;
-    V.Eup = V.nEup;
+    V.emax = max(V.emax, abs(V.E));
     V.f = V.nf;
-    V.acc *= V.naccsc;
-    V.R = V.nR;
-    V.ps = V.nps;
 }
 
 // one cell, step i of its group; returns z, and the up input in this frame
@@ -217,8 +223,11 @@ __device__ __forceinline__ float fwd_cell(const FwdCtx& C, const FwdVars& V, int
     return fmaf(i == 0 ? V.f.Gd0 : V.f.Gd1, V.zsh, rest);
 }
 
-// 16 forward steps with every lane active
-__device__ __forceinline__ void fwd_stage_full(const FwdCtx& C, FwdVars& V, int k) {
+// 16 forward steps after every lane has started.  MASK: some lanes are past
+// the last column (or beyond nv); thr = first step (u) at which this lane is
+// past its last column.
+template <bool MASK>
+__device__ __forceinline__ void fwd_stage_full(const FwdCtx& C, FwdVars& V, int k, int thr) {
     const int c0 = (kCW * k - C.lane) & (kRW - 1);   // this lane's ring column at u = 0
     const float* const pA = C.ring + c0;
     const float* const pB = pA - kRW;                 // after the wrap past column 63
@@ -232,10 +241,11 @@ __device__ __forceinline__ void fwd_stage_full(const FwdCtx& C, FwdVars& V, int 
     for (int u = 0; u < kCW; ++u) {
         const int i = u & 3;
         if (i == 0) fwd_apply(V);
-        if (i == 3) fwd_lookahead<true>(C, V, 4 * k + (u >> 2) + 1);
+        if (i == 3) fwd_lookahead(C, V, 4 * k + (u >> 2) + 1);
         float zuin;
-        const float z = fwd_cell(C, V, i, scv[u], zuin);
-        V.acc = fmaf(z, V.ps, V.acc);
+        float z = fwd_cell(C, V, i, scv[u], zuin);
+        if (MASK) z = (u < thr) ? z : 0.f;
+        V.gsum += z;
         pz[(size_t)u * 32] = z;
         zq[i] = z;
         if (i == 3) {
@@ -250,9 +260,9 @@ __device__ __forceinline__ void fwd_stage_full(const FwdCtx& C, FwdVars& V, int 
     }
 }
 
-// edge stages: per-lane activity; a lane that starts (column 0) takes the
-// frame of the value it receives (lane 0 starts in the frame of the row above)
-__device__ __forceinline__ void fwd_stage_part(const FwdCtx& C, FwdVars& V, int k) {
+// the first two stages: lanes start (column 0) and take the frame of the
+// value they receive (lane 0 starts in the frame of the row above)
+__device__ __forceinline__ void fwd_stage_start(const FwdCtx& C, FwdVars& V, int k) {
     const bool live = C.lane < C.nv;
     float zq[4];
 #pragma unroll 1
@@ -263,21 +273,16 @@ __device__ __forceinline__ void fwd_stage_part(const FwdCtx& C, FwdVars& V, int 
             const int j0 = t - C.lane;
             const bool act = live & (j0 >= 0) & (j0 < C.L2);
             if (i == 0) fwd_apply(V);
-            if (live && j0 == 0 && C.lane > 0) {
+            const int eup_now = __shfl_up_sync(kAll, V.E, 1);
+            if (live && j0 == 0 && !C.l0) {
                 V.E = V.Esent;
-                V.f = fwd_factors(C, V.E, V.Esent, i == 0 ? V.Eup : V.Esent, 4 * k + q);
-                float accsc, ps;
-                int R;
-                part_factors(V.E, V.R, accsc, R, ps);
-                V.acc *= accsc;
-                V.R = R;
-                V.ps = ps;
+                V.f = fwd_factors(C, V.E, V.Esent, i == 0 ? eup_now : V.Esent);
             }
-            if (i == 3) fwd_lookahead<false>(C, V, 4 * k + q + 1);
+            if (i == 3) fwd_lookahead(C, V, 4 * k + q + 1);
             float zuin;
             float z = fwd_cell(C, V, i, C.ring[j0 & (kRW - 1)], zuin);
             z = act ? z : 0.f;
-            V.acc = fmaf(z, V.ps, V.acc);
+            V.gsum += z;
             C.zrow[(size_t)t * 32] = z;
             zq[i] = z;
             if (i == 3) {
@@ -300,84 +305,96 @@ __device__ __forceinline__ void fwd_stage_part(const FwdCtx& C, FwdVars& V, int 
 struct RevF {           // one group of 4 reverse steps, for frame Q
     float d0, d1;       // 2^(Q_{l+1} - Q) for the message of the first / other steps (bottom lane: 0)
     float Gd0, Gd1;
-    float fb[4];        // 2^-Q, plus for the bottom lane the push from below (frame Q)
+    float fb[4];        // 2^-Q, plus for the bottom lane the message from below (frame Q)
     float kA, kB, k2;   // 2^(Q + E_diag - S) for the group's two forward frame groups; 2^(Q - S)
 };
 
 struct RevVars {
     float br, pbp, rsh; // own b and P*b of column j+1; message from lane l+1
-    int Q, Qdn;         // own frame; lane l+1's frame in this group
+    int Q;              // own frame
     int Qsent;          // edge stages: lane l+1's frame of the message in rsh
     RevF f;
-    int nQ, nQdn;
-    float nfJ;
+    int nQ;
+    float nfJ;          // 2^(Q - nQ)
     RevF nf;
-    int jmax;
+    int ebmin, ebmax;   // range of the frame steps (exponent fields)
 };
 
 struct RevCtx {
     float* ring;          // ringS row of this lane
     const float* zr;      // WarpSmem::zr
     const int* er;        // WarpSmem::er
-    const float* bv;      // handoff ring of the row-block below (its lane 0's messages, by its step); zeros for the last
-    const int* bf;        //   and its frames, by its group
+    const float* bv;      // bottom lane: handoff ring of the row-block below (its lane 0's messages,
+    const int* bf;        //   by its step) and its frames, by its group.  Other lanes (and the last row-block): zeros
     float* ov;            // this row-block's handoff ring for the row-block above
     int* of;
     float c, G, cS;       // cS = 2^-Sfrac
-    float notBot, isBot;  // lane != nv-1, lane == nv-1 as 1 / 0
+    float notBot;         // lane != nv-1 as 1 / 0
     int Sint, lane, nv, L2, P;
-    bool l0;              // lane 0: hands its messages to the row-block above
+    bool l0, bot;         // lane 0 hands its messages up; the bottom lane follows the row-block below's frames
 };
 
-// Factors of reverse group h (anti-diagonals tf0 = P + 31 - 4h down to tf0 - 3)
-// in frame Q; qdn0 / qdn1: lane l+1's frames of the messages received in the
-// group's first / other steps.  The diagonal input of lane l at anti-diagonal
-// tf is forward group (tf - 2) / 4 of lane l-1 (lane 0: group + 8 of the row
-// above's last lane): group gA for tf0 and tf0 - 1, gA - 1 for the rest.  The
-// bottom lane's message from below at step tau is the one lane 0 of the
-// row-block below sent at its step tau + 31 (same column): step 4h + 31 (its
-// group h + 7) for the group's first step, 4h + 32 .. 4h + 34 (group h + 8)
-// for the others.
+// Marginal factors of reverse group h (anti-diagonals tf0 = P + 31 - 4h down
+// to tf0 - 3) in frame Q.  The diagonal input of lane l at anti-diagonal tf
+// is forward group (tf - 2) / 4 of lane l-1 (lane 0: group + 8 of the row
+// above's last lane): group gA for tf0 and tf0 - 1, gA - 1 for the rest.
+__device__ __forceinline__ void rev_kfactors(const RevCtx& C, RevF& f, int Q, int h) {
+    const int gA = C.P / 4 + 7 - h;
+    const int EA = C.er[(gA & 15) * kZC + 3 + C.lane];
+    const int EB = C.er[((gA - 1) & 15) * kZC + 3 + C.lane];
+    const int tq = Q - C.Sint;
+    f.kA = p2(tq + EA) * C.cS;
+    f.kB = p2(tq + EB) * C.cS;
+    f.k2 = p2(tq) * C.cS;
+}
+
+// Factors of group h for a lane (not the bottom one) that starts in frame Q;
+// qdn0 / qdn1: lane l+1's frames of the messages it receives in the group's
+// first / other steps.
 __device__ __forceinline__ RevF rev_factors(const RevCtx& C, int Q, int qdn0, int qdn1, int h) {
     RevF f;
     f.d0 = p2(qdn0 - Q) * C.notBot;
     f.d1 = p2(qdn1 - Q) * C.notBot;
     f.Gd0 = C.G * f.d0;
     f.Gd1 = C.G * f.d1;
-    const float fsq = p2(-Q);
-    const float e0 = C.bv[(4 * h + 31) & (kHR - 1)];
-    const float4 e = *reinterpret_cast<const float4*>(C.bv + ((4 * h + 32) & (kHR - 1)));
-    const float g0 = p2(C.bf[(h + 7) & (kHR / 4 - 1)] - Q) * C.isBot;
-    const float g1 = p2(C.bf[(h + 8) & (kHR / 4 - 1)] - Q) * C.isBot;
-    f.fb[0] = fmaf(e0, g0, fsq);
-    f.fb[1] = fmaf(e.x, g1, fsq);
-    f.fb[2] = fmaf(e.y, g1, fsq);
-    f.fb[3] = fmaf(e.z, g1, fsq);
-    const int gA = C.P / 4 + 7 - h;
-    const int EA = C.er[(gA & 15) * kZC + 3 + C.lane];
-    const int EB = C.er[((gA - 1) & 15) * kZC + 3 + C.lane];
-    f.kA = p2(Q + EA - C.Sint) * C.cS;
-    f.kB = p2(Q + EB - C.Sint) * C.cS;
-    f.k2 = p2(Q - C.Sint) * C.cS;
+    f.fb[0] = f.fb[1] = f.fb[2] = f.fb[3] = p2(-Q);
+    rev_kfactors(C, f, Q, h);
     return f;
 }
 
-template <bool FULL>
+// At the last step of a group (before its cell): the next group's frame and
+// every factor of group h (the next one).  The bottom lane takes the frame
+// of lane 0 of the row-block below for the messages it receives: that lane's
+// step tau + 31 feeds step tau here, so messages 2..4 of group h come in its
+// group h + 8 and message 1 (its step 4h + 31) is converted from group h + 7.
 __device__ __forceinline__ void rev_lookahead(const RevCtx& C, RevVars& V, int h) {
-    const int J = expo(V.br);
-    V.jmax = max(V.jmax, abs(J));
-    V.nQ = V.Q + J;
-    V.nQdn = __shfl_down_sync(kAll, V.nQ, 1);
-    const int qdn_now = FULL ? V.Qdn : __shfl_down_sync(kAll, V.Q, 1);
-    V.nfJ = p2(-J);
-    V.nf = rev_factors(C, V.nQ, qdn_now, V.nQdn, h);
+    const int eb = efield(V.br);
+    V.ebmin = min(V.ebmin, eb);
+    V.ebmax = max(V.ebmax, eb);
+    const int qb0 = C.bf[(h + 7) & (kHR / 4 - 1)], qb1 = C.bf[(h + 8) & (kHR / 4 - 1)];
+    const float w = p2(qb0 - qb1);
+    V.nQ = C.bot ? qb1 : V.Q + (eb >> 23) - 127;
+    V.nfJ = C.bot ? w : __int_as_float(0x7f000000 - eb);
+    const float p2J = C.bot ? inv_p2(w) : __int_as_float(eb);
+    const float p2Jdn = __shfl_down_sync(kAll, p2J, 1);
+    V.nf.d0 = V.f.d1 * V.nfJ;
+    V.nf.d1 = V.nf.d0 * p2Jdn;
+    V.nf.Gd0 = C.G * V.nf.d0;
+    V.nf.Gd1 = C.G * V.nf.d1;
+    const float fsq = p2(-V.nQ);
+    const float e0 = C.bv[(4 * h + 31) & (kHR - 1)];
+    const float4 e = *reinterpret_cast<const float4*>(C.bv + ((4 * h + 32) & (kHR - 1)));
+    V.nf.fb[0] = fmaf(e0, w, fsq);
+    V.nf.fb[1] = fsq + e.x;
+    V.nf.fb[2] = fsq + e.y;
+    V.nf.fb[3] = fsq + e.z;
+    rev_kfactors(C, V.nf, V.nQ, h);
 }
 
 __device__ __forceinline__ void rev_apply(RevVars& V) {
     V.br *= V.nfJ;
     V.pbp *= V.nfJ;
     V.Q = V.nQ;
-    V.Qdn = V.nQdn;
     V.f = V.nf;
 }
 
@@ -411,7 +428,7 @@ __device__ __forceinline__ void rev_stage_full(const RevCtx& C, RevVars& V, int 
     for (int u = 0; u < kCW; ++u) {
         const int i = u & 3;
         if (i == 0) rev_apply(V);
-        if (i == 3) rev_lookahead<true>(C, V, 4 * k + (u >> 2) + 1);
+        if (i == 3) rev_lookahead(C, V, 4 * k + (u >> 2) + 1);
         const RevOut o = rev_cell(C, V, i, scv[u], zb[(15 - u) * kZC]);
         (((u <= cb) ? qA : qB) - u)[0] = o.mu;
         mq[i] = o.msg;
@@ -427,7 +444,8 @@ __device__ __forceinline__ void rev_stage_full(const RevCtx& C, RevVars& V, int 
 }
 
 // edge stages: per-lane activity; a lane that starts (column L2-1, where
-// B = 1 + G B_{i+1,j} stays near 1) starts in frame 0
+// B = 1 + G B_{i+1,j} stays near 1) starts in frame 0 (the bottom lane stays
+// on the frames of the row-block below)
 __device__ __forceinline__ void rev_stage_part(const RevCtx& C, RevVars& V, int k) {
     const int m16 = C.P + 16 - kCW * k;
     const float* const zb = C.zr + ((m16 >> 4) & 1) * (16 * kZC) + 3 + C.lane;
@@ -442,11 +460,12 @@ __device__ __forceinline__ void rev_stage_part(const RevCtx& C, RevVars& V, int 
             const int j0 = tf - C.lane;
             const bool act = live & (j0 >= 0) & (j0 < C.L2);
             if (i == 0) rev_apply(V);
-            if (live && j0 == C.L2 - 1) {
+            const int qdn_now = __shfl_down_sync(kAll, V.Q, 1);
+            if (live && j0 == C.L2 - 1 && !C.bot) {
                 V.Q = 0;
-                V.f = rev_factors(C, 0, V.Qsent, i == 0 ? V.Qdn : V.Qsent, 4 * k + q);
+                V.f = rev_factors(C, 0, V.Qsent, i == 0 ? qdn_now : V.Qsent, 4 * k + q);
             }
-            if (i == 3) rev_lookahead<false>(C, V, 4 * k + q + 1);
+            if (i == 3) rev_lookahead(C, V, 4 * k + q + 1);
             const int ci = j0 & (kRW - 1);
             const RevOut o = rev_cell(C, V, i, C.ring[ci], zb[(15 - u) * kZC]);
             if (act) C.ring[ci] = o.mu;
@@ -520,6 +539,12 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
     }
     if (threadIdx.x < kHR) zv[threadIdx.x] = 0.f;
     if (threadIdx.x < kHR / 4) zf[threadIdx.x] = 0;
+    // rings start at zero: a neighbour's look-ahead past the last written group reads zeros
+    auto clear_rings = [&]() {
+        for (int i = lane; i < 2 * kHR; i += 32) (&W.hv[0][0])[i] = 0.f;
+        for (int i = lane; i < 2 * (kHR / 4); i += 32) (&W.hf[0][0])[i] = 0;
+    };
+    clear_rings();
     if (threadIdx.x == 0) {
         sh_err = 0;
         sh_bad = 0;
@@ -532,10 +557,11 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
 
     // ============================== forward ==============================
     FwdVars V;
-    V.acc = 0.f;
-    V.R = 0;
+    V.acc = 0.0;
+    V.gsum = 0.f;
     V.E = 0;
-    V.jmax = 0;
+    V.ebmin = V.ebmax = 0x3f800000;
+    V.emax = 0;
     for (int r = warp; r < nRB; r += kNW) {
         const int nv = min(32, L1 - 32 * r);
         const int nst = (L2 + nv - 1 + kCW - 1) / kCW;
@@ -544,8 +570,8 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
         float* const zblk = LY.zpl + (size_t)r * zst;
         FwdCtx C;
         C.ring = W.ringS + lane * kRW;
-        C.av = hasB ? Wp.hv[((r - 1) / kNW) & 1] : zv;
-        C.af = hasB ? Wp.hf[((r - 1) / kNW) & 1] : zf;
+        C.av = (hasB && lane == 0) ? Wp.hv[((r - 1) / kNW) & 1] : zv;
+        C.af = (hasB && lane == 0) ? Wp.hf[((r - 1) / kNW) & 1] : zf;
         C.ov = W.hv[(r / kNW) & 1];
         C.of = W.hf[(r / kNW) & 1];
         C.zrow = zblk + 2 * 32 + lane;
@@ -553,10 +579,10 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
         C.c = c;
         C.G = G;
         C.notl0 = lane == 0 ? 0.f : 1.f;
-        C.isl0 = lane == 0 ? 1.f : 0.f;
         C.lane = lane;
         C.nv = nv;
         C.L2 = L2;
+        C.l0 = lane == 0;
         C.l31 = lane == 31;
         const Tile tS = make_tile(srow, L2m, W.ringS, nv, lane);
 
@@ -570,6 +596,7 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
         if (0 < nch) tile_load<4>(tS, 0, L2);
         cp_async_commit();
         V.zl = V.zd = V.zsh = 0.f;
+        V.f.d1 = 0.f;  // lane 0 keeps zero neighbour factors; the others set theirs when they start
         for (int k = 0; k < nst; ++k) {
             __syncwarp();
             if (k + 1 < nch) tile_load<4>(tS, k + 1, L2);
@@ -584,44 +611,52 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
             if (k == 0) {  // lane 0 starts in the frame of the row above; group 0's factors
                 if (lane == 0) V.E = C.af[7];
                 V.Esent = __shfl_up_sync(kAll, V.E, 1);
-                fwd_lookahead<false>(C, V, 0);
+                fwd_lookahead(C, V, 0);
             }
-            if ((nv == 32) && (kCW * k >= 31) && (kCW * k + kCW - 1 <= L2 - 1))
-                fwd_stage_full(C, V, k);
+            if (kCW * k < 31)
+                fwd_stage_start(C, V, k);
+            else if (nv == 32 && kCW * k + kCW - 1 <= L2 - 1)
+                fwd_stage_full<false>(C, V, k, 0);
             else
-                fwd_stage_part(C, V, k);
+                fwd_stage_full<true>(C, V, k, lane < nv ? L2 + lane - kCW * k : -1);
             __syncwarp();  // every lane's reads of the row above's ring come before the release
             if (lane == 31) st_release(&progF[warp], (r << 16) | min(k + 1, kStageMask - 1));
         }
+        V.acc = fma((double)V.gsum, p2d(V.E), V.acc);  // the last group's partition
+        V.gsum = 0.f;
+        // lane 1 below, at its last column, converts lane 0's values with this
+        // lane's frame of group 4 nst (one past the last): the final frame
+        if (hasD && nst >= kBack) wait_flag(&progF[wnext], ((r + 1) << 16) + (nst - kBack + 1), &sh_err);
+        if (lane == 31) C.of[(4 * nst) & (kHR / 4 - 1)] = V.E;
         cp_async_wait0();
         __syncwarp();
         if (lane == 31) st_release(&progF[warp], (r << 16) | kStageMask);
     }
 
-    // ---- S = log2(1 + sum_lanes acc 2^R), kept as integer + fraction
+    // ---- S = log2(1 + sum of every lane's partition), kept as integer + fraction
     {
-        const bool has = V.acc > 0.f;
-        const int Rm = (int)block_max(has ? (float)max(V.R, 0) : 0.f, red);
-        float part = has ? V.acc * exp2i(V.R - Rm) : 0.f;
-        if (threadIdx.x == 0) part += exp2i(-Rm);  // alpha[0,0] = 0
-        const float tot = block_sum(part, red);
+        const double tot = block_sum_d(V.acc, reinterpret_cast<double*>(red)) + 1.0;  // alpha[0,0] = 0
         if (threadIdx.x == 0) {
-            const bool fin = tot > 0.f && tot < 3.0e38f;
-            const float l2 = lg2_rr(fin ? tot : 1.f);
-            const float fl = floorf(l2);
-            sh_Sint = Rm + (int)fl;
-            sh_Sfrac = l2 - fl;
+            const int hi = __double2hiint(tot);
+            const int e = ((hi >> 20) & 0x7ff) - 1023;                        // tot = m 2^e, m in [1, 2)
+            const bool fin = e < 1000;
+            const double m = __hiloint2double((hi & 0x800fffff) | 0x3ff00000, __double2loint(tot));
+            const float l2 = lg2_rr((float)m);
+            sh_Sint = e;
+            sh_Sfrac = l2;
             if (!fin) sh_bad = 1;
             if (p.value) p.value[b] = ((float)sh_Sint + sh_Sfrac) / c;
         }
         __syncthreads();  // also: every forward read of the handoff rings is done
     }
+    clear_rings();
+    __syncwarp();
 
     // ============================== reverse ==============================
     const int P = kCW * ((L2 - 1 + kCW - 1) / kCW);
     const int nstR = P / kCW + 2;  // lane 0 reaches column 0 at step P + 31
     RevVars RV;
-    RV.jmax = 0;
+    RV.ebmin = RV.ebmax = 0x3f800000;
     for (int q = warp; q < nRB; q += kNW) {
         const int r = nRB - 1 - q;
         const int nv = min(32, L1 - 32 * r);
@@ -635,15 +670,15 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
         C.ring = W.ringS + lane * kRW;
         C.zr = &W.zr[0][0];
         C.er = W.er;
-        C.bv = hasBelow ? Wp.hv[((q - 1) / kNW) & 1] : zv;
-        C.bf = hasBelow ? Wp.hf[((q - 1) / kNW) & 1] : zf;
+        C.bv = (hasBelow && lane == nv - 1) ? Wp.hv[((q - 1) / kNW) & 1] : zv;
+        C.bf = (hasBelow && lane == nv - 1) ? Wp.hf[((q - 1) / kNW) & 1] : zf;
         C.ov = W.hv[(q / kNW) & 1];
         C.of = W.hf[(q / kNW) & 1];
         C.c = c;
         C.G = G;
         C.cS = ex2f(-sh_Sfrac);
         C.notBot = lane == nv - 1 ? 0.f : 1.f;
-        C.isBot = lane == nv - 1 ? 1.f : 0.f;
+        C.bot = lane == nv - 1;
         C.Sint = sh_Sint;
         C.lane = lane;
         C.nv = nv;
@@ -696,8 +731,8 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
 
         RV.br = RV.pbp = RV.rsh = 0.f;
         RV.Q = 0;
-        RV.Qdn = 0;
         RV.Qsent = 0;
+        RV.f.d1 = 0.f;  // the bottom lane keeps zero neighbour factors; the others set theirs when they start
         for (int k = 0; k < nstR; ++k) {
             const int M = P / kCW + 1 - k;
             __syncwarp();
@@ -712,14 +747,20 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
             if (hasAbove && k >= kBack) wait_flag(&progR[wnext], ((q + 1) << 16) + (k - kBack + 1), &sh_err);
             cp_async_wait1();
             __syncwarp();
-            if (k == 0) rev_lookahead<false>(C, RV, 0);
-            if ((nv == 32) && (kCW * k >= P + 32 - L2) && (kCW * k + kCW - 1 <= P - 1))
+            if (k == 0) rev_lookahead(C, RV, 0);
+            // full: every lane started before the stage (lane 0 starts at step
+            // P - L2 + 32, which must run the start logic) and none finishes in it
+            if ((nv == 32) && (kCW * k > P + 32 - L2) && (kCW * k + kCW - 1 <= P - 1))
                 rev_stage_full(C, RV, k);
             else
                 rev_stage_part(C, RV, k);
             __syncwarp();  // every lane's reads of the row-block below's ring come before the release
             if (lane == 0) st_release(&progR[warp], (q << 16) | min(k + 1, kStageMask - 1));
         }
+        // the row above's bottom lane (and its neighbour), at column 0, read this
+        // lane's frame of group 4 nstR (one past the last): the final frame
+        if (hasAbove && nstR >= kBack) wait_flag(&progR[wnext], ((q + 1) << 16) + (nstR - kBack + 1), &sh_err);
+        if (lane == 0) C.of[(4 * nstR) & (kHR / 4 - 1)] = RV.Q;
         __syncwarp();
         if (out && nch > 0) tile_store(tM, 0, L2);  // the last stage had M = 0
         cp_async_wait0();
@@ -730,7 +771,8 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
     // a frame step outside the window, a partition that overflowed, or a
     // dependency wait that gave up: the caller recomputes this problem with
     // the log-domain kernel
-    const bool outside = max(V.jmax, RV.jmax) > kJMax;
+    const bool outside = min(V.ebmin, RV.ebmin) < ((127 - kJMax) << 23) ||
+                         max(V.ebmax, RV.ebmax) > ((127 + kJMax) << 23) || V.emax > 1000;
     const int redo = __syncthreads_or(outside ? 1 : 0) || sh_err || sh_bad;
     if (threadIdx.x == 0 && p.redo) p.redo[b] = redo;
 }
