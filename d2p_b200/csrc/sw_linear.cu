@@ -28,10 +28,11 @@
 // Structure (shared with sw_wavefront.cu): one CTA per problem; warps own
 // row-blocks of 32 rows (lane = row) and sweep them along anti-diagonals;
 // consecutive row-blocks are ordered by release/acquire progress words.  The
-// forward stores z in a diagonal-major plane (row = forward step + 2, 32 lanes
-// per row) with one coalesced 128-byte store per step, and each lane's frame
-// once per group; the reverse stages the plane 16 rows at a time through
-// shared memory.  Values that cross to the next row-block inside a pass (the
+// forward stores each cell's diagonal term w = P (z_diag + 2^-E) in a
+// diagonal-major plane (row = forward step, 32 lanes per row) with one
+// coalesced 128-byte store per step, and each lane's frame once per group;
+// the reverse stages the plane 16 rows at a time through shared memory, each
+// lane reading its own column (marginal = b w 2^(Q + E - S)).  Values that cross to the next row-block inside a pass (the
 // forward's last lane down, the reverse's lane-0 messages up) go through a
 // small shared-memory ring of the producing warp, one 16-byte store per group
 // by the boundary lane: reading a global line another warp has just written
@@ -54,33 +55,29 @@ using namespace ring;
 constexpr int kMaxRB = 512;              // row-blocks per problem (L1 <= 16384)
 constexpr int kNW = 6;                   // warps per CTA
 constexpr int kJMax = 60;                // largest frame step (log2) a problem may take
-constexpr int kZC = 36;                  // row stride of the reverse's z / frame blocks
 constexpr int kHR = 128;                 // handoff ring: steps per parity
 constexpr int kBack = 8;                 // a producer overwrites ring steps its consumer read 8+ stages ago
 
-// Reverse z / frame blocks: column 3 holds lane 0's diagonal input (the row
-// above's last lane), columns 4..35 the row-block's own lanes 0..31, so lane l
-// reads column 3 + l for every l.
 struct WarpSmem {
     float ringS[32 * kRW];    // scores [rows][64]; reverse: marginals written in place
-    float zr[2][16 * kZC];    // reverse: z of 16 anti-diagonals, two slots
-    int er[16 * kZC];         // reverse: forward frames, 16 group slots
+    float zr[2][16 * 32];     // reverse: the forward's w of 16 anti-diagonals, two slots
+    float er[16 * 32];        // reverse: forward frames, 16 group slots
     // handoff ring, written by this warp's boundary lane for the neighbouring
     // row-block, by step (values) and by group (frames); two parities so that a
     // warp's next row-block never overwrites what the neighbour still reads.
     // Forward: lane 31's z; reverse: lane 0's messages to the row above.
     float hv[2][kHR];
-    int hf[2][kHR / 4];
+    float hf[2][kHR / 4];
 };
 static_assert(sizeof(WarpSmem) % 16 == 0, "per-warp shared blocks must stay 16-byte aligned");
 
 struct Layout {  // per-problem workspace
-    float* zpl;      // [nRB][ZT][32]   z of forward step t at row t + 2 (rows 0, 1: zeros)
-    int* efr;        // [nRB][GT][32]   frame of each lane for each group of 4 forward steps
+    float* zpl;      // [nRB][ZT][32]   w = P (Z_diag + 1) of forward step t, frame E, at row t
+    float* efr;      // [nRB][GT][32]   frame of each lane for each group of 4 forward steps
 };
 
 // Row counts cover every row the reverse's staging reaches past the last
-// step (the row above's z up to 78 rows past L2, its frames up to 20 groups).
+// step (up to 46 rows past L2, and 12 frame groups).
 __host__ __device__ inline int zt_rows(int L2m) { return L2m + 96; }
 __host__ __device__ inline int gt_rows(int L2m) { return (L2m + 96) / 4; }
 
@@ -97,12 +94,13 @@ __device__ inline Layout carve(float* ws, int b, int L1m, int L2m) {
     Layout L;
     L.zpl = (float*)base;
     base += align_up(nrb * zt_rows(L2m) * 32 * 4, 256);
-    L.efr = (int*)base;
+    L.efr = (float*)base;
     return L;
 }
 
-// 2^k for integer k, exact; 0 below 2^-126, clamped at 2^127
-__device__ __forceinline__ float p2(int k) { return exp2i(k); }
+// Frames are integer-valued floats: 2^k is one MUFU ex2, exact for integer k
+// in [-126, 127] (0 below, +inf above; checked on the B200 for |k| <= 150).
+__device__ __forceinline__ float p2(float k) { return ex2f(k); }
 // binary exponent of a non-negative value (0 for zero; 128 for inf / NaN)
 __device__ __forceinline__ int expo(float v) {
     const int bits = __float_as_int(v);
@@ -119,7 +117,11 @@ __device__ __forceinline__ int efield(float v) {
 }
 __device__ __forceinline__ float inv_p2(float w) { return __int_as_float(0x7f000000 - __float_as_int(w)); }
 // 2^E as a double (|E| <= 1022; larger frames flag the problem)
-__device__ __forceinline__ double p2d(int E) { return __hiloint2double((min(max(E, -1022), 1023) + 1023) << 20, 0); }
+__device__ __forceinline__ double p2d(float E) {
+    return __hiloint2double((min(max(__float2int_rn(E), -1022), 1023) + 1023) << 20, 0);
+}
+// J of an exponent field (eb = bits of 2^J) as a float: exact
+__device__ __forceinline__ float efield_j(int eb) { return fmaf((float)eb, 1.0f / 8388608.0f, -127.f); }
 
 // ==========================================================================
 // forward sweep of one row-block
@@ -133,26 +135,26 @@ struct FwdF {           // one group of 4 forward steps, for frame E
 
 struct FwdVars {
     float zl, zd, zsh;  // own z of the previous step; diagonal input of this step; lane l-1's last z
-    int E;              // own frame
-    int Esent;          // edge stages: lane l-1's frame of the value in zsh
+    float E;            // own frame
+    float Esent;        // edge stages: lane l-1's frame of the value in zsh
     FwdF f;
-    int nE;             // the next group, decided one step early
+    float nE;           // the next group, decided one step early
     float nfJ;          // 2^(E - nE)
     FwdF nf;
     float gsum;         // this group's sum of z (frame E)
     double acc;         // partition of this lane's cells so far: sum Z
     int ebmin, ebmax;   // range of the frame steps (exponent fields)
-    int emax;           // largest |E|
+    float emax;         // largest |E|
 };
 
 struct FwdCtx {
     const float* ring;  // this lane's ring row
     const float* av;    // lane 0: handoff ring of the row above (its lane 31's z, by its step);
-    const int* af;      //   and its frames, by its group.  Other lanes (and r = 0): zeros
+    const float* af;    //   and its frames, by its group.  Other lanes (and r = 0): zeros
     float* ov;          // this row-block's handoff ring for the row-block below
-    int* of;
-    float* zrow;        // zpl row 2 (forward step 0) of this row-block, this lane
-    int* erow;          // efr group 0 of this row-block, this lane
+    float* of;
+    float* zrow;        // zpl row 0 (forward step 0) of this row-block, this lane
+    float* erow;        // efr group 0 of this row-block, this lane
     float c, G;
     float notl0;        // lane != 0 as 1 / 0
     int lane, nv, L2;
@@ -162,7 +164,7 @@ struct FwdCtx {
 // Factors of group g for a lane (not lane 0) that starts in frame E; eup0 /
 // eup1: lane l-1's frames of the values it receives in the group's first /
 // other steps.
-__device__ __forceinline__ FwdF fwd_factors(const FwdCtx& C, int E, int eup0, int eup1) {
+__device__ __forceinline__ FwdF fwd_factors(const FwdCtx& C, float E, float eup0, float eup1) {
     FwdF f;
     f.d0 = p2(eup0 - E) * C.notl0;
     f.d1 = p2(eup1 - E) * C.notl0;
@@ -184,9 +186,9 @@ __device__ __forceinline__ void fwd_lookahead(const FwdCtx& C, FwdVars& V, int g
     const int eb = efield(V.zl);
     V.ebmin = min(V.ebmin, eb);
     V.ebmax = max(V.ebmax, eb);
-    const int ea0 = C.af[(g + 7) & (kHR / 4 - 1)], ea1 = C.af[(g + 8) & (kHR / 4 - 1)];
+    const float ea0 = C.af[(g + 7) & (kHR / 4 - 1)], ea1 = C.af[(g + 8) & (kHR / 4 - 1)];
     const float w = p2(ea0 - ea1);
-    V.nE = C.l0 ? ea1 : V.E + (eb >> 23) - 127;
+    V.nE = C.l0 ? ea1 : V.E + efield_j(eb);
     V.nfJ = C.l0 ? w : __int_as_float(0x7f000000 - eb);
     const float p2J = C.l0 ? inv_p2(w) : __int_as_float(eb);
     const float p2Jup = __shfl_up_sync(kAll, p2J, 1);
@@ -210,15 +212,19 @@ __device__ __forceinline__ void fwd_apply(FwdVars& V) {
     V.zl *= V.nfJ;
     V.zd *= V.nfJ;
     V.E = V.nE;
-    V.emax = max(V.emax, abs(V.E));
+    V.emax = fmaxf(V.emax, fabsf(V.E));
     V.f = V.nf;
 }
 
-// one cell, step i of its group; returns z, and the up input in this frame
-// (the next step's diagonal input)
-__device__ __forceinline__ float fwd_cell(const FwdCtx& C, const FwdVars& V, int i, float sc, float& zuin) {
+// one cell, step i of its group; returns z, the up input in this frame (the
+// next step's diagonal input) and w = P (z_diag + 2^-E), the cell's diagonal
+// term, which is all the reverse needs of the forward: marginal = B P (Z_diag
+// + 1) / Z_total = b w 2^(Q + E - S)
+__device__ __forceinline__ float fwd_cell(const FwdCtx& C, const FwdVars& V, int i, float sc, float& zuin,
+                                          float& w) {
     const float P = ex2f(sc * C.c);
-    const float rest = fmaf(C.G, V.zl + V.f.za[i], P * (V.zd + V.f.fs));
+    w = P * (V.zd + V.f.fs);
+    const float rest = fmaf(C.G, V.zl + V.f.za[i], w);
     zuin = fmaf(V.zsh, i == 0 ? V.f.d0 : V.f.d1, V.f.za[i]);
     return fmaf(i == 0 ? V.f.Gd0 : V.f.Gd1, V.zsh, rest);
 }
@@ -235,18 +241,18 @@ __device__ __forceinline__ void fwd_stage_full(const FwdCtx& C, FwdVars& V, int 
 #pragma unroll
     for (int u = 0; u < kCW; ++u) scv[u] = ((u < kRW - c0) ? pA : pB)[u];
     float* const pz = C.zrow + (size_t)(kCW * k) * 32;
-    int* const pe = C.erow + (size_t)(kCW * k / 4) * 32;
+    float* const pe = C.erow + (size_t)(kCW * k / 4) * 32;
     float zq[4];
 #pragma unroll
     for (int u = 0; u < kCW; ++u) {
         const int i = u & 3;
         if (i == 0) fwd_apply(V);
         if (i == 3) fwd_lookahead(C, V, 4 * k + (u >> 2) + 1);
-        float zuin;
-        float z = fwd_cell(C, V, i, scv[u], zuin);
+        float zuin, w;
+        float z = fwd_cell(C, V, i, scv[u], zuin, w);
         if (MASK) z = (u < thr) ? z : 0.f;
         V.gsum += z;
-        pz[(size_t)u * 32] = z;
+        pz[(size_t)u * 32] = w;
         zq[i] = z;
         if (i == 3) {
             const int g = 4 * k + (u >> 2);
@@ -273,17 +279,17 @@ __device__ __forceinline__ void fwd_stage_start(const FwdCtx& C, FwdVars& V, int
             const int j0 = t - C.lane;
             const bool act = live & (j0 >= 0) & (j0 < C.L2);
             if (i == 0) fwd_apply(V);
-            const int eup_now = __shfl_up_sync(kAll, V.E, 1);
+            const float eup_now = __shfl_up_sync(kAll, V.E, 1);
             if (live && j0 == 0 && !C.l0) {
                 V.E = V.Esent;
                 V.f = fwd_factors(C, V.E, V.Esent, i == 0 ? eup_now : V.Esent);
             }
             if (i == 3) fwd_lookahead(C, V, 4 * k + q + 1);
-            float zuin;
-            float z = fwd_cell(C, V, i, C.ring[j0 & (kRW - 1)], zuin);
+            float zuin, w;
+            float z = fwd_cell(C, V, i, C.ring[j0 & (kRW - 1)], zuin, w);
             z = act ? z : 0.f;
             V.gsum += z;
-            C.zrow[(size_t)t * 32] = z;
+            C.zrow[(size_t)t * 32] = w;
             zq[i] = z;
             if (i == 3) {
                 const int g = t >> 2;
@@ -306,15 +312,15 @@ struct RevF {           // one group of 4 reverse steps, for frame Q
     float d0, d1;       // 2^(Q_{l+1} - Q) for the message of the first / other steps (bottom lane: 0)
     float Gd0, Gd1;
     float fb[4];        // 2^-Q, plus for the bottom lane the message from below (frame Q)
-    float kA, kB, k2;   // 2^(Q + E_diag - S) for the group's two forward frame groups; 2^(Q - S)
+    float kE;           // 2^(Q + E - S): E the lane's forward frame of these cells
 };
 
 struct RevVars {
     float br, pbp, rsh; // own b and P*b of column j+1; message from lane l+1
-    int Q;              // own frame
-    int Qsent;          // edge stages: lane l+1's frame of the message in rsh
+    float Q;            // own frame
+    float Qsent;        // edge stages: lane l+1's frame of the message in rsh
     RevF f;
-    int nQ;
+    float nQ;
     float nfJ;          // 2^(Q - nQ)
     RevF nf;
     int ebmin, ebmax;   // range of the frame steps (exponent fields)
@@ -323,35 +329,29 @@ struct RevVars {
 struct RevCtx {
     float* ring;          // ringS row of this lane
     const float* zr;      // WarpSmem::zr
-    const int* er;        // WarpSmem::er
+    const float* er;      // WarpSmem::er
     const float* bv;      // bottom lane: handoff ring of the row-block below (its lane 0's messages,
-    const int* bf;        //   by its step) and its frames, by its group.  Other lanes (and the last row-block): zeros
+    const float* bf;      //   by its step) and its frames, by its group.  Other lanes (and the last row-block): zeros
     float* ov;            // this row-block's handoff ring for the row-block above
-    int* of;
+    float* of;
     float c, G, cS;       // cS = 2^-Sfrac
     float notBot;         // lane != nv-1 as 1 / 0
-    int Sint, lane, nv, L2, P;
+    float Sint;
+    int lane, nv, L2, P;
     bool l0, bot;         // lane 0 hands its messages up; the bottom lane follows the row-block below's frames
 };
 
-// Marginal factors of reverse group h (anti-diagonals tf0 = P + 31 - 4h down
-// to tf0 - 3) in frame Q.  The diagonal input of lane l at anti-diagonal tf
-// is forward group (tf - 2) / 4 of lane l-1 (lane 0: group + 8 of the row
-// above's last lane): group gA for tf0 and tf0 - 1, gA - 1 for the rest.
-__device__ __forceinline__ void rev_kfactors(const RevCtx& C, RevF& f, int Q, int h) {
+// Marginal factor of reverse group h (anti-diagonals tf0 = P + 31 - 4h down
+// to tf0 - 3, all in forward group gA = (tf0 - 3) / 4 of this lane) in frame Q.
+__device__ __forceinline__ void rev_kfactors(const RevCtx& C, RevF& f, float Q, int h) {
     const int gA = C.P / 4 + 7 - h;
-    const int EA = C.er[(gA & 15) * kZC + 3 + C.lane];
-    const int EB = C.er[((gA - 1) & 15) * kZC + 3 + C.lane];
-    const int tq = Q - C.Sint;
-    f.kA = p2(tq + EA) * C.cS;
-    f.kB = p2(tq + EB) * C.cS;
-    f.k2 = p2(tq) * C.cS;
+    f.kE = p2(Q + C.er[(gA & 15) * 32 + C.lane] - C.Sint) * C.cS;
 }
 
 // Factors of group h for a lane (not the bottom one) that starts in frame Q;
 // qdn0 / qdn1: lane l+1's frames of the messages it receives in the group's
 // first / other steps.
-__device__ __forceinline__ RevF rev_factors(const RevCtx& C, int Q, int qdn0, int qdn1, int h) {
+__device__ __forceinline__ RevF rev_factors(const RevCtx& C, float Q, float qdn0, float qdn1, int h) {
     RevF f;
     f.d0 = p2(qdn0 - Q) * C.notBot;
     f.d1 = p2(qdn1 - Q) * C.notBot;
@@ -371,9 +371,9 @@ __device__ __forceinline__ void rev_lookahead(const RevCtx& C, RevVars& V, int h
     const int eb = efield(V.br);
     V.ebmin = min(V.ebmin, eb);
     V.ebmax = max(V.ebmax, eb);
-    const int qb0 = C.bf[(h + 7) & (kHR / 4 - 1)], qb1 = C.bf[(h + 8) & (kHR / 4 - 1)];
+    const float qb0 = C.bf[(h + 7) & (kHR / 4 - 1)], qb1 = C.bf[(h + 8) & (kHR / 4 - 1)];
     const float w = p2(qb0 - qb1);
-    V.nQ = C.bot ? qb1 : V.Q + (eb >> 23) - 127;
+    V.nQ = C.bot ? qb1 : V.Q + efield_j(eb);
     V.nfJ = C.bot ? w : __int_as_float(0x7f000000 - eb);
     const float p2J = C.bot ? inv_p2(w) : __int_as_float(eb);
     const float p2Jdn = __shfl_down_sync(kAll, p2J, 1);
@@ -402,21 +402,26 @@ __device__ __forceinline__ void rev_apply(RevVars& V) {
 struct RevOut {
     float b, pb, msg, mu;
 };
-__device__ __forceinline__ RevOut rev_cell(const RevCtx& C, const RevVars& V, int i, float sc, float ad) {
+__device__ __forceinline__ RevOut rev_cell(const RevCtx& C, const RevVars& V, int i, float sc, float w) {
     RevOut o;
     const float P = ex2f(sc * C.c);
     const float rest = fmaf(C.G, V.br, V.f.fb[i]);
     o.b = fmaf(i == 0 ? V.f.d0 : V.f.d1, V.rsh, rest);
     o.msg = fmaf(i == 0 ? V.f.Gd0 : V.f.Gd1, V.rsh, fmaf(C.G, rest, V.pbp));
     o.pb = P * o.b;
-    o.mu = o.pb * fmaf(ad, i < 2 ? V.f.kA : V.f.kB, V.f.k2);
+    o.mu = o.b * (w * V.f.kE);
     return o;
 }
 
-// 16 reverse steps with every lane active
-__device__ __forceinline__ void rev_stage_full(const RevCtx& C, RevVars& V, int k) {
+// 16 reverse steps after every lane has started.  MASK: some lanes go past
+// column 0 (or are beyond nv); thr = first step (u) at which this lane is past
+// it.  Their marginals land in ring slots whose chunks were already written
+// back (columns -31 .. -1 map to the slots of chunks 2 and 3, stored before
+// the last two stages), and their b, P*b and messages are zeroed.
+template <bool MASK>
+__device__ __forceinline__ void rev_stage_full(const RevCtx& C, RevVars& V, int k, int thr) {
     const int m16 = C.P + 16 - kCW * k;                                   // tf = m16 + 15 - u
-    const float* const zb = C.zr + ((m16 >> 4) & 1) * (16 * kZC) + 3 + C.lane;
+    const float* const zb = C.zr + ((m16 >> 4) & 1) * (16 * 32) + C.lane;
     const int cb = (C.P + 31 - kCW * k - C.lane) & (kRW - 1);            // ring column at u = 0
     float* const qA = C.ring + cb;
     float* const qB = qA + kRW;                                            // after the wrap below column 0
@@ -429,17 +434,19 @@ __device__ __forceinline__ void rev_stage_full(const RevCtx& C, RevVars& V, int 
         const int i = u & 3;
         if (i == 0) rev_apply(V);
         if (i == 3) rev_lookahead(C, V, 4 * k + (u >> 2) + 1);
-        const RevOut o = rev_cell(C, V, i, scv[u], zb[(15 - u) * kZC]);
+        const RevOut o = rev_cell(C, V, i, scv[u], zb[(15 - u) * 32]);
         (((u <= cb) ? qA : qB) - u)[0] = o.mu;
-        mq[i] = o.msg;
+        const bool act = !MASK || u < thr;
+        const float msg = act ? o.msg : 0.f;
+        mq[i] = msg;
         if (i == 3) {
             const int h = 4 * k + (u >> 2);
             sts_group_pred(C.ov + ((4 * h) & (kHR - 1)), C.of + (h & (kHR / 4 - 1)),
                            make_float4(mq[0], mq[1], mq[2], mq[3]), V.Q, C.l0);
         }
-        V.rsh = __shfl_down_sync(kAll, o.msg, 1);
-        V.br = o.b;
-        V.pbp = o.pb;
+        V.rsh = __shfl_down_sync(kAll, msg, 1);
+        V.br = act ? o.b : 0.f;
+        V.pbp = act ? o.pb : 0.f;
     }
 }
 
@@ -448,7 +455,7 @@ __device__ __forceinline__ void rev_stage_full(const RevCtx& C, RevVars& V, int 
 // on the frames of the row-block below)
 __device__ __forceinline__ void rev_stage_part(const RevCtx& C, RevVars& V, int k) {
     const int m16 = C.P + 16 - kCW * k;
-    const float* const zb = C.zr + ((m16 >> 4) & 1) * (16 * kZC) + 3 + C.lane;
+    const float* const zb = C.zr + ((m16 >> 4) & 1) * (16 * 32) + C.lane;
     const bool live = C.lane < C.nv;
     float mq[4];
 #pragma unroll 1
@@ -460,14 +467,14 @@ __device__ __forceinline__ void rev_stage_part(const RevCtx& C, RevVars& V, int 
             const int j0 = tf - C.lane;
             const bool act = live & (j0 >= 0) & (j0 < C.L2);
             if (i == 0) rev_apply(V);
-            const int qdn_now = __shfl_down_sync(kAll, V.Q, 1);
+            const float qdn_now = __shfl_down_sync(kAll, V.Q, 1);
             if (live && j0 == C.L2 - 1 && !C.bot) {
-                V.Q = 0;
-                V.f = rev_factors(C, 0, V.Qsent, i == 0 ? qdn_now : V.Qsent, 4 * k + q);
+                V.Q = 0.f;
+                V.f = rev_factors(C, 0.f, V.Qsent, i == 0 ? qdn_now : V.Qsent, 4 * k + q);
             }
             if (i == 3) rev_lookahead(C, V, 4 * k + q + 1);
             const int ci = j0 & (kRW - 1);
-            const RevOut o = rev_cell(C, V, i, C.ring[ci], zb[(15 - u) * kZC]);
+            const RevOut o = rev_cell(C, V, i, C.ring[ci], zb[(15 - u) * 32]);
             if (act) C.ring[ci] = o.mu;
             const float msg = act ? o.msg : 0.f;
             mq[i] = msg;
@@ -500,7 +507,7 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
     __shared__ int sh_Sint, sh_err, sh_bad;
     __shared__ float sh_Sfrac;
     __shared__ __align__(16) float zv[kHR];   // handoff ring of a missing neighbour: zeros
-    __shared__ int zf[kHR / 4];
+    __shared__ float zf[kHR / 4];
 
     const int b = blockIdx.x;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -538,11 +545,11 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
         progR[threadIdx.x] = -1;
     }
     if (threadIdx.x < kHR) zv[threadIdx.x] = 0.f;
-    if (threadIdx.x < kHR / 4) zf[threadIdx.x] = 0;
+    if (threadIdx.x < kHR / 4) zf[threadIdx.x] = 0.f;
     // rings start at zero: a neighbour's look-ahead past the last written group reads zeros
     auto clear_rings = [&]() {
         for (int i = lane; i < 2 * kHR; i += 32) (&W.hv[0][0])[i] = 0.f;
-        for (int i = lane; i < 2 * (kHR / 4); i += 32) (&W.hf[0][0])[i] = 0;
+        for (int i = lane; i < 2 * (kHR / 4); i += 32) (&W.hf[0][0])[i] = 0.f;
     };
     clear_rings();
     if (threadIdx.x == 0) {
@@ -559,9 +566,9 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
     FwdVars V;
     V.acc = 0.0;
     V.gsum = 0.f;
-    V.E = 0;
+    V.E = 0.f;
     V.ebmin = V.ebmax = 0x3f800000;
-    V.emax = 0;
+    V.emax = 0.f;
     for (int r = warp; r < nRB; r += kNW) {
         const int nv = min(32, L1 - 32 * r);
         const int nst = (L2 + nv - 1 + kCW - 1) / kCW;
@@ -574,7 +581,7 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
         C.af = (hasB && lane == 0) ? Wp.hf[((r - 1) / kNW) & 1] : zf;
         C.ov = W.hv[(r / kNW) & 1];
         C.of = W.hf[(r / kNW) & 1];
-        C.zrow = zblk + 2 * 32 + lane;
+        C.zrow = zblk + lane;
         C.erow = LY.efr + (size_t)r * est + lane;
         C.c = c;
         C.G = G;
@@ -590,9 +597,6 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
         // (row-block r - 2kNW + 1) must be complete before it is reused
         if (r >= 2 * kNW) wait_flag(&progF[wnext], ((r - 2 * kNW + 1) << 16) | kStageMask, &sh_err);
         __syncwarp();
-        // rows 0, 1 of the z plane (steps -2, -1) are zero
-        zblk[lane] = 0.f;
-        zblk[32 + lane] = 0.f;
         if (0 < nch) tile_load<4>(tS, 0, L2);
         cp_async_commit();
         V.zl = V.zd = V.zsh = 0.f;
@@ -663,9 +667,7 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
         const float* srow = S + (size_t)(32 * r) * L2m;
         const bool hasBelow = r + 1 < nRB, hasAbove = r > 0;
         const float* const zblk = LY.zpl + (size_t)r * zst;
-        const int* const eblk = LY.efr + (size_t)r * est;
-        const float* const zab = LY.zpl + (size_t)(r - 1) * zst + 31;
-        const int* const eab = LY.efr + (size_t)(r - 1) * est + 31;
+        const float* const eblk = LY.efr + (size_t)r * est;
         RevCtx C;
         C.ring = W.ringS + lane * kRW;
         C.zr = &W.zr[0][0];
@@ -679,7 +681,7 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
         C.cS = ex2f(-sh_Sfrac);
         C.notBot = lane == nv - 1 ? 0.f : 1.f;
         C.bot = lane == nv - 1;
-        C.Sint = sh_Sint;
+        C.Sint = (float)sh_Sint;
         C.lane = lane;
         C.nv = nv;
         C.L2 = L2;
@@ -688,39 +690,25 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
         const Tile tS = make_tile(srow, L2m, W.ringS, nv, lane);
         const Tile tM = make_tile(out ? out + (size_t)(32 * r) * L2m : srow, L2m, W.ringS, nv, lane);
 
-        // staging for stage kb (M = P/16 + 1 - kb): z rows 16M .. 16M+15 and
-        // the row above's at 16M+32 .. 16M+47; frames of groups 4M-2 .. 4M+3
-        // (the row above's: +8), read by the stage's cells and look-aheads
+        // staging for stage kb (M = P/16 + 1 - kb): w rows 16M .. 16M+15 (2 KB,
+        // contiguous) and the frames of groups 4M-1 .. 4M+3, read by the
+        // stage's cells and look-aheads
         auto batch = [&](int kb) {
             const int M = P / kCW + 1 - kb;
             float* const zd = &W.zr[M & 1][0];
             const float* const zs = zblk + (size_t)(16 * M) * 32;
 #pragma unroll
-            for (int it = 0; it < 4; ++it) {
-                const int cc = lane + 32 * it, row = cc >> 3, c4 = cc & 7;
-                cp_async16(zd + row * kZC + 4 + 4 * c4, zs + row * 32 + 4 * c4, 16);
-            }
-            if (hasAbove && lane < 16) cp_async4(zd + lane * kZC + 3, zab + (size_t)(16 * M + 32 + lane) * 32);
-            const int gl = 4 * M - 2;
+            for (int it = 0; it < 4; ++it) cp_async16(zd + 4 * (lane + 32 * it), zs + 4 * (lane + 32 * it), 16);
+            const int gl = 4 * M - 1;
 #pragma unroll
             for (int it = 0; it < 2; ++it) {
                 const int cc = lane + 32 * it, g = gl + (cc >> 3), c4 = cc & 7;
-                if (cc < 48 && g >= 0)
-                    cp_async16(W.er + (g & 15) * kZC + 4 + 4 * c4, eblk + (size_t)g * 32 + 4 * c4, 16);
-            }
-            if (hasAbove && lane >= 16 && lane < 22) {  // slot g holds the row above's group g + 8 (g >= -2)
-                const int g = gl + lane - 16;
-                cp_async4(W.er + (g & 15) * kZC + 3, eab + (size_t)(g + 8) * 32);
+                if (cc < 40 && g >= 0) cp_async16(W.er + (g & 15) * 32 + 4 * c4, eblk + (size_t)g * 32 + 4 * c4, 16);
             }
         };
 
         if (q >= 2 * kNW) wait_flag(&progR[wnext], ((q - 2 * kNW + 1) << 16) | kStageMask, &sh_err);
         __syncwarp();
-        if (!hasAbove && lane < 16) {  // no row above: lane 0's diagonal inputs are zero
-            W.zr[0][lane * kZC + 3] = 0.f;
-            W.zr[1][lane * kZC + 3] = 0.f;
-            W.er[lane * kZC + 3] = 0;
-        }
         {   // stage 0 reads score chunks M0-2 .. M0 (M0 = P/16 + 1)
             const int M0 = P / kCW + 1;
             for (int ch = M0; ch >= M0 - 2; --ch)
@@ -730,8 +718,8 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
         cp_async_commit();
 
         RV.br = RV.pbp = RV.rsh = 0.f;
-        RV.Q = 0;
-        RV.Qsent = 0;
+        RV.Q = 0.f;
+        RV.Qsent = 0.f;
         RV.f.d1 = 0.f;  // the bottom lane keeps zero neighbour factors; the others set theirs when they start
         for (int k = 0; k < nstR; ++k) {
             const int M = P / kCW + 1 - k;
@@ -749,11 +737,14 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
             __syncwarp();
             if (k == 0) rev_lookahead(C, RV, 0);
             // full: every lane started before the stage (lane 0 starts at step
-            // P - L2 + 32, which must run the start logic) and none finishes in it
-            if ((nv == 32) && (kCW * k > P + 32 - L2) && (kCW * k + kCW - 1 <= P - 1))
-                rev_stage_full(C, RV, k);
-            else
+            // P - L2 + 32, which must run the start logic); masked when a lane
+            // passes column 0 in it (tf - lane < 0 from u = 16M + 16 - lane on)
+            if (kCW * k <= P + 32 - L2)
                 rev_stage_part(C, RV, k);
+            else if (nv == 32 && kCW * k + kCW - 1 <= P - 1)
+                rev_stage_full<false>(C, RV, k, 0);
+            else
+                rev_stage_full<true>(C, RV, k, lane < nv ? 16 * M + 16 - lane : -1);
             __syncwarp();  // every lane's reads of the row-block below's ring come before the release
             if (lane == 0) st_release(&progR[warp], (q << 16) | min(k + 1, kStageMask - 1));
         }
@@ -772,7 +763,7 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
     // dependency wait that gave up: the caller recomputes this problem with
     // the log-domain kernel
     const bool outside = min(V.ebmin, RV.ebmin) < ((127 - kJMax) << 23) ||
-                         max(V.ebmax, RV.ebmax) > ((127 + kJMax) << 23) || V.emax > 1000;
+                         max(V.ebmax, RV.ebmax) > ((127 + kJMax) << 23) || V.emax > 1000.f;
     const int redo = __syncthreads_or(outside ? 1 : 0) || sh_err || sh_bad;
     if (threadIdx.x == 0 && p.redo) p.redo[b] = redo;
 }
