@@ -56,7 +56,8 @@ static size_t op_bytes(int family, int op, int B, int L1, int L2) {
             const size_t lf = family == D2P_FAMILY_LINEAR ? lin_fast_workspace_bytes(B, L1, L2) : 0;
             pe = pe > wf ? pe : wf;
             pe = pe > lf ? pe : lf;
-            return align256(pe) + align256((size_t)(B > 0 ? B : 1) * sizeof(int));
+            // flags, then the CTA order of ragged batches
+            return align256(pe) + 2 * align256((size_t)(B > 0 ? B : 1) * sizeof(int));
         }
         case D2P_OP_HVP:
             return plane_bytes(family, MODE_HVP, B, L1, L2);
@@ -139,9 +140,17 @@ int d2p_sw_forward_backward(const float* scores, const int* lengths, int B, int 
         pe = pe > wf ? pe : wf;
         pe = pe > lf ? pe : lf;
         int* flags = (int*)((char*)workspace + align256(pe));
+        int* order = (int*)((char*)flags + align256((size_t)B * sizeof(int)));
         a.redo = flags;
         a.only = nullptr;
+        a.order = nullptr;
+        if (lengths && !grad_gap && !grad_temperature) {
+            const int ro = launch_lin_order(lengths, B, L1, L2, order, st);
+            if (ro == D2P_OK) a.order = order;
+            else if (ro != kNotHandled) return ro;
+        }
         int rc = launch_lin_fast(a, workspace_bytes, st);
+        a.order = nullptr;
         if (rc == D2P_OK) a.only = flags;
         else if (rc != kNotHandled) return rc;
         rc = launch_wavefront(a, D2P_FAMILY_LINEAR, workspace_bytes, st);

@@ -57,12 +57,16 @@ struct SwArgs {
     float* dot_out;                     //   dot_out[b] = sum_ij dot_with[b,i,j] * dP[b,i,j]
     int* redo;                          // [B] out: set for problems the kernel could not finish
     const int* only;                    // [B] in, optional: run only the problems whose entry is set
+    const int* order;                   // [B] in, optional: problem of each CTA (largest first)
 };
 
 // linear-domain fast path (sw_linear.cu): value + marginals without parameter
 // gradients; returns -1 when the shape or arguments are not covered
 size_t lin_fast_workspace_bytes(int B, int L1, int L2);
 int launch_lin_fast(const SwArgs& a, size_t ws_bytes, cudaStream_t st);
+// order[B]: problems by decreasing estimated cost, for batches of uneven
+// lengths that take more than one wave; returns -1 when ordering cannot help
+int launch_lin_order(const int* lengths, int B, int L1, int L2, int* order, cudaStream_t st);
 
 int launch_lin_plane(const SwArgs& a, cudaStream_t st);
 

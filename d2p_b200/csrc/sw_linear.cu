@@ -509,7 +509,7 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
     __shared__ __align__(16) float zv[kHR];   // handoff ring of a missing neighbour: zeros
     __shared__ float zf[kHR / 4];
 
-    const int b = blockIdx.x;
+    const int b = p.order ? p.order[blockIdx.x] : blockIdx.x;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int L1m = p.L1, L2m = p.L2;
     const int L1 = p.lengths ? min(max(p.lengths[2 * b], 0), L1m) : L1m;
@@ -768,9 +768,65 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
     if (threadIdx.x == 0 && p.redo) p.redo[b] = redo;
 }
 
+// Problems of a ragged batch by decreasing estimated cost (cells plus the
+// row-block pipeline's fill), so that the block scheduler starts the longest
+// CTAs first and the last wave is made of short ones.  One CTA: a 1024-bucket
+// counting sort.  The order within a bucket does not matter: every problem's
+// result is independent of the CTA that computes it.
+constexpr int kOrderThreads = 1024;
+__global__ void __launch_bounds__(kOrderThreads) lin_order_kernel(const int* __restrict__ lengths, int B, int L1m,
+                                                                  int L2m, int* __restrict__ order) {
+    __shared__ int cnt[kOrderThreads];
+    __shared__ int wsum[kOrderThreads / 32];
+    const int t = threadIdx.x;
+    cnt[t] = 0;
+    __syncthreads();
+    const float kmax = (float)L1m * (float)L2m + 48.f * (float)(L1m + L2m);
+    auto bucket = [&](int i) {
+        const int l1 = min(max(lengths[2 * i], 0), L1m), l2 = min(max(lengths[2 * i + 1], 0), L2m);
+        const float key = (float)l1 * (float)l2 + 48.f * (float)(l1 + l2);
+        // largest first: bucket 0 holds the most expensive problems
+        return kOrderThreads - 1 - min(kOrderThreads - 1, (int)(key * (float)(kOrderThreads - 1) / kmax));
+    };
+    for (int i = t; i < B; i += kOrderThreads) atomicAdd(&cnt[bucket(i)], 1);
+    __syncthreads();
+    // exclusive scan of cnt
+    const int v = cnt[t];
+    int x = v;
+    const int lane = t & 31, w = t >> 5;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) wsum[w] = x;
+    __syncthreads();
+    if (w == 0) {
+        int s = wsum[lane];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, s, o);
+            if (lane >= o) s += y;
+        }
+        wsum[lane] = s;
+    }
+    __syncthreads();
+    cnt[t] = x - v + (w > 0 ? wsum[w - 1] : 0);
+    __syncthreads();
+    for (int i = t; i < B; i += kOrderThreads) order[atomicAdd(&cnt[bucket(i)], 1)] = i;
+}
+
 }  // namespace lin
 
 // ------------------------------------------------------------------ host side
+int launch_lin_order(const int* lengths, int B, int L1, int L2, int* order, cudaStream_t st) {
+    if (!lengths || !order || B <= 0) return -1;
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (B <= 2 * sms) return -1;  // one wave: every CTA starts at once
+    lin::lin_order_kernel<<<1, lin::kOrderThreads, 0, st>>>(lengths, B, L1, L2, order);
+    return (int)cudaGetLastError();
+}
 size_t lin_fast_workspace_bytes(int B, int L1, int L2) {
     if (L1 > 32 * lin::kMaxRB || L2 % 4 != 0) return 0;
     return lin::per_problem_bytes(L1, L2) * (size_t)B;

@@ -153,6 +153,24 @@ def test_fast_path_repeatable_across_launches(d2p, cuda_device, L1, L2):
     check("marginals", m0[idx], r64["marginals"], r32["marginals"])
 
 
+def test_ragged_batch_in_several_waves(d2p, cuda_device):
+    """A ragged batch of more than two problems per SM runs its CTAs in order
+    of decreasing cost; every problem must still get its own result."""
+    B, L1, L2 = 400, 96, 128
+    s = scores(B, L1, L2, seed=41)
+    ln = lengths_for(B, L1, L2, seed=42)
+    v, m = torch.ops.d2p.soft_sw_float(s.to(cuda_device), -1.0, 1.0, ln.to(cuda_device))
+    idx = [0, 1, 137, 399]
+    r64 = oracle.sw_linear(s[idx].numpy(), ln[idx].numpy(), -1.0, 1.0, "f64")
+    r32 = oracle.sw_linear(s[idx].numpy(), ln[idx].numpy(), -1.0, 1.0, "f32")
+    check("value", v[idx], r64["value"], r32["value"])
+    check("marginals", m[idx], r64["marginals"], r32["marginals"])
+    # every problem against the log-domain kernel, which runs in batch order
+    v2, m2, _, _ = torch.ops.d2p.soft_sw_with_grads(s.to(cuda_device), -1.0, 1.0, ln.to(cuda_device))
+    torch.testing.assert_close(v, v2, rtol=1e-5, atol=1e-4)
+    torch.testing.assert_close(m, m2, rtol=0, atol=5e-5)
+
+
 # Shapes routed to the register/shared-memory wavefront kernel (L2 % 4 == 0):
 # partial and multiple row-blocks, L2 below/around/above the 16-column chunk.
 FAST = [  # (B, L1, L2, T)
