@@ -238,9 +238,10 @@ def run_ours(args, cfg):
     nk = max(3, args.steps)
     with torch.no_grad():
         def kern():
-            if fam == "linear":  # the op soft_sw's forward calls when gap / T need no gradient
+            # the op the forward calls when the gap parameters and T need no gradient
+            if fam == "linear":
                 return torch.ops.d2p.soft_sw_float(s_dev, gap, T, len_dev)
-            return torch.ops.d2p.soft_sw_affine_with_grads(s_dev, gap[0], gap[1], T, len_dev)
+            return torch.ops.d2p.soft_sw_affine_float(s_dev, gap[0], gap[1], T, len_dev)
         for _ in range(2):
             kern()
         torch.cuda.synchronize()
@@ -313,7 +314,7 @@ def run_ours(args, cfg):
         "bound": bound, "achieved": round(achieved, 4), "peak": round(peak, 4), "unit": unit,
         "frac": round(achieved / peak, 4), "traffic": traffic,
         "kernel": ("lin_fast_kernel: linear-domain value+marginals (d2p_sw_forward_backward)" if fam == "linear"
-                   else "aff fused value+marginals (d2p_sw_affine_forward_backward)"),
+                   else "aff_fast_kernel: linear-domain value+marginals (d2p_sw_affine_forward_backward)"),
         "kernel_ms": round(k_ms, 4), "time_bound_ms": round(max(t_hbm, t_mufu) * 1e3, 4),
         "hbm_gbs_achieved": round(k_bytes / k_s / 1e9, 2), "hbm_peak_gbs": hbm_gbs,
         "mufu_tops_achieved": round(k_mufu / k_s / 1e12, 3), "mufu_peak_tops": round(mufu_peak / 1e12, 3),

@@ -51,7 +51,8 @@ static size_t op_bytes(int family, int op, int B, int L1, int L2) {
             // the fast path's workspace, or the plane engine's (which also serves as
             // the fix-up for problems the fast path flags), then one flag per problem
             size_t pe = plane_bytes(family, MODE_MARG, B, L1, L2);
-            const size_t wf = wavefront_workspace_bytes(family, B, L1, L2);
+            const size_t wf = family == D2P_FAMILY_LINEAR ? wavefront_workspace_bytes(family, B, L1, L2)
+                                                          : aff_fast_workspace_bytes(B, L1, L2, true);
             if (wf == 0) return pe;
             const size_t lf = family == D2P_FAMILY_LINEAR ? lin_fast_workspace_bytes(B, L1, L2) : 0;
             pe = pe > wf ? pe : wf;
@@ -289,8 +290,32 @@ int d2p_sw_affine_forward_backward(const void* scores, int scores_dtype, const i
     a.grad_gap2 = grad_gap_ext;
     a.grad_T = grad_temperature;
     a.ws = (float*)workspace;
-    int rc = launch_wavefront(a, D2P_FAMILY_AFFINE, workspace_bytes, st);
-    if (rc != kNotHandled) return rc;
+    const size_t af = aff_fast_workspace_bytes(B, L1, L2, true);
+    if (af > 0) {
+        // linear-domain kernel (no parameter gradients requested), then the
+        // plane engine for the problems it flagged
+        size_t pe = plane_bytes(D2P_FAMILY_AFFINE, MODE_MARG, B, L1, L2);
+        pe = pe > af ? pe : af;
+        int* flags = (int*)((char*)workspace + align256(pe));
+        int* order = (int*)((char*)flags + align256((size_t)B * sizeof(int)));
+        a.redo = flags;
+        a.only = nullptr;
+        a.order = nullptr;
+        if (lengths && !grad_gap_open && !grad_gap_ext && !grad_temperature) {
+            const int ro = launch_lin_order(lengths, B, L1, L2, order, st);
+            if (ro == D2P_OK) a.order = order;
+            else if (ro != kNotHandled) return ro;
+        }
+        int rc = launch_aff_fast(a, workspace_bytes, st);
+        a.order = nullptr;
+        a.redo = nullptr;
+        if (rc == D2P_OK) {
+            a.only = flags;
+            return launch_aff_plane(a, st);
+        }
+        if (rc != kNotHandled) return rc;
+        a.only = nullptr;
+    }
     return launch_aff_plane(a, st);
 }
 

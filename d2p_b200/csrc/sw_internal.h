@@ -64,6 +64,11 @@ struct SwArgs {
 // gradients; returns -1 when the shape or arguments are not covered
 size_t lin_fast_workspace_bytes(int B, int L1, int L2);
 int launch_lin_fast(const SwArgs& a, size_t ws_bytes, cudaStream_t st);
+// affine-gap linear-domain fast path (sw_affine_fast.cu): value + marginals
+// without parameter gradients, fp32 or bf16 scores (bf16 widened into the
+// workspace first); returns -1 when the shape or arguments are not covered
+size_t aff_fast_workspace_bytes(int B, int L1, int L2, bool bf16);
+int launch_aff_fast(const SwArgs& a, size_t ws_bytes, cudaStream_t st);
 // order[B]: problems by decreasing estimated cost, for batches of uneven
 // lengths that take more than one wave; returns -1 when ordering cannot help
 int launch_lin_order(const int* lengths, int B, int L1, int L2, int* order, cudaStream_t st);

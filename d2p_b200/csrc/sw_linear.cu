@@ -32,11 +32,16 @@
 // diagonal-major plane (row = forward step, 32 lanes per row) with one
 // coalesced 128-byte store per step, and each lane's frame once per group;
 // the reverse stages the plane 16 rows at a time through shared memory, each
-// lane reading its own column (marginal = b w 2^(Q + E - S)).  Values that cross to the next row-block inside a pass (the
-// forward's last lane down, the reverse's lane-0 messages up) go through a
-// small shared-memory ring of the producing warp, one 16-byte store per group
-// by the boundary lane: reading a global line another warp has just written
-// costs about a microsecond, an order of magnitude more than the step it feeds.
+// lane reading its own column (marginal = b w 2^(Q + E - S)).  Values that
+// cross to the next row-block inside a pass (the forward's last lane down, the
+// reverse's lane-0 messages up) are written by the boundary lane once per
+// group (one 16-byte store) to a per-row-block boundary row in global memory;
+// the consumer's reading lane copies each finished producer stage into shared
+// memory with cp.async, one to three stages before its look-aheads read it.
+// Consumers wait for producers, never the reverse: with warps taking
+// row-blocks round-robin, a producer that waited for its consumer could wait
+// on a warp still busy with its own earlier row-block, whose progress waits on
+// the same chain.
 //
 // Reverse indexing: reverse step tau of a row-block works on forward
 // anti-diagonal tf = P + 31 - tau (P = 16 ceil((L2-1)/16)); lane l is at
@@ -55,36 +60,41 @@ using namespace ring;
 constexpr int kMaxRB = 512;              // row-blocks per problem (L1 <= 16384)
 constexpr int kNW = 6;                   // warps per CTA
 constexpr int kJMax = 60;                // largest frame step (log2) a problem may take
-constexpr int kHR = 128;                 // handoff ring: steps per parity
-constexpr int kBack = 8;                 // a producer overwrites ring steps its consumer read 8+ stages ago
+constexpr int kHR = 128;                 // staging ring of a neighbour's boundary values (steps)
 
 struct WarpSmem {
     float ringS[32 * kRW];    // scores [rows][64]; reverse: marginals written in place
     float zr[2][16 * 32];     // reverse: the forward's w of 16 anti-diagonals, two slots
     float er[16 * 32];        // reverse: forward frames, 16 group slots
-    // handoff ring, written by this warp's boundary lane for the neighbouring
-    // row-block, by step (values) and by group (frames); two parities so that a
-    // warp's next row-block never overwrites what the neighbour still reads.
-    // Forward: lane 31's z; reverse: lane 0's messages to the row above.
-    float hv[2][kHR];
-    float hf[2][kHR / 4];
+    // staging of the neighbouring row-block's boundary values, by its step,
+    // and its frames, by its group (forward: the row above's lane 31 z;
+    // reverse: the row-block below's lane 0 messages)
+    float sv[kHR];
+    float sf[kHR / 4];
 };
 static_assert(sizeof(WarpSmem) % 16 == 0, "per-warp shared blocks must stay 16-byte aligned");
 
 struct Layout {  // per-problem workspace
     float* zpl;      // [nRB][ZT][32]   w = P (Z_diag + 1) of forward step t, frame E, at row t
     float* efr;      // [nRB][GT][32]   frame of each lane for each group of 4 forward steps
+    float* hz;       // [nRB][ZT]       boundary values of each row-block, by its step
+    float* hfr;      // [nRB][GT]       and their frames, by its group
 };
 
 // Row counts cover every row the reverse's staging reaches past the last
 // step (up to 46 rows past L2, and 12 frame groups).
 __host__ __device__ inline int zt_rows(int L2m) { return L2m + 96; }
 __host__ __device__ inline int gt_rows(int L2m) { return (L2m + 96) / 4; }
+// boundary rows are stored and staged in 16-byte pieces: strides in whole float4s
+__host__ __device__ inline int hz_stride(int L2m) { return (zt_rows(L2m) + 3) & ~3; }
+__host__ __device__ inline int hf_stride(int L2m) { return (gt_rows(L2m) + 3) & ~3; }
 
 __host__ __device__ inline size_t per_problem_bytes(int L1m, int L2m) {
     const size_t nrb = (size_t)(L1m + 31) / 32;
     size_t b = align_up(nrb * zt_rows(L2m) * 32 * 4, 256);
     b += align_up(nrb * gt_rows(L2m) * 32 * 4, 256);
+    b += align_up(nrb * hz_stride(L2m) * 4, 256);
+    b += align_up(nrb * hf_stride(L2m) * 4, 256);
     return b;
 }
 
@@ -95,6 +105,10 @@ __device__ inline Layout carve(float* ws, int b, int L1m, int L2m) {
     L.zpl = (float*)base;
     base += align_up(nrb * zt_rows(L2m) * 32 * 4, 256);
     L.efr = (float*)base;
+    base += align_up(nrb * gt_rows(L2m) * 32 * 4, 256);
+    L.hz = (float*)base;
+    base += align_up(nrb * hz_stride(L2m) * 4, 256);
+    L.hfr = (float*)base;
     return L;
 }
 
@@ -142,16 +156,18 @@ struct FwdVars {
     float nfJ;          // 2^(E - nE)
     FwdF nf;
     float gsum;         // this group's sum of z (frame E)
-    double acc;         // partition of this lane's cells so far: sum Z
+    double acc;         // partition of this lane's cells so far: sum Z 2^-ab
+    float ab;           // base (log2) of acc: raised with the frames, so that the
+                        // partition may exceed the double range (S > 1023 log2 units)
     int ebmin, ebmax;   // range of the frame steps (exponent fields)
-    float emax;         // largest |E|
+    float emax;         // largest E - ab of a group (must stay inside double range)
 };
 
 struct FwdCtx {
     const float* ring;  // this lane's ring row
-    const float* av;    // lane 0: handoff ring of the row above (its lane 31's z, by its step);
+    const float* av;    // lane 0: the row above's boundary values staged by its step (ring of kHR);
     const float* af;    //   and its frames, by its group.  Other lanes (and r = 0): zeros
-    float* ov;          // this row-block's handoff ring for the row-block below
+    float* ov;          // this row-block's boundary row (global), by step, and its frames by group
     float* of;
     float* zrow;        // zpl row 0 (forward step 0) of this row-block, this lane
     float* erow;        // efr group 0 of this row-block, this lane
@@ -207,13 +223,24 @@ __device__ __forceinline__ void fwd_lookahead(const FwdCtx& C, FwdVars& V, int g
 
 // group boundary: the finished group's partition in absolute terms, then the new frame
 __device__ __forceinline__ void fwd_apply(FwdVars& V) {
-    V.acc = fma((double)V.gsum, p2d(V.E), V.acc);
+    const float dE = V.E - V.ab;
+    V.acc = fma((double)V.gsum, p2d(dE), V.acc);
+    V.emax = fmaxf(V.emax, dE);
     V.gsum = 0.f;
     V.zl *= V.nfJ;
     V.zd *= V.nfJ;
     V.E = V.nE;
-    V.emax = fmaxf(V.emax, fabsf(V.E));
     V.f = V.nf;
+}
+
+// Once per stage: move the partition's base up with the frames (a group's
+// frame moves by at most kJMax, so E - ab stays below 700 + 4 kJMax until the
+// next check).  Frames far below the base add nothing visible to acc.
+__device__ __forceinline__ void acc_rebase(double& acc, float& ab, float E) {
+    if (E - ab > 700.f) {
+        acc *= p2d(ab - E);
+        ab = E;
+    }
 }
 
 // one cell, step i of its group; returns z, the up input in this frame (the
@@ -247,7 +274,10 @@ __device__ __forceinline__ void fwd_stage_full(const FwdCtx& C, FwdVars& V, int 
     for (int u = 0; u < kCW; ++u) {
         const int i = u & 3;
         if (i == 0) fwd_apply(V);
-        if (i == 3) fwd_lookahead(C, V, 4 * k + (u >> 2) + 1);
+        if (i == 3) {
+            if (u == kCW - 1) cp_async_wait1();  // the last look-ahead's boundary values (copied at stage start)
+            fwd_lookahead(C, V, 4 * k + (u >> 2) + 1);
+        }
         float zuin, w;
         float z = fwd_cell(C, V, i, scv[u], zuin, w);
         if (MASK) z = (u < thr) ? z : 0.f;
@@ -257,8 +287,7 @@ __device__ __forceinline__ void fwd_stage_full(const FwdCtx& C, FwdVars& V, int 
         if (i == 3) {
             const int g = 4 * k + (u >> 2);
             pe[(u >> 2) * 32] = V.E;
-            sts_group_pred(C.ov + ((4 * g) & (kHR - 1)), C.of + (g & (kHR / 4 - 1)),
-                           make_float4(zq[0], zq[1], zq[2], zq[3]), V.E, C.l31);
+            stg_group_pred(C.ov + 4 * g, C.of + g, make_float4(zq[0], zq[1], zq[2], zq[3]), V.E, C.l31);
         }
         V.zd = zuin;
         V.zl = z;
@@ -284,7 +313,10 @@ __device__ __forceinline__ void fwd_stage_start(const FwdCtx& C, FwdVars& V, int
                 V.E = V.Esent;
                 V.f = fwd_factors(C, V.E, V.Esent, i == 0 ? eup_now : V.Esent);
             }
-            if (i == 3) fwd_lookahead(C, V, 4 * k + q + 1);
+            if (i == 3) {
+                if (q == 3) cp_async_wait1();
+                fwd_lookahead(C, V, 4 * k + q + 1);
+            }
             float zuin, w;
             float z = fwd_cell(C, V, i, C.ring[j0 & (kRW - 1)], zuin, w);
             z = act ? z : 0.f;
@@ -294,8 +326,7 @@ __device__ __forceinline__ void fwd_stage_start(const FwdCtx& C, FwdVars& V, int
             if (i == 3) {
                 const int g = t >> 2;
                 C.erow[(size_t)g * 32] = V.E;
-                sts_group_pred(C.ov + ((4 * g) & (kHR - 1)), C.of + (g & (kHR / 4 - 1)),
-                               make_float4(zq[0], zq[1], zq[2], zq[3]), V.E, C.l31);
+                stg_group_pred(C.ov + 4 * g, C.of + g, make_float4(zq[0], zq[1], zq[2], zq[3]), V.E, C.l31);
             }
             V.zd = act ? zuin : 0.f;
             V.zl = z;
@@ -330,9 +361,9 @@ struct RevCtx {
     float* ring;          // ringS row of this lane
     const float* zr;      // WarpSmem::zr
     const float* er;      // WarpSmem::er
-    const float* bv;      // bottom lane: handoff ring of the row-block below (its lane 0's messages,
-    const float* bf;      //   by its step) and its frames, by its group.  Other lanes (and the last row-block): zeros
-    float* ov;            // this row-block's handoff ring for the row-block above
+    const float* bv;      // bottom lane: the row-block below's lane-0 messages staged by its step (ring
+    const float* bf;      //   of kHR) and its frames, by its group.  Other lanes (and the last row-block): zeros
+    float* ov;            // this row-block's boundary row (global) for the row-block above
     float* of;
     float c, G, cS;       // cS = 2^-Sfrac
     float notBot;         // lane != nv-1 as 1 / 0
@@ -433,7 +464,10 @@ __device__ __forceinline__ void rev_stage_full(const RevCtx& C, RevVars& V, int 
     for (int u = 0; u < kCW; ++u) {
         const int i = u & 3;
         if (i == 0) rev_apply(V);
-        if (i == 3) rev_lookahead(C, V, 4 * k + (u >> 2) + 1);
+        if (i == 3) {
+            if (u == kCW - 1) cp_async_wait1();
+            rev_lookahead(C, V, 4 * k + (u >> 2) + 1);
+        }
         const RevOut o = rev_cell(C, V, i, scv[u], zb[(15 - u) * 32]);
         (((u <= cb) ? qA : qB) - u)[0] = o.mu;
         const bool act = !MASK || u < thr;
@@ -441,8 +475,7 @@ __device__ __forceinline__ void rev_stage_full(const RevCtx& C, RevVars& V, int 
         mq[i] = msg;
         if (i == 3) {
             const int h = 4 * k + (u >> 2);
-            sts_group_pred(C.ov + ((4 * h) & (kHR - 1)), C.of + (h & (kHR / 4 - 1)),
-                           make_float4(mq[0], mq[1], mq[2], mq[3]), V.Q, C.l0);
+            stg_group_pred(C.ov + 4 * h, C.of + h, make_float4(mq[0], mq[1], mq[2], mq[3]), V.Q, C.l0);
         }
         V.rsh = __shfl_down_sync(kAll, msg, 1);
         V.br = act ? o.b : 0.f;
@@ -472,7 +505,10 @@ __device__ __forceinline__ void rev_stage_part(const RevCtx& C, RevVars& V, int 
                 V.Q = 0.f;
                 V.f = rev_factors(C, 0.f, V.Qsent, i == 0 ? qdn_now : V.Qsent, 4 * k + q);
             }
-            if (i == 3) rev_lookahead(C, V, 4 * k + q + 1);
+            if (i == 3) {
+                if (q == 3) cp_async_wait1();
+                rev_lookahead(C, V, 4 * k + q + 1);
+            }
             const int ci = j0 & (kRW - 1);
             const RevOut o = rev_cell(C, V, i, C.ring[ci], zb[(15 - u) * 32]);
             if (act) C.ring[ci] = o.mu;
@@ -480,8 +516,7 @@ __device__ __forceinline__ void rev_stage_part(const RevCtx& C, RevVars& V, int 
             mq[i] = msg;
             if (i == 3) {
                 const int h = 4 * k + q;
-                sts_group_pred(C.ov + ((4 * h) & (kHR - 1)), C.of + (h & (kHR / 4 - 1)),
-                               make_float4(mq[0], mq[1], mq[2], mq[3]), V.Q, C.l0);
+                stg_group_pred(C.ov + 4 * h, C.of + h, make_float4(mq[0], mq[1], mq[2], mq[3]), V.Q, C.l0);
             }
             V.rsh = __shfl_down_sync(kAll, msg, 1);
             V.br = act ? o.b : 0.f;
@@ -546,25 +581,51 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
     }
     if (threadIdx.x < kHR) zv[threadIdx.x] = 0.f;
     if (threadIdx.x < kHR / 4) zf[threadIdx.x] = 0.f;
-    // rings start at zero: a neighbour's look-ahead past the last written group reads zeros
-    auto clear_rings = [&]() {
-        for (int i = lane; i < 2 * kHR; i += 32) (&W.hv[0][0])[i] = 0.f;
-        for (int i = lane; i < 2 * (kHR / 4); i += 32) (&W.hf[0][0])[i] = 0.f;
-    };
-    clear_rings();
     if (threadIdx.x == 0) {
         sh_err = 0;
         sh_bad = 0;
     }
     __syncthreads();
-    // the neighbouring warps: the one that produces this warp's inputs and the
-    // one that consumes its outputs (row-block r-1 / r+1 forward, r+1 / r-1 reverse)
-    const int wprev = (warp + kNW - 1) % kNW, wnext = (warp + 1) % kNW;
-    WarpSmem& Wp = reinterpret_cast<WarpSmem*>(smem_raw)[wprev];
+    // the warp that computes the neighbouring row-block this warp's inputs come
+    // from (row-block r-1 forward, r+1 reverse): round-robin assignment
+    const int wprev = (warp + kNW - 1) % kNW;
+    const size_t hzst = (size_t)hz_stride(L2m), hfst = (size_t)hf_stride(L2m);
+
+    // Boundary values of the neighbouring row-block (boundary row hz, frames hf),
+    // staged by the one lane that reads them.  Look-ahead q of stage k reads the
+    // neighbour's steps 16k+4q+35 .. 16k+4q+39 and groups 4k+q+8, 4k+q+9: look-
+    // aheads 0..2 need its stages up to k+2, the last one its stage k+3.  The
+    // prologue copies its stages 0..2 (from step 28 and group 4 on); stage k,
+    // once the neighbour has finished its stage k+3, copies that stage (steps
+    // 16k+48 .. 16k+63, groups 4k+12 .. 4k+15) as a copy group of its own, which
+    // the last look-ahead of the stage waits for.
+    auto stage_first = [&](const int* prog, int ordinal, int rb, bool reader) {
+        wait_flag(prog, (ordinal << 16) + 3, &sh_err);
+        if (reader) {
+            const float* const hz = LY.hz + (size_t)rb * hzst;
+            const float* const hf = LY.hfr + (size_t)rb * hfst;
+#pragma unroll
+            for (int i = 0; i < 5; ++i) cp_async16(W.sv + 28 + 4 * i, hz + 28 + 4 * i, 16);
+#pragma unroll
+            for (int i = 0; i < 2; ++i) cp_async16(W.sf + 4 + 4 * i, hf + 4 + 4 * i, 16);
+        }
+    };
+    auto stage_next = [&](const int* prog, int ordinal, int k, int rb, bool reader) {
+        wait_flag(prog, (ordinal << 16) + min(k + 4, kStageMask), &sh_err);
+        if (reader) {
+            const float* const hz = LY.hz + (size_t)rb * hzst;
+            const float* const hf = LY.hfr + (size_t)rb * hfst;
+            const int s0 = kCW * k + 48, g0 = 4 * k + 12;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) cp_async16(W.sv + ((s0 + 4 * i) & (kHR - 1)), hz + s0 + 4 * i, 16);
+            cp_async16(W.sf + (g0 & (kHR / 4 - 1)), hf + g0, 16);
+        }
+    };
 
     // ============================== forward ==============================
     FwdVars V;
     V.acc = 0.0;
+    V.ab = 0.f;
     V.gsum = 0.f;
     V.E = 0.f;
     V.ebmin = V.ebmax = 0x3f800000;
@@ -573,14 +634,14 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
         const int nv = min(32, L1 - 32 * r);
         const int nst = (L2 + nv - 1 + kCW - 1) / kCW;
         const float* srow = S + (size_t)(32 * r) * L2m;
-        const bool hasB = r > 0, hasD = r + 1 < nRB;
+        const bool hasB = r > 0;
         float* const zblk = LY.zpl + (size_t)r * zst;
         FwdCtx C;
         C.ring = W.ringS + lane * kRW;
-        C.av = (hasB && lane == 0) ? Wp.hv[((r - 1) / kNW) & 1] : zv;
-        C.af = (hasB && lane == 0) ? Wp.hf[((r - 1) / kNW) & 1] : zf;
-        C.ov = W.hv[(r / kNW) & 1];
-        C.of = W.hf[(r / kNW) & 1];
+        C.av = (hasB && lane == 0) ? W.sv : zv;
+        C.af = (hasB && lane == 0) ? W.sf : zf;
+        C.ov = LY.hz + (size_t)r * hzst;
+        C.of = LY.hfr + (size_t)r * hfst;
         C.zrow = zblk + lane;
         C.erow = LY.efr + (size_t)r * est + lane;
         C.c = c;
@@ -593,24 +654,19 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
         C.l31 = lane == 31;
         const Tile tS = make_tile(srow, L2m, W.ringS, nv, lane);
 
-        // this ring parity was last written for row-block r - 2kNW: its reader
-        // (row-block r - 2kNW + 1) must be complete before it is reused
-        if (r >= 2 * kNW) wait_flag(&progF[wnext], ((r - 2 * kNW + 1) << 16) | kStageMask, &sh_err);
         __syncwarp();
         if (0 < nch) tile_load<4>(tS, 0, L2);
+        if (hasB) stage_first(&progF[wprev], r - 1, r - 1, lane == 0);
         cp_async_commit();
         V.zl = V.zd = V.zsh = 0.f;
         V.f.d1 = 0.f;  // lane 0 keeps zero neighbour factors; the others set theirs when they start
         for (int k = 0; k < nst; ++k) {
             __syncwarp();
+            if (hasB) stage_next(&progF[wprev], r - 1, k, r - 1, lane == 0);
+            cp_async_commit();
             if (k + 1 < nch) tile_load<4>(tS, k + 1, L2);
             cp_async_commit();
-            // this stage's look-aheads read the row above up to its stage k + 3;
-            // this stage overwrites ring steps that the row-block below read in
-            // its stage k - kBack or earlier
-            if (hasB) wait_flag(&progF[wprev], ((r - 1) << 16) + min(k + 4, kStageMask), &sh_err);
-            if (hasD && k >= kBack) wait_flag(&progF[wnext], ((r + 1) << 16) + (k - kBack + 1), &sh_err);
-            cp_async_wait1();
+            cp_async_wait2();  // everything but this stage's two groups
             __syncwarp();
             if (k == 0) {  // lane 0 starts in the frame of the row above; group 0's factors
                 if (lane == 0) V.E = C.af[7];
@@ -623,15 +679,23 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
                 fwd_stage_full<false>(C, V, k, 0);
             else
                 fwd_stage_full<true>(C, V, k, lane < nv ? L2 + lane - kCW * k : -1);
-            __syncwarp();  // every lane's reads of the row above's ring come before the release
+            acc_rebase(V.acc, V.ab, V.E);
+            __syncwarp();
             if (lane == 31) st_release(&progF[warp], (r << 16) | min(k + 1, kStageMask - 1));
         }
-        V.acc = fma((double)V.gsum, p2d(V.E), V.acc);  // the last group's partition
+        V.acc = fma((double)V.gsum, p2d(V.E - V.ab), V.acc);  // the last group's partition
+        V.emax = fmaxf(V.emax, V.E - V.ab);
         V.gsum = 0.f;
-        // lane 1 below, at its last column, converts lane 0's values with this
-        // lane's frame of group 4 nst (one past the last): the final frame
-        if (hasD && nst >= kBack) wait_flag(&progF[wnext], ((r + 1) << 16) + (nst - kBack + 1), &sh_err);
-        if (lane == 31) C.of[(4 * nst) & (kHR / 4 - 1)] = V.E;
+        // past the last stage the row below's look-aheads read up to 48 steps and
+        // 12 groups further: zeros, in the final frame
+        if (lane == 31) {
+#pragma unroll 4
+            for (int i = 0; i < 12; ++i)
+                *reinterpret_cast<float4*>(C.ov + kCW * nst + 4 * i) = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int i = 0; i < 3; ++i)
+                *reinterpret_cast<float4*>(C.of + 4 * nst + 4 * i) = make_float4(V.E, V.E, V.E, V.E);
+        }
         cp_async_wait0();
         __syncwarp();
         if (lane == 31) st_release(&progF[warp], (r << 16) | kStageMask);
@@ -639,11 +703,14 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
 
     // ---- S = log2(1 + sum of every lane's partition), kept as integer + fraction
     {
-        const double tot = block_sum_d(V.acc, reinterpret_cast<double*>(red)) + 1.0;  // alpha[0,0] = 0
+        // every lane's acc brought to the largest base; alpha[0,0] = 0 adds 2^-abmax
+        const float abmax = block_max(V.ab, red);
+        const double tot = block_sum_d(V.acc * p2d(V.ab - abmax), reinterpret_cast<double*>(red)) + p2d(-abmax);
         if (threadIdx.x == 0) {
             const int hi = __double2hiint(tot);
-            const int e = ((hi >> 20) & 0x7ff) - 1023;                        // tot = m 2^e, m in [1, 2)
-            const bool fin = e < 1000;
+            const int ef = (hi >> 20) & 0x7ff;
+            const int e = ef - 1023 + (int)abmax;                             // tot 2^abmax = m 2^e, m in [1, 2)
+            const bool fin = ef != 0x7ff && ef != 0;
             const double m = __hiloint2double((hi & 0x800fffff) | 0x3ff00000, __double2loint(tot));
             const float l2 = lg2_rr((float)m);
             sh_Sint = e;
@@ -653,9 +720,6 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
         }
         __syncthreads();  // also: every forward read of the handoff rings is done
     }
-    clear_rings();
-    __syncwarp();
-
     // ============================== reverse ==============================
     const int P = kCW * ((L2 - 1 + kCW - 1) / kCW);
     const int nstR = P / kCW + 2;  // lane 0 reaches column 0 at step P + 31
@@ -665,17 +729,17 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
         const int r = nRB - 1 - q;
         const int nv = min(32, L1 - 32 * r);
         const float* srow = S + (size_t)(32 * r) * L2m;
-        const bool hasBelow = r + 1 < nRB, hasAbove = r > 0;
+        const bool hasBelow = r + 1 < nRB;
         const float* const zblk = LY.zpl + (size_t)r * zst;
         const float* const eblk = LY.efr + (size_t)r * est;
         RevCtx C;
         C.ring = W.ringS + lane * kRW;
         C.zr = &W.zr[0][0];
         C.er = W.er;
-        C.bv = (hasBelow && lane == nv - 1) ? Wp.hv[((q - 1) / kNW) & 1] : zv;
-        C.bf = (hasBelow && lane == nv - 1) ? Wp.hf[((q - 1) / kNW) & 1] : zf;
-        C.ov = W.hv[(q / kNW) & 1];
-        C.of = W.hf[(q / kNW) & 1];
+        C.bv = (hasBelow && lane == nv - 1) ? W.sv : zv;
+        C.bf = (hasBelow && lane == nv - 1) ? W.sf : zf;
+        C.ov = LY.hz + (size_t)r * hzst;
+        C.of = LY.hfr + (size_t)r * hfst;
         C.c = c;
         C.G = G;
         C.cS = ex2f(-sh_Sfrac);
@@ -707,7 +771,6 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
             }
         };
 
-        if (q >= 2 * kNW) wait_flag(&progR[wnext], ((q - 2 * kNW + 1) << 16) | kStageMask, &sh_err);
         __syncwarp();
         {   // stage 0 reads score chunks M0-2 .. M0 (M0 = P/16 + 1)
             const int M0 = P / kCW + 1;
@@ -715,6 +778,7 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
                 if (ch >= 0 && ch < nch) tile_load<4>(tS, ch, L2);
         }
         batch(0);
+        if (hasBelow) stage_first(&progR[wprev], q - 1, r + 1, lane == nv - 1);
         cp_async_commit();
 
         RV.br = RV.pbp = RV.rsh = 0.f;
@@ -724,16 +788,13 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
         for (int k = 0; k < nstR; ++k) {
             const int M = P / kCW + 1 - k;
             __syncwarp();
+            if (hasBelow) stage_next(&progR[wprev], q - 1, k, r + 1, lane == nv - 1);
+            cp_async_commit();
             if (out && M + 1 < nch && M + 1 >= 0) tile_store(tM, M + 1, L2);  // no lane touches it any more
             if (M - 3 >= 0 && M - 3 < nch) tile_load<4>(tS, M - 3, L2);       // for stage k + 1
             if (k + 1 < nstR) batch(k + 1);
             cp_async_commit();
-            // this stage's look-aheads read the row-block below up to its stage
-            // k + 3; this stage overwrites ring steps the row above read in its
-            // stage k - kBack or earlier
-            if (hasBelow) wait_flag(&progR[wprev], ((q - 1) << 16) + min(k + 4, kStageMask), &sh_err);
-            if (hasAbove && k >= kBack) wait_flag(&progR[wnext], ((q + 1) << 16) + (k - kBack + 1), &sh_err);
-            cp_async_wait1();
+            cp_async_wait2();  // everything but this stage's two groups
             __syncwarp();
             if (k == 0) rev_lookahead(C, RV, 0);
             // full: every lane started before the stage (lane 0 starts at step
@@ -745,13 +806,19 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
                 rev_stage_full<false>(C, RV, k, 0);
             else
                 rev_stage_full<true>(C, RV, k, lane < nv ? 16 * M + 16 - lane : -1);
-            __syncwarp();  // every lane's reads of the row-block below's ring come before the release
+            __syncwarp();
             if (lane == 0) st_release(&progR[warp], (q << 16) | min(k + 1, kStageMask - 1));
         }
-        // the row above's bottom lane (and its neighbour), at column 0, read this
-        // lane's frame of group 4 nstR (one past the last): the final frame
-        if (hasAbove && nstR >= kBack) wait_flag(&progR[wnext], ((q + 1) << 16) + (nstR - kBack + 1), &sh_err);
-        if (lane == 0) C.of[(4 * nstR) & (kHR / 4 - 1)] = RV.Q;
+        // past the last stage the row above's look-aheads read up to 48 steps and
+        // 12 groups further: zeros, in the final frame
+        if (lane == 0) {
+#pragma unroll 4
+            for (int i = 0; i < 12; ++i)
+                *reinterpret_cast<float4*>(C.ov + kCW * nstR + 4 * i) = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int i = 0; i < 3; ++i)
+                *reinterpret_cast<float4*>(C.of + 4 * nstR + 4 * i) = make_float4(RV.Q, RV.Q, RV.Q, RV.Q);
+        }
         __syncwarp();
         if (out && nch > 0) tile_store(tM, 0, L2);  // the last stage had M = 0
         cp_async_wait0();
@@ -763,8 +830,12 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
     // dependency wait that gave up: the caller recomputes this problem with
     // the log-domain kernel
     const bool outside = min(V.ebmin, RV.ebmin) < ((127 - kJMax) << 23) ||
-                         max(V.ebmax, RV.ebmax) > ((127 + kJMax) << 23) || V.emax > 1000.f;
-    const int redo = __syncthreads_or(outside ? 1 : 0) || sh_err || sh_bad;
+                         max(V.ebmax, RV.ebmax) > ((127 + kJMax) << 23);
+    const int o_win = __syncthreads_or(outside ? 1 : 0);
+    const int o_acc = __syncthreads_or(V.emax > 1000.f ? 1 : 0);
+    // nonzero = recompute; the bits say why (1 frame step, 2 wait gave up,
+    // 4 partition not finite, 8 partition base)
+    const int redo = (o_win ? 1 : 0) | (sh_err ? 2 : 0) | (sh_bad ? 4 : 0) | (o_acc ? 8 : 0);
     if (threadIdx.x == 0 && p.redo) p.redo[b] = redo;
 }
 

@@ -430,6 +430,7 @@ __global__ void __launch_bounds__(kPlaneThreads) aff_plane_kernel(SwArgs p) {
     __shared__ float sh_Sint, sh_Sfrac, sh_dS;
 
     const int b = blockIdx.x;
+    if (p.only && p.only[b] == 0) return;  // fix-up launch: only problems a fast path flagged
     const int L1m = p.L1, L2m = p.L2;
     const int L1 = p.lengths ? min(max(p.lengths[2 * b], 0), L1m) : L1m;
     const int L2 = p.lengths ? min(max(p.lengths[2 * b + 1], 0), L2m) : L2m;

@@ -35,8 +35,11 @@ __device__ __forceinline__ void prefetch_l2(const void* gmem) {
     asm volatile("prefetch.global.L2 [%0];\n" ::"l"(gmem));
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
-__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;\n" ::); }
-__device__ __forceinline__ void cp_async_wait0() { asm volatile("cp.async.wait_group 0;\n" ::); }
+// The waits are compiler memory barriers as well: shared-memory reads of the
+// copied data must not be moved above them.
+__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;\n" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait2() { asm volatile("cp.async.wait_group 2;\n" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait0() { asm volatile("cp.async.wait_group 0;\n" ::: "memory"); }
 
 // ---------------------------------------------------------------- progress flags
 __device__ __forceinline__ int ld_acquire(const int* p) {
@@ -79,6 +82,28 @@ __device__ __forceinline__ void sts_group_pred(float* v4, float* f, float4 v, fl
         " @q st.shared.v4.f32 [%0], {%2, %3, %4, %5};\n"
         " @q st.shared.f32 [%1], %7;\n}\n" ::"r"(a),
         "r"(b), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"((int)pr), "f"(fr));
+}
+
+// The same handoff into global memory (the neighbouring row-block stages it
+// with cp.async one stage ahead)
+__device__ __forceinline__ void stg_group_pred(float* v4, float* f, float4 v, float fr, bool pr) {
+    asm volatile(
+        "{\n .reg .pred q;\n setp.ne.b32 q, %6, 0;\n"
+        " @q st.global.v4.f32 [%0], {%2, %3, %4, %5};\n"
+        " @q st.global.f32 [%1], %7;\n}\n" ::"l"(v4),
+        "l"(f), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"((int)pr), "f"(fr)
+        : "memory");
+}
+// two values per step and one frame (the affine kernel's handoff)
+__device__ __forceinline__ void stg_pair_pred(float* a4, float* b4, float* f, float4 a, float4 b, float fr, bool pr) {
+    asm volatile(
+        "{\n .reg .pred q;\n setp.ne.b32 q, %11, 0;\n"
+        " @q st.global.v4.f32 [%0], {%3, %4, %5, %6};\n"
+        " @q st.global.v4.f32 [%1], {%7, %8, %9, %10};\n"
+        " @q st.global.f32 [%2], %12;\n}\n" ::"l"(a4),
+        "l"(b4), "l"(f), "f"(a.x), "f"(a.y), "f"(a.z), "f"(a.w), "f"(b.x), "f"(b.y), "f"(b.z), "f"(b.w),
+        "r"((int)pr), "f"(fr)
+        : "memory");
 }
 
 // log2 of a positive normal float, with the exponent split off exactly so that

@@ -392,21 +392,27 @@ struct AffFwd {
     Tensor value, marginals, dparams;  // dparams [3,B]: dS/dgap_open, dS/dgap_ext, dS/dT
 };
 
+// want_params: also compute the three parameter gradients (soft_sw_affine_with_grads,
+// or parameters that require grad); without them the linear-domain fast path can run.
 AffFwd aff_forward(const Tensor& scores, const Param& go, const Param& ge, const Param& T,
-                   const Tensor& lengths, const Shape& s) {
+                   const Tensor& lengths, const Shape& s, bool want_params) {
     auto opt = scores.options().dtype(torch::kFloat32);
     AffFwd r;
     r.value = torch::empty({s.B}, opt);
     r.marginals = torch::empty({s.B, s.L1, s.L2}, opt);
-    r.dparams = torch::empty({3, s.B}, opt);
+    float* dp = nullptr;
+    if (want_params) {
+        r.dparams = torch::empty({3, s.B}, opt);
+        dp = r.dparams.data_ptr<float>();
+    }
     size_t wb = 0;
     Tensor ws = workspace(D2P_FAMILY_AFFINE, D2P_OP_FORWARD_BACKWARD, s, scores.device(), &wb);
     const int dt = scores.scalar_type() == torch::kBFloat16 ? D2P_DTYPE_BF16 : D2P_DTYPE_F32;
-    float* dp = r.dparams.data_ptr<float>();
     check_rc(d2p_sw_affine_forward_backward(scores.data_ptr(), dt, len_ptr(lengths), s.B, s.L1, s.L2,
                                             go.host, ge.host, T.host, go.dev, ge.dev, T.dev,
                                             r.value.data_ptr<float>(), r.marginals.data_ptr<float>(), dp,
-                                            dp + s.B, dp + 2 * s.B, ws.data_ptr(), wb, cur_stream()),
+                                            dp ? dp + s.B : nullptr, dp ? dp + 2 * s.B : nullptr, ws.data_ptr(),
+                                            wb, cur_stream()),
              "d2p_sw_affine_forward_backward");
     return r;
 }
@@ -464,7 +470,8 @@ class SoftSWAffineFunction : public torch::autograd::Function<SoftSWAffineFuncti
         Param pe = read_param(gap_ext, scores, "gap_ext");
         Param pT = read_param(temperature, scores, "temperature");
         if (lengths.defined()) validate_lengths(lengths, s, scores.device());
-        AffFwd r = aff_forward(scores, po, pe, pT, lengths, s);
+        const bool want = gap_open.requires_grad() || gap_ext.requires_grad() || temperature.requires_grad();
+        AffFwd r = aff_forward(scores, po, pe, pT, lengths, s, want);
         ctx->save_for_backward({scores, r.marginals, r.dparams, gap_open, gap_ext, temperature});
         ctx->saved_data["lengths"] = lengths.defined() ? c10::IValue(lengths) : c10::IValue();
         return {r.value, r.marginals};
@@ -487,14 +494,18 @@ class SoftSWAffineFunction : public torch::autograd::Function<SoftSWAffineFuncti
             Tensor g = gv.to(torch::kFloat32).contiguous();
             if (g.device() != scores.device()) g = g.to(scores.device());
             grad_scores = torch::empty({s.B, s.L1, s.L2}, opt);
-            Tensor gp = torch::empty({3}, opt);
+            const bool params = dparams.defined();
+            Tensor gp = params ? torch::empty({3}, opt) : Tensor();
             check_rc(d2p_sw_value_backward(g.data_ptr<float>(), marginals.data_ptr<float>(),
-                                           dparams.data_ptr<float>(), 3, s.B, s.L1, s.L2,
-                                           grad_scores.data_ptr<float>(), gp.data_ptr<float>(), cur_stream()),
+                                           params ? dparams.data_ptr<float>() : nullptr, params ? 3 : 0,
+                                           s.B, s.L1, s.L2, grad_scores.data_ptr<float>(),
+                                           params ? gp.data_ptr<float>() : nullptr, cur_stream()),
                      "d2p_sw_value_backward");
-            g_o = gp.narrow(0, 0, 1);
-            g_e = gp.narrow(0, 1, 1);
-            g_T = gp.narrow(0, 2, 1);
+            if (params) {
+                g_o = gp.narrow(0, 0, 1);
+                g_e = gp.narrow(0, 1, 1);
+                g_T = gp.narrow(0, 2, 1);
+            }
             have = true;
         }
         if (gm.defined() && gm.numel() > 0) {
@@ -541,7 +552,7 @@ std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor> soft_sw_affine_with_grads_cud
     po.host = (float)gap_open;
     pe.host = (float)gap_ext;
     pT.host = (float)temperature;
-    AffFwd r = aff_forward(scores, po, pe, pT, len, s);
+    AffFwd r = aff_forward(scores, po, pe, pT, len, s, true);
     return {r.value, r.marginals, r.dparams[0], r.dparams[1], r.dparams[2]};
 }
 

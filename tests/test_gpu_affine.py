@@ -114,3 +114,82 @@ def test_autograd_tensor_params(d2p, cuda_device):
     check("dopen", go.grad, np.array([r64["grad_open"].sum()]), rtol=1e-4, atol=1e-5)
     check("dext", ge.grad, np.array([r64["grad_ext"].sum()]), rtol=1e-4, atol=1e-5)
     check("dT", T.grad, np.array([r64["grad_T"].sum()]), rtol=1e-4, atol=1e-5)
+
+
+# Shapes for the linear-domain fast path (value + marginals, L2 % 4 == 0):
+# single and multiple row-blocks, a partial last row-block, rows shorter than a
+# stage, ragged lengths.
+FASTAFF = [  # (B, L1, L2, T, gap_open, gap_ext, ragged)
+    (2, 1, 4, 1.0, -2.0, -0.5, False), (3, 31, 16, 1.0, -2.0, -0.5, False), (2, 32, 20, 0.5, -2.0, -0.5, False),
+    (2, 33, 64, 1.0, -2.0, -0.5, False), (4, 64, 100, 2.0, -1.7, -0.4, False), (2, 130, 260, 1.0, -2.0, -0.5, False),
+    (1, 200, 8, 1.0, -2.0, -0.5, False), (2, 100, 120, 1.0, -2.0, -0.5, False), (1, 520, 48, 1.0, -2.0, -0.5, False),
+    (6, 70, 96, 1.0, -2.0, -0.5, True), (5, 130, 200, 0.5, -2.0, -0.5, True),
+]
+
+
+@pytest.mark.parametrize("B,L1,L2,T,go,ge,ragged", FASTAFF)
+def test_fast_value_marginals(d2p, cuda_device, B, L1, L2, T, go, ge, ragged):
+    """soft_sw_affine_float with parameters that need no gradient runs the
+    linear-domain kernel (the plane engine recomputes whatever it flags)."""
+    s = scores(B, L1, L2, seed=L1 * 11 + L2 + B)
+    ln = lengths_for(B, L1, L2, seed=L2) if ragged else None
+    if ln is not None:
+        ln[0] = torch.tensor([L1, L2], dtype=torch.int32)
+    v, m = torch.ops.d2p.soft_sw_affine_float(s.to(cuda_device), go, ge, T, None if ln is None else ln.to(cuda_device))
+    lnp = None if ln is None else ln.numpy()
+    r64 = oracle.sw_affine(s.numpy(), lnp, go, ge, T, "f64")
+    r32 = oracle.sw_affine(s.numpy(), lnp, go, ge, T, "f32")
+    check("value", v, r64["value"], r32["value"])
+    check("marginals", m, r64["marginals"], r32["marginals"])
+    if ln is not None:
+        mc = m.cpu()
+        for b, (l1, l2) in enumerate(ln.tolist()):
+            assert torch.count_nonzero(mc[b, l1:, :]) == 0
+            assert torch.count_nonzero(mc[b, :, l2:]) == 0
+
+
+@pytest.mark.parametrize("B,L1,L2", [(4, 256, 1024), (2, 1024, 1024), (3, 768, 700), (2, 70, 2000)])
+def test_fast_long_rows(d2p, cuda_device, B, L1, L2):
+    """Long rows, more row-blocks than warps and partitions beyond the double
+    range of a single accumulator (S > 1023 log2 units at 1024 x 1024): every
+    problem must come out of the linear-domain kernel itself (one it flags is
+    recomputed by the plane engine, whose result would be bitwise the one
+    computed with parameter gradients) and match the oracle."""
+    s = scores(B, L1, L2, seed=L1 + 5 * L2)
+    v, m = torch.ops.d2p.soft_sw_affine_float(s.to(cuda_device), -2.0, -0.5, 1.0, None)
+    v2, m2, _, _, _ = torch.ops.d2p.soft_sw_affine_with_grads(s.to(cuda_device), -2.0, -0.5, 1.0, None)
+    for b in range(B):
+        assert not torch.equal(m[b], m2[b]), f"problem {b} was recomputed by the plane engine"
+    idx = [0, B - 1]
+    r64 = oracle.sw_affine(s[idx].numpy(), None, -2.0, -0.5, 1.0, "f64")
+    r32 = oracle.sw_affine(s[idx].numpy(), None, -2.0, -0.5, 1.0, "f32")
+    check("value", v[idx], r64["value"], r32["value"])
+    check("marginals", m[idx], r64["marginals"], r32["marginals"])
+
+
+def test_fast_bf16_matches_widened_fp32(d2p, cuda_device):
+    """bf16 scores on the fast path give exactly the fp32 result of the
+    widened scores (the widening is exact)."""
+    s = scores(3, 96, 128, seed=77).to(torch.bfloat16)
+    v1, m1 = torch.ops.d2p.soft_sw_affine_float(s.to(cuda_device), -2.0, -0.5, 1.0, None)
+    v2, m2 = torch.ops.d2p.soft_sw_affine_float(s.float().to(cuda_device), -2.0, -0.5, 1.0, None)
+    assert torch.equal(v1, v2) and torch.equal(m1, m2)
+    r64 = oracle.sw_affine(s.float().numpy(), None, -2.0, -0.5, 1.0, "f64")
+    r32 = oracle.sw_affine(s.float().numpy(), None, -2.0, -0.5, 1.0, "f32")
+    check("marginals", m1, r64["marginals"], r32["marginals"])
+
+
+def test_fast_and_plane_agree_and_repeat(d2p, cuda_device):
+    """The fast path (no parameter gradients) and the plane engine (with them)
+    agree, and the fast path is bitwise repeatable with many row-blocks and
+    more problems than two per SM (ragged, so the CTA order is by cost)."""
+    B, L1, L2 = 320, 200, 64
+    s = scores(B, L1, L2, seed=5).to(cuda_device)
+    ln = lengths_for(B, L1, L2, seed=6).to(cuda_device)
+    v1, m1 = torch.ops.d2p.soft_sw_affine_float(s, -2.0, -0.5, 1.0, ln)
+    v2, m2, _, _, _ = torch.ops.d2p.soft_sw_affine_with_grads(s, -2.0, -0.5, 1.0, ln)
+    torch.testing.assert_close(v1, v2, rtol=1e-5, atol=1e-4)
+    torch.testing.assert_close(m1, m2, rtol=0, atol=5e-5)
+    for _ in range(3):
+        v3, m3 = torch.ops.d2p.soft_sw_affine_float(s, -2.0, -0.5, 1.0, ln)
+        assert torch.equal(v3, v1) and torch.equal(m3, m1)

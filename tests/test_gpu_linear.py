@@ -138,8 +138,8 @@ def test_repeatable_bitwise(d2p, cuda_device):
 @pytest.mark.parametrize("L1,L2", [(200, 8), (400, 16), (130, 260), (520, 48)])
 def test_fast_path_repeatable_across_launches(d2p, cuda_device, L1, L2):
     """Many row-blocks per problem and batches larger than the SM count: the
-    row-block handoffs between warps (progress words, shared-memory rings,
-    back-pressure) must give bitwise the same result on every launch, and the
+    row-block handoffs between warps (progress words, boundary rows staged
+    through shared memory) must give bitwise the same result on every launch, and the
     oracle's result on the first."""
     s = scores(300, L1, L2, seed=L1 + L2).to(cuda_device)
     v0, m0 = torch.ops.d2p.soft_sw_float(s, -1.0, 1.0, None)
@@ -169,6 +169,26 @@ def test_ragged_batch_in_several_waves(d2p, cuda_device):
     v2, m2, _, _ = torch.ops.d2p.soft_sw_with_grads(s.to(cuda_device), -1.0, 1.0, ln.to(cuda_device))
     torch.testing.assert_close(v, v2, rtol=1e-5, atol=1e-4)
     torch.testing.assert_close(m, m2, rtol=0, atol=5e-5)
+
+
+@pytest.mark.parametrize("B,L1,L2", [(4, 256, 1024), (2, 1024, 1024), (3, 768, 700), (2, 70, 2000)])
+def test_long_rows(d2p, cuda_device, B, L1, L2):
+    """Rows far longer than a warp's staging window and more row-blocks than
+    warps: every row-block hands its boundary values on through global memory
+    while its consumer may still be several row-blocks behind.  Each problem
+    must come out of the linear-domain kernel itself (a problem it flags is
+    recomputed by the log-domain kernel, whose result would be bitwise the
+    same as the one computed with parameter gradients) and match the oracle."""
+    s = scores(B, L1, L2, seed=L1 + 3 * L2)
+    v, m = torch.ops.d2p.soft_sw_float(s.to(cuda_device), -1.0, 1.0, None)
+    v2, m2, _, _ = torch.ops.d2p.soft_sw_with_grads(s.to(cuda_device), -1.0, 1.0, None)
+    for b in range(B):
+        assert not torch.equal(m[b], m2[b]), f"problem {b} was recomputed by the log-domain kernel"
+    idx = [0, B - 1]
+    r64 = oracle.sw_linear(s[idx].numpy(), None, -1.0, 1.0, "f64")
+    r32 = oracle.sw_linear(s[idx].numpy(), None, -1.0, 1.0, "f32")
+    check("value", v[idx], r64["value"], r32["value"])
+    check("marginals", m[idx], r64["marginals"], r32["marginals"])
 
 
 # Shapes routed to the register/shared-memory wavefront kernel (L2 % 4 == 0):
