@@ -718,6 +718,10 @@ __global__ void __launch_bounds__(kNW * 32, 2) aff_fast_kernel(SwArgs p) {
         __syncthreads();
     }
 
+    // the forward's range checks, folded into one word before the reverse
+    const int fwd_out = ((V.ebmin < ((127 - kJMax) << 23) || V.ebmax > ((127 + kJMax) << 23)) ? 1 : 0) |
+                        (V.emax > 1000.f ? 8 : 0);
+
     // ============================== reverse ==============================
     const int P = kCW * ((L2 - 1 + kCW - 1) / kCW);
     const int nstR = P / kCW + 2;
@@ -815,10 +819,9 @@ __global__ void __launch_bounds__(kNW * 32, 2) aff_fast_kernel(SwArgs p) {
         if (lane == 0) st_release(&progR[warp], (q << 16) | kStageMask);
     }
 
-    const bool outside = min(V.ebmin, RV.ebmin) < ((127 - kJMax) << 23) ||
-                         max(V.ebmax, RV.ebmax) > ((127 + kJMax) << 23);
+    const bool outside = (fwd_out & 1) || RV.ebmin < ((127 - kJMax) << 23) || RV.ebmax > ((127 + kJMax) << 23);
     const int o_win = __syncthreads_or(outside ? 1 : 0);
-    const int o_acc = __syncthreads_or(V.emax > 1000.f ? 1 : 0);
+    const int o_acc = __syncthreads_or(fwd_out & 8);
     // nonzero = recompute; the bits say why (1 frame step, 2 wait gave up,
     // 4 partition not finite, 8 partition base)
     const int redo = (o_win ? 1 : 0) | (sh_err ? 2 : 0) | (sh_bad ? 4 : 0) | (o_acc ? 8 : 0);

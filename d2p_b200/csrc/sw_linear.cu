@@ -47,6 +47,7 @@
 // anti-diagonal tf = P + 31 - tau (P = 16 ceil((L2-1)/16)); lane l is at
 // column tf - l.  Stage k (16 steps) covers tf in [16M, 16M + 15] with
 // M = P/16 + 1 - k for every row-block height.
+#include <stddef.h>
 #include <stdint.h>
 
 #include "sw_common.cuh"
@@ -71,8 +72,12 @@ struct WarpSmem {
     // reverse: the row-block below's lane 0 messages)
     float sv[kHR];
     float sf[kHR / 4];
+    // which neighbour stage each of the 8 stage slots of sv / sf holds when
+    // the neighbour pushed it there itself: (ordinal << 16) | stage
+    int tag[kHR / 16];
 };
 static_assert(sizeof(WarpSmem) % 16 == 0, "per-warp shared blocks must stay 16-byte aligned");
+static_assert(offsetof(WarpSmem, sf) == offsetof(WarpSmem, sv) + 4 * kHR, "sf follows sv");
 
 struct Layout {  // per-problem workspace
     float* zpl;      // [nRB][ZT][32]   w = P (Z_diag + 1) of forward step t, frame E, at row t
@@ -137,6 +142,17 @@ __device__ __forceinline__ double p2d(float E) {
 // J of an exponent field (eb = bits of 2^J) as a float: exact
 __device__ __forceinline__ float efield_j(int eb) { return fmaf((float)eb, 1.0f / 8388608.0f, -127.f); }
 
+// One group of the boundary lane's (bnd) values and its frame: into the
+// staging ring of the consumer row-block's warp while it keeps up (push, pp),
+// else to the row-block's boundary row in global memory, from where the
+// consumer copies it.
+template <class Ctx>
+__device__ __forceinline__ void handoff(const Ctx& C, int g, float4 v, float fr, bool bnd, bool pp) {
+    stg_group_pred(C.ov + 4 * g, C.of + g, v, fr, bnd && !pp);
+    const unsigned sv = C.pv + 16u * (unsigned)(g & (kHR / 4 - 1));  // sf follows sv: 4 kHR bytes on
+    sts_group_pred_s(sv, C.pv + 4u * kHR + 4u * (unsigned)(g & (kHR / 4 - 1)), v, fr, pp);
+}
+
 // ==========================================================================
 // forward sweep of one row-block
 // ==========================================================================
@@ -148,6 +164,7 @@ struct FwdF {           // one group of 4 forward steps, for frame E
 };
 
 struct FwdVars {
+    bool push;          // lane 31, this stage: its values go to the consumer's staging ring
     float zl, zd, zsh;  // own z of the previous step; diagonal input of this step; lane l-1's last z
     float E;            // own frame
     float Esent;        // edge stages: lane l-1's frame of the value in zsh
@@ -169,6 +186,7 @@ struct FwdCtx {
     const float* af;    //   and its frames, by its group.  Other lanes (and r = 0): zeros
     float* ov;          // this row-block's boundary row (global), by step, and its frames by group
     float* of;
+    unsigned pv;        // shared address of the staging ring of the warp computing the row-block below
     float* zrow;        // zpl row 0 (forward step 0) of this row-block, this lane
     float* erow;        // efr group 0 of this row-block, this lane
     float c, G;
@@ -285,9 +303,8 @@ __device__ __forceinline__ void fwd_stage_full(const FwdCtx& C, FwdVars& V, int 
         pz[(size_t)u * 32] = w;
         zq[i] = z;
         if (i == 3) {
-            const int g = 4 * k + (u >> 2);
             pe[(u >> 2) * 32] = V.E;
-            stg_group_pred(C.ov + 4 * g, C.of + g, make_float4(zq[0], zq[1], zq[2], zq[3]), V.E, C.l31);
+            handoff(C, 4 * k + (u >> 2), make_float4(zq[0], zq[1], zq[2], zq[3]), V.E, C.l31, V.push);
         }
         V.zd = zuin;
         V.zl = z;
@@ -326,7 +343,7 @@ __device__ __forceinline__ void fwd_stage_start(const FwdCtx& C, FwdVars& V, int
             if (i == 3) {
                 const int g = t >> 2;
                 C.erow[(size_t)g * 32] = V.E;
-                stg_group_pred(C.ov + 4 * g, C.of + g, make_float4(zq[0], zq[1], zq[2], zq[3]), V.E, C.l31);
+                handoff(C, 4 * k + q, make_float4(zq[0], zq[1], zq[2], zq[3]), V.E, C.l31, V.push);
             }
             V.zd = act ? zuin : 0.f;
             V.zl = z;
@@ -347,6 +364,7 @@ struct RevF {           // one group of 4 reverse steps, for frame Q
 };
 
 struct RevVars {
+    bool push;          // lane 0, this stage: its messages go to the consumer's staging ring
     float br, pbp, rsh; // own b and P*b of column j+1; message from lane l+1
     float Q;            // own frame
     float Qsent;        // edge stages: lane l+1's frame of the message in rsh
@@ -365,6 +383,7 @@ struct RevCtx {
     const float* bf;      //   of kHR) and its frames, by its group.  Other lanes (and the last row-block): zeros
     float* ov;            // this row-block's boundary row (global) for the row-block above
     float* of;
+    unsigned pv;          // shared address of the staging ring of the warp computing the row-block above
     float c, G, cS;       // cS = 2^-Sfrac
     float notBot;         // lane != nv-1 as 1 / 0
     float Sint;
@@ -474,8 +493,7 @@ __device__ __forceinline__ void rev_stage_full(const RevCtx& C, RevVars& V, int 
         const float msg = act ? o.msg : 0.f;
         mq[i] = msg;
         if (i == 3) {
-            const int h = 4 * k + (u >> 2);
-            stg_group_pred(C.ov + 4 * h, C.of + h, make_float4(mq[0], mq[1], mq[2], mq[3]), V.Q, C.l0);
+            handoff(C, 4 * k + (u >> 2), make_float4(mq[0], mq[1], mq[2], mq[3]), V.Q, C.l0, V.push);
         }
         V.rsh = __shfl_down_sync(kAll, msg, 1);
         V.br = act ? o.b : 0.f;
@@ -515,8 +533,7 @@ __device__ __forceinline__ void rev_stage_part(const RevCtx& C, RevVars& V, int 
             const float msg = act ? o.msg : 0.f;
             mq[i] = msg;
             if (i == 3) {
-                const int h = 4 * k + q;
-                stg_group_pred(C.ov + 4 * h, C.of + h, make_float4(mq[0], mq[1], mq[2], mq[3]), V.Q, C.l0);
+                handoff(C, 4 * k + q, make_float4(mq[0], mq[1], mq[2], mq[3]), V.Q, C.l0, V.push);
             }
             V.rsh = __shfl_down_sync(kAll, msg, 1);
             V.br = act ? o.b : 0.f;
@@ -581,45 +598,56 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
     }
     if (threadIdx.x < kHR) zv[threadIdx.x] = 0.f;
     if (threadIdx.x < kHR / 4) zf[threadIdx.x] = 0.f;
+    if (lane < kHR / 16) W.tag[lane] = -1;
     if (threadIdx.x == 0) {
         sh_err = 0;
         sh_bad = 0;
     }
     __syncthreads();
-    // the warp that computes the neighbouring row-block this warp's inputs come
-    // from (row-block r-1 forward, r+1 reverse): round-robin assignment
-    const int wprev = (warp + kNW - 1) % kNW;
+    // the warps that compute the neighbouring row-blocks (round-robin
+    // assignment): wprev produces this warp's inputs (row-block r-1 forward,
+    // r+1 reverse), wnext consumes its outputs
+    const int wprev = (warp + kNW - 1) % kNW, wnext = (warp + 1) % kNW;
+    WarpSmem& Wn = reinterpret_cast<WarpSmem*>(smem_raw)[wnext];
     const size_t hzst = (size_t)hz_stride(L2m), hfst = (size_t)hf_stride(L2m);
 
     // Boundary values of the neighbouring row-block (boundary row hz, frames hf),
-    // staged by the one lane that reads them.  Look-ahead q of stage k reads the
-    // neighbour's steps 16k+4q+35 .. 16k+4q+39 and groups 4k+q+8, 4k+q+9: look-
-    // aheads 0..2 need its stages up to k+2, the last one its stage k+3.  The
-    // prologue copies its stages 0..2 (from step 28 and group 4 on); stage k,
-    // once the neighbour has finished its stage k+3, copies that stage (steps
-    // 16k+48 .. 16k+63, groups 4k+12 .. 4k+15) as a copy group of its own, which
-    // the last look-ahead of the stage waits for.
+    // staged into this warp's ring by the one lane that reads them.  Look-ahead
+    // q of stage k reads the neighbour's steps 16k+4q+35 .. 16k+4q+39 and groups
+    // 4k+q+8, 4k+q+9: look-aheads 0..2 need its stages up to k+2, the last one
+    // its stage k+3.  The prologue copies its stages 0..2 (from step 28 and
+    // group 4 on).  Stage k then needs the neighbour's stage k+3: unless it is
+    // staged already, the stage waits for it and copies it as a copy group of its
+    // own, which the stage's last look-ahead waits for.  A neighbour stage that
+    // the neighbour pushed into the ring itself (tag) is not copied.
+    auto copy_stage = [&](int ordinal, int x, int rb) {  // the reading lane only
+        if (W.tag[x & (kHR / 16 - 1)] == ((ordinal << 16) | x)) return;  // pushed
+        const float* const hz = LY.hz + (size_t)rb * hzst;
+        const float* const hf = LY.hfr + (size_t)rb * hfst;
+        const int s0 = kCW * x, g0 = 4 * x;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) cp_async16(W.sv + ((s0 + 4 * i) & (kHR - 1)), hz + s0 + 4 * i, 16);
+        cp_async16(W.sf + (g0 & (kHR / 4 - 1)), hf + g0, 16);
+    };
     auto stage_first = [&](const int* prog, int ordinal, int rb, bool reader) {
         wait_flag(prog, (ordinal << 16) + 3, &sh_err);
         if (reader) {
             const float* const hz = LY.hz + (size_t)rb * hzst;
             const float* const hf = LY.hfr + (size_t)rb * hfst;
+            if (W.tag[1] != ((ordinal << 16) | 1)) {  // stage 1: steps 28..31, groups 4..7
+                cp_async16(W.sv + 28, hz + 28, 16);
+                cp_async16(W.sf + 4, hf + 4, 16);
+            }
+            if (W.tag[2] != ((ordinal << 16) | 2)) {  // stage 2: steps 32..47, groups 8..11
 #pragma unroll
-            for (int i = 0; i < 5; ++i) cp_async16(W.sv + 28 + 4 * i, hz + 28 + 4 * i, 16);
-#pragma unroll
-            for (int i = 0; i < 2; ++i) cp_async16(W.sf + 4 + 4 * i, hf + 4 + 4 * i, 16);
+                for (int i = 0; i < 4; ++i) cp_async16(W.sv + 32 + 4 * i, hz + 32 + 4 * i, 16);
+                cp_async16(W.sf + 8, hf + 8, 16);
+            }
         }
     };
-    auto stage_next = [&](const int* prog, int ordinal, int k, int rb, bool reader) {
+    auto stage_need = [&](const int* prog, int ordinal, int k, int rb, bool reader) {
         wait_flag(prog, (ordinal << 16) + min(k + 4, kStageMask), &sh_err);
-        if (reader) {
-            const float* const hz = LY.hz + (size_t)rb * hzst;
-            const float* const hf = LY.hfr + (size_t)rb * hfst;
-            const int s0 = kCW * k + 48, g0 = 4 * k + 12;
-#pragma unroll
-            for (int i = 0; i < 4; ++i) cp_async16(W.sv + ((s0 + 4 * i) & (kHR - 1)), hz + s0 + 4 * i, 16);
-            cp_async16(W.sf + (g0 & (kHR / 4 - 1)), hf + g0, 16);
-        }
+        if (reader) copy_stage(ordinal, k + 3, rb);
     };
 
     // ============================== forward ==============================
@@ -642,6 +670,7 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
         C.af = (hasB && lane == 0) ? W.sf : zf;
         C.ov = LY.hz + (size_t)r * hzst;
         C.of = LY.hfr + (size_t)r * hfst;
+        C.pv = (unsigned)__cvta_generic_to_shared(Wn.sv);
         C.zrow = zblk + lane;
         C.erow = LY.efr + (size_t)r * est + lane;
         C.c = c;
@@ -654,7 +683,9 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
         C.l31 = lane == 31;
         const Tile tS = make_tile(srow, L2m, W.ringS, nv, lane);
 
+        const bool hasD = r + 1 < nRB;
         __syncwarp();
+        if (lane == 31) st_release(&progF[warp], r << 16);  // started: the row above may push to this warp
         if (0 < nch) tile_load<4>(tS, 0, L2);
         if (hasB) stage_first(&progF[wprev], r - 1, r - 1, lane == 0);
         cp_async_commit();
@@ -662,12 +693,21 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
         V.f.d1 = 0.f;  // lane 0 keeps zero neighbour factors; the others set theirs when they start
         for (int k = 0; k < nst; ++k) {
             __syncwarp();
-            if (hasB) stage_next(&progF[wprev], r - 1, k, r - 1, lane == 0);
+            if (hasB) stage_need(&progF[wprev], r - 1, k, r - 1, lane == 0);
             cp_async_commit();
             if (k + 1 < nch) tile_load<4>(tS, k + 1, L2);
             cp_async_commit();
             cp_async_wait2();  // everything but this stage's two groups
             __syncwarp();
+            // Push this stage while the row-block below is on its warp and has done
+            // at least k - 8 stages: the stage slot then holds a stage it has read
+            // (stage c reads stages c+2, c+3), and the slots its prologue copies
+            // into (stages 1, 2) are written only with the same stages.
+            V.push = false;
+            if (lane == 31 && hasD) {
+                const int cw = ld_acquire(&progF[wnext]);
+                V.push = (cw >> 16) == r + 1 && (cw & kStageMask) + 8 >= k;
+            }
             if (k == 0) {  // lane 0 starts in the frame of the row above; group 0's factors
                 if (lane == 0) V.E = C.af[7];
                 V.Esent = __shfl_up_sync(kAll, V.E, 1);
@@ -680,6 +720,7 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
             else
                 fwd_stage_full<true>(C, V, k, lane < nv ? L2 + lane - kCW * k : -1);
             acc_rebase(V.acc, V.ab, V.E);
+            if (V.push) Wn.tag[k & (kHR / 16 - 1)] = (r << 16) | k;
             __syncwarp();
             if (lane == 31) st_release(&progF[warp], (r << 16) | min(k + 1, kStageMask - 1));
         }
@@ -701,6 +742,7 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
         if (lane == 31) st_release(&progF[warp], (r << 16) | kStageMask);
     }
 
+    if (lane < kHR / 16) W.tag[lane] = -1;  // forward pushes are no reverse pushes
     // ---- S = log2(1 + sum of every lane's partition), kept as integer + fraction
     {
         // every lane's acc brought to the largest base; alpha[0,0] = 0 adds 2^-abmax
@@ -720,6 +762,10 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
         }
         __syncthreads();  // also: every forward read of the handoff rings is done
     }
+    // the forward's range checks, folded into one word before the reverse
+    const int fwd_out = ((V.ebmin < ((127 - kJMax) << 23) || V.ebmax > ((127 + kJMax) << 23)) ? 1 : 0) |
+                        (V.emax > 1000.f ? 8 : 0);
+
     // ============================== reverse ==============================
     const int P = kCW * ((L2 - 1 + kCW - 1) / kCW);
     const int nstR = P / kCW + 2;  // lane 0 reaches column 0 at step P + 31
@@ -729,7 +775,7 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
         const int r = nRB - 1 - q;
         const int nv = min(32, L1 - 32 * r);
         const float* srow = S + (size_t)(32 * r) * L2m;
-        const bool hasBelow = r + 1 < nRB;
+        const bool hasBelow = r + 1 < nRB, hasAbove = r > 0;
         const float* const zblk = LY.zpl + (size_t)r * zst;
         const float* const eblk = LY.efr + (size_t)r * est;
         RevCtx C;
@@ -740,6 +786,7 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
         C.bf = (hasBelow && lane == nv - 1) ? W.sf : zf;
         C.ov = LY.hz + (size_t)r * hzst;
         C.of = LY.hfr + (size_t)r * hfst;
+        C.pv = (unsigned)__cvta_generic_to_shared(Wn.sv);
         C.c = c;
         C.G = G;
         C.cS = ex2f(-sh_Sfrac);
@@ -772,6 +819,7 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
         };
 
         __syncwarp();
+        if (lane == 0) st_release(&progR[warp], q << 16);  // started: the row-block below may push to this warp
         {   // stage 0 reads score chunks M0-2 .. M0 (M0 = P/16 + 1)
             const int M0 = P / kCW + 1;
             for (int ch = M0; ch >= M0 - 2; --ch)
@@ -788,7 +836,7 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
         for (int k = 0; k < nstR; ++k) {
             const int M = P / kCW + 1 - k;
             __syncwarp();
-            if (hasBelow) stage_next(&progR[wprev], q - 1, k, r + 1, lane == nv - 1);
+            if (hasBelow) stage_need(&progR[wprev], q - 1, k, r + 1, lane == nv - 1);
             cp_async_commit();
             if (out && M + 1 < nch && M + 1 >= 0) tile_store(tM, M + 1, L2);  // no lane touches it any more
             if (M - 3 >= 0 && M - 3 < nch) tile_load<4>(tS, M - 3, L2);       // for stage k + 1
@@ -796,6 +844,11 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
             cp_async_commit();
             cp_async_wait2();  // everything but this stage's two groups
             __syncwarp();
+            RV.push = false;
+            if (lane == 0 && hasAbove) {
+                const int cw = ld_acquire(&progR[wnext]);
+                RV.push = (cw >> 16) == q + 1 && (cw & kStageMask) + 8 >= k;
+            }
             if (k == 0) rev_lookahead(C, RV, 0);
             // full: every lane started before the stage (lane 0 starts at step
             // P - L2 + 32, which must run the start logic); masked when a lane
@@ -806,6 +859,7 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
                 rev_stage_full<false>(C, RV, k, 0);
             else
                 rev_stage_full<true>(C, RV, k, lane < nv ? 16 * M + 16 - lane : -1);
+            if (RV.push) Wn.tag[k & (kHR / 16 - 1)] = (q << 16) | k;
             __syncwarp();
             if (lane == 0) st_release(&progR[warp], (q << 16) | min(k + 1, kStageMask - 1));
         }
@@ -829,10 +883,9 @@ __global__ void __launch_bounds__(kNW * 32, 2) lin_fast_kernel(SwArgs p) {
     // a frame step outside the window, a partition that overflowed, or a
     // dependency wait that gave up: the caller recomputes this problem with
     // the log-domain kernel
-    const bool outside = min(V.ebmin, RV.ebmin) < ((127 - kJMax) << 23) ||
-                         max(V.ebmax, RV.ebmax) > ((127 + kJMax) << 23);
+    const bool outside = (fwd_out & 1) || RV.ebmin < ((127 - kJMax) << 23) || RV.ebmax > ((127 + kJMax) << 23);
     const int o_win = __syncthreads_or(outside ? 1 : 0);
-    const int o_acc = __syncthreads_or(V.emax > 1000.f ? 1 : 0);
+    const int o_acc = __syncthreads_or(fwd_out & 8);
     // nonzero = recompute; the bits say why (1 frame step, 2 wait gave up,
     // 4 partition not finite, 8 partition base)
     const int redo = (o_win ? 1 : 0) | (sh_err ? 2 : 0) | (sh_bad ? 4 : 0) | (o_acc ? 8 : 0);

@@ -74,6 +74,14 @@ __device__ __forceinline__ void wait_flag(const int* flag, int need, int* err) {
 
 // One lane's group handoff into shared memory: four values and a frame word,
 // stored under a predicate (no branch) so the other lanes only pay one issue.
+__device__ __forceinline__ void sts_group_pred_s(unsigned a, unsigned b, float4 v, float fr, bool pr) {
+    asm volatile(
+        "{\n .reg .pred q;\n setp.ne.b32 q, %6, 0;\n"
+        " @q st.shared.v4.f32 [%0], {%2, %3, %4, %5};\n"
+        " @q st.shared.f32 [%1], %7;\n}\n" ::"r"(a),
+        "r"(b), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"((int)pr), "f"(fr)
+        : "memory");
+}
 __device__ __forceinline__ void sts_group_pred(float* v4, float* f, float4 v, float fr, bool pr) {
     const unsigned a = (unsigned)__cvta_generic_to_shared(v4);
     const unsigned b = (unsigned)__cvta_generic_to_shared(f);
