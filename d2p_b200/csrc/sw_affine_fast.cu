@@ -25,6 +25,7 @@
 // The forward stores M per cell (all the reverse needs of it): marginal =
 // BM M 2^(Q + E - S).  One frame per lane covers all three states.
 #include <cuda_bf16.h>
+#include <stddef.h>
 #include <stdint.h>
 
 #include "sw_common.cuh"
@@ -50,8 +51,14 @@ struct WarpSmem {
     float sa[kHR];
     float sb[kHR];
     float sf[kHR / 4];
+    // which neighbour stage each of the 8 stage slots holds when the
+    // neighbour pushed it there itself: (ordinal << 16) | stage
+    int tag[kHR / 16];
 };
 static_assert(sizeof(WarpSmem) % 16 == 0, "per-warp shared blocks must stay 16-byte aligned");
+static_assert(offsetof(WarpSmem, sb) == offsetof(WarpSmem, sa) + 4 * kHR &&
+                  offsetof(WarpSmem, sf) == offsetof(WarpSmem, sa) + 8 * kHR,
+              "sa, sb, sf are contiguous");
 
 struct Layout {  // per-problem workspace
     float* mpl;      // [nRB][ZT][32]   M of forward step t (frame E) at row t
@@ -98,9 +105,17 @@ __device__ __forceinline__ double p2d(float E) {
 }
 __device__ __forceinline__ float efield_j(int eb) { return fmaf((float)eb, 1.0f / 8388608.0f, -127.f); }
 
-// the boundary lane's two values of a group and its frame, to its row-block's boundary rows
-__device__ __forceinline__ void stg_pair_group(float* a4, float* b4, float* f, float4 a, float4 b, float fr, bool pr) {
-    stg_pair_pred(a4, b4, f, a, b, fr, pr);
+// One group of the boundary lane's (bnd) two values and its frame: into the
+// staging ring of the consumer row-block's warp while it keeps up (push, pp;
+// ring at shared address pv: sa, sb, sf), else to the row-block's boundary
+// rows in global memory, from where the consumer copies it (the linear
+// kernel's handoff, sw_linear.cu).
+template <class Ctx>
+__device__ __forceinline__ void handoff(const Ctx& C, int g, float4 a, float4 b, float fr, bool bnd, bool pp) {
+    stg_pair_pred(C.oa + 4 * g, C.ob + 4 * g, C.of + g, a, b, fr, bnd && !pp);
+    const unsigned sa = C.pv + 16u * (unsigned)(g & (kHR / 4 - 1));
+    sts_group_pred_s(sa, C.pv + 8u * kHR + 4u * (unsigned)(g & (kHR / 4 - 1)), a, fr, pp);
+    sts_group_pred_s(sa + 4u * kHR, C.pv + 8u * kHR + 4u * (unsigned)(g & (kHR / 4 - 1)), b, fr, pp);
 }
 
 // ==========================================================================
@@ -115,6 +130,7 @@ struct FwdF {
 };
 
 struct FwdVars {
+    bool push;          // lane 31, this stage: its values go to the consumer's staging ring
     float Mp, Dp, Td;   // own M, D of the previous step; diagonal T of this step (own frame)
     float ur, Tr;       // lane l-1's u and T of the previous step (its frame)
     float Tl;           // own T of the previous step (frame anchor)
@@ -134,9 +150,10 @@ struct FwdCtx {
     const float* au;    // lane 0: the row above's u, T staged by its step, frames by group; zeros otherwise
     const float* at;
     const float* af;
-    float* ou;          // this row-block's boundary rows (global) for the row-block below
-    float* ot;
+    float* oa;          // this row-block's boundary rows (global) for the row-block below: u, T
+    float* ob;
     float* of;
+    unsigned pv;        // shared address of the staging ring of the warp computing the row-block below
     float* mrow;        // mpl row 0 of this row-block, this lane
     float* erow;
     float c, Go, Ge;
@@ -257,8 +274,7 @@ __device__ __forceinline__ void fwd_stage_full(const FwdCtx& C, FwdVars& V, int 
         if (i == 3) {
             const int g = 4 * k + (u >> 2);
             pe[(u >> 2) * 32] = V.E;
-            stg_pair_group(C.ou + 4 * g, C.ot + 4 * g, C.of + g, make_float4(uq[0], uq[1], uq[2], uq[3]),
-                           make_float4(tq[0], tq[1], tq[2], tq[3]), V.E, C.l31);
+            handoff(C, g, make_float4(uq[0], uq[1], uq[2], uq[3]), make_float4(tq[0], tq[1], tq[2], tq[3]), V.E, C.l31, V.push);
         }
         V.Mp = o.M;
         V.Dp = o.D;
@@ -301,8 +317,7 @@ __device__ __forceinline__ void fwd_stage_start(const FwdCtx& C, FwdVars& V, int
             if (i == 3) {
                 const int g = t >> 2;
                 C.erow[(size_t)g * 32] = V.E;
-                stg_pair_group(C.ou + 4 * g, C.ot + 4 * g, C.of + g, make_float4(uq[0], uq[1], uq[2], uq[3]),
-                               make_float4(tq[0], tq[1], tq[2], tq[3]), V.E, C.l31);
+                handoff(C, g, make_float4(uq[0], uq[1], uq[2], uq[3]), make_float4(tq[0], tq[1], tq[2], tq[3]), V.E, C.l31, V.push);
             }
             V.Mp = o.M;
             V.Dp = o.D;
@@ -327,6 +342,7 @@ struct RevF {
 };
 
 struct RevVars {
+    bool push;          // lane 0, this stage: its messages go to the consumer's staging ring
     float BDp, PBp;     // own BD and P BM of column j+1
     float Yr, Xr;       // lane l+1's BI and X of the previous step (its frame)
     float BMl;          // own BM of the previous step (frame anchor)
@@ -344,9 +360,10 @@ struct RevCtx {
     const float* by;    // bottom lane: the row-block below's BI, X staged by its step (frames by
     const float* bx;    //   group); zeros otherwise
     const float* bf;
-    float* oy;          // this row-block's boundary rows (global) for the row-block above
-    float* ox;
+    float* oa;          // this row-block's boundary rows (global) for the row-block above: BI, X
+    float* ob;
     float* of;
+    unsigned pv;        // shared address of the staging ring of the warp computing the row-block above
     float c, Go, Ge, cS;
     float notBot;
     float Sint;
@@ -463,8 +480,7 @@ __device__ __forceinline__ void rev_stage_full(const RevCtx& C, RevVars& V, int 
         xq[i] = xs;
         if (i == 3) {
             const int h = 4 * k + (u >> 2);
-            stg_pair_group(C.oy + 4 * h, C.ox + 4 * h, C.of + h, make_float4(yq[0], yq[1], yq[2], yq[3]),
-                           make_float4(xq[0], xq[1], xq[2], xq[3]), V.Q, C.l0);
+            handoff(C, h, make_float4(yq[0], yq[1], yq[2], yq[3]), make_float4(xq[0], xq[1], xq[2], xq[3]), V.Q, C.l0, V.push);
         }
         V.Yr = __shfl_down_sync(kAll, o.BI, 1);
         V.Xr = __shfl_down_sync(kAll, xs, 1);
@@ -509,8 +525,7 @@ __device__ __forceinline__ void rev_stage_part(const RevCtx& C, RevVars& V, int 
             xq[i] = xs;
             if (i == 3) {
                 const int h = 4 * k + q;
-                stg_pair_group(C.oy + 4 * h, C.ox + 4 * h, C.of + h, make_float4(yq[0], yq[1], yq[2], yq[3]),
-                               make_float4(xq[0], xq[1], xq[2], xq[3]), V.Q, C.l0);
+                handoff(C, h, make_float4(yq[0], yq[1], yq[2], yq[3]), make_float4(xq[0], xq[1], xq[2], xq[3]), V.Q, C.l0, V.push);
             }
             V.Yr = __shfl_down_sync(kAll, o.BI, 1);
             V.Xr = __shfl_down_sync(kAll, xs, 1);
@@ -573,44 +588,45 @@ __global__ void __launch_bounds__(kNW * 32, 2) aff_fast_kernel(SwArgs p) {
     }
     if (threadIdx.x < kHR) zv[threadIdx.x] = 0.f;
     if (threadIdx.x < kHR / 4) zf[threadIdx.x] = 0.f;
+    if (lane < kHR / 16) W.tag[lane] = -1;
     if (threadIdx.x == 0) {
         sh_err = 0;
         sh_bad = 0;
     }
     __syncthreads();
-    const int wprev = (warp + kNW - 1) % kNW;  // the warp of the row-block this warp's inputs come from
+    // the warps of the neighbouring row-blocks: wprev produces this warp's
+    // inputs, wnext consumes its outputs
+    const int wprev = (warp + kNW - 1) % kNW, wnext = (warp + 1) % kNW;
+    WarpSmem& Wn = reinterpret_cast<WarpSmem*>(smem_raw)[wnext];
     const size_t hzst = (size_t)hz_stride(L2m), hfst = (size_t)hf_stride(L2m);
 
     // Boundary values of the neighbouring row-block, staged by the one lane
     // that reads them, on the linear kernel's schedule (sw_linear.cu): the
-    // prologue copies the neighbour's stages 0..2 (from step 28 and group 4 on);
-    // stage k, once the neighbour has finished its stage k+3, copies that stage
-    // as a copy group of its own, which the stage's last look-ahead waits for.
+    // prologue copies the neighbour's stages 1 and 2 (from step 28 and group 4
+    // on); stage k, once the neighbour has finished its stage k+3, copies that
+    // stage as a copy group of its own, which the stage's last look-ahead waits
+    // for.  Stages the neighbour pushed into the ring itself (tag) are not copied.
+    auto copy_stage = [&](int ordinal, int x, const float* ga, const float* gb, const float* gf) {
+        if (W.tag[x & (kHR / 16 - 1)] == ((ordinal << 16) | x)) return;  // pushed
+        const int s0 = x == 1 ? 28 : kCW * x, ns = x == 1 ? 1 : 4, g0 = 4 * x;
+        for (int i = 0; i < ns; ++i) {
+            cp_async16(W.sa + ((s0 + 4 * i) & (kHR - 1)), ga + s0 + 4 * i, 16);
+            cp_async16(W.sb + ((s0 + 4 * i) & (kHR - 1)), gb + s0 + 4 * i, 16);
+        }
+        cp_async16(W.sf + (g0 & (kHR / 4 - 1)), gf + g0, 16);
+    };
     auto stage_first = [&](const int* prog, int ordinal, const float* ga, const float* gb, const float* gf,
                            bool reader) {
         wait_flag(prog, (ordinal << 16) + 3, &sh_err);
         if (reader) {
-#pragma unroll
-            for (int i = 0; i < 5; ++i) {
-                cp_async16(W.sa + 28 + 4 * i, ga + 28 + 4 * i, 16);
-                cp_async16(W.sb + 28 + 4 * i, gb + 28 + 4 * i, 16);
-            }
-#pragma unroll
-            for (int i = 0; i < 2; ++i) cp_async16(W.sf + 4 + 4 * i, gf + 4 + 4 * i, 16);
+            copy_stage(ordinal, 1, ga, gb, gf);
+            copy_stage(ordinal, 2, ga, gb, gf);
         }
     };
     auto stage_next = [&](const int* prog, int ordinal, int k, const float* ga, const float* gb, const float* gf,
                           bool reader) {
         wait_flag(prog, (ordinal << 16) + min(k + 4, kStageMask), &sh_err);
-        if (reader) {
-            const int s0 = kCW * k + 48, g0 = 4 * k + 12;
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                cp_async16(W.sa + ((s0 + 4 * i) & (kHR - 1)), ga + s0 + 4 * i, 16);
-                cp_async16(W.sb + ((s0 + 4 * i) & (kHR - 1)), gb + s0 + 4 * i, 16);
-            }
-            cp_async16(W.sf + (g0 & (kHR / 4 - 1)), gf + g0, 16);
-        }
+        if (reader) copy_stage(ordinal, k + 3, ga, gb, gf);
     };
     // past its last stage a row-block's neighbour reads up to 48 steps and 12
     // groups further: zeros, in the final frame (one lane writes them)
@@ -643,9 +659,10 @@ __global__ void __launch_bounds__(kNW * 32, 2) aff_fast_kernel(SwArgs p) {
         C.au = fromAbove ? W.sa : zv;
         C.at = fromAbove ? W.sb : zv;
         C.af = fromAbove ? W.sf : zf;
-        C.ou = LY.hva + (size_t)r * hzst;
-        C.ot = LY.hvb + (size_t)r * hzst;
+        C.oa = LY.hva + (size_t)r * hzst;
+        C.ob = LY.hvb + (size_t)r * hzst;
         C.of = LY.hfr + (size_t)r * hfst;
+        C.pv = (unsigned)__cvta_generic_to_shared(Wn.sa);
         C.mrow = LY.mpl + (size_t)r * zst + lane;
         C.erow = LY.efr + (size_t)r * est + lane;
         C.c = c;
@@ -661,7 +678,9 @@ __global__ void __launch_bounds__(kNW * 32, 2) aff_fast_kernel(SwArgs p) {
 
         const size_t rA = (size_t)(r - 1);
         const float *const gaA = LY.hva + rA * hzst, *const gbA = LY.hvb + rA * hzst, *const gfA = LY.hfr + rA * hfst;
+        const bool hasD = r + 1 < nRB;
         __syncwarp();
+        if (lane == 31) st_release(&progF[warp], r << 16);  // started: the row above may push to this warp
         if (0 < nch) tile_load<4>(tS, 0, L2);
         if (hasB) stage_first(&progF[wprev], r - 1, gaA, gbA, gfA, lane == 0);
         cp_async_commit();
@@ -675,6 +694,13 @@ __global__ void __launch_bounds__(kNW * 32, 2) aff_fast_kernel(SwArgs p) {
             cp_async_commit();
             cp_async_wait2();  // everything but this stage's two groups
             __syncwarp();
+            // push while the row-block below is on its warp and has done at least
+            // k - 8 stages (the linear kernel's rule, sw_linear.cu)
+            V.push = false;
+            if (lane == 31 && hasD) {
+                const int cw = ld_acquire(&progF[wnext]);
+                V.push = (cw >> 16) == r + 1 && (cw & kStageMask) + 8 >= k;
+            }
             if (k == 0) {
                 if (lane == 0) V.E = C.af[7];
                 V.Esent = __shfl_up_sync(kAll, V.E, 1);
@@ -687,18 +713,20 @@ __global__ void __launch_bounds__(kNW * 32, 2) aff_fast_kernel(SwArgs p) {
             else
                 fwd_stage_full<true>(C, V, k, lane < nv ? L2 + lane - kCW * k : -1);
             acc_rebase(V.acc, V.ab, V.E);
+            if (V.push) Wn.tag[k & (kHR / 16 - 1)] = (r << 16) | k;
             __syncwarp();
             if (lane == 31) st_release(&progF[warp], (r << 16) | min(k + 1, kStageMask - 1));
         }
         V.acc = fma((double)V.gsum, p2d(V.E - V.ab), V.acc);
         V.emax = fmaxf(V.emax, V.E - V.ab);
         V.gsum = 0.f;
-        if (lane == 31) write_tail(C.ou, C.ot, C.of, nst, V.E);
+        if (lane == 31) write_tail(C.oa, C.ob, C.of, nst, V.E);
         cp_async_wait0();
         __syncwarp();
         if (lane == 31) st_release(&progF[warp], (r << 16) | kStageMask);
     }
 
+    if (lane < kHR / 16) W.tag[lane] = -1;  // forward pushes are no reverse pushes
     // ---- S = log2(1 + sum of every lane's partition), kept as integer + fraction
     {
         // every lane's acc brought to the largest base; M[0,0] = 0 adds 2^-abmax
@@ -731,7 +759,7 @@ __global__ void __launch_bounds__(kNW * 32, 2) aff_fast_kernel(SwArgs p) {
         const int r = nRB - 1 - q;
         const int nv = min(32, L1 - 32 * r);
         const float* srow = S + (size_t)(32 * r) * L2m;
-        const bool hasBelow = r + 1 < nRB;
+        const bool hasBelow = r + 1 < nRB, hasAbove = r > 0;
         const float* const mblk = LY.mpl + (size_t)r * zst;
         const float* const eblk = LY.efr + (size_t)r * est;
         RevCtx C;
@@ -742,9 +770,10 @@ __global__ void __launch_bounds__(kNW * 32, 2) aff_fast_kernel(SwArgs p) {
         C.by = fromBelow ? W.sa : zv;
         C.bx = fromBelow ? W.sb : zv;
         C.bf = fromBelow ? W.sf : zf;
-        C.oy = LY.hva + (size_t)r * hzst;
-        C.ox = LY.hvb + (size_t)r * hzst;
+        C.oa = LY.hva + (size_t)r * hzst;
+        C.ob = LY.hvb + (size_t)r * hzst;
         C.of = LY.hfr + (size_t)r * hfst;
+        C.pv = (unsigned)__cvta_generic_to_shared(Wn.sa);
         C.c = c;
         C.Go = Go;
         C.Ge = Ge;
@@ -777,6 +806,7 @@ __global__ void __launch_bounds__(kNW * 32, 2) aff_fast_kernel(SwArgs p) {
         const float *const gaB = LY.hva + rB * hzst, *const gbB = LY.hvb + rB * hzst, *const gfB = LY.hfr + rB * hfst;
 
         __syncwarp();
+        if (lane == 0) st_release(&progR[warp], q << 16);  // started: the row-block below may push to this warp
         {
             const int M0 = P / kCW + 1;
             for (int ch = M0; ch >= M0 - 2; --ch)
@@ -801,6 +831,11 @@ __global__ void __launch_bounds__(kNW * 32, 2) aff_fast_kernel(SwArgs p) {
             cp_async_commit();
             cp_async_wait2();
             __syncwarp();
+            RV.push = false;
+            if (lane == 0 && hasAbove) {
+                const int cw = ld_acquire(&progR[wnext]);
+                RV.push = (cw >> 16) == q + 1 && (cw & kStageMask) + 8 >= k;
+            }
             if (k == 0) rev_lookahead(C, RV, 0);
             if (kCW * k <= P + 32 - L2)
                 rev_stage_part(C, RV, k);
@@ -808,10 +843,11 @@ __global__ void __launch_bounds__(kNW * 32, 2) aff_fast_kernel(SwArgs p) {
                 rev_stage_full<false>(C, RV, k, 0);
             else
                 rev_stage_full<true>(C, RV, k, lane < nv ? 16 * M + 16 - lane : -1);
+            if (RV.push) Wn.tag[k & (kHR / 16 - 1)] = (q << 16) | k;
             __syncwarp();
             if (lane == 0) st_release(&progR[warp], (q << 16) | min(k + 1, kStageMask - 1));
         }
-        if (lane == 0) write_tail(C.oy, C.ox, C.of, nstR, RV.Q);
+        if (lane == 0) write_tail(C.oa, C.ob, C.of, nstR, RV.Q);
         __syncwarp();
         if (out && nch > 0) tile_store(tM, 0, L2);
         cp_async_wait0();

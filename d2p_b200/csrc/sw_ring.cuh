@@ -82,6 +82,13 @@ __device__ __forceinline__ void sts_group_pred_s(unsigned a, unsigned b, float4 
         "r"(b), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"((int)pr), "f"(fr)
         : "memory");
 }
+__device__ __forceinline__ void sts_v4_pred_s(unsigned a, float4 v, bool pr) {
+    asm volatile(
+        "{\n .reg .pred q;\n setp.ne.b32 q, %5, 0;\n"
+        " @q st.shared.v4.f32 [%0], {%1, %2, %3, %4};\n}\n" ::"r"(a),
+        "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"((int)pr)
+        : "memory");
+}
 __device__ __forceinline__ void sts_group_pred(float* v4, float* f, float4 v, float fr, bool pr) {
     const unsigned a = (unsigned)__cvta_generic_to_shared(v4);
     const unsigned b = (unsigned)__cvta_generic_to_shared(f);
