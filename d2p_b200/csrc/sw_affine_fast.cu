@@ -37,7 +37,8 @@ namespace aff {
 using namespace ring;
 
 constexpr int kMaxRB = 512;              // row-blocks per problem (L1 <= 16384)
-constexpr int kNW = 6;                   // warps per CTA
+constexpr int kNW = 6;                   // warps per CTA, two CTAs per SM
+constexpr int kNWWide = 12;              // warps per CTA when the batch leaves SMs idle (one CTA per SM)
 constexpr int kJMax = 60;                // largest frame step (log2) a problem may take
 constexpr int kHR = 128;                 // staging ring of a neighbour's boundary values (steps)
 
@@ -540,10 +541,11 @@ __device__ __forceinline__ void rev_stage_part(const RevCtx& C, RevVars& V, int 
 // ==========================================================================
 // kernel
 // ==========================================================================
-__global__ void __launch_bounds__(kNW * 32, 2) aff_fast_kernel(SwArgs p) {
+template <int NW, int MINB>
+__global__ void __launch_bounds__(NW * 32, MINB) aff_fast_kernel(SwArgs p) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     WarpSmem& W = reinterpret_cast<WarpSmem*>(smem_raw)[threadIdx.x >> 5];
-    __shared__ int progF[kNW], progR[kNW];
+    __shared__ int progF[NW], progR[NW];
     __shared__ __align__(16) float red[4 * 32];
     __shared__ int sh_Sint, sh_err, sh_bad;
     __shared__ float sh_Sfrac;
@@ -570,7 +572,7 @@ __global__ void __launch_bounds__(kNW * 32, 2) aff_fast_kernel(SwArgs p) {
     const size_t est = (size_t)gt_rows(L2m) * 32;
 
     if (out && (L1 < L1m || L2 < L2m)) {
-        for (int i = warp; i < L1m; i += kNW) {
+        for (int i = warp; i < L1m; i += NW) {
             float* row = out + (size_t)i * L2m;
             for (int j = (i < L1 ? L2 : 0) + lane; j < L2m; j += 32) row[j] = 0.f;
         }
@@ -582,7 +584,7 @@ __global__ void __launch_bounds__(kNW * 32, 2) aff_fast_kernel(SwArgs p) {
         }
         return;
     }
-    if (threadIdx.x < kNW) {
+    if (threadIdx.x < NW) {
         progF[threadIdx.x] = -1;
         progR[threadIdx.x] = -1;
     }
@@ -596,7 +598,7 @@ __global__ void __launch_bounds__(kNW * 32, 2) aff_fast_kernel(SwArgs p) {
     __syncthreads();
     // the warps of the neighbouring row-blocks: wprev produces this warp's
     // inputs, wnext consumes its outputs
-    const int wprev = (warp + kNW - 1) % kNW, wnext = (warp + 1) % kNW;
+    const int wprev = (warp + NW - 1) % NW, wnext = (warp + 1) % NW;
     WarpSmem& Wn = reinterpret_cast<WarpSmem*>(smem_raw)[wnext];
     const size_t hzst = (size_t)hz_stride(L2m), hfst = (size_t)hf_stride(L2m);
 
@@ -648,7 +650,7 @@ __global__ void __launch_bounds__(kNW * 32, 2) aff_fast_kernel(SwArgs p) {
     V.E = 0.f;
     V.ebmin = V.ebmax = 0x3f800000;
     V.emax = 0.f;
-    for (int r = warp; r < nRB; r += kNW) {
+    for (int r = warp; r < nRB; r += NW) {
         const int nv = min(32, L1 - 32 * r);
         const int nst = (L2 + nv - 1 + kCW - 1) / kCW;
         const float* srow = S + (size_t)(32 * r) * L2m;
@@ -755,7 +757,7 @@ __global__ void __launch_bounds__(kNW * 32, 2) aff_fast_kernel(SwArgs p) {
     const int nstR = P / kCW + 2;
     RevVars RV;
     RV.ebmin = RV.ebmax = 0x3f800000;
-    for (int q = warp; q < nRB; q += kNW) {
+    for (int q = warp; q < nRB; q += NW) {
         const int r = nRB - 1 - q;
         const int nv = min(32, L1 - 32 * r);
         const float* srow = S + (size_t)(32 * r) * L2m;
@@ -920,20 +922,36 @@ int launch_aff_fast(const SwArgs& a0, size_t ws_bytes, cudaStream_t st) {
     } else if (!a.scores || (((uintptr_t)a.scores) & 15) != 0) {
         return -1;
     }
-    const size_t smem = sizeof(aff::WarpSmem) * aff::kNW;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return (int)e;
+    static int sms[64] = {0};
     static bool attr_set[64] = {false};
     if (dev < 64 && !attr_set[dev]) {
-        e = cudaFuncSetAttribute(aff::aff_fast_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return (int)e;
-        e = cudaFuncSetAttribute(aff::aff_fast_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
-                                 (int)cudaSharedmemCarveoutMaxShared);
+        const size_t s6 = sizeof(aff::WarpSmem) * aff::kNW, s12 = sizeof(aff::WarpSmem) * aff::kNWWide;
+        e = cudaFuncSetAttribute(aff::aff_fast_kernel<aff::kNW, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)s6);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(aff::aff_fast_kernel<aff::kNW, 2>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                     (int)cudaSharedmemCarveoutMaxShared);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(aff::aff_fast_kernel<aff::kNWWide, 1>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s12);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(aff::aff_fast_kernel<aff::kNWWide, 1>,
+                                     cudaFuncAttributePreferredSharedMemoryCarveout,
+                                     (int)cudaSharedmemCarveoutMaxShared);
+        if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
         if (e != cudaSuccess) return (int)e;
         attr_set[dev] = true;
     }
-    aff::aff_fast_kernel<<<a.B, aff::kNW * 32, smem, st>>>(a);
+    // at most one problem per SM: 12 warps per problem when that pays (see launch_lin_fast)
+    if (dev < 64 && a.B <= sms[dev] && lin_wide_pays(a.L1, a.L2)) {
+        aff::aff_fast_kernel<aff::kNWWide, 1>
+            <<<a.B, aff::kNWWide * 32, sizeof(aff::WarpSmem) * aff::kNWWide, st>>>(a);
+    } else {
+        aff::aff_fast_kernel<aff::kNW, 2><<<a.B, aff::kNW * 32, sizeof(aff::WarpSmem) * aff::kNW, st>>>(a);
+    }
     return (int)cudaGetLastError();
 }
 

@@ -63,6 +63,9 @@ struct SwArgs {
 // linear-domain fast path (sw_linear.cu): value + marginals without parameter
 // gradients; returns -1 when the shape or arguments are not covered
 size_t lin_fast_workspace_bytes(int B, int L1, int L2);
+// whether a batch of at most one problem per SM runs the linear-domain
+// kernels with 12 warps per problem rather than 6 (shape L1 x L2)
+bool lin_wide_pays(int L1, int L2);
 int launch_lin_fast(const SwArgs& a, size_t ws_bytes, cudaStream_t st);
 // affine-gap linear-domain fast path (sw_affine_fast.cu): value + marginals
 // without parameter gradients, fp32 or bf16 scores (bf16 widened into the
