@@ -30,17 +30,17 @@
 
 #include "sw_common.cuh"
 #include "sw_internal.h"
+#include "sw_lindomain.cuh"
 #include "sw_ring.cuh"
 
 namespace d2pb {
 namespace aff {
 using namespace ring;
+using namespace ld;
 
 constexpr int kMaxRB = 512;              // row-blocks per problem (L1 <= 16384)
 constexpr int kNW = 6;                   // warps per CTA, two CTAs per SM
 constexpr int kNWWide = 12;              // warps per CTA when the batch leaves SMs idle (one CTA per SM)
-constexpr int kJMax = 60;                // largest frame step (log2) a problem may take
-constexpr int kHR = 128;                 // staging ring of a neighbour's boundary values (steps)
 
 struct WarpSmem {
     float ringS[32 * kRW];    // scores [rows][64]; reverse: marginals written in place
@@ -68,11 +68,6 @@ struct Layout {  // per-problem workspace
     float* hvb;      // [nRB][ZT]                                                    T / X
     float* hfr;      // [nRB][GT]       and their frames, by its group
 };
-__host__ __device__ inline int zt_rows(int L2m) { return L2m + 96; }
-__host__ __device__ inline int gt_rows(int L2m) { return (L2m + 96) / 4; }
-// boundary rows are stored and staged in 16-byte pieces: strides in whole float4s
-__host__ __device__ inline int hz_stride(int L2m) { return (zt_rows(L2m) + 3) & ~3; }
-__host__ __device__ inline int hf_stride(int L2m) { return (gt_rows(L2m) + 3) & ~3; }
 __host__ __device__ inline size_t per_problem_bytes(int L1m, int L2m) {
     const size_t nrb = (size_t)(L1m + 31) / 32;
     return align_up(nrb * zt_rows(L2m) * 32 * 4, 256) + align_up(nrb * gt_rows(L2m) * 32 * 4, 256) +
@@ -93,18 +88,6 @@ __device__ inline Layout carve(float* ws, int b, int L1m, int L2m) {
     L.hfr = (float*)base;
     return L;
 }
-
-// frame arithmetic: the same as the linear kernel's
-__device__ __forceinline__ float p2(float k) { return ex2f(k); }
-__device__ __forceinline__ int efield(float v) {
-    const int b = __float_as_int(v) & 0x7f800000;
-    return b ? b : 0x3f800000;
-}
-__device__ __forceinline__ float inv_p2(float w) { return __int_as_float(0x7f000000 - __float_as_int(w)); }
-__device__ __forceinline__ double p2d(float E) {
-    return __hiloint2double((min(max(__float2int_rn(E), -1022), 1023) + 1023) << 20, 0);
-}
-__device__ __forceinline__ float efield_j(int eb) { return fmaf((float)eb, 1.0f / 8388608.0f, -127.f); }
 
 // One group of the boundary lane's (bnd) two values and its frame: into the
 // staging ring of the consumer row-block's warp while it keeps up (push, pp;
@@ -216,14 +199,6 @@ __device__ __forceinline__ void fwd_apply(FwdVars& V) {
     V.Td *= V.nfJ;
     V.E = V.nE;
     V.f = V.nf;
-}
-
-// once per stage: the partition's base follows the frames (see sw_linear.cu)
-__device__ __forceinline__ void acc_rebase(double& acc, float& ab, float E) {
-    if (E - ab > 700.f) {
-        acc *= p2d(ab - E);
-        ab = E;
-    }
 }
 
 struct FwdOut {

@@ -45,6 +45,17 @@ static size_t plane_bytes(int family, int mode, int B, int L1, int L2) {
     return align256(((size_t)B * plane * np + (size_t)B * frame_stride(L1, L2)) * sizeof(float));
 }
 
+// the shared area of the tangent ops: the linear tangent kernel's workspace
+// (linear family, covered shapes) or the plane engine's, whichever is larger
+static size_t tan_area(int family, int op, int B, int L1, int L2) {
+    size_t pe = plane_bytes(family, op == D2P_OP_HVP ? MODE_HVP : MODE_PT, B, L1, L2);
+    if (family == D2P_FAMILY_LINEAR) {
+        const size_t tf = lin_tan_workspace_bytes(B, L1, L2);
+        pe = pe > tf ? pe : tf;
+    }
+    return align256(pe);
+}
+
 static size_t op_bytes(int family, int op, int B, int L1, int L2) {
     switch (op) {
         case D2P_OP_FORWARD_BACKWARD: {
@@ -61,11 +72,13 @@ static size_t op_bytes(int family, int op, int B, int L1, int L2) {
             return align256(pe) + 2 * align256((size_t)(B > 0 ? B : 1) * sizeof(int));
         }
         case D2P_OP_HVP:
-            return plane_bytes(family, MODE_HVP, B, L1, L2);
         case D2P_OP_PARAM_JACOBIAN:
-            return plane_bytes(family, MODE_PT, B, L1, L2);
+            // the tangent kernel's workspace or the plane engine's (its fix-up),
+            // then one flag per problem
+            return tan_area(family, op, B, L1, L2) + align256((size_t)(B > 0 ? B : 1) * sizeof(int));
         case D2P_OP_BACKWARD_FULL:
-            return plane_bytes(family, MODE_PT, B, L1, L2) + align256((size_t)4 * (B > 0 ? B : 1) * sizeof(float));
+            return tan_area(family, op, B, L1, L2) + align256((size_t)4 * (B > 0 ? B : 1) * sizeof(float)) +
+                   align256((size_t)(B > 0 ? B : 1) * sizeof(int));
         default:
             return (size_t)-1;
     }
@@ -167,6 +180,22 @@ int d2p_sw_forward_backward(const float* scores, const int* lengths, int B, int 
     return launch_lin_plane(a, st);
 }
 
+// One tangent op on the linear family: the linear-domain tangent kernel, then
+// the plane engine for the problems it flagged (or for all, if the shape is not
+// covered).  flags: the op's per-problem flag array in the workspace.
+static int run_lin_tangent(SwArgs a, size_t ws_bytes, int* flags, cudaStream_t st) {
+    a.redo = flags;
+    a.only = nullptr;
+    int rc = launch_lin_tan(a, ws_bytes, st);
+    a.redo = nullptr;
+    if (rc == D2P_OK) {
+        a.only = flags;
+        return launch_lin_plane(a, st);
+    }
+    if (rc != kNotHandled) return rc;
+    return launch_lin_plane(a, st);
+}
+
 int d2p_sw_hvp(const float* scores, const float* tangent, const int* lengths, int B, int L1,
                int L2, float gap, float temperature, float* hvp, void* workspace,
                size_t workspace_bytes, void* stream) {
@@ -182,7 +211,8 @@ int d2p_sw_hvp(const float* scores, const float* tangent, const int* lengths, in
     a.mode = MODE_HVP;
     a.out = hvp;
     a.ws = (float*)workspace;
-    return launch_lin_plane(a, (cudaStream_t)stream);
+    int* flags = (int*)((char*)workspace + tan_area(D2P_FAMILY_LINEAR, D2P_OP_HVP, B, L1, L2));
+    return run_lin_tangent(a, workspace_bytes, flags, (cudaStream_t)stream);
 }
 
 int d2p_sw_param_jacobian(const float* scores, const int* lengths, int B, int L1, int L2,
@@ -200,7 +230,8 @@ int d2p_sw_param_jacobian(const float* scores, const int* lengths, int B, int L1
     a.mode = param_type == 0 ? MODE_PGAP : MODE_PT;
     a.out = jacobian;
     a.ws = (float*)workspace;
-    return launch_lin_plane(a, (cudaStream_t)stream);
+    int* flags = (int*)((char*)workspace + tan_area(D2P_FAMILY_LINEAR, D2P_OP_PARAM_JACOBIAN, B, L1, L2));
+    return run_lin_tangent(a, workspace_bytes, flags, (cudaStream_t)stream);
 }
 
 int d2p_sw_backward_full(const float* scores, const float* grad_marginals, const int* lengths,
@@ -217,8 +248,12 @@ int d2p_sw_backward_full(const float* scores, const float* grad_marginals, const
         cudaError_t e2 = cudaMemsetAsync(grad_temperature, 0, sizeof(float), st);
         return (int)(e1 != cudaSuccess ? e1 : e2);
     }
+    // grad_scores = H . grad_marginals (the Hessian of S is symmetric);
+    // grad_gap / grad_T = sum grad_marginals * dP/dgap, dP/dT
+    const size_t area = tan_area(D2P_FAMILY_LINEAR, D2P_OP_BACKWARD_FULL, B, L1, L2);
     float* planes = (float*)workspace;
-    float* partials = (float*)((char*)workspace + plane_bytes(D2P_FAMILY_LINEAR, MODE_PT, B, L1, L2));
+    float* partials = (float*)((char*)workspace + area);
+    int* flags = (int*)((char*)partials + align256((size_t)4 * B * sizeof(float)));
     SwArgs a = base_args(scores, lengths, B, L1, L2);
     a.gap = gap;
     a.temp = temperature;
@@ -226,18 +261,18 @@ int d2p_sw_backward_full(const float* scores, const float* grad_marginals, const
     a.tangent = grad_marginals;
     a.mode = MODE_HVP;
     a.out = grad_scores;
-    int rc = launch_lin_plane(a, st);
+    int rc = run_lin_tangent(a, workspace_bytes, flags, st);
     if (rc) return rc;
     a.tangent = nullptr;
     a.out = nullptr;
     a.dot_with = grad_marginals;
     a.mode = MODE_PGAP;
     a.dot_out = partials;
-    rc = launch_lin_plane(a, st);
+    rc = run_lin_tangent(a, workspace_bytes, flags, st);
     if (rc) return rc;
     a.mode = MODE_PT;
     a.dot_out = partials + B;
-    rc = launch_lin_plane(a, st);
+    rc = run_lin_tangent(a, workspace_bytes, flags, st);
     if (rc) return rc;
     rc = launch_sum_batches(partials, 1, B, grad_gap, 0, st);
     if (rc) return rc;

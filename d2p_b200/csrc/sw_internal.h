@@ -81,6 +81,12 @@ int launch_lin_plane(const SwArgs& a, cudaStream_t st);
 // D2P_B200_ENGINE=plane selects the general plane engine for every operator
 // (both engines compute the same results; used to cross-check them in tests).
 bool engine_forced_plane();
+
+// linear-domain tangent sweeps (sw_tangent.cu): HVP, dP/dgap, dP/dT, and the
+// dot mode (dot_with / dot_out) of the param modes; sets redo[b] for problems
+// the plane engine must recompute.  Returns -1 when the shape is not covered.
+size_t lin_tan_workspace_bytes(int B, int L1, int L2);
+int launch_lin_tan(const SwArgs& a, size_t ws_bytes, cudaStream_t st);
 int launch_aff_plane(const SwArgs& a, cudaStream_t st);
 
 // elementwise / reduction kernels (sw_elementwise.cu)

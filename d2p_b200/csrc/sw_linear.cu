@@ -52,17 +52,17 @@
 
 #include "sw_common.cuh"
 #include "sw_internal.h"
+#include "sw_lindomain.cuh"
 #include "sw_ring.cuh"
 
 namespace d2pb {
 namespace lin {
 using namespace ring;
+using namespace ld;
 
 constexpr int kMaxRB = 512;              // row-blocks per problem (L1 <= 16384)
 constexpr int kNW = 6;                   // warps per CTA, two CTAs per SM
 constexpr int kNWWide = 12;              // warps per CTA when the batch leaves SMs idle (one CTA per SM)
-constexpr int kJMax = 60;                // largest frame step (log2) a problem may take
-constexpr int kHR = 128;                 // staging ring of a neighbour's boundary values (steps)
 
 struct WarpSmem {
     float ringS[32 * kRW];    // scores [rows][64]; reverse: marginals written in place
@@ -87,13 +87,6 @@ struct Layout {  // per-problem workspace
     float* hfr;      // [nRB][GT]       and their frames, by its group
 };
 
-// Row counts cover every row the reverse's staging reaches past the last
-// step (up to 46 rows past L2, and 12 frame groups).
-__host__ __device__ inline int zt_rows(int L2m) { return L2m + 96; }
-__host__ __device__ inline int gt_rows(int L2m) { return (L2m + 96) / 4; }
-// boundary rows are stored and staged in 16-byte pieces: strides in whole float4s
-__host__ __device__ inline int hz_stride(int L2m) { return (zt_rows(L2m) + 3) & ~3; }
-__host__ __device__ inline int hf_stride(int L2m) { return (gt_rows(L2m) + 3) & ~3; }
 
 __host__ __device__ inline size_t per_problem_bytes(int L1m, int L2m) {
     const size_t nrb = (size_t)(L1m + 31) / 32;
@@ -118,30 +111,6 @@ __device__ inline Layout carve(float* ws, int b, int L1m, int L2m) {
     return L;
 }
 
-// Frames are integer-valued floats: 2^k is one MUFU ex2, exact for integer k
-// in [-126, 127] (0 below, +inf above; checked on the B200 for |k| <= 150).
-__device__ __forceinline__ float p2(float k) { return ex2f(k); }
-// binary exponent of a non-negative value (0 for zero; 128 for inf / NaN)
-__device__ __forceinline__ int expo(float v) {
-    const int bits = __float_as_int(v);
-    return bits > 0 ? (bits >> 23) - 127 : 0;
-}
-
-// Frame steps come from the exponent field of the lane's previous value: for
-// v = m 2^J (m in [1, 2)) the field is the bit pattern of 2^J, so 2^J, 2^-J
-// and J cost one integer operation each.  Zero (a lane that has not started)
-// reads as J = 0.
-__device__ __forceinline__ int efield(float v) {
-    const int b = __float_as_int(v) & 0x7f800000;
-    return b ? b : 0x3f800000;
-}
-__device__ __forceinline__ float inv_p2(float w) { return __int_as_float(0x7f000000 - __float_as_int(w)); }
-// 2^E as a double (|E| <= 1022; larger frames flag the problem)
-__device__ __forceinline__ double p2d(float E) {
-    return __hiloint2double((min(max(__float2int_rn(E), -1022), 1023) + 1023) << 20, 0);
-}
-// J of an exponent field (eb = bits of 2^J) as a float: exact
-__device__ __forceinline__ float efield_j(int eb) { return fmaf((float)eb, 1.0f / 8388608.0f, -127.f); }
 
 // One group of the boundary lane's (bnd) values and its frame: into the
 // staging ring of the consumer row-block's warp while it keeps up (push, pp),
@@ -252,15 +221,6 @@ __device__ __forceinline__ void fwd_apply(FwdVars& V) {
     V.f = V.nf;
 }
 
-// Once per stage: move the partition's base up with the frames (a group's
-// frame moves by at most kJMax, so E - ab stays below 700 + 4 kJMax until the
-// next check).  Frames far below the base add nothing visible to acc.
-__device__ __forceinline__ void acc_rebase(double& acc, float& ab, float E) {
-    if (E - ab > 700.f) {
-        acc *= p2d(ab - E);
-        ab = E;
-    }
-}
 
 // one cell, step i of its group; returns z, the up input in this frame (the
 // next step's diagonal input) and w = P (z_diag + 2^-E), the cell's diagonal

@@ -91,6 +91,60 @@ def test_backward_full(d2p, cuda_device, B, L1, L2, T, gap):
     check("grad_T", gt, r64[2], r32[2], rtol=1e-4, atol=1e-4)
 
 
+# Shapes routed to the linear-domain tangent kernel (L2 % 4 == 0): several
+# row-blocks, partial row-blocks, rows shorter and longer than a stage, ragged.
+TAN = [  # (B, L1, L2, T, gap, ragged)
+    (2, 33, 64, 1.0, -1.0, False), (3, 100, 36, 0.5, -1.0, False), (2, 130, 260, 1.0, -0.5, False),
+    (1, 200, 8, 1.0, -1.0, False), (4, 70, 96, 1.0, -1.0, True), (1, 7, 512, 2.0, -1.0, False),
+]
+
+
+def _tan_inputs(B, L1, L2, ragged, seed):
+    s = scores(B, L1, L2, seed=seed)
+    ln = lengths_for(B, L1, L2, seed=seed + 1) if ragged else None
+    if ln is not None:
+        ln[0] = torch.tensor([L1, L2], dtype=torch.int32)
+    return s, ln
+
+
+@pytest.mark.parametrize("B,L1,L2,T,gap,ragged", TAN)
+def test_tangent_hvp(d2p, cuda_device, B, L1, L2, T, gap, ragged):
+    s, ln = _tan_inputs(B, L1, L2, ragged, 61)
+    V = scores(B, L1, L2, seed=62)
+    H = torch.ops.d2p.soft_sw_hvp(s.to(cuda_device), V.to(cuda_device), gap, T,
+                                  None if ln is None else ln.to(cuda_device))
+    lnp = None if ln is None else ln.numpy()
+    h64 = oracle.sw_linear_hvp(s.numpy(), V.numpy(), lnp, gap, T, "f64")
+    h32 = oracle.sw_linear_hvp(s.numpy(), V.numpy(), lnp, gap, T, "f32")
+    check("hvp", H, h64, h32, rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.parametrize("param_type", [0, 1])
+@pytest.mark.parametrize("B,L1,L2,T,gap,ragged", TAN)
+def test_tangent_param_jacobian(d2p, cuda_device, B, L1, L2, T, gap, ragged, param_type):
+    s, ln = _tan_inputs(B, L1, L2, ragged, 63)
+    J = torch.ops.d2p.soft_sw_param_jacobian(s.to(cuda_device), param_type, gap, T,
+                                             None if ln is None else ln.to(cuda_device))
+    lnp = None if ln is None else ln.numpy()
+    j64 = oracle.sw_linear_param_jacobian(s.numpy(), param_type, lnp, gap, T, "f64")
+    j32 = oracle.sw_linear_param_jacobian(s.numpy(), param_type, lnp, gap, T, "f32")
+    check(f"jac{param_type}", J, j64, j32, rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.parametrize("B,L1,L2,T,gap,ragged", TAN)
+def test_tangent_backward_full(d2p, cuda_device, B, L1, L2, T, gap, ragged):
+    s, ln = _tan_inputs(B, L1, L2, ragged, 65)
+    Gm = scores(B, L1, L2, seed=66)
+    lnd = None if ln is None else ln.to(cuda_device)
+    gs, gg, gt = torch.ops.d2p.soft_sw_backward_full(s.to(cuda_device), Gm.to(cuda_device), gap, T, lnd)
+    lnp = None if ln is None else ln.numpy()
+    r64 = oracle.sw_linear_backward_full(s.numpy(), Gm.numpy(), lnp, gap, T, "f64")
+    r32 = oracle.sw_linear_backward_full(s.numpy(), Gm.numpy(), lnp, gap, T, "f32")
+    check("grad_scores", gs, r64[0], r32[0], rtol=1e-4, atol=1e-5)
+    check("grad_gap", gg, r64[1], r32[1], rtol=1e-4, atol=1e-4)
+    check("grad_T", gt, r64[2], r32[2], rtol=1e-4, atol=1e-4)
+
+
 def test_autograd_value_sum(d2p, cuda_device):
     s = scores(4, 30, 41, seed=21).to(cuda_device).requires_grad_(True)
     res = d2p.soft_sw(s, gap=-1.0, temperature=1.0)
