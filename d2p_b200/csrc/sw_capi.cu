@@ -68,8 +68,10 @@ static size_t op_bytes(int family, int op, int B, int L1, int L2) {
             const size_t lf = family == D2P_FAMILY_LINEAR ? lin_fast_workspace_bytes(B, L1, L2) : 0;
             pe = pe > wf ? pe : wf;
             pe = pe > lf ? pe : lf;
-            // flags, then the CTA order of ragged batches
-            return align256(pe) + 2 * align256((size_t)(B > 0 ? B : 1) * sizeof(int));
+            // flags, the CTA order of ragged batches, the cross-CTA words of
+            // problems spread over several CTAs
+            return align256(pe) + 2 * align256((size_t)(B > 0 ? B : 1) * sizeof(int)) +
+                   align256((size_t)(B > 0 ? B : 1) * kSyncBytes);
         }
         case D2P_OP_HVP:
         case D2P_OP_PARAM_JACOBIAN:
@@ -158,6 +160,7 @@ int d2p_sw_forward_backward(const float* scores, const int* lengths, int B, int 
         a.redo = flags;
         a.only = nullptr;
         a.order = nullptr;
+        a.sync = (int*)((char*)order + align256((size_t)B * sizeof(int)));
         if (lengths && !grad_gap && !grad_temperature) {
             const int ro = launch_lin_order(lengths, B, L1, L2, order, st);
             if (ro == D2P_OK) a.order = order;
@@ -165,6 +168,7 @@ int d2p_sw_forward_backward(const float* scores, const int* lengths, int B, int 
         }
         int rc = launch_lin_fast(a, workspace_bytes, st);
         a.order = nullptr;
+        a.sync = nullptr;
         if (rc == D2P_OK) a.only = flags;
         else if (rc != kNotHandled) return rc;
         rc = launch_wavefront(a, D2P_FAMILY_LINEAR, workspace_bytes, st);

@@ -58,7 +58,17 @@ struct SwArgs {
     int* redo;                          // [B] out: set for problems the kernel could not finish
     const int* only;                    // [B] in, optional: run only the problems whose entry is set
     const int* order;                   // [B] in, optional: problem of each CTA (largest first)
+    int parts;                          // CTAs per problem (1 unless a kernel spreads problems)
+    int* sync;                          // [B][kSyncBytes / 4], zeroed: cross-CTA words of each problem
 };
+
+// A problem spread over several CTAs (a cooperative launch) keeps its
+// cross-CTA progress words, barrier counter and partition partials here:
+// ints [0, kMaxParts) forward progress of each part's last warp, [kMaxParts,
+// 2 kMaxParts) reverse progress, [2 kMaxParts] barrier counter; from byte 256
+// on, two doubles per part (frame base, partition partial).
+constexpr int kMaxParts = 16;
+constexpr size_t kSyncBytes = 512;
 
 // linear-domain fast path (sw_linear.cu): value + marginals without parameter
 // gradients; returns -1 when the shape or arguments are not covered

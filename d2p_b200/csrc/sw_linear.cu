@@ -512,7 +512,12 @@ __device__ __forceinline__ void rev_stage_part(const RevCtx& C, RevVars& V, int 
 // (ordinal << 16 | kStageMask) when the row-block is complete.  The staging
 // for stage k reads the neighbouring row-block up to its stage k + 3, so it
 // waits for k + 4 stages there.
-template <int NW, int MINB>
+// SPLIT: the launch is cooperative and spreads each problem over p.parts CTAs;
+// row-block r goes to warp r mod NW of part (r / NW) mod parts, so the
+// handoff from a part's last warp to the next part's warp 0 crosses CTAs: it
+// takes the global route, with the progress words, the forward -> reverse
+// barrier and the partition partials in the problem's p.sync words.
+template <int NW, int MINB, bool SPLIT>
 __global__ void __launch_bounds__(NW * 32, MINB) lin_fast_kernel(SwArgs p) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     WarpSmem& W = reinterpret_cast<WarpSmem*>(smem_raw)[threadIdx.x >> 5];
@@ -523,8 +528,18 @@ __global__ void __launch_bounds__(NW * 32, MINB) lin_fast_kernel(SwArgs p) {
     __shared__ __align__(16) float zv[kHR];   // handoff ring of a missing neighbour: zeros
     __shared__ float zf[kHR / 4];
 
-    const int b = p.order ? p.order[blockIdx.x] : blockIdx.x;
+    const int K = SPLIT ? p.parts : 1;
+    const int part = SPLIT ? (int)(blockIdx.x % K) : 0;
+    const int bi = SPLIT ? (int)(blockIdx.x / K) : (int)blockIdx.x;
+    const int b = p.order ? p.order[bi] : bi;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int gw = part * NW + warp, NWt = K * NW;  // this warp among the problem's warps
+    // cross-CTA links: warp 0's producer and warp NW-1's consumer sit in the
+    // neighbouring parts; their progress words are global
+    int* const gsync = SPLIT ? p.sync + (size_t)b * (kSyncBytes / 4) : nullptr;
+    const bool xin = SPLIT && K > 1 && warp == 0;
+    const bool xout = SPLIT && K > 1 && warp == NW - 1;
+    const int pin = (part + K - 1) % K;
     const int L1m = p.L1, L2m = p.L2;
     const int L1 = p.lengths ? min(max(p.lengths[2 * b], 0), L1m) : L1m;
     const int L2 = p.lengths ? min(max(p.lengths[2 * b + 1], 0), L2m) : L2m;
@@ -542,13 +557,13 @@ __global__ void __launch_bounds__(NW * 32, MINB) lin_fast_kernel(SwArgs p) {
     const size_t est = (size_t)gt_rows(L2m) * 32;   // efr row-block stride (ints)
 
     if (out && (L1 < L1m || L2 < L2m)) {  // zero the padded part of the marginals
-        for (int i = warp; i < L1m; i += NW) {
+        for (int i = gw; i < L1m; i += NWt) {
             float* row = out + (size_t)i * L2m;
             for (int j = (i < L1 ? L2 : 0) + lane; j < L2m; j += 32) row[j] = 0.f;
         }
     }
     if (L1 == 0 || L2 == 0) {  // S = log(1) = 0 (alpha[0,0] only)
-        if (threadIdx.x == 0) {
+        if (threadIdx.x == 0 && part == 0) {
             if (p.value) p.value[b] = 0.f;
             if (p.redo) p.redo[b] = 0;
         }
@@ -591,8 +606,14 @@ __global__ void __launch_bounds__(NW * 32, MINB) lin_fast_kernel(SwArgs p) {
         for (int i = 0; i < 4; ++i) cp_async16(W.sv + ((s0 + 4 * i) & (kHR - 1)), hz + s0 + 4 * i, 16);
         cp_async16(W.sf + (g0 & (kHR / 4 - 1)), hf + g0, 16);
     };
+    auto wait_prog = [&](const int* prog, bool global, int need) {
+        if (global)
+            wait_flag_gpu(prog, need, &sh_err);
+        else
+            wait_flag(prog, need, &sh_err);
+    };
     auto stage_first = [&](const int* prog, int ordinal, int rb, bool reader) {
-        wait_flag(prog, (ordinal << 16) + 3, &sh_err);
+        wait_prog(prog, xin, (ordinal << 16) + 3);
         if (reader) {
             const float* const hz = LY.hz + (size_t)rb * hzst;
             const float* const hf = LY.hfr + (size_t)rb * hfst;
@@ -608,7 +629,7 @@ __global__ void __launch_bounds__(NW * 32, MINB) lin_fast_kernel(SwArgs p) {
         }
     };
     auto stage_need = [&](const int* prog, int ordinal, int k, int rb, bool reader) {
-        wait_flag(prog, (ordinal << 16) + min(k + 4, kStageMask), &sh_err);
+        wait_prog(prog, xin, (ordinal << 16) + min(k + 4, kStageMask));
         if (reader) copy_stage(ordinal, k + 3, rb);
     };
 
@@ -620,7 +641,9 @@ __global__ void __launch_bounds__(NW * 32, MINB) lin_fast_kernel(SwArgs p) {
     V.E = 0.f;
     V.ebmin = V.ebmax = 0x3f800000;
     V.emax = 0.f;
-    for (int r = warp; r < nRB; r += NW) {
+    const int* const prodF = xin ? gsync + pin : &progF[wprev];
+    const int* const prodR = xin ? gsync + kMaxParts + pin : &progR[wprev];
+    for (int r = gw; r < nRB; r += NWt) {
         const int nv = min(32, L1 - 32 * r);
         const int nst = (L2 + nv - 1 + kCW - 1) / kCW;
         const float* srow = S + (size_t)(32 * r) * L2m;
@@ -649,13 +672,13 @@ __global__ void __launch_bounds__(NW * 32, MINB) lin_fast_kernel(SwArgs p) {
         __syncwarp();
         if (lane == 31) st_release(&progF[warp], r << 16);  // started: the row above may push to this warp
         if (0 < nch) tile_load<4>(tS, 0, L2);
-        if (hasB) stage_first(&progF[wprev], r - 1, r - 1, lane == 0);
+        if (hasB) stage_first(prodF, r - 1, r - 1, lane == 0);
         cp_async_commit();
         V.zl = V.zd = V.zsh = 0.f;
         V.f.d1 = 0.f;  // lane 0 keeps zero neighbour factors; the others set theirs when they start
         for (int k = 0; k < nst; ++k) {
             __syncwarp();
-            if (hasB) stage_need(&progF[wprev], r - 1, k, r - 1, lane == 0);
+            if (hasB) stage_need(prodF, r - 1, k, r - 1, lane == 0);
             cp_async_commit();
             if (k + 1 < nch) tile_load<4>(tS, k + 1, L2);
             cp_async_commit();
@@ -666,7 +689,7 @@ __global__ void __launch_bounds__(NW * 32, MINB) lin_fast_kernel(SwArgs p) {
             // (stage c reads stages c+2, c+3), and the slots its prologue copies
             // into (stages 1, 2) are written only with the same stages.
             V.push = false;
-            if (lane == 31 && hasD) {
+            if (lane == 31 && hasD && !xout) {
                 const int cw = ld_acquire(&progF[wnext]);
                 V.push = (cw >> 16) == r + 1 && (cw & kStageMask) + 8 >= k;
             }
@@ -684,7 +707,10 @@ __global__ void __launch_bounds__(NW * 32, MINB) lin_fast_kernel(SwArgs p) {
             acc_rebase(V.acc, V.ab, V.E);
             if (V.push) Wn.tag[k & (kHR / 16 - 1)] = (r << 16) | k;
             __syncwarp();
-            if (lane == 31) st_release(&progF[warp], (r << 16) | min(k + 1, kStageMask - 1));
+            if (lane == 31) {
+                st_release(&progF[warp], (r << 16) | min(k + 1, kStageMask - 1));
+                if (xout) st_release_gpu(gsync + part, (r << 16) | min(k + 1, kStageMask - 1));
+            }
         }
         V.acc = fma((double)V.gsum, p2d(V.E - V.ab), V.acc);  // the last group's partition
         V.emax = fmaxf(V.emax, V.E - V.ab);
@@ -701,16 +727,40 @@ __global__ void __launch_bounds__(NW * 32, MINB) lin_fast_kernel(SwArgs p) {
         }
         cp_async_wait0();
         __syncwarp();
-        if (lane == 31) st_release(&progF[warp], (r << 16) | kStageMask);
+        if (lane == 31) {
+            st_release(&progF[warp], (r << 16) | kStageMask);
+            if (xout) st_release_gpu(gsync + part, (r << 16) | kStageMask);
+        }
     }
 
     if (lane < kHR / 16) W.tag[lane] = -1;  // forward pushes are no reverse pushes
     // ---- S = log2(1 + sum of every lane's partition), kept as integer + fraction
     {
         // every lane's acc brought to the largest base; alpha[0,0] = 0 adds 2^-abmax
-        const float abmax = block_max(V.ab, red);
-        const double tot = block_sum_d(V.acc * p2d(V.ab - abmax), reinterpret_cast<double*>(red)) + p2d(-abmax);
+        const float abl = block_max(V.ab, red);
+        const double totl = block_sum_d(V.acc * p2d(V.ab - abl), reinterpret_cast<double*>(red));
         if (threadIdx.x == 0) {
+            float abmax = abl;
+            double tot = totl;
+            if (SPLIT && K > 1) {  // every part's partial, after every part's forward
+                double* const gp = reinterpret_cast<double*>(gsync + 64);
+                gp[2 * part] = (double)abl;
+                gp[2 * part + 1] = totl;
+                atom_add_release_gpu(gsync + 2 * kMaxParts, 1);
+                int it = 0;
+                while (ld_acquire_gpu(gsync + 2 * kMaxParts) < K) {
+                    if (++it > kSpinLimit) {
+                        sh_err = 1;
+                        break;
+                    }
+                    __nanosleep(64);
+                }
+                abmax = -3.0e38f;
+                for (int k = 0; k < K; ++k) abmax = fmaxf(abmax, (float)gp[2 * k]);
+                tot = 0.0;
+                for (int k = 0; k < K; ++k) tot = fma(gp[2 * k + 1], p2d((float)gp[2 * k] - abmax), tot);
+            }
+            tot += p2d(-abmax);
             const int hi = __double2hiint(tot);
             const int ef = (hi >> 20) & 0x7ff;
             const int e = ef - 1023 + (int)abmax;                             // tot 2^abmax = m 2^e, m in [1, 2)
@@ -720,7 +770,7 @@ __global__ void __launch_bounds__(NW * 32, MINB) lin_fast_kernel(SwArgs p) {
             sh_Sint = e;
             sh_Sfrac = l2;
             if (!fin) sh_bad = 1;
-            if (p.value) p.value[b] = ((float)sh_Sint + sh_Sfrac) / c;
+            if (p.value && part == 0) p.value[b] = ((float)sh_Sint + sh_Sfrac) / c;
         }
         __syncthreads();  // also: every forward read of the handoff rings is done
     }
@@ -733,7 +783,7 @@ __global__ void __launch_bounds__(NW * 32, MINB) lin_fast_kernel(SwArgs p) {
     const int nstR = P / kCW + 2;  // lane 0 reaches column 0 at step P + 31
     RevVars RV;
     RV.ebmin = RV.ebmax = 0x3f800000;
-    for (int q = warp; q < nRB; q += NW) {
+    for (int q = gw; q < nRB; q += NWt) {
         const int r = nRB - 1 - q;
         const int nv = min(32, L1 - 32 * r);
         const float* srow = S + (size_t)(32 * r) * L2m;
@@ -788,7 +838,7 @@ __global__ void __launch_bounds__(NW * 32, MINB) lin_fast_kernel(SwArgs p) {
                 if (ch >= 0 && ch < nch) tile_load<4>(tS, ch, L2);
         }
         batch(0);
-        if (hasBelow) stage_first(&progR[wprev], q - 1, r + 1, lane == nv - 1);
+        if (hasBelow) stage_first(prodR, q - 1, r + 1, lane == nv - 1);
         cp_async_commit();
 
         RV.br = RV.pbp = RV.rsh = 0.f;
@@ -798,7 +848,7 @@ __global__ void __launch_bounds__(NW * 32, MINB) lin_fast_kernel(SwArgs p) {
         for (int k = 0; k < nstR; ++k) {
             const int M = P / kCW + 1 - k;
             __syncwarp();
-            if (hasBelow) stage_need(&progR[wprev], q - 1, k, r + 1, lane == nv - 1);
+            if (hasBelow) stage_need(prodR, q - 1, k, r + 1, lane == nv - 1);
             cp_async_commit();
             if (out && M + 1 < nch && M + 1 >= 0) tile_store(tM, M + 1, L2);  // no lane touches it any more
             if (M - 3 >= 0 && M - 3 < nch) tile_load<4>(tS, M - 3, L2);       // for stage k + 1
@@ -807,7 +857,7 @@ __global__ void __launch_bounds__(NW * 32, MINB) lin_fast_kernel(SwArgs p) {
             cp_async_wait2();  // everything but this stage's two groups
             __syncwarp();
             RV.push = false;
-            if (lane == 0 && hasAbove) {
+            if (lane == 0 && hasAbove && !xout) {
                 const int cw = ld_acquire(&progR[wnext]);
                 RV.push = (cw >> 16) == q + 1 && (cw & kStageMask) + 8 >= k;
             }
@@ -823,7 +873,10 @@ __global__ void __launch_bounds__(NW * 32, MINB) lin_fast_kernel(SwArgs p) {
                 rev_stage_full<true>(C, RV, k, lane < nv ? 16 * M + 16 - lane : -1);
             if (RV.push) Wn.tag[k & (kHR / 16 - 1)] = (q << 16) | k;
             __syncwarp();
-            if (lane == 0) st_release(&progR[warp], (q << 16) | min(k + 1, kStageMask - 1));
+            if (lane == 0) {
+                st_release(&progR[warp], (q << 16) | min(k + 1, kStageMask - 1));
+                if (xout) st_release_gpu(gsync + kMaxParts + part, (q << 16) | min(k + 1, kStageMask - 1));
+            }
         }
         // past the last stage the row above's look-aheads read up to 48 steps and
         // 12 groups further: zeros, in the final frame
@@ -839,7 +892,10 @@ __global__ void __launch_bounds__(NW * 32, MINB) lin_fast_kernel(SwArgs p) {
         if (out && nch > 0) tile_store(tM, 0, L2);  // the last stage had M = 0
         cp_async_wait0();
         __syncwarp();
-        if (lane == 0) st_release(&progR[warp], (q << 16) | kStageMask);
+        if (lane == 0) {
+            st_release(&progR[warp], (q << 16) | kStageMask);
+            if (xout) st_release_gpu(gsync + kMaxParts + part, (q << 16) | kStageMask);
+        }
     }
 
     // a frame step outside the window, a partition that overflowed, or a
@@ -851,7 +907,12 @@ __global__ void __launch_bounds__(NW * 32, MINB) lin_fast_kernel(SwArgs p) {
     // nonzero = recompute; the bits say why (1 frame step, 2 wait gave up,
     // 4 partition not finite, 8 partition base)
     const int redo = (o_win ? 1 : 0) | (sh_err ? 2 : 0) | (sh_bad ? 4 : 0) | (o_acc ? 8 : 0);
-    if (threadIdx.x == 0 && p.redo) p.redo[b] = redo;
+    if (threadIdx.x == 0 && p.redo) {
+        if (SPLIT)
+            atomicOr(p.redo + b, redo);  // zeroed by the launcher
+        else
+            p.redo[b] = redo;
+    }
 }
 
 // Problems of a ragged batch by decreasing estimated cost (cells plus the
@@ -939,6 +1000,24 @@ static bool wide_pays(int L1, int L2) {
 }
 bool lin_wide_pays(int L1, int L2) { return wide_pays(L1, L2); }
 
+// CTAs per problem for a batch of B problems of 12 warps each, one CTA per SM:
+// the smallest part count within 3 % of the best the pipeline model offers
+// (parts * B <= SMs; a crossing between parts costs about as much as a
+// handoff through global memory, taken into account as 10 % per stage).
+int lin_parts(int B, int L1, int L2, int sms) {
+    const int n = (L1 + 31) / 32, st = (L2 + 31 + lin::kCW - 1) / lin::kCW;
+    if (B <= 0 || n > lin::kMaxRB || 2 * B > sms) return 1;
+    double t[kMaxParts + 1];
+    double best = 1e300;
+    for (int K = 1; K <= kMaxParts && K * B <= sms; ++K) {
+        t[K] = pipeline_stages(n, st, lin::kNWWide * K) * (K > 1 ? 1.1 : 1.0);
+        best = fmin(best, t[K]);
+    }
+    for (int K = 1; K <= kMaxParts && K * B <= sms; ++K)
+        if (t[K] <= 1.03 * best) return K;
+    return 1;
+}
+
 int launch_lin_fast(const SwArgs& a, size_t ws_bytes, cudaStream_t st) {
     if (a.mode != MODE_MARG || !a.redo || a.grad_gap || a.grad_T) return -1;
     if (engine_forced_plane()) return -1;
@@ -954,18 +1033,19 @@ int launch_lin_fast(const SwArgs& a, size_t ws_bytes, cudaStream_t st) {
     static bool attr_set[64] = {false};
     if (dev < 64 && !attr_set[dev]) {
         const size_t s6 = sizeof(lin::WarpSmem) * lin::kNW, s12 = sizeof(lin::WarpSmem) * lin::kNWWide;
-        e = cudaFuncSetAttribute(lin::lin_fast_kernel<lin::kNW, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)s6);
+        const void* k6 = (const void*)lin::lin_fast_kernel<lin::kNW, 2, false>;
+        const void* k12[2] = {(const void*)lin::lin_fast_kernel<lin::kNWWide, 1, false>,
+                              (const void*)lin::lin_fast_kernel<lin::kNWWide, 1, true>};
+        e = cudaFuncSetAttribute(k6, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s6);
         if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(lin::lin_fast_kernel<lin::kNW, 2>, cudaFuncAttributePreferredSharedMemoryCarveout,
+            e = cudaFuncSetAttribute(k6, cudaFuncAttributePreferredSharedMemoryCarveout,
                                      (int)cudaSharedmemCarveoutMaxShared);
-        if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(lin::lin_fast_kernel<lin::kNWWide, 1>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s12);
-        if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(lin::lin_fast_kernel<lin::kNWWide, 1>,
-                                     cudaFuncAttributePreferredSharedMemoryCarveout,
-                                     (int)cudaSharedmemCarveoutMaxShared);
+        for (int i = 0; i < 2 && e == cudaSuccess; ++i) {
+            e = cudaFuncSetAttribute(k12[i], cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s12);
+            if (e == cudaSuccess)
+                e = cudaFuncSetAttribute(k12[i], cudaFuncAttributePreferredSharedMemoryCarveout,
+                                         (int)cudaSharedmemCarveoutMaxShared);
+        }
         if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
         if (e != cudaSuccess) return (int)e;
         attr_set[dev] = true;
@@ -973,11 +1053,26 @@ int launch_lin_fast(const SwArgs& a, size_t ws_bytes, cudaStream_t st) {
     // A batch of at most one problem per SM may run 12 warps per problem,
     // when the pipeline model says that pays (12 warps on one SM run each
     // stage about 25 % slower: measured 1.19 - 1.32 on 256 x 1024 .. 1024 x 1024).
+    // A batch that leaves most SMs idle spreads each problem over several
+    // CTAs (cooperative launch: every part resident at once).
+    const int K = (dev < 64 && a.sync) ? lin_parts(a.B, a.L1, a.L2, sms[dev]) : 1;
+    if (K > 1) {
+        SwArgs s = a;
+        s.parts = K;
+        e = cudaMemsetAsync(s.sync, 0, kSyncBytes * (size_t)a.B, st);
+        if (e == cudaSuccess) e = cudaMemsetAsync(s.redo, 0, sizeof(int) * (size_t)a.B, st);
+        if (e != cudaSuccess) return (int)e;
+        void* args[1] = {&s};
+        e = cudaLaunchCooperativeKernel((const void*)lin::lin_fast_kernel<lin::kNWWide, 1, true>, dim3(a.B * K),
+                                        dim3(lin::kNWWide * 32), args, sizeof(lin::WarpSmem) * lin::kNWWide, st);
+        if (e == cudaSuccess) return 0;
+        cudaGetLastError();  // a cooperative launch that does not fit: one CTA per problem instead
+    }
     if (dev < 64 && a.B <= sms[dev] && wide_pays(a.L1, a.L2)) {
-        lin::lin_fast_kernel<lin::kNWWide, 1>
+        lin::lin_fast_kernel<lin::kNWWide, 1, false>
             <<<a.B, lin::kNWWide * 32, sizeof(lin::WarpSmem) * lin::kNWWide, st>>>(a);
     } else {
-        lin::lin_fast_kernel<lin::kNW, 2><<<a.B, lin::kNW * 32, sizeof(lin::WarpSmem) * lin::kNW, st>>>(a);
+        lin::lin_fast_kernel<lin::kNW, 2, false><<<a.B, lin::kNW * 32, sizeof(lin::WarpSmem) * lin::kNW, st>>>(a);
     }
     return (int)cudaGetLastError();
 }

@@ -72,6 +72,39 @@ __device__ __forceinline__ void wait_flag(const int* flag, int need, int* err) {
     __syncwarp();
 }
 
+// The same progress words in global memory, at GPU scope: between the CTAs
+// that share one problem (every CTA of such a launch is resident at once: it
+// is a cooperative launch).
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_gpu(int* p, int v) {
+    asm volatile("st.release.gpu.global.b32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int atom_add_release_gpu(int* p, int v) {
+    int old;
+    asm volatile("atom.add.release.gpu.global.s32 %0, [%1], %2;\n" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+// wait_flag on a global word (all lanes; bounded like wait_flag)
+__device__ __forceinline__ void wait_flag_gpu(const int* flag, int need, int* err) {
+    int it = 0;
+    if (*(volatile int*)err) {
+        __syncwarp();
+        return;
+    }
+    while (ld_acquire_gpu(flag) < need) {
+        if (++it > kSpinLimit) {
+            *err = 1;
+            break;
+        }
+        __nanosleep(64);
+    }
+    __syncwarp();
+}
+
 // One lane's group handoff into shared memory: four values and a frame word,
 // stored under a predicate (no branch) so the other lanes only pay one issue.
 __device__ __forceinline__ void sts_group_pred_s(unsigned a, unsigned b, float4 v, float fr, bool pr) {

@@ -616,7 +616,7 @@ __global__ void __launch_bounds__(kNW * 32, 1) lin_tan_kernel(SwArgs p) {
         progF[threadIdx.x] = -1;
         progR[threadIdx.x] = -1;
     }
-    if (threadIdx.x < 2 * kHR) zv[threadIdx.x] = 0.f;
+    for (int i = threadIdx.x; i < 2 * kHR; i += blockDim.x) zv[i] = 0.f;  // 256 entries, 192 threads
     if (threadIdx.x < kHR / 4) zf[threadIdx.x] = 0.f;
     if (lane < kHR / 16) W.tag[lane] = -1;
     if (threadIdx.x == 0) {

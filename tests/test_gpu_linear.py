@@ -245,6 +245,29 @@ def test_long_rows(d2p, cuda_device, B, L1, L2):
     check("marginals", m[idx], r64["marginals"], r32["marginals"])
 
 
+@pytest.mark.parametrize("B,L1,L2,ragged", [(4, 1024, 1024, False), (2, 2048, 512, False), (1, 4096, 256, False),
+                                             (3, 1000, 600, True)])
+def test_problem_spread_over_ctas(d2p, cuda_device, B, L1, L2, ragged):
+    """Few problems with many row-blocks: each problem runs on several CTAs
+    (cooperative launch) whose row-block handoffs, forward -> reverse barrier
+    and partition partials go through global memory.  Results must match the
+    oracle and repeat bitwise."""
+    s = scores(B, L1, L2, seed=L1 + L2 + B)
+    ln = lengths_for(B, L1, L2, seed=B) if ragged else None
+    if ln is not None:
+        ln[0] = torch.tensor([L1, L2], dtype=torch.int32)
+    lnd = None if ln is None else ln.to(cuda_device)
+    v, m = torch.ops.d2p.soft_sw_float(s.to(cuda_device), -1.0, 1.0, lnd)
+    v2, m2 = torch.ops.d2p.soft_sw_float(s.to(cuda_device), -1.0, 1.0, lnd)
+    assert torch.equal(v, v2) and torch.equal(m, m2)
+    idx = [0, B - 1] if B > 1 else [0]
+    lnp = None if ln is None else ln[idx].numpy()
+    r64 = oracle.sw_linear(s[idx].numpy(), lnp, -1.0, 1.0, "f64")
+    r32 = oracle.sw_linear(s[idx].numpy(), lnp, -1.0, 1.0, "f32")
+    check("value", v[idx], r64["value"], r32["value"])
+    check("marginals", m[idx], r64["marginals"], r32["marginals"])
+
+
 # Shapes routed to the register/shared-memory wavefront kernel (L2 % 4 == 0):
 # partial and multiple row-blocks, L2 below/around/above the 16-column chunk.
 FAST = [  # (B, L1, L2, T)
