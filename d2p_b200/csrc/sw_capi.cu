@@ -76,11 +76,13 @@ static size_t op_bytes(int family, int op, int B, int L1, int L2) {
         case D2P_OP_HVP:
         case D2P_OP_PARAM_JACOBIAN:
             // the tangent kernel's workspace or the plane engine's (its fix-up),
-            // then one flag per problem
-            return tan_area(family, op, B, L1, L2) + align256((size_t)(B > 0 ? B : 1) * sizeof(int));
+            // then one flag per problem and the cross-CTA words of problems
+            // spread over several CTAs
+            return tan_area(family, op, B, L1, L2) + align256((size_t)(B > 0 ? B : 1) * sizeof(int)) +
+                   align256((size_t)(B > 0 ? B : 1) * kSyncBytes);
         case D2P_OP_BACKWARD_FULL:
             return tan_area(family, op, B, L1, L2) + align256((size_t)4 * (B > 0 ? B : 1) * sizeof(float)) +
-                   align256((size_t)(B > 0 ? B : 1) * sizeof(int));
+                   align256((size_t)(B > 0 ? B : 1) * sizeof(int)) + align256((size_t)(B > 0 ? B : 1) * kSyncBytes);
         default:
             return (size_t)-1;
     }
@@ -190,8 +192,10 @@ int d2p_sw_forward_backward(const float* scores, const int* lengths, int B, int 
 static int run_lin_tangent(SwArgs a, size_t ws_bytes, int* flags, cudaStream_t st) {
     a.redo = flags;
     a.only = nullptr;
+    a.sync = (int*)((char*)flags + align256((size_t)a.B * sizeof(int)));
     int rc = launch_lin_tan(a, ws_bytes, st);
     a.redo = nullptr;
+    a.sync = nullptr;
     if (rc == D2P_OK) {
         a.only = flags;
         return launch_lin_plane(a, st);

@@ -63,12 +63,14 @@ struct SwArgs {
 };
 
 // A problem spread over several CTAs (a cooperative launch) keeps its
-// cross-CTA progress words, barrier counter and partition partials here:
+// cross-CTA progress words, barrier counters and per-part partials here:
 // ints [0, kMaxParts) forward progress of each part's last warp, [kMaxParts,
-// 2 kMaxParts) reverse progress, [2 kMaxParts] barrier counter; from byte 256
-// on, two doubles per part (frame base, partition partial).
+// 2 kMaxParts) reverse progress, 2 kMaxParts + 0 / + 1 two arrival counters;
+// from byte 256 on, kSyncPartDoubles doubles per part (frame base, partition
+// partial, its tangent, a dot-product partial).
 constexpr int kMaxParts = 16;
-constexpr size_t kSyncBytes = 512;
+constexpr int kSyncPartDoubles = 4;
+constexpr size_t kSyncBytes = 256 + 8 * kSyncPartDoubles * kMaxParts;
 
 // linear-domain fast path (sw_linear.cu): value + marginals without parameter
 // gradients; returns -1 when the shape or arguments are not covered
@@ -96,6 +98,9 @@ bool engine_forced_plane();
 // dot mode (dot_with / dot_out) of the param modes; sets redo[b] for problems
 // the plane engine must recompute.  Returns -1 when the shape is not covered.
 size_t lin_tan_workspace_bytes(int B, int L1, int L2);
+// CTAs per problem for B problems of nw warps per CTA, one CTA per SM (the
+// row-block pipeline model; 1 = one CTA per problem)
+int lin_parts_nw(int B, int L1, int L2, int sms, int nw);
 int launch_lin_tan(const SwArgs& a, size_t ws_bytes, cudaStream_t st);
 int launch_aff_plane(const SwArgs& a, cudaStream_t st);
 

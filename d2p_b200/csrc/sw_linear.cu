@@ -744,8 +744,8 @@ __global__ void __launch_bounds__(NW * 32, MINB) lin_fast_kernel(SwArgs p) {
             double tot = totl;
             if (SPLIT && K > 1) {  // every part's partial, after every part's forward
                 double* const gp = reinterpret_cast<double*>(gsync + 64);
-                gp[2 * part] = (double)abl;
-                gp[2 * part + 1] = totl;
+                gp[kSyncPartDoubles * part] = (double)abl;
+                gp[kSyncPartDoubles * part + 1] = totl;
                 atom_add_release_gpu(gsync + 2 * kMaxParts, 1);
                 int it = 0;
                 while (ld_acquire_gpu(gsync + 2 * kMaxParts) < K) {
@@ -756,9 +756,10 @@ __global__ void __launch_bounds__(NW * 32, MINB) lin_fast_kernel(SwArgs p) {
                     __nanosleep(64);
                 }
                 abmax = -3.0e38f;
-                for (int k = 0; k < K; ++k) abmax = fmaxf(abmax, (float)gp[2 * k]);
+                for (int k = 0; k < K; ++k) abmax = fmaxf(abmax, (float)gp[kSyncPartDoubles * k]);
                 tot = 0.0;
-                for (int k = 0; k < K; ++k) tot = fma(gp[2 * k + 1], p2d((float)gp[2 * k] - abmax), tot);
+                for (int k = 0; k < K; ++k)
+                    tot = fma(gp[kSyncPartDoubles * k + 1], p2d((float)gp[kSyncPartDoubles * k] - abmax), tot);
             }
             tot += p2d(-abmax);
             const int hi = __double2hiint(tot);
@@ -1000,17 +1001,17 @@ static bool wide_pays(int L1, int L2) {
 }
 bool lin_wide_pays(int L1, int L2) { return wide_pays(L1, L2); }
 
-// CTAs per problem for a batch of B problems of 12 warps each, one CTA per SM:
+// CTAs per problem for a batch of B problems of nw warps each, one CTA per SM:
 // the smallest part count within 3 % of the best the pipeline model offers
 // (parts * B <= SMs; a crossing between parts costs about as much as a
 // handoff through global memory, taken into account as 10 % per stage).
-int lin_parts(int B, int L1, int L2, int sms) {
+int lin_parts_nw(int B, int L1, int L2, int sms, int nw) {
     const int n = (L1 + 31) / 32, st = (L2 + 31 + lin::kCW - 1) / lin::kCW;
     if (B <= 0 || n > lin::kMaxRB || 2 * B > sms) return 1;
     double t[kMaxParts + 1];
     double best = 1e300;
     for (int K = 1; K <= kMaxParts && K * B <= sms; ++K) {
-        t[K] = pipeline_stages(n, st, lin::kNWWide * K) * (K > 1 ? 1.1 : 1.0);
+        t[K] = pipeline_stages(n, st, nw * K) * (K > 1 ? 1.1 : 1.0);
         best = fmin(best, t[K]);
     }
     for (int K = 1; K <= kMaxParts && K * B <= sms; ++K)
@@ -1055,7 +1056,7 @@ int launch_lin_fast(const SwArgs& a, size_t ws_bytes, cudaStream_t st) {
     // stage about 25 % slower: measured 1.19 - 1.32 on 256 x 1024 .. 1024 x 1024).
     // A batch that leaves most SMs idle spreads each problem over several
     // CTAs (cooperative launch: every part resident at once).
-    const int K = (dev < 64 && a.sync) ? lin_parts(a.B, a.L1, a.L2, sms[dev]) : 1;
+    const int K = (dev < 64 && a.sync) ? lin_parts_nw(a.B, a.L1, a.L2, sms[dev], lin::kNWWide) : 1;
     if (K > 1) {
         SwArgs s = a;
         s.parts = K;

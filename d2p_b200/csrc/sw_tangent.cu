@@ -463,7 +463,7 @@ template <bool DOT>
 __device__ __forceinline__ void rev_emit(const RevCtx& C, RevVars& V, float* slot, float gm, float dmu, bool act) {
     if (act) V.chk = fmaf(dmu, 0.f, V.chk);
     if (DOT) {
-        V.sdot = fmaf(act ? gm : 0.f, dmu, V.sdot);
+        if (act) V.sdot = fmaf(gm, dmu, V.sdot);  // a cell outside the problem may hold inf: no 0 * inf
     } else {
         if (act) *slot = dmu;
     }
@@ -564,7 +564,10 @@ __device__ __forceinline__ void rev_stage_part(const RevCtx& C, RevVars& V, int 
 // direction; DOT: the weights); DOT: sum weight * dmu per problem into
 // dot_out instead of writing dmu to out.
 // ==========================================================================
-template <bool HV, bool DOT>
+// SPLIT: a cooperative launch spreads each problem over p.parts CTAs, as in
+// sw_linear.cu's lin_fast_kernel (the partition's tangent and the dot-mode
+// sums are combined across the parts in part order).
+template <bool HV, bool DOT, bool SPLIT>
 __global__ void __launch_bounds__(kNW * 32, 1) lin_tan_kernel(SwArgs p) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     WarpSmem& W = reinterpret_cast<WarpSmem*>(smem_raw)[threadIdx.x >> 5];
@@ -575,9 +578,17 @@ __global__ void __launch_bounds__(kNW * 32, 1) lin_tan_kernel(SwArgs p) {
     __shared__ __align__(16) float zv[2 * kHR];   // staging of a missing neighbour: zeros
     __shared__ float zf[kHR / 4];
 
-    const int b = blockIdx.x;
+    const int K = SPLIT ? p.parts : 1;
+    const int part = SPLIT ? (int)(blockIdx.x % K) : 0;
+    const int b = SPLIT ? (int)(blockIdx.x / K) : (int)blockIdx.x;
     if (p.only && p.only[b] == 0) return;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int gw = part * kNW + warp, NWt = K * kNW;
+    int* const gsync = SPLIT ? p.sync + (size_t)b * (kSyncBytes / 4) : nullptr;
+    double* const gpart = SPLIT ? reinterpret_cast<double*>(gsync + 64) : nullptr;
+    const bool xin = SPLIT && K > 1 && warp == 0;
+    const bool xout = SPLIT && K > 1 && warp == kNW - 1;
+    const int pin = (part + K - 1) % K;
     const int L1m = p.L1, L2m = p.L2;
     const int L1 = p.lengths ? min(max(p.lengths[2 * b], 0), L1m) : L1m;
     const int L2 = p.lengths ? min(max(p.lengths[2 * b + 1], 0), L2m) : L2m;
@@ -600,13 +611,13 @@ __global__ void __launch_bounds__(kNW * 32, 1) lin_tan_kernel(SwArgs p) {
     const size_t est = (size_t)gt_rows(L2m) * 32;
 
     if (out && (L1 < L1m || L2 < L2m)) {  // zero the padded part of the output
-        for (int i = warp; i < L1m; i += kNW) {
+        for (int i = gw; i < L1m; i += NWt) {
             float* row = out + (size_t)i * L2m;
             for (int j = (i < L1 ? L2 : 0) + lane; j < L2m; j += 32) row[j] = 0.f;
         }
     }
     if (L1 == 0 || L2 == 0) {  // no cells: the output is all zeros
-        if (threadIdx.x == 0) {
+        if (threadIdx.x == 0 && part == 0) {
             if (DOT && p.dot_out) p.dot_out[b] = 0.f;
             if (p.redo) p.redo[b] = 0;
         }
@@ -644,15 +655,21 @@ __global__ void __launch_bounds__(kNW * 32, 1) lin_tan_kernel(SwArgs p) {
         }
         cp_async16(W.sf + (g0 & (kHR / 4 - 1)), hf + g0, 16);
     };
+    auto wait_prog = [&](const int* prog, int need) {
+        if (xin)
+            wait_flag_gpu(prog, need, &sh_err);
+        else
+            wait_flag(prog, need, &sh_err);
+    };
     auto stage_first = [&](const int* prog, int ordinal, int rb, bool reader) {
-        wait_flag(prog, (ordinal << 16) + 3, &sh_err);
+        wait_prog(prog, (ordinal << 16) + 3);
         if (reader) {
             copy_stage(ordinal, 1, rb);
             copy_stage(ordinal, 2, rb);
         }
     };
     auto stage_need = [&](const int* prog, int ordinal, int k, int rb, bool reader) {
-        wait_flag(prog, (ordinal << 16) + min(k + 4, kStageMask), &sh_err);
+        wait_prog(prog, (ordinal << 16) + min(k + 4, kStageMask));
         if (reader) copy_stage(ordinal, k + 3, rb);
     };
     // past its last stage a row-block's neighbour reads up to 48 steps and 12
@@ -675,7 +692,9 @@ __global__ void __launch_bounds__(kNW * 32, 1) lin_tan_kernel(SwArgs p) {
     V.E = 0.f;
     V.ebmin = V.ebmax = 0x3f800000;
     V.emax = 0.f;
-    for (int r = warp; r < nRB; r += kNW) {
+    const int* const prodF = xin ? gsync + pin : &progF[wprev];
+    const int* const prodR = xin ? gsync + kMaxParts + pin : &progR[wprev];
+    for (int r = gw; r < nRB; r += NWt) {
         const int nv = min(32, L1 - 32 * r);
         const int nst = (L2 + nv - 1 + kCW - 1) / kCW;
         const bool hasB = r > 0, hasD = r + 1 < nRB;
@@ -709,13 +728,13 @@ __global__ void __launch_bounds__(kNW * 32, 1) lin_tan_kernel(SwArgs p) {
             tile_load<4>(tS, 0, L2);
             if (HV && !DOT) tile_load<4>(tV, 0, L2);
         }
-        if (hasB) stage_first(&progF[wprev], r - 1, r - 1, lane == 0);
+        if (hasB) stage_first(prodF, r - 1, r - 1, lane == 0);
         cp_async_commit();
         V.zl = V.zd = V.zsh = V.dzl = V.dzd = V.dzsh = 0.f;
         V.f.d1 = 0.f;
         for (int k = 0; k < nst; ++k) {
             __syncwarp();
-            if (hasB) stage_need(&progF[wprev], r - 1, k, r - 1, lane == 0);
+            if (hasB) stage_need(prodF, r - 1, k, r - 1, lane == 0);
             cp_async_commit();
             if (k + 1 < nch) {
                 tile_load<4>(tS, k + 1, L2);
@@ -725,7 +744,7 @@ __global__ void __launch_bounds__(kNW * 32, 1) lin_tan_kernel(SwArgs p) {
             cp_async_wait2();  // everything but this stage's two groups
             __syncwarp();
             V.push = false;
-            if (lane == 31 && hasD) {  // sw_linear.cu's push rule
+            if (lane == 31 && hasD && !xout) {  // sw_linear.cu's push rule
                 const int cw = ld_acquire(&progF[wnext]);
                 V.push = (cw >> 16) == r + 1 && (cw & kStageMask) + 8 >= k;
             }
@@ -743,7 +762,10 @@ __global__ void __launch_bounds__(kNW * 32, 1) lin_tan_kernel(SwArgs p) {
             acc_rebase2(V);
             if (V.push) Wn.tag[k & (kHR / 16 - 1)] = (r << 16) | k;
             __syncwarp();
-            if (lane == 31) st_release(&progF[warp], (r << 16) | min(k + 1, kStageMask - 1));
+            if (lane == 31) {
+                st_release(&progF[warp], (r << 16) | min(k + 1, kStageMask - 1));
+                if (xout) st_release_gpu(gsync + part, (r << 16) | min(k + 1, kStageMask - 1));
+            }
         }
         {
             const double sc = p2d(V.E - V.ab);
@@ -755,7 +777,10 @@ __global__ void __launch_bounds__(kNW * 32, 1) lin_tan_kernel(SwArgs p) {
         if (lane == 31) write_tail(C.ov, C.odv, C.of, nst, V.E);
         cp_async_wait0();
         __syncwarp();
-        if (lane == 31) st_release(&progF[warp], (r << 16) | kStageMask);
+        if (lane == 31) {
+            st_release(&progF[warp], (r << 16) | kStageMask);
+            if (xout) st_release_gpu(gsync + part, (r << 16) | kStageMask);
+        }
     }
     const int fwd_out = ((V.ebmin < ((127 - kJMax) << 23) || V.ebmax > ((127 + kJMax) << 23)) ? 1 : 0) |
                         (V.emax > 1000.f ? 8 : 0);
@@ -764,11 +789,37 @@ __global__ void __launch_bounds__(kNW * 32, 1) lin_tan_kernel(SwArgs p) {
     // ---- S (integer + fraction) and dZ_total / Z_total
     {
         float* redf = reinterpret_cast<float*>(red);
-        const float abmax = block_max(V.ab, redf);
-        const double scl = p2d(V.ab - abmax);
-        const double tot = block_sum_d(V.acc * scl, red) + p2d(-abmax);  // alpha[0,0] = 0
-        const double dtot = block_sum_d(V.dacc * scl, red);
+        const float abl = block_max(V.ab, redf);
+        const double scl = p2d(V.ab - abl);
+        const double totl = block_sum_d(V.acc * scl, red);
+        const double dtotl = block_sum_d(V.dacc * scl, red);
         if (threadIdx.x == 0) {
+            float abmax = abl;
+            double tot = totl, dtot = dtotl;
+            if (SPLIT && K > 1) {  // every part's partials, after every part's forward
+                double* const g = gpart + kSyncPartDoubles * part;
+                g[0] = (double)abl;
+                g[1] = totl;
+                g[2] = dtotl;
+                atom_add_release_gpu(gsync + 2 * kMaxParts, 1);
+                int it = 0;
+                while (ld_acquire_gpu(gsync + 2 * kMaxParts) < K) {
+                    if (++it > kSpinLimit) {
+                        sh_err = 1;
+                        break;
+                    }
+                    __nanosleep(64);
+                }
+                abmax = -3.0e38f;
+                for (int k = 0; k < K; ++k) abmax = fmaxf(abmax, (float)gpart[kSyncPartDoubles * k]);
+                tot = dtot = 0.0;
+                for (int k = 0; k < K; ++k) {
+                    const double sk = p2d((float)gpart[kSyncPartDoubles * k] - abmax);
+                    tot = fma(gpart[kSyncPartDoubles * k + 1], sk, tot);
+                    dtot = fma(gpart[kSyncPartDoubles * k + 2], sk, dtot);
+                }
+            }
+            tot += p2d(-abmax);  // alpha[0,0] = 0
             const int hi = __double2hiint(tot);
             const int ef = (hi >> 20) & 0x7ff;
             const bool fin = ef != 0x7ff && ef != 0;
@@ -789,7 +840,7 @@ __global__ void __launch_bounds__(kNW * 32, 1) lin_tan_kernel(SwArgs p) {
     RV.ebmin = RV.ebmax = 0x3f800000;
     RV.chk = 0.f;
     RV.dot = 0.0;
-    for (int q = warp; q < nRB; q += kNW) {
+    for (int q = gw; q < nRB; q += NWt) {
         const int r = nRB - 1 - q;
         const int nv = min(32, L1 - 32 * r);
         const bool hasBelow = r + 1 < nRB, hasAbove = r > 0;
@@ -858,7 +909,7 @@ __global__ void __launch_bounds__(kNW * 32, 1) lin_tan_kernel(SwArgs p) {
             for (int ch = M0; ch >= M0 - 2; --ch) loads(ch);
         }
         batch(0);
-        if (hasBelow) stage_first(&progR[wprev], q - 1, r + 1, lane == nv - 1);
+        if (hasBelow) stage_first(prodR, q - 1, r + 1, lane == nv - 1);
         cp_async_commit();
 
         RV.br = RV.pbp = RV.rsh = RV.dbr = RV.dpbp = RV.drsh = 0.f;
@@ -868,7 +919,7 @@ __global__ void __launch_bounds__(kNW * 32, 1) lin_tan_kernel(SwArgs p) {
         for (int k = 0; k < nstR; ++k) {
             const int M = P / kCW + 1 - k;
             __syncwarp();
-            if (hasBelow) stage_need(&progR[wprev], q - 1, k, r + 1, lane == nv - 1);
+            if (hasBelow) stage_need(prodR, q - 1, k, r + 1, lane == nv - 1);
             cp_async_commit();
             if (out && M + 1 < nch && M + 1 >= 0) tile_store(tM, M + 1, L2);  // no lane touches it any more
             loads(M - 3);                                                    // for stage k + 1
@@ -877,7 +928,7 @@ __global__ void __launch_bounds__(kNW * 32, 1) lin_tan_kernel(SwArgs p) {
             cp_async_wait2();
             __syncwarp();
             RV.push = false;
-            if (lane == 0 && hasAbove) {
+            if (lane == 0 && hasAbove && !xout) {
                 const int cw = ld_acquire(&progR[wnext]);
                 RV.push = (cw >> 16) == q + 1 && (cw & kStageMask) + 8 >= k;
             }
@@ -892,14 +943,20 @@ __global__ void __launch_bounds__(kNW * 32, 1) lin_tan_kernel(SwArgs p) {
             if (DOT) RV.dot += (double)RV.sdot;
             if (RV.push) Wn.tag[k & (kHR / 16 - 1)] = (q << 16) | k;
             __syncwarp();
-            if (lane == 0) st_release(&progR[warp], (q << 16) | min(k + 1, kStageMask - 1));
+            if (lane == 0) {
+                st_release(&progR[warp], (q << 16) | min(k + 1, kStageMask - 1));
+                if (xout) st_release_gpu(gsync + kMaxParts + part, (q << 16) | min(k + 1, kStageMask - 1));
+            }
         }
         if (lane == 0) write_tail(C.ov, C.odv, C.of, nstR, RV.Q);
         __syncwarp();
         if (out && nch > 0) tile_store(tM, 0, L2);  // the last stage had M = 0
         cp_async_wait0();
         __syncwarp();
-        if (lane == 0) st_release(&progR[warp], (q << 16) | kStageMask);
+        if (lane == 0) {
+            st_release(&progR[warp], (q << 16) | kStageMask);
+            if (xout) st_release_gpu(gsync + kMaxParts + part, (q << 16) | kStageMask);
+        }
     }
 
     // a frame step outside the window, a partition or a tangent that is not
@@ -912,9 +969,26 @@ __global__ void __launch_bounds__(kNW * 32, 1) lin_tan_kernel(SwArgs p) {
     const int redo = (o_win ? 1 : 0) | (sh_err ? 2 : 0) | (sh_bad ? 4 : 0) | (o_acc ? 8 : 0) | (o_tan ? 16 : 0);
     if (DOT) {
         const double tot = block_sum_d(RV.dot, red);
-        if (threadIdx.x == 0 && p.dot_out) p.dot_out[b] = (float)tot;
+        if (threadIdx.x == 0) {
+            if (SPLIT && K > 1) {  // the last part to arrive sums the parts in order
+                gpart[kSyncPartDoubles * part + 3] = tot;
+                if (atom_add_release_gpu(gsync + 2 * kMaxParts + 1, 1) == K - 1) {
+                    (void)ld_acquire_gpu(gsync + 2 * kMaxParts + 1);
+                    double all = 0.0;
+                    for (int k = 0; k < K; ++k) all += gpart[kSyncPartDoubles * k + 3];
+                    if (p.dot_out) p.dot_out[b] = (float)all;
+                }
+            } else if (p.dot_out) {
+                p.dot_out[b] = (float)tot;
+            }
+        }
     }
-    if (threadIdx.x == 0 && p.redo) p.redo[b] = redo;
+    if (threadIdx.x == 0 && p.redo) {
+        if (SPLIT)
+            atomicOr(p.redo + b, redo);  // zeroed by the launcher
+        else
+            p.redo[b] = redo;
+    }
 }
 
 }  // namespace ltan
@@ -943,23 +1017,49 @@ int launch_lin_tan(const SwArgs& a, size_t ws_bytes, cudaStream_t st) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return (int)e;
+    static int sms[64] = {0};
     static bool attr_set[64] = {false};
     if (dev < 64 && !attr_set[dev]) {
-        const void* ks[3] = {(const void*)ltan::lin_tan_kernel<true, false>,
-                             (const void*)ltan::lin_tan_kernel<false, false>,
-                             (const void*)ltan::lin_tan_kernel<true, true>};
+        const void* ks[6] = {(const void*)ltan::lin_tan_kernel<true, false, false>,
+                             (const void*)ltan::lin_tan_kernel<false, false, false>,
+                             (const void*)ltan::lin_tan_kernel<true, true, false>,
+                             (const void*)ltan::lin_tan_kernel<true, false, true>,
+                             (const void*)ltan::lin_tan_kernel<false, false, true>,
+                             (const void*)ltan::lin_tan_kernel<true, true, true>};
         for (const void* k : ks) {
             e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e == cudaSuccess)
+                e = cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                         (int)cudaSharedmemCarveoutMaxShared);
             if (e != cudaSuccess) return (int)e;
         }
+        e = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return (int)e;
         attr_set[dev] = true;
     }
+    // few large problems: several CTAs per problem (sw_linear.cu's rule, with
+    // this kernel's 6 warps per CTA)
+    const int K = (dev < 64 && a.sync) ? lin_parts_nw(a.B, a.L1, a.L2, sms[dev], ltan::kNW) : 1;
+    if (K > 1) {
+        SwArgs s = a;
+        s.parts = K;
+        e = cudaMemsetAsync(s.sync, 0, kSyncBytes * (size_t)a.B, st);
+        if (e == cudaSuccess) e = cudaMemsetAsync(s.redo, 0, sizeof(int) * (size_t)a.B, st);
+        if (e != cudaSuccess) return (int)e;
+        void* args[1] = {&s};
+        const void* k = dot  ? (const void*)ltan::lin_tan_kernel<true, true, true>
+                        : hv ? (const void*)ltan::lin_tan_kernel<true, false, true>
+                             : (const void*)ltan::lin_tan_kernel<false, false, true>;
+        e = cudaLaunchCooperativeKernel(k, dim3(a.B * K), dim3(ltan::kNW * 32), args, smem, st);
+        if (e == cudaSuccess) return 0;
+        cudaGetLastError();  // does not fit: one CTA per problem instead
+    }
     if (dot)
-        ltan::lin_tan_kernel<true, true><<<a.B, ltan::kNW * 32, smem, st>>>(a);
+        ltan::lin_tan_kernel<true, true, false><<<a.B, ltan::kNW * 32, smem, st>>>(a);
     else if (hv)
-        ltan::lin_tan_kernel<true, false><<<a.B, ltan::kNW * 32, smem, st>>>(a);
+        ltan::lin_tan_kernel<true, false, false><<<a.B, ltan::kNW * 32, smem, st>>>(a);
     else
-        ltan::lin_tan_kernel<false, false><<<a.B, ltan::kNW * 32, smem, st>>>(a);
+        ltan::lin_tan_kernel<false, false, false><<<a.B, ltan::kNW * 32, smem, st>>>(a);
     return (int)cudaGetLastError();
 }
 

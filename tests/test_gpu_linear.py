@@ -145,6 +145,33 @@ def test_tangent_backward_full(d2p, cuda_device, B, L1, L2, T, gap, ragged):
     check("grad_T", gt, r64[2], r32[2], rtol=1e-4, atol=1e-4)
 
 
+@pytest.mark.parametrize("B,L1,L2", [(2, 1024, 512), (1, 2048, 256)])
+def test_tangent_spread_over_ctas(d2p, cuda_device, B, L1, L2):
+    """Few problems with many row-blocks: the tangent sweeps run each problem on
+    several CTAs (cooperative launch), the partition's tangent and the dot-mode
+    sums combined across them.  HVP, both Jacobians and backward_full against
+    the oracle; repeat bitwise."""
+    s = scores(B, L1, L2, seed=71)
+    V = scores(B, L1, L2, seed=72)
+    sd, Vd = s.to(cuda_device), V.to(cuda_device)
+    H = torch.ops.d2p.soft_sw_hvp(sd, Vd, -1.0, 1.0, None)
+    assert torch.equal(H, torch.ops.d2p.soft_sw_hvp(sd, Vd, -1.0, 1.0, None))
+    h64 = oracle.sw_linear_hvp(s.numpy(), V.numpy(), None, -1.0, 1.0, "f64")
+    h32 = oracle.sw_linear_hvp(s.numpy(), V.numpy(), None, -1.0, 1.0, "f32")
+    check("hvp", H, h64, h32, rtol=1e-4, atol=1e-5)
+    for pt in (0, 1):
+        J = torch.ops.d2p.soft_sw_param_jacobian(sd, pt, -1.0, 1.0, None)
+        j64 = oracle.sw_linear_param_jacobian(s.numpy(), pt, None, -1.0, 1.0, "f64")
+        j32 = oracle.sw_linear_param_jacobian(s.numpy(), pt, None, -1.0, 1.0, "f32")
+        check(f"jac{pt}", J, j64, j32, rtol=1e-4, atol=1e-5)
+    gs, gg, gt = torch.ops.d2p.soft_sw_backward_full(sd, Vd, -1.0, 1.0, None)
+    r64 = oracle.sw_linear_backward_full(s.numpy(), V.numpy(), None, -1.0, 1.0, "f64")
+    r32 = oracle.sw_linear_backward_full(s.numpy(), V.numpy(), None, -1.0, 1.0, "f32")
+    check("grad_scores", gs, r64[0], r32[0], rtol=1e-4, atol=1e-5)
+    check("grad_gap", gg, r64[1], r32[1], rtol=1e-4, atol=1e-4)
+    check("grad_T", gt, r64[2], r32[2], rtol=1e-4, atol=1e-4)
+
+
 def test_autograd_value_sum(d2p, cuda_device):
     s = scores(4, 30, 41, seed=21).to(cuda_device).requires_grad_(True)
     res = d2p.soft_sw(s, gap=-1.0, temperature=1.0)
