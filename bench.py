@@ -322,6 +322,35 @@ def run_ours(args, cfg):
         "step_frac": round((max(t_hbm, t_mufu) + (8.0 * padded) / (hbm_gbs * 1e9)) / (ms_max * 1e-3), 4),
     }
 
+    # ---------------- Hessian-vector product (BASELINE config 5 reports it) ----------------
+    hvp = None
+    if fam == "linear" and (args.hvp or args.config == "c5"):
+        gv = torch.Generator().manual_seed(2 + 1000 * rank)
+        v_dev = torch.randn(s_host.shape, generator=gv).to(dev)
+        with torch.no_grad():
+            def hvp_step():
+                return torch.ops.d2p.soft_sw_hvp(s_dev, v_dev, gap, T, len_dev)
+            for _ in range(2):
+                hvp_step()
+            barrier()
+            h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            h0.record()
+            for _ in range(nk):
+                hvp_step()
+            h1.record()
+            barrier()
+            h_ms = h0.elapsed_time(h1) / nk
+        th = torch.tensor([h_ms], device=dev)
+        if world > 1:
+            dist.all_reduce(th, op=dist.ReduceOp.MAX)
+        h_ms = float(th.item())
+        # convention: 12 B (scores, V, H) and 10 MUFU per valid cell
+        h_bound = max(12.0 * cells / (hbm_gbs * 1e9), 10.0 * cells / mufu_peak)
+        hvp = {"value": round(total_cells / (h_ms * 1e-3) / 1e9, 3), "unit": "GCUPS", "ms_per_step": round(h_ms, 4),
+               "kernel": "ltan::lin_tan_kernel (d2p_sw_hvp)", "time_bound_ms": round(h_bound * 1e3, 4),
+               "frac": round(h_bound / (h_ms * 1e-3), 4)}
+        del v_dev
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(cfg, args.cpu_seconds)
@@ -342,12 +371,17 @@ def run_ours(args, cfg):
                        "parallelism": f"batch x{world} (one process per GPU), NCCL all_gather of values"},
             "e2e": {"value": round(e2e_gcups, 3), "unit": "GCUPS", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": cfg["B"] * 4, "ms_per_step": round(e2e_ms, 4)},
-            "gpu_launches": args.steps * 4,
+            # per step: the value+marginals kernel, its two (empty) fix-up
+            # launches, the backward's elementwise kernel; ragged batches of more
+            # than two problems per SM add the CTA-order kernel
+            "gpu_launches": args.steps * (5 if (lengths is not None and cfg["B"] > 2 * sm_count) else 4),
             "roofline": roofline,
             "clocks": clk,
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
+        if hvp is not None:
+            line["hvp"] = hvp
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
@@ -471,6 +505,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     ap.add_argument("--ref-step-seconds", type=float, default=6.0)
     ap.add_argument("--batch", type=int, default=0, help="override the per-rank batch (profiling on a small case)")
+    ap.add_argument("--hvp", action="store_true",
+                    help="also time the Hessian-vector product (linear family; on by default for c5)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -49,10 +49,9 @@ static size_t plane_bytes(int family, int mode, int B, int L1, int L2) {
 // (linear family, covered shapes) or the plane engine's, whichever is larger
 static size_t tan_area(int family, int op, int B, int L1, int L2) {
     size_t pe = plane_bytes(family, op == D2P_OP_HVP ? MODE_HVP : MODE_PT, B, L1, L2);
-    if (family == D2P_FAMILY_LINEAR) {
-        const size_t tf = lin_tan_workspace_bytes(B, L1, L2);
-        pe = pe > tf ? pe : tf;
-    }
+    const size_t tf = family == D2P_FAMILY_LINEAR ? lin_tan_workspace_bytes(B, L1, L2)
+                                                  : aff_tan_workspace_bytes(B, L1, L2);
+    pe = pe > tf ? pe : tf;
     return align256(pe);
 }
 
@@ -186,22 +185,23 @@ int d2p_sw_forward_backward(const float* scores, const int* lengths, int B, int 
     return launch_lin_plane(a, st);
 }
 
-// One tangent op on the linear family: the linear-domain tangent kernel, then
-// the plane engine for the problems it flagged (or for all, if the shape is not
-// covered).  flags: the op's per-problem flag array in the workspace.
-static int run_lin_tangent(SwArgs a, size_t ws_bytes, int* flags, cudaStream_t st) {
+// One tangent op: the linear-domain tangent kernel of the family, then the
+// plane engine for the problems it flagged (or for all, if the shape is not
+// covered).  flags: the op's per-problem flag array in the workspace, followed
+// by the cross-CTA words.
+static int run_tangent(int family, SwArgs a, size_t ws_bytes, int* flags, cudaStream_t st) {
     a.redo = flags;
     a.only = nullptr;
     a.sync = (int*)((char*)flags + align256((size_t)a.B * sizeof(int)));
-    int rc = launch_lin_tan(a, ws_bytes, st);
+    int rc = family == D2P_FAMILY_LINEAR ? launch_lin_tan(a, ws_bytes, st) : launch_aff_tan(a, ws_bytes, st);
     a.redo = nullptr;
     a.sync = nullptr;
-    if (rc == D2P_OK) {
-        a.only = flags;
-        return launch_lin_plane(a, st);
-    }
-    if (rc != kNotHandled) return rc;
-    return launch_lin_plane(a, st);
+    if (rc == D2P_OK) a.only = flags;
+    else if (rc != kNotHandled) return rc;
+    return family == D2P_FAMILY_LINEAR ? launch_lin_plane(a, st) : launch_aff_plane(a, st);
+}
+static int run_lin_tangent(SwArgs a, size_t ws_bytes, int* flags, cudaStream_t st) {
+    return run_tangent(D2P_FAMILY_LINEAR, a, ws_bytes, flags, st);
 }
 
 int d2p_sw_hvp(const float* scores, const float* tangent, const int* lengths, int B, int L1,
@@ -378,7 +378,8 @@ int d2p_sw_affine_hvp(const float* scores, const float* tangent, const int* leng
     a.mode = MODE_HVP;
     a.out = hvp;
     a.ws = (float*)workspace;
-    return launch_aff_plane(a, (cudaStream_t)stream);
+    int* flags = (int*)((char*)workspace + tan_area(D2P_FAMILY_AFFINE, D2P_OP_HVP, B, L1, L2));
+    return run_tangent(D2P_FAMILY_AFFINE, a, workspace_bytes, flags, (cudaStream_t)stream);
 }
 
 int d2p_sw_affine_param_jacobian(const float* scores, const int* lengths, int B, int L1, int L2,
@@ -398,7 +399,8 @@ int d2p_sw_affine_param_jacobian(const float* scores, const int* lengths, int B,
     a.mode = param_type == 0 ? MODE_PGAP : (param_type == 1 ? MODE_PGE : MODE_PT);
     a.out = jacobian;
     a.ws = (float*)workspace;
-    return launch_aff_plane(a, (cudaStream_t)stream);
+    int* flags = (int*)((char*)workspace + tan_area(D2P_FAMILY_AFFINE, D2P_OP_PARAM_JACOBIAN, B, L1, L2));
+    return run_tangent(D2P_FAMILY_AFFINE, a, workspace_bytes, flags, (cudaStream_t)stream);
 }
 
 int d2p_sw_affine_backward_full(const float* scores, const float* grad_marginals,
@@ -420,8 +422,10 @@ int d2p_sw_affine_backward_full(const float* scores, const float* grad_marginals
         }
         return D2P_OK;
     }
+    const size_t area = tan_area(D2P_FAMILY_AFFINE, D2P_OP_BACKWARD_FULL, B, L1, L2);
     float* planes = (float*)workspace;
-    float* partials = (float*)((char*)workspace + plane_bytes(D2P_FAMILY_AFFINE, MODE_PT, B, L1, L2));
+    float* partials = (float*)((char*)workspace + area);
+    int* flags = (int*)((char*)partials + align256((size_t)4 * B * sizeof(float)));
     SwArgs a = base_args(scores, lengths, B, L1, L2);
     a.gap = gap_open;
     a.gap2 = gap_ext;
@@ -430,7 +434,7 @@ int d2p_sw_affine_backward_full(const float* scores, const float* grad_marginals
     a.tangent = grad_marginals;
     a.mode = MODE_HVP;
     a.out = grad_scores;
-    int rc = launch_aff_plane(a, st);
+    int rc = run_tangent(D2P_FAMILY_AFFINE, a, workspace_bytes, flags, st);
     if (rc) return rc;
     a.tangent = nullptr;
     a.out = nullptr;
@@ -440,7 +444,7 @@ int d2p_sw_affine_backward_full(const float* scores, const float* grad_marginals
     for (int q = 0; q < 3; ++q) {
         a.mode = modes[q];
         a.dot_out = partials + (size_t)q * B;
-        rc = launch_aff_plane(a, st);
+        rc = run_tangent(D2P_FAMILY_AFFINE, a, workspace_bytes, flags, st);
         if (rc) return rc;
         rc = launch_sum_batches(partials + (size_t)q * B, 1, B, outs[q], 0, st);
         if (rc) return rc;

@@ -98,6 +98,10 @@ bool engine_forced_plane();
 // dot mode (dot_with / dot_out) of the param modes; sets redo[b] for problems
 // the plane engine must recompute.  Returns -1 when the shape is not covered.
 size_t lin_tan_workspace_bytes(int B, int L1, int L2);
+// the affine counterpart (sw_affine_tangent.cu): HVP, dP/d(gap_open),
+// dP/d(gap_ext), dP/dT and their dot mode
+size_t aff_tan_workspace_bytes(int B, int L1, int L2);
+int launch_aff_tan(const SwArgs& a, size_t ws_bytes, cudaStream_t st);
 // CTAs per problem for B problems of nw warps per CTA, one CTA per SM (the
 // row-block pipeline model; 1 = one CTA per problem)
 int lin_parts_nw(int B, int L1, int L2, int sms, int nw);

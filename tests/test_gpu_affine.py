@@ -87,6 +87,60 @@ def test_backward_full(d2p, cuda_device, B, L1, L2, T, go, ge):
         check(f"grad_param{k}", out[k], r64[k], r32[k], rtol=1e-4, atol=1e-4)
 
 
+# Shapes routed to the affine linear-domain tangent kernel (L2 % 4 == 0).
+ATAN = [  # (B, L1, L2, T, gap_open, gap_ext, ragged)
+    (2, 33, 64, 1.0, -2.0, -0.5, False), (3, 100, 36, 0.5, -2.0, -0.5, False),
+    (2, 130, 260, 1.0, -1.7, -0.4, False), (1, 200, 8, 1.0, -2.0, -0.5, False),
+    (4, 70, 96, 1.0, -2.0, -0.5, True), (1, 1024, 256, 1.0, -2.0, -0.5, False),
+]
+
+
+def _atan_inputs(B, L1, L2, ragged, seed):
+    s = scores(B, L1, L2, seed=seed)
+    ln = lengths_for(B, L1, L2, seed=seed + 1) if ragged else None
+    if ln is not None:
+        ln[0] = torch.tensor([L1, L2], dtype=torch.int32)
+    return s, ln
+
+
+@pytest.mark.parametrize("B,L1,L2,T,go,ge,ragged", ATAN)
+def test_tangent_hvp(d2p, cuda_device, B, L1, L2, T, go, ge, ragged):
+    s, ln = _atan_inputs(B, L1, L2, ragged, 81)
+    V = scores(B, L1, L2, seed=82)
+    lnd = None if ln is None else ln.to(cuda_device)
+    H = torch.ops.d2p.soft_sw_affine_hvp(s.to(cuda_device), V.to(cuda_device), go, ge, T, lnd)
+    lnp = None if ln is None else ln.numpy()
+    h64 = oracle.sw_affine_hvp(s.numpy(), V.numpy(), lnp, go, ge, T, "f64")
+    h32 = oracle.sw_affine_hvp(s.numpy(), V.numpy(), lnp, go, ge, T, "f32")
+    check("hvp", H, h64, h32, rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.parametrize("param_type", [0, 1, 2])
+@pytest.mark.parametrize("B,L1,L2,T,go,ge,ragged", ATAN)
+def test_tangent_param_jacobian(d2p, cuda_device, B, L1, L2, T, go, ge, ragged, param_type):
+    s, ln = _atan_inputs(B, L1, L2, ragged, 83)
+    lnd = None if ln is None else ln.to(cuda_device)
+    J = torch.ops.d2p.soft_sw_affine_param_jacobian(s.to(cuda_device), param_type, go, ge, T, lnd)
+    lnp = None if ln is None else ln.numpy()
+    j64 = oracle.sw_affine_param_jacobian(s.numpy(), param_type, lnp, go, ge, T, "f64")
+    j32 = oracle.sw_affine_param_jacobian(s.numpy(), param_type, lnp, go, ge, T, "f32")
+    check(f"jac{param_type}", J, j64, j32, rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.parametrize("B,L1,L2,T,go,ge,ragged", ATAN)
+def test_tangent_backward_full(d2p, cuda_device, B, L1, L2, T, go, ge, ragged):
+    s, ln = _atan_inputs(B, L1, L2, ragged, 85)
+    Gm = scores(B, L1, L2, seed=86)
+    lnd = None if ln is None else ln.to(cuda_device)
+    out = torch.ops.d2p.soft_sw_affine_backward_full(s.to(cuda_device), Gm.to(cuda_device), go, ge, T, lnd)
+    lnp = None if ln is None else ln.numpy()
+    r64 = oracle.sw_affine_backward_full(s.numpy(), Gm.numpy(), lnp, go, ge, T, "f64")
+    r32 = oracle.sw_affine_backward_full(s.numpy(), Gm.numpy(), lnp, go, ge, T, "f32")
+    check("grad_scores", out[0], r64[0], r32[0], rtol=1e-4, atol=1e-5)
+    for k in range(1, 4):
+        check(f"grad_param{k}", out[k], r64[k], r32[k], rtol=1e-4, atol=1e-4)
+
+
 def test_bf16_scores(d2p, cuda_device):
     s = scores(3, 40, 50, seed=12).to(torch.bfloat16)
     res = d2p.soft_sw_affine(s.to(cuda_device), gap_open=-2.0, gap_ext=-0.5, temperature=1.0)
