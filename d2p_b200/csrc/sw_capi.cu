@@ -65,8 +65,10 @@ static size_t op_bytes(int family, int op, int B, int L1, int L2) {
                                                           : aff_fast_workspace_bytes(B, L1, L2, true);
             if (wf == 0) return pe;
             const size_t lf = family == D2P_FAMILY_LINEAR ? lin_fast_workspace_bytes(B, L1, L2) : 0;
+            const size_t tf = family == D2P_FAMILY_LINEAR ? lin_tan_workspace_bytes(B, L1, L2) : 0;
             pe = pe > wf ? pe : wf;
             pe = pe > lf ? pe : lf;
+            pe = pe > tf ? pe : tf;
             // flags, the CTA order of ragged batches, the cross-CTA words of
             // problems spread over several CTAs
             return align256(pe) + 2 * align256((size_t)(B > 0 ? B : 1) * sizeof(int)) +
@@ -150,12 +152,15 @@ int d2p_sw_forward_backward(const float* scores, const int* lengths, int B, int 
     size_t pe = plane_bytes(D2P_FAMILY_LINEAR, MODE_MARG, B, L1, L2);
     const size_t wf = wavefront_workspace_bytes(D2P_FAMILY_LINEAR, B, L1, L2);
     const size_t lf = lin_fast_workspace_bytes(B, L1, L2);
+    const size_t tf = lin_tan_workspace_bytes(B, L1, L2);
     if (wf > 0) {
         // Fast paths, each recomputing what the previous one flagged:
-        //   linear-domain kernel (no parameter gradients requested) ->
-        //   log-domain wavefront kernel -> plane engine.
+        //   linear-domain kernel (value + marginals: sw_linear.cu; with
+        //   parameter gradients: the tangent kernel's gap sweep, sw_tangent.cu,
+        //   for batches of one wave) -> log-domain wavefront kernel -> plane engine.
         pe = pe > wf ? pe : wf;
         pe = pe > lf ? pe : lf;
+        pe = pe > tf ? pe : tf;
         int* flags = (int*)((char*)workspace + align256(pe));
         int* order = (int*)((char*)flags + align256((size_t)B * sizeof(int)));
         a.redo = flags;
@@ -167,7 +172,8 @@ int d2p_sw_forward_backward(const float* scores, const int* lengths, int B, int 
             if (ro == D2P_OK) a.order = order;
             else if (ro != kNotHandled) return ro;
         }
-        int rc = launch_lin_fast(a, workspace_bytes, st);
+        int rc = (grad_gap || grad_temperature) ? launch_lin_tan(a, workspace_bytes, st)
+                                                : launch_lin_fast(a, workspace_bytes, st);
         a.order = nullptr;
         a.sync = nullptr;
         if (rc == D2P_OK) a.only = flags;
@@ -301,6 +307,19 @@ int d2p_sw_value_backward(const float* grad_value, const float* marginals,
     if (n_params > 0 && (!dvalue_dparams || !grad_params)) return D2P_ERR_INVALID_ARGUMENT;
     return launch_value_backward(grad_value, marginals, dvalue_dparams, n_params, B, L1, L2,
                                  grad_scores, grad_params, (cudaStream_t)stream);
+}
+int d2p_sw_value_backward_lengths(const float* grad_value, const float* marginals, const int* lengths,
+                                  const float* dvalue_dparams, int n_params, int B, int L1, int L2,
+                                  float* grad_scores, float* grad_params, void* stream) {
+    if (!lengths || B <= 0)
+        return d2p_sw_value_backward(grad_value, marginals, dvalue_dparams, n_params, B, L1, L2, grad_scores,
+                                     grad_params, stream);
+    if (L1 < 0 || L2 < 0 || n_params < 0) return D2P_ERR_INVALID_ARGUMENT;
+    if (!grad_value || (!marginals && L1 > 0 && L2 > 0) || (!grad_scores && L1 > 0 && L2 > 0))
+        return D2P_ERR_INVALID_ARGUMENT;
+    if (n_params > 0 && (!dvalue_dparams || !grad_params)) return D2P_ERR_INVALID_ARGUMENT;
+    return launch_value_backward_rows(grad_value, marginals, lengths, dvalue_dparams, n_params, B, L1, L2,
+                                      grad_scores, grad_params, (cudaStream_t)stream);
 }
 
 // ---------------------------------------------------------------- affine

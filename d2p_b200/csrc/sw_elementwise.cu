@@ -48,6 +48,54 @@ __global__ void __launch_bounds__(256) value_backward_kernel(const float* __rest
     }
 }
 
+// The same with per-problem lengths: one warp per row; cells outside the
+// problem (marginals 0 there) are written as 0 without being read, which saves
+// the read of a ragged batch's padding.
+__global__ void __launch_bounds__(256) value_backward_rows_kernel(const float* __restrict__ g,
+                                                                  const float* __restrict__ marg,
+                                                                  const int* __restrict__ lengths, int B, int L1,
+                                                                  int L2, float* __restrict__ out,
+                                                                  const float* __restrict__ dparams, int n_params,
+                                                                  float* __restrict__ gparams) {
+    const int lane = threadIdx.x & 31;
+    const long long rows = (long long)B * L1;
+    const long long w0 = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const long long nw = ((long long)gridDim.x * blockDim.x) >> 5;
+    const bool vec = (L2 & 3) == 0 && ((((uintptr_t)marg) | ((uintptr_t)out)) & 15) == 0;
+    for (long long row = w0; row < rows; row += nw) {
+        const int b = (int)(row / L1), i = (int)(row - (long long)b * L1);
+        const int l1 = min(max(lengths[2 * b], 0), L1), l2 = min(max(lengths[2 * b + 1], 0), L2);
+        const int valid = i < l1 ? l2 : 0;  // columns [0, valid) hold marginals
+        const float gb = __ldg(g + b);
+        const size_t base = (size_t)row * L2;
+        if (vec) {
+            const float4* __restrict__ m4 = reinterpret_cast<const float4*>(marg + base);
+            float4* __restrict__ o4 = reinterpret_cast<float4*>(out + base);
+            for (int c = lane; c < (L2 >> 2); c += 32) {
+                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (4 * c < valid) {
+                    v = __ldcs(m4 + c);
+                    v.x *= gb;
+                    v.y = 4 * c + 1 < valid ? v.y * gb : 0.f;
+                    v.z = 4 * c + 2 < valid ? v.z * gb : 0.f;
+                    v.w = 4 * c + 3 < valid ? v.w * gb : 0.f;
+                }
+                __stcs(o4 + c, v);
+            }
+        } else {
+            for (int c = lane; c < L2; c += 32) out[base + c] = c < valid ? gb * marg[base + c] : 0.f;
+        }
+    }
+    if (blockIdx.x == 0 && threadIdx.x < 32 && n_params > 0 && gparams) {  // as value_backward_kernel
+        for (int pi = 0; pi < n_params; ++pi) {
+            float acc = 0.f;
+            for (int b = threadIdx.x; b < B; b += 32) acc += g[b] * dparams[(size_t)pi * B + b];
+            acc = warp_sum(acc);
+            if (threadIdx.x == 0) gparams[pi] = acc;
+        }
+    }
+}
+
 // out[p] (+)= sum_b partials[p*B + b], deterministic (one warp).
 __global__ void sum_batches_kernel(const float* __restrict__ partials, int P, int B,
                                    float* __restrict__ out, int accumulate) {
@@ -70,6 +118,18 @@ static int grid_for(size_t work_items) {
     if (want > cap) want = cap;
     if (want < 1) want = 1;
     return (int)want;
+}
+
+int launch_value_backward_rows(const float* grad_value, const float* marginals, const int* lengths,
+                               const float* dparams, int n_params, int B, int L1, int L2,
+                               float* grad_scores, float* grad_params, cudaStream_t st) {
+    if (!lengths || (long long)B * L1 == 0 || L2 == 0)
+        return launch_value_backward(grad_value, marginals, dparams, n_params, B, L1, L2, grad_scores,
+                                     grad_params, st);
+    const int grid = grid_for((size_t)B * L1 * 32);
+    value_backward_rows_kernel<<<grid, 256, 0, st>>>(grad_value, marginals, lengths, B, L1, L2, grad_scores,
+                                                     dparams, n_params, grad_params);
+    return (int)cudaGetLastError();
 }
 
 int launch_value_backward(const float* grad_value, const float* marginals, const float* dparams,

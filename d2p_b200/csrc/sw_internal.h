@@ -112,6 +112,11 @@ int launch_aff_plane(const SwArgs& a, cudaStream_t st);
 int launch_value_backward(const float* grad_value, const float* marginals, const float* dparams,
                           int n_params, int B, int L1, int L2, float* grad_scores,
                           float* grad_params, cudaStream_t st);
+// the same with per-problem lengths (null: as launch_value_backward): cells
+// outside each problem are written as 0 without reading the marginals
+int launch_value_backward_rows(const float* grad_value, const float* marginals, const int* lengths,
+                               const float* dparams, int n_params, int B, int L1, int L2,
+                               float* grad_scores, float* grad_params, cudaStream_t st);
 int launch_sum_batches(const float* partials, int P, int B, float* out, int accumulate,
                        cudaStream_t st);
 

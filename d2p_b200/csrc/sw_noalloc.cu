@@ -20,8 +20,10 @@
 //   * sizes whose workspace (d2p_sw_workspace_bytes for the linear
 //     forward/backward) exceeds D2P_STATIC_SCRATCH_BYTES are rejected with
 //     D2P_ERR_WORKSPACE_TOO_SMALL before any device work.
-// No part of the scratch has to start at zero: every kernel on this path
-// writes each scratch word before reading it, so nothing is cleared.
+// What must start at zero is cleared inside each call: when the call spreads
+// a few large problems over several CTAs, the launcher zeroes their cross-CTA
+// progress words, barrier counters and recompute flags with cudaMemsetAsync
+// on the caller's stream; every other scratch word is written before it is read.
 #include <mutex>
 
 #include "../../include/d2p_b200.h"

@@ -439,7 +439,9 @@ struct RevOut {
     float b, pb, msg, db, dpb, dmsg, dmu;
 };
 // one cell, step i of its group: vv the lane's V here (HVP), w / dw the
-// forward's diagonal term and its tangent
+// forward's diagonal term and its tangent.  PG: the marginal itself (in dmu),
+// no tangent of the reverse.
+template <bool PG>
 __device__ __forceinline__ RevOut rev_cell(const RevCtx& C, const RevVars& V, int i, float sc, float vv, float w,
                                            float dw) {
     RevOut o;
@@ -450,6 +452,11 @@ __device__ __forceinline__ RevOut rev_cell(const RevCtx& C, const RevVars& V, in
     o.b = fmaf(d, V.rsh, rest);
     o.msg = fmaf(Gd, V.rsh, fmaf(C.G, rest, V.pbp));
     o.pb = P * o.b;
+    if (PG) {
+        o.db = o.dmsg = o.dpb = 0.f;
+        o.dmu = o.b * (w * V.f.kE);
+        return o;
+    }
     const float drest = fmaf(C.G, fmaf(C.dir.gam, V.br, V.dbr), V.f.dfb[i]);
     o.db = fmaf(d, V.drsh, drest);
     o.dmsg = fmaf(C.G, fmaf(C.dir.gam, o.b, o.db), V.dpbp);
@@ -459,17 +466,20 @@ __device__ __forceinline__ RevOut rev_cell(const RevCtx& C, const RevVars& V, in
     return o;
 }
 
-template <bool DOT>
+// DOT: sum gm * dmu; PG: write the marginal and sum score * marginal (gm is
+// the score); otherwise write dmu
+template <bool DOT, bool PG>
 __device__ __forceinline__ void rev_emit(const RevCtx& C, RevVars& V, float* slot, float gm, float dmu, bool act) {
     if (act) V.chk = fmaf(dmu, 0.f, V.chk);
-    if (DOT) {
+    if (DOT || PG) {
         if (act) V.sdot = fmaf(gm, dmu, V.sdot);  // a cell outside the problem may hold inf: no 0 * inf
-    } else {
+    }
+    if (!DOT) {
         if (act) *slot = dmu;
     }
 }
 
-template <bool MASK, bool HV, bool DOT>
+template <bool MASK, bool HV, bool DOT, bool PG>
 __device__ __forceinline__ void rev_stage_full(const RevCtx& C, RevVars& V, int k, int thr) {
     const int m16 = C.P + 16 - kCW * k;
     const int slot = ((m16 >> 4) & 1) * (16 * 32) + C.lane;
@@ -492,10 +502,11 @@ __device__ __forceinline__ void rev_stage_full(const RevCtx& C, RevVars& V, int 
             if (u == kCW - 1) cp_async_wait1();
             rev_lookahead(C, V, 4 * k + (u >> 2) + 1);
         }
-        const RevOut o = rev_cell(C, V, i, scv[u], DOT ? 0.f : vvv[u], zb[(15 - u) * 32], dzb[(15 - u) * 32]);
+        const RevOut o =
+            rev_cell<PG>(C, V, i, scv[u], DOT ? 0.f : vvv[u], zb[(15 - u) * 32], PG ? 0.f : dzb[(15 - u) * 32]);
         const bool act = !MASK || u < thr;
         const int col = (u <= cb) ? cb - u : cb - u + kRW;
-        rev_emit<DOT>(C, V, C.ring + col, vvv[u], o.dmu, act);
+        rev_emit<DOT, PG>(C, V, C.ring + col, PG ? scv[u] : vvv[u], o.dmu, act);
         const float msg = act ? o.msg : 0.f, dmsg = act ? o.dmsg : 0.f;
         mq[i] = msg;
         dmq[i] = dmsg;
@@ -511,7 +522,7 @@ __device__ __forceinline__ void rev_stage_full(const RevCtx& C, RevVars& V, int 
     }
 }
 
-template <bool HV, bool DOT>
+template <bool HV, bool DOT, bool PG>
 __device__ __forceinline__ void rev_stage_part(const RevCtx& C, RevVars& V, int k) {
     const int m16 = C.P + 16 - kCW * k;
     const int slot = ((m16 >> 4) & 1) * (16 * 32) + C.lane;
@@ -538,9 +549,9 @@ __device__ __forceinline__ void rev_stage_part(const RevCtx& C, RevVars& V, int 
                 rev_lookahead(C, V, 4 * k + q + 1);
             }
             const int ci = j0 & (kRW - 1);
-            const float vv = HV ? C.vring[ci] : 0.f;
-            const RevOut o = rev_cell(C, V, i, C.ring[ci], DOT ? 0.f : vv, zb[(15 - u) * 32], dzb[(15 - u) * 32]);
-            rev_emit<DOT>(C, V, C.ring + ci, vv, o.dmu, act);
+            const float vv = HV ? C.vring[ci] : 0.f, sc = C.ring[ci];
+            const RevOut o = rev_cell<PG>(C, V, i, sc, DOT ? 0.f : vv, zb[(15 - u) * 32], PG ? 0.f : dzb[(15 - u) * 32]);
+            rev_emit<DOT, PG>(C, V, C.ring + ci, PG ? sc : vv, o.dmu, act);
             const float msg = act ? o.msg : 0.f, dmsg = act ? o.dmsg : 0.f;
             mq[i] = msg;
             dmq[i] = dmsg;
@@ -567,7 +578,11 @@ __device__ __forceinline__ void rev_stage_part(const RevCtx& C, RevVars& V, int 
 // SPLIT: a cooperative launch spreads each problem over p.parts CTAs, as in
 // sw_linear.cu's lin_fast_kernel (the partition's tangent and the dot-mode
 // sums are combined across the parts in part order).
-template <bool HV, bool DOT, bool SPLIT>
+// PG: value + marginals + dS/dgap + dS/dT (soft_sw_with_grads): the forward
+// carries the tangent along gap (dS/dgap = T dZ/Z), the reverse writes the
+// marginals and sums score x marginal, and dS/dT follows from Euler's identity
+// for the degree-1 homogeneous S(s, gap, T): S = sum s mu + gap dS/dgap + T dS/dT.
+template <bool HV, bool DOT, bool SPLIT, bool PG>
 __global__ void __launch_bounds__(kNW * 32, 1) lin_tan_kernel(SwArgs p) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     WarpSmem& W = reinterpret_cast<WarpSmem*>(smem_raw)[threadIdx.x >> 5];
@@ -599,7 +614,7 @@ __global__ void __launch_bounds__(kNW * 32, 1) lin_tan_kernel(SwArgs p) {
     Dir dir;  // dP = P (vs V + ss s), dG = G gam
     dir.vs = p.mode == MODE_HVP ? 1.f / T : 0.f;
     dir.ss = p.mode == MODE_PT ? -1.f / (T * T) : 0.f;
-    dir.gam = p.mode == MODE_PGAP ? 1.f / T : (p.mode == MODE_PT ? -gapn / (T * T) : 0.f);
+    dir.gam = (PG || p.mode == MODE_PGAP) ? 1.f / T : (p.mode == MODE_PT ? -gapn / (T * T) : 0.f);
     const size_t plane = (size_t)L1m * L2m;
     const float* __restrict__ S = p.scores + (size_t)b * plane;
     const float* __restrict__ Vp = HV ? (DOT ? p.dot_with : p.tangent) + (size_t)b * plane : nullptr;
@@ -619,6 +634,11 @@ __global__ void __launch_bounds__(kNW * 32, 1) lin_tan_kernel(SwArgs p) {
     if (L1 == 0 || L2 == 0) {  // no cells: the output is all zeros
         if (threadIdx.x == 0 && part == 0) {
             if (DOT && p.dot_out) p.dot_out[b] = 0.f;
+            if (PG) {  // S = log(1) = 0, and so its derivatives
+                if (p.value) p.value[b] = 0.f;
+                if (p.grad_gap) p.grad_gap[b] = 0.f;
+                if (p.grad_T) p.grad_T[b] = 0.f;
+            }
             if (p.redo) p.redo[b] = 0;
         }
         return;
@@ -829,6 +849,10 @@ __global__ void __launch_bounds__(kNW * 32, 1) lin_tan_kernel(SwArgs p) {
             const double q = dtot / tot;
             sh_dSr = (float)q;
             if (!fin || !(fabs(q) < 1e30)) sh_bad = 1;
+            if (PG && part == 0) {
+                if (p.value) p.value[b] = ((float)sh_Sint + sh_Sfrac) / c;
+                if (p.grad_gap) p.grad_gap[b] = (float)(q * (double)T);
+            }
         }
         __syncthreads();
     }
@@ -935,12 +959,12 @@ __global__ void __launch_bounds__(kNW * 32, 1) lin_tan_kernel(SwArgs p) {
             if (k == 0) rev_lookahead(C, RV, 0);
             RV.sdot = 0.f;
             if (kCW * k <= P + 32 - L2)
-                rev_stage_part<HV, DOT>(C, RV, k);
+                rev_stage_part<HV, DOT, PG>(C, RV, k);
             else if (nv == 32 && kCW * k + kCW - 1 <= P - 1)
-                rev_stage_full<false, HV, DOT>(C, RV, k, 0);
+                rev_stage_full<false, HV, DOT, PG>(C, RV, k, 0);
             else
-                rev_stage_full<true, HV, DOT>(C, RV, k, lane < nv ? 16 * M + 16 - lane : -1);
-            if (DOT) RV.dot += (double)RV.sdot;
+                rev_stage_full<true, HV, DOT, PG>(C, RV, k, lane < nv ? 16 * M + 16 - lane : -1);
+            if (DOT || PG) RV.dot += (double)RV.sdot;
             if (RV.push) Wn.tag[k & (kHR / 16 - 1)] = (q << 16) | k;
             __syncwarp();
             if (lane == 0) {
@@ -967,19 +991,28 @@ __global__ void __launch_bounds__(kNW * 32, 1) lin_tan_kernel(SwArgs p) {
     const int o_acc = __syncthreads_or(fwd_out & 8);
     const int o_tan = __syncthreads_or(RV.chk != 0.f ? 1 : 0);
     const int redo = (o_win ? 1 : 0) | (sh_err ? 2 : 0) | (sh_bad ? 4 : 0) | (o_acc ? 8 : 0) | (o_tan ? 16 : 0);
-    if (DOT) {
+    if (DOT || PG) {
         const double tot = block_sum_d(RV.dot, red);
         if (threadIdx.x == 0) {
+            // DOT: the weighted sum; PG: dS/dT = (S - sum s mu - gap dS/dgap) / T
+            auto finish = [&](double all) {
+                if (DOT && p.dot_out) p.dot_out[b] = (float)all;
+                if (PG && p.grad_T) {
+                    const double S = ((double)sh_Sint + (double)sh_Sfrac) / (double)c;
+                    const double dgap = (double)sh_dSr * (double)T;
+                    p.grad_T[b] = (float)((S - all - (double)gapn * dgap) / (double)T);
+                }
+            };
             if (SPLIT && K > 1) {  // the last part to arrive sums the parts in order
                 gpart[kSyncPartDoubles * part + 3] = tot;
                 if (atom_add_release_gpu(gsync + 2 * kMaxParts + 1, 1) == K - 1) {
                     (void)ld_acquire_gpu(gsync + 2 * kMaxParts + 1);
                     double all = 0.0;
                     for (int k = 0; k < K; ++k) all += gpart[kSyncPartDoubles * k + 3];
-                    if (p.dot_out) p.dot_out[b] = (float)all;
+                    finish(all);
                 }
-            } else if (p.dot_out) {
-                p.dot_out[b] = (float)tot;
+            } else {
+                finish(tot);
             }
         }
     }
@@ -1000,7 +1033,8 @@ size_t lin_tan_workspace_bytes(int B, int L1, int L2) {
 }
 
 int launch_lin_tan(const SwArgs& a, size_t ws_bytes, cudaStream_t st) {
-    if (a.mode != MODE_HVP && a.mode != MODE_PGAP && a.mode != MODE_PT) return -1;
+    const bool pg = a.mode == MODE_MARG && (a.grad_gap || a.grad_T);
+    if (a.mode != MODE_HVP && a.mode != MODE_PGAP && a.mode != MODE_PT && !pg) return -1;
     if (!a.redo || engine_forced_plane()) return -1;
     if (a.L2 % 4 != 0 || a.L1 > 32 * ltan::kMaxRB || a.L1 == 0 || a.L2 == 0) return -1;
     const bool dot = a.dot_with != nullptr;
@@ -1008,6 +1042,7 @@ int launch_lin_tan(const SwArgs& a, size_t ws_bytes, cudaStream_t st) {
     if (a.mode == MODE_HVP && (dot || !a.tangent)) return -1;
     if (dot && !a.dot_out) return -1;
     if (!dot && !a.out) return -1;
+    if (pg && (dot || a.tangent)) return -1;
     auto al16 = [](const void* q) { return (((uintptr_t)q) & 15) == 0; };
     if (!a.scores || !al16(a.scores) || (a.out && !al16(a.out)) || !al16(a.ws) || !a.ws) return -1;
     if ((a.tangent && !al16(a.tangent)) || (dot && !al16(a.dot_with))) return -1;
@@ -1020,12 +1055,14 @@ int launch_lin_tan(const SwArgs& a, size_t ws_bytes, cudaStream_t st) {
     static int sms[64] = {0};
     static bool attr_set[64] = {false};
     if (dev < 64 && !attr_set[dev]) {
-        const void* ks[6] = {(const void*)ltan::lin_tan_kernel<true, false, false>,
-                             (const void*)ltan::lin_tan_kernel<false, false, false>,
-                             (const void*)ltan::lin_tan_kernel<true, true, false>,
-                             (const void*)ltan::lin_tan_kernel<true, false, true>,
-                             (const void*)ltan::lin_tan_kernel<false, false, true>,
-                             (const void*)ltan::lin_tan_kernel<true, true, true>};
+        const void* ks[8] = {(const void*)ltan::lin_tan_kernel<true, false, false, false>,
+                             (const void*)ltan::lin_tan_kernel<false, false, false, false>,
+                             (const void*)ltan::lin_tan_kernel<true, true, false, false>,
+                             (const void*)ltan::lin_tan_kernel<true, false, true, false>,
+                             (const void*)ltan::lin_tan_kernel<false, false, true, false>,
+                             (const void*)ltan::lin_tan_kernel<true, true, true, false>,
+                             (const void*)ltan::lin_tan_kernel<false, false, false, true>,
+                             (const void*)ltan::lin_tan_kernel<false, false, true, true>};
         for (const void* k : ks) {
             e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
             if (e == cudaSuccess)
@@ -1037,6 +1074,9 @@ int launch_lin_tan(const SwArgs& a, size_t ws_bytes, cudaStream_t st) {
         if (e != cudaSuccess) return (int)e;
         attr_set[dev] = true;
     }
+    // value + marginals + parameter gradients: only while one wave of CTAs
+    // (one per SM) holds the batch; larger batches run the log-domain kernel
+    if (pg && (dev >= 64 || a.B > sms[dev])) return -1;
     // few large problems: several CTAs per problem (sw_linear.cu's rule, with
     // this kernel's 6 warps per CTA)
     const int K = (dev < 64 && a.sync) ? lin_parts_nw(a.B, a.L1, a.L2, sms[dev], ltan::kNW) : 1;
@@ -1047,19 +1087,22 @@ int launch_lin_tan(const SwArgs& a, size_t ws_bytes, cudaStream_t st) {
         if (e == cudaSuccess) e = cudaMemsetAsync(s.redo, 0, sizeof(int) * (size_t)a.B, st);
         if (e != cudaSuccess) return (int)e;
         void* args[1] = {&s};
-        const void* k = dot  ? (const void*)ltan::lin_tan_kernel<true, true, true>
-                        : hv ? (const void*)ltan::lin_tan_kernel<true, false, true>
-                             : (const void*)ltan::lin_tan_kernel<false, false, true>;
+        const void* k = pg    ? (const void*)ltan::lin_tan_kernel<false, false, true, true>
+                        : dot ? (const void*)ltan::lin_tan_kernel<true, true, true, false>
+                        : hv  ? (const void*)ltan::lin_tan_kernel<true, false, true, false>
+                              : (const void*)ltan::lin_tan_kernel<false, false, true, false>;
         e = cudaLaunchCooperativeKernel(k, dim3(a.B * K), dim3(ltan::kNW * 32), args, smem, st);
         if (e == cudaSuccess) return 0;
         cudaGetLastError();  // does not fit: one CTA per problem instead
     }
-    if (dot)
-        ltan::lin_tan_kernel<true, true, false><<<a.B, ltan::kNW * 32, smem, st>>>(a);
+    if (pg)
+        ltan::lin_tan_kernel<false, false, false, true><<<a.B, ltan::kNW * 32, smem, st>>>(a);
+    else if (dot)
+        ltan::lin_tan_kernel<true, true, false, false><<<a.B, ltan::kNW * 32, smem, st>>>(a);
     else if (hv)
-        ltan::lin_tan_kernel<true, false, false><<<a.B, ltan::kNW * 32, smem, st>>>(a);
+        ltan::lin_tan_kernel<true, false, false, false><<<a.B, ltan::kNW * 32, smem, st>>>(a);
     else
-        ltan::lin_tan_kernel<false, false, false><<<a.B, ltan::kNW * 32, smem, st>>>(a);
+        ltan::lin_tan_kernel<false, false, false, false><<<a.B, ltan::kNW * 32, smem, st>>>(a);
     return (int)cudaGetLastError();
 }
 

@@ -243,7 +243,10 @@ class SoftSWFunction : public torch::autograd::Function<SoftSWFunction> {
         c10::cuda::CUDAGuard guard(scores.device());
         auto opt = scores.options();
         Tensor gv = grad_outputs[0], gm = grad_outputs[1];
-        Tensor grad_scores, grad_gap = torch::zeros({1}, opt), grad_T = torch::zeros({1}, opt);
+        // parameters that need no gradient get none (no zero-filled tensors)
+        Tensor grad_scores;
+        Tensor grad_gap = ctx->needs_input_grad(1) ? torch::zeros({1}, opt) : Tensor();
+        Tensor grad_T = ctx->needs_input_grad(2) ? torch::zeros({1}, opt) : Tensor();
         bool have = false;
         if (gv.defined() && gv.numel() > 0) {
             Tensor g = gv.to(torch::kFloat32).contiguous();
@@ -251,11 +254,12 @@ class SoftSWFunction : public torch::autograd::Function<SoftSWFunction> {
             grad_scores = torch::empty({s.B, s.L1, s.L2}, opt);
             const bool params = dparams.defined();
             Tensor gp = params ? torch::empty({2}, opt) : Tensor();
-            check_rc(d2p_sw_value_backward(g.data_ptr<float>(), marginals.data_ptr<float>(),
-                                           params ? dparams.data_ptr<float>() : nullptr, params ? 2 : 0,
-                                           s.B, s.L1, s.L2, grad_scores.data_ptr<float>(),
-                                           params ? gp.data_ptr<float>() : nullptr, cur_stream()),
-                     "d2p_sw_value_backward");
+            check_rc(d2p_sw_value_backward_lengths(g.data_ptr<float>(), marginals.data_ptr<float>(),
+                                                   lengths.defined() ? lengths.data_ptr<int>() : nullptr,
+                                                   params ? dparams.data_ptr<float>() : nullptr, params ? 2 : 0,
+                                                   s.B, s.L1, s.L2, grad_scores.data_ptr<float>(),
+                                                   params ? gp.data_ptr<float>() : nullptr, cur_stream()),
+                     "d2p_sw_value_backward_lengths");
             if (params) {
                 grad_gap = gp.narrow(0, 0, 1);
                 grad_T = gp.narrow(0, 1, 1);
@@ -266,11 +270,13 @@ class SoftSWFunction : public torch::autograd::Function<SoftSWFunction> {
             Tensor G = prep_grad(gm, scores, "grad_posteriors");
             auto r = lin_backward_full_raw(scores, G, host_value(gap), host_value(temperature), lengths, s);
             grad_scores = have ? grad_scores + std::get<0>(r) : std::get<0>(r);
-            grad_gap = grad_gap + std::get<1>(r);
-            grad_T = grad_T + std::get<2>(r);
+            if (ctx->needs_input_grad(1)) grad_gap = grad_gap + std::get<1>(r);
+            if (ctx->needs_input_grad(2)) grad_T = grad_T + std::get<2>(r);
             have = true;
         }
         if (!have) grad_scores = torch::zeros({s.B, s.L1, s.L2}, opt);
+        if (!ctx->needs_input_grad(1)) grad_gap = Tensor();
+        if (!ctx->needs_input_grad(2)) grad_T = Tensor();
         return {grad_scores, grad_gap, grad_T, Tensor()};
     }
 };
@@ -487,8 +493,11 @@ class SoftSWAffineFunction : public torch::autograd::Function<SoftSWAffineFuncti
         c10::cuda::CUDAGuard guard(scores.device());
         auto opt = scores.options().dtype(torch::kFloat32);
         Tensor gv = grad_outputs[0], gm = grad_outputs[1];
-        Tensor grad_scores, g_o = torch::zeros({1}, opt), g_e = torch::zeros({1}, opt),
-                            g_T = torch::zeros({1}, opt);
+        // parameters that need no gradient get none (no zero-filled tensors)
+        Tensor grad_scores;
+        Tensor g_o = ctx->needs_input_grad(1) ? torch::zeros({1}, opt) : Tensor();
+        Tensor g_e = ctx->needs_input_grad(2) ? torch::zeros({1}, opt) : Tensor();
+        Tensor g_T = ctx->needs_input_grad(3) ? torch::zeros({1}, opt) : Tensor();
         bool have = false;
         if (gv.defined() && gv.numel() > 0) {
             Tensor g = gv.to(torch::kFloat32).contiguous();
@@ -496,11 +505,12 @@ class SoftSWAffineFunction : public torch::autograd::Function<SoftSWAffineFuncti
             grad_scores = torch::empty({s.B, s.L1, s.L2}, opt);
             const bool params = dparams.defined();
             Tensor gp = params ? torch::empty({3}, opt) : Tensor();
-            check_rc(d2p_sw_value_backward(g.data_ptr<float>(), marginals.data_ptr<float>(),
-                                           params ? dparams.data_ptr<float>() : nullptr, params ? 3 : 0,
-                                           s.B, s.L1, s.L2, grad_scores.data_ptr<float>(),
-                                           params ? gp.data_ptr<float>() : nullptr, cur_stream()),
-                     "d2p_sw_value_backward");
+            check_rc(d2p_sw_value_backward_lengths(g.data_ptr<float>(), marginals.data_ptr<float>(),
+                                                   lengths.defined() ? lengths.data_ptr<int>() : nullptr,
+                                                   params ? dparams.data_ptr<float>() : nullptr, params ? 3 : 0,
+                                                   s.B, s.L1, s.L2, grad_scores.data_ptr<float>(),
+                                                   params ? gp.data_ptr<float>() : nullptr, cur_stream()),
+                     "d2p_sw_value_backward_lengths");
             if (params) {
                 g_o = gp.narrow(0, 0, 1);
                 g_e = gp.narrow(0, 1, 1);
@@ -514,12 +524,15 @@ class SoftSWAffineFunction : public torch::autograd::Function<SoftSWAffineFuncti
             auto r = aff_backward_full_raw(sf, G, host_value(go), host_value(ge), host_value(temperature),
                                            lengths, s);
             grad_scores = have ? grad_scores + std::get<0>(r) : std::get<0>(r);
-            g_o = g_o + std::get<1>(r);
-            g_e = g_e + std::get<2>(r);
-            g_T = g_T + std::get<3>(r);
+            if (ctx->needs_input_grad(1)) g_o = g_o + std::get<1>(r);
+            if (ctx->needs_input_grad(2)) g_e = g_e + std::get<2>(r);
+            if (ctx->needs_input_grad(3)) g_T = g_T + std::get<3>(r);
             have = true;
         }
         if (!have) grad_scores = torch::zeros({s.B, s.L1, s.L2}, opt);
+        if (!ctx->needs_input_grad(1)) g_o = Tensor();
+        if (!ctx->needs_input_grad(2)) g_e = Tensor();
+        if (!ctx->needs_input_grad(3)) g_T = Tensor();
         return {grad_scores, g_o, g_e, g_T, Tensor()};
     }
 };

@@ -139,6 +139,14 @@ D2P_API int d2p_sw_value_backward(const float* grad_value, const float* marginal
                           const float* dvalue_dparams, int n_params, int B, int L1, int L2,
                           float* grad_scores, float* grad_params, void* stream);
 
+/* d2p_sw_value_backward for a ragged batch: lengths [B, 2] (NULL: full
+ * problems).  Cells outside each problem (where the marginals are 0) get 0
+ * without the marginals being read.  Same replacement as above. */
+D2P_API int d2p_sw_value_backward_lengths(const float* grad_value, const float* marginals,
+                                          const int* lengths, const float* dvalue_dparams,
+                                          int n_params, int B, int L1, int L2, float* grad_scores,
+                                          float* grad_params, void* stream);
+
 /* ------------------------------------------------------------------------
  * Affine gap (reference family src/sw_affine); parameters (gap_open, gap_ext, T)
  * --------------------------------------------------------------------- */

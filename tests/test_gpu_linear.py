@@ -179,6 +179,23 @@ def test_autograd_value_sum(d2p, cuda_device):
     assert torch.equal(s.grad, res.marginals.detach())
 
 
+@pytest.mark.parametrize("B,L1,L2", [(6, 70, 96), (5, 33, 47)])
+def test_autograd_value_weighted_ragged(d2p, cuda_device, B, L1, L2):
+    """The value branch of the backward on a ragged batch: grad = w_b * marginals
+    inside each problem and exactly 0 in its padding (written without reading
+    the marginals there)."""
+    s = scores(B, L1, L2, seed=23).to(cuda_device).requires_grad_(True)
+    ln = lengths_for(B, L1, L2, seed=24).to(cuda_device)
+    w = torch.linspace(0.5, 2.0, B, device=cuda_device)
+    res = d2p.soft_sw(s, gap=-1.0, temperature=1.0, lengths=ln)
+    (res.value * w).sum().backward()
+    want = w[:, None, None] * res.marginals.detach()
+    torch.testing.assert_close(s.grad, want, rtol=1e-6, atol=0)
+    for b, (l1, l2) in enumerate(ln.tolist()):
+        assert torch.count_nonzero(s.grad[b, l1:, :]) == 0
+        assert torch.count_nonzero(s.grad[b, :, l2:]) == 0
+
+
 def test_autograd_tensor_params(d2p, cuda_device):
     s0 = scores(3, 12, 17, seed=22)
     s = s0.to(cuda_device).requires_grad_(True)
@@ -252,6 +269,16 @@ def test_ragged_batch_in_several_waves(d2p, cuda_device):
     torch.testing.assert_close(m, m2, rtol=0, atol=5e-5)
 
 
+def _log_domain_marginals(s, gap, T):
+    """Marginals from the log-domain kernel: soft_sw_with_grads on a batch of
+    more problems than SMs (one wave of the linear-domain gradient path no
+    longer holds it), padded with copies of the first problem."""
+    sms = torch.cuda.get_device_properties(s.device).multi_processor_count
+    pad = s[:1].expand(sms + 1 - s.shape[0], -1, -1) if s.shape[0] <= sms else s[:0]
+    _, m, _, _ = torch.ops.d2p.soft_sw_with_grads(torch.cat([s, pad]).contiguous(), gap, T, None)
+    return m[: s.shape[0]]
+
+
 @pytest.mark.parametrize("B,L1,L2", [(4, 256, 1024), (2, 1024, 1024), (3, 768, 700), (2, 70, 2000)])
 def test_long_rows(d2p, cuda_device, B, L1, L2):
     """Rows far longer than a warp's staging window and more row-blocks than
@@ -259,12 +286,17 @@ def test_long_rows(d2p, cuda_device, B, L1, L2):
     while its consumer may still be several row-blocks behind.  Each problem
     must come out of the linear-domain kernel itself (a problem it flags is
     recomputed by the log-domain kernel, whose result would be bitwise the
-    same as the one computed with parameter gradients) and match the oracle."""
+    log-domain kernel's own) and match the oracle.  The linear-domain
+    gradient path (soft_sw_with_grads, one wave) gives the same marginals."""
     s = scores(B, L1, L2, seed=L1 + 3 * L2)
     v, m = torch.ops.d2p.soft_sw_float(s.to(cuda_device), -1.0, 1.0, None)
-    v2, m2, _, _ = torch.ops.d2p.soft_sw_with_grads(s.to(cuda_device), -1.0, 1.0, None)
+    m2 = _log_domain_marginals(s.to(cuda_device), -1.0, 1.0)
     for b in range(B):
         assert not torch.equal(m[b], m2[b]), f"problem {b} was recomputed by the log-domain kernel"
+    torch.testing.assert_close(m, m2, rtol=0, atol=5e-5)
+    v3, m3, _, _ = torch.ops.d2p.soft_sw_with_grads(s.to(cuda_device), -1.0, 1.0, None)
+    torch.testing.assert_close(v3, v, rtol=1e-6, atol=1e-4)
+    torch.testing.assert_close(m3, m, rtol=0, atol=1e-6)
     idx = [0, B - 1]
     r64 = oracle.sw_linear(s[idx].numpy(), None, -1.0, 1.0, "f64")
     r32 = oracle.sw_linear(s[idx].numpy(), None, -1.0, 1.0, "f32")
@@ -389,13 +421,20 @@ def test_low_temperature_fallback_precision(d2p, cuda_device):
 
 
 def test_fast_paths_agree_512(d2p, cuda_device):
-    """The linear-domain path (no parameter gradients) and the log-domain path
-    (with them) give the same value and marginals at BASELINE config-2 size."""
+    """The linear-domain paths (value + marginals; with parameter gradients)
+    and the log-domain kernel give the same marginals at BASELINE config-2 size,
+    and the two gradient paths the same dS/dgap and dS/dT."""
     s = scores(2, 512, 512, seed=5).to(cuda_device)
     v1, m1 = torch.ops.d2p.soft_sw_float(s, -1.0, 1.0, None)
-    v2, m2, _, _ = torch.ops.d2p.soft_sw_with_grads(s, -1.0, 1.0, None)
+    v2, m2, g2, t2 = torch.ops.d2p.soft_sw_with_grads(s, -1.0, 1.0, None)
     torch.testing.assert_close(v1, v2, rtol=1e-5, atol=1e-4)
     torch.testing.assert_close(m1, m2, rtol=0, atol=5e-5)
+    torch.testing.assert_close(m1, _log_domain_marginals(s, -1.0, 1.0), rtol=0, atol=5e-5)
+    sms = torch.cuda.get_device_properties(s.device).multi_processor_count
+    big = torch.cat([s, s[:1].expand(sms, -1, -1)]).contiguous()  # more problems than SMs: log-domain kernel
+    _, _, g3, t3 = torch.ops.d2p.soft_sw_with_grads(big, -1.0, 1.0, None)
+    torch.testing.assert_close(g2, g3[:2], rtol=1e-5, atol=1e-3)
+    torch.testing.assert_close(t2, t3[:2], rtol=1e-4, atol=1e-2)
 
 
 @pytest.mark.parametrize("scale,T", [(40.0, 0.5), (8.0, 0.1)])
