@@ -1,8 +1,11 @@
 // sw_capi.cu -- extern "C" entry points of libd2p_b200.so (declared in include/d2p_b200.h).
 //
 // Argument checking, workspace carving and kernel selection live here; the
-// kernels themselves are in sw_plane.cu (general engine), sw_wavefront.cu (fast
-// value+marginals path) and sw_elementwise.cu.
+// kernels themselves are in sw_linear.cu / sw_affine_fast.cu (linear-domain
+// value + marginals), sw_tangent.cu / sw_affine_tangent.cu (linear-domain
+// tangent sweeps), sw_wavefront.cu (log-domain value + marginals + parameter
+// gradients for batches over one wave), sw_plane.cu (general engine and fix-up)
+// and sw_elementwise.cu.
 #include <limits.h>
 #include <stdint.h>
 #include <stdlib.h>
@@ -157,7 +160,8 @@ int d2p_sw_forward_backward(const float* scores, const int* lengths, int B, int 
         // Fast paths, each recomputing what the previous one flagged:
         //   linear-domain kernel (value + marginals: sw_linear.cu; with
         //   parameter gradients: the tangent kernel's gap sweep, sw_tangent.cu,
-        //   for batches of one wave) -> log-domain wavefront kernel -> plane engine.
+        //   for batches of one wave) -> plane engine;
+        //   otherwise log-domain wavefront kernel -> plane engine.
         pe = pe > wf ? pe : wf;
         pe = pe > lf ? pe : lf;
         pe = pe > tf ? pe : tf;
@@ -176,8 +180,15 @@ int d2p_sw_forward_backward(const float* scores, const int* lengths, int B, int 
                                                 : launch_lin_fast(a, workspace_bytes, st);
         a.order = nullptr;
         a.sync = nullptr;
-        if (rc == D2P_OK) a.only = flags;
-        else if (rc != kNotHandled) return rc;
+        if (rc == D2P_OK) {
+            // flagged problems (low temperatures, extreme scores) go to the plane
+            // engine, whose value + marginals mode follows the reference's
+            // score-unit arithmetic
+            a.only = flags;
+            a.redo = nullptr;
+            return launch_lin_plane(a, st);
+        }
+        if (rc != kNotHandled) return rc;
         rc = launch_wavefront(a, D2P_FAMILY_LINEAR, workspace_bytes, st);
         if (rc == D2P_OK) {
             a.only = flags;

@@ -26,8 +26,16 @@
 // k-1) and the planes store a - F[k].  Differences of frames are exact, so every
 // weight 2^(v - a) is formed from small numbers.  S is kept as integer + fraction.
 //
-// The fast path for linear value+marginals (sw_wavefront.cu) supersedes this
-// engine when shapes allow; this engine remains the general implementation.
+// The linear value + marginals mode is the exception: it is the fix-up of every
+// problem the linear-domain kernels flag (low temperatures, extreme scores), so
+// it follows the reference's arithmetic instead -- alpha in score units, and in
+// the reverse pass each cell's incoming weights divided by their own sum, like
+// the reference's softmax.  The rounding of a large stored alpha then cancels
+// out of the flow through the cell instead of accumulating along the paths.
+//
+// The linear-domain kernels (sw_linear.cu, sw_affine_fast.cu, sw_tangent.cu,
+// sw_affine_tangent.cu) supersede this engine where their range allows; this
+// engine remains the general implementation.
 #include "sw_common.cuh"
 #include "sw_internal.h"
 
@@ -166,7 +174,8 @@ struct FrameWin {
 // LINEAR GAP
 // ==========================================================================
 // workspace planes per problem (each L1max*L2max floats):
-//   0: a - F (framed scaled alpha)  1: beta  2: tangent forward (dalpha or U)
+//   0: a - F (framed scaled alpha; value + marginals: alpha, score units)
+//   1: beta (value + marginals: beta / N)  2: tangent forward (dalpha or U)
 //   3: tangent backward (dbeta or W)  4: R = (alpha - E[v]) / T  (PT mode)
 template <int MODE>
 __global__ void __launch_bounds__(kPlaneThreads) lin_plane_kernel(SwArgs p) {
@@ -225,6 +234,21 @@ __global__ void __launch_bounds__(kPlaneThreads) lin_plane_kernel(SwArgs p) {
         for (int i = ilo + threadIdx.x; i <= ihi; i += blockDim.x) {
             const int j = k - i;
             const size_t q = (size_t)(i - 1) * W + (j - 1);
+            if (MODE == MODE_MARG) {
+                // value + marginals keep alpha in score units, as the reference
+                // does (src/sw/kernels_cpu.cpp:70-150): each exponent is a
+                // difference of score-unit values, scaled by log2(e)/T only
+                // after the largest term is subtracted
+                const float sc = s[q];
+                const bool up = i > 1, lf = j > 1, dg = up && lf;
+                const float v0 = dg ? A[q - W - 1] + sc : kNeg;
+                const float v1 = up ? A[q - W] + gapn : kNeg;
+                const float v2 = lf ? A[q - 1] + gapn : kNeg;
+                const float m = fmaxf(fmaxf(v0, v1), fmaxf(v2, sc));
+                const float sum = (ex2f((v0 - m) * c) + ex2f((v1 - m) * c)) + (ex2f((v2 - m) * c) + ex2f((sc - m) * c));
+                A[q] = m + lg2f(sum) * ic;
+                continue;
+            }
             const float x = s[q] * c;
             const bool up = i > 1, lf = j > 1, dg = up && lf;
             const float v0 = dg ? A[q - W - 1] + x - d2 : kNeg;
@@ -271,8 +295,28 @@ __global__ void __launch_bounds__(kPlaneThreads) lin_plane_kernel(SwArgs p) {
         Fg[L1 + L2 + 1] = sh_F[(L1 + L2 + 1) & 1];
         Fg[L1 + L2 + 2] = Fg[L1 + L2 + 1];
     }
+    if (MODE == MODE_MARG) {
+        // S = M + T ln(exp(-M/T) + sum exp((alpha - M)/T)), M the largest alpha
+        // (score units; the origin alpha[0,0] = 0 is the exp(-M/T) term)
+        float mx = 0.f;
+        for (int i = 1 + (threadIdx.x >> 5); i <= L1; i += blockDim.x >> 5)
+            for (int j = 1 + (threadIdx.x & 31); j <= L2; j += 32) mx = fmaxf(mx, A[(size_t)(i - 1) * W + (j - 1)]);
+        const float M = block_max(mx, red);
+        double z = 0.0;
+        for (int i = 1 + (threadIdx.x >> 5); i <= L1; i += blockDim.x >> 5)
+            for (int j = 1 + (threadIdx.x & 31); j <= L2; j += 32)
+                z += (double)ex2f((A[(size_t)(i - 1) * W + (j - 1)] - M) * c);
+        const double zt = block_sum_d(z, reinterpret_cast<double*>(red));
+        if (threadIdx.x == 0) {
+            sh_Sint = M;  // S = Sint + Sfrac, score units
+            sh_dS = 0.f;
+            sh_Sfrac = lg2f((float)(zt + (double)ex2f(-M * c))) * ic;
+            if (p.value) p.value[b] = sh_Sint + sh_Sfrac;
+        }
+        __syncthreads();
+    }
     const FrameLse tot = block_frame_lse(acc, red);
-    if (threadIdx.x == 0) {
+    if (threadIdx.x == 0 && MODE != MODE_MARG) {
         const float l2 = tot.m + lg2f(tot.s);
         const float fl = floorf(l2);
         sh_Sint = tot.R + fl;
@@ -301,6 +345,36 @@ __global__ void __launch_bounds__(kPlaneThreads) lin_plane_kernel(SwArgs p) {
             const float x = sc * c;
             const bool up = i > 1, lf = j > 1, dg = up && lf;
             const bool hasD = (i < L1) && (j < L2), hasU = i < L1, hasL = j < L2;
+            if (MODE == MODE_MARG) {
+                // score units (see the forward).  The incoming weights of this
+                // cell are normalised by their own sum N, as the reference's
+                // softmax does (src/sw/kernels_cpu.cpp:41-62, :200-260), so the
+                // rounding of the stored alpha does not scale the flow through
+                // the cell; Bt holds beta / N for the predecessors' gathers.
+                const float lp = fminf(((a - Sint) - Sfrac) * c, 0.f);
+                const float binit = ex2f(lp);
+                float beta = binit;
+                if (hasD) beta += Bt[q + W + 1] * ex2f(((a - A[q + W + 1]) + s[q + W + 1]) * c);
+                if (hasU) beta += Bt[q + W] * ex2f(((a - A[q + W]) + gapn) * c);
+                if (hasL) beta += Bt[q + 1] * ex2f(((a - A[q + 1]) + gapn) * c);
+                const float ea = dg ? ((A[q - W - 1] - a) + sc) * c : kNeg;
+                const float es = (sc - a) * c;
+                const float eu = up ? ((A[q - W] - a) + gapn) * c : kNeg;
+                const float el = lf ? ((A[q - 1] - a) + gapn) * c : kNeg;
+                const float wa = dg ? ex2f(ea) : 0.f, wsk = ex2f(es);
+                const float wu = up ? ex2f(eu) : 0.f, wl = lf ? ex2f(el) : 0.f;
+                const float N = (wa + wsk) + (wu + wl);  // 1 up to rounding, >= 1/4
+                const float bn = beta / N;
+                Bt[q] = bn;
+                if (out) out[q] = bn * (wa + wsk);
+                gsum += (double)(bn * (wu + wl));
+                // dS/dT = entropy of the path distribution: visit probability x
+                // local choice entropy (of the normalised weights) + end-cell
+                // entropy
+                const float hloc = (dg ? -wa * ea : 0.f) + (up ? -wu * eu : 0.f) + (lf ? -wl * el : 0.f) - wsk * es;
+                hsum += (double)bn * (double)hloc + (double)beta * (double)lg2f(N) - (double)binit * (double)lp;
+                continue;
+            }
             const float lp = fminf((a - Sfrac) + (F0 - Sint), 0.f);
             const float binit = ex2f(lp);
             float beta = binit;
@@ -315,19 +389,7 @@ __global__ void __launch_bounds__(kPlaneThreads) lin_plane_kernel(SwArgs p) {
             const float es = x - F0 - a;
             const float wa = dg ? ex2f(ea) : 0.f;
             const float wsk = ex2f(es);
-            if (MODE == MODE_MARG) {
-                const float eu = up ? A[q - W] + g + (Fm1 - F0) - a : kNeg;
-                const float el = lf ? A[q - 1] + g + (Fm1 - F0) - a : kNeg;
-                const float wu = up ? ex2f(eu) : 0.f;
-                const float wl = lf ? ex2f(el) : 0.f;
-                const float mu = beta * (wa + wsk);
-                if (out) out[q] = mu;
-                gsum += (double)(beta * (wu + wl));
-                // dS/dT = entropy of the path distribution: visit probability x
-                // local choice entropy + end-cell entropy (non-negative terms).
-                const float hloc = (dg ? -wa * ea : 0.f) + (up ? -wu * eu : 0.f) + (lf ? -wl * el : 0.f) - wsk * es;
-                hsum += (double)beta * (double)hloc - (double)binit * (double)lp;
-            } else if (MODE == MODE_HVP) {
+            if (MODE == MODE_HVP) {
                 const float da = TG[q];
                 const float vv = V[q];
                 float db = binit * (da - dS) * iT;
@@ -404,7 +466,7 @@ __global__ void __launch_bounds__(kPlaneThreads) lin_plane_kernel(SwArgs p) {
     if (MODE == MODE_MARG && (p.grad_gap || p.grad_T)) {
         // the origin alpha[0,0] = 0 is a possible end state (empty alignment)
         if (threadIdx.x == 0) {
-            const float lp0 = fminf(-Sfrac - Sint, 0.f);
+            const float lp0 = fminf((-Sint - Sfrac) * c, 0.f);  // score units
             hsum += (double)ex2f(lp0) * (double)(-lp0);
         }
         const double G = block_sum_d(gsum, reinterpret_cast<double*>(red));
