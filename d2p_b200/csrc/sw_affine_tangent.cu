@@ -26,6 +26,13 @@
 // and their tangents forward, BI, X and theirs in the reverse), the split of
 // large problems over several CTAs and the fix-up contract are those of
 // sw_tangent.cu.
+//
+// PG (value + marginals + dS/dgap_open, dS/dgap_ext, dS/dT, for gap parameters
+// that need gradients): a forward-only sweep carries the tangent along gap_ext
+// (dS/dgap_ext = T dZ/Z), then a full sweep carries the one along gap_open,
+// writes the marginals and sums score x marginal; dS/dT follows from Euler's
+// identity for the degree-1 homogeneous S(s, go, ge, T):
+// S = sum s mu + go dS/dgo + ge dS/dge + T dS/dT.
 #include <stddef.h>
 #include <stdint.h>
 
@@ -263,7 +270,7 @@ __device__ __forceinline__ void fwd_commit(FwdVars& V, const FwdOut& o) {
     V.dTr = __shfl_up_sync(kAll, o.dT, 1);
 }
 
-template <bool MASK, bool HV>
+template <bool MASK, bool HV, bool PG>
 __device__ __forceinline__ void fwd_stage_full(const FwdCtx& C, FwdVars& V, int k, int thr) {
     const int c0 = (kCW * k - C.lane) & (kRW - 1);
     float scv[kCW], vvv[kCW];
@@ -296,7 +303,7 @@ __device__ __forceinline__ void fwd_stage_full(const FwdCtx& C, FwdVars& V, int 
         V.gsum += o.T;
         V.dgsum += o.dT;
         pm[(size_t)u * 32] = o.M;
-        pdm[(size_t)u * 32] = o.dM;
+        if (!PG) pdm[(size_t)u * 32] = o.dM;  // PG: the reverse needs no dM
         uq[i] = o.u;
         tq[i] = o.T;
         duq[i] = o.du;
@@ -311,7 +318,7 @@ __device__ __forceinline__ void fwd_stage_full(const FwdCtx& C, FwdVars& V, int 
     }
 }
 
-template <bool HV>
+template <bool HV, bool PG>
 __device__ __forceinline__ void fwd_stage_start(const FwdCtx& C, FwdVars& V, int k) {
     const bool live = C.lane < C.nv;
     float uq[4], tq[4], duq[4], dtq[4];
@@ -345,7 +352,7 @@ __device__ __forceinline__ void fwd_stage_start(const FwdCtx& C, FwdVars& V, int
             V.gsum += o.T;
             V.dgsum += o.dT;
             C.mrow[(size_t)t * 32] = o.M;
-            C.dmrow[(size_t)t * 32] = o.dM;
+            if (!PG) C.dmrow[(size_t)t * 32] = o.dM;
             uq[i] = o.u;
             tq[i] = o.T;
             duq[i] = o.du;
@@ -476,7 +483,9 @@ __device__ __forceinline__ void rev_apply(RevVars& V) {
 struct RevOut {
     float BM, BI, BD, PB, dBI, dBD, dPB, dmu;
 };
-// m / dm: the forward's M and dM of this cell
+// m / dm: the forward's M and dM of this cell.  PG: the marginal itself (in
+// dmu), no tangent of the reverse.
+template <bool PG>
 __device__ __forceinline__ RevOut rev_cell(const RevCtx& C, const RevVars& V, int i, float sc, float vv, float m,
                                            float dm) {
     RevOut o;
@@ -488,6 +497,11 @@ __device__ __forceinline__ RevOut rev_cell(const RevCtx& C, const RevVars& V, in
     o.BI = fmaf(i == 0 ? V.f.Ged0 : V.f.Ged1, V.Yr, fmaf(C.Ge, V.f.ya[i], c1));
     o.BM = fmaf(i == 0 ? V.f.God0 : V.f.God1, V.Yr, fmaf(C.Go, V.f.ya[i], fmaf(C.Go, V.BDp, c1)));
     o.PB = P * o.BM;
+    if (PG) {
+        o.dBI = o.dBD = o.dPB = 0.f;
+        o.dmu = o.BM * (m * V.f.kE);
+        return o;
+    }
     const float BIdn = fmaf(V.Yr, d, V.f.ya[i]);
     const float dBIdn = fmaf(V.dYr, d, V.f.dya[i]);
     const float dc1 = fmaf(V.dXr, d, V.f.dxa[i]);
@@ -500,12 +514,15 @@ __device__ __forceinline__ RevOut rev_cell(const RevCtx& C, const RevVars& V, in
     return o;
 }
 
-template <bool DOT>
+// DOT: sum gm * dmu; PG: write the marginal and sum score * marginal (gm is
+// the score); otherwise write dmu
+template <bool DOT, bool PG>
 __device__ __forceinline__ void rev_emit(RevVars& V, float* slot, float gm, float dmu, bool act) {
     if (act) V.chk = fmaf(dmu, 0.f, V.chk);
-    if (DOT) {
+    if (DOT || PG) {
         if (act) V.sdot = fmaf(gm, dmu, V.sdot);
-    } else {
+    }
+    if (!DOT) {
         if (act) *slot = dmu;
     }
 }
@@ -531,7 +548,7 @@ __device__ __forceinline__ void rev_commit(RevVars& V, const RevOut& o, bool act
     V.BMl = act ? o.BM : 0.f;
 }
 
-template <bool MASK, bool HV, bool DOT>
+template <bool MASK, bool HV, bool DOT, bool PG>
 __device__ __forceinline__ void rev_stage_full(const RevCtx& C, RevVars& V, int k, int thr) {
     const int m16 = C.P + 16 - kCW * k;
     const int slot = ((m16 >> 4) & 1) * (16 * 32) + C.lane;
@@ -554,10 +571,11 @@ __device__ __forceinline__ void rev_stage_full(const RevCtx& C, RevVars& V, int 
             if (u == kCW - 1) cp_async_wait1();
             rev_lookahead(C, V, 4 * k + (u >> 2) + 1);
         }
-        const RevOut o = rev_cell(C, V, i, scv[u], DOT ? 0.f : vvv[u], zb[(15 - u) * 32], dzb[(15 - u) * 32]);
+        const RevOut o =
+            rev_cell<PG>(C, V, i, scv[u], DOT ? 0.f : vvv[u], zb[(15 - u) * 32], PG ? 0.f : dzb[(15 - u) * 32]);
         const bool act = !MASK || u < thr;
         const int col = (u <= cb) ? cb - u : cb - u + kRW;
-        rev_emit<DOT>(V, C.ring + col, vvv[u], o.dmu, act);
+        rev_emit<DOT, PG>(V, C.ring + col, PG ? scv[u] : vvv[u], o.dmu, act);
         rev_commit(V, o, act, yq[i], xq[i], dyq[i], dxq[i]);
         if (i == 3)
             handoff4(C, 4 * k + (u >> 2), make_float4(yq[0], yq[1], yq[2], yq[3]),
@@ -566,7 +584,7 @@ __device__ __forceinline__ void rev_stage_full(const RevCtx& C, RevVars& V, int 
     }
 }
 
-template <bool HV, bool DOT>
+template <bool HV, bool DOT, bool PG>
 __device__ __forceinline__ void rev_stage_part(const RevCtx& C, RevVars& V, int k) {
     const int m16 = C.P + 16 - kCW * k;
     const int slot = ((m16 >> 4) & 1) * (16 * 32) + C.lane;
@@ -594,8 +612,9 @@ __device__ __forceinline__ void rev_stage_part(const RevCtx& C, RevVars& V, int 
             }
             const int ci = j0 & (kRW - 1);
             const float vv = HV ? C.vring[ci] : 0.f;
-            const RevOut o = rev_cell(C, V, i, C.ring[ci], DOT ? 0.f : vv, zb[(15 - u) * 32], dzb[(15 - u) * 32]);
-            rev_emit<DOT>(V, C.ring + ci, vv, o.dmu, act);
+            const float sc = C.ring[ci];
+            const RevOut o = rev_cell<PG>(C, V, i, sc, DOT ? 0.f : vv, zb[(15 - u) * 32], PG ? 0.f : dzb[(15 - u) * 32]);
+            rev_emit<DOT, PG>(V, C.ring + ci, PG ? sc : vv, o.dmu, act);
             rev_commit(V, o, act, yq[i], xq[i], dyq[i], dxq[i]);
             if (i == 3)
                 handoff4(C, 4 * k + q, make_float4(yq[0], yq[1], yq[2], yq[3]),
@@ -609,7 +628,7 @@ __device__ __forceinline__ void rev_stage_part(const RevCtx& C, RevVars& V, int 
 // ==========================================================================
 // kernel (sw_tangent.cu's lin_tan_kernel with the affine cell)
 // ==========================================================================
-template <bool HV, bool DOT, bool SPLIT>
+template <bool HV, bool DOT, bool SPLIT, bool PG>
 __global__ void __launch_bounds__(kNW * 32, 1) aff_tan_kernel(SwArgs p) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     WarpSmem& W = reinterpret_cast<WarpSmem*>(smem_raw)[threadIdx.x >> 5];
@@ -643,12 +662,13 @@ __global__ void __launch_bounds__(kNW * 32, 1) aff_tan_kernel(SwArgs p) {
     const float iT = 1.f / T, iT2 = 1.f / (T * T);
     dir.vs = p.mode == MODE_HVP ? iT : 0.f;
     dir.ss = p.mode == MODE_PT ? -iT2 : 0.f;
-    dir.go = p.mode == MODE_PGAP ? iT : (p.mode == MODE_PT ? -go * iT2 : 0.f);
-    dir.ge = p.mode == MODE_PGE ? iT : (p.mode == MODE_PT ? -ge * iT2 : 0.f);
+    const bool fwd_only = PG && p.pg_fwd_only;  // PG: the sweep along gap_ext
+    dir.go = PG ? (fwd_only ? 0.f : iT) : (p.mode == MODE_PGAP ? iT : (p.mode == MODE_PT ? -go * iT2 : 0.f));
+    dir.ge = PG ? (fwd_only ? iT : 0.f) : (p.mode == MODE_PGE ? iT : (p.mode == MODE_PT ? -ge * iT2 : 0.f));
     const size_t plane = (size_t)L1m * L2m;
     const float* __restrict__ S = p.scores + (size_t)b * plane;
     const float* __restrict__ Vp = HV ? (DOT ? p.dot_with : p.tangent) + (size_t)b * plane : nullptr;
-    float* __restrict__ out = (!DOT && p.out) ? p.out + (size_t)b * plane : nullptr;
+    float* __restrict__ out = (!DOT && !fwd_only && p.out) ? p.out + (size_t)b * plane : nullptr;
     const Layout LY = carve(p.ws, b, L1m, L2m);
     const int nRB = (L1 + 31) / 32;
     const int nch = (L2 + kCW - 1) / kCW;
@@ -664,7 +684,15 @@ __global__ void __launch_bounds__(kNW * 32, 1) aff_tan_kernel(SwArgs p) {
     if (L1 == 0 || L2 == 0) {
         if (threadIdx.x == 0 && part == 0) {
             if (DOT && p.dot_out) p.dot_out[b] = 0.f;
-            if (p.redo) p.redo[b] = 0;
+            if (PG && fwd_only) {
+                if (p.pg_ext) p.pg_ext[b] = 0.f;
+            } else if (PG) {  // S = log(1) = 0, and so its derivatives
+                if (p.value) p.value[b] = 0.f;
+                if (p.grad_gap) p.grad_gap[b] = 0.f;
+                if (p.grad_gap2) p.grad_gap2[b] = 0.f;
+                if (p.grad_T) p.grad_T[b] = 0.f;
+            }
+            if (p.redo && !PG) p.redo[b] = 0;  // PG: zeroed by the launcher
         }
         return;
     }
@@ -796,11 +824,11 @@ __global__ void __launch_bounds__(kNW * 32, 1) aff_tan_kernel(SwArgs p) {
                 fwd_lookahead(C, V, 0);
             }
             if (kCW * k < 31)
-                fwd_stage_start<HV && !DOT>(C, V, k);
+                fwd_stage_start<HV && !DOT, PG>(C, V, k);
             else if (nv == 32 && kCW * k + kCW - 1 <= L2 - 1)
-                fwd_stage_full<false, HV && !DOT>(C, V, k, 0);
+                fwd_stage_full<false, HV && !DOT, PG>(C, V, k, 0);
             else
-                fwd_stage_full<true, HV && !DOT>(C, V, k, lane < nv ? L2 + lane - kCW * k : -1);
+                fwd_stage_full<true, HV && !DOT, PG>(C, V, k, lane < nv ? L2 + lane - kCW * k : -1);
             acc_rebase2(V);
             if (V.push) Wn.tag[k & (kHR / 16 - 1)] = (r << 16) | k;
             __syncwarp();
@@ -870,8 +898,23 @@ __global__ void __launch_bounds__(kNW * 32, 1) aff_tan_kernel(SwArgs p) {
             const double q = dtot / tot;
             sh_dSr = (float)q;
             if (!fin || !(fabs(q) < 1e30)) sh_bad = 1;
+            if (PG && part == 0) {
+                if (fwd_only) {
+                    if (p.pg_ext) p.pg_ext[b] = (float)(q * (double)T);
+                } else {
+                    if (p.value) p.value[b] = ((float)sh_Sint + sh_Sfrac) / c;
+                    if (p.grad_gap) p.grad_gap[b] = (float)(q * (double)T);
+                }
+            }
         }
         __syncthreads();
+    }
+    if (fwd_only) {  // PG along gap_ext: the forward is all this sweep needs
+        const int o_win = __syncthreads_or(fwd_out & 1);
+        const int o_acc = __syncthreads_or(fwd_out & 8);
+        if (threadIdx.x == 0 && p.redo)
+            atomicOr(p.redo + b, (o_win ? 1 : 0) | (sh_err ? 2 : 0) | (sh_bad ? 4 : 0) | (o_acc ? 8 : 0));
+        return;
     }
 
     // ============================== reverse ==============================
@@ -926,7 +969,7 @@ __global__ void __launch_bounds__(kNW * 32, 1) aff_tan_kernel(SwArgs p) {
             for (int it = 0; it < 4; ++it) {
                 const int e = 4 * (lane + 32 * it);
                 cp_async16(&W.zr[M & 1][0] + e, mblk + o16 + e, 16);
-                cp_async16(&W.dzr[M & 1][0] + e, dmblk + o16 + e, 16);
+                if (!PG) cp_async16(&W.dzr[M & 1][0] + e, dmblk + o16 + e, 16);
             }
             const int gl = 4 * M - 1;
 #pragma unroll
@@ -976,12 +1019,12 @@ __global__ void __launch_bounds__(kNW * 32, 1) aff_tan_kernel(SwArgs p) {
             if (k == 0) rev_lookahead(C, RV, 0);
             RV.sdot = 0.f;
             if (kCW * k <= P + 32 - L2)
-                rev_stage_part<HV, DOT>(C, RV, k);
+                rev_stage_part<HV, DOT, PG>(C, RV, k);
             else if (nv == 32 && kCW * k + kCW - 1 <= P - 1)
-                rev_stage_full<false, HV, DOT>(C, RV, k, 0);
+                rev_stage_full<false, HV, DOT, PG>(C, RV, k, 0);
             else
-                rev_stage_full<true, HV, DOT>(C, RV, k, lane < nv ? 16 * M + 16 - lane : -1);
-            if (DOT) RV.dot += (double)RV.sdot;
+                rev_stage_full<true, HV, DOT, PG>(C, RV, k, lane < nv ? 16 * M + 16 - lane : -1);
+            if (DOT || PG) RV.dot += (double)RV.sdot;
             if (RV.push) Wn.tag[k & (kHR / 16 - 1)] = (q << 16) | k;
             __syncwarp();
             if (lane == 0) {
@@ -1005,24 +1048,36 @@ __global__ void __launch_bounds__(kNW * 32, 1) aff_tan_kernel(SwArgs p) {
     const int o_acc = __syncthreads_or(fwd_out & 8);
     const int o_tan = __syncthreads_or(RV.chk != 0.f ? 1 : 0);
     const int redo = (o_win ? 1 : 0) | (sh_err ? 2 : 0) | (sh_bad ? 4 : 0) | (o_acc ? 8 : 0) | (o_tan ? 16 : 0);
-    if (DOT) {
+    if (DOT || PG) {
         const double tot = block_sum_d(RV.dot, red);
         if (threadIdx.x == 0) {
+            // DOT: the weighted sum; PG: dS/dgap_ext from the forward-only sweep,
+            // dS/dT = (S - sum s mu - go dS/dgo - ge dS/dge) / T
+            auto finish = [&](double all) {
+                if (DOT && p.dot_out) p.dot_out[b] = (float)all;
+                if (PG) {
+                    const double S = ((double)sh_Sint + (double)sh_Sfrac) / (double)c;
+                    const double eo = (double)sh_dSr * (double)T;
+                    const double ee = p.pg_ext ? (double)p.pg_ext[b] : 0.0;
+                    if (p.grad_gap2) p.grad_gap2[b] = (float)ee;
+                    if (p.grad_T) p.grad_T[b] = (float)((S - all - (double)go * eo - (double)ge * ee) / (double)T);
+                }
+            };
             if (SPLIT && K > 1) {
                 gpart[kSyncPartDoubles * part + 3] = tot;
                 if (atom_add_release_gpu(gsync + 2 * kMaxParts + 1, 1) == K - 1) {
                     (void)ld_acquire_gpu(gsync + 2 * kMaxParts + 1);
                     double all = 0.0;
                     for (int k = 0; k < K; ++k) all += gpart[kSyncPartDoubles * k + 3];
-                    if (p.dot_out) p.dot_out[b] = (float)all;
+                    finish(all);
                 }
-            } else if (p.dot_out) {
-                p.dot_out[b] = (float)tot;
+            } else {
+                finish(tot);
             }
         }
     }
     if (threadIdx.x == 0 && p.redo) {
-        if (SPLIT)
+        if (SPLIT || PG)
             atomicOr(p.redo + b, redo);
         else
             p.redo[b] = redo;
@@ -1038,14 +1093,17 @@ size_t aff_tan_workspace_bytes(int B, int L1, int L2) {
 }
 
 int launch_aff_tan(const SwArgs& a, size_t ws_bytes, cudaStream_t st) {
-    if (a.mode != MODE_HVP && a.mode != MODE_PGAP && a.mode != MODE_PGE && a.mode != MODE_PT) return -1;
+    // PG: value + marginals + parameter gradients (two sweeps, see the kernel)
+    const bool pg = a.mode == MODE_MARG && (a.grad_gap || a.grad_gap2 || a.grad_T);
+    if (a.mode != MODE_HVP && a.mode != MODE_PGAP && a.mode != MODE_PGE && a.mode != MODE_PT && !pg) return -1;
     if (!a.redo || engine_forced_plane()) return -1;
     if (a.L2 % 4 != 0 || a.L1 > 32 * atan_::kMaxRB || a.L1 == 0 || a.L2 == 0) return -1;
     const bool dot = a.dot_with != nullptr;
     const bool hv = a.mode == MODE_HVP || dot;
     if (a.mode == MODE_HVP && (dot || !a.tangent)) return -1;
     if (dot && !a.dot_out) return -1;
-    if (!dot && !a.out) return -1;
+    if (!dot && !a.out && !pg) return -1;
+    if (pg && (dot || a.tangent || !a.pg_ext)) return -1;
     auto al16 = [](const void* q) { return (((uintptr_t)q) & 15) == 0; };
     if (!a.scores || !al16(a.scores) || (a.out && !al16(a.out)) || !a.ws) return -1;
     if ((a.tangent && !al16(a.tangent)) || (dot && !al16(a.dot_with))) return -1;
@@ -1058,12 +1116,14 @@ int launch_aff_tan(const SwArgs& a, size_t ws_bytes, cudaStream_t st) {
     static int sms[64] = {0};
     static bool attr_set[64] = {false};
     if (dev < 64 && !attr_set[dev]) {
-        const void* ks[6] = {(const void*)atan_::aff_tan_kernel<true, false, false>,
-                             (const void*)atan_::aff_tan_kernel<false, false, false>,
-                             (const void*)atan_::aff_tan_kernel<true, true, false>,
-                             (const void*)atan_::aff_tan_kernel<true, false, true>,
-                             (const void*)atan_::aff_tan_kernel<false, false, true>,
-                             (const void*)atan_::aff_tan_kernel<true, true, true>};
+        const void* ks[8] = {(const void*)atan_::aff_tan_kernel<true, false, false, false>,
+                             (const void*)atan_::aff_tan_kernel<false, false, false, false>,
+                             (const void*)atan_::aff_tan_kernel<true, true, false, false>,
+                             (const void*)atan_::aff_tan_kernel<true, false, true, false>,
+                             (const void*)atan_::aff_tan_kernel<false, false, true, false>,
+                             (const void*)atan_::aff_tan_kernel<true, true, true, false>,
+                             (const void*)atan_::aff_tan_kernel<false, false, false, true>,
+                             (const void*)atan_::aff_tan_kernel<false, false, true, true>};
         for (const void* k : ks) {
             e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
             if (e == cudaSuccess)
@@ -1076,27 +1136,44 @@ int launch_aff_tan(const SwArgs& a, size_t ws_bytes, cudaStream_t st) {
         attr_set[dev] = true;
     }
     const int K = (dev < 64 && a.sync) ? lin_parts_nw(a.B, a.L1, a.L2, sms[dev], atan_::kNW) : 1;
-    if (K > 1) {
-        SwArgs s = a;
-        s.parts = K;
-        e = cudaMemsetAsync(s.sync, 0, kSyncBytes * (size_t)a.B, st);
-        if (e == cudaSuccess) e = cudaMemsetAsync(s.redo, 0, sizeof(int) * (size_t)a.B, st);
-        if (e != cudaSuccess) return (int)e;
-        void* args[1] = {&s};
-        const void* k = dot  ? (const void*)atan_::aff_tan_kernel<true, true, true>
-                        : hv ? (const void*)atan_::aff_tan_kernel<true, false, true>
-                             : (const void*)atan_::aff_tan_kernel<false, false, true>;
-        e = cudaLaunchCooperativeKernel(k, dim3(a.B * K), dim3(atan_::kNW * 32), args, smem, st);
-        if (e == cudaSuccess) return 0;
-        cudaGetLastError();
-    }
-    if (dot)
-        atan_::aff_tan_kernel<true, true, false><<<a.B, atan_::kNW * 32, smem, st>>>(a);
-    else if (hv)
-        atan_::aff_tan_kernel<true, false, false><<<a.B, atan_::kNW * 32, smem, st>>>(a);
-    else
-        atan_::aff_tan_kernel<false, false, false><<<a.B, atan_::kNW * 32, smem, st>>>(a);
-    return (int)cudaGetLastError();
+    // one sweep; the flags are zeroed by the caller of a spread launch, once
+    // before the two PG sweeps (each ORs its bits in)
+    auto sweep = [&](const SwArgs& x, bool zero_redo) -> cudaError_t {
+        cudaError_t err;
+        if (K > 1) {
+            SwArgs s = x;
+            s.parts = K;
+            err = cudaMemsetAsync(s.sync, 0, kSyncBytes * (size_t)s.B, st);
+            if (err == cudaSuccess && zero_redo) err = cudaMemsetAsync(s.redo, 0, sizeof(int) * (size_t)s.B, st);
+            if (err != cudaSuccess) return err;
+            void* args[1] = {&s};
+            const void* k = pg    ? (const void*)atan_::aff_tan_kernel<false, false, true, true>
+                            : dot ? (const void*)atan_::aff_tan_kernel<true, true, true, false>
+                            : hv  ? (const void*)atan_::aff_tan_kernel<true, false, true, false>
+                                  : (const void*)atan_::aff_tan_kernel<false, false, true, false>;
+            err = cudaLaunchCooperativeKernel(k, dim3(s.B * K), dim3(atan_::kNW * 32), args, smem, st);
+            if (err == cudaSuccess) return err;
+            cudaGetLastError();  // does not fit: one CTA per problem instead
+        }
+        if (pg)
+            atan_::aff_tan_kernel<false, false, false, true><<<x.B, atan_::kNW * 32, smem, st>>>(x);
+        else if (dot)
+            atan_::aff_tan_kernel<true, true, false, false><<<x.B, atan_::kNW * 32, smem, st>>>(x);
+        else if (hv)
+            atan_::aff_tan_kernel<true, false, false, false><<<x.B, atan_::kNW * 32, smem, st>>>(x);
+        else
+            atan_::aff_tan_kernel<false, false, false, false><<<x.B, atan_::kNW * 32, smem, st>>>(x);
+        return cudaGetLastError();
+    };
+    if (!pg) return (int)sweep(a, true);
+    e = cudaMemsetAsync(a.redo, 0, sizeof(int) * (size_t)a.B, st);
+    if (e != cudaSuccess) return (int)e;
+    SwArgs x = a;
+    x.pg_fwd_only = 1;  // along gap_ext: writes pg_ext
+    e = sweep(x, false);
+    if (e != cudaSuccess) return (int)e;
+    x.pg_fwd_only = 0;  // along gap_open: value, marginals, the three gradients
+    return (int)sweep(x, false);
 }
 
 }  // namespace d2pb

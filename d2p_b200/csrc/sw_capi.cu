@@ -68,7 +68,8 @@ static size_t op_bytes(int family, int op, int B, int L1, int L2) {
                                                           : aff_fast_workspace_bytes(B, L1, L2, true);
             if (wf == 0) return pe;
             const size_t lf = family == D2P_FAMILY_LINEAR ? lin_fast_workspace_bytes(B, L1, L2) : 0;
-            const size_t tf = family == D2P_FAMILY_LINEAR ? lin_tan_workspace_bytes(B, L1, L2) : 0;
+            const size_t tf = family == D2P_FAMILY_LINEAR ? lin_tan_workspace_bytes(B, L1, L2)
+                                                          : aff_tan_workspace_bytes(B, L1, L2);
             pe = pe > wf ? pe : wf;
             pe = pe > lf ? pe : lf;
             pe = pe > tf ? pe : tf;
@@ -365,21 +366,36 @@ int d2p_sw_affine_forward_backward(const void* scores, int scores_dtype, const i
     a.ws = (float*)workspace;
     const size_t af = aff_fast_workspace_bytes(B, L1, L2, true);
     if (af > 0) {
-        // linear-domain kernel (no parameter gradients requested), then the
-        // plane engine for the problems it flagged
+        // linear-domain kernels -- value + marginals: sw_affine_fast.cu; with
+        // parameter gradients: the tangent kernel's two gap sweeps,
+        // sw_affine_tangent.cu -- then the plane engine for the problems they
+        // flagged
+        const bool grads = grad_gap_open || grad_gap_ext || grad_temperature;
         size_t pe = plane_bytes(D2P_FAMILY_AFFINE, MODE_MARG, B, L1, L2);
+        const size_t tf = aff_tan_workspace_bytes(B, L1, L2);
         pe = pe > af ? pe : af;
+        pe = pe > tf ? pe : tf;
         int* flags = (int*)((char*)workspace + align256(pe));
         int* order = (int*)((char*)flags + align256((size_t)B * sizeof(int)));
         a.redo = flags;
         a.only = nullptr;
         a.order = nullptr;
-        if (lengths && !grad_gap_open && !grad_gap_ext && !grad_temperature) {
-            const int ro = launch_lin_order(lengths, B, L1, L2, order, st);
-            if (ro == D2P_OK) a.order = order;
-            else if (ro != kNotHandled) return ro;
+        int rc;
+        if (grads) {
+            // the order slot holds dS/dgap_ext between the two sweeps
+            a.pg_ext = (float*)order;
+            a.sync = (int*)((char*)order + align256((size_t)B * sizeof(int)));
+            rc = launch_aff_tan(a, workspace_bytes, st);
+            a.pg_ext = nullptr;
+            a.sync = nullptr;
+        } else {
+            if (lengths) {
+                const int ro = launch_lin_order(lengths, B, L1, L2, order, st);
+                if (ro == D2P_OK) a.order = order;
+                else if (ro != kNotHandled) return ro;
+            }
+            rc = launch_aff_fast(a, workspace_bytes, st);
         }
-        int rc = launch_aff_fast(a, workspace_bytes, st);
         a.order = nullptr;
         a.redo = nullptr;
         if (rc == D2P_OK) {

@@ -60,6 +60,11 @@ struct SwArgs {
     const int* order;                   // [B] in, optional: problem of each CTA (largest first)
     int parts;                          // CTAs per problem (1 unless a kernel spreads problems)
     int* sync;                          // [B][kSyncBytes / 4], zeroed: cross-CTA words of each problem
+    // affine value + marginals + parameter gradients on the tangent kernel:
+    // a forward-only sweep along gap_ext leaves dS/dgap_ext in pg_ext [B],
+    // then the full sweep along gap_open reads it
+    int pg_fwd_only;
+    float* pg_ext;
 };
 
 // A problem spread over several CTAs (a cooperative launch) keeps its

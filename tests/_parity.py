@@ -15,6 +15,19 @@ def scores(B, L1, L2, seed=0, scale=1.0):
     return torch.randn(B, L1, L2, generator=g) * scale
 
 
+def plane_engine(op, s, *params):
+    """Outputs of `op(scores, *params, lengths)` computed by the plane engine:
+    `s` padded with one zero column and `lengths` set to its true shape.  No
+    fast path covers a padded row length that is not a multiple of 4, and the
+    plane engine's arithmetic does not depend on the padding, so this is
+    bitwise what the plane engine gives for a problem a fast path flags."""
+    B, L1, L2 = s.shape
+    sp = torch.nn.functional.pad(s, (0, 1)).contiguous()
+    ln = torch.tensor([[L1, L2]] * B, dtype=torch.int32, device=s.device)
+    outs = op(sp, *params, ln)
+    return [o[..., :L2] if o.dim() == 3 else o for o in outs]
+
+
 def lengths_for(B, L1, L2, seed=1, lo=1):
     g = torch.Generator().manual_seed(seed)
     l1 = torch.randint(lo, L1 + 1, (B,), generator=g)

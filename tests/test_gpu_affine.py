@@ -4,7 +4,7 @@ import pytest
 import torch
 
 import oracle
-from tests._parity import check, lengths_for, scores
+from tests._parity import check, lengths_for, plane_engine, scores
 
 pytestmark = pytest.mark.gpu
 
@@ -206,19 +206,27 @@ def test_fast_value_marginals(d2p, cuda_device, B, L1, L2, T, go, ge, ragged):
 def test_fast_long_rows(d2p, cuda_device, B, L1, L2):
     """Long rows, more row-blocks than warps and partitions beyond the double
     range of a single accumulator (S > 1023 log2 units at 1024 x 1024): every
-    problem must come out of the linear-domain kernel itself (one it flags is
-    recomputed by the plane engine, whose result would be bitwise the one
-    computed with parameter gradients) and match the oracle."""
+    problem must come out of the linear-domain kernels themselves (one they
+    flag is recomputed by the plane engine, whose result would be bitwise the
+    plane engine's own) and match the oracle -- value + marginals, and with
+    parameter gradients (the tangent kernel's two gap sweeps)."""
     s = scores(B, L1, L2, seed=L1 + 5 * L2)
     v, m = torch.ops.d2p.soft_sw_affine_float(s.to(cuda_device), -2.0, -0.5, 1.0, None)
-    v2, m2, _, _, _ = torch.ops.d2p.soft_sw_affine_with_grads(s.to(cuda_device), -2.0, -0.5, 1.0, None)
+    v2, m2, g1, g2, g3 = torch.ops.d2p.soft_sw_affine_with_grads(s.to(cuda_device), -2.0, -0.5, 1.0, None)
+    _, mp = plane_engine(torch.ops.d2p.soft_sw_affine_float, s.to(cuda_device), -2.0, -0.5, 1.0)
     for b in range(B):
-        assert not torch.equal(m[b], m2[b]), f"problem {b} was recomputed by the plane engine"
+        assert not torch.equal(m[b], mp[b]), f"problem {b} was recomputed by the plane engine"
+        assert not torch.equal(m2[b], mp[b]), f"problem {b} (with gradients) was recomputed by the plane engine"
     idx = [0, B - 1]
     r64 = oracle.sw_affine(s[idx].numpy(), None, -2.0, -0.5, 1.0, "f64")
     r32 = oracle.sw_affine(s[idx].numpy(), None, -2.0, -0.5, 1.0, "f32")
     check("value", v[idx], r64["value"], r32["value"])
     check("marginals", m[idx], r64["marginals"], r32["marginals"])
+    check("value (with grads)", v2[idx], r64["value"], r32["value"])
+    check("marginals (with grads)", m2[idx], r64["marginals"], r32["marginals"])
+    check("grad_open", g1[idx], r64["grad_open"], r32["grad_open"], rtol=1e-4, atol=1e-5)
+    check("grad_ext", g2[idx], r64["grad_ext"], r32["grad_ext"], rtol=1e-4, atol=1e-5)
+    check("grad_T", g3[idx], r64["grad_T"], r32["grad_T"], rtol=1e-4, atol=1e-5)
 
 
 def test_fast_bf16_matches_widened_fp32(d2p, cuda_device):
@@ -234,16 +242,58 @@ def test_fast_bf16_matches_widened_fp32(d2p, cuda_device):
 
 
 def test_fast_and_plane_agree_and_repeat(d2p, cuda_device):
-    """The fast path (no parameter gradients) and the plane engine (with them)
-    agree, and the fast path is bitwise repeatable with many row-blocks and
-    more problems than two per SM (ragged, so the CTA order is by cost)."""
+    """The fast paths (value + marginals; with parameter gradients, over more
+    than one wave of CTAs) and the plane engine agree, and the fast path is
+    bitwise repeatable with many row-blocks and more problems than two per SM
+    (ragged, so the CTA order is by cost)."""
     B, L1, L2 = 320, 200, 64
     s = scores(B, L1, L2, seed=5).to(cuda_device)
     ln = lengths_for(B, L1, L2, seed=6).to(cuda_device)
     v1, m1 = torch.ops.d2p.soft_sw_affine_float(s, -2.0, -0.5, 1.0, ln)
-    v2, m2, _, _, _ = torch.ops.d2p.soft_sw_affine_with_grads(s, -2.0, -0.5, 1.0, ln)
+    v2, m2, a2, b2, c2 = torch.ops.d2p.soft_sw_affine_with_grads(s, -2.0, -0.5, 1.0, ln)
     torch.testing.assert_close(v1, v2, rtol=1e-5, atol=1e-4)
     torch.testing.assert_close(m1, m2, rtol=0, atol=5e-5)
+    sp = torch.nn.functional.pad(s, (0, 1)).contiguous()  # row length 65: the plane engine
+    v3, m3, a3, b3, c3 = torch.ops.d2p.soft_sw_affine_with_grads(sp, -2.0, -0.5, 1.0, ln)
+    torch.testing.assert_close(v2, v3, rtol=1e-5, atol=1e-4)
+    torch.testing.assert_close(m2, m3[..., :L2], rtol=0, atol=5e-5)
+    for x, y in ((a2, a3), (b2, b3), (c2, c3)):
+        torch.testing.assert_close(x, y, rtol=1e-4, atol=1e-4)
     for _ in range(3):
         v3, m3 = torch.ops.d2p.soft_sw_affine_float(s, -2.0, -0.5, 1.0, ln)
         assert torch.equal(v3, v1) and torch.equal(m3, m1)
+
+
+@pytest.mark.parametrize("B,L1,L2,T,go,ge,ragged", [
+    (3, 100, 120, 1.0, -2.0, -0.5, False),
+    (5, 64, 256, 0.5, -1.5, -0.3, True),
+    (1, 1024, 256, 1.0, -2.0, -0.5, False),  # one large problem: spread over several CTAs
+    (2, 300, 512, 1.0, -2.0, -0.5, True),
+    (160, 40, 64, 1.0, -2.0, -0.5, True),  # more problems than SMs
+])
+def test_fast_param_grads(d2p, cuda_device, B, L1, L2, T, go, ge, ragged):
+    """Value, marginals and dS/dgap_open, dS/dgap_ext, dS/dT from the tangent
+    kernel's two gap sweeps (Euler's identity for dS/dT) against the oracle;
+    no problem may have been handed to the plane engine."""
+    s = scores(B, L1, L2, seed=B + L1 + 7 * L2)
+    ln = lengths_for(B, L1, L2, seed=L2, lo=L1 // 2) if ragged else None
+    lnd = None if ln is None else ln.to(cuda_device)
+    v, m, a, b, c = torch.ops.d2p.soft_sw_affine_with_grads(s.to(cuda_device), go, ge, T, lnd)
+    lnp = None if ln is None else ln.numpy()
+    r64 = oracle.sw_affine(s.numpy(), lnp, go, ge, T, "f64")
+    r32 = oracle.sw_affine(s.numpy(), lnp, go, ge, T, "f32")
+    check("value", v, r64["value"], r32["value"])
+    check("marginals", m, r64["marginals"], r32["marginals"])
+    check("grad_open", a, r64["grad_open"], r32["grad_open"], rtol=1e-4, atol=1e-5)
+    check("grad_ext", b, r64["grad_ext"], r32["grad_ext"], rtol=1e-4, atol=1e-5)
+    check("grad_T", c, r64["grad_T"], r32["grad_T"], rtol=1e-4, atol=1e-5)
+    sp = torch.nn.functional.pad(s, (0, 1)).contiguous().to(cuda_device)
+    lp = lnd if lnd is not None else torch.tensor([[L1, L2]] * B, dtype=torch.int32, device=cuda_device)
+    _, mp, _, _, _ = torch.ops.d2p.soft_sw_affine_with_grads(sp, go, ge, T, lp)
+    for bb in range(B):
+        assert not torch.equal(m[bb], mp[bb, :, :L2]), f"problem {bb} was recomputed by the plane engine"
+    if ln is not None:
+        mc = m.cpu()
+        for bb, (l1, l2) in enumerate(ln.tolist()):
+            assert torch.count_nonzero(mc[bb, l1:, :]) == 0
+            assert torch.count_nonzero(mc[bb, :, l2:]) == 0

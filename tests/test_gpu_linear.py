@@ -10,7 +10,7 @@ import pytest
 import torch
 
 import oracle
-from tests._parity import check, lengths_for, scores
+from tests._parity import check, lengths_for, plane_engine, scores
 
 pytestmark = pytest.mark.gpu
 
@@ -285,14 +285,16 @@ def test_long_rows(d2p, cuda_device, B, L1, L2):
     warps: every row-block hands its boundary values on through global memory
     while its consumer may still be several row-blocks behind.  Each problem
     must come out of the linear-domain kernel itself (a problem it flags is
-    recomputed by the log-domain kernel, whose result would be bitwise the
-    log-domain kernel's own) and match the oracle.  The linear-domain
-    gradient path (soft_sw_with_grads, one wave) gives the same marginals."""
+    recomputed by the plane engine, whose result would be bitwise the plane
+    engine's own) and match the oracle and the log-domain kernel.  The
+    linear-domain gradient path (soft_sw_with_grads, one wave) gives the same
+    marginals."""
     s = scores(B, L1, L2, seed=L1 + 3 * L2)
     v, m = torch.ops.d2p.soft_sw_float(s.to(cuda_device), -1.0, 1.0, None)
-    m2 = _log_domain_marginals(s.to(cuda_device), -1.0, 1.0)
+    _, mp = plane_engine(torch.ops.d2p.soft_sw_float, s.to(cuda_device), -1.0, 1.0)
     for b in range(B):
-        assert not torch.equal(m[b], m2[b]), f"problem {b} was recomputed by the log-domain kernel"
+        assert not torch.equal(m[b], mp[b]), f"problem {b} was recomputed by the plane engine"
+    m2 = _log_domain_marginals(s.to(cuda_device), -1.0, 1.0)
     torch.testing.assert_close(m, m2, rtol=0, atol=5e-5)
     v3, m3, _, _ = torch.ops.d2p.soft_sw_with_grads(s.to(cuda_device), -1.0, 1.0, None)
     torch.testing.assert_close(v3, v, rtol=1e-6, atol=1e-4)
