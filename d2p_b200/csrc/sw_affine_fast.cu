@@ -516,7 +516,12 @@ __device__ __forceinline__ void rev_stage_part(const RevCtx& C, RevVars& V, int 
 // ==========================================================================
 // kernel
 // ==========================================================================
-template <int NW, int MINB>
+// SPLIT: the launch is cooperative and spreads each problem over p.parts CTAs
+// (sw_linear.cu's scheme): row-block r goes to warp r mod NW of part
+// (r / NW) mod parts, the handoff from a part's last warp to the next part's
+// warp 0 takes the global route, and the progress words, the forward ->
+// reverse barrier and the partition partials sit in the problem's p.sync words.
+template <int NW, int MINB, bool SPLIT>
 __global__ void __launch_bounds__(NW * 32, MINB) aff_fast_kernel(SwArgs p) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     WarpSmem& W = reinterpret_cast<WarpSmem*>(smem_raw)[threadIdx.x >> 5];
@@ -527,8 +532,18 @@ __global__ void __launch_bounds__(NW * 32, MINB) aff_fast_kernel(SwArgs p) {
     __shared__ __align__(16) float zv[kHR];   // staging of a missing neighbour: zeros
     __shared__ float zf[kHR / 4];
 
-    const int b = p.order ? p.order[blockIdx.x] : blockIdx.x;
+    const int K = SPLIT ? p.parts : 1;
+    const int part = SPLIT ? (int)(blockIdx.x % K) : 0;
+    const int bi = SPLIT ? (int)(blockIdx.x / K) : (int)blockIdx.x;
+    const int b = p.order ? p.order[bi] : bi;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int gw = part * NW + warp, NWt = K * NW;  // this warp among the problem's warps
+    // cross-CTA links: warp 0's producer and warp NW-1's consumer sit in the
+    // neighbouring parts; their progress words are global
+    int* const gsync = SPLIT ? p.sync + (size_t)b * (kSyncBytes / 4) : nullptr;
+    const bool xin = SPLIT && K > 1 && warp == 0;
+    const bool xout = SPLIT && K > 1 && warp == NW - 1;
+    const int pin = (part + K - 1) % K;
     const int L1m = p.L1, L2m = p.L2;
     const int L1 = p.lengths ? min(max(p.lengths[2 * b], 0), L1m) : L1m;
     const int L2 = p.lengths ? min(max(p.lengths[2 * b + 1], 0), L2m) : L2m;
@@ -547,13 +562,13 @@ __global__ void __launch_bounds__(NW * 32, MINB) aff_fast_kernel(SwArgs p) {
     const size_t est = (size_t)gt_rows(L2m) * 32;
 
     if (out && (L1 < L1m || L2 < L2m)) {
-        for (int i = warp; i < L1m; i += NW) {
+        for (int i = gw; i < L1m; i += NWt) {
             float* row = out + (size_t)i * L2m;
             for (int j = (i < L1 ? L2 : 0) + lane; j < L2m; j += 32) row[j] = 0.f;
         }
     }
     if (L1 == 0 || L2 == 0) {
-        if (threadIdx.x == 0) {
+        if (threadIdx.x == 0 && part == 0) {
             if (p.value) p.value[b] = 0.f;
             if (p.redo) p.redo[b] = 0;
         }
@@ -592,9 +607,15 @@ __global__ void __launch_bounds__(NW * 32, MINB) aff_fast_kernel(SwArgs p) {
         }
         cp_async16(W.sf + (g0 & (kHR / 4 - 1)), gf + g0, 16);
     };
+    auto wait_prog = [&](const int* prog, int need) {
+        if (xin)
+            wait_flag_gpu(prog, need, &sh_err);
+        else
+            wait_flag(prog, need, &sh_err);
+    };
     auto stage_first = [&](const int* prog, int ordinal, const float* ga, const float* gb, const float* gf,
                            bool reader) {
-        wait_flag(prog, (ordinal << 16) + 3, &sh_err);
+        wait_prog(prog, (ordinal << 16) + 3);
         if (reader) {
             copy_stage(ordinal, 1, ga, gb, gf);
             copy_stage(ordinal, 2, ga, gb, gf);
@@ -602,7 +623,7 @@ __global__ void __launch_bounds__(NW * 32, MINB) aff_fast_kernel(SwArgs p) {
     };
     auto stage_next = [&](const int* prog, int ordinal, int k, const float* ga, const float* gb, const float* gf,
                           bool reader) {
-        wait_flag(prog, (ordinal << 16) + min(k + 4, kStageMask), &sh_err);
+        wait_prog(prog, (ordinal << 16) + min(k + 4, kStageMask));
         if (reader) copy_stage(ordinal, k + 3, ga, gb, gf);
     };
     // past its last stage a row-block's neighbour reads up to 48 steps and 12
@@ -625,7 +646,9 @@ __global__ void __launch_bounds__(NW * 32, MINB) aff_fast_kernel(SwArgs p) {
     V.E = 0.f;
     V.ebmin = V.ebmax = 0x3f800000;
     V.emax = 0.f;
-    for (int r = warp; r < nRB; r += NW) {
+    const int* const prodF = xin ? gsync + pin : &progF[wprev];
+    const int* const prodR = xin ? gsync + kMaxParts + pin : &progR[wprev];
+    for (int r = gw; r < nRB; r += NWt) {
         const int nv = min(32, L1 - 32 * r);
         const int nst = (L2 + nv - 1 + kCW - 1) / kCW;
         const float* srow = S + (size_t)(32 * r) * L2m;
@@ -659,13 +682,13 @@ __global__ void __launch_bounds__(NW * 32, MINB) aff_fast_kernel(SwArgs p) {
         __syncwarp();
         if (lane == 31) st_release(&progF[warp], r << 16);  // started: the row above may push to this warp
         if (0 < nch) tile_load<4>(tS, 0, L2);
-        if (hasB) stage_first(&progF[wprev], r - 1, gaA, gbA, gfA, lane == 0);
+        if (hasB) stage_first(prodF, r - 1, gaA, gbA, gfA, lane == 0);
         cp_async_commit();
         V.Mp = V.Dp = V.Td = V.ur = V.Tr = V.Tl = 0.f;
         V.f.d1 = 0.f;
         for (int k = 0; k < nst; ++k) {
             __syncwarp();
-            if (hasB) stage_next(&progF[wprev], r - 1, k, gaA, gbA, gfA, lane == 0);
+            if (hasB) stage_next(prodF, r - 1, k, gaA, gbA, gfA, lane == 0);
             cp_async_commit();
             if (k + 1 < nch) tile_load<4>(tS, k + 1, L2);
             cp_async_commit();
@@ -674,7 +697,7 @@ __global__ void __launch_bounds__(NW * 32, MINB) aff_fast_kernel(SwArgs p) {
             // push while the row-block below is on its warp and has done at least
             // k - 8 stages (the linear kernel's rule, sw_linear.cu)
             V.push = false;
-            if (lane == 31 && hasD) {
+            if (lane == 31 && hasD && !xout) {
                 const int cw = ld_acquire(&progF[wnext]);
                 V.push = (cw >> 16) == r + 1 && (cw & kStageMask) + 8 >= k;
             }
@@ -692,7 +715,10 @@ __global__ void __launch_bounds__(NW * 32, MINB) aff_fast_kernel(SwArgs p) {
             acc_rebase(V.acc, V.ab, V.E);
             if (V.push) Wn.tag[k & (kHR / 16 - 1)] = (r << 16) | k;
             __syncwarp();
-            if (lane == 31) st_release(&progF[warp], (r << 16) | min(k + 1, kStageMask - 1));
+            if (lane == 31) {
+                st_release(&progF[warp], (r << 16) | min(k + 1, kStageMask - 1));
+                if (xout) st_release_gpu(gsync + part, (r << 16) | min(k + 1, kStageMask - 1));
+            }
         }
         V.acc = fma((double)V.gsum, p2d(V.E - V.ab), V.acc);
         V.emax = fmaxf(V.emax, V.E - V.ab);
@@ -700,16 +726,41 @@ __global__ void __launch_bounds__(NW * 32, MINB) aff_fast_kernel(SwArgs p) {
         if (lane == 31) write_tail(C.oa, C.ob, C.of, nst, V.E);
         cp_async_wait0();
         __syncwarp();
-        if (lane == 31) st_release(&progF[warp], (r << 16) | kStageMask);
+        if (lane == 31) {
+            st_release(&progF[warp], (r << 16) | kStageMask);
+            if (xout) st_release_gpu(gsync + part, (r << 16) | kStageMask);
+        }
     }
 
     if (lane < kHR / 16) W.tag[lane] = -1;  // forward pushes are no reverse pushes
     // ---- S = log2(1 + sum of every lane's partition), kept as integer + fraction
     {
         // every lane's acc brought to the largest base; M[0,0] = 0 adds 2^-abmax
-        const float abmax = block_max(V.ab, red);
-        const double tot = block_sum_d(V.acc * p2d(V.ab - abmax), reinterpret_cast<double*>(red)) + p2d(-abmax);
+        const float abl = block_max(V.ab, red);
+        const double totl = block_sum_d(V.acc * p2d(V.ab - abl), reinterpret_cast<double*>(red));
         if (threadIdx.x == 0) {
+            float abmax = abl;
+            double tot = totl;
+            if (SPLIT && K > 1) {  // every part's partial, after every part's forward
+                double* const gp = reinterpret_cast<double*>(gsync + 64);
+                gp[kSyncPartDoubles * part] = (double)abl;
+                gp[kSyncPartDoubles * part + 1] = totl;
+                atom_add_release_gpu(gsync + 2 * kMaxParts, 1);
+                int it = 0;
+                while (ld_acquire_gpu(gsync + 2 * kMaxParts) < K) {
+                    if (++it > kSpinLimit) {
+                        sh_err = 1;
+                        break;
+                    }
+                    __nanosleep(64);
+                }
+                abmax = -3.0e38f;
+                for (int k = 0; k < K; ++k) abmax = fmaxf(abmax, (float)gp[kSyncPartDoubles * k]);
+                tot = 0.0;
+                for (int k = 0; k < K; ++k)
+                    tot = fma(gp[kSyncPartDoubles * k + 1], p2d((float)gp[kSyncPartDoubles * k] - abmax), tot);
+            }
+            tot += p2d(-abmax);
             const int hi = __double2hiint(tot);
             const int ef = (hi >> 20) & 0x7ff;
             const int e = ef - 1023 + (int)abmax;
@@ -718,7 +769,7 @@ __global__ void __launch_bounds__(NW * 32, MINB) aff_fast_kernel(SwArgs p) {
             sh_Sint = e;
             sh_Sfrac = lg2_rr((float)m);
             if (!fin) sh_bad = 1;
-            if (p.value) p.value[b] = ((float)sh_Sint + sh_Sfrac) / c;
+            if (p.value && part == 0) p.value[b] = ((float)sh_Sint + sh_Sfrac) / c;
         }
         __syncthreads();
     }
@@ -732,7 +783,7 @@ __global__ void __launch_bounds__(NW * 32, MINB) aff_fast_kernel(SwArgs p) {
     const int nstR = P / kCW + 2;
     RevVars RV;
     RV.ebmin = RV.ebmax = 0x3f800000;
-    for (int q = warp; q < nRB; q += NW) {
+    for (int q = gw; q < nRB; q += NWt) {
         const int r = nRB - 1 - q;
         const int nv = min(32, L1 - 32 * r);
         const float* srow = S + (size_t)(32 * r) * L2m;
@@ -790,7 +841,7 @@ __global__ void __launch_bounds__(NW * 32, MINB) aff_fast_kernel(SwArgs p) {
                 if (ch >= 0 && ch < nch) tile_load<4>(tS, ch, L2);
         }
         batch(0);
-        if (hasBelow) stage_first(&progR[wprev], q - 1, gaB, gbB, gfB, lane == nv - 1);
+        if (hasBelow) stage_first(prodR, q - 1, gaB, gbB, gfB, lane == nv - 1);
         cp_async_commit();
 
         RV.BDp = RV.PBp = RV.Yr = RV.Xr = RV.BMl = 0.f;
@@ -800,7 +851,7 @@ __global__ void __launch_bounds__(NW * 32, MINB) aff_fast_kernel(SwArgs p) {
         for (int k = 0; k < nstR; ++k) {
             const int M = P / kCW + 1 - k;
             __syncwarp();
-            if (hasBelow) stage_next(&progR[wprev], q - 1, k, gaB, gbB, gfB, lane == nv - 1);
+            if (hasBelow) stage_next(prodR, q - 1, k, gaB, gbB, gfB, lane == nv - 1);
             cp_async_commit();
             if (out && M + 1 < nch && M + 1 >= 0) tile_store(tM, M + 1, L2);
             if (M - 3 >= 0 && M - 3 < nch) tile_load<4>(tS, M - 3, L2);
@@ -809,7 +860,7 @@ __global__ void __launch_bounds__(NW * 32, MINB) aff_fast_kernel(SwArgs p) {
             cp_async_wait2();
             __syncwarp();
             RV.push = false;
-            if (lane == 0 && hasAbove) {
+            if (lane == 0 && hasAbove && !xout) {
                 const int cw = ld_acquire(&progR[wnext]);
                 RV.push = (cw >> 16) == q + 1 && (cw & kStageMask) + 8 >= k;
             }
@@ -822,14 +873,20 @@ __global__ void __launch_bounds__(NW * 32, MINB) aff_fast_kernel(SwArgs p) {
                 rev_stage_full<true>(C, RV, k, lane < nv ? 16 * M + 16 - lane : -1);
             if (RV.push) Wn.tag[k & (kHR / 16 - 1)] = (q << 16) | k;
             __syncwarp();
-            if (lane == 0) st_release(&progR[warp], (q << 16) | min(k + 1, kStageMask - 1));
+            if (lane == 0) {
+                st_release(&progR[warp], (q << 16) | min(k + 1, kStageMask - 1));
+                if (xout) st_release_gpu(gsync + kMaxParts + part, (q << 16) | min(k + 1, kStageMask - 1));
+            }
         }
         if (lane == 0) write_tail(C.oa, C.ob, C.of, nstR, RV.Q);
         __syncwarp();
         if (out && nch > 0) tile_store(tM, 0, L2);
         cp_async_wait0();
         __syncwarp();
-        if (lane == 0) st_release(&progR[warp], (q << 16) | kStageMask);
+        if (lane == 0) {
+            st_release(&progR[warp], (q << 16) | kStageMask);
+            if (xout) st_release_gpu(gsync + kMaxParts + part, (q << 16) | kStageMask);
+        }
     }
 
     const bool outside = (fwd_out & 1) || RV.ebmin < ((127 - kJMax) << 23) || RV.ebmax > ((127 + kJMax) << 23);
@@ -838,7 +895,12 @@ __global__ void __launch_bounds__(NW * 32, MINB) aff_fast_kernel(SwArgs p) {
     // nonzero = recompute; the bits say why (1 frame step, 2 wait gave up,
     // 4 partition not finite, 8 partition base)
     const int redo = (o_win ? 1 : 0) | (sh_err ? 2 : 0) | (sh_bad ? 4 : 0) | (o_acc ? 8 : 0);
-    if (threadIdx.x == 0 && p.redo) p.redo[b] = redo;
+    if (threadIdx.x == 0 && p.redo) {
+        if (SPLIT)
+            atomicOr(p.redo + b, redo);  // zeroed by the launcher
+        else
+            p.redo[b] = redo;
+    }
 }
 
 // bf16 scores are widened into the workspace once per call
@@ -902,30 +964,42 @@ int launch_aff_fast(const SwArgs& a0, size_t ws_bytes, cudaStream_t st) {
     if (e != cudaSuccess) return (int)e;
     static int sms[64] = {0};
     static bool attr_set[64] = {false};
+    const size_t s6 = sizeof(aff::WarpSmem) * aff::kNW, s12 = sizeof(aff::WarpSmem) * aff::kNWWide;
     if (dev < 64 && !attr_set[dev]) {
-        const size_t s6 = sizeof(aff::WarpSmem) * aff::kNW, s12 = sizeof(aff::WarpSmem) * aff::kNWWide;
-        e = cudaFuncSetAttribute(aff::aff_fast_kernel<aff::kNW, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)s6);
-        if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(aff::aff_fast_kernel<aff::kNW, 2>, cudaFuncAttributePreferredSharedMemoryCarveout,
-                                     (int)cudaSharedmemCarveoutMaxShared);
-        if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(aff::aff_fast_kernel<aff::kNWWide, 1>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s12);
-        if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(aff::aff_fast_kernel<aff::kNWWide, 1>,
-                                     cudaFuncAttributePreferredSharedMemoryCarveout,
-                                     (int)cudaSharedmemCarveoutMaxShared);
+        const void* ks[3] = {(const void*)aff::aff_fast_kernel<aff::kNW, 2, false>,
+                             (const void*)aff::aff_fast_kernel<aff::kNWWide, 1, false>,
+                             (const void*)aff::aff_fast_kernel<aff::kNWWide, 1, true>};
+        for (int i = 0; i < 3 && e == cudaSuccess; ++i) {
+            e = cudaFuncSetAttribute(ks[i], cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(i == 0 ? s6 : s12));
+            if (e == cudaSuccess)
+                e = cudaFuncSetAttribute(ks[i], cudaFuncAttributePreferredSharedMemoryCarveout,
+                                         (int)cudaSharedmemCarveoutMaxShared);
+        }
         if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
         if (e != cudaSuccess) return (int)e;
         attr_set[dev] = true;
     }
-    // at most one problem per SM: 12 warps per problem when that pays (see launch_lin_fast)
+    // A batch that leaves most SMs idle spreads each problem over several CTAs
+    // of 12 warps (cooperative launch: every part resident at once); at most
+    // one problem per SM runs 12 warps per problem when that pays (see
+    // launch_lin_fast).
+    const int K = (dev < 64 && a.sync) ? lin_parts_nw(a.B, a.L1, a.L2, sms[dev], aff::kNWWide) : 1;
+    if (K > 1) {
+        SwArgs s = a;
+        s.parts = K;
+        e = cudaMemsetAsync(s.sync, 0, kSyncBytes * (size_t)a.B, st);
+        if (e == cudaSuccess) e = cudaMemsetAsync(s.redo, 0, sizeof(int) * (size_t)a.B, st);
+        if (e != cudaSuccess) return (int)e;
+        void* args[1] = {&s};
+        e = cudaLaunchCooperativeKernel((const void*)aff::aff_fast_kernel<aff::kNWWide, 1, true>, dim3(a.B * K),
+                                        dim3(aff::kNWWide * 32), args, s12, st);
+        if (e == cudaSuccess) return 0;
+        cudaGetLastError();  // a cooperative launch that does not fit: one CTA per problem instead
+    }
     if (dev < 64 && a.B <= sms[dev] && lin_wide_pays(a.L1, a.L2)) {
-        aff::aff_fast_kernel<aff::kNWWide, 1>
-            <<<a.B, aff::kNWWide * 32, sizeof(aff::WarpSmem) * aff::kNWWide, st>>>(a);
+        aff::aff_fast_kernel<aff::kNWWide, 1, false><<<a.B, aff::kNWWide * 32, s12, st>>>(a);
     } else {
-        aff::aff_fast_kernel<aff::kNW, 2><<<a.B, aff::kNW * 32, sizeof(aff::WarpSmem) * aff::kNW, st>>>(a);
+        aff::aff_fast_kernel<aff::kNW, 2, false><<<a.B, aff::kNW * 32, s6, st>>>(a);
     }
     return (int)cudaGetLastError();
 }

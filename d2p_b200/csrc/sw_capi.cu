@@ -394,7 +394,9 @@ int d2p_sw_affine_forward_backward(const void* scores, int scores_dtype, const i
                 if (ro == D2P_OK) a.order = order;
                 else if (ro != kNotHandled) return ro;
             }
+            a.sync = (int*)((char*)order + align256((size_t)B * sizeof(int)));
             rc = launch_aff_fast(a, workspace_bytes, st);
+            a.sync = nullptr;
         }
         a.order = nullptr;
         a.redo = nullptr;

@@ -217,6 +217,8 @@ def test_fast_long_rows(d2p, cuda_device, B, L1, L2):
     for b in range(B):
         assert not torch.equal(m[b], mp[b]), f"problem {b} was recomputed by the plane engine"
         assert not torch.equal(m2[b], mp[b]), f"problem {b} (with gradients) was recomputed by the plane engine"
+    v4, m4 = torch.ops.d2p.soft_sw_affine_float(s.to(cuda_device), -2.0, -0.5, 1.0, None)
+    assert torch.equal(v4, v) and torch.equal(m4, m), "problems spread over several CTAs must repeat bitwise"
     idx = [0, B - 1]
     r64 = oracle.sw_affine(s[idx].numpy(), None, -2.0, -0.5, 1.0, "f64")
     r32 = oracle.sw_affine(s[idx].numpy(), None, -2.0, -0.5, 1.0, "f32")
