@@ -52,7 +52,7 @@ static size_t plane_bytes(int family, int mode, int B, int L1, int L2) {
 // (linear family, covered shapes) or the plane engine's, whichever is larger
 static size_t tan_area(int family, int op, int B, int L1, int L2) {
     size_t pe = plane_bytes(family, op == D2P_OP_HVP ? MODE_HVP : MODE_PT, B, L1, L2);
-    const size_t tf = family == D2P_FAMILY_LINEAR ? lin_tan_workspace_bytes(B, L1, L2)
+    const size_t tf = family == D2P_FAMILY_LINEAR ? lin_tan_workspace_bytes(B, L1, L2, op == D2P_OP_BACKWARD_FULL)
                                                   : aff_tan_workspace_bytes(B, L1, L2);
     pe = pe > tf ? pe : tf;
     return align256(pe);
@@ -287,7 +287,37 @@ int d2p_sw_backward_full(const float* scores, const float* grad_marginals, const
     a.tangent = grad_marginals;
     a.mode = MODE_HVP;
     a.out = grad_scores;
-    int rc = run_lin_tangent(a, workspace_bytes, flags, st);
+    // one sweep pair of the tangent kernel: H . grad_marginals, and the
+    // parameter parts as tangents of dS/dgap and dS/dT (sw_tangent.cu); the
+    // problems it flags get the plane engine's three sweeps
+    a.dot_out = partials;
+    a.redo = flags;
+    a.sync = (int*)((char*)flags + align256((size_t)B * sizeof(int)));
+    int rc = launch_lin_tan(a, workspace_bytes, st);
+    a.redo = nullptr;
+    a.sync = nullptr;
+    a.dot_out = nullptr;
+    if (rc == D2P_OK) {
+        a.only = flags;
+        rc = launch_lin_plane(a, st);
+        if (rc) return rc;
+        a.tangent = nullptr;
+        a.out = nullptr;
+        a.dot_with = grad_marginals;
+        a.mode = MODE_PGAP;
+        a.dot_out = partials;
+        rc = launch_lin_plane(a, st);
+        if (rc) return rc;
+        a.mode = MODE_PT;
+        a.dot_out = partials + B;
+        rc = launch_lin_plane(a, st);
+        if (rc) return rc;
+        rc = launch_sum_batches(partials, 1, B, grad_gap, 0, st);
+        if (rc) return rc;
+        return launch_sum_batches(partials + B, 1, B, grad_temperature, 0, st);
+    }
+    if (rc != kNotHandled) return rc;
+    rc = run_lin_tangent(a, workspace_bytes, flags, st);
     if (rc) return rc;
     a.tangent = nullptr;
     a.out = nullptr;

@@ -72,9 +72,9 @@ struct SwArgs {
 // ints [0, kMaxParts) forward progress of each part's last warp, [kMaxParts,
 // 2 kMaxParts) reverse progress, 2 kMaxParts + 0 / + 1 two arrival counters;
 // from byte 256 on, kSyncPartDoubles doubles per part (frame base, partition
-// partial, its tangent, a dot-product partial).
+// partial, its tangent, two dot-product partials).
 constexpr int kMaxParts = 16;
-constexpr int kSyncPartDoubles = 4;
+constexpr int kSyncPartDoubles = 5;
 constexpr size_t kSyncBytes = 256 + 8 * kSyncPartDoubles * kMaxParts;
 
 // linear-domain fast path (sw_linear.cu): value + marginals without parameter
@@ -102,7 +102,9 @@ bool engine_forced_plane();
 // linear-domain tangent sweeps (sw_tangent.cu): HVP, dP/dgap, dP/dT, and the
 // dot mode (dot_with / dot_out) of the param modes; sets redo[b] for problems
 // the plane engine must recompute.  Returns -1 when the shape is not covered.
-size_t lin_tan_workspace_bytes(int B, int L1, int L2);
+// bf: the fused backward_full sweep, which also keeps the gap part of Z and
+// its tangent per cell
+size_t lin_tan_workspace_bytes(int B, int L1, int L2, bool bf = false);
 // the affine counterpart (sw_affine_tangent.cu): HVP, dP/d(gap_open),
 // dP/d(gap_ext), dP/dT and their dot mode
 size_t aff_tan_workspace_bytes(int B, int L1, int L2);

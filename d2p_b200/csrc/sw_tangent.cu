@@ -25,6 +25,15 @@
 // mode, sums weight * dmu per problem.  A problem whose frames leave the
 // window, whose partition is not finite, or whose tangent overflowed, is
 // flagged, and the caller recomputes it with the plane engine (sw_plane.cu).
+//
+// BF (backward_full in one sweep pair): the HVP along the weight plane g gives
+// grad_scores = H g (the Hessian of S is symmetric).  The parameter parts are
+// sum g dP/dgap = d(dS/dgap)[g] and sum g dP/dT = d(dS/dT)[g].  dS/dgap is
+// the sum over cells of the gap flow B gz / Z_total, with gz = G (Z_up +
+// Z_left) the gap part of Z, so its tangent along g is a per-cell sum in the
+// reverse, from gz and dgz kept by the forward.  Differentiating Euler's
+// identity S = sum s mu + gap dS/dgap + T dS/dT along g gives
+// d(dS/dT)[g] = -(sum s H g + gap d(dS/dgap)[g]) / T.
 #include <stddef.h>
 #include <stdint.h>
 
@@ -46,6 +55,8 @@ struct WarpSmem {
     float ringV[32 * kRW];    // the direction V (HVP) or the weights of the dot mode, likewise
     float zr[2][16 * 32];     // reverse: the forward's w of 16 anti-diagonals, two slots
     float dzr[2][16 * 32];    //          and its dw
+    float gzr[2][16 * 32];    //          BF: the gap part of Z
+    float dgzr[2][16 * 32];   //          and its tangent
     float er[16 * 32];        // reverse: forward frames, 16 group slots
     // staging of the neighbouring row-block's boundary values and tangents by
     // its step, and their frames by its group; tags as in sw_linear.cu
@@ -66,15 +77,17 @@ struct Layout {  // per-problem workspace
     float* hz;    // [nRB][HZ]       boundary values of each row-block, by its step
     float* hdz;   // [nRB][HZ]       and their tangents
     float* hfr;   // [nRB][HF]       and their frames, by its group
+    float* gzpl;  // [nRB][ZT][32]   BF: gap part of Z (frame E)
+    float* dgzpl; // [nRB][ZT][32]   BF: its tangent
 };
-__host__ __device__ inline size_t per_problem_bytes(int L1m, int L2m) {
+__host__ __device__ inline size_t per_problem_bytes(int L1m, int L2m, bool bf = false) {
     const size_t nrb = (size_t)(L1m + 31) / 32;
-    return 2 * align_up(nrb * zt_rows(L2m) * 32 * 4, 256) + align_up(nrb * gt_rows(L2m) * 32 * 4, 256) +
+    return (bf ? 4 : 2) * align_up(nrb * zt_rows(L2m) * 32 * 4, 256) + align_up(nrb * gt_rows(L2m) * 32 * 4, 256) +
            2 * align_up(nrb * hz_stride(L2m) * 4, 256) + align_up(nrb * hf_stride(L2m) * 4, 256);
 }
-__device__ inline Layout carve(float* ws, int b, int L1m, int L2m) {
+__device__ inline Layout carve(float* ws, int b, int L1m, int L2m, bool bf) {
     const size_t nrb = (size_t)(L1m + 31) / 32;
-    char* base = (char*)ws + (size_t)b * per_problem_bytes(L1m, L2m);
+    char* base = (char*)ws + (size_t)b * per_problem_bytes(L1m, L2m, bf);
     Layout L;
     L.zpl = (float*)base;
     base += align_up(nrb * zt_rows(L2m) * 32 * 4, 256);
@@ -87,6 +100,10 @@ __device__ inline Layout carve(float* ws, int b, int L1m, int L2m) {
     L.hdz = (float*)base;
     base += align_up(nrb * hz_stride(L2m) * 4, 256);
     L.hfr = (float*)base;
+    base += align_up(nrb * hf_stride(L2m) * 4, 256);
+    L.gzpl = bf ? (float*)base : nullptr;
+    base += align_up(nrb * zt_rows(L2m) * 32 * 4, 256);
+    L.dgzpl = bf ? (float*)base : nullptr;
     return L;
 }
 
@@ -143,6 +160,8 @@ struct FwdCtx {
     unsigned pv;         // shared address of the consumer warp's staging ring
     float* zrow;         // zpl row 0 of this row-block, this lane
     float* dzrow;        // dzpl likewise
+    float* gzrow;        // BF: gzpl, dgzpl likewise
+    float* dgzrow;
     float* erow;
     float c, G;
     Dir dir;
@@ -218,9 +237,11 @@ __device__ __forceinline__ void acc_rebase2(FwdVars& V) {
 }
 
 struct FwdOut {
-    float z, dz, zuin, dzuin, w, dw;
+    float z, dz, zuin, dzuin, w, dw, gz, dgz;
 };
-// one cell, step i of its group (vv: the lane's V at this cell, HVP only)
+// one cell, step i of its group (vv: the lane's V at this cell, HVP only).
+// BF: also the gap part of Z and its tangent (gam = 0 along a score direction).
+template <bool BF>
 __device__ __forceinline__ FwdOut fwd_cell(const FwdCtx& C, const FwdVars& V, int i, float sc, float vv) {
     FwdOut o;
     const float P = ex2f(sc * C.c);
@@ -228,16 +249,19 @@ __device__ __forceinline__ FwdOut fwd_cell(const FwdCtx& C, const FwdVars& V, in
     const float d = i == 0 ? V.f.d0 : V.f.d1, Gd = i == 0 ? V.f.Gd0 : V.f.Gd1;
     o.w = P * (V.zd + V.f.fs);
     o.dw = fmaf(o.w, vp, P * V.dzd);
-    const float rest = fmaf(C.G, V.zl + V.f.za[i], o.w);
+    const float zin = V.zl + V.f.za[i], dzin = V.dzl + V.f.dza[i];
+    const float rest = fmaf(C.G, zin, o.w);
     o.z = fmaf(Gd, V.zsh, rest);
-    const float drest = fmaf(C.G, V.dzl + V.f.dza[i], o.dw);
+    const float drest = fmaf(C.G, dzin, o.dw);
     o.dz = fmaf(C.dir.gam, o.z - o.w, fmaf(Gd, V.dzsh, drest));
+    o.gz = BF ? fmaf(Gd, V.zsh, C.G * zin) : 0.f;
+    o.dgz = BF ? fmaf(Gd, V.dzsh, C.G * dzin) : 0.f;
     o.zuin = fmaf(V.zsh, d, V.f.za[i]);
     o.dzuin = fmaf(V.dzsh, d, V.f.dza[i]);
     return o;
 }
 
-template <bool MASK, bool HV>
+template <bool MASK, bool HV, bool BF>
 __device__ __forceinline__ void fwd_stage_full(const FwdCtx& C, FwdVars& V, int k, int thr) {
     const int c0 = (kCW * k - C.lane) & (kRW - 1);
     float scv[kCW], vvv[kCW];
@@ -249,6 +273,8 @@ __device__ __forceinline__ void fwd_stage_full(const FwdCtx& C, FwdVars& V, int 
     }
     float* const pz = C.zrow + (size_t)(kCW * k) * 32;
     float* const pdz = C.dzrow + (size_t)(kCW * k) * 32;
+    float* const pgz = BF ? C.gzrow + (size_t)(kCW * k) * 32 : nullptr;
+    float* const pdgz = BF ? C.dgzrow + (size_t)(kCW * k) * 32 : nullptr;
     float* const pe = C.erow + (size_t)(kCW * k / 4) * 32;
     float zq[4], dzq[4];
 #pragma unroll
@@ -259,7 +285,7 @@ __device__ __forceinline__ void fwd_stage_full(const FwdCtx& C, FwdVars& V, int 
             if (u == kCW - 1) cp_async_wait1();
             fwd_lookahead(C, V, 4 * k + (u >> 2) + 1);
         }
-        FwdOut o = fwd_cell(C, V, i, scv[u], vvv[u]);
+        FwdOut o = fwd_cell<BF>(C, V, i, scv[u], vvv[u]);
         if (MASK) {
             const bool act = u < thr;
             o.z = act ? o.z : 0.f;
@@ -269,6 +295,10 @@ __device__ __forceinline__ void fwd_stage_full(const FwdCtx& C, FwdVars& V, int 
         V.dgsum += o.dz;
         pz[(size_t)u * 32] = o.w;
         pdz[(size_t)u * 32] = o.dw;
+        if (BF) {
+            pgz[(size_t)u * 32] = o.gz;
+            pdgz[(size_t)u * 32] = o.dgz;
+        }
         zq[i] = o.z;
         dzq[i] = o.dz;
         if (i == 3) {
@@ -285,7 +315,7 @@ __device__ __forceinline__ void fwd_stage_full(const FwdCtx& C, FwdVars& V, int 
     }
 }
 
-template <bool HV>
+template <bool HV, bool BF>
 __device__ __forceinline__ void fwd_stage_start(const FwdCtx& C, FwdVars& V, int k) {
     const bool live = C.lane < C.nv;
     float zq[4], dzq[4];
@@ -307,13 +337,17 @@ __device__ __forceinline__ void fwd_stage_start(const FwdCtx& C, FwdVars& V, int
                 fwd_lookahead(C, V, 4 * k + q + 1);
             }
             const int col = j0 & (kRW - 1);
-            FwdOut o = fwd_cell(C, V, i, C.ring[col], HV ? C.vring[col] : 0.f);
+            FwdOut o = fwd_cell<BF>(C, V, i, C.ring[col], HV ? C.vring[col] : 0.f);
             o.z = act ? o.z : 0.f;
             o.dz = act ? o.dz : 0.f;
             V.gsum += o.z;
             V.dgsum += o.dz;
             C.zrow[(size_t)t * 32] = o.w;
             C.dzrow[(size_t)t * 32] = o.dw;
+            if (BF) {
+                C.gzrow[(size_t)t * 32] = o.gz;
+                C.dgzrow[(size_t)t * 32] = o.dgz;
+            }
             zq[i] = o.z;
             dzq[i] = o.dz;
             if (i == 3) {
@@ -353,8 +387,10 @@ struct RevVars {
     RevF nf;
     int ebmin, ebmax;
     float chk;              // fma(dmu, 0, chk) over the lane's cells: not 0 if a tangent overflowed
-    float sdot;             // dot mode: this stage's sum of weight * dmu
+    float sdot;             // dot mode: this stage's sum of weight * dmu (BF: score * dmu)
     double dot;
+    float sgap;             // BF: this stage's sum of the gap flows' tangents
+    double dot2;
 };
 
 struct RevCtx {
@@ -362,6 +398,8 @@ struct RevCtx {
     const float* vring;
     const float* zr;      // WarpSmem::zr, dzr
     const float* dzr;
+    const float* gzr;     // BF: WarpSmem::gzr, dgzr
+    const float* dgzr;
     const float* er;
     const float* bv;      // bottom lane: staged messages, tangents (bv + kHR), frames of the row-block below
     const float* bf;
@@ -436,14 +474,16 @@ __device__ __forceinline__ void rev_apply(RevVars& V) {
 }
 
 struct RevOut {
-    float b, pb, msg, db, dpb, dmsg, dmu;
+    float b, pb, msg, db, dpb, dmsg, dmu, dgf;
 };
 // one cell, step i of its group: vv the lane's V here (HVP), w / dw the
 // forward's diagonal term and its tangent.  PG: the marginal itself (in dmu),
 // no tangent of the reverse.
-template <bool PG>
+// BF: gz / dgz the forward's gap part of Z and its tangent; dgf the tangent of
+// the cell's gap flow B gz / Z_total
+template <bool PG, bool BF>
 __device__ __forceinline__ RevOut rev_cell(const RevCtx& C, const RevVars& V, int i, float sc, float vv, float w,
-                                           float dw) {
+                                           float dw, float gz, float dgz) {
     RevOut o;
     const float P = ex2f(sc * C.c);
     const float vp = fmaf(C.dir.vs, vv, C.dir.ss * sc);
@@ -452,6 +492,7 @@ __device__ __forceinline__ RevOut rev_cell(const RevCtx& C, const RevVars& V, in
     o.b = fmaf(d, V.rsh, rest);
     o.msg = fmaf(Gd, V.rsh, fmaf(C.G, rest, V.pbp));
     o.pb = P * o.b;
+    o.dgf = 0.f;
     if (PG) {
         o.db = o.dmsg = o.dpb = 0.f;
         o.dmu = o.b * (w * V.f.kE);
@@ -463,28 +504,42 @@ __device__ __forceinline__ RevOut rev_cell(const RevCtx& C, const RevVars& V, in
     o.dpb = P * fmaf(vp, o.b, o.db);
     const float mu = o.b * (w * V.f.kE);
     o.dmu = fmaf(fmaf(o.db, w, o.b * dw), V.f.kE, -mu * C.dSr);
+    if (BF) {
+        const float gf = o.b * (gz * V.f.kE);
+        o.dgf = fmaf(fmaf(o.db, gz, o.b * dgz), V.f.kE, -gf * C.dSr);
+    }
     return o;
 }
 
 // DOT: sum gm * dmu; PG: write the marginal and sum score * marginal (gm is
 // the score); otherwise write dmu
-template <bool DOT, bool PG>
-__device__ __forceinline__ void rev_emit(const RevCtx& C, RevVars& V, float* slot, float gm, float dmu, bool act) {
+template <bool DOT, bool PG, bool BF>
+__device__ __forceinline__ void rev_emit(const RevCtx& C, RevVars& V, float* slot, float gm, float dmu, bool act,
+                                         float sc, float dgf) {
     if (act) V.chk = fmaf(dmu, 0.f, V.chk);
     if (DOT || PG) {
         if (act) V.sdot = fmaf(gm, dmu, V.sdot);  // a cell outside the problem may hold inf: no 0 * inf
+    }
+    if (BF) {
+        if (act) {
+            V.chk = fmaf(dgf, 0.f, V.chk);
+            V.sdot = fmaf(sc, dmu, V.sdot);
+            V.sgap += dgf;
+        }
     }
     if (!DOT) {
         if (act) *slot = dmu;
     }
 }
 
-template <bool MASK, bool HV, bool DOT, bool PG>
+template <bool MASK, bool HV, bool DOT, bool PG, bool BF>
 __device__ __forceinline__ void rev_stage_full(const RevCtx& C, RevVars& V, int k, int thr) {
     const int m16 = C.P + 16 - kCW * k;
     const int slot = ((m16 >> 4) & 1) * (16 * 32) + C.lane;
     const float* const zb = C.zr + slot;
     const float* const dzb = C.dzr + slot;
+    const float* const gzb = BF ? C.gzr + slot : nullptr;
+    const float* const dgzb = BF ? C.dgzr + slot : nullptr;
     const int cb = (C.P + 31 - kCW * k - C.lane) & (kRW - 1);
     float scv[kCW], vvv[kCW];
 #pragma unroll
@@ -502,11 +557,12 @@ __device__ __forceinline__ void rev_stage_full(const RevCtx& C, RevVars& V, int 
             if (u == kCW - 1) cp_async_wait1();
             rev_lookahead(C, V, 4 * k + (u >> 2) + 1);
         }
-        const RevOut o =
-            rev_cell<PG>(C, V, i, scv[u], DOT ? 0.f : vvv[u], zb[(15 - u) * 32], PG ? 0.f : dzb[(15 - u) * 32]);
+        const RevOut o = rev_cell<PG, BF>(C, V, i, scv[u], DOT ? 0.f : vvv[u], zb[(15 - u) * 32],
+                                          PG ? 0.f : dzb[(15 - u) * 32], BF ? gzb[(15 - u) * 32] : 0.f,
+                                          BF ? dgzb[(15 - u) * 32] : 0.f);
         const bool act = !MASK || u < thr;
         const int col = (u <= cb) ? cb - u : cb - u + kRW;
-        rev_emit<DOT, PG>(C, V, C.ring + col, PG ? scv[u] : vvv[u], o.dmu, act);
+        rev_emit<DOT, PG, BF>(C, V, C.ring + col, PG ? scv[u] : vvv[u], o.dmu, act, scv[u], o.dgf);
         const float msg = act ? o.msg : 0.f, dmsg = act ? o.dmsg : 0.f;
         mq[i] = msg;
         dmq[i] = dmsg;
@@ -522,12 +578,14 @@ __device__ __forceinline__ void rev_stage_full(const RevCtx& C, RevVars& V, int 
     }
 }
 
-template <bool HV, bool DOT, bool PG>
+template <bool HV, bool DOT, bool PG, bool BF>
 __device__ __forceinline__ void rev_stage_part(const RevCtx& C, RevVars& V, int k) {
     const int m16 = C.P + 16 - kCW * k;
     const int slot = ((m16 >> 4) & 1) * (16 * 32) + C.lane;
     const float* const zb = C.zr + slot;
     const float* const dzb = C.dzr + slot;
+    const float* const gzb = BF ? C.gzr + slot : nullptr;
+    const float* const dgzb = BF ? C.dgzr + slot : nullptr;
     const bool live = C.lane < C.nv;
     float mq[4], dmq[4];
 #pragma unroll 1
@@ -550,8 +608,10 @@ __device__ __forceinline__ void rev_stage_part(const RevCtx& C, RevVars& V, int 
             }
             const int ci = j0 & (kRW - 1);
             const float vv = HV ? C.vring[ci] : 0.f, sc = C.ring[ci];
-            const RevOut o = rev_cell<PG>(C, V, i, sc, DOT ? 0.f : vv, zb[(15 - u) * 32], PG ? 0.f : dzb[(15 - u) * 32]);
-            rev_emit<DOT, PG>(C, V, C.ring + ci, PG ? sc : vv, o.dmu, act);
+            const RevOut o = rev_cell<PG, BF>(C, V, i, sc, DOT ? 0.f : vv, zb[(15 - u) * 32],
+                                              PG ? 0.f : dzb[(15 - u) * 32], BF ? gzb[(15 - u) * 32] : 0.f,
+                                              BF ? dgzb[(15 - u) * 32] : 0.f);
+            rev_emit<DOT, PG, BF>(C, V, C.ring + ci, PG ? sc : vv, o.dmu, act, sc, o.dgf);
             const float msg = act ? o.msg : 0.f, dmsg = act ? o.dmsg : 0.f;
             mq[i] = msg;
             dmq[i] = dmsg;
@@ -582,7 +642,7 @@ __device__ __forceinline__ void rev_stage_part(const RevCtx& C, RevVars& V, int 
 // carries the tangent along gap (dS/dgap = T dZ/Z), the reverse writes the
 // marginals and sums score x marginal, and dS/dT follows from Euler's identity
 // for the degree-1 homogeneous S(s, gap, T): S = sum s mu + gap dS/dgap + T dS/dT.
-template <bool HV, bool DOT, bool SPLIT, bool PG>
+template <bool HV, bool DOT, bool SPLIT, bool PG, bool BF>
 __global__ void __launch_bounds__(kNW * 32, 1) lin_tan_kernel(SwArgs p) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     WarpSmem& W = reinterpret_cast<WarpSmem*>(smem_raw)[threadIdx.x >> 5];
@@ -619,7 +679,7 @@ __global__ void __launch_bounds__(kNW * 32, 1) lin_tan_kernel(SwArgs p) {
     const float* __restrict__ S = p.scores + (size_t)b * plane;
     const float* __restrict__ Vp = HV ? (DOT ? p.dot_with : p.tangent) + (size_t)b * plane : nullptr;
     float* __restrict__ out = (!DOT && p.out) ? p.out + (size_t)b * plane : nullptr;
-    const Layout LY = carve(p.ws, b, L1m, L2m);
+    const Layout LY = carve(p.ws, b, L1m, L2m, BF);
     const int nRB = (L1 + 31) / 32;
     const int nch = (L2 + kCW - 1) / kCW;
     const size_t zst = (size_t)zt_rows(L2m) * 32;
@@ -634,6 +694,7 @@ __global__ void __launch_bounds__(kNW * 32, 1) lin_tan_kernel(SwArgs p) {
     if (L1 == 0 || L2 == 0) {  // no cells: the output is all zeros
         if (threadIdx.x == 0 && part == 0) {
             if (DOT && p.dot_out) p.dot_out[b] = 0.f;
+            if (BF && p.dot_out) p.dot_out[b] = p.dot_out[p.B + b] = 0.f;
             if (PG) {  // S = log(1) = 0, and so its derivatives
                 if (p.value) p.value[b] = 0.f;
                 if (p.grad_gap) p.grad_gap[b] = 0.f;
@@ -729,6 +790,8 @@ __global__ void __launch_bounds__(kNW * 32, 1) lin_tan_kernel(SwArgs p) {
         C.pv = (unsigned)__cvta_generic_to_shared(Wn.sv);
         C.zrow = LY.zpl + (size_t)r * zst + lane;
         C.dzrow = LY.dzpl + (size_t)r * zst + lane;
+        C.gzrow = BF ? LY.gzpl + (size_t)r * zst + lane : nullptr;
+        C.dgzrow = BF ? LY.dgzpl + (size_t)r * zst + lane : nullptr;
         C.erow = LY.efr + (size_t)r * est + lane;
         C.c = c;
         C.G = G;
@@ -774,11 +837,11 @@ __global__ void __launch_bounds__(kNW * 32, 1) lin_tan_kernel(SwArgs p) {
                 fwd_lookahead(C, V, 0);
             }
             if (kCW * k < 31)
-                fwd_stage_start<HV && !DOT>(C, V, k);
+                fwd_stage_start<HV && !DOT, BF>(C, V, k);
             else if (nv == 32 && kCW * k + kCW - 1 <= L2 - 1)
-                fwd_stage_full<false, HV && !DOT>(C, V, k, 0);
+                fwd_stage_full<false, HV && !DOT, BF>(C, V, k, 0);
             else
-                fwd_stage_full<true, HV && !DOT>(C, V, k, lane < nv ? L2 + lane - kCW * k : -1);
+                fwd_stage_full<true, HV && !DOT, BF>(C, V, k, lane < nv ? L2 + lane - kCW * k : -1);
             acc_rebase2(V);
             if (V.push) Wn.tag[k & (kHR / 16 - 1)] = (r << 16) | k;
             __syncwarp();
@@ -864,18 +927,23 @@ __global__ void __launch_bounds__(kNW * 32, 1) lin_tan_kernel(SwArgs p) {
     RV.ebmin = RV.ebmax = 0x3f800000;
     RV.chk = 0.f;
     RV.dot = 0.0;
+    RV.dot2 = 0.0;
     for (int q = gw; q < nRB; q += NWt) {
         const int r = nRB - 1 - q;
         const int nv = min(32, L1 - 32 * r);
         const bool hasBelow = r + 1 < nRB, hasAbove = r > 0;
         const float* const zblk = LY.zpl + (size_t)r * zst;
         const float* const dzblk = LY.dzpl + (size_t)r * zst;
+        const float* const gzblk = BF ? LY.gzpl + (size_t)r * zst : nullptr;
+        const float* const dgzblk = BF ? LY.dgzpl + (size_t)r * zst : nullptr;
         const float* const eblk = LY.efr + (size_t)r * est;
         RevCtx C;
         C.ring = W.ringS + lane * kRW;
         C.vring = W.ringV + lane * kRW;
         C.zr = &W.zr[0][0];
         C.dzr = &W.dzr[0][0];
+        C.gzr = &W.gzr[0][0];
+        C.dgzr = &W.dgzr[0][0];
         C.er = W.er;
         C.bv = (hasBelow && lane == nv - 1) ? W.sv : zv;
         C.bf = (hasBelow && lane == nv - 1) ? W.sf : zf;
@@ -911,6 +979,10 @@ __global__ void __launch_bounds__(kNW * 32, 1) lin_tan_kernel(SwArgs p) {
                 const int e = 4 * (lane + 32 * it);
                 cp_async16(&W.zr[M & 1][0] + e, zblk + o16 + e, 16);
                 cp_async16(&W.dzr[M & 1][0] + e, dzblk + o16 + e, 16);
+                if (BF) {
+                    cp_async16(&W.gzr[M & 1][0] + e, gzblk + o16 + e, 16);
+                    cp_async16(&W.dgzr[M & 1][0] + e, dgzblk + o16 + e, 16);
+                }
             }
             const int gl = 4 * M - 1;
 #pragma unroll
@@ -958,13 +1030,15 @@ __global__ void __launch_bounds__(kNW * 32, 1) lin_tan_kernel(SwArgs p) {
             }
             if (k == 0) rev_lookahead(C, RV, 0);
             RV.sdot = 0.f;
+            RV.sgap = 0.f;
             if (kCW * k <= P + 32 - L2)
-                rev_stage_part<HV, DOT, PG>(C, RV, k);
+                rev_stage_part<HV, DOT, PG, BF>(C, RV, k);
             else if (nv == 32 && kCW * k + kCW - 1 <= P - 1)
-                rev_stage_full<false, HV, DOT, PG>(C, RV, k, 0);
+                rev_stage_full<false, HV, DOT, PG, BF>(C, RV, k, 0);
             else
-                rev_stage_full<true, HV, DOT, PG>(C, RV, k, lane < nv ? 16 * M + 16 - lane : -1);
-            if (DOT || PG) RV.dot += (double)RV.sdot;
+                rev_stage_full<true, HV, DOT, PG, BF>(C, RV, k, lane < nv ? 16 * M + 16 - lane : -1);
+            if (DOT || PG || BF) RV.dot += (double)RV.sdot;
+            if (BF) RV.dot2 += (double)RV.sgap;
             if (RV.push) Wn.tag[k & (kHR / 16 - 1)] = (q << 16) | k;
             __syncwarp();
             if (lane == 0) {
@@ -991,28 +1065,38 @@ __global__ void __launch_bounds__(kNW * 32, 1) lin_tan_kernel(SwArgs p) {
     const int o_acc = __syncthreads_or(fwd_out & 8);
     const int o_tan = __syncthreads_or(RV.chk != 0.f ? 1 : 0);
     const int redo = (o_win ? 1 : 0) | (sh_err ? 2 : 0) | (sh_bad ? 4 : 0) | (o_acc ? 8 : 0) | (o_tan ? 16 : 0);
-    if (DOT || PG) {
+    if (DOT || PG || BF) {
         const double tot = block_sum_d(RV.dot, red);
+        const double tot2 = BF ? block_sum_d(RV.dot2, red) : 0.0;
         if (threadIdx.x == 0) {
-            // DOT: the weighted sum; PG: dS/dT = (S - sum s mu - gap dS/dgap) / T
-            auto finish = [&](double all) {
+            // DOT: the weighted sum; PG: dS/dT = (S - sum s mu - gap dS/dgap) / T;
+            // BF: d(dS/dgap)[g] and d(dS/dT)[g] = -(sum s H g + gap d(dS/dgap)[g]) / T
+            auto finish = [&](double all, double all2) {
                 if (DOT && p.dot_out) p.dot_out[b] = (float)all;
                 if (PG && p.grad_T) {
                     const double S = ((double)sh_Sint + (double)sh_Sfrac) / (double)c;
                     const double dgap = (double)sh_dSr * (double)T;
                     p.grad_T[b] = (float)((S - all - (double)gapn * dgap) / (double)T);
                 }
+                if (BF && p.dot_out) {
+                    p.dot_out[b] = (float)all2;
+                    p.dot_out[p.B + b] = (float)(-(all + (double)gapn * all2) / (double)T);
+                }
             };
             if (SPLIT && K > 1) {  // the last part to arrive sums the parts in order
                 gpart[kSyncPartDoubles * part + 3] = tot;
+                if (BF) gpart[kSyncPartDoubles * part + 4] = tot2;
                 if (atom_add_release_gpu(gsync + 2 * kMaxParts + 1, 1) == K - 1) {
                     (void)ld_acquire_gpu(gsync + 2 * kMaxParts + 1);
-                    double all = 0.0;
-                    for (int k = 0; k < K; ++k) all += gpart[kSyncPartDoubles * k + 3];
-                    finish(all);
+                    double all = 0.0, all2 = 0.0;
+                    for (int k = 0; k < K; ++k) {
+                        all += gpart[kSyncPartDoubles * k + 3];
+                        if (BF) all2 += gpart[kSyncPartDoubles * k + 4];
+                    }
+                    finish(all, all2);
                 }
             } else {
-                finish(tot);
+                finish(tot, tot2);
             }
         }
     }
@@ -1027,9 +1111,9 @@ __global__ void __launch_bounds__(kNW * 32, 1) lin_tan_kernel(SwArgs p) {
 }  // namespace ltan
 
 // ------------------------------------------------------------------ host side
-size_t lin_tan_workspace_bytes(int B, int L1, int L2) {
+size_t lin_tan_workspace_bytes(int B, int L1, int L2, bool bf) {
     if (L1 > 32 * ltan::kMaxRB || L2 % 4 != 0) return 0;
-    return ltan::per_problem_bytes(L1, L2) * (size_t)B;
+    return ltan::per_problem_bytes(L1, L2, bf) * (size_t)B;
 }
 
 int launch_lin_tan(const SwArgs& a, size_t ws_bytes, cudaStream_t st) {
@@ -1038,6 +1122,9 @@ int launch_lin_tan(const SwArgs& a, size_t ws_bytes, cudaStream_t st) {
     if (!a.redo || engine_forced_plane()) return -1;
     if (a.L2 % 4 != 0 || a.L1 > 32 * ltan::kMaxRB || a.L1 == 0 || a.L2 == 0) return -1;
     const bool dot = a.dot_with != nullptr;
+    // backward_full in one sweep pair: the HVP along the weights (tangent),
+    // with dot_out receiving [B] d(dS/dgap) and [B] d(dS/dT)
+    const bool bf = a.mode == MODE_HVP && !dot && a.dot_out != nullptr;
     const bool hv = a.mode == MODE_HVP || dot;
     if (a.mode == MODE_HVP && (dot || !a.tangent)) return -1;
     if (dot && !a.dot_out) return -1;
@@ -1047,7 +1134,7 @@ int launch_lin_tan(const SwArgs& a, size_t ws_bytes, cudaStream_t st) {
     if (!a.scores || !al16(a.scores) || (a.out && !al16(a.out)) || !al16(a.ws) || !a.ws) return -1;
     if ((a.tangent && !al16(a.tangent)) || (dot && !al16(a.dot_with))) return -1;
     if ((((uintptr_t)a.ws) & 255) != 0) return -1;
-    if (ws_bytes < ltan::per_problem_bytes(a.L1, a.L2) * (size_t)a.B) return -1;
+    if (ws_bytes < ltan::per_problem_bytes(a.L1, a.L2, bf) * (size_t)a.B) return -1;
     const size_t smem = sizeof(ltan::WarpSmem) * ltan::kNW;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -1055,14 +1142,16 @@ int launch_lin_tan(const SwArgs& a, size_t ws_bytes, cudaStream_t st) {
     static int sms[64] = {0};
     static bool attr_set[64] = {false};
     if (dev < 64 && !attr_set[dev]) {
-        const void* ks[8] = {(const void*)ltan::lin_tan_kernel<true, false, false, false>,
-                             (const void*)ltan::lin_tan_kernel<false, false, false, false>,
-                             (const void*)ltan::lin_tan_kernel<true, true, false, false>,
-                             (const void*)ltan::lin_tan_kernel<true, false, true, false>,
-                             (const void*)ltan::lin_tan_kernel<false, false, true, false>,
-                             (const void*)ltan::lin_tan_kernel<true, true, true, false>,
-                             (const void*)ltan::lin_tan_kernel<false, false, false, true>,
-                             (const void*)ltan::lin_tan_kernel<false, false, true, true>};
+        const void* ks[10] = {(const void*)ltan::lin_tan_kernel<true, false, false, false, false>,
+                              (const void*)ltan::lin_tan_kernel<false, false, false, false, false>,
+                              (const void*)ltan::lin_tan_kernel<true, true, false, false, false>,
+                              (const void*)ltan::lin_tan_kernel<true, false, true, false, false>,
+                              (const void*)ltan::lin_tan_kernel<false, false, true, false, false>,
+                              (const void*)ltan::lin_tan_kernel<true, true, true, false, false>,
+                              (const void*)ltan::lin_tan_kernel<false, false, false, true, false>,
+                              (const void*)ltan::lin_tan_kernel<false, false, true, true, false>,
+                              (const void*)ltan::lin_tan_kernel<true, false, false, false, true>,
+                              (const void*)ltan::lin_tan_kernel<true, false, true, false, true>};
         for (const void* k : ks) {
             e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
             if (e == cudaSuccess)
@@ -1087,22 +1176,25 @@ int launch_lin_tan(const SwArgs& a, size_t ws_bytes, cudaStream_t st) {
         if (e == cudaSuccess) e = cudaMemsetAsync(s.redo, 0, sizeof(int) * (size_t)a.B, st);
         if (e != cudaSuccess) return (int)e;
         void* args[1] = {&s};
-        const void* k = pg    ? (const void*)ltan::lin_tan_kernel<false, false, true, true>
-                        : dot ? (const void*)ltan::lin_tan_kernel<true, true, true, false>
-                        : hv  ? (const void*)ltan::lin_tan_kernel<true, false, true, false>
-                              : (const void*)ltan::lin_tan_kernel<false, false, true, false>;
+        const void* k = pg    ? (const void*)ltan::lin_tan_kernel<false, false, true, true, false>
+                        : bf  ? (const void*)ltan::lin_tan_kernel<true, false, true, false, true>
+                        : dot ? (const void*)ltan::lin_tan_kernel<true, true, true, false, false>
+                        : hv  ? (const void*)ltan::lin_tan_kernel<true, false, true, false, false>
+                              : (const void*)ltan::lin_tan_kernel<false, false, true, false, false>;
         e = cudaLaunchCooperativeKernel(k, dim3(a.B * K), dim3(ltan::kNW * 32), args, smem, st);
         if (e == cudaSuccess) return 0;
         cudaGetLastError();  // does not fit: one CTA per problem instead
     }
     if (pg)
-        ltan::lin_tan_kernel<false, false, false, true><<<a.B, ltan::kNW * 32, smem, st>>>(a);
+        ltan::lin_tan_kernel<false, false, false, true, false><<<a.B, ltan::kNW * 32, smem, st>>>(a);
+    else if (bf)
+        ltan::lin_tan_kernel<true, false, false, false, true><<<a.B, ltan::kNW * 32, smem, st>>>(a);
     else if (dot)
-        ltan::lin_tan_kernel<true, true, false, false><<<a.B, ltan::kNW * 32, smem, st>>>(a);
+        ltan::lin_tan_kernel<true, true, false, false, false><<<a.B, ltan::kNW * 32, smem, st>>>(a);
     else if (hv)
-        ltan::lin_tan_kernel<true, false, false, false><<<a.B, ltan::kNW * 32, smem, st>>>(a);
+        ltan::lin_tan_kernel<true, false, false, false, false><<<a.B, ltan::kNW * 32, smem, st>>>(a);
     else
-        ltan::lin_tan_kernel<false, false, false, false><<<a.B, ltan::kNW * 32, smem, st>>>(a);
+        ltan::lin_tan_kernel<false, false, false, false, false><<<a.B, ltan::kNW * 32, smem, st>>>(a);
     return (int)cudaGetLastError();
 }
 

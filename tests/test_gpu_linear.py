@@ -96,6 +96,7 @@ def test_backward_full(d2p, cuda_device, B, L1, L2, T, gap):
 TAN = [  # (B, L1, L2, T, gap, ragged)
     (2, 33, 64, 1.0, -1.0, False), (3, 100, 36, 0.5, -1.0, False), (2, 130, 260, 1.0, -0.5, False),
     (1, 200, 8, 1.0, -1.0, False), (4, 70, 96, 1.0, -1.0, True), (1, 7, 512, 2.0, -1.0, False),
+    (2, 40, 64, 0.1, -1.0, False),  # flagged at T = 0.1: the plane engine's sweeps
 ]
 
 
