@@ -573,7 +573,7 @@ __global__ void __launch_bounds__(NW * 32, MINB) lin_fast_kernel(SwArgs p) {
         progF[threadIdx.x] = -1;
         progR[threadIdx.x] = -1;
     }
-    if (threadIdx.x < kHR) zv[threadIdx.x] = 0.f;
+    for (int i = threadIdx.x; i < kHR; i += blockDim.x) zv[i] = 0.f;
     if (threadIdx.x < kHR / 4) zf[threadIdx.x] = 0.f;
     if (lane < kHR / 16) W.tag[lane] = -1;
     if (threadIdx.x == 0) {

@@ -483,3 +483,24 @@ def test_fp64_error_not_worse_than_reference_512(d2p, cuda_device):
     print(f"512x512 marginal max|err| vs fp64: ours {e_ours:.3e}  reference fp32 {e_ref:.3e}")
     assert e_ours <= e_ref
     check("value", v, r64["value"], r32["value"])
+
+
+def test_many_waves_ragged(d2p, cuda_device):
+    """A ragged batch of several waves of CTAs (ordered by cost): parity with
+    the oracle on a sample of problems, zero padding, bitwise repeatable."""
+    B, L1, L2 = 640, 96, 128
+    s = scores(B, L1, L2, seed=640)
+    ln = lengths_for(B, L1, L2, seed=641, lo=8)
+    sd, lnd = s.to(cuda_device), ln.to(cuda_device)
+    v, m = torch.ops.d2p.soft_sw_float(sd, -1.0, 1.0, lnd)
+    v2, m2 = torch.ops.d2p.soft_sw_float(sd, -1.0, 1.0, lnd)
+    assert torch.equal(v, v2) and torch.equal(m, m2)
+    idx = list(range(0, B, 37)) + [B - 1]
+    r64 = oracle.sw_linear(s[idx].numpy(), ln[idx].numpy(), -1.0, 1.0, "f64")
+    r32 = oracle.sw_linear(s[idx].numpy(), ln[idx].numpy(), -1.0, 1.0, "f32")
+    check("value", v[idx], r64["value"], r32["value"])
+    check("marginals", m[idx], r64["marginals"], r32["marginals"])
+    mc = m.cpu()
+    for k, b in enumerate(idx):
+        l1, l2 = ln[b].tolist()
+        assert torch.count_nonzero(mc[b, l1:, :]) == 0 and torch.count_nonzero(mc[b, :, l2:]) == 0
