@@ -187,6 +187,16 @@ D2P_API int d2p_sw_affine_backward_full(const float* scores, const float* grad_m
                                 float* grad_temperature, void* workspace,
                                 size_t workspace_bytes, void* stream);
 
+/* Diagnostic: runs the kernels' bounded wait on a progress word that nothing
+ * ever sets, on `stream`, and writes 1 to *status (device int) once the wait
+ * has given up (0 would mean it saw the word set).  scope 0: a word in shared
+ * memory (the wait between warps of one CTA); scope 1: the global word `word`
+ * (device int, 0 and left untouched by the caller; the wait between the CTAs
+ * of a problem spread over several CTAs).  The wait ends after its poll limit
+ * (well under a second to a few seconds, depending on the scope) and the
+ * context stays usable.  No counterpart in the reference. */
+D2P_API int d2p_wait_selftest(int scope, const int* word, int* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
