@@ -32,9 +32,11 @@
 // reused for its output (alpha in the forward, the marginal in the reverse).
 //
 // Reverse pass: beta is propagated in push form through registers and shuffles
-// (no atomics, deterministic):
-//   beta_ij = 2^min(a_ij - S, 0) + sum over successors of beta_succ * w(succ <- ij)
-//   marginal_ij = beta_ij * (w_align + w_sky),  dS/dgap = sum beta*(w_up + w_left),
+// (no atomics, deterministic).  With N_ij the sum of the cell's four incoming
+// weights (1 up to rounding; dividing by it keeps the rounding of the stored
+// alpha from scaling the flow, as the reference's softmax does):
+//   beta_ij = 2^min(a_ij - S, 0) + sum over successors of beta_succ * w(succ <- ij) / N_succ
+//   marginal_ij = beta_ij (w_align + w_sky) / N_ij,  dS/dgap = sum beta (w_up + w_left) / N,
 //   dS/dT = path entropy (sum of non-negative terms).
 // Semantics follow the reference (src/sw/kernels_cpu.cpp:70-279).
 #include <stdint.h>
@@ -294,15 +296,24 @@ __device__ __forceinline__ RevCell rev_cell(const RevCtx& C, const RevVars& V, f
     const float lp = fminf(a + c0, 0.f);
     const float binit = ex2f(lp);
     const float beta = binit + (V.pleft + inc);
+    // The cell's incoming weights are divided by their own sum N (1 up to the
+    // rounding of the stored alpha, >= 1/4), as the reference's softmax
+    // normalises them (src/sw/kernels_cpu.cpp:41-62): the rounding of a large
+    // alpha then cancels out of the flow through the cell instead of adding up
+    // along the paths (at T = 0.1 it took the marginals to 2.5-3.6x the
+    // reference's own fp32 error).
+    const float N = (wa + wsk) + (wu + wl);
+    const float bn = __fdividef(beta, N);
     RevCell r;
-    const float pu = beta * wu;
-    r.pd = beta * wa;
-    r.pl = beta * wl;
+    const float pu = bn * wu;
+    r.pd = bn * wa;
+    r.pl = bn * wl;
     r.send = pu + V.pdiag;
     r.gs = pu + r.pl;
+    // local choice entropy of the normalised weights: h / N + lg2 N
     const float h = -fmaf(wu, eu, fmaf(wl, el, fmaf(wa, ea, wsk * es)));
-    r.hs = fmaf(beta, h, -binit * lp);
-    r.wsum = beta * (wa + wsk);
+    r.hs = fmaf(bn, h, fmaf(beta, lg2f(N), -binit * lp));
+    r.wsum = bn * (wa + wsk);
     return r;
 }
 
