@@ -517,3 +517,47 @@ def test_many_waves_ragged(d2p, cuda_device):
     for k, b in enumerate(idx):
         l1, l2 = ln[b].tolist()
         assert torch.count_nonzero(mc[b, l1:, :]) == 0 and torch.count_nonzero(mc[b, :, l2:]) == 0
+
+
+def _kernel_names(fn):
+    from torch.profiler import ProfilerActivity, profile
+
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        fn()
+        torch.cuda.synchronize()
+    return [e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA]
+
+
+@pytest.mark.parametrize("B,L1,L2", [(1, 6, 7), (2, 64, 96)])
+def test_value_backward_runs_no_tangent_sweep(d2p, cuda_device, B, L1, L2):
+    """The reference's behaviour, checked by kernel name in its own test
+    (tests/test_soft_sw_regular.py:721-743): a backward that only reaches the
+    value runs no HVP or parameter-Jacobian sweep; one that reaches the
+    marginals (even with a zero gradient) does.  The kernels here are named
+    after this library's engines: the tangent sweeps are lin_tan_kernel
+    (linear-domain; HVP and both Jacobians fused into one sweep pair for
+    backward_full) or lin_plane_kernel<1..4> (plane engine: HVP, dP/dgap, dP/dT)
+    on shapes the linear-domain kernels do not take (a row length that is not a
+    multiple of 4)."""
+    def tangent(names):
+        return [n for n in names if "lin_tan_kernel" in n or any(f"lin_plane_kernel<{m}>" in n for m in (1, 2, 4))]
+
+    def value_only():
+        s = torch.randn(B, L1, L2, device=cuda_device, generator=torch.Generator(cuda_device).manual_seed(1),
+                        requires_grad=True)
+        v, _ = torch.ops.d2p.soft_sw_float(s, -1.0, 1.0, None)
+        v.sum().backward()
+
+    def zero_marginal_grad():
+        s = torch.randn(B, L1, L2, device=cuda_device, generator=torch.Generator(cuda_device).manual_seed(1),
+                        requires_grad=True)
+        v, m = torch.ops.d2p.soft_sw_float(s, -1.0, 1.0, None)
+        (v.sum() + 0.0 * m.sum()).backward()
+
+    value_only()  # warm-up outside the profiler
+    names = _kernel_names(value_only)
+    assert names, "no CUDA kernels recorded"
+    assert not tangent(names), tangent(names)
+    names = _kernel_names(zero_marginal_grad)
+    assert tangent(names), names
