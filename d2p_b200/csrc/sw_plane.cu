@@ -26,12 +26,14 @@
 // k-1) and the planes store a - F[k].  Differences of frames are exact, so every
 // weight 2^(v - a) is formed from small numbers.  S is kept as integer + fraction.
 //
-// The linear value + marginals mode is the exception: it is the fix-up of every
-// problem the linear-domain kernels flag (low temperatures, extreme scores), so
-// it follows the reference's arithmetic instead -- alpha in score units, and in
-// the reverse pass each cell's incoming weights divided by their own sum, like
-// the reference's softmax.  The rounding of a large stored alpha then cancels
-// out of the flow through the cell instead of accumulating along the paths.
+// The value + marginals modes are the fix-up of every problem the
+// linear-domain kernels flag (low temperatures, extreme scores), so their
+// reverse passes follow the reference's arithmetic: each cell's (each state's)
+// incoming weights are divided by their own sum, like the reference's softmax,
+// and every exponent is formed with the large values cancelling first.  The
+// rounding of a large stored alpha then cancels out of the flow through the
+// cell instead of accumulating along the paths.  The linear mode also keeps
+// alpha in score units, as the reference does.
 //
 // The linear-domain kernels (sw_linear.cu, sw_affine_fast.cu, sw_tangent.cu,
 // sw_affine_tangent.cu) supersede this engine where their range allows; this
@@ -335,7 +337,7 @@ __global__ void __launch_bounds__(kPlaneThreads) lin_plane_kernel(SwArgs p) {
     double gsum = 0.0, hsum = 0.0;
     float dsum = 0.f;
     for (int k = L1 + L2; k >= 2; --k) {
-        const float F0 = Fg[k], Fm1 = Fg[k - 1], Fm2 = Fg[k - 2], Fp1 = Fg[k + 1], Fp2 = Fg[k + 2];
+        const float F0 = Fg[k], Fm2 = Fg[k - 2], Fp1 = Fg[k + 1], Fp2 = Fg[k + 2];
         const int ilo = max(1, k - L2), ihi = min(L1, k - 1);
         for (int i = ilo + threadIdx.x; i <= ihi; i += blockDim.x) {
             const int j = k - i;
@@ -653,6 +655,88 @@ __global__ void __launch_bounds__(kPlaneThreads) aff_plane_kernel(SwArgs p) {
             const float lpd = fminf((ad - Sfrac) + (F0 - Sint), 0.f);
             const float bim = ex2f(lpm), bii = ex2f(lpi), bid = ex2f(lpd);
             float bm = bim, bi = bii, bd = bid;
+            if (MODE == MODE_MARG) {
+                // Value + marginals, the fix-up of problems the linear-domain
+                // kernels flag (low temperatures, extreme scores).  Every exponent
+                // is formed with the two framed alphas cancelling first, and each
+                // state's incoming weights are divided by their sum N, as the
+                // reference's softmax normalises them (src/sw_affine/kernels_cpu.cpp:
+                // 53-87, :199-346): the rounding of a large stored alpha then does
+                // not scale the flow through the cell.  B* hold beta / N for the
+                // predecessors' gathers; beta itself is the state's visit
+                // probability (the marginal, for M).
+                const size_t qD = q + W + 1, qU = q + W, qL = q + 1;
+                if (hasD) {
+                    const float xs = score(qD) * c, fd = F0 - Fp2, amD = AM[qD], bMD = BM[qD];
+                    bm += bMD * ex2f(((am - amD) + fd) + xs);
+                    bi += bMD * ex2f(((ai - amD) + fd) + xs);
+                    bd += bMD * ex2f(((ad - amD) + fd) + xs);
+                }
+                if (hasU) {
+                    const float f1 = F0 - Fp1, aiU = AI[qU], bIU = BI[qU];
+                    bm += bIU * ex2f(((am - aiU) + f1) + go);
+                    bi += bIU * ex2f(((ai - aiU) + f1) + ge);
+                }
+                if (hasL) {
+                    const float f1 = F0 - Fp1, adL = AD[qL], bDL = BD[qL];
+                    bm += bDL * ex2f(((am - adL) + f1) + go);
+                    bd += bDL * ex2f(((ad - adL) + f1) + ge);
+                }
+                // own incoming weights (exponents e = v - a) and their sums
+                const float es = (x - am) - F0;
+                const float wsk = ex2f(es);
+                float NM = wsk, hm = -wsk * es;
+                if (dg) {
+                    const float f2 = Fm2 - F0;
+                    const float e0 = ((AM[q - W - 1] - am) + f2) + x;
+                    const float e1 = ((AI[q - W - 1] - am) + f2) + x;
+                    const float e2 = ((AD[q - W - 1] - am) + f2) + x;
+                    const float w0 = ex2f(e0), w1 = ex2f(e1), w2 = ex2f(e2);
+                    NM += (w0 + w1) + w2;
+                    hm -= w0 * e0;
+                    if (AI[q - W - 1] > kNegThresh) hm -= w1 * e1;
+                    if (AD[q - W - 1] > kNegThresh) hm -= w2 * e2;
+                }
+                float NI = 0.f, hi = 0.f, woi = 0.f, wei = 0.f;
+                if (up) {  // I(ij): opened from M above, extended from I above
+                    const float f1 = Fm1 - F0;
+                    const float e0 = ((AM[q - W] - ai) + f1) + go, e1 = ((AI[q - W] - ai) + f1) + ge;
+                    woi = ex2f(e0);
+                    wei = ex2f(e1);
+                    NI = woi + wei;
+                    hi = -woi * e0;
+                    if (AI[q - W] > kNegThresh) hi -= wei * e1;
+                }
+                float ND = 0.f, hd = 0.f, wod = 0.f, wed = 0.f;
+                if (lf) {  // D(ij): opened from M on the left, extended from D on the left
+                    const float f1 = Fm1 - F0;
+                    const float e0 = ((AM[q - 1] - ad) + f1) + go, e1 = ((AD[q - 1] - ad) + f1) + ge;
+                    wod = ex2f(e0);
+                    wed = ex2f(e1);
+                    ND = wod + wed;
+                    hd = -wod * e0;
+                    if (AD[q - 1] > kNegThresh) hd -= wed * e1;
+                }
+                const float bmn = bm / NM;                      // NM >= 1/4
+                const float bin = NI > 0.f ? bi / NI : 0.f;     // NI, ND >= 1/2 when reachable
+                const float bdn = ND > 0.f ? bd / ND : 0.f;
+                BM[q] = bmn;
+                BI[q] = bin;
+                BD[q] = bdn;
+                if (out) out[q] = bm;
+                so += (double)(bin * woi) + (double)(bdn * wod);
+                se += (double)(bin * wei) + (double)(bdn * wed);
+                // dS/dT: end-state terms + visit probability x local choice
+                // entropy of the normalised weights (h / N + lg2 N)
+                double hs = -(double)bim * (double)lpm;
+                if (ai > kNegThresh) hs -= (double)bii * (double)lpi;
+                if (ad > kNegThresh) hs -= (double)bid * (double)lpd;
+                hs += (double)bmn * (double)hm + (double)bm * (double)lg2f(NM);
+                if (NI > 0.f) hs += (double)bin * (double)hi + (double)bi * (double)lg2f(NI);
+                if (ND > 0.f) hs += (double)bdn * (double)hd + (double)bd * (double)lg2f(ND);
+                hsum += hs;
+                continue;
+            }
             // successor transition weights (framed exponents)
             float xs = 0.f, wMM = 0.f, wIM = 0.f, wDM = 0.f, wMI = 0.f, wII = 0.f, wMD = 0.f, wDD = 0.f;
             const size_t qD = q + W + 1, qU = q + W, qL = q + 1;
@@ -686,45 +770,7 @@ __global__ void __launch_bounds__(kPlaneThreads) aff_plane_kernel(SwArgs p) {
             BM[q] = bm;
             BI[q] = bi;
             BD[q] = bd;
-            if (MODE == MODE_MARG) {
-                if (out) out[q] = bm;
-                // path entropy (dS/dT): end-state terms ...
-                double hs = -(double)bim * (double)lpm;
-                if (ai > kNegThresh) hs -= (double)bii * (double)lpi;
-                if (ad > kNegThresh) hs -= (double)bid * (double)lpd;
-                // ... plus visit probability x local choice entropy
-                {
-                    const float es = x - F0 - am;
-                    float hm = -ex2f(es) * es;
-                    if (dg) {
-                        const float base = x + (Fm2 - F0) - am;
-                        const float q0 = AM[q - W - 1] + base, q1 = AI[q - W - 1] + base, q2 = AD[q - W - 1] + base;
-                        hm -= ex2f(q0) * q0;
-                        if (AI[q - W - 1] > kNegThresh) hm -= ex2f(q1) * q1;
-                        if (AD[q - W - 1] > kNegThresh) hm -= ex2f(q2) * q2;
-                    }
-                    hs += (double)bm * (double)hm;
-                }
-                if (up) {  // incoming gap transitions of I(ij)
-                    const float q0 = AM[q - W] + go + (Fm1 - F0) - ai, q1 = AI[q - W] + ge + (Fm1 - F0) - ai;
-                    const float w0 = ex2f(q0), w1 = ex2f(q1);
-                    so += (double)(bi * w0);
-                    se += (double)(bi * w1);
-                    float hi = -w0 * q0;
-                    if (AI[q - W] > kNegThresh) hi -= w1 * q1;
-                    hs += (double)bi * (double)hi;
-                }
-                if (lf) {  // incoming gap transitions of D(ij)
-                    const float q0 = AM[q - 1] + go + (Fm1 - F0) - ad, q1 = AD[q - 1] + ge + (Fm1 - F0) - ad;
-                    const float w0 = ex2f(q0), w1 = ex2f(q1);
-                    so += (double)(bd * w0);
-                    se += (double)(bd * w1);
-                    float hd = -w0 * q0;
-                    if (AD[q - 1] > kNegThresh) hd -= w1 * q1;
-                    hs += (double)bd * (double)hd;
-                }
-                hsum += hs;
-            } else if (MODE == MODE_HVP) {
+            if (MODE == MODE_HVP) {
                 const float dm = TM[q], di = TI[q], dd = TD[q];
                 float dbm = bim * (dm - dS) * iT;
                 float dbi = bii * (di - dS) * iT;

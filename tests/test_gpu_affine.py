@@ -299,3 +299,23 @@ def test_fast_param_grads(d2p, cuda_device, B, L1, L2, T, go, ge, ragged):
         for bb, (l1, l2) in enumerate(ln.tolist()):
             assert torch.count_nonzero(mc[bb, l1:, :]) == 0
             assert torch.count_nonzero(mc[bb, :, l2:]) == 0
+
+
+def test_low_temperature_fix_up_precision(d2p, cuda_device):
+    """T = 0.1 on N(0,1) scores: the linear-domain kernels flag these problems
+    and the plane engine recomputes them, its reverse normalising each state's
+    incoming weights; value, marginals and the three gradients must stay at
+    the reference's own fp32 level."""
+    B, L, T, go, ge = 3, 96, 0.1, -2.0, -0.5
+    s = scores(B, L, L, seed=L + B)
+    r64 = oracle.sw_affine(s.numpy(), None, go, ge, T, "f64")
+    r32 = oracle.sw_affine(s.numpy(), None, go, ge, T, "f32")
+    v, m = torch.ops.d2p.soft_sw_affine_float(s.to(cuda_device), go, ge, T, None)
+    check("value", v, r64["value"], r32["value"])
+    check("marginals", m, r64["marginals"], r32["marginals"])
+    v2, m2, a, b, c = torch.ops.d2p.soft_sw_affine_with_grads(s.to(cuda_device), go, ge, T, None)
+    check("value (with grads)", v2, r64["value"], r32["value"])
+    check("marginals (with grads)", m2, r64["marginals"], r32["marginals"])
+    check("grad_open", a, r64["grad_open"], r32["grad_open"], rtol=1e-4, atol=1e-5)
+    check("grad_ext", b, r64["grad_ext"], r32["grad_ext"], rtol=1e-4, atol=1e-5)
+    check("grad_T", c, r64["grad_T"], r32["grad_T"], rtol=1e-4, atol=1e-5)
