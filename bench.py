@@ -392,10 +392,12 @@ def run_ours(args, cfg):
                        "parallelism": f"batch x{world} (one process per GPU), NCCL all_gather of values"},
             "e2e": {"value": round(e2e_gcups, 3), "unit": "GCUPS", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": cfg["B"] * 4, "ms_per_step": round(e2e_ms, 4)},
-            # per step: the value+marginals kernel, its two (empty) fix-up
-            # launches, the backward's elementwise kernel; ragged batches of more
-            # than two problems per SM add the CTA-order kernel
-            "gpu_launches": args.steps * (5 if (lengths is not None and cfg["B"] > 2 * sm_count) else 4),
+            # per step: the value+marginals kernel, its (empty) plane-engine
+            # fix-up launch and the backward's elementwise kernel; bf16 scores
+            # add the widening kernel, ragged batches of more than two problems
+            # per SM the CTA-order kernel
+            "gpu_launches": args.steps * (3 + (1 if cfg["dtype"] == "bf16" else 0) +
+                                          (1 if (lengths is not None and cfg["B"] > 2 * sm_count) else 0)),
             "roofline": roofline,
             "clocks": clk,
         }
