@@ -51,7 +51,8 @@ CONFIGS = {
                dtype="f32", desc="soft_sw [32,4096,4096] fp32 0.5*N(0,1), gap -1, T 1"),
 }
 
-# Algorithmic cost per valid cell (fixed convention):
+# Algorithmic cost per valid cell (a fixed convention from the log-domain algorithm,
+# independent of how this implementation does the work):
 #   fused DP kernel (value + marginals): read scores 4 B (bf16: 2 B) + write marginals 4 B;
 #     MUFU 10 (forward LSE 4 ex2 + 1 lg2, reverse 1 ex2 beta_init + 4 ex2 weights);
 #     affine: 22 MUFU.
