@@ -319,3 +319,44 @@ def test_low_temperature_fix_up_precision(d2p, cuda_device):
     check("grad_open", a, r64["grad_open"], r32["grad_open"], rtol=1e-4, atol=1e-5)
     check("grad_ext", b, r64["grad_ext"], r32["grad_ext"], rtol=1e-4, atol=1e-5)
     check("grad_T", c, r64["grad_T"], r32["grad_T"], rtol=1e-4, atol=1e-5)
+
+
+def test_empty_problems_every_path(d2p, cuda_device):
+    """Problems with a zero length (S = 0: only the empty alignment) beside
+    full ones, on every value path of both families: value + marginals, with
+    parameter gradients in one wave, and (linear) over more than one wave.
+    Values, marginals and gradients against the oracle; the empty problems'
+    outputs are exactly zero."""
+    L1, L2 = 40, 48
+    s = scores(4, L1, L2, seed=44)
+    ln = torch.tensor([[0, L2], [L1, 0], [0, 0], [L1, L2]], dtype=torch.int32)
+    sd, lnd = s.to(cuda_device), ln.to(cuda_device)
+    a64 = oracle.sw_affine(s.numpy(), ln.numpy(), -2.0, -0.5, 1.0, "f64")
+    a32 = oracle.sw_affine(s.numpy(), ln.numpy(), -2.0, -0.5, 1.0, "f32")
+    v, m = torch.ops.d2p.soft_sw_affine_float(sd, -2.0, -0.5, 1.0, lnd)
+    check("affine value", v, a64["value"], a32["value"])
+    check("affine marginals", m, a64["marginals"], a32["marginals"])
+    v, m, go, ge, gT = torch.ops.d2p.soft_sw_affine_with_grads(sd, -2.0, -0.5, 1.0, lnd)
+    check("affine value (with grads)", v, a64["value"], a32["value"])
+    check("affine marginals (with grads)", m, a64["marginals"], a32["marginals"])
+    for name, g, key in (("grad_open", go, "grad_open"), ("grad_ext", ge, "grad_ext"), ("grad_T", gT, "grad_T")):
+        check(f"affine {name}", g, a64[key], a32[key], rtol=1e-4, atol=1e-5)
+        assert torch.all(g[:3] == 0)
+    assert torch.all(v[:3] == 0) and torch.count_nonzero(m[:3]) == 0
+    r64 = oracle.sw_linear(s.numpy(), ln.numpy(), -1.0, 1.0, "f64")
+    r32 = oracle.sw_linear(s.numpy(), ln.numpy(), -1.0, 1.0, "f32")
+    sms = torch.cuda.get_device_properties(cuda_device).multi_processor_count
+    big_s = torch.cat([sd, sd[3:].expand(sms, -1, -1)]).contiguous()
+    big_l = torch.cat([lnd, lnd[3:].expand(sms, -1)]).contiguous()
+    v1, m1 = torch.ops.d2p.soft_sw_float(sd, -1.0, 1.0, lnd)
+    runs = [("one wave", torch.ops.d2p.soft_sw_with_grads(sd, -1.0, 1.0, lnd)),
+            ("log-domain kernel", [t[:4] for t in torch.ops.d2p.soft_sw_with_grads(big_s, -1.0, 1.0, big_l)])]
+    check("linear value", v1, r64["value"], r32["value"])
+    check("linear marginals", m1, r64["marginals"], r32["marginals"])
+    for name, (v, m, gg, gt) in runs:
+        check(f"linear value ({name})", v, r64["value"], r32["value"])
+        check(f"linear marginals ({name})", m, r64["marginals"], r32["marginals"])
+        check(f"linear grad_gap ({name})", gg, r64["grad_gap"], r32["grad_gap"], rtol=1e-4, atol=1e-5)
+        check(f"linear grad_T ({name})", gt, r64["grad_T"], r32["grad_T"], rtol=1e-4, atol=1e-5)
+        assert torch.all(v[:3] == 0) and torch.all(gg[:3] == 0) and torch.all(gt[:3] == 0)
+        assert torch.count_nonzero(m[:3]) == 0
