@@ -931,6 +931,13 @@ __global__ void bf16_to_f32_kernel(const __nv_bfloat16* __restrict__ in, float* 
 }  // namespace aff
 
 // ------------------------------------------------------------------ host side
+int launch_bf16_widen(const __nv_bfloat16* in, float* out, size_t n, cudaStream_t st) {
+    if (n == 0) return 0;
+    if ((((uintptr_t)in) & 15) != 0 || (((uintptr_t)out) & 15) != 0) return -1;
+    aff::bf16_to_f32_kernel<<<1184, 256, 0, st>>>(in, out, n);
+    return (int)cudaGetLastError();
+}
+
 size_t aff_fast_workspace_bytes(int B, int L1, int L2, bool bf16) {
     if (L1 > 32 * aff::kMaxRB || L2 % 4 != 0) return 0;
     size_t b = aff::per_problem_bytes(L1, L2) * (size_t)B;

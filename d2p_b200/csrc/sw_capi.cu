@@ -73,6 +73,12 @@ static size_t op_bytes(int family, int op, int B, int L1, int L2) {
             pe = pe > wf ? pe : wf;
             pe = pe > lf ? pe : lf;
             pe = pe > tf ? pe : tf;
+            if (family == D2P_FAMILY_AFFINE && tf > 0) {
+                // bf16 scores with parameter gradients: the tangent kernel's
+                // area, then the widened scores
+                const size_t tw = align256(tf) + align256((size_t)B * L1 * L2 * sizeof(float));
+                pe = pe > tw ? pe : tw;
+            }
             // flags, the CTA order of ragged batches, the cross-CTA words of
             // problems spread over several CTAs
             return align256(pe) + 2 * align256((size_t)(B > 0 ? B : 1) * sizeof(int)) +
@@ -405,6 +411,10 @@ int d2p_sw_affine_forward_backward(const void* scores, int scores_dtype, const i
         const size_t tf = aff_tan_workspace_bytes(B, L1, L2);
         pe = pe > af ? pe : af;
         pe = pe > tf ? pe : tf;
+        if (tf > 0) {
+            const size_t tw = align256(tf) + align256((size_t)B * L1 * L2 * sizeof(float));
+            pe = pe > tw ? pe : tw;
+        }
         int* flags = (int*)((char*)workspace + align256(pe));
         int* order = (int*)((char*)flags + align256((size_t)B * sizeof(int)));
         a.redo = flags;
@@ -415,7 +425,18 @@ int d2p_sw_affine_forward_backward(const void* scores, int scores_dtype, const i
             // the order slot holds dS/dgap_ext between the two sweeps
             a.pg_ext = (float*)order;
             a.sync = (int*)((char*)order + align256((size_t)B * sizeof(int)));
-            rc = launch_aff_tan(a, workspace_bytes, st);
+            rc = kNotHandled;
+            SwArgs t = a;
+            if (a.scores_bf16 && tf > 0) {
+                // the tangent kernel reads fp32: widen bf16 scores (exactly) into
+                // the workspace after its area; a flagged problem's plane-engine
+                // fix-up reads the bf16 input itself (scores_bf16 stays set)
+                float* wide = (float*)((char*)workspace + align256(tf));
+                const int wr = launch_bf16_widen(a.scores_bf16, wide, (size_t)B * L1 * L2, st);
+                if (wr == D2P_OK) t.scores = wide;
+                else if (wr != kNotHandled) return wr;
+            }
+            if (t.scores) rc = launch_aff_tan(t, align256(tf), st);
             a.pg_ext = nullptr;
             a.sync = nullptr;
         } else {

@@ -89,6 +89,8 @@ int launch_lin_fast(const SwArgs& a, size_t ws_bytes, cudaStream_t st);
 // workspace first); returns -1 when the shape or arguments are not covered
 size_t aff_fast_workspace_bytes(int B, int L1, int L2, bool bf16);
 int launch_aff_fast(const SwArgs& a, size_t ws_bytes, cudaStream_t st);
+// bf16 -> fp32 copy of n scores (both pointers 16-byte aligned; exact)
+int launch_bf16_widen(const __nv_bfloat16* in, float* out, size_t n, cudaStream_t st);
 // order[B]: problems by decreasing estimated cost, for batches of uneven
 // lengths that take more than one wave; returns -1 when ordering cannot help
 int launch_lin_order(const int* lengths, int B, int L1, int L2, int* order, cudaStream_t st);

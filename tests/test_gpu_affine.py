@@ -360,3 +360,28 @@ def test_empty_problems_every_path(d2p, cuda_device):
         check(f"linear grad_T ({name})", gt, r64["grad_T"], r32["grad_T"], rtol=1e-4, atol=1e-5)
         assert torch.all(v[:3] == 0) and torch.all(gg[:3] == 0) and torch.all(gt[:3] == 0)
         assert torch.count_nonzero(m[:3]) == 0
+
+
+def test_bf16_param_grads_on_the_tangent_kernel(d2p, cuda_device):
+    """bf16 scores with parameter gradients: the scores are widened (exactly)
+    for the tangent kernel's two gap sweeps, so every output equals the fp32
+    result of the widened scores bitwise, and no problem falls back to the
+    plane engine."""
+    B, L1, L2 = 4, 96, 128
+    s = scores(B, L1, L2, seed=88).to(torch.bfloat16)
+    w = s.float()
+    out_b = torch.ops.d2p.soft_sw_affine_with_grads(s.to(cuda_device), -2.0, -0.5, 1.0, None)
+    out_f = torch.ops.d2p.soft_sw_affine_with_grads(w.to(cuda_device), -2.0, -0.5, 1.0, None)
+    for x, y in zip(out_b, out_f):
+        assert torch.equal(x, y)
+    wp = torch.nn.functional.pad(w, (0, 1)).contiguous().to(cuda_device)  # row length 129: the plane engine
+    lp = torch.tensor([[L1, L2]] * B, dtype=torch.int32, device=cuda_device)
+    mp = torch.ops.d2p.soft_sw_affine_with_grads(wp, -2.0, -0.5, 1.0, lp)[1][..., :L2]
+    for b in range(B):
+        assert not torch.equal(out_b[1][b], mp[b]), f"problem {b} was recomputed by the plane engine"
+    r64 = oracle.sw_affine(w.numpy(), None, -2.0, -0.5, 1.0, "f64")
+    r32 = oracle.sw_affine(w.numpy(), None, -2.0, -0.5, 1.0, "f32")
+    check("marginals", out_b[1], r64["marginals"], r32["marginals"])
+    check("grad_open", out_b[2], r64["grad_open"], r32["grad_open"], rtol=1e-4, atol=1e-5)
+    check("grad_ext", out_b[3], r64["grad_ext"], r32["grad_ext"], rtol=1e-4, atol=1e-5)
+    check("grad_T", out_b[4], r64["grad_T"], r32["grad_T"], rtol=1e-4, atol=1e-5)
