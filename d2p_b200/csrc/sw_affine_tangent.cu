@@ -28,11 +28,14 @@
 // sw_tangent.cu.
 //
 // PG (value + marginals + dS/dgap_open, dS/dgap_ext, dS/dT, for gap parameters
-// that need gradients): a forward-only sweep carries the tangent along gap_ext
-// (dS/dgap_ext = T dZ/Z), then a full sweep carries the one along gap_open,
-// writes the marginals and sums score x marginal; dS/dT follows from Euler's
-// identity for the degree-1 homogeneous S(s, go, ge, T):
-// S = sum s mu + go dS/dgo + ge dS/dge + T dS/dT.
+// that need gradients), one sweep pair: the forward carries the tangent along
+// gap_open, so dS/dgo = T dZ/Z, the expected number of gap openings.  Every
+// visit of an I or D state is entered by exactly one opening or one extension,
+// so the expected number of extensions, dS/dge, is the sum of the I and D
+// visit probabilities (BI I + BD D) / Z_total minus dS/dgo; the forward keeps
+// I and D per cell for it.  The reverse also writes the marginals and sums
+// score x marginal, and dS/dT follows from Euler's identity for the degree-1
+// homogeneous S(s, go, ge, T): S = sum s mu + go dS/dgo + ge dS/dge + T dS/dT.
 #include <stddef.h>
 #include <stdint.h>
 
@@ -53,7 +56,8 @@ struct WarpSmem {
     float ringS[32 * kRW];    // scores; reverse: dmu written in place
     float ringV[32 * kRW];    // the direction (HVP) or the dot-mode weights
     float zr[2][16 * 32];     // reverse: the forward's M of 16 anti-diagonals, two slots
-    float dzr[2][16 * 32];    //          and its dM
+    float dzr[2][16 * 32];    //          and its dM (PG: the forward's I)
+    float xr[2][16 * 32];     //          PG: the forward's D
     float er[16 * 32];        // reverse: forward frames
     // staging of the neighbouring row-block's boundary values by its step
     // (forward: u, T, du, dT; reverse: BI, X, dBI, dX) and frames by group
@@ -77,15 +81,16 @@ struct Layout {
     float* efr;   // [nRB][GT][32] frames
     float* h[4];  // [nRB][HZ]     boundary rows (the four values above)
     float* hfr;   // [nRB][HF]     their frames
+    float* xpl;   // [nRB][ZT][32] PG: D of forward step t (dmpl then holds I)
 };
-__host__ __device__ inline size_t per_problem_bytes(int L1m, int L2m) {
+__host__ __device__ inline size_t per_problem_bytes(int L1m, int L2m, bool pg = false) {
     const size_t nrb = (size_t)(L1m + 31) / 32;
-    return 2 * align_up(nrb * zt_rows(L2m) * 32 * 4, 256) + align_up(nrb * gt_rows(L2m) * 32 * 4, 256) +
+    return (pg ? 3 : 2) * align_up(nrb * zt_rows(L2m) * 32 * 4, 256) + align_up(nrb * gt_rows(L2m) * 32 * 4, 256) +
            4 * align_up(nrb * hz_stride(L2m) * 4, 256) + align_up(nrb * hf_stride(L2m) * 4, 256);
 }
-__device__ inline Layout carve(float* ws, int b, int L1m, int L2m) {
+__device__ inline Layout carve(float* ws, int b, int L1m, int L2m, bool pg) {
     const size_t nrb = (size_t)(L1m + 31) / 32;
-    char* base = (char*)ws + (size_t)b * per_problem_bytes(L1m, L2m);
+    char* base = (char*)ws + (size_t)b * per_problem_bytes(L1m, L2m, pg);
     Layout L;
     L.mpl = (float*)base;
     base += align_up(nrb * zt_rows(L2m) * 32 * 4, 256);
@@ -98,6 +103,8 @@ __device__ inline Layout carve(float* ws, int b, int L1m, int L2m) {
         base += align_up(nrb * hz_stride(L2m) * 4, 256);
     }
     L.hfr = (float*)base;
+    base += align_up(nrb * hf_stride(L2m) * 4, 256);
+    L.xpl = pg ? (float*)base : nullptr;
     return L;
 }
 
@@ -158,6 +165,7 @@ struct FwdCtx {
     unsigned pv;
     float* mrow;
     float* dmrow;
+    float* xrow;         // PG: xpl row 0 of this row-block, this lane
     float* erow;
     float c, Go, Ge;
     Dir dir;
@@ -233,7 +241,7 @@ __device__ __forceinline__ void acc_rebase2(FwdVars& V) {
 }
 
 struct FwdOut {
-    float M, D, T, u, Tdn;
+    float M, D, T, u, Tdn, I;
     float dM, dD, dT, du, dTdn;
 };
 __device__ __forceinline__ FwdOut fwd_cell(const FwdCtx& C, const FwdVars& V, int i, float sc, float vv) {
@@ -243,6 +251,7 @@ __device__ __forceinline__ FwdOut fwd_cell(const FwdCtx& C, const FwdVars& V, in
     const float d = i == 0 ? V.f.d0 : V.f.d1;
     o.M = P * (V.Td + V.f.fs);
     const float I = fmaf(V.ur, d, V.f.ua[i]);
+    o.I = I;
     o.D = fmaf(C.Ge, V.Dp, C.Go * V.Mp);
     o.T = o.M + I + o.D;
     o.u = fmaf(i == 0 ? V.f.Ged0 : V.f.Ged1, V.ur, fmaf(C.Go, o.M, C.Ge * V.f.ua[i]));
@@ -282,6 +291,7 @@ __device__ __forceinline__ void fwd_stage_full(const FwdCtx& C, FwdVars& V, int 
     }
     float* const pm = C.mrow + (size_t)(kCW * k) * 32;
     float* const pdm = C.dmrow + (size_t)(kCW * k) * 32;
+    float* const px = PG ? C.xrow + (size_t)(kCW * k) * 32 : nullptr;
     float* const pe = C.erow + (size_t)(kCW * k / 4) * 32;
     float uq[4], tq[4], duq[4], dtq[4];
 #pragma unroll
@@ -303,7 +313,12 @@ __device__ __forceinline__ void fwd_stage_full(const FwdCtx& C, FwdVars& V, int 
         V.gsum += o.T;
         V.dgsum += o.dT;
         pm[(size_t)u * 32] = o.M;
-        if (!PG) pdm[(size_t)u * 32] = o.dM;  // PG: the reverse needs no dM
+        if (PG) {  // the reverse needs no dM: the I and D visit sums take I and D
+            pdm[(size_t)u * 32] = o.I;
+            px[(size_t)u * 32] = o.D;
+        } else {
+            pdm[(size_t)u * 32] = o.dM;
+        }
         uq[i] = o.u;
         tq[i] = o.T;
         duq[i] = o.du;
@@ -352,7 +367,12 @@ __device__ __forceinline__ void fwd_stage_start(const FwdCtx& C, FwdVars& V, int
             V.gsum += o.T;
             V.dgsum += o.dT;
             C.mrow[(size_t)t * 32] = o.M;
-            if (!PG) C.dmrow[(size_t)t * 32] = o.dM;
+            if (PG) {
+                C.dmrow[(size_t)t * 32] = act ? o.I : 0.f;
+                C.xrow[(size_t)t * 32] = o.D;
+            } else {
+                C.dmrow[(size_t)t * 32] = o.dM;
+            }
             uq[i] = o.u;
             tq[i] = o.T;
             duq[i] = o.du;
@@ -398,6 +418,8 @@ struct RevVars {
     float chk;
     float sdot;
     double dot;
+    float sgap;             // PG: this stage's sum of the I and D visit probabilities
+    double dot2;
 };
 
 struct RevCtx {
@@ -405,6 +427,7 @@ struct RevCtx {
     const float* vring;
     const float* zr;
     const float* dzr;
+    const float* xr;       // PG: WarpSmem::xr
     const float* er;
     const float* bs;     // bottom lane: staging rows BI, X, dBI, dX (bs + i kHR) of the row-block below
     const float* bf;
@@ -481,13 +504,14 @@ __device__ __forceinline__ void rev_apply(RevVars& V) {
 }
 
 struct RevOut {
-    float BM, BI, BD, PB, dBI, dBD, dPB, dmu;
+    float BM, BI, BD, PB, dBI, dBD, dPB, dmu, gv;
 };
 // m / dm: the forward's M and dM of this cell.  PG: the marginal itself (in
-// dmu), no tangent of the reverse.
+// dmu) and the cell's I and D visit probabilities (in gv; dm is then the
+// forward's I, x its D), no tangent of the reverse.
 template <bool PG>
 __device__ __forceinline__ RevOut rev_cell(const RevCtx& C, const RevVars& V, int i, float sc, float vv, float m,
-                                           float dm) {
+                                           float dm, float x) {
     RevOut o;
     const float P = ex2f(sc * C.c);
     const float vp = fmaf(C.dir.vs, vv, C.dir.ss * sc);
@@ -500,8 +524,10 @@ __device__ __forceinline__ RevOut rev_cell(const RevCtx& C, const RevVars& V, in
     if (PG) {
         o.dBI = o.dBD = o.dPB = 0.f;
         o.dmu = o.BM * (m * V.f.kE);
+        o.gv = fmaf(o.BI, dm, o.BD * x) * V.f.kE;
         return o;
     }
+    o.gv = 0.f;
     const float BIdn = fmaf(V.Yr, d, V.f.ya[i]);
     const float dBIdn = fmaf(V.dYr, d, V.f.dya[i]);
     const float dc1 = fmaf(V.dXr, d, V.f.dxa[i]);
@@ -517,10 +543,16 @@ __device__ __forceinline__ RevOut rev_cell(const RevCtx& C, const RevVars& V, in
 // DOT: sum gm * dmu; PG: write the marginal and sum score * marginal (gm is
 // the score); otherwise write dmu
 template <bool DOT, bool PG>
-__device__ __forceinline__ void rev_emit(RevVars& V, float* slot, float gm, float dmu, bool act) {
+__device__ __forceinline__ void rev_emit(RevVars& V, float* slot, float gm, float dmu, bool act, float gv) {
     if (act) V.chk = fmaf(dmu, 0.f, V.chk);
     if (DOT || PG) {
         if (act) V.sdot = fmaf(gm, dmu, V.sdot);
+    }
+    if (PG) {
+        if (act) {
+            V.chk = fmaf(gv, 0.f, V.chk);
+            V.sgap += gv;
+        }
     }
     if (!DOT) {
         if (act) *slot = dmu;
@@ -554,6 +586,7 @@ __device__ __forceinline__ void rev_stage_full(const RevCtx& C, RevVars& V, int 
     const int slot = ((m16 >> 4) & 1) * (16 * 32) + C.lane;
     const float* const zb = C.zr + slot;
     const float* const dzb = C.dzr + slot;
+    const float* const xb = C.xr + slot;
     const int cb = (C.P + 31 - kCW * k - C.lane) & (kRW - 1);
     float scv[kCW], vvv[kCW];
 #pragma unroll
@@ -571,11 +604,11 @@ __device__ __forceinline__ void rev_stage_full(const RevCtx& C, RevVars& V, int 
             if (u == kCW - 1) cp_async_wait1();
             rev_lookahead(C, V, 4 * k + (u >> 2) + 1);
         }
-        const RevOut o =
-            rev_cell<PG>(C, V, i, scv[u], DOT ? 0.f : vvv[u], zb[(15 - u) * 32], PG ? 0.f : dzb[(15 - u) * 32]);
+        const RevOut o = rev_cell<PG>(C, V, i, scv[u], DOT ? 0.f : vvv[u], zb[(15 - u) * 32], dzb[(15 - u) * 32],
+                                      PG ? xb[(15 - u) * 32] : 0.f);
         const bool act = !MASK || u < thr;
         const int col = (u <= cb) ? cb - u : cb - u + kRW;
-        rev_emit<DOT, PG>(V, C.ring + col, PG ? scv[u] : vvv[u], o.dmu, act);
+        rev_emit<DOT, PG>(V, C.ring + col, PG ? scv[u] : vvv[u], o.dmu, act, o.gv);
         rev_commit(V, o, act, yq[i], xq[i], dyq[i], dxq[i]);
         if (i == 3)
             handoff4(C, 4 * k + (u >> 2), make_float4(yq[0], yq[1], yq[2], yq[3]),
@@ -590,6 +623,7 @@ __device__ __forceinline__ void rev_stage_part(const RevCtx& C, RevVars& V, int 
     const int slot = ((m16 >> 4) & 1) * (16 * 32) + C.lane;
     const float* const zb = C.zr + slot;
     const float* const dzb = C.dzr + slot;
+    const float* const xb = C.xr + slot;
     const bool live = C.lane < C.nv;
     float yq[4], xq[4], dyq[4], dxq[4];
 #pragma unroll 1
@@ -613,8 +647,9 @@ __device__ __forceinline__ void rev_stage_part(const RevCtx& C, RevVars& V, int 
             const int ci = j0 & (kRW - 1);
             const float vv = HV ? C.vring[ci] : 0.f;
             const float sc = C.ring[ci];
-            const RevOut o = rev_cell<PG>(C, V, i, sc, DOT ? 0.f : vv, zb[(15 - u) * 32], PG ? 0.f : dzb[(15 - u) * 32]);
-            rev_emit<DOT, PG>(V, C.ring + ci, PG ? sc : vv, o.dmu, act);
+            const RevOut o = rev_cell<PG>(C, V, i, sc, DOT ? 0.f : vv, zb[(15 - u) * 32], dzb[(15 - u) * 32],
+                                          PG ? xb[(15 - u) * 32] : 0.f);
+            rev_emit<DOT, PG>(V, C.ring + ci, PG ? sc : vv, o.dmu, act, o.gv);
             rev_commit(V, o, act, yq[i], xq[i], dyq[i], dxq[i]);
             if (i == 3)
                 handoff4(C, 4 * k + q, make_float4(yq[0], yq[1], yq[2], yq[3]),
@@ -662,14 +697,13 @@ __global__ void __launch_bounds__(kNW * 32, 1) aff_tan_kernel(SwArgs p) {
     const float iT = 1.f / T, iT2 = 1.f / (T * T);
     dir.vs = p.mode == MODE_HVP ? iT : 0.f;
     dir.ss = p.mode == MODE_PT ? -iT2 : 0.f;
-    const bool fwd_only = PG && p.pg_fwd_only;  // PG: the sweep along gap_ext
-    dir.go = PG ? (fwd_only ? 0.f : iT) : (p.mode == MODE_PGAP ? iT : (p.mode == MODE_PT ? -go * iT2 : 0.f));
-    dir.ge = PG ? (fwd_only ? iT : 0.f) : (p.mode == MODE_PGE ? iT : (p.mode == MODE_PT ? -ge * iT2 : 0.f));
+    dir.go = PG ? iT : (p.mode == MODE_PGAP ? iT : (p.mode == MODE_PT ? -go * iT2 : 0.f));
+    dir.ge = PG ? 0.f : (p.mode == MODE_PGE ? iT : (p.mode == MODE_PT ? -ge * iT2 : 0.f));
     const size_t plane = (size_t)L1m * L2m;
     const float* __restrict__ S = p.scores + (size_t)b * plane;
     const float* __restrict__ Vp = HV ? (DOT ? p.dot_with : p.tangent) + (size_t)b * plane : nullptr;
-    float* __restrict__ out = (!DOT && !fwd_only && p.out) ? p.out + (size_t)b * plane : nullptr;
-    const Layout LY = carve(p.ws, b, L1m, L2m);
+    float* __restrict__ out = (!DOT && p.out) ? p.out + (size_t)b * plane : nullptr;
+    const Layout LY = carve(p.ws, b, L1m, L2m, PG);
     const int nRB = (L1 + 31) / 32;
     const int nch = (L2 + kCW - 1) / kCW;
     const size_t zst = (size_t)zt_rows(L2m) * 32;
@@ -684,9 +718,7 @@ __global__ void __launch_bounds__(kNW * 32, 1) aff_tan_kernel(SwArgs p) {
     if (L1 == 0 || L2 == 0) {
         if (threadIdx.x == 0 && part == 0) {
             if (DOT && p.dot_out) p.dot_out[b] = 0.f;
-            if (PG && fwd_only) {
-                if (p.pg_ext) p.pg_ext[b] = 0.f;
-            } else if (PG) {  // S = log(1) = 0, and so its derivatives
+            if (PG) {  // S = log(1) = 0, and so its derivatives
                 if (p.value) p.value[b] = 0.f;
                 if (p.grad_gap) p.grad_gap[b] = 0.f;
                 if (p.grad_gap2) p.grad_gap2[b] = 0.f;
@@ -777,6 +809,7 @@ __global__ void __launch_bounds__(kNW * 32, 1) aff_tan_kernel(SwArgs p) {
         C.pv = (unsigned)__cvta_generic_to_shared(Wn.s0);
         C.mrow = LY.mpl + (size_t)r * zst + lane;
         C.dmrow = LY.dmpl + (size_t)r * zst + lane;
+        C.xrow = PG ? LY.xpl + (size_t)r * zst + lane : nullptr;
         C.erow = LY.efr + (size_t)r * est + lane;
         C.c = c;
         C.Go = Go;
@@ -899,22 +932,11 @@ __global__ void __launch_bounds__(kNW * 32, 1) aff_tan_kernel(SwArgs p) {
             sh_dSr = (float)q;
             if (!fin || !(fabs(q) < 1e30)) sh_bad = 1;
             if (PG && part == 0) {
-                if (fwd_only) {
-                    if (p.pg_ext) p.pg_ext[b] = (float)(q * (double)T);
-                } else {
-                    if (p.value) p.value[b] = ((float)sh_Sint + sh_Sfrac) / c;
-                    if (p.grad_gap) p.grad_gap[b] = (float)(q * (double)T);
-                }
+                if (p.value) p.value[b] = ((float)sh_Sint + sh_Sfrac) / c;
+                if (p.grad_gap) p.grad_gap[b] = (float)(q * (double)T);
             }
         }
         __syncthreads();
-    }
-    if (fwd_only) {  // PG along gap_ext: the forward is all this sweep needs
-        const int o_win = __syncthreads_or(fwd_out & 1);
-        const int o_acc = __syncthreads_or(fwd_out & 8);
-        if (threadIdx.x == 0 && p.redo)
-            atomicOr(p.redo + b, (o_win ? 1 : 0) | (sh_err ? 2 : 0) | (sh_bad ? 4 : 0) | (o_acc ? 8 : 0));
-        return;
     }
 
     // ============================== reverse ==============================
@@ -924,18 +946,21 @@ __global__ void __launch_bounds__(kNW * 32, 1) aff_tan_kernel(SwArgs p) {
     RV.ebmin = RV.ebmax = 0x3f800000;
     RV.chk = 0.f;
     RV.dot = 0.0;
+    RV.dot2 = 0.0;
     for (int q = gw; q < nRB; q += NWt) {
         const int r = nRB - 1 - q;
         const int nv = min(32, L1 - 32 * r);
         const bool hasBelow = r + 1 < nRB, hasAbove = r > 0;
         const float* const mblk = LY.mpl + (size_t)r * zst;
         const float* const dmblk = LY.dmpl + (size_t)r * zst;
+        const float* const xblk = PG ? LY.xpl + (size_t)r * zst : nullptr;
         const float* const eblk = LY.efr + (size_t)r * est;
         RevCtx C;
         C.ring = W.ringS + lane * kRW;
         C.vring = W.ringV + lane * kRW;
         C.zr = &W.zr[0][0];
         C.dzr = &W.dzr[0][0];
+        C.xr = &W.xr[0][0];
         C.er = W.er;
         C.bs = (hasBelow && lane == nv - 1) ? W.s0 : zv;
         C.bf = (hasBelow && lane == nv - 1) ? W.sf : zf;
@@ -969,7 +994,8 @@ __global__ void __launch_bounds__(kNW * 32, 1) aff_tan_kernel(SwArgs p) {
             for (int it = 0; it < 4; ++it) {
                 const int e = 4 * (lane + 32 * it);
                 cp_async16(&W.zr[M & 1][0] + e, mblk + o16 + e, 16);
-                if (!PG) cp_async16(&W.dzr[M & 1][0] + e, dmblk + o16 + e, 16);
+                cp_async16(&W.dzr[M & 1][0] + e, dmblk + o16 + e, 16);  // PG: I
+                if (PG) cp_async16(&W.xr[M & 1][0] + e, xblk + o16 + e, 16);
             }
             const int gl = 4 * M - 1;
 #pragma unroll
@@ -1018,6 +1044,7 @@ __global__ void __launch_bounds__(kNW * 32, 1) aff_tan_kernel(SwArgs p) {
             }
             if (k == 0) rev_lookahead(C, RV, 0);
             RV.sdot = 0.f;
+            RV.sgap = 0.f;
             if (kCW * k <= P + 32 - L2)
                 rev_stage_part<HV, DOT, PG>(C, RV, k);
             else if (nv == 32 && kCW * k + kCW - 1 <= P - 1)
@@ -1025,6 +1052,7 @@ __global__ void __launch_bounds__(kNW * 32, 1) aff_tan_kernel(SwArgs p) {
             else
                 rev_stage_full<true, HV, DOT, PG>(C, RV, k, lane < nv ? 16 * M + 16 - lane : -1);
             if (DOT || PG) RV.dot += (double)RV.sdot;
+            if (PG) RV.dot2 += (double)RV.sgap;
             if (RV.push) Wn.tag[k & (kHR / 16 - 1)] = (q << 16) | k;
             __syncwarp();
             if (lane == 0) {
@@ -1050,29 +1078,34 @@ __global__ void __launch_bounds__(kNW * 32, 1) aff_tan_kernel(SwArgs p) {
     const int redo = (o_win ? 1 : 0) | (sh_err ? 2 : 0) | (sh_bad ? 4 : 0) | (o_acc ? 8 : 0) | (o_tan ? 16 : 0);
     if (DOT || PG) {
         const double tot = block_sum_d(RV.dot, red);
+        const double tot2 = PG ? block_sum_d(RV.dot2, red) : 0.0;
         if (threadIdx.x == 0) {
-            // DOT: the weighted sum; PG: dS/dgap_ext from the forward-only sweep,
+            // DOT: the weighted sum.  PG: dS/dge = (I and D visits) - dS/dgo,
             // dS/dT = (S - sum s mu - go dS/dgo - ge dS/dge) / T
-            auto finish = [&](double all) {
+            auto finish = [&](double all, double visits) {
                 if (DOT && p.dot_out) p.dot_out[b] = (float)all;
                 if (PG) {
                     const double S = ((double)sh_Sint + (double)sh_Sfrac) / (double)c;
                     const double eo = (double)sh_dSr * (double)T;
-                    const double ee = p.pg_ext ? (double)p.pg_ext[b] : 0.0;
+                    const double ee = visits - eo;
                     if (p.grad_gap2) p.grad_gap2[b] = (float)ee;
                     if (p.grad_T) p.grad_T[b] = (float)((S - all - (double)go * eo - (double)ge * ee) / (double)T);
                 }
             };
             if (SPLIT && K > 1) {
                 gpart[kSyncPartDoubles * part + 3] = tot;
+                if (PG) gpart[kSyncPartDoubles * part + 4] = tot2;
                 if (atom_add_release_gpu(gsync + 2 * kMaxParts + 1, 1) == K - 1) {
                     (void)ld_acquire_gpu(gsync + 2 * kMaxParts + 1);
-                    double all = 0.0;
-                    for (int k = 0; k < K; ++k) all += gpart[kSyncPartDoubles * k + 3];
-                    finish(all);
+                    double all = 0.0, all2 = 0.0;
+                    for (int k = 0; k < K; ++k) {
+                        all += gpart[kSyncPartDoubles * k + 3];
+                        if (PG) all2 += gpart[kSyncPartDoubles * k + 4];
+                    }
+                    finish(all, all2);
                 }
             } else {
-                finish(tot);
+                finish(tot, tot2);
             }
         }
     }
@@ -1087,9 +1120,9 @@ __global__ void __launch_bounds__(kNW * 32, 1) aff_tan_kernel(SwArgs p) {
 }  // namespace atan_
 
 // ------------------------------------------------------------------ host side
-size_t aff_tan_workspace_bytes(int B, int L1, int L2) {
+size_t aff_tan_workspace_bytes(int B, int L1, int L2, bool pg) {
     if (L1 > 32 * atan_::kMaxRB || L2 % 4 != 0) return 0;
-    return atan_::per_problem_bytes(L1, L2) * (size_t)B;
+    return atan_::per_problem_bytes(L1, L2, pg) * (size_t)B;
 }
 
 int launch_aff_tan(const SwArgs& a, size_t ws_bytes, cudaStream_t st) {
@@ -1103,12 +1136,12 @@ int launch_aff_tan(const SwArgs& a, size_t ws_bytes, cudaStream_t st) {
     if (a.mode == MODE_HVP && (dot || !a.tangent)) return -1;
     if (dot && !a.dot_out) return -1;
     if (!dot && !a.out && !pg) return -1;
-    if (pg && (dot || a.tangent || !a.pg_ext)) return -1;
+    if (pg && (dot || a.tangent)) return -1;
     auto al16 = [](const void* q) { return (((uintptr_t)q) & 15) == 0; };
     if (!a.scores || !al16(a.scores) || (a.out && !al16(a.out)) || !a.ws) return -1;
     if ((a.tangent && !al16(a.tangent)) || (dot && !al16(a.dot_with))) return -1;
     if ((((uintptr_t)a.ws) & 255) != 0) return -1;
-    if (ws_bytes < atan_::per_problem_bytes(a.L1, a.L2) * (size_t)a.B) return -1;
+    if (ws_bytes < atan_::per_problem_bytes(a.L1, a.L2, pg) * (size_t)a.B) return -1;
     const size_t smem = sizeof(atan_::WarpSmem) * atan_::kNW;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -1136,8 +1169,8 @@ int launch_aff_tan(const SwArgs& a, size_t ws_bytes, cudaStream_t st) {
         attr_set[dev] = true;
     }
     const int K = (dev < 64 && a.sync) ? lin_parts_nw(a.B, a.L1, a.L2, sms[dev], atan_::kNW) : 1;
-    // one sweep; the flags are zeroed by the caller of a spread launch, once
-    // before the two PG sweeps (each ORs its bits in)
+    // one sweep pair; a spread launch zeroes the flags itself unless told not
+    // to (PG zeroes them before the launch: its kernels OR their bits in)
     auto sweep = [&](const SwArgs& x, bool zero_redo) -> cudaError_t {
         cudaError_t err;
         if (K > 1) {
@@ -1166,14 +1199,10 @@ int launch_aff_tan(const SwArgs& a, size_t ws_bytes, cudaStream_t st) {
         return cudaGetLastError();
     };
     if (!pg) return (int)sweep(a, true);
+    // PG: one sweep pair; its flags are ORed in (zeroed here)
     e = cudaMemsetAsync(a.redo, 0, sizeof(int) * (size_t)a.B, st);
     if (e != cudaSuccess) return (int)e;
-    SwArgs x = a;
-    x.pg_fwd_only = 1;  // along gap_ext: writes pg_ext
-    e = sweep(x, false);
-    if (e != cudaSuccess) return (int)e;
-    x.pg_fwd_only = 0;  // along gap_open: value, marginals, the three gradients
-    return (int)sweep(x, false);
+    return (int)sweep(a, false);
 }
 
 }  // namespace d2pb

@@ -69,7 +69,7 @@ static size_t op_bytes(int family, int op, int B, int L1, int L2) {
             if (wf == 0) return pe;
             const size_t lf = family == D2P_FAMILY_LINEAR ? lin_fast_workspace_bytes(B, L1, L2) : 0;
             const size_t tf = family == D2P_FAMILY_LINEAR ? lin_tan_workspace_bytes(B, L1, L2)
-                                                          : aff_tan_workspace_bytes(B, L1, L2);
+                                                          : aff_tan_workspace_bytes(B, L1, L2, true);
             pe = pe > wf ? pe : wf;
             pe = pe > lf ? pe : lf;
             pe = pe > tf ? pe : tf;
@@ -403,12 +403,12 @@ int d2p_sw_affine_forward_backward(const void* scores, int scores_dtype, const i
     const size_t af = aff_fast_workspace_bytes(B, L1, L2, true);
     if (af > 0) {
         // linear-domain kernels -- value + marginals: sw_affine_fast.cu; with
-        // parameter gradients: the tangent kernel's two gap sweeps,
+        // parameter gradients: the tangent kernel's gap sweep pair,
         // sw_affine_tangent.cu -- then the plane engine for the problems they
         // flagged
         const bool grads = grad_gap_open || grad_gap_ext || grad_temperature;
         size_t pe = plane_bytes(D2P_FAMILY_AFFINE, MODE_MARG, B, L1, L2);
-        const size_t tf = aff_tan_workspace_bytes(B, L1, L2);
+        const size_t tf = aff_tan_workspace_bytes(B, L1, L2, true);
         pe = pe > af ? pe : af;
         pe = pe > tf ? pe : tf;
         if (tf > 0) {
@@ -422,8 +422,6 @@ int d2p_sw_affine_forward_backward(const void* scores, int scores_dtype, const i
         a.order = nullptr;
         int rc;
         if (grads) {
-            // the order slot holds dS/dgap_ext between the two sweeps
-            a.pg_ext = (float*)order;
             a.sync = (int*)((char*)order + align256((size_t)B * sizeof(int)));
             rc = kNotHandled;
             SwArgs t = a;
@@ -437,7 +435,6 @@ int d2p_sw_affine_forward_backward(const void* scores, int scores_dtype, const i
                 else if (wr != kNotHandled) return wr;
             }
             if (t.scores) rc = launch_aff_tan(t, align256(tf), st);
-            a.pg_ext = nullptr;
             a.sync = nullptr;
         } else {
             if (lengths) {

@@ -60,11 +60,6 @@ struct SwArgs {
     const int* order;                   // [B] in, optional: problem of each CTA (largest first)
     int parts;                          // CTAs per problem (1 unless a kernel spreads problems)
     int* sync;                          // [B][kSyncBytes / 4], zeroed: cross-CTA words of each problem
-    // affine value + marginals + parameter gradients on the tangent kernel:
-    // a forward-only sweep along gap_ext leaves dS/dgap_ext in pg_ext [B],
-    // then the full sweep along gap_open reads it
-    int pg_fwd_only;
-    float* pg_ext;
 };
 
 // A problem spread over several CTAs (a cooperative launch) keeps its
@@ -109,7 +104,8 @@ bool engine_forced_plane();
 size_t lin_tan_workspace_bytes(int B, int L1, int L2, bool bf = false);
 // the affine counterpart (sw_affine_tangent.cu): HVP, dP/d(gap_open),
 // dP/d(gap_ext), dP/dT and their dot mode
-size_t aff_tan_workspace_bytes(int B, int L1, int L2);
+// pg: value + marginals + parameter gradients (keeps I and D per cell too)
+size_t aff_tan_workspace_bytes(int B, int L1, int L2, bool pg = false);
 int launch_aff_tan(const SwArgs& a, size_t ws_bytes, cudaStream_t st);
 // CTAs per problem for B problems of nw warps per CTA, one CTA per SM (the
 // row-block pipeline model; 1 = one CTA per problem)
