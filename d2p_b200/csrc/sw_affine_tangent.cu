@@ -1126,7 +1126,7 @@ size_t aff_tan_workspace_bytes(int B, int L1, int L2, bool pg) {
 }
 
 int launch_aff_tan(const SwArgs& a, size_t ws_bytes, cudaStream_t st) {
-    // PG: value + marginals + parameter gradients (two sweeps, see the kernel)
+    // PG: value + marginals + parameter gradients (one sweep pair, see the kernel)
     const bool pg = a.mode == MODE_MARG && (a.grad_gap || a.grad_gap2 || a.grad_T);
     if (a.mode != MODE_HVP && a.mode != MODE_PGAP && a.mode != MODE_PGE && a.mode != MODE_PT && !pg) return -1;
     if (!a.redo || engine_forced_plane()) return -1;

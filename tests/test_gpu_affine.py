@@ -209,7 +209,7 @@ def test_fast_long_rows(d2p, cuda_device, B, L1, L2):
     problem must come out of the linear-domain kernels themselves (one they
     flag is recomputed by the plane engine, whose result would be bitwise the
     plane engine's own) and match the oracle -- value + marginals, and with
-    parameter gradients (the tangent kernel's two gap sweeps)."""
+    parameter gradients (the tangent kernel's gap sweep pair)."""
     s = scores(B, L1, L2, seed=L1 + 5 * L2)
     v, m = torch.ops.d2p.soft_sw_affine_float(s.to(cuda_device), -2.0, -0.5, 1.0, None)
     v2, m2, g1, g2, g3 = torch.ops.d2p.soft_sw_affine_with_grads(s.to(cuda_device), -2.0, -0.5, 1.0, None)
@@ -275,7 +275,8 @@ def test_fast_and_plane_agree_and_repeat(d2p, cuda_device):
 ])
 def test_fast_param_grads(d2p, cuda_device, B, L1, L2, T, go, ge, ragged):
     """Value, marginals and dS/dgap_open, dS/dgap_ext, dS/dT from the tangent
-    kernel's two gap sweeps (Euler's identity for dS/dT) against the oracle;
+    kernel's gap sweep pair (dS/dgap_ext from the I and D visits, Euler's
+    identity for dS/dT) against the oracle;
     no problem may have been handed to the plane engine."""
     s = scores(B, L1, L2, seed=B + L1 + 7 * L2)
     ln = lengths_for(B, L1, L2, seed=L2, lo=L1 // 2) if ragged else None
@@ -364,7 +365,7 @@ def test_empty_problems_every_path(d2p, cuda_device):
 
 def test_bf16_param_grads_on_the_tangent_kernel(d2p, cuda_device):
     """bf16 scores with parameter gradients: the scores are widened (exactly)
-    for the tangent kernel's two gap sweeps, so every output equals the fp32
+    for the tangent kernel's gap sweep pair, so every output equals the fp32
     result of the widened scores bitwise, and no problem falls back to the
     plane engine."""
     B, L1, L2 = 4, 96, 128
