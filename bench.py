@@ -16,8 +16,15 @@ through the public API with every step's scores copied from pinned host memory
 and its values copied back; the copy for the next step overlaps the current
 step's compute (a copy stream and two device buffers), all inside the timed
 region.
-``--impl reference`` times the reference's own CPU kernels (oracle/_ref, built
-from the reference sources) on the host cores, on the same config.
+``strong`` (N > 1) is the same step with the config's batch split across the
+ranks (rank r takes the contiguous slice ``shard_bounds(B, N, r)`` of one
+globally seeded batch), timed the same way: the fixed-total-work curve.
+``hvp`` times the Hessian-vector product over the same batch (linear family).
+The MUFU roofline denominator is measured in the same run (``d2p_mufu_probe``,
+an ex2.approx throughput kernel).
+``--impl reference`` times the reference's own CPU operators (oracle/_ref, built
+from the reference sources: its schemas, CPU bindings, autograd and kernels)
+through ``torch.ops.d2p`` with ``value.sum().backward()``, on the host cores.
 """
 from __future__ import annotations
 
@@ -69,6 +76,36 @@ def load_peaks():
         return float(d["hbm_gbs"]), float(d.get("sm_max_mhz", 1965.0)), "measured"
     except Exception:
         return 6650.0, 1965.0, "fallback"
+
+
+def measure_mufu_peak(dev) -> float:
+    """ex2.approx operations per second of the whole GPU, by d2p_mufu_probe
+    (best of 5 launches after 3 warm-ups, CUDA events on the launching stream)."""
+    import ctypes
+
+    import torch
+
+    lib = ctypes.CDLL(os.path.join(ROOT, "d2p_b200", "libd2p_b200.so"))
+    lib.d2p_mufu_probe.restype = ctypes.c_int
+    lib.d2p_mufu_probe.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]
+    threads, chains = 512, 8  # D2P_MUFU_PROBE_THREADS, D2P_MUFU_PROBE_CHAINS
+    blocks = 4 * torch.cuda.get_device_properties(dev).multi_processor_count
+    iters = 4096
+    out = torch.empty(blocks * threads, device=dev)
+    st = torch.cuda.current_stream(dev)
+    best = None
+    for k in range(8):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        rc = lib.d2p_mufu_probe(ctypes.c_void_p(out.data_ptr()), blocks, iters, ctypes.c_void_p(st.cuda_stream))
+        e1.record(st)
+        if rc != 0:
+            raise RuntimeError(f"d2p_mufu_probe failed: {rc}")
+        torch.cuda.synchronize(dev)
+        if k >= 3:
+            t = e0.elapsed_time(e1) * 1e-3
+            best = t if best is None else min(best, t)
+    return blocks * threads * chains * iters / best
 
 
 # ----------------------------------------------------------------------------
@@ -303,6 +340,47 @@ def run_ours(args, cfg):
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_ms = float(te.item())
 
+    # ---------------- strong scaling: one global batch split across the ranks ----------------
+    # Rank r computes the slice shard_bounds(B, N, r) of the globally seeded
+    # batch (seed 0: rank 0's own inputs above) and the values are gathered,
+    # as soft_sw_sharded does.  At N = 1 this is the step timed above.
+    strong = None
+    if world > 1:
+        from d2p_b200.shard import shard_bounds
+
+        g_host, g_len = make_inputs(cfg, 0)
+        lo, hi = shard_bounds(cfg["B"], world, rank)
+        sh_dev = g_host[lo:hi].to(dev).requires_grad_(True)
+        sh_len = g_len[lo:hi].to(dev) if g_len is not None else None
+        del g_host
+        vals_g = torch.empty(cfg["B"], device=dev)
+
+        def strong_step():
+            if fam == "linear":
+                res = d2p.soft_sw(sh_dev, gap=gap, temperature=T, lengths=sh_len)
+            else:
+                res = d2p.soft_sw_affine(sh_dev, gap_open=gap[0], gap_ext=gap[1], temperature=T, lengths=sh_len)
+            torch.autograd.grad(res.value.sum(), sh_dev)
+            vals_g.copy_(gather_values(res.value.detach(), cfg["B"]))
+
+        for _ in range(args.warmup):
+            strong_step()
+        barrier()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(args.steps):
+            strong_step()
+        s1.record()
+        barrier()
+        ts = torch.tensor([s0.elapsed_time(s1) / args.steps], device=dev)
+        dist.all_reduce(ts, op=dist.ReduceOp.MAX)
+        st_ms = float(ts.item())
+        g_cells = valid_cells(cfg, g_len)
+        strong = {"value": round(g_cells / (st_ms * 1e-3) / 1e9, 3), "unit": "GCUPS", "ms_per_step": round(st_ms, 4),
+                  "global_batch": cfg["B"], "per_rank_batch": hi - lo,
+                  "note": "fixed total work: the config's batch split across the ranks, values all-gathered"}
+        del sh_dev
+
     total_cells = cells * world
     gcups = total_cells / (ms_max * 1e-3) / 1e9
     e2e_gcups = total_cells / (e2e_ms * 1e-3) / 1e9
@@ -316,7 +394,8 @@ def run_ours(args, cfg):
     # cells of the marginals are zero-filled: 4 B each)
     k_bytes = cells * score_bytes + padded * 4
     k_mufu = cells * MUFU_PER_CELL[fam]
-    mufu_peak = sm_count * MUFU_PER_SM_CLK * sm_max_mhz * 1e6  # ops/s at max SM clock
+    mufu_nominal = sm_count * MUFU_PER_SM_CLK * sm_max_mhz * 1e6  # ops/s at max SM clock
+    mufu_peak = measure_mufu_peak(dev)  # measured ex2.approx throughput, this GPU, this run
     t_hbm = k_bytes / (hbm_gbs * 1e9)
     t_mufu = k_mufu / mufu_peak
     bound = "mufu" if t_mufu >= t_hbm else "hbm"
@@ -340,13 +419,16 @@ def run_ours(args, cfg):
         "kernel_ms": round(k_ms, 4), "time_bound_ms": round(max(t_hbm, t_mufu) * 1e3, 4),
         "hbm_gbs_achieved": round(k_bytes / k_s / 1e9, 2), "hbm_peak_gbs": hbm_gbs,
         "mufu_tops_achieved": round(k_mufu / k_s / 1e12, 3), "mufu_peak_tops": round(mufu_peak / 1e12, 3),
-        "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs; MUFU = {sm_count} SM x 16/clk x {sm_max_mhz:.0f} MHz)",
+        "mufu_nominal_tops": round(mufu_nominal / 1e12, 3),
+        "peak_source": (f"HBM: {peak_src} (MEASURED_PEAKS.json hbm_gbs); MUFU: measured in this run by "
+                        f"d2p_mufu_probe (ex2.approx throughput; nominal {sm_count} SM x 16/clk x "
+                        f"{sm_max_mhz:.0f} MHz = {mufu_nominal / 1e12:.3f} Tops/s)"),
         "step_frac": round((max(t_hbm, t_mufu) + (8.0 * padded) / (hbm_gbs * 1e9)) / (ms_max * 1e-3), 4),
     }
 
     # ---------------- Hessian-vector product (BASELINE config 5 reports it) ----------------
     hvp = None
-    if fam == "linear" and (args.hvp or args.config == "c5"):
+    if fam == "linear" and not args.no_hvp:
         gv = torch.Generator().manual_seed(2 + 1000 * rank)
         v_dev = torch.randn(s_host.shape, generator=gv).to(dev)
         with torch.no_grad():
@@ -409,6 +491,8 @@ def run_ours(args, cfg):
             line["cpu_baseline"] = cpu
         if hvp is not None:
             line["hvp"] = hvp
+        if strong is not None:
+            line["strong"] = strong
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
@@ -417,56 +501,139 @@ def run_ours(args, cfg):
 # ----------------------------------------------------------------------------
 # reference CPU (oracle/_ref = the reference's own CPU kernels)
 # ----------------------------------------------------------------------------
-def _ref_step(cfg, s_np, len_np):
-    import oracle
-
-    if cfg["family"] == "linear":
-        r = oracle.sw_linear(s_np, len_np, cfg["gap"], cfg["T"], "ref")
-    else:
-        r = oracle.sw_affine(s_np, len_np, cfg["gap"][0], cfg["gap"][1], cfg["T"], "ref")
-    # value.sum().backward(): grad = 1 * marginals (the reference recomputes the
-    # reverse DP here; timing the elementwise product is the cheaper variant)
-    _ = r["marginals"] * 1.0
-    return r
+REF_OPS = os.path.join(ROOT, "oracle", "_ref", "libref_sw_ops.so")
+REF_CUDA_OPS = os.path.join(ROOT, "oracle", "_ref", "libref_sw_cuda_ops.so")
 
 
-def cpu_baseline(cfg, seconds: float, cores=None):
-    import numpy as np
-    import oracle
-
-    kind = "reference" if oracle.ref_available() else "port"
-    ncores = cores or os.cpu_count() or 1
-    oracle.set_threads(ncores)
+def _ref_inputs(cfg):
+    """The config's seeded inputs as the reference takes them: fp32 scores (bf16
+    scores upcast, as the reference's autocast rule does) and int32 lengths."""
     s_host, lengths = make_inputs(cfg, 0)
-    s_np = s_host.float().numpy()
-    len_np = lengths.numpy() if lengths is not None else None
-    impl = "ref" if kind == "reference" else "f32"
-    # bounded sample: grow the number of problems until one call takes >= ~0.5 s
+    return s_host.float(), lengths
+
+
+def _ref_fwd_bwd(cfg, s, ln):
+    """One step through the reference's own operators: forward (value +
+    marginals) and value.sum().backward() through its autograd Function."""
+    x = s.detach().requires_grad_(True)
+    if cfg["family"] == "linear":
+        v, m = __import__("torch").ops.d2p.soft_sw_float(x, cfg["gap"], cfg["T"], ln)
+    else:
+        v, m = __import__("torch").ops.d2p.soft_sw_affine_float(x, cfg["gap"][0], cfg["gap"][1], cfg["T"], ln)
+    v.sum().backward()
+    return v, x.grad
+
+
+def _cells(cfg, ln, nb):
+    import numpy as np
+
+    if ln is None:
+        return nb * cfg["L1"] * cfg["L2"]
+    ln = ln.cpu().numpy()
+    return int(np.sum(ln[:, 0].astype(np.int64) * ln[:, 1]))
+
+
+def _ref_cpu(cfg, steps: int, warmup: int, budget_s: float):
+    """The reference's CPU operators on every host core, on a bounded sample of
+    the config (the first nb problems, nb doubled until one step takes about
+    budget_s / 2).  Returns (GCUPS, ms per step, cores, sample, kind)."""
+    import torch
+
+    ncores = os.cpu_count() or 1
+    torch.set_num_threads(ncores)
+    s_all, ln_all = _ref_inputs(cfg)
+    kind = "reference"
+    if os.path.exists(REF_OPS):
+        torch.ops.load_library(REF_OPS)
+        step = lambda s, ln: _ref_fwd_bwd(cfg, s, ln)  # noqa: E731
+        path = "torch.ops.d2p (reference CPU operators) + value.sum().backward()"
+    else:  # no operator build: the reference's CPU kernels, or the port, through the oracle
+        import oracle
+
+        kind = "reference" if oracle.ref_available() else "port"
+        impl = "ref" if kind == "reference" else "f32"
+
+        def step(s, ln):
+            lnp = None if ln is None else ln.numpy()
+            if cfg["family"] == "linear":
+                return oracle.sw_linear(s.numpy(), lnp, cfg["gap"], cfg["T"], impl)
+            return oracle.sw_affine(s.numpy(), lnp, cfg["gap"][0], cfg["gap"][1], cfg["T"], impl)
+        path = f"CPU kernels ({impl}) through ctypes"
     nb = min(cfg["B"], max(1, ncores))
     while True:
-        sub = s_np[:nb]
-        ln = len_np[:nb] if len_np is not None else None
+        sub, ln = s_all[:nb], (ln_all[:nb] if ln_all is not None else None)
         t0 = time.perf_counter()
-        if impl == "ref":
-            _ref_step(cfg, sub, ln)
-        else:
-            oracle.sw_linear(sub, ln, cfg["gap"], cfg["T"], "f32")
+        step(sub, ln)
         dt = time.perf_counter() - t0
-        if dt >= 0.5 or nb >= cfg["B"]:
+        if dt * 2 > budget_s or nb >= cfg["B"]:
             break
         nb = min(cfg["B"], nb * 2)
-    reps = max(1, int(seconds / max(dt, 1e-3)))
-    best = dt
-    for _ in range(reps - 1):
+    for _ in range(warmup):
+        step(sub, ln)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step(sub, ln)
+    dt = (time.perf_counter() - t0) / steps
+    g = _cells(cfg, ln, nb) / dt / 1e9
+    sample = (f"{nb} of {cfg['B']} problems of {cfg['L1']}x{cfg['L2']} ({args_config_name(cfg)}) per step, "
+              f"fwd+bwd via {path}")
+    return g, dt * 1e3, ncores, sample, kind
+
+
+def _ref_cuda(cfg, budget_s: float):
+    """The reference's CUDA operators (its torch_cuda.cpp + kernels.cu built for
+    sm_100a) on cuda:0: fwd + value.sum().backward() through its autograd,
+    timed with CUDA events, on the first nb problems of the config (nb halved
+    from the full batch until one step fits budget_s).  None when unavailable."""
+    import torch
+
+    if not (torch.cuda.is_available() and os.path.exists(REF_CUDA_OPS)):
+        return None
+    torch.ops.load_library(REF_CUDA_OPS)
+    s_all, ln_all = _ref_inputs(cfg)
+    dev = torch.device("cuda", 0)
+    nb = cfg["B"]
+    while True:
+        s = s_all[:nb].to(dev)
+        ln = ln_all[:nb].to(dev) if ln_all is not None else None
+        torch.cuda.synchronize()
         t0 = time.perf_counter()
-        if impl == "ref":
-            _ref_step(cfg, sub, ln)
-        else:
-            oracle.sw_linear(sub, ln, cfg["gap"], cfg["T"], "f32")
-        best = min(best, time.perf_counter() - t0)
-    c = int(np.sum(ln[:, 0].astype(np.int64) * ln[:, 1])) if ln is not None else nb * cfg["L1"] * cfg["L2"]
-    return {"value": round(c / best / 1e9, 5), "unit": "GCUPS", "cores": ncores, "kind": kind,
-            "sample": f"{nb} problems of {cfg['L1']}x{cfg['L2']} ({args_config_name(cfg)}), fwd+bwd, best of {reps}"}
+        _ref_fwd_bwd(cfg, s, ln)
+        torch.cuda.synchronize()
+        dt = time.perf_counter() - t0
+        if dt <= budget_s or nb == 1:
+            break
+        nb = max(1, nb // 2)
+    _ref_fwd_bwd(cfg, s, ln)  # warm-up
+    reps = max(1, min(5, int(budget_s / max(dt, 1e-3))))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(reps):
+        _ref_fwd_bwd(cfg, s, ln)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    cells = _cells(cfg, ln, nb)
+    return {"value": round(cells / (ms * 1e-3) / 1e9, 4), "unit": "GCUPS", "ms_per_step": round(ms, 3),
+            "sample": f"{nb} of {cfg['B']} problems of {cfg['L1']}x{cfg['L2']}, fwd+bwd, {reps} steps",
+            "build": "reference src/sw{,_affine}/{torch_cuda.cpp,kernels.cu}, nvcc -gencode "
+                     "arch=compute_100a,code=sm_100a (oracle/Makefile)"}
+
+
+def cpu_baseline(cfg, seconds: float):
+    """The reference's CPU operators timed on the host cores, in a child process
+    (its operators register the same torch.ops.d2p names as this library)."""
+    name = args_config_name(cfg)
+    cmd = [sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--cpu-only",
+           "--steps", "2", "--warmup", "3", "--config", name, "--ref-step-seconds", str(seconds)]
+    r = subprocess.run(cmd, capture_output=True, text=True, env=dict(os.environ, RANK="0", WORLD_SIZE="1"))
+    for line in r.stdout.splitlines()[::-1]:
+        if line.startswith("{"):
+            d = json.loads(line)
+            return d["cpu_baseline"]
+    return {"value": None, "unit": "GCUPS", "cores": os.cpu_count(), "kind": "reference",
+            "sample": "failed: " + (r.stderr.strip().splitlines() or ["no output"])[-1][:200]}
 
 
 def args_config_name(cfg):
@@ -480,44 +647,22 @@ def run_reference(args, cfg):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    import numpy as np
-    import oracle
-
-    kind = "reference" if oracle.ref_available() else "port"
-    ncores = os.cpu_count() or 1
-    oracle.set_threads(ncores)
-    s_host, lengths = make_inputs(cfg, 0)
-    s_np = s_host.float().numpy()
-    len_np = lengths.numpy() if lengths is not None else None
-    # bounded per-step sample sized so the whole run stays within a few minutes
-    nb = min(cfg["B"], max(1, ncores))
-    budget = args.ref_step_seconds
-    while True:
-        t0 = time.perf_counter()
-        _ref_step(cfg, s_np[:nb], len_np[:nb] if len_np is not None else None)
-        dt = time.perf_counter() - t0
-        if dt * 2 > budget or nb >= cfg["B"]:
-            break
-        nb = min(cfg["B"], nb * 2)
-    sub = s_np[:nb]
-    ln = len_np[:nb] if len_np is not None else None
-    for _ in range(args.warmup):
-        _ref_step(cfg, sub, ln)
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        _ref_step(cfg, sub, ln)
-    dt = (time.perf_counter() - t0) / args.steps
-    c = int(np.sum(ln[:, 0].astype(np.int64) * ln[:, 1])) if ln is not None else nb * cfg["L1"] * cfg["L2"]
-    g = c / dt / 1e9
-    sample = f"{nb} of {cfg['B']} problems of {cfg['L1']}x{cfg['L2']} per step, fwd+bwd"
+    g, ms, ncores, sample, kind = _ref_cpu(cfg, args.steps, args.warmup, args.ref_step_seconds)
     line = {
         "impl": "reference", "metric": METRIC, "value": round(g, 5), "unit": "GCUPS", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1))",
         "config": {"workload": f"{args.config}: {cfg['desc']}", "sample": sample},
         "cpu_baseline": {"value": round(g, 5), "unit": "GCUPS", "cores": ncores, "kind": kind, "sample": sample},
         "e2e": {"value": round(g, 5), "unit": "GCUPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if not args.cpu_only:
+        try:
+            rc = _ref_cuda(cfg, args.ref_cuda_seconds)
+        except Exception as exc:  # reported, not fatal: the CPU figure is the arm's value
+            rc = {"value": None, "error": f"{type(exc).__name__}: {str(exc)[:200]}"}
+        if rc is not None:
+            line["ref_cuda"] = rc
     print(json.dumps(line), flush=True)
 
 
@@ -529,11 +674,13 @@ def main():
     ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--cpu-seconds", type=float, default=8.0)
+    ap.add_argument("--cpu-seconds", type=float, default=4.0)
     ap.add_argument("--ref-step-seconds", type=float, default=6.0)
+    ap.add_argument("--cpu-only", action="store_true", help="reference arm: skip the reference CUDA leg")
+    ap.add_argument("--ref-cuda-seconds", type=float, default=5.0)
     ap.add_argument("--batch", type=int, default=0, help="override the per-rank batch (profiling on a small case)")
-    ap.add_argument("--hvp", action="store_true",
-                    help="also time the Hessian-vector product (linear family; on by default for c5)")
+    ap.add_argument("--no-hvp", action="store_true",
+                    help="skip the Hessian-vector product leg (timed by default for the linear family)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

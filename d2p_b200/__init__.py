@@ -10,6 +10,9 @@ tensors and autocast rules are registered for torch.compile (d2p/__init__.py).
 """
 from . import _ops  # loads the native extension (fails loudly if missing)
 from . import _compile  # noqa: F401  register_fake / register_autocast
+from . import _pt2_ops  # the d2p_py:: custom ops torch.compile traces
+
+_ops._pt2_mod = _pt2_ops
 from .sw import SoftSW, SoftSWAffine, SWResult, soft_sw, soft_sw_affine
 from . import ops
 

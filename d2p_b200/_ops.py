@@ -83,15 +83,12 @@ _load_extension()
 #: the full ``torch.ops.d2p`` namespace for advanced users
 d2p = torch.ops.d2p
 
+# The d2p_py:: custom ops (set by the package __init__ once both modules are
+# loaded): no import may run inside a call that Dynamo traces.
 _pt2_mod = None
 
 
 def _get_pt2_ops():
-    global _pt2_mod
-    if _pt2_mod is None:
-        from . import _pt2_ops
-
-        _pt2_mod = _pt2_ops
     return _pt2_mod
 
 

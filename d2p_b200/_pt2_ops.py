@@ -13,18 +13,6 @@ from typing import Optional
 import torch
 from torch.library import custom_op
 
-from ._pt2_utils import _is_fake_tensor
-
-
-def _scalar(value, default: float = 0.0) -> float:
-    if isinstance(value, (int, float)):
-        return float(value)
-    if isinstance(value, torch.Tensor):
-        if _is_fake_tensor(value):
-            return default
-        return float(value.item())
-    return float(value)
-
 
 def _add(a, b):
     if a is None:
@@ -114,25 +102,52 @@ def _(scores, gap, temperature, lengths):
     return _like(scores, "B", "P")
 
 
+# The backward of the tensor-parameter ops needs the parameters' values as
+# scalars.  Read while tracing, they would be frozen into the compiled graph
+# (or be data-dependent), so the backward formulas call these ops, which take
+# the parameters as tensors and read them only when they run.
+@custom_op("d2p_py::soft_sw_param_grads_t", mutates_args=())
+def soft_sw_param_grads_t(scores: torch.Tensor, gap: torch.Tensor, temperature: torch.Tensor,
+                          lengths: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    _, _, dgap, dt = torch.ops.d2p.soft_sw_with_grads(scores, float(gap), float(temperature), lengths)
+    return dgap, dt
+
+
+@soft_sw_param_grads_t.register_fake
+def _(scores, gap, temperature, lengths):
+    return _like(scores, "B", "B")
+
+
+@custom_op("d2p_py::soft_sw_backward_full_t", mutates_args=())
+def soft_sw_backward_full_t(scores: torch.Tensor, grad_alignment: torch.Tensor, gap: torch.Tensor,
+                            temperature: torch.Tensor,
+                            lengths: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    a, b, c = torch.ops.d2p.soft_sw_backward_full(scores, grad_alignment, float(gap), float(temperature), lengths)
+    return a, b, c
+
+
+@soft_sw_backward_full_t.register_fake
+def _(scores, grad_alignment, gap, temperature, lengths):
+    return _like(scores, "P", "1", "1")
+
+
 def _soft_sw_setup(ctx, inputs, output):
     scores, gap, temperature, lengths = inputs
-    ctx.save_for_backward(scores, output[1])
-    ctx.gap = _scalar(gap)
-    ctx.temperature = _scalar(temperature)
+    ctx.save_for_backward(scores, output[1], gap.detach(), temperature.detach())
     ctx.lengths = lengths
 
 
 def _soft_sw_backward(ctx, grad_value, grad_marg):
-    scores, marg = ctx.saved_tensors
+    scores, marg, gap, temperature = ctx.saved_tensors
     grad_scores = _expand_batch(grad_value, marg)
     need_gap, need_t = ctx.needs_input_grad[1], ctx.needs_input_grad[2]
     g_gap = g_t = None
     if grad_value is not None and (need_gap or need_t):
-        _, _, dgap, dt = soft_sw_with_grads(scores, ctx.gap, ctx.temperature, ctx.lengths)
+        dgap, dt = soft_sw_param_grads_t(scores, gap, temperature, ctx.lengths)
         g_gap = _batch_dot(grad_value, dgap) if need_gap else None
         g_t = _batch_dot(grad_value, dt) if need_t else None
     if grad_marg is not None:
-        gs, gg, gt = soft_sw_backward_full(scores, grad_marg, ctx.gap, ctx.temperature, ctx.lengths)
+        gs, gg, gt = soft_sw_backward_full_t(scores, grad_marg, gap, temperature, ctx.lengths)
         grad_scores = _add(grad_scores, gs)
         g_gap = _add(g_gap, gg) if need_gap else None
         g_t = _add(g_t, gt) if need_t else None
@@ -234,25 +249,51 @@ def _(scores, gap_open, gap_ext, temperature, lengths):
     return _like(scores, "B", "P")
 
 
+@custom_op("d2p_py::soft_sw_affine_param_grads_t", mutates_args=())
+def soft_sw_affine_param_grads_t(scores: torch.Tensor, gap_open: torch.Tensor, gap_ext: torch.Tensor,
+                                 temperature: torch.Tensor,
+                                 lengths: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    r = torch.ops.d2p.soft_sw_affine_with_grads(scores, float(gap_open), float(gap_ext), float(temperature), lengths)
+    return r[2], r[3], r[4]
+
+
+@soft_sw_affine_param_grads_t.register_fake
+def _(scores, gap_open, gap_ext, temperature, lengths):
+    return _like(scores, "B", "B", "B")
+
+
+@custom_op("d2p_py::soft_sw_affine_backward_full_t", mutates_args=())
+def soft_sw_affine_backward_full_t(scores: torch.Tensor, grad_alignment: torch.Tensor, gap_open: torch.Tensor,
+                                   gap_ext: torch.Tensor, temperature: torch.Tensor, lengths: torch.Tensor
+                                   ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    a, b, c, d = torch.ops.d2p.soft_sw_affine_backward_full(scores, grad_alignment, float(gap_open), float(gap_ext),
+                                                            float(temperature), lengths)
+    return a, b, c, d
+
+
+@soft_sw_affine_backward_full_t.register_fake
+def _(scores, grad_alignment, gap_open, gap_ext, temperature, lengths):
+    return _like(scores, "P", "1", "1", "1")
+
+
 def _soft_sw_affine_setup(ctx, inputs, output):
     scores, go, ge, temperature, lengths = inputs
-    ctx.save_for_backward(scores, output[1])
-    ctx.go, ctx.ge, ctx.temperature = _scalar(go), _scalar(ge), _scalar(temperature)
+    ctx.save_for_backward(scores, output[1], go.detach(), ge.detach(), temperature.detach())
     ctx.lengths = lengths
 
 
 def _soft_sw_affine_backward(ctx, grad_value, grad_marg):
-    scores, marg = ctx.saved_tensors
+    scores, marg, go, ge, temperature = ctx.saved_tensors
     grad_scores = _expand_batch(grad_value, marg)
     need = ctx.needs_input_grad[1:4]
     grads = [None, None, None]
     if grad_value is not None and any(need):
-        fwd = soft_sw_affine_with_grads(scores, ctx.go, ctx.ge, ctx.temperature, ctx.lengths)
+        pg = soft_sw_affine_param_grads_t(scores, go, ge, temperature, ctx.lengths)
         for k in range(3):
             if need[k]:
-                grads[k] = _batch_dot(grad_value, fwd[2 + k])
+                grads[k] = _batch_dot(grad_value, pg[k])
     if grad_marg is not None:
-        r = soft_sw_affine_backward_full(scores, grad_marg, ctx.go, ctx.ge, ctx.temperature, ctx.lengths)
+        r = soft_sw_affine_backward_full_t(scores, grad_marg, go, ge, temperature, ctx.lengths)
         grad_scores = _add(grad_scores, r[0])
         for k in range(3):
             if need[k]:

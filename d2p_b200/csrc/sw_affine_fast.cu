@@ -969,28 +969,28 @@ int launch_aff_fast(const SwArgs& a0, size_t ws_bytes, cudaStream_t st) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return (int)e;
-    static int sms[64] = {0};
-    static bool attr_set[64] = {false};
+    static DeviceSetup setup;
     const size_t s6 = sizeof(aff::WarpSmem) * aff::kNW, s12 = sizeof(aff::WarpSmem) * aff::kNWWide;
-    if (dev < 64 && !attr_set[dev]) {
+    int nsm = 0;
+    const int se = device_setup(setup, dev, [s6, s12] {
         const void* ks[3] = {(const void*)aff::aff_fast_kernel<aff::kNW, 2, false>,
                              (const void*)aff::aff_fast_kernel<aff::kNWWide, 1, false>,
                              (const void*)aff::aff_fast_kernel<aff::kNWWide, 1, true>};
-        for (int i = 0; i < 3 && e == cudaSuccess; ++i) {
-            e = cudaFuncSetAttribute(ks[i], cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(i == 0 ? s6 : s12));
-            if (e == cudaSuccess)
-                e = cudaFuncSetAttribute(ks[i], cudaFuncAttributePreferredSharedMemoryCarveout,
+        cudaError_t r = cudaSuccess;
+        for (int i = 0; i < 3 && r == cudaSuccess; ++i) {
+            r = cudaFuncSetAttribute(ks[i], cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(i == 0 ? s6 : s12));
+            if (r == cudaSuccess)
+                r = cudaFuncSetAttribute(ks[i], cudaFuncAttributePreferredSharedMemoryCarveout,
                                          (int)cudaSharedmemCarveoutMaxShared);
         }
-        if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
-        if (e != cudaSuccess) return (int)e;
-        attr_set[dev] = true;
-    }
+        return (int)r;
+    }, &nsm);
+    if (se != 0) return se;
     // A batch that leaves most SMs idle spreads each problem over several CTAs
     // of 12 warps (cooperative launch: every part resident at once); at most
     // one problem per SM runs 12 warps per problem when that pays (see
     // launch_lin_fast).
-    const int K = (dev < 64 && a.sync) ? lin_parts_nw(a.B, a.L1, a.L2, sms[dev], aff::kNWWide) : 1;
+    const int K = a.sync ? lin_parts_nw(a.B, a.L1, a.L2, nsm, aff::kNWWide) : 1;
     if (K > 1) {
         SwArgs s = a;
         s.parts = K;
@@ -1003,7 +1003,7 @@ int launch_aff_fast(const SwArgs& a0, size_t ws_bytes, cudaStream_t st) {
         if (e == cudaSuccess) return 0;
         cudaGetLastError();  // a cooperative launch that does not fit: one CTA per problem instead
     }
-    if (dev < 64 && a.B <= sms[dev] && lin_wide_pays(a.L1, a.L2)) {
+    if (a.B <= nsm && lin_wide_pays(a.L1, a.L2)) {
         aff::aff_fast_kernel<aff::kNWWide, 1, false><<<a.B, aff::kNWWide * 32, s12, st>>>(a);
     } else {
         aff::aff_fast_kernel<aff::kNW, 2, false><<<a.B, aff::kNW * 32, s6, st>>>(a);

@@ -1146,9 +1146,9 @@ int launch_aff_tan(const SwArgs& a, size_t ws_bytes, cudaStream_t st) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return (int)e;
-    static int sms[64] = {0};
-    static bool attr_set[64] = {false};
-    if (dev < 64 && !attr_set[dev]) {
+    static DeviceSetup setup;
+    int nsm = 0;
+    const int se = device_setup(setup, dev, [smem] {
         const void* ks[8] = {(const void*)atan_::aff_tan_kernel<true, false, false, false>,
                              (const void*)atan_::aff_tan_kernel<false, false, false, false>,
                              (const void*)atan_::aff_tan_kernel<true, true, false, false>,
@@ -1158,17 +1158,16 @@ int launch_aff_tan(const SwArgs& a, size_t ws_bytes, cudaStream_t st) {
                              (const void*)atan_::aff_tan_kernel<false, false, false, true>,
                              (const void*)atan_::aff_tan_kernel<false, false, true, true>};
         for (const void* k : ks) {
-            e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            if (e == cudaSuccess)
-                e = cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout,
+            cudaError_t r = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (r == cudaSuccess)
+                r = cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout,
                                          (int)cudaSharedmemCarveoutMaxShared);
-            if (e != cudaSuccess) return (int)e;
+            if (r != cudaSuccess) return (int)r;
         }
-        e = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
-        if (e != cudaSuccess) return (int)e;
-        attr_set[dev] = true;
-    }
-    const int K = (dev < 64 && a.sync) ? lin_parts_nw(a.B, a.L1, a.L2, sms[dev], atan_::kNW) : 1;
+        return 0;
+    }, &nsm);
+    if (se != 0) return se;
+    const int K = a.sync ? lin_parts_nw(a.B, a.L1, a.L2, nsm, atan_::kNW) : 1;
     // one sweep pair; a spread launch zeroes the flags itself unless told not
     // to (PG zeroes them before the launch: its kernels OR their bits in)
     auto sweep = [&](const SwArgs& x, bool zero_redo) -> cudaError_t {

@@ -25,12 +25,11 @@ constexpr int kNotHandled = -1;
 static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 bool engine_forced_plane() {
-    static int v = -1;
-    if (v < 0) {
+    static const bool v = [] {  // read once (thread-safe static initialisation)
         const char* e = getenv("D2P_B200_ENGINE");
-        v = (e && strcmp(e, "plane") == 0) ? 1 : 0;
-    }
-    return v == 1;
+        return e && strcmp(e, "plane") == 0;
+    }();
+    return v;
 }
 
 static bool dims_ok(int B, int L1, int L2) {

@@ -5,7 +5,48 @@
 #include <cuda_runtime.h>
 #include <stddef.h>
 
+#include <atomic>
+#include <mutex>
+
 namespace d2pb {
+
+// One-time set-up of a launcher on a device (kernel attributes), safe when
+// several host threads make their first call at once.  `setup()` runs once
+// per device under the lock and returns a cudaError_t; the device's SM count
+// is published with release ordering only after it, so a thread that reads a
+// nonzero count has also seen the attributes set.  Devices past the cache
+// run the set-up on every call.  Returns a cudaError_t and the SM count
+// through *sms.
+constexpr int kMaxSetupDevices = 64;
+struct DeviceSetup {
+    std::atomic<int> sms[kMaxSetupDevices];
+    std::mutex mu;
+};
+template <class F>
+inline int device_setup(DeviceSetup& ds, int dev, F&& setup, int* sms) {
+    if (dev >= 0 && dev < kMaxSetupDevices) {
+        const int n = ds.sms[dev].load(std::memory_order_acquire);
+        if (n > 0) {
+            *sms = n;
+            return 0;
+        }
+    }
+    std::lock_guard<std::mutex> lk(ds.mu);
+    if (dev >= 0 && dev < kMaxSetupDevices) {
+        const int n = ds.sms[dev].load(std::memory_order_relaxed);
+        if (n > 0) {
+            *sms = n;
+            return 0;
+        }
+    }
+    cudaError_t e = (cudaError_t)setup();
+    int n = 0;
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return (int)e;
+    if (dev >= 0 && dev < kMaxSetupDevices) ds.sms[dev].store(n, std::memory_order_release);
+    *sms = n;
+    return 0;
+}
 
 // operator modes (one kernel instantiation each)
 enum SwMode : int {

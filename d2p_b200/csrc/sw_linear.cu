@@ -1030,33 +1030,32 @@ int launch_lin_fast(const SwArgs& a, size_t ws_bytes, cudaStream_t st) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return (int)e;
-    static int sms[64] = {0};
-    static bool attr_set[64] = {false};
-    if (dev < 64 && !attr_set[dev]) {
+    static DeviceSetup setup;
+    int nsm = 0;
+    const int se = device_setup(setup, dev, [] {
         const size_t s6 = sizeof(lin::WarpSmem) * lin::kNW, s12 = sizeof(lin::WarpSmem) * lin::kNWWide;
         const void* k6 = (const void*)lin::lin_fast_kernel<lin::kNW, 2, false>;
         const void* k12[2] = {(const void*)lin::lin_fast_kernel<lin::kNWWide, 1, false>,
                               (const void*)lin::lin_fast_kernel<lin::kNWWide, 1, true>};
-        e = cudaFuncSetAttribute(k6, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s6);
-        if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(k6, cudaFuncAttributePreferredSharedMemoryCarveout,
+        cudaError_t r = cudaFuncSetAttribute(k6, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s6);
+        if (r == cudaSuccess)
+            r = cudaFuncSetAttribute(k6, cudaFuncAttributePreferredSharedMemoryCarveout,
                                      (int)cudaSharedmemCarveoutMaxShared);
-        for (int i = 0; i < 2 && e == cudaSuccess; ++i) {
-            e = cudaFuncSetAttribute(k12[i], cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s12);
-            if (e == cudaSuccess)
-                e = cudaFuncSetAttribute(k12[i], cudaFuncAttributePreferredSharedMemoryCarveout,
+        for (int i = 0; i < 2 && r == cudaSuccess; ++i) {
+            r = cudaFuncSetAttribute(k12[i], cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s12);
+            if (r == cudaSuccess)
+                r = cudaFuncSetAttribute(k12[i], cudaFuncAttributePreferredSharedMemoryCarveout,
                                          (int)cudaSharedmemCarveoutMaxShared);
         }
-        if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
-        if (e != cudaSuccess) return (int)e;
-        attr_set[dev] = true;
-    }
+        return (int)r;
+    }, &nsm);
+    if (se != 0) return se;
     // A batch of at most one problem per SM may run 12 warps per problem,
     // when the pipeline model says that pays (12 warps on one SM run each
     // stage about 25 % slower: measured 1.19 - 1.32 on 256 x 1024 .. 1024 x 1024).
     // A batch that leaves most SMs idle spreads each problem over several
     // CTAs (cooperative launch: every part resident at once).
-    const int K = (dev < 64 && a.sync) ? lin_parts_nw(a.B, a.L1, a.L2, sms[dev], lin::kNWWide) : 1;
+    const int K = a.sync ? lin_parts_nw(a.B, a.L1, a.L2, nsm, lin::kNWWide) : 1;
     if (K > 1) {
         SwArgs s = a;
         s.parts = K;
@@ -1069,7 +1068,7 @@ int launch_lin_fast(const SwArgs& a, size_t ws_bytes, cudaStream_t st) {
         if (e == cudaSuccess) return 0;
         cudaGetLastError();  // a cooperative launch that does not fit: one CTA per problem instead
     }
-    if (dev < 64 && a.B <= sms[dev] && wide_pays(a.L1, a.L2)) {
+    if (a.B <= nsm && wide_pays(a.L1, a.L2)) {
         lin::lin_fast_kernel<lin::kNWWide, 1, false>
             <<<a.B, lin::kNWWide * 32, sizeof(lin::WarpSmem) * lin::kNWWide, st>>>(a);
     } else {

@@ -1139,9 +1139,9 @@ int launch_lin_tan(const SwArgs& a, size_t ws_bytes, cudaStream_t st) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return (int)e;
-    static int sms[64] = {0};
-    static bool attr_set[64] = {false};
-    if (dev < 64 && !attr_set[dev]) {
+    static DeviceSetup setup;
+    int nsm = 0;
+    const int se = device_setup(setup, dev, [smem] {
         const void* ks[10] = {(const void*)ltan::lin_tan_kernel<true, false, false, false, false>,
                               (const void*)ltan::lin_tan_kernel<false, false, false, false, false>,
                               (const void*)ltan::lin_tan_kernel<true, true, false, false, false>,
@@ -1153,22 +1153,21 @@ int launch_lin_tan(const SwArgs& a, size_t ws_bytes, cudaStream_t st) {
                               (const void*)ltan::lin_tan_kernel<true, false, false, false, true>,
                               (const void*)ltan::lin_tan_kernel<true, false, true, false, true>};
         for (const void* k : ks) {
-            e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            if (e == cudaSuccess)
-                e = cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout,
+            cudaError_t r = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (r == cudaSuccess)
+                r = cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout,
                                          (int)cudaSharedmemCarveoutMaxShared);
-            if (e != cudaSuccess) return (int)e;
+            if (r != cudaSuccess) return (int)r;
         }
-        e = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
-        if (e != cudaSuccess) return (int)e;
-        attr_set[dev] = true;
-    }
+        return 0;
+    }, &nsm);
+    if (se != 0) return se;
     // value + marginals + parameter gradients: only while one wave of CTAs
     // (one per SM) holds the batch; larger batches run the log-domain kernel
-    if (pg && (dev >= 64 || a.B > sms[dev])) return -1;
+    if (pg && a.B > nsm) return -1;
     // few large problems: several CTAs per problem (sw_linear.cu's rule, with
     // this kernel's 6 warps per CTA)
-    const int K = (dev < 64 && a.sync) ? lin_parts_nw(a.B, a.L1, a.L2, sms[dev], ltan::kNW) : 1;
+    const int K = a.sync ? lin_parts_nw(a.B, a.L1, a.L2, nsm, ltan::kNW) : 1;
     if (K > 1) {
         SwArgs s = a;
         s.parts = K;

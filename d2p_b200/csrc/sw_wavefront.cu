@@ -748,12 +748,12 @@ int launch_wavefront(const SwArgs& a, int family, size_t ws_bytes, cudaStream_t 
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return (int)e;
-    static bool attr_set[64] = {false};
-    if (dev < 64 && !attr_set[dev]) {
-        e = cudaFuncSetAttribute(wf::lin_marg_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return (int)e;
-        attr_set[dev] = true;
-    }
+    static DeviceSetup setup;
+    int nsm = 0;
+    const int se = device_setup(setup, dev, [smem] {
+        return (int)cudaFuncSetAttribute(wf::lin_marg_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    }, &nsm);
+    if (se != 0) return se;
     wf::lin_marg_kernel<<<a.B, wf::kNW * 32, smem, st>>>(a);
     return (int)cudaGetLastError();
 }

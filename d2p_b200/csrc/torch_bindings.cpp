@@ -73,6 +73,21 @@ Shape checked_shape(const Tensor& scores) {
     return s;
 }
 
+// src/sw_affine/torch_cuda.cpp:35-67: the affine family's limit counts its three
+// state tables, 3 (L1 + 1) (L2 + 1) <= INT_MAX, with the reference's messages.
+Shape checked_affine_shape(const Tensor& scores) {
+    TORCH_CHECK(scores.dim() == 3, "scores must be 3D (B, L1, L2)");
+    Shape s{checked_dim(scores.size(0), "scores batch dimension"),
+            checked_dim(scores.size(1), "scores L1 dimension"),
+            checked_dim(scores.size(2), "scores L2 dimension")};
+    TORCH_CHECK(s.L1 <= std::numeric_limits<int>::max() - s.L2,
+                "sw_affine dimensions too large: L1 + L2 exceeds CUDA int index range");
+    const int64_t cells = 3 * (static_cast<int64_t>(s.L1) + 1) * (static_cast<int64_t>(s.L2) + 1);
+    TORCH_CHECK(cells <= static_cast<int64_t>(std::numeric_limits<int>::max()),
+                "sw_affine DP table too large: 3 * (L1 + 1) * (L2 + 1) exceeds CUDA int index range");
+    return s;
+}
+
 // src/sw/torch_cuda.cpp:67-97: same checks and messages.  The range check needs
 // the values on the host (one small device->host copy), as in the reference.
 void validate_lengths(const Tensor& lengths, const Shape& s, const torch::Device& device) {
@@ -308,7 +323,8 @@ std::tuple<Tensor, Tensor, Tensor, Tensor> soft_sw_with_grads_cuda(Tensor scores
     pg.host = (float)gap;
     pT.host = (float)temperature;
     LinFwd r = lin_forward(scores, pg, pT, len, s, true);
-    return {r.value, r.marginals, r.dparams[0], r.dparams[1]};
+    // the schema's outputs are independent tensors: no views of one buffer
+    return {r.value, r.marginals, r.dparams[0].clone(), r.dparams[1].clone()};
 }
 
 Tensor soft_sw_hvp_cuda(Tensor scores, Tensor tangent, double gap, double temperature,
@@ -470,7 +486,7 @@ class SoftSWAffineFunction : public torch::autograd::Function<SoftSWAffineFuncti
         Tensor lengths = lengths_opt.has_value() ? *lengths_opt : Tensor();
         ctx->set_materialize_grads(false);
         D2PB_CHECK_AFF_SCORES(scores);
-        const Shape s = checked_shape(scores);
+        const Shape s = checked_affine_shape(scores);
         c10::cuda::CUDAGuard guard(scores.device());
         Param po = read_param(gap_open, scores, "gap_open");
         Param pe = read_param(gap_ext, scores, "gap_ext");
@@ -489,7 +505,7 @@ class SoftSWAffineFunction : public torch::autograd::Function<SoftSWAffineFuncti
         Tensor go = saved[3], ge = saved[4], temperature = saved[5];
         Tensor lengths;
         if (!ctx->saved_data["lengths"].isNone()) lengths = ctx->saved_data["lengths"].toTensor();
-        const Shape s = checked_shape(scores);
+        const Shape s = checked_affine_shape(scores);
         c10::cuda::CUDAGuard guard(scores.device());
         auto opt = scores.options().dtype(torch::kFloat32);
         Tensor gv = grad_outputs[0], gm = grad_outputs[1];
@@ -545,7 +561,7 @@ std::vector<Tensor> soft_sw_affine_cuda(Tensor scores, Tensor gap_open, Tensor g
 std::vector<Tensor> soft_sw_affine_float_cuda(Tensor scores, double gap_open, double gap_ext,
                                               double temperature, c10::optional<Tensor> lengths) {
     D2PB_CHECK_AFF_SCORES(scores);
-    const Shape s = checked_shape(scores);
+    const Shape s = checked_affine_shape(scores);
     c10::cuda::CUDAGuard guard(scores.device());
     Tensor len = resolve_lengths(lengths, s, scores.device());
     auto cpu = torch::TensorOptions().dtype(torch::kFloat32);
@@ -558,7 +574,7 @@ std::vector<Tensor> soft_sw_affine_float_cuda(Tensor scores, double gap_open, do
 std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor> soft_sw_affine_with_grads_cuda(
     Tensor scores, double gap_open, double gap_ext, double temperature, c10::optional<Tensor> lengths) {
     D2PB_CHECK_AFF_SCORES(scores);
-    const Shape s = checked_shape(scores);
+    const Shape s = checked_affine_shape(scores);
     c10::cuda::CUDAGuard guard(scores.device());
     Tensor len = resolve_lengths(lengths, s, scores.device());
     Param po, pe, pT;
@@ -566,7 +582,7 @@ std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor> soft_sw_affine_with_grads_cud
     pe.host = (float)gap_ext;
     pT.host = (float)temperature;
     AffFwd r = aff_forward(scores, po, pe, pT, len, s, true);
-    return {r.value, r.marginals, r.dparams[0], r.dparams[1], r.dparams[2]};
+    return {r.value, r.marginals, r.dparams[0].clone(), r.dparams[1].clone(), r.dparams[2].clone()};
 }
 
 Tensor soft_sw_affine_hvp_cuda(Tensor scores, Tensor tangent, double gap_open, double gap_ext,
@@ -577,7 +593,7 @@ Tensor soft_sw_affine_hvp_cuda(Tensor scores, Tensor tangent, double gap_open, d
     TORCH_CHECK(scores.sizes() == tangent.sizes(), "scores and tangent must have same shape");
     TORCH_CHECK(tangent.device() == scores.device(), "tangent must be on same device as scores, got ",
                 tangent.device(), " vs ", scores.device());
-    const Shape s = checked_shape(scores);
+    const Shape s = checked_affine_shape(scores);
     c10::cuda::CUDAGuard guard(scores.device());
     Tensor len = resolve_lengths(lengths, s, scores.device());
     return aff_hvp_raw(scores, tangent, (float)gap_open, (float)gap_ext, (float)temperature, len, s);
@@ -589,7 +605,7 @@ Tensor soft_sw_affine_param_jacobian_cuda(Tensor scores, int64_t param_type, dou
     D2PB_CHECK_INPUT(scores);
     TORCH_CHECK(scores.dim() == 3, "scores must be 3D");
     TORCH_CHECK(param_type >= 0 && param_type <= 2, "param_type must be 0, 1, or 2");
-    const Shape s = checked_shape(scores);
+    const Shape s = checked_affine_shape(scores);
     c10::cuda::CUDAGuard guard(scores.device());
     Tensor len = resolve_lengths(lengths, s, scores.device());
     return aff_jac_raw(scores, (int)param_type, (float)gap_open, (float)gap_ext, (float)temperature, len, s);
@@ -605,7 +621,7 @@ std::tuple<Tensor, Tensor, Tensor, Tensor> soft_sw_affine_backward_full_cuda(
     TORCH_CHECK(grad_alignment.device() == scores.device(),
                 "grad_alignment must be on same device as scores, got ", grad_alignment.device(), " vs ",
                 scores.device());
-    const Shape s = checked_shape(scores);
+    const Shape s = checked_affine_shape(scores);
     c10::cuda::CUDAGuard guard(scores.device());
     Tensor len = resolve_lengths(lengths, s, scores.device());
     Tensor G = grad_alignment.contiguous();
@@ -737,13 +753,78 @@ TORCH_LIBRARY_IMPL(d2p, CPU, m) {
     for (const char* name : kOps) m.impl(name, torch::CppFunction::makeFromBoxedFunction<&reject_cpu>());
 }
 
+// The autograd kernels.  Fake tensors (FakeTensorMode, meta tracing) carry
+// the Python dispatch key and no storage: they are handed on below autograd,
+// where the registered fake kernel describes the outputs (no autograd graph is
+// recorded for them; torch.compile traces the d2p_py:: custom ops, which carry
+// their own autograd formulas).  Real tensors run the autograd Functions.
+bool is_python_tensor(const Tensor& t) { return t.defined() && t.key_set().has(c10::DispatchKey::Python); }
+
+template <class Sig>
+c10::TypedOperatorHandle<Sig> op_handle(const char* name) {
+    return c10::Dispatcher::singleton().findSchemaOrThrow(name, "").typed<Sig>();
+}
+
+// the C++ signatures the kernels were registered with (arguments by value)
+using ForwardT = std::vector<Tensor>(Tensor, Tensor, Tensor, Tensor);
+using ForwardF = std::vector<Tensor>(Tensor, double, double, c10::optional<Tensor>);
+using AffForwardT = std::vector<Tensor>(Tensor, Tensor, Tensor, Tensor, Tensor);
+using AffForwardF = std::vector<Tensor>(Tensor, double, double, double, c10::optional<Tensor>);
+
+template <const char* Name>
+std::vector<Tensor> fwd_t_autograd(Tensor scores, Tensor gap, Tensor temperature, Tensor lengths) {
+    if (is_python_tensor(scores)) {
+        static auto op = op_handle<ForwardT>(Name);
+        at::AutoDispatchBelowADInplaceOrView below;
+        return op.call(scores, gap, temperature, lengths);
+    }
+    return soft_sw_cuda(scores, gap, temperature, lengths);
+}
+template <const char* Name>
+std::vector<Tensor> fwd_f_autograd(Tensor scores, double gap, double temperature, c10::optional<Tensor> lengths) {
+    if (is_python_tensor(scores)) {
+        static auto op = op_handle<ForwardF>(Name);
+        at::AutoDispatchBelowADInplaceOrView below;
+        return op.call(scores, gap, temperature, lengths);
+    }
+    return soft_sw_float_cuda(scores, gap, temperature, lengths);
+}
+template <const char* Name>
+std::vector<Tensor> aff_fwd_t_autograd(Tensor scores, Tensor go, Tensor ge, Tensor temperature, Tensor lengths) {
+    if (is_python_tensor(scores)) {
+        static auto op = op_handle<AffForwardT>(Name);
+        at::AutoDispatchBelowADInplaceOrView below;
+        return op.call(scores, go, ge, temperature, lengths);
+    }
+    return soft_sw_affine_cuda(scores, go, ge, temperature, lengths);
+}
+template <const char* Name>
+std::vector<Tensor> aff_fwd_f_autograd(Tensor scores, double go, double ge, double temperature,
+                                       c10::optional<Tensor> lengths) {
+    if (is_python_tensor(scores)) {
+        static auto op = op_handle<AffForwardF>(Name);
+        at::AutoDispatchBelowADInplaceOrView below;
+        return op.call(scores, go, ge, temperature, lengths);
+    }
+    return soft_sw_affine_float_cuda(scores, go, ge, temperature, lengths);
+}
+
+constexpr char kSoftSW[] = "d2p::soft_sw";
+constexpr char kSoftSWFloat[] = "d2p::soft_sw_float";
+constexpr char kSWForward[] = "d2p::sw_forward";
+constexpr char kSWForwardT[] = "d2p::sw_forward_t";
+constexpr char kSoftSWAffine[] = "d2p::soft_sw_affine";
+constexpr char kSoftSWAffineFloat[] = "d2p::soft_sw_affine_float";
+constexpr char kSWAffineForward[] = "d2p::sw_affine_forward";
+constexpr char kSWAffineForwardT[] = "d2p::sw_affine_forward_t";
+
 TORCH_LIBRARY_IMPL(d2p, AutogradCUDA, m) {
-    m.impl("soft_sw", soft_sw_cuda);
-    m.impl("soft_sw_float", soft_sw_float_cuda);
-    m.impl("sw_forward", sw_forward_cuda);
-    m.impl("sw_forward_t", sw_forward_t_cuda);
-    m.impl("soft_sw_affine", soft_sw_affine_cuda);
-    m.impl("soft_sw_affine_float", soft_sw_affine_float_cuda);
-    m.impl("sw_affine_forward", sw_affine_forward_cuda);
-    m.impl("sw_affine_forward_t", sw_affine_forward_t_cuda);
+    m.impl("soft_sw", fwd_t_autograd<kSoftSW>);
+    m.impl("soft_sw_float", fwd_f_autograd<kSoftSWFloat>);
+    m.impl("sw_forward", fwd_f_autograd<kSWForward>);
+    m.impl("sw_forward_t", fwd_t_autograd<kSWForwardT>);
+    m.impl("soft_sw_affine", aff_fwd_t_autograd<kSoftSWAffine>);
+    m.impl("soft_sw_affine_float", aff_fwd_f_autograd<kSoftSWAffineFloat>);
+    m.impl("sw_affine_forward", aff_fwd_f_autograd<kSWAffineForward>);
+    m.impl("sw_affine_forward_t", aff_fwd_t_autograd<kSWAffineForwardT>);
 }

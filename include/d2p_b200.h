@@ -197,6 +197,16 @@ D2P_API int d2p_sw_affine_backward_full(const float* scores, const float* grad_m
  * context stays usable.  No counterpart in the reference. */
 D2P_API int d2p_wait_selftest(int scope, const int* word, int* status, void* stream);
 
+/* Diagnostic: MUFU (ex2.approx) throughput probe, for the transcendental
+ * roofline.  Launches `blocks` CTAs of D2P_MUFU_PROBE_THREADS threads on
+ * `stream`; each thread runs D2P_MUFU_PROBE_CHAINS independent ex2 chains of
+ * `iters` steps and writes one float to out[blocks * D2P_MUFU_PROBE_THREADS]
+ * (device).  ex2 operations per launch = blocks * threads * chains * iters; the
+ * caller times the launch.  No counterpart in the reference. */
+#define D2P_MUFU_PROBE_THREADS 512
+#define D2P_MUFU_PROBE_CHAINS 8
+D2P_API int d2p_mufu_probe(float* out, int blocks, int iters, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

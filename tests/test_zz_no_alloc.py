@@ -47,19 +47,22 @@ def test_rejects_sizes_beyond_static_scratch(lib):
     assert rc == 1002  # D2P_ERR_WORKSPACE_TOO_SMALL
 
 
-def _run(lib, fn_static, s, ln, gap, T):
+def _run(lib, fn_static, s, ln, gap, T, grads=True):
+    """One call; without `grads` no dS/dgap, dS/dT pointers are passed, which
+    sends the call through the value + marginals kernel instead of the
+    gradient sweep."""
     import torch
 
     B, L1, L2 = s.shape
     dev = s.device
     v = torch.empty(B, device=dev)
     m = torch.empty(B, L1, L2, device=dev)
-    gg = torch.empty(B, device=dev)
-    gt = torch.empty(B, device=dev)
+    gg = torch.zeros(B, device=dev)
+    gt = torch.zeros(B, device=dev)
     st = torch.cuda.current_stream().cuda_stream
     lp = P(ln.data_ptr()) if ln is not None else None
     args = [P(s.data_ptr()), lp, B, L1, L2, gap, T, None, None, P(v.data_ptr()), P(m.data_ptr()),
-            P(gg.data_ptr()), P(gt.data_ptr())]
+            P(gg.data_ptr()) if grads else None, P(gt.data_ptr()) if grads else None]
     if fn_static:
         rc = lib.d2p_sw_forward_backward_static(*args, P(st))
     else:
@@ -85,16 +88,23 @@ def _case(B, L1, L2, seed, ragged, device):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("B,L1,L2,ragged", [(8, 96, 128, False), (5, 70, 66, True), (3, 40, 37, True)])
-def test_static_matches_workspace_entry_point(lib, cuda_device, B, L1, L2, ragged):
+@pytest.mark.parametrize("B,L1,L2,ragged,grads", [
+    (8, 96, 128, False, True), (5, 70, 66, True, True), (3, 40, 37, True, True),
+    # value + marginals only: the linear-domain kernel runs in the scratch
+    (8, 96, 128, False, False), (5, 70, 64, True, False),
+    # few large problems: each is spread over several CTAs, whose progress
+    # words and partition partials also live in the scratch (cleared per call)
+    (2, 1024, 1024, False, False),
+])
+def test_static_matches_workspace_entry_point(lib, cuda_device, B, L1, L2, ragged, grads):
     import torch
 
     assert lib.d2p_sw_workspace_bytes(0, 0, B, L1, L2) <= STATIC_BYTES
     for call in range(2):  # two calls in a row, different inputs
         s, ln = _case(B, L1, L2, seed=1000 * call + L1 + L2, ragged=ragged, device=cuda_device)
         gap, T = -0.5 - 0.25 * call, 1.0 - 0.3 * call
-        got = _run(lib, True, s, ln, gap, T)
-        ref = _run(lib, False, s, ln, gap, T)
+        got = _run(lib, True, s, ln, gap, T, grads)
+        ref = _run(lib, False, s, ln, gap, T, grads)
         for name, a, b in zip(("value", "marginals", "grad_gap", "grad_T"), got, ref):
             assert torch.isfinite(a).all(), name
             np.testing.assert_allclose(a.numpy(), b.numpy(), rtol=RTOL, atol=ATOL, err_msg=f"call {call}: {name}")
