@@ -67,10 +67,12 @@ static size_t op_bytes(int family, int op, int B, int L1, int L2) {
                                                           : aff_fast_workspace_bytes(B, L1, L2, true);
             if (wf == 0) return pe;
             const size_t lf = family == D2P_FAMILY_LINEAR ? lin_fast_workspace_bytes(B, L1, L2) : 0;
+            const size_t sf = family == D2P_FAMILY_LINEAR ? lin_strip_workspace_bytes(B, L1, L2) : 0;
             const size_t tf = family == D2P_FAMILY_LINEAR ? lin_tan_workspace_bytes(B, L1, L2)
                                                           : aff_tan_workspace_bytes(B, L1, L2, true);
             pe = pe > wf ? pe : wf;
             pe = pe > lf ? pe : lf;
+            pe = pe > sf ? pe : sf;
             pe = pe > tf ? pe : tf;
             if (family == D2P_FAMILY_AFFINE && tf > 0) {
                 // bf16 scores with parameter gradients: the tangent kernel's
@@ -161,6 +163,7 @@ int d2p_sw_forward_backward(const float* scores, const int* lengths, int B, int 
     size_t pe = plane_bytes(D2P_FAMILY_LINEAR, MODE_MARG, B, L1, L2);
     const size_t wf = wavefront_workspace_bytes(D2P_FAMILY_LINEAR, B, L1, L2);
     const size_t lf = lin_fast_workspace_bytes(B, L1, L2);
+    const size_t sf = lin_strip_workspace_bytes(B, L1, L2);
     const size_t tf = lin_tan_workspace_bytes(B, L1, L2);
     if (wf > 0) {
         // Fast paths, each recomputing what the previous one flagged:
@@ -170,6 +173,7 @@ int d2p_sw_forward_backward(const float* scores, const int* lengths, int B, int 
         //   otherwise log-domain wavefront kernel -> plane engine.
         pe = pe > wf ? pe : wf;
         pe = pe > lf ? pe : lf;
+        pe = pe > sf ? pe : sf;
         pe = pe > tf ? pe : tf;
         int* flags = (int*)((char*)workspace + align256(pe));
         int* order = (int*)((char*)flags + align256((size_t)B * sizeof(int)));
@@ -182,8 +186,15 @@ int d2p_sw_forward_backward(const float* scores, const int* lengths, int B, int 
             if (ro == D2P_OK) a.order = order;
             else if (ro != kNotHandled) return ro;
         }
-        int rc = (grad_gap || grad_temperature) ? launch_lin_tan(a, workspace_bytes, st)
-                                                : launch_lin_fast(a, workspace_bytes, st);
+        int rc;
+        if (grad_gap || grad_temperature) {
+            rc = launch_lin_tan(a, workspace_bytes, st);
+        } else {
+            // problems of at most 512 rows: the column-sweep strip kernel;
+            // others: the anti-diagonal row-block pipeline
+            rc = launch_lin_strip(a, workspace_bytes, st);
+            if (rc == kNotHandled) rc = launch_lin_fast(a, workspace_bytes, st);
+        }
         a.order = nullptr;
         a.sync = nullptr;
         if (rc == D2P_OK) {

@@ -120,6 +120,11 @@ size_t lin_fast_workspace_bytes(int B, int L1, int L2);
 // kernels with 12 warps per problem rather than 6 (shape L1 x L2)
 bool lin_wide_pays(int L1, int L2);
 int launch_lin_fast(const SwArgs& a, size_t ws_bytes, cudaStream_t st);
+// column-sweep strip kernel (sw_strip.cu): value + marginals without parameter
+// gradients for problems of at most 512 rows (L1 % 16 == 0, L2 % 4 == 0);
+// returns -1 when the shape or arguments are not covered
+size_t lin_strip_workspace_bytes(int B, int L1, int L2);
+int launch_lin_strip(const SwArgs& a, size_t ws_bytes, cudaStream_t st);
 // affine-gap linear-domain fast path (sw_affine_fast.cu): value + marginals
 // without parameter gradients, fp32 or bf16 scores (bf16 widened into the
 // workspace first); returns -1 when the shape or arguments are not covered

@@ -564,3 +564,65 @@ def test_value_backward_runs_no_tangent_sweep(d2p, cuda_device, B, L1, L2):
     assert not tangent(names), tangent(names)
     names = _kernel_names(zero_marginal_grad)
     assert tangent(names), names
+
+
+# Shapes the column-sweep strip kernel takes (at most 512 rows, L1 % 16 == 0,
+# L2 % 4 == 0): one strip per lane partly or wholly past the problem, column
+# blocks and tiles cut by L2, ragged lengths (rows masked inside a strip).
+STRIP = [  # (B, L1, L2, T, gap, ragged)
+    (2, 16, 4, 1.0, -1.0, False), (3, 32, 20, 0.5, -1.0, False), (2, 48, 12, 1.0, -0.5, False),
+    (4, 64, 100, 2.0, -1.0, False), (2, 256, 1024, 1.0, -1.0, False), (2, 496, 64, 1.0, -1.0, False),
+    (3, 512, 36, 0.7, -1.3, False), (2, 512, 512, 1.0, -1.0, False), (1, 512, 2000, 1.0, -1.0, False),
+    (6, 512, 96, 1.0, -0.5, True), (5, 96, 128, 0.5, -1.0, True), (4, 512, 512, 0.5, -0.5, True),
+]
+
+
+@pytest.mark.parametrize("B,L1,L2,T,gap,ragged", STRIP)
+def test_strip_kernel(d2p, cuda_device, B, L1, L2, T, gap, ragged):
+    """The strip kernel against the oracle, padding exactly zero, and the result
+    its own: the plane engine's (the fix-up of flagged problems) differs in the
+    last bits."""
+    s = scores(B, L1, L2, seed=L1 * 31 + L2 + B)
+    ln = lengths_for(B, L1, L2, seed=L1 + L2, lo=1) if ragged else None
+    if ln is not None:
+        ln[0] = torch.tensor([L1, L2], dtype=torch.int32)
+        ln[-1] = torch.tensor([1, max(1, L2 // 3)], dtype=torch.int32)
+    lnd = None if ln is None else ln.to(cuda_device)
+    v, m = torch.ops.d2p.soft_sw_float(s.to(cuda_device), gap, T, lnd)
+    lnp = None if ln is None else ln.numpy()
+    r64 = oracle.sw_linear(s.numpy(), lnp, gap, T, "f64")
+    r32 = oracle.sw_linear(s.numpy(), lnp, gap, T, "f32")
+    check("value", v, r64["value"], r32["value"])
+    check("marginals", m, r64["marginals"], r32["marginals"])
+    if ln is not None:
+        mc = m.cpu()
+        for b, (l1, l2) in enumerate(ln.tolist()):
+            assert torch.count_nonzero(mc[b, l1:, :]) == 0 and torch.count_nonzero(mc[b, :, l2:]) == 0
+    if ln is None:
+        _, mp = plane_engine(torch.ops.d2p.soft_sw_float, s.to(cuda_device), gap, T)
+        for b in range(B):
+            assert not torch.equal(m[b], mp[b]), f"problem {b} was recomputed by the plane engine"
+    v2, m2 = torch.ops.d2p.soft_sw_float(s.to(cuda_device), gap, T, lnd)
+    assert torch.equal(v, v2) and torch.equal(m, m2)
+
+
+def test_strip_kernel_runs(d2p, cuda_device):
+    """A 512-row batch runs the strip kernel (no anti-diagonal kernel) and its
+    flagged-problem fix-up."""
+    s = scores(3, 512, 64, seed=77).to(cuda_device)
+    torch.ops.d2p.soft_sw_float(s, -1.0, 1.0, None)
+    names = _kernel_names(lambda: torch.ops.d2p.soft_sw_float(s, -1.0, 1.0, None))
+    assert any("lin_strip_kernel" in n for n in names), names
+    assert not any("lin_fast_kernel" in n for n in names), names
+
+
+def test_strip_kernel_low_temperature(d2p, cuda_device):
+    """T = 0.1: frame steps beyond the window flag the problems; the plane
+    engine's result stands (the reference's precision)."""
+    B, L1, L2, T = 2, 96, 96, 0.1
+    s = scores(B, L1, L2, seed=5)
+    v, m = torch.ops.d2p.soft_sw_float(s.to(cuda_device), -1.0, T, None)
+    r64 = oracle.sw_linear(s.numpy(), None, -1.0, T, "f64")
+    r32 = oracle.sw_linear(s.numpy(), None, -1.0, T, "f32")
+    check("value", v, r64["value"], r32["value"])
+    check("marginals", m, r64["marginals"], r32["marginals"])
