@@ -157,11 +157,17 @@ __device__ __forceinline__ void tma_load_tile(const CUtensorMap* tm, float* dst,
         : "memory");
 }
 
+// Marginal tiles are written once and not read again in the launch: evict
+// them from L2 first, so that the scores and kept values read a second time
+// stay.
 __device__ __forceinline__ void tma_store_tile(const CUtensorMap* tm, const float* src, int x, int y, int b) {
-    asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.tile.bulk_group [%0, {%1, %2, %3, %4}], [%5];" ::"l"(
-                     (unsigned long long)tm),
-                 "r"(x), "r"(y), "r"(0), "r"(b), "r"(smem_u32(src))
-                 : "memory");
+    unsigned long long pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    asm volatile(
+        "cp.async.bulk.tensor.4d.global.shared::cta.tile.bulk_group.L2::cache_hint [%0, {%1, %2, %3, %4}], [%5], "
+        "%6;" ::"l"((unsigned long long)tm),
+        "r"(x), "r"(y), "r"(0), "r"(b), "r"(smem_u32(src)), "l"(pol)
+        : "memory");
     asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
 // n bytes (a multiple of 16) from global src to shared dst (both 16-byte aligned), arriving on bar
