@@ -15,6 +15,7 @@ from . import _pt2_ops  # the d2p_py:: custom ops torch.compile traces
 _ops._pt2_mod = _pt2_ops
 from .sw import SoftSW, SoftSWAffine, SWResult, soft_sw, soft_sw_affine
 from . import ops
+from .engine import engine_counts, set_engine, use_engine
 
 # legacy flat aliases (d2p/__init__.py, soft Smith-Waterman lines)
 soft_sw_float = _ops.soft_sw_float
@@ -34,5 +35,5 @@ __all__ = [
     "soft_sw", "soft_sw_affine", "SWResult", "SoftSW", "SoftSWAffine", "ops",
     "soft_sw_float", "soft_sw_with_grads", "soft_sw_hvp", "soft_sw_param_jacobian", "soft_sw_backward_full",
     "soft_sw_affine_float", "soft_sw_affine_with_grads", "soft_sw_affine_hvp", "soft_sw_affine_param_jacobian",
-    "soft_sw_affine_backward_full",
+    "soft_sw_affine_backward_full", "engine_counts", "set_engine", "use_engine",
 ]

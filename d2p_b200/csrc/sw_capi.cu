@@ -11,6 +11,8 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <atomic>
+
 #include "../../include/d2p_b200.h"
 #include "sw_internal.h"
 
@@ -24,13 +26,21 @@ constexpr int kNotHandled = -1;
 
 static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
-bool engine_forced_plane() {
-    static const bool v = [] {  // read once (thread-safe static initialisation)
-        const char* e = getenv("D2P_B200_ENGINE");
-        return e && strcmp(e, "plane") == 0;
-    }();
-    return v;
+// Engine selection: 0 automatic, 1 the plane engine for every operator, 2 the
+// row-block pipeline for linear value + marginals.  Starts from
+// D2P_B200_ENGINE ("plane", "pipeline"); d2p_set_engine changes it.
+static std::atomic<int> g_engine{-1};
+static int engine_mode() {
+    const int v = g_engine.load(std::memory_order_acquire);
+    if (v >= 0) return v;
+    const char* e = getenv("D2P_B200_ENGINE");
+    const int m = e && strcmp(e, "plane") == 0 ? 1 : e && strcmp(e, "pipeline") == 0 ? 2 : 0;
+    int unset = -1;
+    g_engine.compare_exchange_strong(unset, m, std::memory_order_acq_rel);
+    return g_engine.load(std::memory_order_acquire);
 }
+bool engine_forced_plane() { return engine_mode() == 1; }
+bool engine_forced_pipeline() { return engine_mode() == 2; }
 
 static bool dims_ok(int B, int L1, int L2) {
     if (B < 0 || L1 < 0 || L2 < 0) return false;
@@ -60,16 +70,16 @@ static size_t tan_area(int family, int op, int B, int L1, int L2) {
 static size_t op_bytes(int family, int op, int B, int L1, int L2) {
     switch (op) {
         case D2P_OP_FORWARD_BACKWARD: {
-            // the fast path's workspace, or the plane engine's (which also serves as
-            // the fix-up for problems the fast path flags), then one flag per problem
+            // the fast kernels' workspace, or the plane engine's (which also serves as
+            // the fix-up for problems the fast kernels flag), then one flag per problem
             size_t pe = plane_bytes(family, MODE_MARG, B, L1, L2);
             const size_t wf = family == D2P_FAMILY_LINEAR ? wavefront_workspace_bytes(family, B, L1, L2)
                                                           : aff_fast_workspace_bytes(B, L1, L2, true);
-            if (wf == 0) return pe;
             const size_t lf = family == D2P_FAMILY_LINEAR ? lin_fast_workspace_bytes(B, L1, L2) : 0;
             const size_t sf = family == D2P_FAMILY_LINEAR ? lin_strip_workspace_bytes(B, L1, L2) : 0;
             const size_t tf = family == D2P_FAMILY_LINEAR ? lin_tan_workspace_bytes(B, L1, L2)
                                                           : aff_tan_workspace_bytes(B, L1, L2, true);
+            if (wf == 0 && lf == 0 && sf == 0 && tf == 0) return pe;
             pe = pe > wf ? pe : wf;
             pe = pe > lf ? pe : lf;
             pe = pe > sf ? pe : sf;
@@ -80,9 +90,9 @@ static size_t op_bytes(int family, int op, int B, int L1, int L2) {
                 const size_t tw = align256(tf) + align256((size_t)B * L1 * L2 * sizeof(float));
                 pe = pe > tw ? pe : tw;
             }
-            // flags, the CTA order of ragged batches, the cross-CTA words of
-            // problems spread over several CTAs
-            return align256(pe) + 2 * align256((size_t)(B > 0 ? B : 1) * sizeof(int)) +
+            // flags, the CTA order of ragged batches, the log-domain fix-up's
+            // flags, the cross-CTA words of problems spread over several CTAs
+            return align256(pe) + 3 * align256((size_t)(B > 0 ? B : 1) * sizeof(int)) +
                    align256((size_t)(B > 0 ? B : 1) * kSyncBytes);
         }
         case D2P_OP_HVP:
@@ -117,6 +127,24 @@ using namespace d2pb;
 extern "C" {
 
 int d2p_version(void) { return 100; }
+
+int d2p_set_engine(int engine, int* previous) {
+    if (engine < D2P_ENGINE_AUTO || engine > D2P_ENGINE_PIPELINE) return D2P_ERR_INVALID_ARGUMENT;
+    const int prev = engine_mode();
+    g_engine.store(engine, std::memory_order_release);
+    if (previous) *previous = prev;
+    return D2P_OK;
+}
+
+int d2p_engine_counts(unsigned long long* counts, int n) {
+    if (!counts || n < 0 || n > 3) return D2P_ERR_INVALID_ARGUMENT;
+    unsigned long long c[3] = {0, 0, 0};
+    int rc = wavefront_fixup_count(&c[0]);
+    if (rc == D2P_OK) rc = plane_problem_counts(&c[1]);
+    if (rc != D2P_OK) return rc;
+    for (int i = 0; i < n; ++i) counts[i] = c[i];
+    return D2P_OK;
+}
 
 const char* d2p_error_string(int code) {
     switch (code) {
@@ -165,42 +193,55 @@ int d2p_sw_forward_backward(const float* scores, const int* lengths, int B, int 
     const size_t lf = lin_fast_workspace_bytes(B, L1, L2);
     const size_t sf = lin_strip_workspace_bytes(B, L1, L2);
     const size_t tf = lin_tan_workspace_bytes(B, L1, L2);
-    if (wf > 0) {
-        // Fast paths, each recomputing what the previous one flagged:
-        //   linear-domain kernel (value + marginals: sw_linear.cu; with
-        //   parameter gradients: the tangent kernel's gap sweep, sw_tangent.cu,
-        //   for batches of one wave) -> plane engine;
-        //   otherwise log-domain wavefront kernel -> plane engine.
+    if (wf > 0 || lf > 0 || sf > 0 || tf > 0) {
+        // Fast kernels, each later one recomputing what the earlier flagged:
+        //   value + marginals: the column-sweep strip kernel (at most 512
+        //   rows) or the anti-diagonal row-block pipeline (sw_linear.cu) ->
+        //   the normalised log-domain kernel (sw_wavefront.cu) -> plane engine;
+        //   with parameter gradients: the tangent kernel's gap sweep
+        //   (sw_tangent.cu) -> plane engine;
+        //   shapes no linear-domain kernel covers: log-domain -> plane engine.
         pe = pe > wf ? pe : wf;
         pe = pe > lf ? pe : lf;
         pe = pe > sf ? pe : sf;
         pe = pe > tf ? pe : tf;
+        const size_t fb = align256((size_t)B * sizeof(int));
         int* flags = (int*)((char*)workspace + align256(pe));
-        int* order = (int*)((char*)flags + align256((size_t)B * sizeof(int)));
+        int* order = (int*)((char*)flags + fb);
+        int* flags2 = (int*)((char*)order + fb);
         a.redo = flags;
         a.only = nullptr;
         a.order = nullptr;
-        a.sync = (int*)((char*)order + align256((size_t)B * sizeof(int)));
-        if (lengths && !grad_gap && !grad_temperature) {
+        a.sync = (int*)((char*)flags2 + fb);
+        const bool pgrad = grad_gap || grad_temperature;
+        if (lengths && !pgrad) {
             const int ro = launch_lin_order(lengths, B, L1, L2, order, st);
             if (ro == D2P_OK) a.order = order;
             else if (ro != kNotHandled) return ro;
         }
         int rc;
-        if (grad_gap || grad_temperature) {
+        if (pgrad) {
             rc = launch_lin_tan(a, workspace_bytes, st);
         } else {
-            // problems of at most 512 rows: the column-sweep strip kernel;
-            // others: the anti-diagonal row-block pipeline
             rc = launch_lin_strip(a, workspace_bytes, st);
             if (rc == kNotHandled) rc = launch_lin_fast(a, workspace_bytes, st);
         }
         a.order = nullptr;
         a.sync = nullptr;
+        if (rc == D2P_OK && !pgrad) {
+            // flagged problems (low temperatures, extreme scores): the log-domain
+            // kernel, then the plane engine (the reference's score-unit
+            // arithmetic) for any it flags in turn
+            SwArgs w = a;
+            w.only = flags;
+            w.redo = flags2;
+            const int rw = launch_wavefront(w, D2P_FAMILY_LINEAR, workspace_bytes, st);
+            if (rw != D2P_OK && rw != kNotHandled) return rw;
+            a.only = rw == D2P_OK ? flags2 : flags;
+            a.redo = nullptr;
+            return launch_lin_plane(a, st);
+        }
         if (rc == D2P_OK) {
-            // flagged problems (low temperatures, extreme scores) go to the plane
-            // engine, whose value + marginals mode follows the reference's
-            // score-unit arithmetic
             a.only = flags;
             a.redo = nullptr;
             return launch_lin_plane(a, st);

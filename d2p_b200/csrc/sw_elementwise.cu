@@ -107,6 +107,41 @@ __global__ void sum_batches_kernel(const float* __restrict__ partials, int P, in
     }
 }
 
+// Row repacking for kernels that move rows by TMA (16-byte row strides): one
+// warp per row, 4-byte coalesced loads and stores.  pad: in [B][L1][L2] ->
+// out [B][L1p][L2p] with zeros in the added rows and columns; unpad: the
+// [L1][L2] corner of each padded problem back to [B][L1][L2].
+__global__ void __launch_bounds__(256) pad_rows_kernel(const float* __restrict__ in, int L1, int L2,
+                                                       float* __restrict__ out, int L1p, int L2p,
+                                                       long long rows) {
+    const int lane = threadIdx.x & 31;
+    const long long w0 = (long long)blockIdx.x * 8 + (threadIdx.x >> 5), ws = (long long)gridDim.x * 8;
+    for (long long r = w0; r < rows; r += ws) {
+        const long long b = r / L1p;
+        const int i = (int)(r - b * L1p);
+        float* __restrict__ o = out + r * L2p;
+        const float* __restrict__ s = in + (b * L1 + i) * (long long)L2;
+        const int n = i < L1 ? L2 : 0;
+#pragma unroll 4
+        for (int j = lane; j < L2p; j += 32) o[j] = j < n ? __ldg(s + j) : 0.f;
+    }
+}
+
+__global__ void __launch_bounds__(256) unpad_rows_kernel(const float* __restrict__ in, int L1p, int L2p,
+                                                         float* __restrict__ out, int L1, int L2,
+                                                         long long rows) {
+    const int lane = threadIdx.x & 31;
+    const long long w0 = (long long)blockIdx.x * 8 + (threadIdx.x >> 5), ws = (long long)gridDim.x * 8;
+    for (long long r = w0; r < rows; r += ws) {
+        const long long b = r / L1;
+        const int i = (int)(r - b * L1);
+        const float* __restrict__ s = in + (b * L1p + i) * (long long)L2p;
+        float* __restrict__ o = out + r * L2;
+#pragma unroll 4
+        for (int j = lane; j < L2; j += 32) __stcs(o + j, __ldcs(s + j));
+    }
+}
+
 static int grid_for(size_t work_items) {
     int dev = 0, sms = 148;
     if (cudaGetDevice(&dev) == cudaSuccess) {
@@ -141,6 +176,20 @@ int launch_value_backward(const float* grad_value, const float* marginals, const
     const int grid = grid_for(total / 4 + 1);
     value_backward_kernel<<<grid, 256, 0, st>>>(grad_value, marginals, dparams, n_params, B,
                                                 plane > 0 ? plane : 1, grad_scores, grad_params);
+    return (int)cudaGetLastError();
+}
+
+int launch_pad_rows(const float* in, int B, int L1, int L2, float* out, int L1p, int L2p, cudaStream_t st) {
+    const long long rows = (long long)B * L1p;
+    if (rows == 0 || L2p == 0) return 0;
+    pad_rows_kernel<<<grid_for((size_t)rows * 32), 256, 0, st>>>(in, L1, L2, out, L1p, L2p, rows);
+    return (int)cudaGetLastError();
+}
+
+int launch_unpad_rows(const float* in, int L1p, int L2p, float* out, int B, int L1, int L2, cudaStream_t st) {
+    const long long rows = (long long)B * L1;
+    if (rows == 0 || L2 == 0) return 0;
+    unpad_rows_kernel<<<grid_for((size_t)rows * 32), 256, 0, st>>>(in, L1p, L2p, out, L1, L2, rows);
     return (int)cudaGetLastError();
 }
 

@@ -137,10 +137,18 @@ int launch_bf16_widen(const __nv_bfloat16* in, float* out, size_t n, cudaStream_
 int launch_lin_order(const int* lengths, int B, int L1, int L2, int* order, cudaStream_t st);
 
 int launch_lin_plane(const SwArgs& a, cudaStream_t st);
+// engine counters of the current device (cumulative, read synchronously):
+// problems the plane engine computed [linear, affine], and problems the
+// log-domain kernel recomputed after a linear-domain kernel flagged them
+int plane_problem_counts(unsigned long long* n2);
+int wavefront_fixup_count(unsigned long long* n);
 
-// D2P_B200_ENGINE=plane selects the general plane engine for every operator
-// (both engines compute the same results; used to cross-check them in tests).
+// D2P_B200_ENGINE=plane selects the general plane engine for every operator,
+// D2P_B200_ENGINE=pipeline the anti-diagonal row-block pipeline
+// (lin_fast_kernel) for linear value + marginals at every size (the engines
+// compute the same results; used to cross-check and time them).
 bool engine_forced_plane();
+bool engine_forced_pipeline();
 
 // linear-domain tangent sweeps (sw_tangent.cu): HVP, dP/dgap, dP/dT, and the
 // dot mode (dot_with / dot_out) of the param modes; sets redo[b] for problems
@@ -170,5 +178,8 @@ int launch_value_backward_rows(const float* grad_value, const float* marginals, 
                                float* grad_scores, float* grad_params, cudaStream_t st);
 int launch_sum_batches(const float* partials, int P, int B, float* out, int accumulate,
                        cudaStream_t st);
+// [B][L1][L2] <-> [B][L1p][L2p] (L1p >= L1, L2p >= L2; zeros in the padding)
+int launch_pad_rows(const float* in, int B, int L1, int L2, float* out, int L1p, int L2p, cudaStream_t st);
+int launch_unpad_rows(const float* in, int L1p, int L2p, float* out, int B, int L1, int L2, cudaStream_t st);
 
 }  // namespace d2pb

@@ -19,7 +19,8 @@
 // Values from the row-block above or below come with their own frames.  If a
 // frame step leaves [2^-60, 2^60] (score magnitudes far beyond the usual ones,
 // or a temperature far below 1), the problem is flagged and the caller
-// recomputes it with the log-domain kernel (sw_wavefront.cu).
+// recomputes it with the log-domain kernel (sw_wavefront.cu), and what that
+// flags in turn with the plane engine (sw_plane.cu).
 //
 // Dependency chain.  A lane's new value depends on its neighbour's value of
 // the previous step through a warp shuffle and ONE fused multiply-add: the

@@ -45,6 +45,14 @@ namespace d2pb {
 
 constexpr int kPlaneThreads = 512;
 
+// problems this engine computed, linear and affine (cumulative on the device;
+// d2p_engine_counts reads them)
+__device__ unsigned long long g_plane_problems[2];
+
+int plane_problem_counts(unsigned long long* n2) {
+    return (int)cudaMemcpyFromSymbol(n2, g_plane_problems, 2 * sizeof(unsigned long long));
+}
+
 // --------------------------------------------------------------------------
 // helpers
 // --------------------------------------------------------------------------
@@ -187,6 +195,7 @@ __global__ void __launch_bounds__(kPlaneThreads) lin_plane_kernel(SwArgs p) {
 
     const int b = blockIdx.x;
     if (p.only && p.only[b] == 0) return;  // fix-up launch: only problems a fast path flagged
+    if (threadIdx.x == 0) atomicAdd(&g_plane_problems[0], 1ull);
     const int L1m = p.L1, L2m = p.L2;
     // lengths are validated by the caller; clamp so a bad value can never index
     // outside the padded problem
@@ -495,6 +504,7 @@ __global__ void __launch_bounds__(kPlaneThreads) aff_plane_kernel(SwArgs p) {
 
     const int b = blockIdx.x;
     if (p.only && p.only[b] == 0) return;  // fix-up launch: only problems a fast path flagged
+    if (threadIdx.x == 0) atomicAdd(&g_plane_problems[1], 1ull);
     const int L1m = p.L1, L2m = p.L2;
     const int L1 = p.lengths ? min(max(p.lengths[2 * b], 0), L1m) : L1m;
     const int L2 = p.lengths ? min(max(p.lengths[2 * b + 1], 0), L2m) : L2m;

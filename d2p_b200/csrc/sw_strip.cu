@@ -200,7 +200,8 @@ __device__ __forceinline__ bool bar_wait(unsigned long long* bar, unsigned parit
 
 struct Args {
     const int* lengths;
-    int B, L1, L2;
+    int B, L1, L2;      // the planes' layout (rows of whole 16-byte units)
+    int L1v, L2v;       // the problems' padded shape inside it (lengths are clamped to it)
     float gap, temp;
     const float* gap_dev;
     const float* temp_dev;
@@ -224,8 +225,8 @@ __device__ __forceinline__ void prob_init(const Args& A, int b, int w, int lane,
     p.gl = gapn * p.c;
     p.G = ex2f(p.gl);
     p.G2 = ex2f(2.f * p.gl);
-    p.L1 = A.lengths ? min(max(A.lengths[2 * b], 0), A.L1) : A.L1;
-    p.L2 = A.lengths ? min(max(A.lengths[2 * b + 1], 0), A.L2) : A.L2;
+    p.L1 = A.lengths ? min(max(A.lengths[2 * b], 0), A.L1v) : A.L1v;
+    p.L2 = A.lengths ? min(max(A.lengths[2 * b + 1], 0), A.L2v) : A.L2v;
     p.nv = min(max(p.L1 - kWR * w - kR * lane, 0), kR);
 }
 
@@ -836,8 +837,8 @@ __global__ void __launch_bounds__(64 * kMaxW, 2) lin_strip_kernel(const __grid_c
     const int w = fwd ? wid : wid - W;               // row block
     WarpSmem& WS = S.w[wid];                         // this warp's tiles (2W of them are allocated)
     const int b = A.order ? A.order[blockIdx.x] : (int)blockIdx.x;
-    const int L1 = A.lengths ? min(max(A.lengths[2 * b], 0), A.L1) : A.L1;
-    const int L2 = A.lengths ? min(max(A.lengths[2 * b + 1], 0), A.L2) : A.L2;
+    const int L1 = A.lengths ? min(max(A.lengths[2 * b], 0), A.L1v) : A.L1v;
+    const int L2 = A.lengths ? min(max(A.lengths[2 * b + 1], 0), A.L2v) : A.L2v;
     const int Wact = (L1 > 0 && L2 > 0) ? warps_for(L1) : 0;   // row blocks with rows of the problem
     if (lane == 0) {
         for (int i = 0; i < kNS; ++i)
@@ -945,26 +946,48 @@ bool strip_tensor_map(CUtensorMap* tm, const float* base, int B, int L1, int L2)
 }
 }  // namespace
 
-static bool strip_shape_ok(int L1, int L2) {
-    return L1 > 0 && L2 > 0 && L1 <= strip::kWR * strip::kMaxW && L1 % strip::kR == 0 && L2 % 4 == 0;
+// Any problem of at most 512 rows.  Planes whose rows are not whole 16-byte
+// units (L2 % 4 != 0), or whose row count is not a multiple of 4, cannot be
+// TMA tensors: they are copied into padded planes in the workspace, and the
+// marginals copied back (8 + 8 bytes per cell, at HBM rate).
+static bool strip_shape_ok(int L1, int L2) { return L1 > 0 && L2 > 0 && L1 <= strip::kWR * strip::kMaxW; }
+static int round4(int x) { return (x + 3) & ~3; }
+static size_t align256z(size_t x) { return (x + 255) & ~(size_t)255; }
+static bool strip_repack(int L1, int L2) { return L1 % strip::kR != 0 || L2 % 4 != 0; }
+// [kept planes][padded scores][padded marginals]
+static size_t strip_plane_area(int B, int L1, int L2) {
+    return align256z(strip::per_problem_bytes(round4(L1), round4(L2)) * (size_t)B);
+}
+static size_t strip_padded_bytes(int B, int L1, int L2) {
+    return align256z((size_t)B * round4(L1) * round4(L2) * sizeof(float));
 }
 
 size_t lin_strip_workspace_bytes(int B, int L1, int L2) {
     if (!strip_shape_ok(L1, L2)) return 0;
-    return strip::per_problem_bytes(L1, L2) * (size_t)B;
+    if (!strip_repack(L1, L2)) return strip::per_problem_bytes(L1, L2) * (size_t)B;
+    return strip_plane_area(B, L1, L2) + 2 * strip_padded_bytes(B, L1, L2);
 }
 
 int launch_lin_strip(const SwArgs& a, size_t ws_bytes, cudaStream_t st) {
     if (a.mode != MODE_MARG || !a.redo || a.grad_gap || a.grad_T || !a.out || !a.scores) return -1;
-    if (engine_forced_plane()) return -1;
+    if (engine_forced_plane() || engine_forced_pipeline()) return -1;
     if (!strip_shape_ok(a.L1, a.L2)) return -1;
-    if ((((uintptr_t)a.scores) & 15) != 0 || (((uintptr_t)a.out) & 15) != 0) return -1;
-    if ((((uintptr_t)a.ws) & 255) != 0) return -1;
-    const size_t per = strip::per_problem_bytes(a.L1, a.L2);
-    if (!a.ws || ws_bytes < per * (size_t)a.B) return -1;
-    CUtensorMap tmS, tmO;
-    if (!strip_tensor_map(&tmS, a.scores, a.B, a.L1, a.L2) || !strip_tensor_map(&tmO, a.out, a.B, a.L1, a.L2))
+    if ((((uintptr_t)a.ws) & 255) != 0 || !a.ws) return -1;
+    const bool repack = strip_repack(a.L1, a.L2);
+    const int L1p = round4(a.L1), L2p = round4(a.L2);
+    const size_t per = strip::per_problem_bytes(L1p, L2p);
+    if (ws_bytes < lin_strip_workspace_bytes(a.B, a.L1, a.L2)) return -1;
+    const float* sc = a.scores;
+    float* out = a.out;
+    if (repack) {
+        float* ps = (float*)((char*)a.ws + strip_plane_area(a.B, a.L1, a.L2));
+        sc = ps;
+        out = (float*)((char*)ps + strip_padded_bytes(a.B, a.L1, a.L2));
+    } else if ((((uintptr_t)a.scores) & 15) != 0 || (((uintptr_t)a.out) & 15) != 0) {
         return -1;
+    }
+    CUtensorMap tmS, tmO;
+    if (!strip_tensor_map(&tmS, sc, a.B, L1p, L2p) || !strip_tensor_map(&tmO, out, a.B, L1p, L2p)) return -1;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return (int)e;
@@ -978,8 +1001,10 @@ int launch_lin_strip(const SwArgs& a, size_t ws_bytes, cudaStream_t st) {
     strip::Args A;
     A.lengths = a.lengths;
     A.B = a.B;
-    A.L1 = a.L1;
-    A.L2 = a.L2;
+    A.L1 = L1p;
+    A.L2 = L2p;
+    A.L1v = a.L1;
+    A.L2v = a.L2;
     A.gap = a.gap;
     A.temp = a.temp;
     A.gap_dev = a.gap_dev;
@@ -989,9 +1014,15 @@ int launch_lin_strip(const SwArgs& a, size_t ws_bytes, cudaStream_t st) {
     A.redo = a.redo;
     A.order = a.order;
     A.ws_stride = per;
-    const int W = strip::warps_for(a.L1);
+    const int W = strip::warps_for(L1p);
+    if (repack) {
+        const int rc = launch_pad_rows(a.scores, a.B, a.L1, a.L2, const_cast<float*>(sc), L1p, L2p, st);
+        if (rc) return rc;
+    }
     strip::lin_strip_kernel<<<a.B, 64 * W, strip::smem_bytes_for(W), st>>>(tmS, tmO, A);
-    return (int)cudaGetLastError();
+    cudaError_t e2 = cudaGetLastError();
+    if (e2 != cudaSuccess || !repack) return (int)e2;
+    return launch_unpad_rows(out, L1p, L2p, a.out, a.B, a.L1, a.L2, st);
 }
 
 }  // namespace d2pb

@@ -431,6 +431,10 @@ __device__ __forceinline__ void rev_stage_part(const RevCtx& C, RevVars& V, int 
 // Progress: warp w publishes (ordinal << 16 | stages done) after every stage of
 // its current row-block (ordinal = r forward, nRB-1-r reverse), and
 // (ordinal << 16 | kStageMask) when the row-block is complete.
+// problems this kernel recomputed after a linear-domain kernel flagged them
+// (cumulative on the device; d2p_engine_counts reads it)
+__device__ unsigned long long g_fixups;
+
 __global__ void __launch_bounds__(kNW * 32) lin_marg_kernel(SwArgs p) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     WarpSmem& W = reinterpret_cast<WarpSmem*>(smem_raw)[threadIdx.x >> 5];
@@ -440,7 +444,13 @@ __global__ void __launch_bounds__(kNW * 32) lin_marg_kernel(SwArgs p) {
     __shared__ float sh_Sfrac;
 
     const int b = blockIdx.x;
-    if (p.only && p.only[b] == 0) return;  // fallback launch: only problems the fast path flagged
+    if (p.only) {   // fix-up launch: only the problems a linear-domain kernel flagged
+        if (p.only[b] == 0) {
+            if (p.redo && threadIdx.x == 0) p.redo[b] = 0;
+            return;
+        }
+        if (threadIdx.x == 0) atomicAdd(&g_fixups, 1ull);
+    }
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int L1m = p.L1, L2m = p.L2;
     const int L1 = p.lengths ? min(max(p.lengths[2 * b], 0), L1m) : L1m;
@@ -730,6 +740,10 @@ __global__ void __launch_bounds__(kNW * 32) lin_marg_kernel(SwArgs p) {
 }  // namespace wf
 
 // ------------------------------------------------------------------ host side
+int wavefront_fixup_count(unsigned long long* n) {
+    return (int)cudaMemcpyFromSymbol(n, wf::g_fixups, sizeof(unsigned long long));
+}
+
 size_t wavefront_workspace_bytes(int family, int B, int L1, int L2) {
     if (family != 0) return 0;
     if (L1 > 32 * wf::kMaxRB || L2 % 4 != 0) return 0;

@@ -207,6 +207,29 @@ D2P_API int d2p_wait_selftest(int scope, const int* word, int* status, void* str
 #define D2P_MUFU_PROBE_CHAINS 8
 D2P_API int d2p_mufu_probe(float* out, int blocks, int iters, void* stream);
 
+/* Engine selection for the whole process (all devices): D2P_ENGINE_AUTO picks
+ * per shape (the default, or what D2P_B200_ENGINE names at load: "plane",
+ * "pipeline"); D2P_ENGINE_PLANE runs the general plane engine for every
+ * operator; D2P_ENGINE_PIPELINE runs the anti-diagonal row-block pipeline for
+ * linear value + marginals at every size.  The engines compute the same
+ * results; the switch exists to cross-check and time them.  *previous (may
+ * be NULL) receives the setting before the call.  Takes effect for launches
+ * issued after it returns.  No reference counterpart. */
+#define D2P_ENGINE_AUTO 0
+#define D2P_ENGINE_PLANE 1
+#define D2P_ENGINE_PIPELINE 2
+D2P_API int d2p_set_engine(int engine, int* previous);
+
+/* Engine counters of the current device, cumulative since the library was
+ * loaded: counts[0] = linear problems the log-domain kernel recomputed after a
+ * linear-domain kernel flagged them (low temperatures, extreme scores);
+ * counts[1] = linear problems the plane engine computed (shapes no fast
+ * kernel covers, and problems both fast kernels flagged); counts[2] = affine
+ * problems the plane engine computed.  n: entries to fill (at most 3).
+ * Synchronises with the device.  No reference counterpart: the reference has
+ * one engine per family. */
+D2P_API int d2p_engine_counts(unsigned long long* counts, int n);
+
 #ifdef __cplusplus
 }
 #endif

@@ -21,16 +21,15 @@ def scores(B, L1, L2, seed=0, scale=1.0):
 
 
 def plane_engine(op, s, *params):
-    """Outputs of `op(scores, *params, lengths)` computed by the plane engine:
-    `s` padded with one zero column and `lengths` set to its true shape.  No
-    fast path covers a padded row length that is not a multiple of 4, and the
-    plane engine's arithmetic does not depend on the padding, so this is
-    bitwise what the plane engine gives for a problem a fast path flags."""
-    B, L1, L2 = s.shape
-    sp = torch.nn.functional.pad(s, (0, 1)).contiguous()
-    ln = torch.tensor([[L1, L2]] * B, dtype=torch.int32, device=s.device)
-    outs = op(sp, *params, ln)
-    return [o[..., :L2] if o.dim() == 3 else o for o in outs]
+    """Outputs of `op(scores, *params, None)` computed by the plane engine
+    (d2p_b200.use_engine("plane")): bitwise what the plane engine gives for a
+    problem a fast kernel flags."""
+    from d2p_b200.engine import use_engine
+
+    with use_engine("plane"):
+        outs = op(s, *params, None)
+        torch.cuda.synchronize()
+    return list(outs)
 
 
 def lengths_for(B, L1, L2, seed=1, lo=1):
