@@ -36,6 +36,19 @@
 // I and D per cell for it.  The reverse also writes the marginals and sums
 // score x marginal, and dS/dT follows from Euler's identity for the degree-1
 // homogeneous S(s, go, ge, T): S = sum s mu + go dS/dgo + ge dS/dge + T dS/dT.
+//
+// BF (backward_full): the HVP along the weight plane g gives grad_scores = H g
+// (the Hessian of S is symmetric); the parameter parts are the tangents along
+// g of dS/dgo, dS/dge and dS/dT.  A gap is opened from an M cell with weight
+// Go (BI_down + BD_right) = BM - c1, so
+//   dS/dgo = E[openings] = sum M (BM - c1) / Z_total,
+// a sum over cells of values the HVP sweeps hold, and so is its tangent (dM,
+// dBM, dc1).  The sweep pair also sums s H g; d(dS/dT)[g] = -(sum s H g + go
+// d(dS/dgo)[g] + ge d(dS/dge)[g]) / T by Euler's identity, with d(dS/dge)[g]
+// read from dot_out[B + b], which the caller's dot sweep along gap_ext wrote
+// before this launch.  (dS/dge as gap cells minus openings, the gap cells from
+// the position sums of path ends and starts, needs no second sweep pair but
+// cancels: its fp32 error reached 3.7x the reference's.)
 #include <stddef.h>
 #include <stdint.h>
 
@@ -420,6 +433,8 @@ struct RevVars {
     double dot;
     float sgap;             // PG: this stage's sum of the I and D visit probabilities
     double dot2;
+    float sx1;              // BF: this stage's sum of the openings' tangent
+    double dot3;
 };
 
 struct RevCtx {
@@ -505,11 +520,12 @@ __device__ __forceinline__ void rev_apply(RevVars& V) {
 
 struct RevOut {
     float BM, BI, BD, PB, dBI, dBD, dPB, dmu, gv;
+    float x1;               // BF: the cell's share of d(dS/dgo)[g]
 };
 // m / dm: the forward's M and dM of this cell.  PG: the marginal itself (in
 // dmu) and the cell's I and D visit probabilities (in gv; dm is then the
 // forward's I, x its D), no tangent of the reverse.
-template <bool PG>
+template <bool PG, bool BF>
 __device__ __forceinline__ RevOut rev_cell(const RevCtx& C, const RevVars& V, int i, float sc, float vv, float m,
                                            float dm, float x) {
     RevOut o;
@@ -521,6 +537,7 @@ __device__ __forceinline__ RevOut rev_cell(const RevCtx& C, const RevVars& V, in
     o.BI = fmaf(i == 0 ? V.f.Ged0 : V.f.Ged1, V.Yr, fmaf(C.Ge, V.f.ya[i], c1));
     o.BM = fmaf(i == 0 ? V.f.God0 : V.f.God1, V.Yr, fmaf(C.Go, V.f.ya[i], fmaf(C.Go, V.BDp, c1)));
     o.PB = P * o.BM;
+    o.x1 = 0.f;
     if (PG) {
         o.dBI = o.dBD = o.dPB = 0.f;
         o.dmu = o.BM * (m * V.f.kE);
@@ -537,7 +554,19 @@ __device__ __forceinline__ RevOut rev_cell(const RevCtx& C, const RevVars& V, in
     o.dPB = P * fmaf(vp, o.BM, dBM);
     const float mu = o.BM * (m * V.f.kE);
     o.dmu = fmaf(fmaf(dBM, m, o.BM * dm), V.f.kE, -mu * C.dSr);
+    if (BF) {   // openings from this M cell, M (BM - c1) / Z, and their tangent
+        const float op = o.BM - c1;
+        const float mk = m * V.f.kE;
+        o.x1 = fmaf(fmaf(dm, op, m * (dBM - dc1)), V.f.kE, -(mk * op) * C.dSr);
+    }
     return o;
+}
+
+// BF: the cell's shares of sum s dmu and of the openings' tangent
+__device__ __forceinline__ void bf_emit(RevVars& V, const RevOut& o, float sc, bool act) {
+    if (!act) return;
+    V.sdot = fmaf(sc, o.dmu, V.sdot);
+    V.sx1 += o.x1;
 }
 
 // DOT: sum gm * dmu; PG: write the marginal and sum score * marginal (gm is
@@ -580,7 +609,7 @@ __device__ __forceinline__ void rev_commit(RevVars& V, const RevOut& o, bool act
     V.BMl = act ? o.BM : 0.f;
 }
 
-template <bool MASK, bool HV, bool DOT, bool PG>
+template <bool MASK, bool HV, bool DOT, bool PG, bool BF>
 __device__ __forceinline__ void rev_stage_full(const RevCtx& C, RevVars& V, int k, int thr) {
     const int m16 = C.P + 16 - kCW * k;
     const int slot = ((m16 >> 4) & 1) * (16 * 32) + C.lane;
@@ -604,11 +633,12 @@ __device__ __forceinline__ void rev_stage_full(const RevCtx& C, RevVars& V, int 
             if (u == kCW - 1) cp_async_wait1();
             rev_lookahead(C, V, 4 * k + (u >> 2) + 1);
         }
-        const RevOut o = rev_cell<PG>(C, V, i, scv[u], DOT ? 0.f : vvv[u], zb[(15 - u) * 32], dzb[(15 - u) * 32],
-                                      PG ? xb[(15 - u) * 32] : 0.f);
+        const RevOut o = rev_cell<PG, BF>(C, V, i, scv[u], DOT ? 0.f : vvv[u], zb[(15 - u) * 32],
+                                          dzb[(15 - u) * 32], PG ? xb[(15 - u) * 32] : 0.f);
         const bool act = !MASK || u < thr;
         const int col = (u <= cb) ? cb - u : cb - u + kRW;
         rev_emit<DOT, PG>(V, C.ring + col, PG ? scv[u] : vvv[u], o.dmu, act, o.gv);
+        if (BF) bf_emit(V, o, scv[u], act);
         rev_commit(V, o, act, yq[i], xq[i], dyq[i], dxq[i]);
         if (i == 3)
             handoff4(C, 4 * k + (u >> 2), make_float4(yq[0], yq[1], yq[2], yq[3]),
@@ -617,7 +647,7 @@ __device__ __forceinline__ void rev_stage_full(const RevCtx& C, RevVars& V, int 
     }
 }
 
-template <bool HV, bool DOT, bool PG>
+template <bool HV, bool DOT, bool PG, bool BF>
 __device__ __forceinline__ void rev_stage_part(const RevCtx& C, RevVars& V, int k) {
     const int m16 = C.P + 16 - kCW * k;
     const int slot = ((m16 >> 4) & 1) * (16 * 32) + C.lane;
@@ -647,9 +677,10 @@ __device__ __forceinline__ void rev_stage_part(const RevCtx& C, RevVars& V, int 
             const int ci = j0 & (kRW - 1);
             const float vv = HV ? C.vring[ci] : 0.f;
             const float sc = C.ring[ci];
-            const RevOut o = rev_cell<PG>(C, V, i, sc, DOT ? 0.f : vv, zb[(15 - u) * 32], dzb[(15 - u) * 32],
-                                          PG ? xb[(15 - u) * 32] : 0.f);
+            const RevOut o = rev_cell<PG, BF>(C, V, i, sc, DOT ? 0.f : vv, zb[(15 - u) * 32], dzb[(15 - u) * 32],
+                                              PG ? xb[(15 - u) * 32] : 0.f);
             rev_emit<DOT, PG>(V, C.ring + ci, PG ? sc : vv, o.dmu, act, o.gv);
+            if (BF) bf_emit(V, o, sc, act);
             rev_commit(V, o, act, yq[i], xq[i], dyq[i], dxq[i]);
             if (i == 3)
                 handoff4(C, 4 * k + q, make_float4(yq[0], yq[1], yq[2], yq[3]),
@@ -663,7 +694,7 @@ __device__ __forceinline__ void rev_stage_part(const RevCtx& C, RevVars& V, int 
 // ==========================================================================
 // kernel (sw_tangent.cu's lin_tan_kernel with the affine cell)
 // ==========================================================================
-template <bool HV, bool DOT, bool SPLIT, bool PG>
+template <bool HV, bool DOT, bool SPLIT, bool PG, bool BF>
 __global__ void __launch_bounds__(kNW * 32, 1) aff_tan_kernel(SwArgs p) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     WarpSmem& W = reinterpret_cast<WarpSmem*>(smem_raw)[threadIdx.x >> 5];
@@ -718,6 +749,7 @@ __global__ void __launch_bounds__(kNW * 32, 1) aff_tan_kernel(SwArgs p) {
     if (L1 == 0 || L2 == 0) {
         if (threadIdx.x == 0 && part == 0) {
             if (DOT && p.dot_out) p.dot_out[b] = 0.f;
+            if (BF && p.dot_out) p.dot_out[b] = p.dot_out[2 * p.B + b] = 0.f;
             if (PG) {  // S = log(1) = 0, and so its derivatives
                 if (p.value) p.value[b] = 0.f;
                 if (p.grad_gap) p.grad_gap[b] = 0.f;
@@ -947,6 +979,7 @@ __global__ void __launch_bounds__(kNW * 32, 1) aff_tan_kernel(SwArgs p) {
     RV.chk = 0.f;
     RV.dot = 0.0;
     RV.dot2 = 0.0;
+    RV.dot3 = 0.0;
     for (int q = gw; q < nRB; q += NWt) {
         const int r = nRB - 1 - q;
         const int nv = min(32, L1 - 32 * r);
@@ -1045,14 +1078,16 @@ __global__ void __launch_bounds__(kNW * 32, 1) aff_tan_kernel(SwArgs p) {
             if (k == 0) rev_lookahead(C, RV, 0);
             RV.sdot = 0.f;
             RV.sgap = 0.f;
+            RV.sx1 = 0.f;
             if (kCW * k <= P + 32 - L2)
-                rev_stage_part<HV, DOT, PG>(C, RV, k);
+                rev_stage_part<HV, DOT, PG, BF>(C, RV, k);
             else if (nv == 32 && kCW * k + kCW - 1 <= P - 1)
-                rev_stage_full<false, HV, DOT, PG>(C, RV, k, 0);
+                rev_stage_full<false, HV, DOT, PG, BF>(C, RV, k, 0);
             else
-                rev_stage_full<true, HV, DOT, PG>(C, RV, k, lane < nv ? 16 * M + 16 - lane : -1);
-            if (DOT || PG) RV.dot += (double)RV.sdot;
+                rev_stage_full<true, HV, DOT, PG, BF>(C, RV, k, lane < nv ? 16 * M + 16 - lane : -1);
+            if (DOT || PG || BF) RV.dot += (double)RV.sdot;
             if (PG) RV.dot2 += (double)RV.sgap;
+            if (BF) RV.dot3 += (double)RV.sx1;
             if (RV.push) Wn.tag[k & (kHR / 16 - 1)] = (q << 16) | k;
             __syncwarp();
             if (lane == 0) {
@@ -1076,13 +1111,21 @@ __global__ void __launch_bounds__(kNW * 32, 1) aff_tan_kernel(SwArgs p) {
     const int o_acc = __syncthreads_or(fwd_out & 8);
     const int o_tan = __syncthreads_or(RV.chk != 0.f ? 1 : 0);
     const int redo = (o_win ? 1 : 0) | (sh_err ? 2 : 0) | (sh_bad ? 4 : 0) | (o_acc ? 8 : 0) | (o_tan ? 16 : 0);
-    if (DOT || PG) {
+    if (DOT || PG || BF) {
         const double tot = block_sum_d(RV.dot, red);
         const double tot2 = PG ? block_sum_d(RV.dot2, red) : 0.0;
+        const double tot3 = BF ? block_sum_d(RV.dot3, red) : 0.0;
         if (threadIdx.x == 0) {
             // DOT: the weighted sum.  PG: dS/dge = (I and D visits) - dS/dgo,
-            // dS/dT = (S - sum s mu - go dS/dgo - ge dS/dge) / T
-            auto finish = [&](double all, double visits) {
+            // dS/dT = (S - sum s mu - go dS/dgo - ge dS/dge) / T.  BF: the
+            // tangents along g of dS/dgo (all3) and, by Euler, of dS/dT from
+            // sum s dmu (all) and the caller's d(dS/dge)[g] in dot_out[B + b]
+            auto finish = [&](double all, double visits, double all3) {
+                if (BF && p.dot_out) {
+                    const double gge = (double)p.dot_out[p.B + b];
+                    p.dot_out[b] = (float)all3;
+                    p.dot_out[2 * p.B + b] = (float)(-(all + (double)go * all3 + (double)ge * gge) / (double)T);
+                }
                 if (DOT && p.dot_out) p.dot_out[b] = (float)all;
                 if (PG) {
                     const double S = ((double)sh_Sint + (double)sh_Sfrac) / (double)c;
@@ -1095,17 +1138,19 @@ __global__ void __launch_bounds__(kNW * 32, 1) aff_tan_kernel(SwArgs p) {
             if (SPLIT && K > 1) {
                 gpart[kSyncPartDoubles * part + 3] = tot;
                 if (PG) gpart[kSyncPartDoubles * part + 4] = tot2;
+                if (BF) gpart[kSyncPartDoubles * part + 4] = tot3;   // (slot 4: PG's, unused by BF)
                 if (atom_add_release_gpu(gsync + 2 * kMaxParts + 1, 1) == K - 1) {
                     (void)ld_acquire_gpu(gsync + 2 * kMaxParts + 1);
-                    double all = 0.0, all2 = 0.0;
+                    double all = 0.0, all2 = 0.0, all3 = 0.0;
                     for (int k = 0; k < K; ++k) {
                         all += gpart[kSyncPartDoubles * k + 3];
                         if (PG) all2 += gpart[kSyncPartDoubles * k + 4];
+                        if (BF) all3 += gpart[kSyncPartDoubles * k + 4];
                     }
-                    finish(all, all2);
+                    finish(all, all2, all3);
                 }
             } else {
-                finish(tot, tot2);
+                finish(tot, tot2, tot3);
             }
         }
     }
@@ -1133,6 +1178,10 @@ int launch_aff_tan(const SwArgs& a, size_t ws_bytes, cudaStream_t st) {
     if (a.L2 % 4 != 0 || a.L1 > 32 * atan_::kMaxRB || a.L1 == 0 || a.L2 == 0) return -1;
     const bool dot = a.dot_with != nullptr;
     const bool hv = a.mode == MODE_HVP || dot;
+    // BF: backward_full's sweep pair -- the HVP along a.tangent into a.out,
+    // and per problem d(dS/dgo) and d(dS/dT) along it into a.dot_out[b] and
+    // [2 B + b], from d(dS/dge) in a.dot_out[B + b] (written before)
+    const bool bf = a.mode == MODE_HVP && !dot && a.dot_out != nullptr;
     if (a.mode == MODE_HVP && (dot || !a.tangent)) return -1;
     if (dot && !a.dot_out) return -1;
     if (!dot && !a.out && !pg) return -1;
@@ -1149,14 +1198,16 @@ int launch_aff_tan(const SwArgs& a, size_t ws_bytes, cudaStream_t st) {
     static DeviceSetup setup;
     int nsm = 0;
     const int se = device_setup(setup, dev, [smem] {
-        const void* ks[8] = {(const void*)atan_::aff_tan_kernel<true, false, false, false>,
-                             (const void*)atan_::aff_tan_kernel<false, false, false, false>,
-                             (const void*)atan_::aff_tan_kernel<true, true, false, false>,
-                             (const void*)atan_::aff_tan_kernel<true, false, true, false>,
-                             (const void*)atan_::aff_tan_kernel<false, false, true, false>,
-                             (const void*)atan_::aff_tan_kernel<true, true, true, false>,
-                             (const void*)atan_::aff_tan_kernel<false, false, false, true>,
-                             (const void*)atan_::aff_tan_kernel<false, false, true, true>};
+        const void* ks[10] = {(const void*)atan_::aff_tan_kernel<true, false, false, false, false>,
+                              (const void*)atan_::aff_tan_kernel<false, false, false, false, false>,
+                              (const void*)atan_::aff_tan_kernel<true, true, false, false, false>,
+                              (const void*)atan_::aff_tan_kernel<true, false, true, false, false>,
+                              (const void*)atan_::aff_tan_kernel<false, false, true, false, false>,
+                              (const void*)atan_::aff_tan_kernel<true, true, true, false, false>,
+                              (const void*)atan_::aff_tan_kernel<false, false, false, true, false>,
+                              (const void*)atan_::aff_tan_kernel<false, false, true, true, false>,
+                              (const void*)atan_::aff_tan_kernel<true, false, false, false, true>,
+                              (const void*)atan_::aff_tan_kernel<true, false, true, false, true>};
         for (const void* k : ks) {
             cudaError_t r = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
             if (r == cudaSuccess)
@@ -1179,22 +1230,25 @@ int launch_aff_tan(const SwArgs& a, size_t ws_bytes, cudaStream_t st) {
             if (err == cudaSuccess && zero_redo) err = cudaMemsetAsync(s.redo, 0, sizeof(int) * (size_t)s.B, st);
             if (err != cudaSuccess) return err;
             void* args[1] = {&s};
-            const void* k = pg    ? (const void*)atan_::aff_tan_kernel<false, false, true, true>
-                            : dot ? (const void*)atan_::aff_tan_kernel<true, true, true, false>
-                            : hv  ? (const void*)atan_::aff_tan_kernel<true, false, true, false>
-                                  : (const void*)atan_::aff_tan_kernel<false, false, true, false>;
+            const void* k = pg    ? (const void*)atan_::aff_tan_kernel<false, false, true, true, false>
+                            : bf  ? (const void*)atan_::aff_tan_kernel<true, false, true, false, true>
+                            : dot ? (const void*)atan_::aff_tan_kernel<true, true, true, false, false>
+                            : hv  ? (const void*)atan_::aff_tan_kernel<true, false, true, false, false>
+                                  : (const void*)atan_::aff_tan_kernel<false, false, true, false, false>;
             err = cudaLaunchCooperativeKernel(k, dim3(s.B * K), dim3(atan_::kNW * 32), args, smem, st);
             if (err == cudaSuccess) return err;
             cudaGetLastError();  // does not fit: one CTA per problem instead
         }
         if (pg)
-            atan_::aff_tan_kernel<false, false, false, true><<<x.B, atan_::kNW * 32, smem, st>>>(x);
+            atan_::aff_tan_kernel<false, false, false, true, false><<<x.B, atan_::kNW * 32, smem, st>>>(x);
+        else if (bf)
+            atan_::aff_tan_kernel<true, false, false, false, true><<<x.B, atan_::kNW * 32, smem, st>>>(x);
         else if (dot)
-            atan_::aff_tan_kernel<true, true, false, false><<<x.B, atan_::kNW * 32, smem, st>>>(x);
+            atan_::aff_tan_kernel<true, true, false, false, false><<<x.B, atan_::kNW * 32, smem, st>>>(x);
         else if (hv)
-            atan_::aff_tan_kernel<true, false, false, false><<<x.B, atan_::kNW * 32, smem, st>>>(x);
+            atan_::aff_tan_kernel<true, false, false, false, false><<<x.B, atan_::kNW * 32, smem, st>>>(x);
         else
-            atan_::aff_tan_kernel<false, false, false, false><<<x.B, atan_::kNW * 32, smem, st>>>(x);
+            atan_::aff_tan_kernel<false, false, false, false, false><<<x.B, atan_::kNW * 32, smem, st>>>(x);
         return cudaGetLastError();
     };
     if (!pg) return (int)sweep(a, true);

@@ -103,8 +103,11 @@ static size_t op_bytes(int family, int op, int B, int L1, int L2) {
             return tan_area(family, op, B, L1, L2) + align256((size_t)(B > 0 ? B : 1) * sizeof(int)) +
                    align256((size_t)(B > 0 ? B : 1) * kSyncBytes);
         case D2P_OP_BACKWARD_FULL:
+            // the tangent area, per-problem partials, flags, cross-CTA words,
+            // and a second flag array (affine: the gap_ext dot sweep's)
             return tan_area(family, op, B, L1, L2) + align256((size_t)4 * (B > 0 ? B : 1) * sizeof(float)) +
-                   align256((size_t)(B > 0 ? B : 1) * sizeof(int)) + align256((size_t)(B > 0 ? B : 1) * kSyncBytes);
+                   2 * align256((size_t)(B > 0 ? B : 1) * sizeof(int)) +
+                   align256((size_t)(B > 0 ? B : 1) * kSyncBytes);
         default:
             return (size_t)-1;
     }
@@ -569,6 +572,8 @@ int d2p_sw_affine_backward_full(const float* scores, const float* grad_marginals
         }
         return D2P_OK;
     }
+    // grad_scores = H . grad_marginals (the Hessian of S is symmetric);
+    // grad_gap_open / _ext / T = sum grad_marginals * dP/dgo, dP/dge, dP/dT
     const size_t area = tan_area(D2P_FAMILY_AFFINE, D2P_OP_BACKWARD_FULL, B, L1, L2);
     float* planes = (float*)workspace;
     float* partials = (float*)((char*)workspace + area);
@@ -581,13 +586,58 @@ int d2p_sw_affine_backward_full(const float* scores, const float* grad_marginals
     a.tangent = grad_marginals;
     a.mode = MODE_HVP;
     a.out = grad_scores;
-    int rc = run_tangent(D2P_FAMILY_AFFINE, a, workspace_bytes, flags, st);
+    const int modes[3] = {MODE_PGAP, MODE_PGE, MODE_PT};
+    float* outs[3] = {grad_gap_open, grad_gap_ext, grad_temperature};
+    int* const sync = (int*)((char*)flags + align256((size_t)B * sizeof(int)));
+    int* const flags2 = (int*)((char*)sync + align256((size_t)B * kSyncBytes));
+    // Two sweep pairs of the tangent kernel (sw_affine_tangent.cu): the dot
+    // sweep along gap_ext (d(dS/dge)[g] per problem), then the BF sweep (H . g,
+    // d(dS/dgo)[g], and d(dS/dT)[g] by Euler's identity from the first).
+    // Problems either flags get the plane engine's HVP and three dot sweeps.
+    SwArgs d = a;
+    d.mode = MODE_PGE;
+    d.tangent = nullptr;
+    d.out = nullptr;
+    d.dot_with = grad_marginals;
+    d.dot_out = partials + (size_t)B;
+    d.redo = flags2;
+    d.sync = sync;
+    int rc = launch_aff_tan(d, workspace_bytes, st);
+    if (rc == D2P_OK) {
+        a.dot_out = partials;
+        a.redo = flags;
+        a.sync = sync;
+        rc = launch_aff_tan(a, workspace_bytes, st);
+        a.redo = nullptr;
+        a.sync = nullptr;
+        a.dot_out = nullptr;
+        if (rc == D2P_OK) rc = launch_or_flags(flags, flags2, B, st);
+        if (rc) return rc;
+        a.only = flags;
+        rc = launch_aff_plane(a, st);
+        if (rc) return rc;
+        a.tangent = nullptr;
+        a.out = nullptr;
+        a.dot_with = grad_marginals;
+        for (int q = 0; q < 3; ++q) {
+            a.mode = modes[q];
+            a.dot_out = partials + (size_t)q * B;
+            rc = launch_aff_plane(a, st);
+            if (rc) return rc;
+        }
+        for (int q = 0; q < 3; ++q) {
+            rc = launch_sum_batches(partials + (size_t)q * B, 1, B, outs[q], 0, st);
+            if (rc) return rc;
+        }
+        return D2P_OK;
+    }
+    if (rc != kNotHandled) return rc;
+    // shapes the tangent kernel does not take: the HVP and three dot sweep pairs
+    rc = run_tangent(D2P_FAMILY_AFFINE, a, workspace_bytes, flags, st);
     if (rc) return rc;
     a.tangent = nullptr;
     a.out = nullptr;
     a.dot_with = grad_marginals;
-    const int modes[3] = {MODE_PGAP, MODE_PGE, MODE_PT};
-    float* outs[3] = {grad_gap_open, grad_gap_ext, grad_temperature};
     for (int q = 0; q < 3; ++q) {
         a.mode = modes[q];
         a.dot_out = partials + (size_t)q * B;

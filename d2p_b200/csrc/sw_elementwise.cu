@@ -193,6 +193,16 @@ int launch_unpad_rows(const float* in, int L1p, int L2p, float* out, int B, int 
     return (int)cudaGetLastError();
 }
 
+__global__ void or_flags_kernel(int* __restrict__ a, const int* __restrict__ b, int n) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) a[i] |= b[i];
+}
+
+int launch_or_flags(int* a, const int* b, int n, cudaStream_t st) {
+    if (n <= 0) return 0;
+    or_flags_kernel<<<(n + 255) / 256 < 148 ? (n + 255) / 256 : 148, 256, 0, st>>>(a, b, n);
+    return (int)cudaGetLastError();
+}
+
 int launch_sum_batches(const float* partials, int P, int B, float* out, int accumulate,
                        cudaStream_t st) {
     sum_batches_kernel<<<1, 32, 0, st>>>(partials, P, B, out, accumulate);

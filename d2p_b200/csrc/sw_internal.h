@@ -121,8 +121,9 @@ size_t lin_fast_workspace_bytes(int B, int L1, int L2);
 bool lin_wide_pays(int L1, int L2);
 int launch_lin_fast(const SwArgs& a, size_t ws_bytes, cudaStream_t st);
 // column-sweep strip kernel (sw_strip.cu): value + marginals without parameter
-// gradients for problems of at most 512 rows (L1 % 16 == 0, L2 % 4 == 0);
-// returns -1 when the shape or arguments are not covered
+// gradients for problems of at most 512 rows (planes whose rows are not whole
+// 16-byte units go through padded copies in the workspace); returns -1 when
+// the shape or arguments are not covered
 size_t lin_strip_workspace_bytes(int B, int L1, int L2);
 int launch_lin_strip(const SwArgs& a, size_t ws_bytes, cudaStream_t st);
 // affine-gap linear-domain fast path (sw_affine_fast.cu): value + marginals
@@ -178,6 +179,8 @@ int launch_value_backward_rows(const float* grad_value, const float* marginals, 
                                float* grad_scores, float* grad_params, cudaStream_t st);
 int launch_sum_batches(const float* partials, int P, int B, float* out, int accumulate,
                        cudaStream_t st);
+// a[i] |= b[i] for n problem flags
+int launch_or_flags(int* a, const int* b, int n, cudaStream_t st);
 // [B][L1][L2] <-> [B][L1p][L2p] (L1p >= L1, L2p >= L2; zeros in the padding)
 int launch_pad_rows(const float* in, int B, int L1, int L2, float* out, int L1p, int L2p, cudaStream_t st);
 int launch_unpad_rows(const float* in, int L1p, int L2p, float* out, int B, int L1, int L2, cudaStream_t st);

@@ -390,3 +390,25 @@ def test_bf16_param_grads_on_the_tangent_kernel(d2p, cuda_device):
     check("grad_open", out_b[2], r64["grad_open"], r32["grad_open"])
     check("grad_ext", out_b[3], r64["grad_ext"], r32["grad_ext"])
     check("grad_T", out_b[4], r64["grad_T"], r32["grad_T"])
+
+
+def test_backward_full_is_two_sweep_pairs(d2p, cuda_device):
+    """backward_full runs two tangent-kernel launches: the dot sweep along
+    gap_ext, then the BF sweep (H g, the gap_open part and, by Euler's
+    identity, the temperature part), where it ran four; the plane engine's
+    fix-up launches find nothing to do.  A problem spread over several CTAs
+    (B = 1) takes the same two launches."""
+    from torch.profiler import ProfilerActivity, profile
+
+    for B, L1, L2 in [(3, 130, 260), (1, 1024, 256)]:
+        s = scores(B, L1, L2, seed=91).to(cuda_device)
+        G = scores(B, L1, L2, seed=92).to(cuda_device)
+        torch.ops.d2p.soft_sw_affine_backward_full(s, G, -2.0, -0.5, 1.0, None)
+        c0 = d2p.engine_counts()
+        torch.cuda.synchronize()
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            torch.ops.d2p.soft_sw_affine_backward_full(s, G, -2.0, -0.5, 1.0, None)
+            torch.cuda.synchronize()
+        names = [e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA]
+        assert sum("aff_tan_kernel" in n for n in names) == 2, names
+        assert d2p.engine_counts() == c0, "a problem reached the plane engine"
