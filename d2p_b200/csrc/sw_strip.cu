@@ -109,15 +109,20 @@ struct Meet {                          // the reverse's values at the cut, per r
 
 // The warps' tiles come last, so that a CTA of W warps per direction
 // allocates 2W of them.
+// A CTA has Wc slots, each a forward and a reverse warp on one row block of a
+// problem; a problem's row blocks take consecutive slots o .. o + Wp - 1.
 struct CtaSmem {
-    Hand h[kMaxW];                     // by row block
+    Hand h[kMaxW];                     // by slot
     Meet meet[kMaxW];
     int progF[kMaxW], progR[kMaxW];    // blocks published (forward / reverse ordinal)
-    int consF[kMaxW], consR[kMaxW];    // blocks read by the row block's consumer
+    int consF[kMaxW], consR[kMaxW];    // blocks read by the slot's consumer
     float pbase[3 * kMaxW];            // partition partials: base (log2) ...
-    double psum[3 * kMaxW];            //   ... and sum: forward, reverse, crossing per row block
-    int err;
-    WarpSmem w[2 * kMaxW];             // by warp: forward warps 0..W-1, reverse warps W..2W-1
+    double psum[3 * kMaxW];            //   ... and sum: forward, reverse, crossing per slot
+    unsigned long long pbar[kMaxW];    // by a problem's first slot: its barrier at the column cut
+    int err[kMaxW];                    //   and its flags
+    int slot[kMaxW];                   // problem * 4 + row block of each slot (-1: none)
+    int slot_ok[kMaxW];                // the slot's problem passed the table check
+    WarpSmem w[2 * kMaxW];             // by warp: forward warps 0..Wc-1, reverse warps Wc..2Wc-1
 };
 __host__ __device__ constexpr size_t smem_bytes_for(int W) {
     return offsetof(CtaSmem, w) + 2 * (size_t)W * sizeof(WarpSmem) + 256;   // + alignment slack
@@ -209,6 +214,7 @@ struct Args {
     float* ws;
     int* redo;
     const int* order;
+    const int* pack;    // [B][kMaxW] or null: problem * 4 + row block of each slot of each CTA (-1: none)
     size_t ws_stride;   // bytes of workspace per problem
 };
 
@@ -410,8 +416,28 @@ __device__ __forceinline__ void group_P(const Prob& p, const float* tile, int la
 __device__ __forceinline__ float4 f4(float a, float b, float c, float d) { return make_float4(a, b, c, d); }
 __device__ __forceinline__ float f4at(const float4& v, int r) { return r == 0 ? v.x : r == 1 ? v.y : r == 2 ? v.z : v.w; }
 
-// every warp of the CTA, whichever code path it reaches the barrier from
-__device__ __forceinline__ void cta_barrier() { asm volatile("bar.sync 1, %0;" ::"r"(blockDim.x) : "memory"); }
+// One problem's barrier at the column cut: each of its 2 Wact warps arrives
+// once per phase (0, then 1) on the mbarrier its first slot holds, and every
+// lane polls for the phase (a wait polled by one lane while the others sit in
+// __syncwarp measured 0.14 ms per barrier at C2, against a few microseconds).
+// The wait is bounded; one that gives up flags the problem (bit 2).
+__device__ __forceinline__ void prob_barrier(unsigned long long* bar, unsigned phase, int* err, int lane) {
+    __syncwarp();
+    const unsigned m = smem_u32(bar);
+    if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(m) : "memory");
+    bool ok = false;
+    for (int it = 0; it < (1 << 22) && !ok; ++it) {
+        unsigned done;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(done)
+            : "r"(m), "r"(phase)
+            : "memory");
+        ok = done != 0;
+    }
+    if (!ok && lane == 0) atomicOr(err, 2);
+    __syncwarp();
+}
 
 // The partition partials (log2 base, sum) of one warp -> the CTA's table.
 __device__ __forceinline__ void put_partial(CtaSmem& S, int slot, float base, double sum, int lane) {
@@ -427,12 +453,15 @@ __device__ __forceinline__ void put_partial(CtaSmem& S, int slot, float base, do
     }
 }
 
-// S = log2(1 + sum of the partials), as integer + fraction; false when not finite
-__device__ __forceinline__ bool partition(const CtaSmem& S, int n, float& Sint, float& Sfrac) {
+// S = log2(1 + sum of the partials of slots o .. o + n - 1), as integer +
+// fraction; false when not finite
+__device__ __forceinline__ bool partition(const CtaSmem& S, int o, int n, float& Sint, float& Sfrac) {
     float m = -3.0e38f;
-    for (int v = 0; v < n; ++v) m = fmaxf(m, S.pbase[v]);
+    for (int g = 0; g < 3; ++g)
+        for (int v = o; v < o + n; ++v) m = fmaxf(m, S.pbase[g * kMaxW + v]);
     double tot = 0.0;
-    for (int v = 0; v < n; ++v) tot = fma(S.psum[v], ld::p2d(S.pbase[v] - m), tot);
+    for (int g = 0; g < 3; ++g)
+        for (int v = o; v < o + n; ++v) tot = fma(S.psum[g * kMaxW + v], ld::p2d(S.pbase[g * kMaxW + v] - m), tot);
     tot += ld::p2d(-m);   // alpha[0,0] = 0 adds 1
     const int hi = __double2hiint(tot);
     const int ef = (hi >> 20) & 0x7ff;
@@ -461,7 +490,10 @@ struct Sweep {
     const float4* kb;
     float4* kp;
     float* pfr;
+    int* err;           // the problem's flags
+    unsigned long long* pbar;
     int b, w, lane, nT, nL, y0;
+    int s, o, Wp;       // slot, the problem's first slot, its slots
     bool above, below;
 };
 
@@ -489,10 +521,10 @@ __device__ __forceinline__ void fwd_block(const Sweep& sw, const Prob& p, FwdSta
                                           float Sfrac) {
     CtaSmem& S = *sw.S;
     WarpSmem& WS = *sw.WS;
-    const Hand& Hup = S.h[sw.above ? sw.w - 1 : 0];
-    Hand& Hme = S.h[sw.w];
+    const Hand& Hup = S.h[sw.above ? sw.s - 1 : sw.s];
+    Hand& Hme = S.h[sw.s];
     const int lane = sw.lane, slot = bk % kHB, nT = sw.nT, nL = sw.nL;
-    int* const err = &S.err;
+    int* const err = sw.err;
     if (!bar_wait(&WS.bar[bk % kNS], (unsigned)(bk / kNS) & 1u)) *err = 1;
     float* const tile = WS.sc[bk % kNS];
     if (bk > 0) {   // the block's frame, from the strip's values
@@ -507,10 +539,10 @@ __device__ __forceinline__ void fwd_block(const Sweep& sw, const Prob& p, FwdSta
     }
     float Ein = 0.f;   // the row above the warp for this block: its frame
     if (sw.above) {
-        ring::wait_flag(&S.progF[sw.w - 1], bk + 1, err);
+        ring::wait_flag(&S.progF[sw.s - 1], bk + 1, err);
         Ein = Hup.fe[slot];
     }
-    if (sw.below && bk >= kHB) ring::wait_flag(&S.consF[sw.w + 1], bk - kHB + 1, err);   // ring space
+    if (sw.below && bk >= kHB) ring::wait_flag(&S.consF[sw.s + 1], bk - kHB + 1, err);   // ring space
     FwdK K;
     fwd_consts(p, st.E, Ein, sw.above, lane, K);
     float kE = 0.f;
@@ -568,11 +600,11 @@ __device__ __forceinline__ void fwd_block(const Sweep& sw, const Prob& p, FwdSta
     }
     if (sw.above) {
         __syncwarp();
-        if (lane == 0) ring::st_release(&S.consF[sw.w], bk + 1);
+        if (lane == 0) ring::st_release(&S.consF[sw.s], bk + 1);
     }
     if (sw.below && lane == 31) {   // the warp's last row of this block, for the warp below
         Hme.fe[slot] = st.E;
-        ring::st_release(&S.progF[sw.w], bk + 1);
+        ring::st_release(&S.progF[sw.s], bk + 1);
     }
     if (!P2) {
         st.acc = fma((double)gs, ld::p2d(st.E - st.ab), st.acc);
@@ -606,18 +638,18 @@ __device__ void run_fwd(const Sweep& sw, const Args& A) {
     for (int bk = 0; bk < nL; ++bk) fwd_block<MASK, false>(sw, p, st, bk, 0.f, 0.f);
 
     // the cut
-    put_partial(S, w, st.ab, st.acc, lane);
-    cta_barrier();   // phase 1 done: every partial and the reverse's values at the cut are in
+    put_partial(S, sw.s, st.ab, st.acc, lane);
+    prob_barrier(sw.pbar, 0, sw.err, lane);   // phase 1 done: every partial and the reverse's values at the cut are in
     if (nL < nT) {   // the moves across the cut: Z_{i,m} (G B_{i,m+1} + P_{i+1,m+1} B_{i+1,m+1})
-        const Meet& M = S.meet[w];
+        const Meet& M = S.meet[sw.s];
         const float Ql = M.Q[lane];
         float pn, Qb;   // the row below the strip: P B at the cut and its frame
         if (lane < 31) {
             pn = M.PB[kR * (lane + 1)];
             Qb = M.Q[lane + 1];
         } else if (sw.below) {
-            pn = S.meet[w + 1].PB[0];
-            Qb = S.meet[w + 1].Q[0];
+            pn = S.meet[sw.s + 1].PB[0];
+            Qb = S.meet[sw.s + 1].Q[0];
         } else {
             pn = 0.f;
             Qb = Ql;
@@ -627,11 +659,11 @@ __device__ void run_fwd(const Sweep& sw, const Args& A) {
         for (int r = 0; r < kR; ++r)
             s1 = fmaf(st.z[r], fmaf(p.G, M.B[kR * lane + r], r + 1 < kR ? M.PB[kR * lane + r + 1] : 0.f), s1);
         const double cr = (double)s1 + (double)(st.z[kR - 1] * pn) * ld::p2d(Qb - Ql);
-        put_partial(S, 2 * kMaxW + w, st.E + Ql, cr, lane);
+        put_partial(S, 2 * kMaxW + sw.s, st.E + Ql, cr, lane);
     }
-    cta_barrier();
+    prob_barrier(sw.pbar, 1, sw.err, lane);
     float Sint, Sfrac;
-    const bool fin = partition(S, 3 * kMaxW, Sint, Sfrac);
+    const bool fin = partition(S, sw.o, sw.Wp, Sint, Sfrac);
     if (w == 0 && lane == 0 && A.value) A.value[sw.b] = (Sint + Sfrac) / p.c;
 
     if (nL < nT) {
@@ -645,7 +677,7 @@ __device__ void run_fwd(const Sweep& sw, const Args& A) {
     for (int bk = nL; bk < nT; ++bk) fwd_block<MASK, true>(sw, p, st, bk, Sint, Sfrac);
 
     const bool bad = __any_sync(kAll, st.jmax > ld::kJMax);
-    if (lane == 0 && (bad || !fin)) atomicOr(&S.err, bad ? 4 : 8);
+    if (lane == 0 && (bad || !fin)) atomicOr(sw.err, bad ? 4 : 8);
 }
 
 // ------------------------------------------------------------------ reverse
@@ -667,10 +699,10 @@ __device__ __forceinline__ void rev_block(const Sweep& sw, const Prob& p, RevSta
                                           float Sfrac) {
     CtaSmem& S = *sw.S;
     WarpSmem& WS = *sw.WS;
-    const Hand& Hdn = S.h[sw.below ? sw.w + 1 : sw.w];
-    Hand& Hme = S.h[sw.w];
+    const Hand& Hdn = S.h[sw.below ? sw.s + 1 : sw.s];
+    Hand& Hme = S.h[sw.s];
     const int lane = sw.lane, slot = rb % kHB, nT = sw.nT, bk = nT - 1 - rb, r0 = nT - sw.nL;
-    int* const err = &S.err;
+    int* const err = sw.err;
     if (!bar_wait(&WS.bar[rb % kNS], (unsigned)(rb / kNS) & 1u)) *err = 1;
     float* const tile = WS.sc[rb % kNS];
     if (rb > 0) {   // the block's reverse frame
@@ -688,10 +720,10 @@ __device__ __forceinline__ void rev_block(const Sweep& sw, const Prob& p, RevSta
     }
     float Qin = 0.f;   // the row below the warp for this block: its frame
     if (sw.below) {
-        ring::wait_flag(&S.progR[sw.w + 1], rb + 1, err);
+        ring::wait_flag(&S.progR[sw.s + 1], rb + 1, err);
         Qin = Hdn.re[slot];
     }
-    if (sw.above && rb >= kHB) ring::wait_flag(&S.consR[sw.w - 1], rb - kHB + 1, err);   // ring space
+    if (sw.above && rb >= kHB) ring::wait_flag(&S.consR[sw.s - 1], rb - kHB + 1, err);   // ring space
     RevK K;
     rev_consts(p, st.Q, Qin, sw.below, lane, K);
     float kE = 0.f;
@@ -764,11 +796,11 @@ __device__ __forceinline__ void rev_block(const Sweep& sw, const Prob& p, RevSta
     st.pbin = (sw.below ? Hdn.rp[slot][0] : 0.f) * K.m1;
     if (sw.below) {
         __syncwarp();
-        if (lane == 0) ring::st_release(&S.consR[sw.w], rb + 1);
+        if (lane == 0) ring::st_release(&S.consR[sw.s], rb + 1);
     }
     if (sw.above && lane == 0) {   // the warp's first row of this block, for the warp above
         Hme.re[slot] = st.Q;
-        ring::st_release(&S.progR[sw.w], rb + 1);
+        ring::st_release(&S.progR[sw.s], rb + 1);
     }
     if (!P2) {
         st.acc = fma((double)gs, ld::p2d(st.Q - st.ab), st.acc);
@@ -802,18 +834,18 @@ __device__ void run_rev(const Sweep& sw, const Args& A) {
     for (int rb = 0; rb < nT - nL; ++rb) rev_block<MASK, false>(sw, p, st, rb, 0.f, 0.f);
 
     // the cut: B and P B at its right column (zero when nothing is right of it)
-    Meet& M = S.meet[w];
+    Meet& M = S.meet[sw.s];
 #pragma unroll
     for (int r = 0; r < kR; ++r) {
         M.B[kR * lane + r] = st.Bv[r];
         M.PB[kR * lane + r] = st.PB[r];
     }
     M.Q[lane] = st.Q;
-    put_partial(S, kMaxW + w, st.ab, st.acc, lane);
-    cta_barrier();
-    cta_barrier();   // the forward warps have added the moves across the cut
+    put_partial(S, kMaxW + sw.s, st.ab, st.acc, lane);
+    prob_barrier(sw.pbar, 0, sw.err, lane);
+    prob_barrier(sw.pbar, 1, sw.err, lane);   // the forward warps have added the moves across the cut
     float Sint, Sfrac;
-    partition(S, 3 * kMaxW, Sint, Sfrac);
+    partition(S, sw.o, sw.Wp, Sint, Sfrac);
 
     if (lane == 0) {   // the kept w of the last block left of the cut: group 1, then group 0
         load_kept(sw, 0, nL - 1, 1);
@@ -823,95 +855,234 @@ __device__ void run_rev(const Sweep& sw, const Args& A) {
     for (int rb = nT - nL; rb < nT; ++rb) rev_block<MASK, true>(sw, p, st, rb, Sint, Sfrac);
 
     const bool bad = __any_sync(kAll, st.jmax > ld::kJMax);
-    if (lane == 0 && bad) atomicOr(&S.err, 4);
+    if (lane == 0 && bad) atomicOr(sw.err, 4);
 }
 
+// rows and columns of problem b inside the padded shape
+__device__ __forceinline__ void prob_shape(const Args& A, int b, int& L1, int& L2) {
+    L1 = A.lengths ? min(max(A.lengths[2 * b], 0), A.L1v) : A.L1v;
+    L2 = A.lengths ? min(max(A.lengths[2 * b + 1], 0), A.L2v) : A.L2v;
+}
+
+// Without a packing table a CTA is one problem: Wc = row blocks of the padded
+// plane, slot = row block.  With one (ragged batches), a CTA has kMaxW slots
+// and the table gives each slot's problem and row block; a problem holds
+// max(Wact, 1) consecutive slots, and the last of them also writes the zeros
+// of the padded plane's row blocks past them.
 __global__ void __launch_bounds__(64 * kMaxW, 2) lin_strip_kernel(const __grid_constant__ CUtensorMap tmS,
                                                                 const __grid_constant__ CUtensorMap tmO,
                                                                 const Args A) {
     extern __shared__ unsigned char smem_raw[];
     CtaSmem& S = *reinterpret_cast<CtaSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 255) & ~(uintptr_t)255);
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    const int W = warps_for(A.L1);
-    const bool fwd = wid < W;
-    const int w = fwd ? wid : wid - W;               // row block
-    WarpSmem& WS = S.w[wid];                         // this warp's tiles (2W of them are allocated)
-    const int b = A.order ? A.order[blockIdx.x] : (int)blockIdx.x;
-    const int L1 = A.lengths ? min(max(A.lengths[2 * b], 0), A.L1v) : A.L1v;
-    const int L2 = A.lengths ? min(max(A.lengths[2 * b + 1], 0), A.L2v) : A.L2v;
-    const int Wact = (L1 > 0 && L2 > 0) ? warps_for(L1) : 0;   // row blocks with rows of the problem
+    const int Wall = warps_for(A.L1);                // row blocks of the padded plane
+    const int Wc = A.pack ? kMaxW : Wall;            // slots of this CTA
+    const bool fwd = wid < Wc;
+    const int s = fwd ? wid : wid - Wc;              // slot
+    WarpSmem& WS = S.w[wid];                         // this warp's tiles (2 Wc of them are allocated)
     if (lane == 0) {
         for (int i = 0; i < kNS; ++i)
             asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&WS.bar[i])) : "memory");
         for (int i = 0; i < 2; ++i)
             asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&WS.kbar[i])) : "memory");
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (threadIdx.x < kMaxW) {
         S.progF[threadIdx.x] = S.progR[threadIdx.x] = 0;
         S.consF[threadIdx.x] = S.consR[threadIdx.x] = 0;
+        S.err[threadIdx.x] = 0;
+        S.slot_ok[threadIdx.x] = 0;
+        S.slot[threadIdx.x] = -1;
     }
-    if (threadIdx.x < 3 * kMaxW) {   // partials of row blocks without rows: nothing
+    if (threadIdx.x < 3 * kMaxW) {   // partials of slots without rows: nothing
         S.pbase[threadIdx.x] = -3.0e38f;
         S.psum[threadIdx.x] = 0.0;
     }
-    if (threadIdx.x == 0) S.err = 0;
+    __syncwarp();
+    if (threadIdx.x == 0) {
+        // the slots' problems; a problem whose slots do not match the table is
+        // left to the fix-up engines (flag 1), and none of its warps runs
+        const int cb = A.order ? A.order[blockIdx.x] : (int)blockIdx.x;
+        for (int q = 0; q < Wc; ++q) S.slot[q] = A.pack ? A.pack[(size_t)kMaxW * blockIdx.x + q] : cb * 4 + q;
+        for (int o = 0; o < Wc; ++o) {
+            const int e = S.slot[o];
+            if (e < 0 || (e & 3) != 0) continue;   // not a problem's first slot
+            int L1, L2;
+            prob_shape(A, e >> 2, L1, L2);
+            const int Wact = (L1 > 0 && L2 > 0) ? warps_for(L1) : 0;
+            const int Wp = A.pack ? max(Wact, 1) : Wall;
+            bool ok = o + Wp <= Wc;
+            for (int q = o; ok && q < o + Wp; ++q) ok = S.slot[q] == e + (q - o);
+            S.err[o] = ok ? 0 : 1;
+            if (!ok) continue;
+            for (int q = o; q < o + Wp; ++q) S.slot_ok[q] = 1;
+            if (Wact > 0)
+                asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(&S.pbar[o])), "r"(2 * Wact)
+                             : "memory");
+        }
+    }
+    if (lane == 0) asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     __syncthreads();
 
-    char* const base = reinterpret_cast<char*>(A.ws) + (size_t)b * A.ws_stride;
-    const int nT = (L2 + kBC - 1) / kBC;
-    const int nTall = (A.L2 + kBC - 1) / kBC;
-    Sweep sw;
-    sw.tmS = &tmS;
-    sw.tmO = &tmO;
-    sw.S = &S;
-    sw.WS = &WS;
-    sw.kb = reinterpret_cast<const float4*>(base) + (size_t)w * nT * kBC * 32;
-    sw.kp = reinterpret_cast<float4*>(base) + (size_t)w * nT * kBC * 32 + lane;
-    sw.pfr = reinterpret_cast<float*>(base + plane_bytes_of(W, A.L2)) + (size_t)w * nT * 32 + lane;
-    sw.b = b;
-    sw.w = w;
-    sw.lane = lane;
-    sw.nT = nT;
-    sw.nL = (nT + 1) / 2;                            // blocks left of the cut
-    sw.y0 = 32 * w;
-    sw.above = w > 0;
-    sw.below = w + 1 < Wact;
-    // output tiles that no sweep writes (past the problem's columns, or rows of
-    // a row block without rows of the problem): zeros, stored by the forward
-    // warp from its kept slots (4 KB, free until its phase 2)
-    const int zfrom = w < Wact ? nT : 0;
-    if (fwd && zfrom < nTall) {
-        float4* zt = &WS.kr[0][0];
-        for (int i = lane; i < kTileFloats / 4; i += 32) zt[i] = f4(0.f, 0.f, 0.f, 0.f);
-        fence_async_smem();
-        __syncwarp();
-        if (lane == 0)
-            for (int t = zfrom; t < nTall; ++t) tma_store_tile(&tmO, reinterpret_cast<float*>(zt), kBC * t, sw.y0, b);
-    }
-    if (w < Wact) {
-        // cells outside the problem in this row block: rows past L1, or a last block cut by L2
-        const bool mask = L1 < kWR * (w + 1) || L2 % kBC != 0;
-        if (fwd) {
-            if (mask)
-                run_fwd<true>(sw, A);
-            else
-                run_fwd<false>(sw, A);
-        } else {
-            if (mask)
-                run_rev<true>(sw, A);
-            else
-                run_rev<false>(sw, A);
+    if (S.slot_ok[s]) {
+        const int e = S.slot[s];
+        const int b = e >> 2, w = e & 3, o = s - w;
+        int L1, L2;
+        prob_shape(A, b, L1, L2);
+        const int Wact = (L1 > 0 && L2 > 0) ? warps_for(L1) : 0;   // row blocks with rows of the problem
+        const int Wp = A.pack ? max(Wact, 1) : Wall;
+        char* const base = reinterpret_cast<char*>(A.ws) + (size_t)b * A.ws_stride;
+        const int nT = (L2 + kBC - 1) / kBC;
+        const int nTall = (A.L2 + kBC - 1) / kBC;
+        Sweep sw;
+        sw.tmS = &tmS;
+        sw.tmO = &tmO;
+        sw.S = &S;
+        sw.WS = &WS;
+        sw.kb = reinterpret_cast<const float4*>(base) + (size_t)w * nT * kBC * 32;
+        sw.kp = reinterpret_cast<float4*>(base) + (size_t)w * nT * kBC * 32 + lane;
+        sw.pfr = reinterpret_cast<float*>(base + plane_bytes_of(Wall, A.L2)) + (size_t)w * nT * 32 + lane;
+        sw.err = &S.err[o];
+        sw.pbar = &S.pbar[o];
+        sw.b = b;
+        sw.w = w;
+        sw.s = s;
+        sw.o = o;
+        sw.Wp = Wp;
+        sw.lane = lane;
+        sw.nT = nT;
+        sw.nL = (nT + 1) / 2;                        // blocks left of the cut
+        sw.y0 = 32 * w;
+        sw.above = w > 0;
+        sw.below = w + 1 < Wact;
+        // output tiles that no sweep writes (past the problem's columns, rows
+        // of a row block without rows of the problem, and -- from the problem's
+        // last slot -- the padded plane's row blocks past its slots): zeros,
+        // stored by the forward warp from its kept slots (4 KB, free until its
+        // phase 2)
+        const int zfrom = w < Wact ? nT : 0;
+        const int zrb = w == Wp - 1 ? Wall : w + 1;  // row blocks w .. zrb - 1
+        if (fwd && (zfrom < nTall || zrb > w + 1)) {
+            float4* zt = &WS.kr[0][0];
+            for (int i = lane; i < kTileFloats / 4; i += 32) zt[i] = f4(0.f, 0.f, 0.f, 0.f);
+            fence_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                for (int t = zfrom; t < nTall; ++t) tma_store_tile(&tmO, reinterpret_cast<float*>(zt), kBC * t, sw.y0, b);
+                for (int r = w + 1; r < zrb; ++r)
+                    for (int t = 0; t < nTall; ++t) tma_store_tile(&tmO, reinterpret_cast<float*>(zt), kBC * t, 32 * r, b);
+            }
         }
-    } else {
-        cta_barrier();   // the two barriers at the cut of the warps with rows
-        cta_barrier();
+        if (w < Wact) {
+            // cells outside the problem in this row block: rows past L1, or a last block cut by L2
+            const bool mask = L1 < kWR * (w + 1) || L2 % kBC != 0;
+            if (fwd) {
+                if (mask)
+                    run_fwd<true>(sw, A);
+                else
+                    run_fwd<false>(sw, A);
+            } else {
+                if (mask)
+                    run_rev<true>(sw, A);
+                else
+                    run_rev<false>(sw, A);
+            }
+        }
+        if (lane == 0) tma_store_wait0();
     }
-    if (lane == 0) tma_store_wait0();
     __syncthreads();
     if (threadIdx.x == 0) {
-        if (Wact == 0 && A.value) A.value[b] = 0.f;
-        if (A.redo) A.redo[b] = S.err;
+        for (int o = 0; o < Wc; ++o) {
+            const int e = S.slot[o];
+            if (e < 0 || (e & 3) != 0) continue;
+            const int b = e >> 2;
+            int L1, L2;
+            prob_shape(A, b, L1, L2);
+            if ((L1 == 0 || L2 == 0) && A.value && S.err[o] == 0) A.value[b] = 0.f;
+            if (A.redo) A.redo[b] = S.err[o];
+        }
+    }
+}
+
+// The packing table of a ragged batch (one CTA of 1024 threads).  A problem
+// takes max(Wact, 1) slots (its class, 1..4); CTAs are filled class by class,
+// each class in the given order (largest cost first): one 4-slot problem; a
+// 3-slot problem with a 1-slot one; two 2-slot problems (the last, if their
+// number is odd, with two 1-slot ones); the remaining 1-slot problems four by
+// four.  pack[kMaxW c + q] = problem * 4 + row block of slot q of CTA c (-1:
+// none); *ncta = CTAs used.  Deterministic: ranks come from ballots in order.
+__global__ void __launch_bounds__(1024) strip_pack_kernel(const int* __restrict__ lengths, int B, int L1v, int L2v,
+                                                          const int* __restrict__ order, int* __restrict__ pack,
+                                                          int* __restrict__ ncta) {
+    __shared__ int cnt[5], run[5], wtot[32][5], wpre[32][5];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    for (int i = tid; i < kMaxW * B; i += blockDim.x) pack[i] = -1;
+    if (tid < 5) cnt[tid] = run[tid] = 0;
+    __syncthreads();
+    auto cls_of = [&](int k, int& b) {
+        if (k >= B) return 0;
+        b = order ? order[k] : k;
+        const int l1 = min(max(lengths[2 * b], 0), L1v), l2 = min(max(lengths[2 * b + 1], 0), L2v);
+        return (l1 > 0 && l2 > 0) ? min(warps_for(l1), kMaxW) : 1;
+    };
+    for (int k0 = 0; k0 < B; k0 += blockDim.x) {
+        int b = 0;
+        const int c = cls_of(k0 + tid, b);
+        if (c > 0) atomicAdd(&cnt[c], 1);
+    }
+    __syncthreads();
+    const int n1 = cnt[1], n2 = cnt[2], n3 = cnt[3], n4 = cnt[4];
+    const int m13 = min(n1, n3);                      // 1-slot problems beside 3-slot ones
+    const int n2h = (n2 + 1) / 2;
+    const int m2 = (n2 & 1) ? min(2, n1 - m13) : 0;   // 1-slot problems in the odd 2-slot CTA
+    const int rem1 = n1 - m13 - m2;
+    if (tid == 0) *ncta = n4 + n3 + n2h + (rem1 + kMaxW - 1) / kMaxW;
+    for (int k0 = 0; k0 < B; k0 += blockDim.x) {
+        int b = 0;
+        const int c = cls_of(k0 + tid, b);
+        int lpre[5];
+#pragma unroll
+        for (int q = 1; q <= 4; ++q) {
+            const unsigned m = __ballot_sync(0xffffffffu, c == q);
+            lpre[q] = __popc(m & ((1u << lane) - 1u));
+            if (lane == 0) wtot[warp][q] = __popc(m);
+        }
+        __syncthreads();
+        if (tid < 4) {
+            const int q = tid + 1;
+            int acc = run[q];
+            for (int v = 0; v < (int)(blockDim.x >> 5); ++v) {
+                wpre[v][q] = acc;
+                acc += wtot[v][q];
+            }
+            run[q] = acc;
+        }
+        __syncthreads();
+        if (c > 0) {
+            const int r = wpre[warp][c] + lpre[c];    // rank within the class, in order
+            int cta, q0;
+            if (c == 4) {
+                cta = r;
+                q0 = 0;
+            } else if (c == 3) {
+                cta = n4 + r;
+                q0 = 0;
+            } else if (c == 2) {
+                cta = n4 + n3 + r / 2;
+                q0 = 2 * (r & 1);
+            } else if (r < m13) {
+                cta = n4 + r;
+                q0 = 3;
+            } else if (r < m13 + m2) {
+                cta = n4 + n3 + n2h - 1;
+                q0 = 2 + (r - m13);
+            } else {
+                const int r1 = r - m13 - m2;
+                cta = n4 + n3 + n2h + r1 / kMaxW;
+                q0 = r1 % kMaxW;
+            }
+            for (int j = 0; j < c; ++j) pack[(size_t)kMaxW * cta + q0 + j] = b * 4 + j;
+        }
+        __syncthreads();
     }
 }
 
@@ -961,11 +1132,16 @@ static size_t strip_plane_area(int B, int L1, int L2) {
 static size_t strip_padded_bytes(int B, int L1, int L2) {
     return align256z((size_t)B * round4(L1) * round4(L2) * sizeof(float));
 }
+// the packing table of a ragged batch and its CTA count
+static size_t strip_pack_bytes(int B) { return align256z((size_t)strip::kMaxW * B * sizeof(int)) + 256; }
+static size_t strip_main_bytes(int B, int L1, int L2) {
+    return strip_repack(L1, L2) ? strip_plane_area(B, L1, L2) + 2 * strip_padded_bytes(B, L1, L2)
+                                : strip_plane_area(B, L1, L2);
+}
 
 size_t lin_strip_workspace_bytes(int B, int L1, int L2) {
     if (!strip_shape_ok(L1, L2)) return 0;
-    if (!strip_repack(L1, L2)) return strip::per_problem_bytes(L1, L2) * (size_t)B;
-    return strip_plane_area(B, L1, L2) + 2 * strip_padded_bytes(B, L1, L2);
+    return strip_main_bytes(B, L1, L2) + strip_pack_bytes(B);
 }
 
 int launch_lin_strip(const SwArgs& a, size_t ws_bytes, cudaStream_t st) {
@@ -1013,13 +1189,28 @@ int launch_lin_strip(const SwArgs& a, size_t ws_bytes, cudaStream_t st) {
     A.ws = a.ws;
     A.redo = a.redo;
     A.order = a.order;
+    A.pack = nullptr;
     A.ws_stride = per;
     const int W = strip::warps_for(L1p);
     if (repack) {
         const int rc = launch_pad_rows(a.scores, a.B, a.L1, a.L2, const_cast<float*>(sc), L1p, L2p, st);
         if (rc) return rc;
     }
-    strip::lin_strip_kernel<<<a.B, 64 * W, strip::smem_bytes_for(W), st>>>(tmS, tmO, A);
+    // ragged batches of problems over 128 rows: several problems per CTA,
+    // by the packing table (CTAs past the table's count find no slot and exit)
+    const bool pack = a.lengths && W > 1 && a.B > 1;
+    if (pack) {
+        int* const tab = (int*)((char*)a.ws + strip_main_bytes(a.B, a.L1, a.L2));
+        int* const ncta = (int*)((char*)tab + align256z((size_t)strip::kMaxW * a.B * sizeof(int)));
+        strip::strip_pack_kernel<<<1, 1024, 0, st>>>(a.lengths, a.B, a.L1, a.L2, a.order, tab, ncta);
+        const cudaError_t pe = cudaGetLastError();
+        if (pe != cudaSuccess) return (int)pe;
+        A.pack = tab;
+        A.order = nullptr;
+        strip::lin_strip_kernel<<<a.B, 64 * strip::kMaxW, strip::smem_bytes_for(strip::kMaxW), st>>>(tmS, tmO, A);
+    } else {
+        strip::lin_strip_kernel<<<a.B, 64 * W, strip::smem_bytes_for(W), st>>>(tmS, tmO, A);
+    }
     cudaError_t e2 = cudaGetLastError();
     if (e2 != cudaSuccess || !repack) return (int)e2;
     return launch_unpad_rows(out, L1p, L2p, a.out, a.B, a.L1, a.L2, st);

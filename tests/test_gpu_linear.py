@@ -702,3 +702,32 @@ def test_pipeline_engine_matches_strip(d2p, cuda_device):
     assert not any("lin_strip_kernel" in n for n in names), names
     torch.testing.assert_close(v2, v, rtol=1e-6, atol=1e-4)
     torch.testing.assert_close(m2, m, rtol=0, atol=1e-6)
+
+
+def test_strip_packs_ragged_problems(d2p, cuda_device):
+    """A ragged batch packs several problems per CTA (strip_pack_kernel): every
+    slot class (1-4 row blocks of 128), empty problems and 1-row problems in
+    one batch, against the oracle, padding exactly zero, no problem left to a
+    fix-up engine, and bitwise the same results run twice."""
+    L1, L2 = 512, 300
+    shapes = [(512, 300), (0, 40), (30, 0), (1, 1), (128, 77), (129, 64), (384, 17), (257, 300), (5, 299),
+              (500, 3), (64, 64), (200, 150), (1, 300), (385, 200), (127, 128), (256, 256), (100, 9)]
+    B = len(shapes)
+    s = scores(B, L1, L2, seed=404)
+    ln = torch.tensor(shapes, dtype=torch.int32)
+    sd, lnd = s.to(cuda_device), ln.to(cuda_device)
+    torch.ops.d2p.soft_sw_float(sd, -1.0, 1.0, lnd)
+    c0 = d2p.engine_counts()
+    names = _kernel_names(lambda: torch.ops.d2p.soft_sw_float(sd, -1.0, 1.0, lnd))
+    v, m = torch.ops.d2p.soft_sw_float(sd, -1.0, 1.0, lnd)
+    assert d2p.engine_counts() == c0, "a problem left the strip kernel"
+    assert any("strip_pack_kernel" in n for n in names), names
+    r64 = oracle.sw_linear(s.numpy(), ln.numpy(), -1.0, 1.0, "f64")
+    r32 = oracle.sw_linear(s.numpy(), ln.numpy(), -1.0, 1.0, "f32")
+    check("value", v, r64["value"], r32["value"])
+    check("marginals", m, r64["marginals"], r32["marginals"])
+    mc = m.cpu()
+    for b, (l1, l2) in enumerate(shapes):
+        assert torch.count_nonzero(mc[b, l1:, :]) == 0 and torch.count_nonzero(mc[b, :, l2:]) == 0
+    v2, m2 = torch.ops.d2p.soft_sw_float(sd, -1.0, 1.0, lnd)
+    assert torch.equal(v, v2) and torch.equal(m, m2)
