@@ -138,6 +138,10 @@ int launch_bf16_widen(const __nv_bfloat16* in, float* out, size_t n, cudaStream_
 int launch_lin_order(const int* lengths, int B, int L1, int L2, int* order, cudaStream_t st);
 
 int launch_lin_plane(const SwArgs& a, cudaStream_t st);
+// soft Needleman-Wunsch (sw_nw.cu): workspace of one operator, and one sweep
+// pair in a.mode (MODE_MARG, MODE_HVP, MODE_PGAP, MODE_PT)
+size_t nw_workspace_bytes(int op, int B, int L1, int L2);
+int launch_nw(const SwArgs& a, cudaStream_t st);
 // engine counters of the current device (cumulative, read synchronously):
 // problems the plane engine computed [linear, affine], and problems the
 // log-domain kernel recomputed after a linear-domain kernel flagged them

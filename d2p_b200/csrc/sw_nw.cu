@@ -1,0 +1,390 @@
+// sw_nw.cu -- soft Needleman-Wunsch (global alignment, linear gap): value,
+// marginals, dS/dgap and dS/dT, the Hessian-vector product, the parameter
+// Jacobians dP/dgap and dP/dT, and their contraction with a weight plane
+// (backward_full).
+//
+// Recurrences (src/nw/kernels_cpu.cpp:79-642 restated, natural units):
+//   alpha[0,0] = 0, alpha[i,0] = i gap, alpha[0,j] = j gap,
+//   alpha[i,j] = T log sum_k exp(v_k / T),  v = (alpha[i-1,j-1] + s_ij,
+//                alpha[i-1,j] + gap, alpha[i,j-1] + gap),
+//   S = alpha[L1, L2];  w_k = exp((v_k - alpha[i,j]) / T) normalised by their sum.
+// The reverse is the flow of the path distribution: beta[L1,L2] = 1 and
+// beta[c] = sum over the successors d of c of beta[d] w_{c->d}(d); the marginal
+// of cell (i,j) is beta[i,j] w_diag(i,j).  Every global path with m diagonal
+// cells has L1 + L2 - 2 m gap cells, so dS/dgap = E[gaps] = L1 + L2 - 2 sum mu
+// exactly, and dS/dT = (S - sum s mu - gap dS/dgap) / T (S is homogeneous of
+// degree 1 in (s, gap, T)).
+//
+// Tangents along a direction (V in the scores, or gap, or T): the forward
+// carries d alpha = sum_k w_k dv_k (+ (alpha - E[v]) / T along T), the
+// reverse d beta[c] = sum_d (d beta[d] w_{c->d}(d) + beta[d] dw_{c->d}(d)),
+// dw_k = w_k (dv_k - d alpha) / T (+ w_k (E[v] - v_k) / T^2 along T), and the
+// marginal's tangent d beta w_diag + beta dw_diag (src/nw/kernels_cpu.cpp:278-642).
+//
+// Engine.  One CTA per problem sweeps the anti-diagonals (k = i + j), the
+// threads striding over the cells of a diagonal, with one barrier per
+// diagonal.  Per-cell values live in diagonal-major planes in the workspace
+// ([k][i]: one diagonal is contiguous, so its loads and stores coalesce):
+// alpha and the three normalised weights from the forward, beta from the
+// reverse, and for a tangent its forward and reverse values.  The reverse is a
+// gather over the successors (no atomics: deterministic).  A general engine:
+// any size, every mode; per-problem sums are block reductions in fp64.
+#include <math.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../../include/d2p_b200.h"
+#include "sw_common.cuh"
+#include "sw_internal.h"
+
+namespace d2pb {
+namespace nw {
+
+constexpr int kThreads = 256;
+
+// planes of one problem, each (L1m + L2m + 1) (L1m + 1) floats
+enum Plane : int { kA = 0, kWd, kWu, kWl, kB, kT1, kT2, kT3, kNumPlanes };
+__host__ __device__ inline size_t plane_floats(int L1m, int L2m) {
+    return ((size_t)L1m + L2m + 1) * ((size_t)L1m + 1);
+}
+__host__ __device__ inline int planes_for(int mode) {
+    // MARG: alpha, weights, beta; HVP / PGAP: + the forward tangent and the
+    // reverse tangent; PT: + E[v] as well
+    return mode == MODE_MARG ? 5 : (mode == MODE_PT ? 8 : 7);
+}
+__host__ __device__ inline size_t per_problem_bytes(int L1m, int L2m, int mode) {
+    const size_t b = plane_floats(L1m, L2m) * sizeof(float) * planes_for(mode);
+    return (b + 255) & ~(size_t)255;
+}
+
+struct Ctx {
+    float* p[kNumPlanes];
+    int stride;   // L1m + 1
+    __device__ float& at(int plane, int k, int i) const { return p[plane][(size_t)k * stride + i]; }
+};
+
+__device__ __forceinline__ double block_sum(double v, double* red) {
+    for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    double t = 0.0;
+    if (threadIdx.x < 32) {
+        t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0;
+        for (int o = 16; o >= 1; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    }
+    return t;   // valid in thread 0
+}
+
+// One CTA per problem.  MODE: MODE_MARG (value, marginals, dS/dgap, dS/dT),
+// MODE_HVP (out = d marginals along p.tangent), MODE_PGAP / MODE_PT (out =
+// dP/dtheta; with dot_with, dot_out[b] = sum dot_with * dP/dtheta).
+template <int MODE>
+__global__ void __launch_bounds__(kThreads) nw_kernel(SwArgs p) {
+    __shared__ double red[32];
+    const int b = blockIdx.x;
+    const int L1m = p.L1, L2m = p.L2;
+    const int L1 = p.lengths ? min(max(p.lengths[2 * b], 0), L1m) : L1m;
+    const int L2 = p.lengths ? min(max(p.lengths[2 * b + 1], 0), L2m) : L2m;
+    const float gap = p.gap_dev ? __ldg(p.gap_dev) : p.gap;
+    const float T = p.temp_dev ? __ldg(p.temp_dev) : p.temp;
+    const float iT = 1.f / T;
+    const size_t plane = (size_t)L1m * L2m;
+    const float* __restrict__ S = p.scores + (size_t)b * plane;
+    const float* __restrict__ V = MODE == MODE_HVP ? p.tangent + (size_t)b * plane : nullptr;
+    const float* __restrict__ Gw = p.dot_with ? p.dot_with + (size_t)b * plane : nullptr;
+    float* __restrict__ out = p.out ? p.out + (size_t)b * plane : nullptr;
+    Ctx C;
+    {
+        float* base = reinterpret_cast<float*>(reinterpret_cast<char*>(p.ws) + (size_t)b * per_problem_bytes(L1m, L2m, MODE));
+        const size_t pf = plane_floats(L1m, L2m);
+        for (int q = 0; q < kNumPlanes; ++q) C.p[q] = q < planes_for(MODE) ? base + (size_t)q * pf : nullptr;
+        C.stride = L1m + 1;
+    }
+    const bool TAN = MODE != MODE_MARG;
+    // the forward tangent (dalpha, or U) and the reverse tangent (dbeta, or W)
+    const int kF = kT1, kR = kT2, kEv = kT3;
+
+    // padding of the output: zeros outside the problem
+    if (out) {
+        for (size_t e = threadIdx.x; e < plane; e += blockDim.x) {
+            const int i = (int)(e / L2m), j = (int)(e - (size_t)i * L2m);
+            if (i >= L1 || j >= L2) out[e] = 0.f;
+        }
+    }
+    // boundary cells: alpha = index x gap; the gap tangent is the index
+    for (int q = threadIdx.x; q <= max(L1, L2); q += blockDim.x) {
+        if (q <= L1) {   // (q, 0)
+            C.at(kA, q, q) = (float)q * gap;
+            if (TAN) C.at(kF, q, q) = MODE == MODE_PGAP ? (float)q : 0.f;
+        }
+        if (q >= 1 && q <= L2) {   // (0, q)
+            C.at(kA, q, 0) = (float)q * gap;
+            if (TAN) C.at(kF, q, 0) = MODE == MODE_PGAP ? (float)q : 0.f;
+        }
+    }
+    __syncthreads();
+
+    // ------------------------------------------------------------- forward
+    for (int k = 2; k <= L1 + L2; ++k) {
+        const int i0 = max(1, k - L2), i1 = min(L1, k - 1);
+        for (int i = i0 + threadIdx.x; i <= i1; i += blockDim.x) {
+            const int j = k - i;
+            const size_t si = (size_t)(i - 1) * L2m + (j - 1);
+            const float sc = S[si];
+            const float vd = C.at(kA, k - 2, i - 1) + sc;
+            const float vu = C.at(kA, k - 1, i - 1) + gap;
+            const float vl = C.at(kA, k - 1, i) + gap;
+            const float m = fmaxf(vd, fmaxf(vu, vl));
+            const float ed = expf((vd - m) * iT), eu = expf((vu - m) * iT), el = expf((vl - m) * iT);
+            const float sum = (ed + eu) + el;
+            const float a = fmaf(T, logf(sum), m);
+            const float is = 1.f / sum;
+            const float wd = ed * is, wu = eu * is, wl = el * is;
+            C.at(kA, k, i) = a;
+            C.at(kWd, k, i) = wd;
+            C.at(kWu, k, i) = wu;
+            C.at(kWl, k, i) = wl;
+            if (TAN) {
+                // tangents of the three options
+                float td = C.at(kF, k - 2, i - 1), tu = C.at(kF, k - 1, i - 1), tl = C.at(kF, k - 1, i);
+                if (MODE == MODE_HVP) td += V[si];
+                if (MODE == MODE_PGAP) {
+                    tu += 1.f;
+                    tl += 1.f;
+                }
+                float f = fmaf(wd, td, fmaf(wu, tu, wl * tl));
+                if (MODE == MODE_PT) {
+                    const float ev = fmaf(wd, vd, fmaf(wu, vu, wl * vl));
+                    C.at(kEv, k, i) = ev;
+                    f = fmaf(a - ev, iT, f);
+                }
+                C.at(kF, k, i) = f;
+            }
+        }
+        __syncthreads();
+    }
+
+    // ------------------------------------------------------------- reverse
+    double smu = 0.0, ssmu = 0.0, sdot = 0.0;
+    for (int k = L1 + L2; k >= 0; --k) {
+        const int i0 = max(0, k - L2), i1 = min(L1, k);
+        for (int i = i0 + threadIdx.x; i <= i1; i += blockDim.x) {
+            const int j = k - i;
+            const bool interior = i >= 1 && j >= 1;
+            float be = 0.f, tb = 0.f;
+            const float fc = TAN ? C.at(kF, k, i) : 0.f;
+            const float ac = C.at(kA, k, i);
+            if (k == L1 + L2) {
+                be = 1.f;   // the end cell (L1, L2); its tangent is 0
+            } else {
+                // successors: (i+1, j+1) by its diagonal option, (i+1, j) by
+                // its up option (if j >= 1), (i, j+1) by its left option (if i >= 1)
+                auto take = [&](int kd, int id, int opt, int si_d) {
+                    const float bd = C.at(kB, kd, id);
+                    const float w = C.at(opt, kd, id);
+                    be = fmaf(bd, w, be);
+                    if (TAN) {
+                        // dw of the option c -> d at d: w (dv - d alpha_d) / T (+ the T term)
+                        float dv = fc;
+                        if (MODE == MODE_HVP && opt == kWd) dv += V[si_d];
+                        if (MODE == MODE_PGAP && opt != kWd) dv += 1.f;
+                        const float fd = C.at(kF, kd, id);
+                        float eu = fd;
+                        if (MODE == MODE_PT) eu = fd - (C.at(kA, kd, id) - C.at(kEv, kd, id)) * iT;
+                        float dw = w * (dv - eu) * iT;
+                        if (MODE == MODE_PT) {
+                            const float v = ac + (opt == kWd ? S[si_d] : gap);
+                            dw = fmaf(w * (C.at(kEv, kd, id) - v), iT * iT, dw);
+                        }
+                        tb = fmaf(C.at(kR, kd, id), w, fmaf(bd, dw, tb));
+                    }
+                };
+                if (i + 1 <= L1 && j + 1 <= L2) take(k + 2, i + 1, kWd, i * L2m + j);
+                if (i + 1 <= L1 && j >= 1) take(k + 1, i + 1, kWu, 0);
+                if (j + 1 <= L2 && i >= 1) take(k + 1, i, kWl, 0);
+            }
+            C.at(kB, k, i) = be;
+            if (TAN) C.at(kR, k, i) = tb;
+            if (interior) {
+                const size_t si = (size_t)(i - 1) * L2m + (j - 1);
+                const float wd = C.at(kWd, k, i);
+                if (MODE == MODE_MARG) {
+                    const float mu = be * wd;
+                    if (out) out[si] = mu;
+                    smu += (double)mu;
+                    ssmu += (double)mu * (double)S[si];
+                } else {
+                    // the tangent of this cell's diagonal weight
+                    float dv = C.at(kF, k - 2, i - 1);
+                    if (MODE == MODE_HVP) dv += V[si];
+                    float eu = fc;
+                    if (MODE == MODE_PT) eu = fc - (ac - C.at(kEv, k, i)) * iT;
+                    float dwd = wd * (dv - eu) * iT;
+                    if (MODE == MODE_PT) {
+                        const float vd = C.at(kA, k - 2, i - 1) + S[si];
+                        dwd = fmaf(wd * (C.at(kEv, k, i) - vd), iT * iT, dwd);
+                    }
+                    const float dmu = fmaf(tb, wd, be * dwd);
+                    if (out) out[si] = dmu;
+                    if (Gw) sdot += (double)Gw[si] * (double)dmu;
+                }
+            }
+        }
+        __syncthreads();
+    }
+
+    if (MODE == MODE_MARG) {
+        const double tmu = block_sum(smu, red);
+        const double tsmu = block_sum(ssmu, red);
+        if (threadIdx.x == 0) {
+            const float Sv = C.at(kA, L1 + L2, L1);
+            const double dgap = (double)(L1 + L2) - 2.0 * tmu;
+            if (p.value) p.value[b] = Sv;
+            if (p.grad_gap) p.grad_gap[b] = (float)dgap;
+            if (p.grad_T) p.grad_T[b] = (float)(((double)Sv - tsmu - (double)gap * dgap) / (double)T);
+        }
+    } else if (p.dot_out) {
+        const double t = block_sum(sdot, red);
+        if (threadIdx.x == 0) p.dot_out[b] = (float)t;
+    }
+}
+
+}  // namespace nw
+
+// ------------------------------------------------------------------ host side
+size_t nw_workspace_bytes(int op, int B, int L1, int L2) {
+    const size_t fb = nw::per_problem_bytes(L1, L2, op == D2P_OP_FORWARD_BACKWARD ? MODE_MARG : MODE_PT);
+    size_t n = (fb * (size_t)(B > 0 ? B : 1) + 255) & ~(size_t)255;
+    if (op == D2P_OP_BACKWARD_FULL) n += ((size_t)2 * (B > 0 ? B : 1) * sizeof(float) + 255) & ~(size_t)255;
+    return n;
+}
+
+int launch_nw(const SwArgs& a, cudaStream_t st) {
+    if (a.B == 0) return 0;
+    switch (a.mode) {
+        case MODE_MARG: nw::nw_kernel<MODE_MARG><<<a.B, nw::kThreads, 0, st>>>(a); break;
+        case MODE_HVP: nw::nw_kernel<MODE_HVP><<<a.B, nw::kThreads, 0, st>>>(a); break;
+        case MODE_PGAP: nw::nw_kernel<MODE_PGAP><<<a.B, nw::kThreads, 0, st>>>(a); break;
+        case MODE_PT: nw::nw_kernel<MODE_PT><<<a.B, nw::kThreads, 0, st>>>(a); break;
+        default: return kErrInvalid;
+    }
+    return (int)cudaGetLastError();
+}
+
+}  // namespace d2pb
+
+using namespace d2pb;
+
+// ---------------------------------------------------------------- C ABI
+extern "C" {
+
+static bool nw_dims_ok(int B, int L1, int L2) {
+    if (B < 0 || L1 < 0 || L2 < 0) return false;
+    return (long long)(L1 + 1) * (long long)(L2 + 1) <= 2147483647LL;
+}
+
+static SwArgs nw_args(const float* scores, const int* lengths, int B, int L1, int L2, float gap, float T,
+                      void* ws) {
+    SwArgs a{};
+    a.scores = scores;
+    a.lengths = lengths;
+    a.B = B;
+    a.L1 = L1;
+    a.L2 = L2;
+    a.gap = gap;
+    a.temp = T;
+    a.ws = (float*)ws;
+    return a;
+}
+
+int d2p_nw_forward_backward(const float* scores, const int* lengths, int B, int L1, int L2, float gap,
+                            float temperature, const float* gap_dev, const float* temperature_dev, float* value,
+                            float* marginals, float* grad_gap, float* grad_temperature, void* workspace,
+                            size_t workspace_bytes, void* stream) {
+    if (!nw_dims_ok(B, L1, L2)) return D2P_ERR_TOO_LARGE;
+    if (B == 0) return D2P_OK;
+    if (!scores || !value || !marginals) return D2P_ERR_INVALID_ARGUMENT;
+    if (!workspace || workspace_bytes < nw_workspace_bytes(D2P_OP_FORWARD_BACKWARD, B, L1, L2))
+        return D2P_ERR_WORKSPACE_TOO_SMALL;
+    SwArgs a = nw_args(scores, lengths, B, L1, L2, gap, temperature, workspace);
+    a.gap_dev = gap_dev;
+    a.temp_dev = temperature_dev;
+    a.mode = MODE_MARG;
+    a.value = value;
+    a.out = marginals;
+    a.grad_gap = grad_gap;
+    a.grad_T = grad_temperature;
+    return launch_nw(a, (cudaStream_t)stream);
+}
+
+int d2p_nw_hvp(const float* scores, const float* tangent, const int* lengths, int B, int L1, int L2, float gap,
+               float temperature, float* hvp, void* workspace, size_t workspace_bytes, void* stream) {
+    if (!nw_dims_ok(B, L1, L2)) return D2P_ERR_TOO_LARGE;
+    if (B == 0) return D2P_OK;
+    if (!scores || !tangent || !hvp) return D2P_ERR_INVALID_ARGUMENT;
+    if (!workspace || workspace_bytes < nw_workspace_bytes(D2P_OP_HVP, B, L1, L2)) return D2P_ERR_WORKSPACE_TOO_SMALL;
+    SwArgs a = nw_args(scores, lengths, B, L1, L2, gap, temperature, workspace);
+    a.mode = MODE_HVP;
+    a.tangent = tangent;
+    a.out = hvp;
+    return launch_nw(a, (cudaStream_t)stream);
+}
+
+int d2p_nw_param_jacobian(const float* scores, const int* lengths, int B, int L1, int L2, int param_type,
+                          float gap, float temperature, float* jacobian, void* workspace,
+                          size_t workspace_bytes, void* stream) {
+    if (!nw_dims_ok(B, L1, L2)) return D2P_ERR_TOO_LARGE;
+    if (param_type != 0 && param_type != 1) return D2P_ERR_INVALID_ARGUMENT;
+    if (B == 0) return D2P_OK;
+    if (!scores || !jacobian) return D2P_ERR_INVALID_ARGUMENT;
+    if (!workspace || workspace_bytes < nw_workspace_bytes(D2P_OP_PARAM_JACOBIAN, B, L1, L2))
+        return D2P_ERR_WORKSPACE_TOO_SMALL;
+    SwArgs a = nw_args(scores, lengths, B, L1, L2, gap, temperature, workspace);
+    a.mode = param_type == 0 ? MODE_PGAP : MODE_PT;
+    a.out = jacobian;
+    return launch_nw(a, (cudaStream_t)stream);
+}
+
+int d2p_nw_backward_full(const float* scores, const float* grad_marginals, const int* lengths, int B, int L1,
+                         int L2, float gap, float temperature, float* grad_scores, float* grad_gap,
+                         float* grad_temperature, void* workspace, size_t workspace_bytes, void* stream) {
+    if (!nw_dims_ok(B, L1, L2)) return D2P_ERR_TOO_LARGE;
+    if (!grad_scores || !grad_gap || !grad_temperature) return D2P_ERR_INVALID_ARGUMENT;
+    cudaStream_t st = (cudaStream_t)stream;
+    if (B == 0) {
+        cudaError_t e1 = cudaMemsetAsync(grad_gap, 0, sizeof(float), st);
+        cudaError_t e2 = cudaMemsetAsync(grad_temperature, 0, sizeof(float), st);
+        return (int)(e1 != cudaSuccess ? e1 : e2);
+    }
+    if (!scores || !grad_marginals) return D2P_ERR_INVALID_ARGUMENT;
+    if (!workspace || workspace_bytes < nw_workspace_bytes(D2P_OP_BACKWARD_FULL, B, L1, L2))
+        return D2P_ERR_WORKSPACE_TOO_SMALL;
+    // grad_scores = H . grad_marginals (the Hessian of S is symmetric);
+    // grad_gap / grad_T = sum grad_marginals * dP/dgap, dP/dT
+    const size_t area = nw::per_problem_bytes(L1, L2, MODE_PT) * (size_t)B;
+    float* partials = (float*)((char*)workspace + ((area + 255) & ~(size_t)255));
+    SwArgs a = nw_args(scores, lengths, B, L1, L2, gap, temperature, workspace);
+    a.mode = MODE_HVP;
+    a.tangent = grad_marginals;
+    a.out = grad_scores;
+    int rc = launch_nw(a, st);
+    if (rc) return rc;
+    a.tangent = nullptr;
+    a.out = nullptr;
+    a.dot_with = grad_marginals;
+    const int modes[2] = {MODE_PGAP, MODE_PT};
+    float* outs[2] = {grad_gap, grad_temperature};
+    for (int q = 0; q < 2; ++q) {
+        a.mode = modes[q];
+        a.dot_out = partials + (size_t)q * B;
+        rc = launch_nw(a, st);
+        if (rc) return rc;
+        rc = launch_sum_batches(partials + (size_t)q * B, 1, B, outs[q], 0, st);
+        if (rc) return rc;
+    }
+    return D2P_OK;
+}
+
+}  // extern "C"

@@ -49,6 +49,7 @@ extern "C" {
 
 #define D2P_FAMILY_LINEAR 0
 #define D2P_FAMILY_AFFINE 1
+#define D2P_FAMILY_NW 2 /* soft Needleman-Wunsch, linear gap (d2p_nw_*) */
 
 #define D2P_OP_FORWARD_BACKWARD 0
 #define D2P_OP_HVP 1
@@ -206,6 +207,27 @@ D2P_API int d2p_wait_selftest(int scope, const int* word, int* status, void* str
 #define D2P_MUFU_PROBE_THREADS 512
 #define D2P_MUFU_PROBE_CHAINS 8
 D2P_API int d2p_mufu_probe(float* out, int blocks, int iters, void* stream);
+
+/* ---- soft Needleman-Wunsch (global alignment, linear gap) ----
+ * The same operator set as the linear soft Smith-Waterman entry points above,
+ * with S = alpha[L1, L2] and marginal = P(the path's diagonal move into
+ * (i, j)); workspace from d2p_sw_workspace_bytes(D2P_FAMILY_NW, op, ...).
+ * They replace the reference's nw launchers (src/nw/kernels.cuh) behind its
+ * soft_nw operators (src/nw/torch_cuda.cpp, src/nw/registry.cpp:35-49). */
+D2P_API int d2p_nw_forward_backward(const float* scores, const int* lengths, int B, int L1, int L2, float gap,
+                                    float temperature, const float* gap_dev, const float* temperature_dev,
+                                    float* value, float* marginals, float* grad_gap, float* grad_temperature,
+                                    void* workspace, size_t workspace_bytes, void* stream);
+D2P_API int d2p_nw_hvp(const float* scores, const float* tangent, const int* lengths, int B, int L1, int L2,
+                       float gap, float temperature, float* hvp, void* workspace, size_t workspace_bytes,
+                       void* stream);
+D2P_API int d2p_nw_param_jacobian(const float* scores, const int* lengths, int B, int L1, int L2, int param_type,
+                                  float gap, float temperature, float* jacobian, void* workspace,
+                                  size_t workspace_bytes, void* stream);
+D2P_API int d2p_nw_backward_full(const float* scores, const float* grad_marginals, const int* lengths, int B,
+                                 int L1, int L2, float gap, float temperature, float* grad_scores,
+                                 float* grad_gap, float* grad_temperature, void* workspace,
+                                 size_t workspace_bytes, void* stream);
 
 /* Engine selection for the whole process (all devices): D2P_ENGINE_AUTO picks
  * per shape (the default, or what D2P_B200_ENGINE names at load: "plane",
