@@ -324,3 +324,101 @@ def sw_affine_backward_full(scores, grad_alignment, lengths=None, gap_open=-2.0,
         jac = sw_affine_param_jacobian(scores, p, lengths, gap_open, gap_ext, T, impl)
         outs.append(np.array([(G * jac).sum()], dt))
     return tuple(outs)
+
+
+# ----------------------------------------------------------------------------
+# Needleman-Wunsch (global alignment, linear gap): nw_oracle.c, or the
+# reference's src/nw/kernels_cpu.cpp; op-level orchestration as
+# src/nw/torch_cpu.cpp:294-520
+# ----------------------------------------------------------------------------
+
+def _nw_call(impl, name_ref, name_oracle):
+    if impl == "ref":
+        return _lib("ref"), name_ref, _F
+    return _lib("oracle"), name_oracle + ("_f64" if impl == "f64" else "_f32"), (_D if impl == "f64" else _F)
+
+
+def nw_linear(scores, lengths=None, gap=-1.0, T=1.0, impl="f32") -> dict:
+    """value, marginals, grad_gap, grad_T (+ alpha) as soft_nw_with_grads."""
+    dt = _dt(impl)
+    s = _arr(scores, dt)
+    B, L1, L2 = s.shape
+    ln = _lens(lengths, B, L1, L2)
+    A = (L1 + 1) * (L2 + 1)
+    alpha = np.zeros((B, A), dt)
+    value = np.zeros(B, dt)
+    beta = np.zeros((B, A), dt)
+    marg = np.zeros((B, L1, L2), dt)
+    gg = np.zeros(B, dt)
+    gT = np.zeros(B, dt)
+    lib, name, R = _nw_call(impl, "nw_forward_cpu", "oracle_nw_forward")
+    if impl == "ref":
+        _fn(lib, name, [_P] * 4 + [_I] * 3 + [_F] * 2)(_ptr(s), _ptr(alpha), _ptr(value), _ptr(ln), B, L1, L2, gap,
+                                                        T)
+        _fn(lib, "nw_backward_cpu", [_P] * 8 + [_I] * 3 + [_F] * 2)(
+            _ptr(alpha), _ptr(s), _ptr(value), _ptr(beta), _ptr(marg), _ptr(gg), _ptr(gT), _ptr(ln), B, L1, L2, gap,
+            T)
+    else:
+        _fn(lib, name, [_P, _P, _I, _I, _I, R, R, _P, _P])(_ptr(s), _ptr(ln), B, L1, L2, gap, T, _ptr(alpha),
+                                                          _ptr(value))
+        g = _fn(lib, name.replace("forward", "backward"), [_P, _P, _I, _I, _I, R, R] + [_P] * 6)
+        g(_ptr(s), _ptr(ln), B, L1, L2, gap, T, _ptr(alpha), _ptr(value), _ptr(beta), _ptr(marg), _ptr(gg), _ptr(gT))
+    return {"value": value, "marginals": marg, "grad_gap": gg, "grad_T": gT, "alpha": alpha}
+
+
+def nw_linear_hvp(scores, V, lengths=None, gap=-1.0, T=1.0, impl="f32") -> np.ndarray:
+    dt = _dt(impl)
+    s = _arr(scores, dt)
+    v = _arr(V, dt)
+    B, L1, L2 = s.shape
+    ln = _lens(lengths, B, L1, L2)
+    A = (L1 + 1) * (L2 + 1)
+    base = nw_linear(s, ln, gap, T, impl)
+    alpha, value = base["alpha"], base["value"]
+    w1, w2, w3 = (np.zeros((B, A), dt) for _ in range(3))
+    H = np.zeros((B, L1, L2), dt)
+    lib, name, R = _nw_call(impl, "nw_hvp_cpu", "oracle_nw_hvp")
+    if impl == "ref":
+        dsc = np.zeros(B, dt)
+        _fn(lib, name, [_P] * 10 + [_I] * 3 + [_F] * 2)(
+            _ptr(alpha), _ptr(s), _ptr(value), _ptr(v), _ptr(w1), _ptr(dsc), _ptr(w2), _ptr(w3), _ptr(H), _ptr(ln),
+            B, L1, L2, gap, T)
+    else:
+        _fn(lib, name, [_P, _P, _P, _I, _I, _I, R, R] + [_P] * 5)(
+            _ptr(s), _ptr(v), _ptr(ln), B, L1, L2, gap, T, _ptr(alpha), _ptr(w1), _ptr(w2), _ptr(w3), _ptr(H))
+    return H
+
+
+def nw_linear_param_jacobian(scores, param_type, lengths=None, gap=-1.0, T=1.0, impl="f32") -> np.ndarray:
+    """dP/dgap (param_type 0) or dP/dT (1), as soft_nw_param_jacobian_cpu."""
+    if param_type not in (0, 1):
+        raise ValueError("param_type must be 0 or 1")
+    dt = _dt(impl)
+    s = _arr(scores, dt)
+    B, L1, L2 = s.shape
+    ln = _lens(lengths, B, L1, L2)
+    base = nw_linear(s, ln, gap, T, impl)
+    dS = base["grad_gap"] if param_type == 0 else base["grad_T"]
+    alpha, value = base["alpha"], base["value"]
+    A = (L1 + 1) * (L2 + 1)
+    w1, w2, w3 = (np.zeros((B, A), dt) for _ in range(3))
+    dP = np.zeros((B, L1, L2), dt)
+    lib, name, R = _nw_call(impl, "nw_param_grad_cpu", "oracle_nw_param_grad")
+    if impl == "ref":
+        _fn(lib, name, [_P] * 9 + [_I] * 3 + [_F] * 2 + [_I])(
+            _ptr(alpha), _ptr(s), _ptr(value), _ptr(dS), _ptr(w1), _ptr(w2), _ptr(w3), _ptr(dP), _ptr(ln), B, L1, L2,
+            gap, T, param_type)
+    else:
+        _fn(lib, name, [_P, _P, _I, _I, _I, R, R] + [_P] * 5 + [_I])(
+            _ptr(s), _ptr(ln), B, L1, L2, gap, T, _ptr(alpha), _ptr(w1), _ptr(w2), _ptr(w3), _ptr(dP), param_type)
+    return dP
+
+
+def nw_linear_backward_full(scores, grad_alignment, lengths=None, gap=-1.0, T=1.0, impl="f32"):
+    """(grad_scores, grad_gap[1], grad_T[1]) as soft_nw_backward_full_cpu (torch_cpu.cpp:430-520)."""
+    dt = _dt(impl)
+    G = _arr(grad_alignment, dt)
+    gs = nw_linear_hvp(scores, G, lengths, gap, T, impl)
+    jg = nw_linear_param_jacobian(scores, 0, lengths, gap, T, impl)
+    jt = nw_linear_param_jacobian(scores, 1, lengths, gap, T, impl)
+    return gs, np.array([(G * jg).sum()], dt), np.array([(G * jt).sum()], dt)

@@ -30,9 +30,14 @@
 #ifdef ORACLE_F64
 #define REAL double
 #define SFX(name) name##_f64
+#define R_EXP exp
+#define R_LOG log
 #else
 #define REAL float
 #define SFX(name) name##_f32
+/* float exp / log as the reference calls them (std::exp, std::log on float) */
+#define R_EXP expf
+#define R_LOG logf
 #endif
 
 #define O_NINF ((REAL)-1e30)
@@ -52,7 +57,7 @@ static inline void kahan_add(kahan_t *k, REAL v) {
 static inline REAL o_safe_exp(REAL x) {
     if (x < (REAL)-88) return (REAL)0;
     if (x > (REAL)88) x = (REAL)88;
-    return (REAL)exp((double)x);
+    return R_EXP(x);
 }
 
 static inline REAL o_max2(REAL a, REAL b) { return a > b ? a : b; }
@@ -68,7 +73,7 @@ static inline REAL o_lse2(REAL a, REAL b, REAL T) {
     kahan_t k = {0, 0};
     kahan_add(&k, o_safe_exp((a - m) / T));
     kahan_add(&k, o_safe_exp((b - m) / T));
-    return m + T * (REAL)log((double)k.sum);
+    return m + T * R_LOG(k.sum);
 }
 
 static inline REAL o_lse4(REAL a, REAL b, REAL c, REAL d, REAL T) {
@@ -79,7 +84,7 @@ static inline REAL o_lse4(REAL a, REAL b, REAL c, REAL d, REAL T) {
     kahan_add(&k, o_safe_exp((b - m) / T));
     kahan_add(&k, o_safe_exp((c - m) / T));
     kahan_add(&k, o_safe_exp((d - m) / T));
-    return m + T * (REAL)log((double)k.sum);
+    return m + T * R_LOG(k.sum);
 }
 
 /* softmax weights with -inf options forced to 0
@@ -154,7 +159,7 @@ static REAL lin_forward_one(const REAL *s, REAL *a, int L1, int L2, int L1max,
     for (int i = 0; i <= L1; ++i)
         for (int j = 0; j <= L2; ++j)
             if (a[AIDX(i, j)] > O_NINF) kahan_add(&z, o_safe_exp((a[AIDX(i, j)] - m) / T));
-    return m + T * (REAL)log((double)z.sum);
+    return m + T * R_LOG(z.sum);
 }
 
 /* Backward for one problem: src/sw/kernels_cpu.cpp:156-279. */
@@ -413,7 +418,7 @@ static REAL aff_forward_one(const REAL *s, REAL *a, int L1, int L2, int L1max, i
                 REAL val = a[st * plane + AIDX(i, j)];
                 if (val > O_NINF) kahan_add(&z, o_safe_exp((val - m) / T));
             }
-    return m + T * (REAL)log((double)z.sum);
+    return m + T * R_LOG(z.sum);
 }
 
 /* src/sw_affine/kernels_cpu.cpp:199-346 */

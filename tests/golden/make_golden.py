@@ -1,6 +1,7 @@
 """Generate the golden fixtures in tests/golden/ from the REFERENCE's own CPU
-kernels (src/sw/kernels_cpu.cpp, src/sw_affine/kernels_cpu.cpp compiled from the
-reference sources into oracle/_ref/libref_sw_cpu.so by oracle/Makefile).
+kernels (src/sw/kernels_cpu.cpp, src/sw_affine/kernels_cpu.cpp,
+src/nw/kernels_cpu.cpp compiled from the reference sources into
+oracle/_ref/libref_sw_cpu.so by oracle/Makefile).
 
 Run in a container where the reference sources are present:
     make -C oracle && python tests/golden/make_golden.py
@@ -25,6 +26,11 @@ CASES = [
     ("ragged_t05", 3, 12, 10, 0.5, -0.5, (-1.7, -0.4), True),
     ("sharp_t01", 2, 6, 11, 0.1, -1.0, (-2.0, -0.5), False),
     ("row1", 2, 1, 8, 1.0, -1.0, (-2.0, -0.5), False),
+]
+
+# Needleman-Wunsch only (files named nw_*): name, B, L1, L2, T, gap, lengths
+NW_CASES = [
+    ("nw_edges", 6, 9, 7, 0.8, -0.7, [[9, 7], [0, 7], [9, 0], [0, 0], [1, 7], [9, 1]]),
 ]
 
 
@@ -60,8 +66,33 @@ def main():
             out[f"aff_jac{p}"] = oracle.sw_affine_param_jacobian(s, p, ln, go, ge, T, "ref")
         bf = oracle.sw_affine_backward_full(s, G, ln, go, ge, T, "ref")
         out["aff_bf_scores"], out["aff_bf_open"], out["aff_bf_ext"], out["aff_bf_T"] = bf
+        out.update(_nw_outputs(s, V, G, ln, gap, T))
         np.savez_compressed(os.path.join(HERE, name + ".npz"), **out)
         print("wrote", name)
+    # Needleman-Wunsch edge cases: empty sequences (lengths 0 on either side)
+    # and a single row / column
+    for name, B, L1, L2, T, gap, lens in NW_CASES:
+        g = torch.Generator().manual_seed(zlib.crc32(name.encode()))
+        s = torch.randn(B, L1, L2, generator=g).numpy()
+        V = torch.randn(B, L1, L2, generator=g).numpy()
+        G = torch.randn(B, L1, L2, generator=g).numpy()
+        ln = np.array(lens, np.int32)
+        out = dict(scores=s, tangent=V, grad_marginals=G, T=np.float32(T), gap=np.float32(gap), lengths=ln)
+        out.update(_nw_outputs(s, V, G, ln, gap, T))
+        np.savez_compressed(os.path.join(HERE, name + ".npz"), **out)
+        print("wrote", name)
+
+
+def _nw_outputs(s, V, G, ln, gap, T):
+    out = {}
+    r = oracle.nw_linear(s, ln, gap, T, "ref")
+    for k in ("value", "marginals", "grad_gap", "grad_T"):
+        out["nw_" + k] = r[k]
+    out["nw_hvp"] = oracle.nw_linear_hvp(s, V, ln, gap, T, "ref")
+    out["nw_jac0"] = oracle.nw_linear_param_jacobian(s, 0, ln, gap, T, "ref")
+    out["nw_jac1"] = oracle.nw_linear_param_jacobian(s, 1, ln, gap, T, "ref")
+    out["nw_bf_scores"], out["nw_bf_gap"], out["nw_bf_T"] = oracle.nw_linear_backward_full(s, G, ln, gap, T, "ref")
+    return out
 
 
 if __name__ == "__main__":

@@ -10,7 +10,10 @@ import pytest
 
 import oracle
 
-GOLDEN = sorted(glob.glob(os.path.join(os.path.dirname(__file__), "golden", "*.npz")))
+ALL = sorted(glob.glob(os.path.join(os.path.dirname(__file__), "golden", "*.npz")))
+# Smith-Waterman fixtures; files named nw_* hold Needleman-Wunsch cases only
+GOLDEN = [p for p in ALL if not os.path.basename(p).startswith("nw_")]
+NW_GOLDEN = [p for p in ALL if "nw_value" in np.load(p).files]
 
 
 def _load(path):
@@ -30,6 +33,7 @@ def _close(a, b, rtol, atol, what):
 
 def test_fixtures_present():
     assert len(GOLDEN) >= 4
+    assert len(NW_GOLDEN) >= 5
 
 
 @pytest.mark.parametrize("path", GOLDEN, ids=[os.path.basename(p) for p in GOLDEN])
@@ -104,3 +108,33 @@ def test_oracle_semantics_value_includes_origin():
     assert abs(r["value"][0] - np.log(1 + np.exp(x))) < 1e-12
     r0 = oracle.sw_linear(s, np.array([[0, 1]], np.int32), -1.0, 1.0, "f64")
     assert r0["value"][0] == 0.0 and np.all(r0["marginals"] == 0)
+
+
+@pytest.mark.parametrize("path", NW_GOLDEN, ids=[os.path.basename(p) for p in NW_GOLDEN])
+def test_nw_restatement_matches_reference_golden(path):
+    """nw_oracle.c reproduces the reference's src/nw/kernels_cpu.cpp bit for bit
+    (same operation order), including empty sequences on either side."""
+    d = _load(path)
+    s, ln, gap, T = d["scores"], d["lengths"], float(d["gap"]), float(d["T"])
+    r = oracle.nw_linear(s, ln, gap, T, "f32")
+    for k in ("value", "marginals", "grad_gap", "grad_T"):
+        _close(r[k], d["nw_" + k], 0, 0, k)
+    _close(oracle.nw_linear_hvp(s, d["tangent"], ln, gap, T, "f32"), d["nw_hvp"], 0, 0, "hvp")
+    for p in (0, 1):
+        _close(oracle.nw_linear_param_jacobian(s, p, ln, gap, T, "f32"), d[f"nw_jac{p}"], 0, 0, f"jac{p}")
+    bf = oracle.nw_linear_backward_full(s, d["grad_marginals"], ln, gap, T, "f32")
+    _close(bf[0], d["nw_bf_scores"], 0, 0, "bf scores")
+    _close(bf[1], d["nw_bf_gap"], 1e-6, 1e-7, "bf gap")
+    _close(bf[2], d["nw_bf_T"], 1e-6, 1e-7, "bf T")
+    # the double build agrees to fp32 accuracy, and the closed forms hold:
+    # dS/dgap = L1 + L2 - 2 sum(marginals) (every global path with m diagonal
+    # cells has L1 + L2 - 2m gaps), dS/dT = (S - sum s mu - gap dS/dgap) / T
+    r64 = oracle.nw_linear(s, ln, gap, T, "f64")
+    _close(r64["value"], d["nw_value"], 1e-5, 1e-5, "f64 value")
+    _close(r64["marginals"], d["nw_marginals"], 1e-4, 1e-5, "f64 marginals")
+    B, L1, L2 = s.shape
+    lens = np.tile([L1, L2], (B, 1)) if ln is None else ln
+    mu = r64["marginals"]
+    _close(r64["grad_gap"], lens.sum(1) - 2 * mu.sum((1, 2)), 1e-9, 1e-9, "dS/dgap closed form")
+    _close(r64["grad_T"], (r64["value"] - (s * mu).sum((1, 2)) - gap * r64["grad_gap"]) / T, 1e-9, 1e-9,
+           "dS/dT closed form")
