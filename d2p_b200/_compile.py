@@ -1,4 +1,5 @@
-"""Fake-tensor (meta) shapes and autocast rules for the soft Smith-Waterman ops.
+"""Fake-tensor (meta) shapes and autocast rules for the soft Smith-Waterman and
+linear soft Needleman-Wunsch ops.
 
 Mirrors d2p/_compile.py:18-250 (register_fake) and :857-901 (register_autocast)
 for the sw / sw_affine families.  Output shapes per op:
@@ -54,6 +55,20 @@ _OUTPUTS = {
     "sw_affine_marginals_grad_gap_open": _P,
     "sw_affine_marginals_grad_gap_ext": _P,
     "sw_affine_marginals_grad_temp": _P,
+    # soft Needleman-Wunsch, linear gap (d2p/_compile.py:257-308)
+    "soft_nw": [_B, _P],
+    "soft_nw_float": [_B, _P],
+    "soft_nw_with_grads": (_B, _P, _B, _B),
+    "soft_nw_hvp": _P,
+    "soft_nw_param_jacobian": _P,
+    "soft_nw_backward_full": (_P, _ONE, _ONE),
+    "nw_forward": [_B, _P],
+    "nw_forward_t": [_B, _P],
+    "nw_value_grad_params": (_B, _B),
+    "nw_marginals_backward": (_P, _ONE, _ONE),
+    "nw_marginals_hvp": _P,
+    "nw_marginals_grad_gap": _P,
+    "nw_marginals_grad_temp": _P,
 }
 
 

@@ -1,7 +1,8 @@
 """Low-level operator access: loads the native libraries and wraps torch.ops.d2p.*.
 
-Mirrors d2p/_ops.py (loader :25-167, soft Smith-Waterman wrappers :170-210) for
-the soft Smith-Waterman family.  The extension is in-tree (``_C.so`` next to this
+Mirrors d2p/_ops.py (loader :25-167, soft Smith-Waterman wrappers :170-210,
+soft Needleman-Wunsch wrappers :241-246) for the soft Smith-Waterman family and
+the linear soft Needleman-Wunsch operators.  The extension is in-tree (``_C.so`` next to this
 file, linked to ``libd2p_b200.so``); there is no CPU kernel and no fallback:
 importing fails loudly when the extension is missing, and CPU tensors are
 rejected by the ops themselves.
@@ -150,6 +151,21 @@ sw_affine_marginals_grad_gap_open = _wrap("sw_affine_marginals_grad_gap_open")
 sw_affine_marginals_grad_gap_ext = _wrap("sw_affine_marginals_grad_gap_ext")
 sw_affine_marginals_grad_temp = _wrap("sw_affine_marginals_grad_temp")
 
+# Needleman-Wunsch (linear gap)
+soft_nw = _wrap("soft_nw")
+soft_nw_float = _wrap("soft_nw_float")
+soft_nw_with_grads = _wrap("soft_nw_with_grads")
+soft_nw_hvp = _wrap("soft_nw_hvp")
+soft_nw_param_jacobian = _wrap("soft_nw_param_jacobian")
+soft_nw_backward_full = _wrap("soft_nw_backward_full")
+nw_forward = _wrap("nw_forward")
+nw_forward_t = _wrap("nw_forward_t")
+nw_value_grad_params = _wrap("nw_value_grad_params")
+nw_marginals_backward = _wrap("nw_marginals_backward")
+nw_marginals_hvp = _wrap("nw_marginals_hvp")
+nw_marginals_grad_gap = _wrap("nw_marginals_grad_gap")
+nw_marginals_grad_temp = _wrap("nw_marginals_grad_temp")
+
 OP_NAMES = (
     "soft_sw", "soft_sw_float", "soft_sw_with_grads", "soft_sw_hvp", "soft_sw_param_jacobian",
     "soft_sw_backward_full", "sw_forward", "sw_forward_t", "sw_value_grad_params",
@@ -159,4 +175,7 @@ OP_NAMES = (
     "sw_affine_forward_t", "sw_affine_value_grad_params", "sw_affine_marginals_backward",
     "sw_affine_marginals_hvp", "sw_affine_marginals_grad_gap_open", "sw_affine_marginals_grad_gap_ext",
     "sw_affine_marginals_grad_temp",
+    "soft_nw", "soft_nw_float", "soft_nw_with_grads", "soft_nw_hvp", "soft_nw_param_jacobian",
+    "soft_nw_backward_full", "nw_forward", "nw_forward_t", "nw_value_grad_params", "nw_marginals_backward",
+    "nw_marginals_hvp", "nw_marginals_grad_gap", "nw_marginals_grad_temp",
 )

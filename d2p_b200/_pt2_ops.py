@@ -1,6 +1,7 @@
 """PT2-safe custom ops (``d2p_py::*``) used while compiling or on fake tensors.
 
-Mirrors the soft Smith-Waterman part of d2p/_pt2_ops.py:72-487: each op wraps
+Mirrors the soft Smith-Waterman and linear soft Needleman-Wunsch parts of
+d2p/_pt2_ops.py:72-570: each op wraps
 the dispatcher op, carries a fake implementation, and the differentiable ones
 (``soft_sw``, ``soft_sw_float``, affine analogues) register an autograd formula
 built from the saved marginals (value branch) and ``*_backward_full`` (marginal
@@ -44,147 +45,142 @@ def _like(scores, *kinds):
 
 
 # --------------------------------------------------------------------------- linear
-@custom_op("d2p_py::soft_sw_with_grads", mutates_args=())
-def soft_sw_with_grads(scores: torch.Tensor, gap: float, temperature: float,
-                       lengths: Optional[torch.Tensor]) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
-    v, m, gg, gt = torch.ops.d2p.soft_sw_with_grads(scores, gap, temperature, lengths)
-    return v, m, gg, gt
+# The linear-gap Smith-Waterman ops (prefix "soft_sw") and the Needleman-Wunsch
+# ops (prefix "soft_nw", d2p/_pt2_ops.py:495-570) have the same schemas and
+# autograd formulas; one factory builds both sets.
+def _make_linear_family(prefix: str):
+    raw = torch.ops.d2p
+
+    @custom_op(f"d2p_py::{prefix}_with_grads", mutates_args=())
+    def with_grads(scores: torch.Tensor, gap: float, temperature: float,
+                   lengths: Optional[torch.Tensor]) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+        v, m, gg, gt = getattr(raw, f"{prefix}_with_grads")(scores, gap, temperature, lengths)
+        return v, m, gg, gt
+
+    @with_grads.register_fake
+    def _(scores, gap, temperature, lengths):
+        return _like(scores, "B", "P", "B", "B")
+
+    @custom_op(f"d2p_py::{prefix}_hvp", mutates_args=())
+    def hvp(scores: torch.Tensor, tangent: torch.Tensor, gap: float, temperature: float,
+            lengths: Optional[torch.Tensor]) -> torch.Tensor:
+        return getattr(raw, f"{prefix}_hvp")(scores, tangent, gap, temperature, lengths)
+
+    @hvp.register_fake
+    def _(scores, tangent, gap, temperature, lengths):
+        return _like(scores, "P")
+
+    @custom_op(f"d2p_py::{prefix}_param_jacobian", mutates_args=())
+    def param_jacobian(scores: torch.Tensor, param_type: int, gap: float, temperature: float,
+                       lengths: Optional[torch.Tensor]) -> torch.Tensor:
+        return getattr(raw, f"{prefix}_param_jacobian")(scores, param_type, gap, temperature, lengths)
+
+    @param_jacobian.register_fake
+    def _(scores, param_type, gap, temperature, lengths):
+        return _like(scores, "P")
+
+    @custom_op(f"d2p_py::{prefix}_backward_full", mutates_args=())
+    def backward_full(scores: torch.Tensor, grad_alignment: torch.Tensor, gap: float, temperature: float,
+                      lengths: Optional[torch.Tensor]) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        a, b, c = getattr(raw, f"{prefix}_backward_full")(scores, grad_alignment, gap, temperature, lengths)
+        return a, b, c
+
+    @backward_full.register_fake
+    def _(scores, grad_alignment, gap, temperature, lengths):
+        return _like(scores, "P", "1", "1")
+
+    @custom_op(f"d2p_py::{prefix}", mutates_args=())
+    def tensor_op(scores: torch.Tensor, gap: torch.Tensor, temperature: torch.Tensor,
+                  lengths: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        v, m = getattr(raw, prefix)(scores, gap, temperature, lengths)
+        return v, m
+
+    @tensor_op.register_fake
+    def _(scores, gap, temperature, lengths):
+        return _like(scores, "B", "P")
+
+    # The backward of the tensor-parameter op needs the parameters' values as
+    # scalars.  Read while tracing, they would be frozen into the compiled
+    # graph (or be data-dependent), so the backward formula calls these ops,
+    # which take the parameters as tensors and read them only when they run.
+    @custom_op(f"d2p_py::{prefix}_param_grads_t", mutates_args=())
+    def param_grads_t(scores: torch.Tensor, gap: torch.Tensor, temperature: torch.Tensor,
+                      lengths: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        _, _, dgap, dt = getattr(raw, f"{prefix}_with_grads")(scores, float(gap), float(temperature), lengths)
+        return dgap, dt
+
+    @param_grads_t.register_fake
+    def _(scores, gap, temperature, lengths):
+        return _like(scores, "B", "B")
+
+    @custom_op(f"d2p_py::{prefix}_backward_full_t", mutates_args=())
+    def backward_full_t(scores: torch.Tensor, grad_alignment: torch.Tensor, gap: torch.Tensor,
+                        temperature: torch.Tensor,
+                        lengths: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        a, b, c = getattr(raw, f"{prefix}_backward_full")(scores, grad_alignment, float(gap), float(temperature),
+                                                           lengths)
+        return a, b, c
+
+    @backward_full_t.register_fake
+    def _(scores, grad_alignment, gap, temperature, lengths):
+        return _like(scores, "P", "1", "1")
+
+    def tensor_setup(ctx, inputs, output):
+        scores, gap, temperature, lengths = inputs
+        ctx.save_for_backward(scores, output[1], gap.detach(), temperature.detach())
+        ctx.lengths = lengths
+
+    def tensor_backward(ctx, grad_value, grad_marg):
+        scores, marg, gap, temperature = ctx.saved_tensors
+        grad_scores = _expand_batch(grad_value, marg)
+        need_gap, need_t = ctx.needs_input_grad[1], ctx.needs_input_grad[2]
+        g_gap = g_t = None
+        if grad_value is not None and (need_gap or need_t):
+            dgap, dt = param_grads_t(scores, gap, temperature, ctx.lengths)
+            g_gap = _batch_dot(grad_value, dgap) if need_gap else None
+            g_t = _batch_dot(grad_value, dt) if need_t else None
+        if grad_marg is not None:
+            gs, gg, gt = backward_full_t(scores, grad_marg, gap, temperature, ctx.lengths)
+            grad_scores = _add(grad_scores, gs)
+            g_gap = _add(g_gap, gg) if need_gap else None
+            g_t = _add(g_t, gt) if need_t else None
+        return grad_scores, g_gap, g_t, None
+
+    tensor_op.register_autograd(tensor_backward, setup_context=tensor_setup)
+
+    @custom_op(f"d2p_py::{prefix}_float", mutates_args=())
+    def float_op(scores: torch.Tensor, gap: float, temperature: float,
+                 lengths: Optional[torch.Tensor]) -> tuple[torch.Tensor, torch.Tensor]:
+        v, m = getattr(raw, f"{prefix}_float")(scores, gap, temperature, lengths)
+        return v, m
+
+    @float_op.register_fake
+    def _(scores, gap, temperature, lengths):
+        return _like(scores, "B", "P")
+
+    def float_setup(ctx, inputs, output):
+        scores, gap, temperature, lengths = inputs
+        ctx.save_for_backward(scores, output[1])
+        ctx.gap, ctx.temperature, ctx.lengths = gap, temperature, lengths
+
+    def float_backward(ctx, grad_value, grad_marg):
+        scores, marg = ctx.saved_tensors
+        grad_scores = _expand_batch(grad_value, marg)
+        if grad_marg is not None:
+            gs, _, _ = backward_full(scores, grad_marg, ctx.gap, ctx.temperature, ctx.lengths)
+            grad_scores = _add(grad_scores, gs)
+        return grad_scores, None, None, None
+
+    float_op.register_autograd(float_backward, setup_context=float_setup)
+    return {
+        prefix: tensor_op, f"{prefix}_float": float_op, f"{prefix}_with_grads": with_grads,
+        f"{prefix}_hvp": hvp, f"{prefix}_param_jacobian": param_jacobian, f"{prefix}_backward_full": backward_full,
+        f"{prefix}_param_grads_t": param_grads_t, f"{prefix}_backward_full_t": backward_full_t,
+    }
 
 
-@soft_sw_with_grads.register_fake
-def _(scores, gap, temperature, lengths):
-    return _like(scores, "B", "P", "B", "B")
-
-
-@custom_op("d2p_py::soft_sw_hvp", mutates_args=())
-def soft_sw_hvp(scores: torch.Tensor, tangent: torch.Tensor, gap: float, temperature: float,
-                lengths: Optional[torch.Tensor]) -> torch.Tensor:
-    return torch.ops.d2p.soft_sw_hvp(scores, tangent, gap, temperature, lengths)
-
-
-@soft_sw_hvp.register_fake
-def _(scores, tangent, gap, temperature, lengths):
-    return _like(scores, "P")
-
-
-@custom_op("d2p_py::soft_sw_param_jacobian", mutates_args=())
-def soft_sw_param_jacobian(scores: torch.Tensor, param_type: int, gap: float, temperature: float,
-                           lengths: Optional[torch.Tensor]) -> torch.Tensor:
-    return torch.ops.d2p.soft_sw_param_jacobian(scores, param_type, gap, temperature, lengths)
-
-
-@soft_sw_param_jacobian.register_fake
-def _(scores, param_type, gap, temperature, lengths):
-    return _like(scores, "P")
-
-
-@custom_op("d2p_py::soft_sw_backward_full", mutates_args=())
-def soft_sw_backward_full(scores: torch.Tensor, grad_alignment: torch.Tensor, gap: float,
-                          temperature: float, lengths: Optional[torch.Tensor]) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
-    a, b, c = torch.ops.d2p.soft_sw_backward_full(scores, grad_alignment, gap, temperature, lengths)
-    return a, b, c
-
-
-@soft_sw_backward_full.register_fake
-def _(scores, grad_alignment, gap, temperature, lengths):
-    return _like(scores, "P", "1", "1")
-
-
-@custom_op("d2p_py::soft_sw", mutates_args=())
-def soft_sw(scores: torch.Tensor, gap: torch.Tensor, temperature: torch.Tensor,
-            lengths: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-    v, m = torch.ops.d2p.soft_sw(scores, gap, temperature, lengths)
-    return v, m
-
-
-@soft_sw.register_fake
-def _(scores, gap, temperature, lengths):
-    return _like(scores, "B", "P")
-
-
-# The backward of the tensor-parameter ops needs the parameters' values as
-# scalars.  Read while tracing, they would be frozen into the compiled graph
-# (or be data-dependent), so the backward formulas call these ops, which take
-# the parameters as tensors and read them only when they run.
-@custom_op("d2p_py::soft_sw_param_grads_t", mutates_args=())
-def soft_sw_param_grads_t(scores: torch.Tensor, gap: torch.Tensor, temperature: torch.Tensor,
-                          lengths: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-    _, _, dgap, dt = torch.ops.d2p.soft_sw_with_grads(scores, float(gap), float(temperature), lengths)
-    return dgap, dt
-
-
-@soft_sw_param_grads_t.register_fake
-def _(scores, gap, temperature, lengths):
-    return _like(scores, "B", "B")
-
-
-@custom_op("d2p_py::soft_sw_backward_full_t", mutates_args=())
-def soft_sw_backward_full_t(scores: torch.Tensor, grad_alignment: torch.Tensor, gap: torch.Tensor,
-                            temperature: torch.Tensor,
-                            lengths: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
-    a, b, c = torch.ops.d2p.soft_sw_backward_full(scores, grad_alignment, float(gap), float(temperature), lengths)
-    return a, b, c
-
-
-@soft_sw_backward_full_t.register_fake
-def _(scores, grad_alignment, gap, temperature, lengths):
-    return _like(scores, "P", "1", "1")
-
-
-def _soft_sw_setup(ctx, inputs, output):
-    scores, gap, temperature, lengths = inputs
-    ctx.save_for_backward(scores, output[1], gap.detach(), temperature.detach())
-    ctx.lengths = lengths
-
-
-def _soft_sw_backward(ctx, grad_value, grad_marg):
-    scores, marg, gap, temperature = ctx.saved_tensors
-    grad_scores = _expand_batch(grad_value, marg)
-    need_gap, need_t = ctx.needs_input_grad[1], ctx.needs_input_grad[2]
-    g_gap = g_t = None
-    if grad_value is not None and (need_gap or need_t):
-        dgap, dt = soft_sw_param_grads_t(scores, gap, temperature, ctx.lengths)
-        g_gap = _batch_dot(grad_value, dgap) if need_gap else None
-        g_t = _batch_dot(grad_value, dt) if need_t else None
-    if grad_marg is not None:
-        gs, gg, gt = soft_sw_backward_full_t(scores, grad_marg, gap, temperature, ctx.lengths)
-        grad_scores = _add(grad_scores, gs)
-        g_gap = _add(g_gap, gg) if need_gap else None
-        g_t = _add(g_t, gt) if need_t else None
-    return grad_scores, g_gap, g_t, None
-
-
-soft_sw.register_autograd(_soft_sw_backward, setup_context=_soft_sw_setup)
-
-
-@custom_op("d2p_py::soft_sw_float", mutates_args=())
-def soft_sw_float(scores: torch.Tensor, gap: float, temperature: float,
-                  lengths: Optional[torch.Tensor]) -> tuple[torch.Tensor, torch.Tensor]:
-    v, m = torch.ops.d2p.soft_sw_float(scores, gap, temperature, lengths)
-    return v, m
-
-
-@soft_sw_float.register_fake
-def _(scores, gap, temperature, lengths):
-    return _like(scores, "B", "P")
-
-
-def _soft_sw_float_setup(ctx, inputs, output):
-    scores, gap, temperature, lengths = inputs
-    ctx.save_for_backward(scores, output[1])
-    ctx.gap, ctx.temperature, ctx.lengths = gap, temperature, lengths
-
-
-def _soft_sw_float_backward(ctx, grad_value, grad_marg):
-    scores, marg = ctx.saved_tensors
-    grad_scores = _expand_batch(grad_value, marg)
-    if grad_marg is not None:
-        gs, _, _ = soft_sw_backward_full(scores, grad_marg, ctx.gap, ctx.temperature, ctx.lengths)
-        grad_scores = _add(grad_scores, gs)
-    return grad_scores, None, None, None
-
-
-soft_sw_float.register_autograd(_soft_sw_float_backward, setup_context=_soft_sw_float_setup)
+globals().update(_make_linear_family("soft_sw"))
+globals().update(_make_linear_family("soft_nw"))
 
 
 # --------------------------------------------------------------------------- affine

@@ -10,10 +10,13 @@
 //   S = alpha[L1, L2];  w_k = exp((v_k - alpha[i,j]) / T) normalised by their sum.
 // The reverse is the flow of the path distribution: beta[L1,L2] = 1 and
 // beta[c] = sum over the successors d of c of beta[d] w_{c->d}(d); the marginal
-// of cell (i,j) is beta[i,j] w_diag(i,j).  Every global path with m diagonal
-// cells has L1 + L2 - 2 m gap cells, so dS/dgap = E[gaps] = L1 + L2 - 2 sum mu
-// exactly, and dS/dT = (S - sum s mu - gap dS/dgap) / T (S is homogeneous of
-// degree 1 in (s, gap, T)).
+// of cell (i,j) is beta[i,j] w_diag(i,j).  dS/dgap = E[gaps] = the flow
+// through gap moves (beta (w_up + w_left) per cell, plus k gaps for a path
+// that reaches the boundary cell (i, 0) or (0, j), k = i + j), and dS/dT =
+// (S - E[path score]) / T is the entropy of the path distribution: the sum of
+// each cell's choice entropy -sum w ln w weighted by beta (equal to the
+// reference's (S - sum s mu - gap dS/dgap) / T, src/nw/kernels_cpu.cpp:161-262,
+// without its cancellation).
 //
 // Tangents along a direction (V in the scores, or gap, or T): the forward
 // carries d alpha = sum_k w_k dv_k (+ (alpha - E[v]) / T along T), the
@@ -26,7 +29,8 @@
 // diagonal.  Per-cell values live in diagonal-major planes in the workspace
 // ([k][i]: one diagonal is contiguous, so its loads and stores coalesce):
 // alpha and the three normalised weights from the forward, beta from the
-// reverse, and for a tangent its forward and reverse values.  The reverse is a
+// reverse, and for a tangent its forward and reverse values.  alpha and the
+// forward tangent are stored relative to an integer frame per diagonal.  The reverse is a
 // gather over the successors (no atomics: deterministic).  A general engine:
 // any size, every mode; per-problem sums are block reductions in fp64.
 #include <math.h>
@@ -42,23 +46,28 @@ namespace nw {
 
 constexpr int kThreads = 256;
 
-// planes of one problem, each (L1m + L2m + 1) (L1m + 1) floats
+// planes of one problem, each (L1m + L2m + 1) (L1m + 1) floats, then the
+// frames of the diagonals (alpha's and the forward tangent's), L1m + L2m + 1
+// floats each
 enum Plane : int { kA = 0, kWd, kWu, kWl, kB, kT1, kT2, kT3, kNumPlanes };
 __host__ __device__ inline size_t plane_floats(int L1m, int L2m) {
     return ((size_t)L1m + L2m + 1) * ((size_t)L1m + 1);
 }
 __host__ __device__ inline int planes_for(int mode) {
-    // MARG: alpha, weights, beta; HVP / PGAP: + the forward tangent and the
-    // reverse tangent; PT: + E[v] as well
-    return mode == MODE_MARG ? 5 : (mode == MODE_PT ? 8 : 7);
+    // MARG: alpha, weights, beta, each cell's choice entropy; HVP / PGAP:
+    // alpha, weights, beta, the forward tangent and the reverse tangent; PT:
+    // + E[v] as well
+    return mode == MODE_MARG ? 6 : (mode == MODE_PT ? 8 : 7);
 }
 __host__ __device__ inline size_t per_problem_bytes(int L1m, int L2m, int mode) {
-    const size_t b = plane_floats(L1m, L2m) * sizeof(float) * planes_for(mode);
+    const size_t b = (plane_floats(L1m, L2m) * planes_for(mode) + 2 * ((size_t)L1m + L2m + 1)) * sizeof(float);
     return (b + 255) & ~(size_t)255;
 }
 
 struct Ctx {
     float* p[kNumPlanes];
+    float* O;     // alpha's frame of each diagonal (integer-valued): alpha = A + O[k]
+    float* D;     // the forward tangent's: dalpha = F + D[k]
     int stride;   // L1m + 1
     __device__ float& at(int plane, int k, int i) const { return p[plane][(size_t)k * stride + i]; }
 };
@@ -80,6 +89,14 @@ __device__ __forceinline__ double block_sum(double v, double* red) {
 // One CTA per problem.  MODE: MODE_MARG (value, marginals, dS/dgap, dS/dT),
 // MODE_HVP (out = d marginals along p.tangent), MODE_PGAP / MODE_PT (out =
 // dP/dtheta; with dot_with, dot_out[b] = sum dot_with * dP/dtheta).
+//
+// Frames.  alpha grows along the diagonals (about k gap on diagonal k), so it
+// is stored as A = alpha - O[k], with O[k] an integer-valued float taken from
+// the previous diagonal's middle cell: every option v - alpha is then formed
+// from small stored values plus an exact difference of frames, instead of as
+// a difference of two large rounded numbers.  The forward tangent (which grows
+// like the expected number of gaps, or the path's sum of V) keeps a frame D[k]
+// the same way.
 template <int MODE>
 __global__ void __launch_bounds__(kThreads) nw_kernel(SwArgs p) {
     __shared__ double red[32];
@@ -100,11 +117,14 @@ __global__ void __launch_bounds__(kThreads) nw_kernel(SwArgs p) {
         float* base = reinterpret_cast<float*>(reinterpret_cast<char*>(p.ws) + (size_t)b * per_problem_bytes(L1m, L2m, MODE));
         const size_t pf = plane_floats(L1m, L2m);
         for (int q = 0; q < kNumPlanes; ++q) C.p[q] = q < planes_for(MODE) ? base + (size_t)q * pf : nullptr;
+        C.O = base + pf * planes_for(MODE);
+        C.D = C.O + (L1m + L2m + 1);
         C.stride = L1m + 1;
     }
     const bool TAN = MODE != MODE_MARG;
     // the forward tangent (dalpha, or U) and the reverse tangent (dbeta, or W)
     const int kF = kT1, kR = kT2, kEv = kT3;
+    const int K = L1 + L2;   // the end cell's diagonal
 
     // padding of the output: zeros outside the problem
     if (out) {
@@ -113,29 +133,34 @@ __global__ void __launch_bounds__(kThreads) nw_kernel(SwArgs p) {
             if (i >= L1 || j >= L2) out[e] = 0.f;
         }
     }
-    // boundary cells: alpha = index x gap; the gap tangent is the index
-    for (int q = threadIdx.x; q <= max(L1, L2); q += blockDim.x) {
-        if (q <= L1) {   // (q, 0)
-            C.at(kA, q, q) = (float)q * gap;
-            if (TAN) C.at(kF, q, q) = MODE == MODE_PGAP ? (float)q : 0.f;
-        }
-        if (q >= 1 && q <= L2) {   // (0, q)
-            C.at(kA, q, 0) = (float)q * gap;
-            if (TAN) C.at(kF, q, 0) = MODE == MODE_PGAP ? (float)q : 0.f;
-        }
-    }
-    __syncthreads();
 
     // ------------------------------------------------------------- forward
-    for (int k = 2; k <= L1 + L2; ++k) {
-        const int i0 = max(1, k - L2), i1 = min(L1, k - 1);
+    float O1 = 0.f, O2 = 0.f, D1 = 0.f, D2 = 0.f;   // frames of diagonals k-1, k-2
+    for (int k = 0; k <= K; ++k) {
+        float Ok = 0.f, Dk = 0.f;
+        if (k >= 2) {   // from the previous diagonal's middle cell (the same value in every thread)
+            const int im = (max(0, k - 1 - L2) + min(L1, k - 1)) >> 1;
+            Ok = O1 + rintf(C.at(kA, k - 1, im));
+            if (TAN) Dk = D1 + rintf(C.at(kF, k - 1, im));
+        }
+        if (threadIdx.x == 0) {
+            C.O[k] = Ok;
+            C.D[k] = Dk;
+        }
+        const float dO1 = O1 - Ok, dO2 = O2 - Ok, dD1 = D1 - Dk, dD2 = D2 - Dk;   // exact
+        const int i0 = max(0, k - L2), i1 = min(L1, k);
         for (int i = i0 + threadIdx.x; i <= i1; i += blockDim.x) {
             const int j = k - i;
+            if (i == 0 || j == 0) {   // boundary: alpha = k gap; the gap tangent is k
+                C.at(kA, k, i) = fmaf((float)k, gap, -Ok);
+                if (TAN) C.at(kF, k, i) = (MODE == MODE_PGAP ? (float)k : 0.f) - Dk;
+                continue;
+            }
             const size_t si = (size_t)(i - 1) * L2m + (j - 1);
             const float sc = S[si];
-            const float vd = C.at(kA, k - 2, i - 1) + sc;
-            const float vu = C.at(kA, k - 1, i - 1) + gap;
-            const float vl = C.at(kA, k - 1, i) + gap;
+            const float vd = C.at(kA, k - 2, i - 1) + (sc + dO2);
+            const float vu = C.at(kA, k - 1, i - 1) + (gap + dO1);
+            const float vl = C.at(kA, k - 1, i) + (gap + dO1);
             const float m = fmaxf(vd, fmaxf(vu, vl));
             const float ed = expf((vd - m) * iT), eu = expf((vu - m) * iT), el = expf((vl - m) * iT);
             const float sum = (ed + eu) + el;
@@ -146,9 +171,15 @@ __global__ void __launch_bounds__(kThreads) nw_kernel(SwArgs p) {
             C.at(kWd, k, i) = wd;
             C.at(kWu, k, i) = wu;
             C.at(kWl, k, i) = wl;
+            if (MODE == MODE_MARG) {
+                // the entropy of the cell's choice, -sum w ln w = ln(sum) +
+                // sum w (m - v) / T: a sum of non-negative terms
+                C.at(kT1, k, i) = logf(sum) + iT * fmaf(wd, m - vd, fmaf(wu, m - vu, wl * (m - vl)));
+            }
             if (TAN) {
-                // tangents of the three options
-                float td = C.at(kF, k - 2, i - 1), tu = C.at(kF, k - 1, i - 1), tl = C.at(kF, k - 1, i);
+                // tangents of the three options, in this diagonal's frame
+                float td = C.at(kF, k - 2, i - 1) + dD2, tu = C.at(kF, k - 1, i - 1) + dD1,
+                      tl = C.at(kF, k - 1, i) + dD1;
                 if (MODE == MODE_HVP) td += V[si];
                 if (MODE == MODE_PGAP) {
                     tu += 1.f;
@@ -164,11 +195,19 @@ __global__ void __launch_bounds__(kThreads) nw_kernel(SwArgs p) {
             }
         }
         __syncthreads();
+        O2 = O1;
+        O1 = Ok;
+        D2 = D1;
+        D1 = Dk;
     }
 
     // ------------------------------------------------------------- reverse
-    double smu = 0.0, ssmu = 0.0, sdot = 0.0;
-    for (int k = L1 + L2; k >= 0; --k) {
+    double sgap = 0.0, sent = 0.0, sdot = 0.0;
+    for (int k = K; k >= 0; --k) {
+        const float Ok = C.O[k], Dk = C.D[k];
+        const float Ok1 = k + 1 <= K ? C.O[k + 1] : 0.f, Ok2 = k + 2 <= K ? C.O[k + 2] : 0.f;
+        const float Dk1 = k + 1 <= K ? C.D[k + 1] : 0.f, Dk2 = k + 2 <= K ? C.D[k + 2] : 0.f;
+        const float Om2 = k >= 2 ? C.O[k - 2] : 0.f, Dm2 = k >= 2 ? C.D[k - 2] : 0.f;
         const int i0 = max(0, k - L2), i1 = min(L1, k);
         for (int i = i0 + threadIdx.x; i <= i1; i += blockDim.x) {
             const int j = k - i;
@@ -176,18 +215,19 @@ __global__ void __launch_bounds__(kThreads) nw_kernel(SwArgs p) {
             float be = 0.f, tb = 0.f;
             const float fc = TAN ? C.at(kF, k, i) : 0.f;
             const float ac = C.at(kA, k, i);
-            if (k == L1 + L2) {
+            if (k == K) {
                 be = 1.f;   // the end cell (L1, L2); its tangent is 0
             } else {
                 // successors: (i+1, j+1) by its diagonal option, (i+1, j) by
                 // its up option (if j >= 1), (i, j+1) by its left option (if i >= 1)
-                auto take = [&](int kd, int id, int opt, int si_d) {
+                auto take = [&](int kd, int id, int opt, int si_d, float dO, float dD) {
+                    // dO, dD: this cell's frames minus the successor's (exact)
                     const float bd = C.at(kB, kd, id);
                     const float w = C.at(opt, kd, id);
                     be = fmaf(bd, w, be);
                     if (TAN) {
                         // dw of the option c -> d at d: w (dv - d alpha_d) / T (+ the T term)
-                        float dv = fc;
+                        float dv = fc + dD;
                         if (MODE == MODE_HVP && opt == kWd) dv += V[si_d];
                         if (MODE == MODE_PGAP && opt != kWd) dv += 1.f;
                         const float fd = C.at(kF, kd, id);
@@ -195,35 +235,36 @@ __global__ void __launch_bounds__(kThreads) nw_kernel(SwArgs p) {
                         if (MODE == MODE_PT) eu = fd - (C.at(kA, kd, id) - C.at(kEv, kd, id)) * iT;
                         float dw = w * (dv - eu) * iT;
                         if (MODE == MODE_PT) {
-                            const float v = ac + (opt == kWd ? S[si_d] : gap);
+                            const float v = ac + ((opt == kWd ? S[si_d] : gap) + dO);
                             dw = fmaf(w * (C.at(kEv, kd, id) - v), iT * iT, dw);
                         }
                         tb = fmaf(C.at(kR, kd, id), w, fmaf(bd, dw, tb));
                     }
                 };
-                if (i + 1 <= L1 && j + 1 <= L2) take(k + 2, i + 1, kWd, i * L2m + j);
-                if (i + 1 <= L1 && j >= 1) take(k + 1, i + 1, kWu, 0);
-                if (j + 1 <= L2 && i >= 1) take(k + 1, i, kWl, 0);
+                if (i + 1 <= L1 && j + 1 <= L2) take(k + 2, i + 1, kWd, i * L2m + j, Ok - Ok2, Dk - Dk2);
+                if (i + 1 <= L1 && j >= 1) take(k + 1, i + 1, kWu, 0, Ok - Ok1, Dk - Dk1);
+                if (j + 1 <= L2 && i >= 1) take(k + 1, i, kWl, 0, Ok - Ok1, Dk - Dk1);
             }
             C.at(kB, k, i) = be;
             if (TAN) C.at(kR, k, i) = tb;
+            if (MODE == MODE_MARG && !interior) sgap += (double)be * (double)k;   // a path ending at (i, 0) or (0, j) takes k more gaps
             if (interior) {
                 const size_t si = (size_t)(i - 1) * L2m + (j - 1);
                 const float wd = C.at(kWd, k, i);
                 if (MODE == MODE_MARG) {
                     const float mu = be * wd;
                     if (out) out[si] = mu;
-                    smu += (double)mu;
-                    ssmu += (double)mu * (double)S[si];
+                    sgap += (double)be * (double)(C.at(kWu, k, i) + C.at(kWl, k, i));
+                    sent += (double)be * (double)C.at(kT1, k, i);
                 } else {
                     // the tangent of this cell's diagonal weight
-                    float dv = C.at(kF, k - 2, i - 1);
+                    float dv = C.at(kF, k - 2, i - 1) + (Dm2 - Dk);
                     if (MODE == MODE_HVP) dv += V[si];
                     float eu = fc;
                     if (MODE == MODE_PT) eu = fc - (ac - C.at(kEv, k, i)) * iT;
                     float dwd = wd * (dv - eu) * iT;
                     if (MODE == MODE_PT) {
-                        const float vd = C.at(kA, k - 2, i - 1) + S[si];
+                        const float vd = C.at(kA, k - 2, i - 1) + (S[si] + (Om2 - Ok));
                         dwd = fmaf(wd * (C.at(kEv, k, i) - vd), iT * iT, dwd);
                     }
                     const float dmu = fmaf(tb, wd, be * dwd);
@@ -236,14 +277,18 @@ __global__ void __launch_bounds__(kThreads) nw_kernel(SwArgs p) {
     }
 
     if (MODE == MODE_MARG) {
-        const double tmu = block_sum(smu, red);
-        const double tsmu = block_sum(ssmu, red);
+        // dS/dgap = E[gaps]: the flows through gap moves; dS/dT = (S - E[path
+        // score]) / T, the entropy of the path distribution: the cells' choice
+        // entropies weighted by their visit probabilities (both sums of
+        // non-negative terms, free of the cancellation in S - sum s mu - gap
+        // dS/dgap)
+        const double tgap = block_sum(sgap, red);
+        const double tent = block_sum(sent, red);
         if (threadIdx.x == 0) {
-            const float Sv = C.at(kA, L1 + L2, L1);
-            const double dgap = (double)(L1 + L2) - 2.0 * tmu;
-            if (p.value) p.value[b] = Sv;
-            if (p.grad_gap) p.grad_gap[b] = (float)dgap;
-            if (p.grad_T) p.grad_T[b] = (float)(((double)Sv - tsmu - (double)gap * dgap) / (double)T);
+            const double Sv = (double)C.at(kA, K, L1) + (double)C.O[K];
+            if (p.value) p.value[b] = (float)Sv;
+            if (p.grad_gap) p.grad_gap[b] = (float)tgap;
+            if (p.grad_T) p.grad_T[b] = (float)tent;
         }
     } else if (p.dot_out) {
         const double t = block_sum(sdot, red);

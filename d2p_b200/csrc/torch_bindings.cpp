@@ -1,9 +1,10 @@
 // torch_bindings.cpp -- the reference's dispatcher surface (torch.ops.d2p.*) for the
-// soft Smith-Waterman family, implemented on top of the C ABI in
+// soft Smith-Waterman family and the linear soft Needleman-Wunsch operators,
+// implemented on top of the C ABI in
 // include/d2p_b200.h (libd2p_b200.so).
 //
 // Schemas are the reference's, verbatim (src/sw/registry.cpp:30-44,
-// src/sw_affine/registry.cpp:27-42), so code written against d2p's ops binds
+// src/sw_affine/registry.cpp:27-42, src/nw/registry.cpp:35-49), so code written against d2p's ops binds
 // unchanged.  CUDA and AutogradCUDA keys are registered exactly as the reference
 // does (src/sw/torch_cuda.cpp:857-883, src/sw_affine/torch_cuda.cpp:914-948);
 // there is no CPU kernel and no fallback: CPU tensors are rejected with the
@@ -61,14 +62,14 @@ int checked_dim(int64_t value, const char* name) {
     return static_cast<int>(value);
 }
 
-Shape checked_shape(const Tensor& scores) {
+Shape checked_shape(const Tensor& scores, int fam = D2P_FAMILY_LINEAR) {
     TORCH_CHECK(scores.dim() == 3, "scores must be 3D (B, L1, L2)");
     Shape s{checked_dim(scores.size(0), "scores batch dimension"),
             checked_dim(scores.size(1), "scores L1 dimension"),
             checked_dim(scores.size(2), "scores L2 dimension")};
     const int64_t cells = (static_cast<int64_t>(s.L1) + 1) * (static_cast<int64_t>(s.L2) + 1);
     TORCH_CHECK(cells <= static_cast<int64_t>(std::numeric_limits<int>::max()),
-                "SW CUDA DP table is too large for 32-bit kernel indexing: ",
+                fam == D2P_FAMILY_NW ? "NW" : "SW", " CUDA DP table is too large for 32-bit kernel indexing: ",
                 "(L1 + 1) * (L2 + 1) = ", cells, " exceeds ", std::numeric_limits<int>::max());
     return s;
 }
@@ -163,7 +164,7 @@ struct LinFwd {
 // want_params: also compute dS/dgap and dS/dT (needed by soft_sw_with_grads and
 // when gap or temperature require grad); without them the linear-domain fast
 // path can run.
-LinFwd lin_forward(const Tensor& scores, const Param& gap, const Param& T, const Tensor& lengths,
+LinFwd lin_forward(int fam, const Tensor& scores, const Param& gap, const Param& T, const Tensor& lengths,
                    const Shape& s, bool want_params) {
     auto opt = scores.options();
     LinFwd r;
@@ -177,57 +178,65 @@ LinFwd lin_forward(const Tensor& scores, const Param& gap, const Param& T, const
         gt = gg + s.B;
     }
     size_t wb = 0;
-    Tensor ws = workspace(D2P_FAMILY_LINEAR, D2P_OP_FORWARD_BACKWARD, s, scores.device(), &wb);
-    check_rc(d2p_sw_forward_backward(scores.data_ptr<float>(), len_ptr(lengths), s.B, s.L1, s.L2,
-                                     gap.host, T.host, gap.dev, T.dev, r.value.data_ptr<float>(),
-                                     r.marginals.data_ptr<float>(), gg, gt, ws.data_ptr(), wb, cur_stream()),
-             "d2p_sw_forward_backward");
+    Tensor ws = workspace(fam, D2P_OP_FORWARD_BACKWARD, s, scores.device(), &wb);
+    const bool nw = fam == D2P_FAMILY_NW;
+    check_rc((nw ? d2p_nw_forward_backward : d2p_sw_forward_backward)(
+                 scores.data_ptr<float>(), len_ptr(lengths), s.B, s.L1, s.L2, gap.host, T.host, gap.dev, T.dev,
+                 r.value.data_ptr<float>(), r.marginals.data_ptr<float>(), gg, gt, ws.data_ptr(), wb, cur_stream()),
+             nw ? "d2p_nw_forward_backward" : "d2p_sw_forward_backward");
     return r;
 }
 
-Tensor lin_hvp_raw(const Tensor& scores, const Tensor& tangent, float gap, float T,
+Tensor lin_hvp_raw(int fam, const Tensor& scores, const Tensor& tangent, float gap, float T,
                    const Tensor& lengths, const Shape& s) {
     Tensor H = torch::empty({s.B, s.L1, s.L2}, scores.options());
     size_t wb = 0;
-    Tensor ws = workspace(D2P_FAMILY_LINEAR, D2P_OP_HVP, s, scores.device(), &wb);
-    check_rc(d2p_sw_hvp(scores.data_ptr<float>(), tangent.data_ptr<float>(), len_ptr(lengths), s.B,
-                        s.L1, s.L2, gap, T, H.data_ptr<float>(), ws.data_ptr(), wb, cur_stream()),
-             "d2p_sw_hvp");
+    Tensor ws = workspace(fam, D2P_OP_HVP, s, scores.device(), &wb);
+    const bool nw = fam == D2P_FAMILY_NW;
+    check_rc((nw ? d2p_nw_hvp : d2p_sw_hvp)(scores.data_ptr<float>(), tangent.data_ptr<float>(), len_ptr(lengths),
+                                            s.B, s.L1, s.L2, gap, T, H.data_ptr<float>(), ws.data_ptr(), wb,
+                                            cur_stream()),
+             nw ? "d2p_nw_hvp" : "d2p_sw_hvp");
     return H;
 }
 
-Tensor lin_jac_raw(const Tensor& scores, int param_type, float gap, float T, const Tensor& lengths,
+Tensor lin_jac_raw(int fam, const Tensor& scores, int param_type, float gap, float T, const Tensor& lengths,
                    const Shape& s) {
     Tensor J = torch::empty({s.B, s.L1, s.L2}, scores.options());
     size_t wb = 0;
-    Tensor ws = workspace(D2P_FAMILY_LINEAR, D2P_OP_PARAM_JACOBIAN, s, scores.device(), &wb);
-    check_rc(d2p_sw_param_jacobian(scores.data_ptr<float>(), len_ptr(lengths), s.B, s.L1, s.L2,
-                                   param_type, gap, T, J.data_ptr<float>(), ws.data_ptr(), wb,
-                                   cur_stream()),
-             "d2p_sw_param_jacobian");
+    Tensor ws = workspace(fam, D2P_OP_PARAM_JACOBIAN, s, scores.device(), &wb);
+    const bool nw = fam == D2P_FAMILY_NW;
+    check_rc((nw ? d2p_nw_param_jacobian : d2p_sw_param_jacobian)(scores.data_ptr<float>(), len_ptr(lengths), s.B,
+                                                                  s.L1, s.L2, param_type, gap, T,
+                                                                  J.data_ptr<float>(), ws.data_ptr(), wb,
+                                                                  cur_stream()),
+             nw ? "d2p_nw_param_jacobian" : "d2p_sw_param_jacobian");
     return J;
 }
 
-std::tuple<Tensor, Tensor, Tensor> lin_backward_full_raw(const Tensor& scores, const Tensor& G,
+std::tuple<Tensor, Tensor, Tensor> lin_backward_full_raw(int fam, const Tensor& scores, const Tensor& G,
                                                          float gap, float T, const Tensor& lengths,
                                                          const Shape& s) {
     auto opt = scores.options();
     Tensor gs = torch::empty({s.B, s.L1, s.L2}, opt);
     Tensor gg = torch::empty({1}, opt), gT = torch::empty({1}, opt);
     size_t wb = 0;
-    Tensor ws = workspace(D2P_FAMILY_LINEAR, D2P_OP_BACKWARD_FULL, s, scores.device(), &wb);
-    check_rc(d2p_sw_backward_full(scores.data_ptr<float>(), G.data_ptr<float>(), len_ptr(lengths),
-                                  s.B, s.L1, s.L2, gap, T, gs.data_ptr<float>(), gg.data_ptr<float>(),
-                                  gT.data_ptr<float>(), ws.data_ptr(), wb, cur_stream()),
-             "d2p_sw_backward_full");
+    Tensor ws = workspace(fam, D2P_OP_BACKWARD_FULL, s, scores.device(), &wb);
+    const bool nw = fam == D2P_FAMILY_NW;
+    check_rc((nw ? d2p_nw_backward_full : d2p_sw_backward_full)(
+                 scores.data_ptr<float>(), G.data_ptr<float>(), len_ptr(lengths), s.B, s.L1, s.L2, gap, T,
+                 gs.data_ptr<float>(), gg.data_ptr<float>(), gT.data_ptr<float>(), ws.data_ptr(), wb, cur_stream()),
+             nw ? "d2p_nw_backward_full" : "d2p_sw_backward_full");
     return {gs, gg, gT};
 }
 
 // =============================================================================
 // linear gap: autograd function (reference SoftSWRegularCUDAFunction,
-// src/sw/torch_cuda.cpp:178-411)
+// src/sw/torch_cuda.cpp:178-411; for FAM = D2P_FAMILY_NW SoftNWCUDAFunction,
+// src/nw/torch_cuda.cpp:115-330, which has the same outputs and gradients)
 // =============================================================================
-class SoftSWFunction : public torch::autograd::Function<SoftSWFunction> {
+template <int FAM>
+class LinFamilyFunction : public torch::autograd::Function<LinFamilyFunction<FAM>> {
    public:
     // lengths travels as an optional non-variable argument: autograd records
     // metadata (device, dtype) for every Tensor input, which an undefined
@@ -237,12 +246,12 @@ class SoftSWFunction : public torch::autograd::Function<SoftSWFunction> {
         Tensor lengths = lengths_opt.has_value() ? *lengths_opt : Tensor();
         ctx->set_materialize_grads(false);
         D2PB_CHECK_INPUT(scores);
-        const Shape s = checked_shape(scores);
+        const Shape s = checked_shape(scores, FAM);
         c10::cuda::CUDAGuard guard(scores.device());
         Param pg = read_param(gap, scores, "gap");
         Param pT = read_param(temperature, scores, "temperature");
         if (lengths.defined()) validate_lengths(lengths, s, scores.device());
-        LinFwd r = lin_forward(scores, pg, pT, lengths, s, gap.requires_grad() || temperature.requires_grad());
+        LinFwd r = lin_forward(FAM, scores, pg, pT, lengths, s, gap.requires_grad() || temperature.requires_grad());
         ctx->save_for_backward({scores, r.marginals, r.dparams, gap, temperature});
         ctx->saved_data["lengths"] = lengths.defined() ? c10::IValue(lengths) : c10::IValue();
         return {r.value, r.marginals};
@@ -254,7 +263,7 @@ class SoftSWFunction : public torch::autograd::Function<SoftSWFunction> {
         Tensor gap = saved[3], temperature = saved[4];
         Tensor lengths;
         if (!ctx->saved_data["lengths"].isNone()) lengths = ctx->saved_data["lengths"].toTensor();
-        const Shape s = checked_shape(scores);
+        const Shape s = checked_shape(scores, FAM);
         c10::cuda::CUDAGuard guard(scores.device());
         auto opt = scores.options();
         Tensor gv = grad_outputs[0], gm = grad_outputs[1];
@@ -283,7 +292,7 @@ class SoftSWFunction : public torch::autograd::Function<SoftSWFunction> {
         }
         if (gm.defined() && gm.numel() > 0) {
             Tensor G = prep_grad(gm, scores, "grad_posteriors");
-            auto r = lin_backward_full_raw(scores, G, host_value(gap), host_value(temperature), lengths, s);
+            auto r = lin_backward_full_raw(FAM, scores, G, host_value(gap), host_value(temperature), lengths, s);
             grad_scores = have ? grad_scores + std::get<0>(r) : std::get<0>(r);
             if (ctx->needs_input_grad(1)) grad_gap = grad_gap + std::get<1>(r);
             if (ctx->needs_input_grad(2)) grad_T = grad_T + std::get<2>(r);
@@ -296,38 +305,42 @@ class SoftSWFunction : public torch::autograd::Function<SoftSWFunction> {
     }
 };
 
-std::vector<Tensor> soft_sw_cuda(Tensor scores, Tensor gap, Tensor temperature, Tensor lengths) {
-    return SoftSWFunction::apply(scores, gap, temperature, c10::optional<Tensor>(lengths));
+template <int FAM>
+std::vector<Tensor> soft_lin_cuda(Tensor scores, Tensor gap, Tensor temperature, Tensor lengths) {
+    return LinFamilyFunction<FAM>::apply(scores, gap, temperature, c10::optional<Tensor>(lengths));
 }
 
-std::vector<Tensor> soft_sw_float_cuda(Tensor scores, double gap, double temperature,
+template <int FAM>
+std::vector<Tensor> soft_lin_float_cuda(Tensor scores, double gap, double temperature,
                                        c10::optional<Tensor> lengths) {
     D2PB_CHECK_INPUT(scores);
-    const Shape s = checked_shape(scores);
+    const Shape s = checked_shape(scores, FAM);
     c10::cuda::CUDAGuard guard(scores.device());
     Tensor len = resolve_lengths(lengths, s, scores.device());
     auto cpu = torch::TensorOptions().dtype(torch::kFloat32);
-    return SoftSWFunction::apply(scores, torch::full({1}, (float)gap, cpu),
+    return LinFamilyFunction<FAM>::apply(scores, torch::full({1}, (float)gap, cpu),
                                  torch::full({1}, (float)temperature, cpu),
                                  len.defined() ? c10::optional<Tensor>(len) : c10::nullopt);
 }
 
-std::tuple<Tensor, Tensor, Tensor, Tensor> soft_sw_with_grads_cuda(Tensor scores, double gap,
+template <int FAM>
+std::tuple<Tensor, Tensor, Tensor, Tensor> soft_lin_with_grads_cuda(Tensor scores, double gap,
                                                                    double temperature,
                                                                    c10::optional<Tensor> lengths) {
     D2PB_CHECK_INPUT(scores);
-    const Shape s = checked_shape(scores);
+    const Shape s = checked_shape(scores, FAM);
     c10::cuda::CUDAGuard guard(scores.device());
     Tensor len = resolve_lengths(lengths, s, scores.device());
     Param pg, pT;
     pg.host = (float)gap;
     pT.host = (float)temperature;
-    LinFwd r = lin_forward(scores, pg, pT, len, s, true);
+    LinFwd r = lin_forward(FAM, scores, pg, pT, len, s, true);
     // the schema's outputs are independent tensors: no views of one buffer
     return {r.value, r.marginals, r.dparams[0].clone(), r.dparams[1].clone()};
 }
 
-Tensor soft_sw_hvp_cuda(Tensor scores, Tensor tangent, double gap, double temperature,
+template <int FAM>
+Tensor soft_lin_hvp_cuda(Tensor scores, Tensor tangent, double gap, double temperature,
                         c10::optional<Tensor> lengths) {
     D2PB_CHECK_INPUT(scores);
     D2PB_CHECK_INPUT(tangent);
@@ -335,24 +348,26 @@ Tensor soft_sw_hvp_cuda(Tensor scores, Tensor tangent, double gap, double temper
     TORCH_CHECK(scores.sizes() == tangent.sizes(), "scores and tangent must have same shape");
     TORCH_CHECK(tangent.device() == scores.device(), "tangent must be on same device as scores, got ",
                 tangent.device(), " vs ", scores.device());
-    const Shape s = checked_shape(scores);
+    const Shape s = checked_shape(scores, FAM);
     c10::cuda::CUDAGuard guard(scores.device());
     Tensor len = resolve_lengths(lengths, s, scores.device());
-    return lin_hvp_raw(scores, tangent, (float)gap, (float)temperature, len, s);
+    return lin_hvp_raw(FAM, scores, tangent, (float)gap, (float)temperature, len, s);
 }
 
-Tensor soft_sw_param_jacobian_cuda(Tensor scores, int64_t param_type, double gap, double temperature,
+template <int FAM>
+Tensor soft_lin_param_jacobian_cuda(Tensor scores, int64_t param_type, double gap, double temperature,
                                    c10::optional<Tensor> lengths) {
     D2PB_CHECK_INPUT(scores);
     TORCH_CHECK(scores.dim() == 3, "scores must be 3D");
     TORCH_CHECK(param_type >= 0 && param_type <= 1, "param_type must be 0 or 1");
-    const Shape s = checked_shape(scores);
+    const Shape s = checked_shape(scores, FAM);
     c10::cuda::CUDAGuard guard(scores.device());
     Tensor len = resolve_lengths(lengths, s, scores.device());
-    return lin_jac_raw(scores, (int)param_type, (float)gap, (float)temperature, len, s);
+    return lin_jac_raw(FAM, scores, (int)param_type, (float)gap, (float)temperature, len, s);
 }
 
-std::tuple<Tensor, Tensor, Tensor> soft_sw_backward_full_cuda(Tensor scores, Tensor grad_alignment,
+template <int FAM>
+std::tuple<Tensor, Tensor, Tensor> soft_lin_backward_full_cuda(Tensor scores, Tensor grad_alignment,
                                                               double gap, double temperature,
                                                               c10::optional<Tensor> lengths) {
     D2PB_CHECK_INPUT(scores);
@@ -362,40 +377,49 @@ std::tuple<Tensor, Tensor, Tensor> soft_sw_backward_full_cuda(Tensor scores, Ten
     TORCH_CHECK(grad_alignment.device() == scores.device(),
                 "grad_alignment must be on same device as scores, got ", grad_alignment.device(), " vs ",
                 scores.device());
-    const Shape s = checked_shape(scores);
+    const Shape s = checked_shape(scores, FAM);
     c10::cuda::CUDAGuard guard(scores.device());
     Tensor len = resolve_lengths(lengths, s, scores.device());
     Tensor G = grad_alignment.contiguous();
     if (G.scalar_type() != torch::kFloat32) G = G.to(torch::kFloat32);
-    return lin_backward_full_raw(scores, G, (float)gap, (float)temperature, len, s);
+    return lin_backward_full_raw(FAM, scores, G, (float)gap, (float)temperature, len, s);
 }
 
-// namespaced aliases (src/sw/torch_cuda.cpp:778-848)
-std::vector<Tensor> sw_forward_cuda(Tensor scores, double gap, double temp, c10::optional<Tensor> lengths) {
-    return soft_sw_float_cuda(scores, gap, temp, lengths);
+// namespaced aliases (src/sw/torch_cuda.cpp:778-848; src/nw/torch_cuda.cpp:700-785)
+template <int FAM>
+std::vector<Tensor> lin_forward_alias(Tensor scores, double gap, double temp, c10::optional<Tensor> lengths) {
+    return soft_lin_float_cuda<FAM>(scores, gap, temp, lengths);
 }
-std::vector<Tensor> sw_forward_t_cuda(Tensor scores, Tensor gap, Tensor temp, Tensor lengths) {
-    return soft_sw_cuda(scores, gap, temp, lengths);
+template <int FAM>
+std::vector<Tensor> lin_forward_t_alias(Tensor scores, Tensor gap, Tensor temp, Tensor lengths) {
+    return soft_lin_cuda<FAM>(scores, gap, temp, lengths);
 }
-std::tuple<Tensor, Tensor> sw_value_grad_params_cuda(Tensor scores, double gap, double temp,
-                                                     c10::optional<Tensor> lengths) {
-    auto r = soft_sw_with_grads_cuda(scores, gap, temp, lengths);
+template <int FAM>
+std::tuple<Tensor, Tensor> lin_value_grad_params_alias(Tensor scores, double gap, double temp,
+                                                       c10::optional<Tensor> lengths) {
+    auto r = soft_lin_with_grads_cuda<FAM>(scores, gap, temp, lengths);
     return {std::get<2>(r), std::get<3>(r)};
 }
-std::tuple<Tensor, Tensor, Tensor> sw_marginals_backward_cuda(Tensor scores, Tensor grad_marginals,
-                                                              double gap, double temp,
-                                                              c10::optional<Tensor> lengths) {
-    return soft_sw_backward_full_cuda(scores, grad_marginals, gap, temp, lengths);
+template <int FAM>
+std::tuple<Tensor, Tensor, Tensor> lin_marginals_backward_alias(Tensor scores, Tensor grad_marginals, double gap,
+                                                                double temp, c10::optional<Tensor> lengths) {
+    return soft_lin_backward_full_cuda<FAM>(scores, grad_marginals, gap, temp, lengths);
 }
-Tensor sw_marginals_hvp_cuda(Tensor scores, Tensor v, double gap, double temp, c10::optional<Tensor> lengths) {
-    return soft_sw_hvp_cuda(scores, v, gap, temp, lengths);
+template <int FAM>
+Tensor lin_marginals_hvp_alias(Tensor scores, Tensor v, double gap, double temp, c10::optional<Tensor> lengths) {
+    return soft_lin_hvp_cuda<FAM>(scores, v, gap, temp, lengths);
 }
-Tensor sw_marginals_grad_gap_cuda(Tensor scores, double gap, double temp, c10::optional<Tensor> lengths) {
-    return soft_sw_param_jacobian_cuda(scores, 0, gap, temp, lengths);
+template <int FAM>
+Tensor lin_marginals_grad_gap_alias(Tensor scores, double gap, double temp, c10::optional<Tensor> lengths) {
+    return soft_lin_param_jacobian_cuda<FAM>(scores, 0, gap, temp, lengths);
 }
-Tensor sw_marginals_grad_temp_cuda(Tensor scores, double gap, double temp, c10::optional<Tensor> lengths) {
-    return soft_sw_param_jacobian_cuda(scores, 1, gap, temp, lengths);
+template <int FAM>
+Tensor lin_marginals_grad_temp_alias(Tensor scores, double gap, double temp, c10::optional<Tensor> lengths) {
+    return soft_lin_param_jacobian_cuda<FAM>(scores, 1, gap, temp, lengths);
 }
+
+constexpr int kSW = D2P_FAMILY_LINEAR;
+constexpr int kNW = D2P_FAMILY_NW;
 
 // =============================================================================
 // affine gap
@@ -685,6 +709,20 @@ TORCH_LIBRARY_FRAGMENT(d2p, m) {
     m.def("sw_marginals_hvp(Tensor scores, Tensor v, float gap, float temp, Tensor? lengths) -> Tensor");
     m.def("sw_marginals_grad_gap(Tensor scores, float gap, float temp, Tensor? lengths) -> Tensor");
     m.def("sw_marginals_grad_temp(Tensor scores, float gap, float temp, Tensor? lengths) -> Tensor");
+    // soft Needleman-Wunsch, linear gap (src/nw/registry.cpp:35-49)
+    m.def("soft_nw(Tensor scores, Tensor gap, Tensor temperature, Tensor lengths) -> Tensor[]");
+    m.def("soft_nw_float(Tensor scores, float gap, float temperature, Tensor? lengths) -> Tensor[]");
+    m.def("soft_nw_with_grads(Tensor scores, float gap, float temperature, Tensor? lengths) -> (Tensor, Tensor, Tensor, Tensor)");
+    m.def("soft_nw_hvp(Tensor scores, Tensor tangent, float gap, float temperature, Tensor? lengths) -> Tensor");
+    m.def("soft_nw_param_jacobian(Tensor scores, int param_type, float gap, float temperature, Tensor? lengths) -> Tensor");
+    m.def("soft_nw_backward_full(Tensor scores, Tensor grad_alignment, float gap, float temperature, Tensor? lengths) -> (Tensor, Tensor, Tensor)");
+    m.def("nw_forward(Tensor scores, float gap, float temp, Tensor? lengths) -> Tensor[]");
+    m.def("nw_forward_t(Tensor scores, Tensor gap, Tensor temp, Tensor lengths) -> Tensor[]");
+    m.def("nw_value_grad_params(Tensor scores, float gap, float temp, Tensor? lengths) -> (Tensor, Tensor)");
+    m.def("nw_marginals_backward(Tensor scores, Tensor grad_marginals, float gap, float temp, Tensor? lengths) -> (Tensor, Tensor, Tensor)");
+    m.def("nw_marginals_hvp(Tensor scores, Tensor v, float gap, float temp, Tensor? lengths) -> Tensor");
+    m.def("nw_marginals_grad_gap(Tensor scores, float gap, float temp, Tensor? lengths) -> Tensor");
+    m.def("nw_marginals_grad_temp(Tensor scores, float gap, float temp, Tensor? lengths) -> Tensor");
     // src/sw_affine/registry.cpp:27-42
     m.def("soft_sw_affine(Tensor scores, Tensor gap_open, Tensor gap_ext, Tensor temperature, Tensor lengths) -> Tensor[]");
     m.def("soft_sw_affine_float(Tensor scores, float gap_open, float gap_ext, float temperature, Tensor? lengths) -> Tensor[]");
@@ -703,19 +741,32 @@ TORCH_LIBRARY_FRAGMENT(d2p, m) {
 }
 
 TORCH_LIBRARY_IMPL(d2p, CUDA, m) {
-    m.impl("soft_sw", soft_sw_cuda);
-    m.impl("soft_sw_float", soft_sw_float_cuda);
-    m.impl("soft_sw_with_grads", soft_sw_with_grads_cuda);
-    m.impl("soft_sw_hvp", soft_sw_hvp_cuda);
-    m.impl("soft_sw_param_jacobian", soft_sw_param_jacobian_cuda);
-    m.impl("soft_sw_backward_full", soft_sw_backward_full_cuda);
-    m.impl("sw_forward", sw_forward_cuda);
-    m.impl("sw_forward_t", sw_forward_t_cuda);
-    m.impl("sw_value_grad_params", sw_value_grad_params_cuda);
-    m.impl("sw_marginals_backward", sw_marginals_backward_cuda);
-    m.impl("sw_marginals_hvp", sw_marginals_hvp_cuda);
-    m.impl("sw_marginals_grad_gap", sw_marginals_grad_gap_cuda);
-    m.impl("sw_marginals_grad_temp", sw_marginals_grad_temp_cuda);
+    m.impl("soft_sw", soft_lin_cuda<kSW>);
+    m.impl("soft_sw_float", soft_lin_float_cuda<kSW>);
+    m.impl("soft_sw_with_grads", soft_lin_with_grads_cuda<kSW>);
+    m.impl("soft_sw_hvp", soft_lin_hvp_cuda<kSW>);
+    m.impl("soft_sw_param_jacobian", soft_lin_param_jacobian_cuda<kSW>);
+    m.impl("soft_sw_backward_full", soft_lin_backward_full_cuda<kSW>);
+    m.impl("sw_forward", lin_forward_alias<kSW>);
+    m.impl("sw_forward_t", lin_forward_t_alias<kSW>);
+    m.impl("sw_value_grad_params", lin_value_grad_params_alias<kSW>);
+    m.impl("sw_marginals_backward", lin_marginals_backward_alias<kSW>);
+    m.impl("sw_marginals_hvp", lin_marginals_hvp_alias<kSW>);
+    m.impl("sw_marginals_grad_gap", lin_marginals_grad_gap_alias<kSW>);
+    m.impl("sw_marginals_grad_temp", lin_marginals_grad_temp_alias<kSW>);
+    m.impl("soft_nw", soft_lin_cuda<kNW>);
+    m.impl("soft_nw_float", soft_lin_float_cuda<kNW>);
+    m.impl("soft_nw_with_grads", soft_lin_with_grads_cuda<kNW>);
+    m.impl("soft_nw_hvp", soft_lin_hvp_cuda<kNW>);
+    m.impl("soft_nw_param_jacobian", soft_lin_param_jacobian_cuda<kNW>);
+    m.impl("soft_nw_backward_full", soft_lin_backward_full_cuda<kNW>);
+    m.impl("nw_forward", lin_forward_alias<kNW>);
+    m.impl("nw_forward_t", lin_forward_t_alias<kNW>);
+    m.impl("nw_value_grad_params", lin_value_grad_params_alias<kNW>);
+    m.impl("nw_marginals_backward", lin_marginals_backward_alias<kNW>);
+    m.impl("nw_marginals_hvp", lin_marginals_hvp_alias<kNW>);
+    m.impl("nw_marginals_grad_gap", lin_marginals_grad_gap_alias<kNW>);
+    m.impl("nw_marginals_grad_temp", lin_marginals_grad_temp_alias<kNW>);
     m.impl("soft_sw_affine", soft_sw_affine_cuda);
     m.impl("soft_sw_affine_float", soft_sw_affine_float_cuda);
     m.impl("soft_sw_affine_with_grads", soft_sw_affine_with_grads_cuda);
@@ -737,7 +788,7 @@ TORCH_LIBRARY_IMPL(d2p, CUDA, m) {
 void reject_cpu(const c10::OperatorHandle& op, torch::jit::Stack*) {
     TORCH_CHECK(false, op.schema().name(),
                 ": scores must be a CUDA tensor (d2p_b200 implements the soft Smith-Waterman "
-                "operators for CUDA devices only)");
+                "and Needleman-Wunsch operators for CUDA devices only)");
 }
 
 TORCH_LIBRARY_IMPL(d2p, CPU, m) {
@@ -749,7 +800,9 @@ TORCH_LIBRARY_IMPL(d2p, CPU, m) {
         "soft_sw_affine_param_jacobian", "soft_sw_affine_backward_full", "sw_affine_forward",
         "sw_affine_forward_t", "sw_affine_value_grad_params", "sw_affine_marginals_backward",
         "sw_affine_marginals_hvp", "sw_affine_marginals_grad_gap_open", "sw_affine_marginals_grad_gap_ext",
-        "sw_affine_marginals_grad_temp"};
+        "sw_affine_marginals_grad_temp", "soft_nw", "soft_nw_float", "soft_nw_with_grads", "soft_nw_hvp",
+        "soft_nw_param_jacobian", "soft_nw_backward_full", "nw_forward", "nw_forward_t", "nw_value_grad_params",
+        "nw_marginals_backward", "nw_marginals_hvp", "nw_marginals_grad_gap", "nw_marginals_grad_temp"};
     for (const char* name : kOps) m.impl(name, torch::CppFunction::makeFromBoxedFunction<&reject_cpu>());
 }
 
@@ -771,23 +824,23 @@ using ForwardF = std::vector<Tensor>(Tensor, double, double, c10::optional<Tenso
 using AffForwardT = std::vector<Tensor>(Tensor, Tensor, Tensor, Tensor, Tensor);
 using AffForwardF = std::vector<Tensor>(Tensor, double, double, double, c10::optional<Tensor>);
 
-template <const char* Name>
+template <const char* Name, int FAM>
 std::vector<Tensor> fwd_t_autograd(Tensor scores, Tensor gap, Tensor temperature, Tensor lengths) {
     if (is_python_tensor(scores)) {
         static auto op = op_handle<ForwardT>(Name);
         at::AutoDispatchBelowADInplaceOrView below;
         return op.call(scores, gap, temperature, lengths);
     }
-    return soft_sw_cuda(scores, gap, temperature, lengths);
+    return soft_lin_cuda<FAM>(scores, gap, temperature, lengths);
 }
-template <const char* Name>
+template <const char* Name, int FAM>
 std::vector<Tensor> fwd_f_autograd(Tensor scores, double gap, double temperature, c10::optional<Tensor> lengths) {
     if (is_python_tensor(scores)) {
         static auto op = op_handle<ForwardF>(Name);
         at::AutoDispatchBelowADInplaceOrView below;
         return op.call(scores, gap, temperature, lengths);
     }
-    return soft_sw_float_cuda(scores, gap, temperature, lengths);
+    return soft_lin_float_cuda<FAM>(scores, gap, temperature, lengths);
 }
 template <const char* Name>
 std::vector<Tensor> aff_fwd_t_autograd(Tensor scores, Tensor go, Tensor ge, Tensor temperature, Tensor lengths) {
@@ -817,12 +870,20 @@ constexpr char kSoftSWAffine[] = "d2p::soft_sw_affine";
 constexpr char kSoftSWAffineFloat[] = "d2p::soft_sw_affine_float";
 constexpr char kSWAffineForward[] = "d2p::sw_affine_forward";
 constexpr char kSWAffineForwardT[] = "d2p::sw_affine_forward_t";
+constexpr char kSoftNW[] = "d2p::soft_nw";
+constexpr char kSoftNWFloat[] = "d2p::soft_nw_float";
+constexpr char kNWForward[] = "d2p::nw_forward";
+constexpr char kNWForwardT[] = "d2p::nw_forward_t";
 
 TORCH_LIBRARY_IMPL(d2p, AutogradCUDA, m) {
-    m.impl("soft_sw", fwd_t_autograd<kSoftSW>);
-    m.impl("soft_sw_float", fwd_f_autograd<kSoftSWFloat>);
-    m.impl("sw_forward", fwd_f_autograd<kSWForward>);
-    m.impl("sw_forward_t", fwd_t_autograd<kSWForwardT>);
+    m.impl("soft_sw", fwd_t_autograd<kSoftSW, kSW>);
+    m.impl("soft_sw_float", fwd_f_autograd<kSoftSWFloat, kSW>);
+    m.impl("sw_forward", fwd_f_autograd<kSWForward, kSW>);
+    m.impl("sw_forward_t", fwd_t_autograd<kSWForwardT, kSW>);
+    m.impl("soft_nw", fwd_t_autograd<kSoftNW, kNW>);
+    m.impl("soft_nw_float", fwd_f_autograd<kSoftNWFloat, kNW>);
+    m.impl("nw_forward", fwd_f_autograd<kNWForward, kNW>);
+    m.impl("nw_forward_t", fwd_t_autograd<kNWForwardT, kNW>);
     m.impl("soft_sw_affine", aff_fwd_t_autograd<kSoftSWAffine>);
     m.impl("soft_sw_affine_float", aff_fwd_f_autograd<kSoftSWAffineFloat>);
     m.impl("sw_affine_forward", aff_fwd_f_autograd<kSWAffineForward>);

@@ -1,5 +1,6 @@
 """Low-level operator access (d2p/ops/__init__.py): ``ops.sw``, ``ops.sw_affine`` and
-the flat op wrappers of the soft Smith-Waterman family."""
+the flat op wrappers of the soft Smith-Waterman family and of the linear soft
+Needleman-Wunsch operators."""
 from . import sw, sw_affine
 from .._ops import (  # noqa: F401
     d2p,
@@ -11,6 +12,9 @@ from .._ops import (  # noqa: F401
     sw_affine_forward, sw_affine_forward_t, sw_affine_value_grad_params, sw_affine_marginals_backward,
     sw_affine_marginals_hvp, sw_affine_marginals_grad_gap_open, sw_affine_marginals_grad_gap_ext,
     sw_affine_marginals_grad_temp,
+    soft_nw, soft_nw_float, soft_nw_with_grads, soft_nw_hvp, soft_nw_param_jacobian, soft_nw_backward_full,
+    nw_forward, nw_forward_t, nw_value_grad_params, nw_marginals_backward, nw_marginals_hvp,
+    nw_marginals_grad_gap, nw_marginals_grad_temp,
 )
 
 __all__ = [
@@ -24,4 +28,7 @@ __all__ = [
     "sw_affine_forward", "sw_affine_forward_t", "sw_affine_value_grad_params", "sw_affine_marginals_backward",
     "sw_affine_marginals_hvp", "sw_affine_marginals_grad_gap_open", "sw_affine_marginals_grad_gap_ext",
     "sw_affine_marginals_grad_temp",
+    "soft_nw", "soft_nw_float", "soft_nw_with_grads", "soft_nw_hvp", "soft_nw_param_jacobian",
+    "soft_nw_backward_full", "nw_forward", "nw_forward_t", "nw_value_grad_params", "nw_marginals_backward",
+    "nw_marginals_hvp", "nw_marginals_grad_gap", "nw_marginals_grad_temp",
 ]

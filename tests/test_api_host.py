@@ -71,6 +71,13 @@ SCHEMAS = {
     "sw_affine_marginals_grad_temp": "sw_affine_marginals_grad_temp(Tensor scores, float gap_open, float gap_ext, "
                                      "float temp, Tensor? lengths) -> Tensor",
 }
+# src/nw/registry.cpp:35-49, verbatim: the linear soft Needleman-Wunsch ops have
+# the linear soft Smith-Waterman schemas under their own names
+SCHEMAS.update({
+    name.replace("soft_sw", "soft_nw").replace("sw_", "nw_"):
+        SCHEMAS[name].replace("soft_sw", "soft_nw").replace("sw_", "nw_")
+    for name in list(SCHEMAS) if "affine" not in name
+})
 
 
 def _schema(name):
@@ -90,7 +97,7 @@ def _call_args(name, s, B):
     fl = (-2.0, -0.5, 1.0) if aff else (-1.0, 1.0)
     t = [s.new_tensor([v]) for v in fl]
     ln = torch.full((B, 2), 1, dtype=torch.int32, device=s.device)
-    if name in ("soft_sw", "sw_forward_t", "soft_sw_affine", "sw_affine_forward_t"):
+    if name in ("soft_sw", "sw_forward_t", "soft_sw_affine", "sw_affine_forward_t", "soft_nw", "nw_forward_t"):
         return (s, *t, ln)
     if "hvp" in name or "backward" in name:
         return (s, torch.zeros_like(s), *fl, None)
@@ -111,6 +118,8 @@ LAYOUT = {
     "sw_affine_marginals_hvp": "P", "sw_affine_marginals_grad_gap_open": "P",
     "sw_affine_marginals_grad_gap_ext": "P", "sw_affine_marginals_grad_temp": "P",
 }
+LAYOUT.update({k.replace("soft_sw", "soft_nw").replace("sw_", "nw_"): v for k, v in list(LAYOUT.items())
+               if "affine" not in k})
 
 
 @pytest.mark.parametrize("name", sorted(SCHEMAS))
@@ -129,7 +138,8 @@ def test_fake_kernels_give_the_reference_shapes(name):
     assert all(o.dtype == torch.float32 for o in outs)
 
 
-@pytest.mark.parametrize("name", ["soft_sw_float", "soft_sw_hvp", "soft_sw_affine_float", "sw_affine_marginals_hvp"])
+@pytest.mark.parametrize("name", ["soft_sw_float", "soft_sw_hvp", "soft_sw_affine_float", "sw_affine_marginals_hvp",
+                                  "soft_nw_float", "nw_marginals_backward"])
 def test_cpu_tensors_are_rejected(name):
     """No CPU kernel and no silent fallback: a CPU input raises, naming CUDA."""
     s = torch.randn(2, 4, 5)

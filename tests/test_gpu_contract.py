@@ -226,6 +226,15 @@ def test_alias_ops_match_primary_ops(d2p, cuda_device):
     same(ops.sw_affine_marginals_grad_gap_open(s, *p, ln), ops.soft_sw_affine_param_jacobian(s, 0, *p, ln))
     same(ops.sw_affine_marginals_grad_gap_ext(s, *p, ln), ops.soft_sw_affine_param_jacobian(s, 1, *p, ln))
     same(ops.sw_affine_marginals_grad_temp(s, *p, ln), ops.soft_sw_affine_param_jacobian(s, 2, *p, ln))
+    # the nw_* names of the linear soft Needleman-Wunsch ops (src/nw/torch_cuda.cpp:700-785)
+    same(ops.nw_forward(s, -1.0, 1.0, ln), ops.soft_nw_float(s, -1.0, 1.0, ln))
+    same(ops.nw_forward_t(s, gap, T, ln), ops.soft_nw(s, gap, T, ln))
+    wn = ops.soft_nw_with_grads(s, -1.0, 1.0, ln)
+    same(ops.nw_value_grad_params(s, -1.0, 1.0, ln), (wn[2], wn[3]))
+    same(ops.nw_marginals_backward(s, G, -1.0, 1.0, ln), ops.soft_nw_backward_full(s, G, -1.0, 1.0, ln))
+    same(ops.nw_marginals_hvp(s, G, -1.0, 1.0, ln), ops.soft_nw_hvp(s, G, -1.0, 1.0, ln))
+    same(ops.nw_marginals_grad_gap(s, -1.0, 1.0, ln), ops.soft_nw_param_jacobian(s, 0, -1.0, 1.0, ln))
+    same(ops.nw_marginals_grad_temp(s, -1.0, 1.0, ln), ops.soft_nw_param_jacobian(s, 1, -1.0, 1.0, ln))
 
 
 def test_outputs_are_independent_tensors(d2p, cuda_device):
@@ -260,7 +269,7 @@ def test_fake_shapes_match_real_outputs(d2p, cuda_device):
 
 
 @pytest.mark.parametrize("tensor_params", [False, True])
-@pytest.mark.parametrize("family", ["linear", "affine"])
+@pytest.mark.parametrize("family", ["linear", "affine", "nw"])
 def test_compile_fullgraph_forward_backward(d2p, cuda_device, family, tensor_params):
     """torch.compile(fullgraph=True) traces the public API through the
     d2p_py:: custom ops and their autograd formulas: value, marginals and every
@@ -271,7 +280,7 @@ def test_compile_fullgraph_forward_backward(d2p, cuda_device, family, tensor_par
 
     def run(fn):
         s = s0.clone().requires_grad_(True)
-        if family == "linear":
+        if family in ("linear", "nw"):
             params = [torch.tensor([-1.0], device=cuda_device, requires_grad=True),
                       torch.tensor([0.9], device=cuda_device, requires_grad=True)] if tensor_params else [-1.0, 0.9]
         else:
@@ -285,6 +294,9 @@ def test_compile_fullgraph_forward_backward(d2p, cuda_device, family, tensor_par
     def f(s, *params):
         if family == "linear":
             r = d2p.soft_sw(s, gap=params[0], temperature=params[1])
+        elif family == "nw":
+            r = d2p.soft_nw(s, gap=params[0], temperature=params[1])
+            return r.score.sum() + (r.alignment * W).sum(), r.score, r.alignment
         else:
             r = d2p.soft_sw_affine(s, gap_open=params[0], gap_ext=params[1], temperature=params[2])
         return r.value.sum() + (r.marginals * W).sum(), r.value, r.marginals
