@@ -422,3 +422,105 @@ def nw_linear_backward_full(scores, grad_alignment, lengths=None, gap=-1.0, T=1.
     jg = nw_linear_param_jacobian(scores, 0, lengths, gap, T, impl)
     jt = nw_linear_param_jacobian(scores, 1, lengths, gap, T, impl)
     return gs, np.array([(G * jg).sum()], dt), np.array([(G * jt).sum()], dt)
+
+
+# ----------------------------------------------------------------------------
+# Needleman-Wunsch, affine gaps: nw_affine_oracle.c, or the reference's
+# src/nw_affine/kernels_cpu.cpp; op-level orchestration as
+# src/nw_affine/torch_cpu.cpp:180-580
+# ----------------------------------------------------------------------------
+
+def _nwa_call(impl, name_ref, name_oracle):
+    if impl == "ref":
+        return _lib("ref"), name_ref, _F
+    return _lib("oracle"), name_oracle + ("_f64" if impl == "f64" else "_f32"), (_D if impl == "f64" else _F)
+
+
+def nw_affine(scores, lengths=None, gap_open=-2.0, gap_ext=-0.5, T=1.0, impl="f32") -> dict:
+    """value, marginals, grad_open, grad_ext, grad_T (+ alpha) as soft_nw_affine_with_grads."""
+    dt = _dt(impl)
+    s = _arr(scores, dt)
+    B, L1, L2 = s.shape
+    ln = _lens(lengths, B, L1, L2)
+    A3 = 3 * (L1 + 1) * (L2 + 1)
+    alpha = np.zeros((B, A3), dt)
+    beta = np.zeros((B, A3), dt)
+    value = np.zeros(B, dt)
+    marg = np.zeros((B, L1, L2), dt)
+    go_, ge_, gT = (np.zeros(B, dt) for _ in range(3))
+    lib, name, R = _nwa_call(impl, "nw_affine_forward_cpu", "oracle_nwa_forward")
+    if impl == "ref":
+        _fn(lib, name, [_P] * 4 + [_I] * 3 + [_F] * 3)(_ptr(s), _ptr(alpha), _ptr(value), _ptr(ln), B, L1, L2,
+                                                        gap_open, gap_ext, T)
+        _fn(lib, "nw_affine_backward_cpu", [_P] * 9 + [_I] * 3 + [_F] * 3)(
+            _ptr(alpha), _ptr(s), _ptr(value), _ptr(beta), _ptr(marg), _ptr(go_), _ptr(ge_), _ptr(gT), _ptr(ln),
+            B, L1, L2, gap_open, gap_ext, T)
+    else:
+        _fn(lib, name, [_P, _P, _I, _I, _I, R, R, R, _P, _P])(_ptr(s), _ptr(ln), B, L1, L2, gap_open, gap_ext, T,
+                                                             _ptr(alpha), _ptr(value))
+        _fn(lib, name.replace("forward", "backward"), [_P, _P, _I, _I, _I, R, R, R] + [_P] * 7)(
+            _ptr(s), _ptr(ln), B, L1, L2, gap_open, gap_ext, T, _ptr(alpha), _ptr(value), _ptr(beta), _ptr(marg),
+            _ptr(go_), _ptr(ge_), _ptr(gT))
+    return {"value": value, "marginals": marg, "grad_open": go_, "grad_ext": ge_, "grad_T": gT, "alpha": alpha}
+
+
+def nw_affine_hvp(scores, V, lengths=None, gap_open=-2.0, gap_ext=-0.5, T=1.0, impl="f32") -> np.ndarray:
+    dt = _dt(impl)
+    s = _arr(scores, dt)
+    v = _arr(V, dt)
+    B, L1, L2 = s.shape
+    ln = _lens(lengths, B, L1, L2)
+    A3 = 3 * (L1 + 1) * (L2 + 1)
+    base = nw_affine(s, ln, gap_open, gap_ext, T, impl)
+    alpha, value = base["alpha"], base["value"]
+    w1, w2, w3 = (np.zeros((B, A3), dt) for _ in range(3))
+    H = np.zeros((B, L1, L2), dt)
+    lib, name, R = _nwa_call(impl, "nw_affine_hvp_cpu", "oracle_nwa_hvp")
+    if impl == "ref":
+        dsc = np.zeros(B, dt)
+        _fn(lib, name, [_P] * 10 + [_I] * 3 + [_F] * 3)(
+            _ptr(alpha), _ptr(s), _ptr(value), _ptr(v), _ptr(w1), _ptr(dsc), _ptr(w2), _ptr(w3), _ptr(H), _ptr(ln),
+            B, L1, L2, gap_open, gap_ext, T)
+    else:
+        _fn(lib, name, [_P, _P, _P, _I, _I, _I, R, R, R] + [_P] * 5)(
+            _ptr(s), _ptr(v), _ptr(ln), B, L1, L2, gap_open, gap_ext, T, _ptr(alpha), _ptr(w1), _ptr(w2), _ptr(w3),
+            _ptr(H))
+    return H
+
+
+def nw_affine_param_jacobian(scores, param_type, lengths=None, gap_open=-2.0, gap_ext=-0.5, T=1.0,
+                             impl="f32") -> np.ndarray:
+    """dP/dgap_open (param_type 0), dP/dgap_ext (1) or dP/dT (2)."""
+    if param_type not in (0, 1, 2):
+        raise ValueError("param_type must be 0, 1, or 2")
+    dt = _dt(impl)
+    s = _arr(scores, dt)
+    B, L1, L2 = s.shape
+    ln = _lens(lengths, B, L1, L2)
+    base = nw_affine(s, ln, gap_open, gap_ext, T, impl)
+    dS = base[("grad_open", "grad_ext", "grad_T")[param_type]]
+    alpha, value = base["alpha"], base["value"]
+    A3 = 3 * (L1 + 1) * (L2 + 1)
+    w1, w2, w3 = (np.zeros((B, A3), dt) for _ in range(3))
+    dP = np.zeros((B, L1, L2), dt)
+    lib, name, R = _nwa_call(impl, "nw_affine_param_grad_cpu", "oracle_nwa_param_grad")
+    if impl == "ref":
+        _fn(lib, name, [_P] * 9 + [_I] * 3 + [_F] * 3 + [_I])(
+            _ptr(alpha), _ptr(s), _ptr(value), _ptr(dS), _ptr(w1), _ptr(w2), _ptr(w3), _ptr(dP), _ptr(ln), B, L1, L2,
+            gap_open, gap_ext, T, param_type)
+    else:
+        _fn(lib, name, [_P, _P, _I, _I, _I, R, R, R] + [_P] * 5 + [_I])(
+            _ptr(s), _ptr(ln), B, L1, L2, gap_open, gap_ext, T, _ptr(alpha), _ptr(w1), _ptr(w2), _ptr(w3), _ptr(dP),
+            param_type)
+    return dP
+
+
+def nw_affine_backward_full(scores, grad_alignment, lengths=None, gap_open=-2.0, gap_ext=-0.5, T=1.0,
+                            impl="f32"):
+    """(grad_scores, grad_open[1], grad_ext[1], grad_T[1]) as soft_nw_affine_backward_full_cpu
+    (src/nw_affine/torch_cpu.cpp:474-570)."""
+    dt = _dt(impl)
+    G = _arr(grad_alignment, dt)
+    gs = nw_affine_hvp(scores, G, lengths, gap_open, gap_ext, T, impl)
+    js = [nw_affine_param_jacobian(scores, p, lengths, gap_open, gap_ext, T, impl) for p in (0, 1, 2)]
+    return (gs,) + tuple(np.array([(G * j).sum()], dt) for j in js)

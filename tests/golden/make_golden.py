@@ -1,6 +1,6 @@
 """Generate the golden fixtures in tests/golden/ from the REFERENCE's own CPU
 kernels (src/sw/kernels_cpu.cpp, src/sw_affine/kernels_cpu.cpp,
-src/nw/kernels_cpu.cpp compiled from the reference sources into
+src/nw/kernels_cpu.cpp, src/nw_affine/kernels_cpu.cpp compiled from the reference sources into
 oracle/_ref/libref_sw_cpu.so by oracle/Makefile).
 
 Run in a container where the reference sources are present:
@@ -32,6 +32,8 @@ CASES = [
 NW_CASES = [
     ("nw_edges", 6, 9, 7, 0.8, -0.7, [[9, 7], [0, 7], [9, 0], [0, 0], [1, 7], [9, 1]]),
 ]
+# the affine gap penalties of the Needleman-Wunsch edge cases
+NW_AFFINE = (-1.5, -0.4)
 
 
 def main():
@@ -67,6 +69,7 @@ def main():
         bf = oracle.sw_affine_backward_full(s, G, ln, go, ge, T, "ref")
         out["aff_bf_scores"], out["aff_bf_open"], out["aff_bf_ext"], out["aff_bf_T"] = bf
         out.update(_nw_outputs(s, V, G, ln, gap, T))
+        out.update(_nwa_outputs(s, V, G, ln, go, ge, T))
         np.savez_compressed(os.path.join(HERE, name + ".npz"), **out)
         print("wrote", name)
     # Needleman-Wunsch edge cases: empty sequences (lengths 0 on either side)
@@ -77,8 +80,11 @@ def main():
         V = torch.randn(B, L1, L2, generator=g).numpy()
         G = torch.randn(B, L1, L2, generator=g).numpy()
         ln = np.array(lens, np.int32)
-        out = dict(scores=s, tangent=V, grad_marginals=G, T=np.float32(T), gap=np.float32(gap), lengths=ln)
+        go, ge = NW_AFFINE
+        out = dict(scores=s, tangent=V, grad_marginals=G, T=np.float32(T), gap=np.float32(gap),
+                   gap_open=np.float32(go), gap_ext=np.float32(ge), lengths=ln)
         out.update(_nw_outputs(s, V, G, ln, gap, T))
+        out.update(_nwa_outputs(s, V, G, ln, go, ge, T))
         np.savez_compressed(os.path.join(HERE, name + ".npz"), **out)
         print("wrote", name)
 
@@ -92,6 +98,19 @@ def _nw_outputs(s, V, G, ln, gap, T):
     out["nw_jac0"] = oracle.nw_linear_param_jacobian(s, 0, ln, gap, T, "ref")
     out["nw_jac1"] = oracle.nw_linear_param_jacobian(s, 1, ln, gap, T, "ref")
     out["nw_bf_scores"], out["nw_bf_gap"], out["nw_bf_T"] = oracle.nw_linear_backward_full(s, G, ln, gap, T, "ref")
+    return out
+
+
+def _nwa_outputs(s, V, G, ln, go, ge, T):
+    out = {}
+    r = oracle.nw_affine(s, ln, go, ge, T, "ref")
+    for k in ("value", "marginals", "grad_open", "grad_ext", "grad_T"):
+        out["nwa_" + k] = r[k]
+    out["nwa_hvp"] = oracle.nw_affine_hvp(s, V, ln, go, ge, T, "ref")
+    for p in range(3):
+        out[f"nwa_jac{p}"] = oracle.nw_affine_param_jacobian(s, p, ln, go, ge, T, "ref")
+    bf = oracle.nw_affine_backward_full(s, G, ln, go, ge, T, "ref")
+    out["nwa_bf_scores"], out["nwa_bf_open"], out["nwa_bf_ext"], out["nwa_bf_T"] = bf
     return out
 
 

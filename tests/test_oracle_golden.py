@@ -138,3 +138,39 @@ def test_nw_restatement_matches_reference_golden(path):
     _close(r64["grad_gap"], lens.sum(1) - 2 * mu.sum((1, 2)), 1e-9, 1e-9, "dS/dgap closed form")
     _close(r64["grad_T"], (r64["value"] - (s * mu).sum((1, 2)) - gap * r64["grad_gap"]) / T, 1e-9, 1e-9,
            "dS/dT closed form")
+
+
+NWA_GOLDEN = [p for p in ALL if "nwa_value" in np.load(p).files]
+
+
+@pytest.mark.parametrize("path", NWA_GOLDEN, ids=[os.path.basename(p) for p in NWA_GOLDEN])
+def test_nw_affine_restatement_matches_reference_golden(path):
+    """nw_affine_oracle.c reproduces the reference's src/nw_affine/kernels_cpu.cpp
+    bit for bit (same operation order, Kahan sums and skip thresholds),
+    including empty sequences on either side; the double build agrees to fp32
+    accuracy."""
+    d = _load(path)
+    s, ln, go, ge, T = d["scores"], d["lengths"], float(d["gap_open"]), float(d["gap_ext"]), float(d["T"])
+    r = oracle.nw_affine(s, ln, go, ge, T, "f32")
+    for k in ("value", "marginals", "grad_open", "grad_ext", "grad_T"):
+        _close(r[k], d["nwa_" + k], 0, 0, k)
+    _close(oracle.nw_affine_hvp(s, d["tangent"], ln, go, ge, T, "f32"), d["nwa_hvp"], 0, 0, "hvp")
+    for p in (0, 1, 2):
+        _close(oracle.nw_affine_param_jacobian(s, p, ln, go, ge, T, "f32"), d[f"nwa_jac{p}"], 0, 0, f"jac{p}")
+    bf = oracle.nw_affine_backward_full(s, d["grad_marginals"], ln, go, ge, T, "f32")
+    _close(bf[0], d["nwa_bf_scores"], 0, 0, "bf scores")
+    for q, k in ((1, "open"), (2, "ext"), (3, "T")):
+        _close(bf[q], d["nwa_bf_" + k], 1e-6, 1e-7, "bf " + k)
+    r64 = oracle.nw_affine(s, ln, go, ge, T, "f64")
+    _close(r64["value"], d["nwa_value"], 1e-5, 1e-5, "f64 value")
+    _close(r64["marginals"], d["nwa_marginals"], 1e-4, 1e-5, "f64 marginals")
+    # the marginals of an empty problem are zero, and its value is the single
+    # all-gap path's: open + (L - 1) ext for L > 0 gaps, 0 for none
+    B, L1, L2 = s.shape
+    lens = np.tile([L1, L2], (B, 1)) if ln is None or ln.size == 0 else ln
+    for b, (l1, l2) in enumerate(lens):
+        if l1 == 0 or l2 == 0:
+            n = int(l1 + l2)
+            want = 0.0 if n == 0 else go + (n - 1) * ge
+            assert abs(float(r64["value"][b]) - want) < 1e-9, (b, r64["value"][b], want)
+            assert np.all(r64["marginals"][b] == 0)
