@@ -1,6 +1,6 @@
 """d2p_b200 -- B200-native (sm_100a) soft Smith-Waterman operators, a drop-in for
-d2p's ``soft_sw`` / ``soft_sw_affine`` path, plus the linear-gap soft
-Needleman-Wunsch operators (``soft_nw``).
+d2p's ``soft_sw`` / ``soft_sw_affine`` path, plus the soft Needleman-Wunsch
+operators (``soft_nw``, ``soft_nw_affine``).
 
     import d2p_b200 as d2p
     result = d2p.soft_sw(scores, gap=-1.0, temperature=1.0)        # value [B], marginals [B,L1,L2]
@@ -15,7 +15,7 @@ from . import _pt2_ops  # the d2p_py:: custom ops torch.compile traces
 
 _ops._pt2_mod = _pt2_ops
 from .sw import SoftSW, SoftSWAffine, SWResult, soft_sw, soft_sw_affine
-from .nw import NWResult, SoftNW, soft_nw
+from .nw import NWResult, SoftNW, SoftNWAffine, soft_nw, soft_nw_affine
 from . import ops
 from .engine import engine_counts, set_engine, use_engine
 
@@ -35,6 +35,11 @@ soft_nw_with_grads = _ops.soft_nw_with_grads
 soft_nw_hvp = _ops.soft_nw_hvp
 soft_nw_param_jacobian = _ops.soft_nw_param_jacobian
 soft_nw_backward_full = _ops.soft_nw_backward_full
+soft_nw_affine_float = _ops.soft_nw_affine_float
+soft_nw_affine_with_grads = _ops.soft_nw_affine_with_grads
+soft_nw_affine_hvp = _ops.soft_nw_affine_hvp
+soft_nw_affine_param_jacobian = _ops.soft_nw_affine_param_jacobian
+soft_nw_affine_backward_full = _ops.soft_nw_affine_backward_full
 
 __version__ = "0.1.0"
 
@@ -44,5 +49,7 @@ __all__ = [
     "soft_sw_affine_float", "soft_sw_affine_with_grads", "soft_sw_affine_hvp", "soft_sw_affine_param_jacobian",
     "soft_sw_affine_backward_full", "engine_counts", "set_engine", "use_engine",
     "soft_nw", "NWResult", "SoftNW", "soft_nw_float", "soft_nw_with_grads", "soft_nw_hvp",
-    "soft_nw_param_jacobian", "soft_nw_backward_full",
+    "soft_nw_param_jacobian", "soft_nw_backward_full", "soft_nw_affine", "SoftNWAffine", "soft_nw_affine_float",
+    "soft_nw_affine_with_grads", "soft_nw_affine_hvp", "soft_nw_affine_param_jacobian",
+    "soft_nw_affine_backward_full",
 ]

@@ -1,5 +1,5 @@
 """Fake-tensor (meta) shapes and autocast rules for the soft Smith-Waterman and
-linear soft Needleman-Wunsch ops.
+soft Needleman-Wunsch ops.
 
 Mirrors d2p/_compile.py:18-250 (register_fake) and :857-901 (register_autocast)
 for the sw / sw_affine families.  Output shapes per op:
@@ -69,6 +69,21 @@ _OUTPUTS = {
     "nw_marginals_hvp": _P,
     "nw_marginals_grad_gap": _P,
     "nw_marginals_grad_temp": _P,
+    # soft Needleman-Wunsch, affine gaps (d2p/_compile.py:311-370)
+    "soft_nw_affine": [_B, _P],
+    "soft_nw_affine_float": [_B, _P],
+    "soft_nw_affine_with_grads": (_B, _P, _B, _B, _B),
+    "soft_nw_affine_hvp": _P,
+    "soft_nw_affine_param_jacobian": _P,
+    "soft_nw_affine_backward_full": (_P, _ONE, _ONE, _ONE),
+    "nw_affine_forward": [_B, _P],
+    "nw_affine_forward_t": [_B, _P],
+    "nw_affine_value_grad_params": (_B, _B, _B),
+    "nw_affine_marginals_backward": (_P, _ONE, _ONE, _ONE),
+    "nw_affine_marginals_hvp": _P,
+    "nw_affine_marginals_grad_gap_open": _P,
+    "nw_affine_marginals_grad_gap_ext": _P,
+    "nw_affine_marginals_grad_temp": _P,
 }
 
 

@@ -1,8 +1,8 @@
 """Low-level operator access: loads the native libraries and wraps torch.ops.d2p.*.
 
 Mirrors d2p/_ops.py (loader :25-167, soft Smith-Waterman wrappers :170-210,
-soft Needleman-Wunsch wrappers :241-246) for the soft Smith-Waterman family and
-the linear soft Needleman-Wunsch operators.  The extension is in-tree (``_C.so`` next to this
+soft Needleman-Wunsch wrappers :241-254) for the soft Smith-Waterman and soft
+Needleman-Wunsch (linear and affine gaps) operators.  The extension is in-tree (``_C.so`` next to this
 file, linked to ``libd2p_b200.so``); there is no CPU kernel and no fallback:
 importing fails loudly when the extension is missing, and CPU tensors are
 rejected by the ops themselves.
@@ -166,6 +166,22 @@ nw_marginals_hvp = _wrap("nw_marginals_hvp")
 nw_marginals_grad_gap = _wrap("nw_marginals_grad_gap")
 nw_marginals_grad_temp = _wrap("nw_marginals_grad_temp")
 
+# Needleman-Wunsch (affine gaps)
+soft_nw_affine = _wrap("soft_nw_affine")
+soft_nw_affine_float = _wrap("soft_nw_affine_float")
+soft_nw_affine_with_grads = _wrap("soft_nw_affine_with_grads")
+soft_nw_affine_hvp = _wrap("soft_nw_affine_hvp")
+soft_nw_affine_param_jacobian = _wrap("soft_nw_affine_param_jacobian")
+soft_nw_affine_backward_full = _wrap("soft_nw_affine_backward_full")
+nw_affine_forward = _wrap("nw_affine_forward")
+nw_affine_forward_t = _wrap("nw_affine_forward_t")
+nw_affine_value_grad_params = _wrap("nw_affine_value_grad_params")
+nw_affine_marginals_backward = _wrap("nw_affine_marginals_backward")
+nw_affine_marginals_hvp = _wrap("nw_affine_marginals_hvp")
+nw_affine_marginals_grad_gap_open = _wrap("nw_affine_marginals_grad_gap_open")
+nw_affine_marginals_grad_gap_ext = _wrap("nw_affine_marginals_grad_gap_ext")
+nw_affine_marginals_grad_temp = _wrap("nw_affine_marginals_grad_temp")
+
 OP_NAMES = (
     "soft_sw", "soft_sw_float", "soft_sw_with_grads", "soft_sw_hvp", "soft_sw_param_jacobian",
     "soft_sw_backward_full", "sw_forward", "sw_forward_t", "sw_value_grad_params",
@@ -178,4 +194,8 @@ OP_NAMES = (
     "soft_nw", "soft_nw_float", "soft_nw_with_grads", "soft_nw_hvp", "soft_nw_param_jacobian",
     "soft_nw_backward_full", "nw_forward", "nw_forward_t", "nw_value_grad_params", "nw_marginals_backward",
     "nw_marginals_hvp", "nw_marginals_grad_gap", "nw_marginals_grad_temp",
+    "soft_nw_affine", "soft_nw_affine_float", "soft_nw_affine_with_grads", "soft_nw_affine_hvp",
+    "soft_nw_affine_param_jacobian", "soft_nw_affine_backward_full", "nw_affine_forward", "nw_affine_forward_t",
+    "nw_affine_value_grad_params", "nw_affine_marginals_backward", "nw_affine_marginals_hvp",
+    "nw_affine_marginals_grad_gap_open", "nw_affine_marginals_grad_gap_ext", "nw_affine_marginals_grad_temp",
 )

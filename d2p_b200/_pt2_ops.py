@@ -1,7 +1,7 @@
 """PT2-safe custom ops (``d2p_py::*``) used while compiling or on fake tensors.
 
-Mirrors the soft Smith-Waterman and linear soft Needleman-Wunsch parts of
-d2p/_pt2_ops.py:72-570: each op wraps
+Mirrors the soft Smith-Waterman and soft Needleman-Wunsch parts of
+d2p/_pt2_ops.py:72-660: each op wraps
 the dispatcher op, carries a fake implementation, and the differentiable ones
 (``soft_sw``, ``soft_sw_float``, affine analogues) register an autograd formula
 built from the saved marginals (value branch) and ``*_backward_full`` (marginal
@@ -184,148 +184,143 @@ globals().update(_make_linear_family("soft_nw"))
 
 
 # --------------------------------------------------------------------------- affine
-@custom_op("d2p_py::soft_sw_affine_with_grads", mutates_args=())
-def soft_sw_affine_with_grads(scores: torch.Tensor, gap_open: float, gap_ext: float, temperature: float,
-                              lengths: Optional[torch.Tensor]) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
-    v, m, a, b, c = torch.ops.d2p.soft_sw_affine_with_grads(scores, gap_open, gap_ext, temperature, lengths)
-    return v, m, a, b, c
+# The affine-gap Smith-Waterman ops (prefix "soft_sw_affine") and the affine
+# Needleman-Wunsch ops (prefix "soft_nw_affine", d2p/_pt2_ops.py:575-660)
+# have the same schemas and autograd formulas; one factory builds both sets.
+def _make_affine_family(prefix: str):
+    raw = torch.ops.d2p
 
+    @custom_op(f"d2p_py::{prefix}_with_grads", mutates_args=())
+    def with_grads(scores: torch.Tensor, gap_open: float, gap_ext: float, temperature: float,
+                   lengths: Optional[torch.Tensor]
+                   ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+        v, m, a, b, c = getattr(raw, f"{prefix}_with_grads")(scores, gap_open, gap_ext, temperature, lengths)
+        return v, m, a, b, c
 
-@soft_sw_affine_with_grads.register_fake
-def _(scores, gap_open, gap_ext, temperature, lengths):
-    return _like(scores, "B", "P", "B", "B", "B")
+    @with_grads.register_fake
+    def _(scores, gap_open, gap_ext, temperature, lengths):
+        return _like(scores, "B", "P", "B", "B", "B")
 
+    @custom_op(f"d2p_py::{prefix}_hvp", mutates_args=())
+    def hvp(scores: torch.Tensor, tangent: torch.Tensor, gap_open: float, gap_ext: float,
+            temperature: float, lengths: Optional[torch.Tensor]) -> torch.Tensor:
+        return getattr(raw, f"{prefix}_hvp")(scores, tangent, gap_open, gap_ext, temperature, lengths)
 
-@custom_op("d2p_py::soft_sw_affine_hvp", mutates_args=())
-def soft_sw_affine_hvp(scores: torch.Tensor, tangent: torch.Tensor, gap_open: float, gap_ext: float,
+    @hvp.register_fake
+    def _(scores, tangent, gap_open, gap_ext, temperature, lengths):
+        return _like(scores, "P")
+
+    @custom_op(f"d2p_py::{prefix}_param_jacobian", mutates_args=())
+    def param_jacobian(scores: torch.Tensor, param_type: int, gap_open: float, gap_ext: float,
                        temperature: float, lengths: Optional[torch.Tensor]) -> torch.Tensor:
-    return torch.ops.d2p.soft_sw_affine_hvp(scores, tangent, gap_open, gap_ext, temperature, lengths)
+        return getattr(raw, f"{prefix}_param_jacobian")(scores, param_type, gap_open, gap_ext, temperature, lengths)
+
+    @param_jacobian.register_fake
+    def _(scores, param_type, gap_open, gap_ext, temperature, lengths):
+        return _like(scores, "P")
+
+    @custom_op(f"d2p_py::{prefix}_backward_full", mutates_args=())
+    def backward_full(scores: torch.Tensor, grad_alignment: torch.Tensor, gap_open: float, gap_ext: float,
+                      temperature: float, lengths: Optional[torch.Tensor]
+                      ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+        a, b, c, d = getattr(raw, f"{prefix}_backward_full")(scores, grad_alignment, gap_open, gap_ext,
+                                                              temperature, lengths)
+        return a, b, c, d
+
+    @backward_full.register_fake
+    def _(scores, grad_alignment, gap_open, gap_ext, temperature, lengths):
+        return _like(scores, "P", "1", "1", "1")
+
+    @custom_op(f"d2p_py::{prefix}", mutates_args=())
+    def tensor_op(scores: torch.Tensor, gap_open: torch.Tensor, gap_ext: torch.Tensor,
+                  temperature: torch.Tensor, lengths: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        v, m = getattr(raw, prefix)(scores, gap_open, gap_ext, temperature, lengths)
+        return v, m
+
+    @tensor_op.register_fake
+    def _(scores, gap_open, gap_ext, temperature, lengths):
+        return _like(scores, "B", "P")
+
+    # parameters as tensors, read only when the op runs (see the linear family)
+    @custom_op(f"d2p_py::{prefix}_param_grads_t", mutates_args=())
+    def param_grads_t(scores: torch.Tensor, gap_open: torch.Tensor, gap_ext: torch.Tensor,
+                      temperature: torch.Tensor,
+                      lengths: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        r = getattr(raw, f"{prefix}_with_grads")(scores, float(gap_open), float(gap_ext), float(temperature),
+                                                  lengths)
+        return r[2], r[3], r[4]
+
+    @param_grads_t.register_fake
+    def _(scores, gap_open, gap_ext, temperature, lengths):
+        return _like(scores, "B", "B", "B")
+
+    @custom_op(f"d2p_py::{prefix}_backward_full_t", mutates_args=())
+    def backward_full_t(scores: torch.Tensor, grad_alignment: torch.Tensor, gap_open: torch.Tensor,
+                        gap_ext: torch.Tensor, temperature: torch.Tensor, lengths: torch.Tensor
+                        ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+        a, b, c, d = getattr(raw, f"{prefix}_backward_full")(scores, grad_alignment, float(gap_open),
+                                                              float(gap_ext), float(temperature), lengths)
+        return a, b, c, d
+
+    @backward_full_t.register_fake
+    def _(scores, grad_alignment, gap_open, gap_ext, temperature, lengths):
+        return _like(scores, "P", "1", "1", "1")
+
+    def tensor_setup(ctx, inputs, output):
+        scores, go, ge, temperature, lengths = inputs
+        ctx.save_for_backward(scores, output[1], go.detach(), ge.detach(), temperature.detach())
+        ctx.lengths = lengths
+
+    def tensor_backward(ctx, grad_value, grad_marg):
+        scores, marg, go, ge, temperature = ctx.saved_tensors
+        grad_scores = _expand_batch(grad_value, marg)
+        need = ctx.needs_input_grad[1:4]
+        grads = [None, None, None]
+        if grad_value is not None and any(need):
+            pg = param_grads_t(scores, go, ge, temperature, ctx.lengths)
+            for k in range(3):
+                if need[k]:
+                    grads[k] = _batch_dot(grad_value, pg[k])
+        if grad_marg is not None:
+            r = backward_full_t(scores, grad_marg, go, ge, temperature, ctx.lengths)
+            grad_scores = _add(grad_scores, r[0])
+            for k in range(3):
+                if need[k]:
+                    grads[k] = _add(grads[k], r[1 + k])
+        return grad_scores, grads[0], grads[1], grads[2], None
+
+    tensor_op.register_autograd(tensor_backward, setup_context=tensor_setup)
+
+    @custom_op(f"d2p_py::{prefix}_float", mutates_args=())
+    def float_op(scores: torch.Tensor, gap_open: float, gap_ext: float, temperature: float,
+                 lengths: Optional[torch.Tensor]) -> tuple[torch.Tensor, torch.Tensor]:
+        v, m = getattr(raw, f"{prefix}_float")(scores, gap_open, gap_ext, temperature, lengths)
+        return v, m
+
+    @float_op.register_fake
+    def _(scores, gap_open, gap_ext, temperature, lengths):
+        return _like(scores, "B", "P")
+
+    def float_setup(ctx, inputs, output):
+        scores, go, ge, temperature, lengths = inputs
+        ctx.save_for_backward(scores, output[1])
+        ctx.go, ctx.ge, ctx.temperature, ctx.lengths = go, ge, temperature, lengths
+
+    def float_backward(ctx, grad_value, grad_marg):
+        scores, marg = ctx.saved_tensors
+        grad_scores = _expand_batch(grad_value, marg)
+        if grad_marg is not None:
+            r = backward_full(scores, grad_marg, ctx.go, ctx.ge, ctx.temperature, ctx.lengths)
+            grad_scores = _add(grad_scores, r[0])
+        return grad_scores, None, None, None, None
+
+    float_op.register_autograd(float_backward, setup_context=float_setup)
+    return {
+        prefix: tensor_op, f"{prefix}_float": float_op, f"{prefix}_with_grads": with_grads, f"{prefix}_hvp": hvp,
+        f"{prefix}_param_jacobian": param_jacobian, f"{prefix}_backward_full": backward_full,
+        f"{prefix}_param_grads_t": param_grads_t, f"{prefix}_backward_full_t": backward_full_t,
+    }
 
 
-@soft_sw_affine_hvp.register_fake
-def _(scores, tangent, gap_open, gap_ext, temperature, lengths):
-    return _like(scores, "P")
-
-
-@custom_op("d2p_py::soft_sw_affine_param_jacobian", mutates_args=())
-def soft_sw_affine_param_jacobian(scores: torch.Tensor, param_type: int, gap_open: float, gap_ext: float,
-                                  temperature: float, lengths: Optional[torch.Tensor]) -> torch.Tensor:
-    return torch.ops.d2p.soft_sw_affine_param_jacobian(scores, param_type, gap_open, gap_ext, temperature,
-                                                       lengths)
-
-
-@soft_sw_affine_param_jacobian.register_fake
-def _(scores, param_type, gap_open, gap_ext, temperature, lengths):
-    return _like(scores, "P")
-
-
-@custom_op("d2p_py::soft_sw_affine_backward_full", mutates_args=())
-def soft_sw_affine_backward_full(scores: torch.Tensor, grad_alignment: torch.Tensor, gap_open: float,
-                                 gap_ext: float, temperature: float,
-                                 lengths: Optional[torch.Tensor]) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
-    a, b, c, d = torch.ops.d2p.soft_sw_affine_backward_full(scores, grad_alignment, gap_open, gap_ext,
-                                                            temperature, lengths)
-    return a, b, c, d
-
-
-@soft_sw_affine_backward_full.register_fake
-def _(scores, grad_alignment, gap_open, gap_ext, temperature, lengths):
-    return _like(scores, "P", "1", "1", "1")
-
-
-@custom_op("d2p_py::soft_sw_affine", mutates_args=())
-def soft_sw_affine(scores: torch.Tensor, gap_open: torch.Tensor, gap_ext: torch.Tensor,
-                   temperature: torch.Tensor, lengths: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-    v, m = torch.ops.d2p.soft_sw_affine(scores, gap_open, gap_ext, temperature, lengths)
-    return v, m
-
-
-@soft_sw_affine.register_fake
-def _(scores, gap_open, gap_ext, temperature, lengths):
-    return _like(scores, "B", "P")
-
-
-@custom_op("d2p_py::soft_sw_affine_param_grads_t", mutates_args=())
-def soft_sw_affine_param_grads_t(scores: torch.Tensor, gap_open: torch.Tensor, gap_ext: torch.Tensor,
-                                 temperature: torch.Tensor,
-                                 lengths: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
-    r = torch.ops.d2p.soft_sw_affine_with_grads(scores, float(gap_open), float(gap_ext), float(temperature), lengths)
-    return r[2], r[3], r[4]
-
-
-@soft_sw_affine_param_grads_t.register_fake
-def _(scores, gap_open, gap_ext, temperature, lengths):
-    return _like(scores, "B", "B", "B")
-
-
-@custom_op("d2p_py::soft_sw_affine_backward_full_t", mutates_args=())
-def soft_sw_affine_backward_full_t(scores: torch.Tensor, grad_alignment: torch.Tensor, gap_open: torch.Tensor,
-                                   gap_ext: torch.Tensor, temperature: torch.Tensor, lengths: torch.Tensor
-                                   ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
-    a, b, c, d = torch.ops.d2p.soft_sw_affine_backward_full(scores, grad_alignment, float(gap_open), float(gap_ext),
-                                                            float(temperature), lengths)
-    return a, b, c, d
-
-
-@soft_sw_affine_backward_full_t.register_fake
-def _(scores, grad_alignment, gap_open, gap_ext, temperature, lengths):
-    return _like(scores, "P", "1", "1", "1")
-
-
-def _soft_sw_affine_setup(ctx, inputs, output):
-    scores, go, ge, temperature, lengths = inputs
-    ctx.save_for_backward(scores, output[1], go.detach(), ge.detach(), temperature.detach())
-    ctx.lengths = lengths
-
-
-def _soft_sw_affine_backward(ctx, grad_value, grad_marg):
-    scores, marg, go, ge, temperature = ctx.saved_tensors
-    grad_scores = _expand_batch(grad_value, marg)
-    need = ctx.needs_input_grad[1:4]
-    grads = [None, None, None]
-    if grad_value is not None and any(need):
-        pg = soft_sw_affine_param_grads_t(scores, go, ge, temperature, ctx.lengths)
-        for k in range(3):
-            if need[k]:
-                grads[k] = _batch_dot(grad_value, pg[k])
-    if grad_marg is not None:
-        r = soft_sw_affine_backward_full_t(scores, grad_marg, go, ge, temperature, ctx.lengths)
-        grad_scores = _add(grad_scores, r[0])
-        for k in range(3):
-            if need[k]:
-                grads[k] = _add(grads[k], r[1 + k])
-    return grad_scores, grads[0], grads[1], grads[2], None
-
-
-soft_sw_affine.register_autograd(_soft_sw_affine_backward, setup_context=_soft_sw_affine_setup)
-
-
-@custom_op("d2p_py::soft_sw_affine_float", mutates_args=())
-def soft_sw_affine_float(scores: torch.Tensor, gap_open: float, gap_ext: float, temperature: float,
-                         lengths: Optional[torch.Tensor]) -> tuple[torch.Tensor, torch.Tensor]:
-    v, m = torch.ops.d2p.soft_sw_affine_float(scores, gap_open, gap_ext, temperature, lengths)
-    return v, m
-
-
-@soft_sw_affine_float.register_fake
-def _(scores, gap_open, gap_ext, temperature, lengths):
-    return _like(scores, "B", "P")
-
-
-def _soft_sw_affine_float_setup(ctx, inputs, output):
-    scores, go, ge, temperature, lengths = inputs
-    ctx.save_for_backward(scores, output[1])
-    ctx.go, ctx.ge, ctx.temperature, ctx.lengths = go, ge, temperature, lengths
-
-
-def _soft_sw_affine_float_backward(ctx, grad_value, grad_marg):
-    scores, marg = ctx.saved_tensors
-    grad_scores = _expand_batch(grad_value, marg)
-    if grad_marg is not None:
-        r = soft_sw_affine_backward_full(scores, grad_marg, ctx.go, ctx.ge, ctx.temperature, ctx.lengths)
-        grad_scores = _add(grad_scores, r[0])
-    return grad_scores, None, None, None, None
-
-
-soft_sw_affine_float.register_autograd(_soft_sw_affine_float_backward,
-                                       setup_context=_soft_sw_affine_float_setup)
+globals().update(_make_affine_family("soft_sw_affine"))
+globals().update(_make_affine_family("soft_nw_affine"))

@@ -142,6 +142,10 @@ int launch_lin_plane(const SwArgs& a, cudaStream_t st);
 // pair in a.mode (MODE_MARG, MODE_HVP, MODE_PGAP, MODE_PT)
 size_t nw_workspace_bytes(int op, int B, int L1, int L2);
 int launch_nw(const SwArgs& a, cudaStream_t st);
+// soft Needleman-Wunsch with affine gaps (sw_nw_affine.cu): the same, in
+// a.mode MODE_MARG, MODE_HVP, MODE_PGAP (open), MODE_PGE (ext), MODE_PT
+size_t nwa_workspace_bytes(int op, int B, int L1, int L2);
+int launch_nwa(const SwArgs& a, cudaStream_t st);
 // engine counters of the current device (cumulative, read synchronously):
 // problems the plane engine computed [linear, affine], and problems the
 // log-domain kernel recomputed after a linear-domain kernel flagged them

@@ -1,10 +1,12 @@
 // torch_bindings.cpp -- the reference's dispatcher surface (torch.ops.d2p.*) for the
-// soft Smith-Waterman family and the linear soft Needleman-Wunsch operators,
+// soft Smith-Waterman family and the soft Needleman-Wunsch operators (linear and
+// affine gaps),
 // implemented on top of the C ABI in
 // include/d2p_b200.h (libd2p_b200.so).
 //
 // Schemas are the reference's, verbatim (src/sw/registry.cpp:30-44,
-// src/sw_affine/registry.cpp:27-42, src/nw/registry.cpp:35-49), so code written against d2p's ops binds
+// src/sw_affine/registry.cpp:27-42, src/nw/registry.cpp:35-49,
+// src/nw_affine/registry.cpp:35-50), so code written against d2p's ops binds
 // unchanged.  CUDA and AutogradCUDA keys are registered exactly as the reference
 // does (src/sw/torch_cuda.cpp:857-883, src/sw_affine/torch_cuda.cpp:914-948);
 // there is no CPU kernel and no fallback: CPU tensors are rejected with the
@@ -434,13 +436,23 @@ constexpr int kNW = D2P_FAMILY_NW;
     TORCH_CHECK((x).scalar_type() == torch::kFloat32 || (x).scalar_type() == torch::kBFloat16, \
                 #x " must be float32, got ", (x).scalar_type())
 
+// SW affine reads fp32 or bf16 scores; NW affine fp32, as the reference
+// (src/nw_affine/torch_cuda.cpp:57-58)
+void check_aff_scores(const Tensor& scores, int fam) {
+    if (fam == D2P_FAMILY_NW_AFFINE) {
+        D2PB_CHECK_INPUT(scores);
+    } else {
+        D2PB_CHECK_AFF_SCORES(scores);
+    }
+}
+
 struct AffFwd {
     Tensor value, marginals, dparams;  // dparams [3,B]: dS/dgap_open, dS/dgap_ext, dS/dT
 };
 
 // want_params: also compute the three parameter gradients (soft_sw_affine_with_grads,
 // or parameters that require grad); without them the linear-domain fast path can run.
-AffFwd aff_forward(const Tensor& scores, const Param& go, const Param& ge, const Param& T,
+AffFwd aff_forward(int fam, const Tensor& scores, const Param& go, const Param& ge, const Param& T,
                    const Tensor& lengths, const Shape& s, bool want_params) {
     auto opt = scores.options().dtype(torch::kFloat32);
     AffFwd r;
@@ -452,7 +464,16 @@ AffFwd aff_forward(const Tensor& scores, const Param& go, const Param& ge, const
         dp = r.dparams.data_ptr<float>();
     }
     size_t wb = 0;
-    Tensor ws = workspace(D2P_FAMILY_AFFINE, D2P_OP_FORWARD_BACKWARD, s, scores.device(), &wb);
+    Tensor ws = workspace(fam, D2P_OP_FORWARD_BACKWARD, s, scores.device(), &wb);
+    if (fam == D2P_FAMILY_NW_AFFINE) {
+        check_rc(d2p_nw_affine_forward_backward(scores.data_ptr<float>(), len_ptr(lengths), s.B, s.L1, s.L2,
+                                                go.host, ge.host, T.host, go.dev, ge.dev, T.dev,
+                                                r.value.data_ptr<float>(), r.marginals.data_ptr<float>(), dp,
+                                                dp ? dp + s.B : nullptr, dp ? dp + 2 * s.B : nullptr,
+                                                ws.data_ptr(), wb, cur_stream()),
+                 "d2p_nw_affine_forward_backward");
+        return r;
+    }
     const int dt = scores.scalar_type() == torch::kBFloat16 ? D2P_DTYPE_BF16 : D2P_DTYPE_F32;
     check_rc(d2p_sw_affine_forward_backward(scores.data_ptr(), dt, len_ptr(lengths), s.B, s.L1, s.L2,
                                             go.host, ge.host, T.host, go.dev, ge.dev, T.dev,
@@ -463,53 +484,60 @@ AffFwd aff_forward(const Tensor& scores, const Param& go, const Param& ge, const
     return r;
 }
 
-Tensor aff_hvp_raw(const Tensor& scores, const Tensor& tangent, float go, float ge, float T,
+Tensor aff_hvp_raw(int fam, const Tensor& scores, const Tensor& tangent, float go, float ge, float T,
                    const Tensor& lengths, const Shape& s) {
     Tensor H = torch::empty({s.B, s.L1, s.L2}, scores.options());
     size_t wb = 0;
-    Tensor ws = workspace(D2P_FAMILY_AFFINE, D2P_OP_HVP, s, scores.device(), &wb);
-    check_rc(d2p_sw_affine_hvp(scores.data_ptr<float>(), tangent.data_ptr<float>(), len_ptr(lengths), s.B,
-                               s.L1, s.L2, go, ge, T, H.data_ptr<float>(), ws.data_ptr(), wb, cur_stream()),
-             "d2p_sw_affine_hvp");
+    Tensor ws = workspace(fam, D2P_OP_HVP, s, scores.device(), &wb);
+    const bool nw = fam == D2P_FAMILY_NW_AFFINE;
+    check_rc((nw ? d2p_nw_affine_hvp : d2p_sw_affine_hvp)(scores.data_ptr<float>(), tangent.data_ptr<float>(),
+                                                          len_ptr(lengths), s.B, s.L1, s.L2, go, ge, T,
+                                                          H.data_ptr<float>(), ws.data_ptr(), wb, cur_stream()),
+             nw ? "d2p_nw_affine_hvp" : "d2p_sw_affine_hvp");
     return H;
 }
 
-Tensor aff_jac_raw(const Tensor& scores, int param_type, float go, float ge, float T,
+Tensor aff_jac_raw(int fam, const Tensor& scores, int param_type, float go, float ge, float T,
                    const Tensor& lengths, const Shape& s) {
     Tensor J = torch::empty({s.B, s.L1, s.L2}, scores.options());
     size_t wb = 0;
-    Tensor ws = workspace(D2P_FAMILY_AFFINE, D2P_OP_PARAM_JACOBIAN, s, scores.device(), &wb);
-    check_rc(d2p_sw_affine_param_jacobian(scores.data_ptr<float>(), len_ptr(lengths), s.B, s.L1, s.L2,
-                                          param_type, go, ge, T, J.data_ptr<float>(), ws.data_ptr(), wb,
-                                          cur_stream()),
-             "d2p_sw_affine_param_jacobian");
+    Tensor ws = workspace(fam, D2P_OP_PARAM_JACOBIAN, s, scores.device(), &wb);
+    const bool nw = fam == D2P_FAMILY_NW_AFFINE;
+    check_rc((nw ? d2p_nw_affine_param_jacobian : d2p_sw_affine_param_jacobian)(
+                 scores.data_ptr<float>(), len_ptr(lengths), s.B, s.L1, s.L2, param_type, go, ge, T,
+                 J.data_ptr<float>(), ws.data_ptr(), wb, cur_stream()),
+             nw ? "d2p_nw_affine_param_jacobian" : "d2p_sw_affine_param_jacobian");
     return J;
 }
 
-std::tuple<Tensor, Tensor, Tensor, Tensor> aff_backward_full_raw(const Tensor& scores, const Tensor& G,
+std::tuple<Tensor, Tensor, Tensor, Tensor> aff_backward_full_raw(int fam, const Tensor& scores, const Tensor& G,
                                                                  float go, float ge, float T,
                                                                  const Tensor& lengths, const Shape& s) {
     auto opt = scores.options();
     Tensor gs = torch::empty({s.B, s.L1, s.L2}, opt);
     Tensor a = torch::empty({1}, opt), b = torch::empty({1}, opt), c = torch::empty({1}, opt);
     size_t wb = 0;
-    Tensor ws = workspace(D2P_FAMILY_AFFINE, D2P_OP_BACKWARD_FULL, s, scores.device(), &wb);
-    check_rc(d2p_sw_affine_backward_full(scores.data_ptr<float>(), G.data_ptr<float>(), len_ptr(lengths),
-                                         s.B, s.L1, s.L2, go, ge, T, gs.data_ptr<float>(), a.data_ptr<float>(),
-                                         b.data_ptr<float>(), c.data_ptr<float>(), ws.data_ptr(), wb,
-                                         cur_stream()),
-             "d2p_sw_affine_backward_full");
+    Tensor ws = workspace(fam, D2P_OP_BACKWARD_FULL, s, scores.device(), &wb);
+    const bool nw = fam == D2P_FAMILY_NW_AFFINE;
+    check_rc((nw ? d2p_nw_affine_backward_full : d2p_sw_affine_backward_full)(
+                 scores.data_ptr<float>(), G.data_ptr<float>(), len_ptr(lengths), s.B, s.L1, s.L2, go, ge, T,
+                 gs.data_ptr<float>(), a.data_ptr<float>(), b.data_ptr<float>(), c.data_ptr<float>(), ws.data_ptr(),
+                 wb, cur_stream()),
+             nw ? "d2p_nw_affine_backward_full" : "d2p_sw_affine_backward_full");
     return {gs, a, b, c};
 }
 
-// reference SoftSWAffineCUDAFunction (src/sw_affine/torch_cuda.cpp:126-400)
-class SoftSWAffineFunction : public torch::autograd::Function<SoftSWAffineFunction> {
+// reference SoftSWAffineCUDAFunction (src/sw_affine/torch_cuda.cpp:126-400); for
+// FAM = D2P_FAMILY_NW_AFFINE SoftNWAffineCUDAFunction
+// (src/nw_affine/torch_cuda.cpp:170-420), same outputs and gradients, fp32 scores
+template <int FAM>
+class AffFamilyFunction : public torch::autograd::Function<AffFamilyFunction<FAM>> {
    public:
     static tensor_list forward(AutogradContext* ctx, Tensor scores, Tensor gap_open, Tensor gap_ext,
                                Tensor temperature, c10::optional<Tensor> lengths_opt) {
         Tensor lengths = lengths_opt.has_value() ? *lengths_opt : Tensor();
         ctx->set_materialize_grads(false);
-        D2PB_CHECK_AFF_SCORES(scores);
+        check_aff_scores(scores, FAM);
         const Shape s = checked_affine_shape(scores);
         c10::cuda::CUDAGuard guard(scores.device());
         Param po = read_param(gap_open, scores, "gap_open");
@@ -517,7 +545,7 @@ class SoftSWAffineFunction : public torch::autograd::Function<SoftSWAffineFuncti
         Param pT = read_param(temperature, scores, "temperature");
         if (lengths.defined()) validate_lengths(lengths, s, scores.device());
         const bool want = gap_open.requires_grad() || gap_ext.requires_grad() || temperature.requires_grad();
-        AffFwd r = aff_forward(scores, po, pe, pT, lengths, s, want);
+        AffFwd r = aff_forward(FAM, scores, po, pe, pT, lengths, s, want);
         ctx->save_for_backward({scores, r.marginals, r.dparams, gap_open, gap_ext, temperature});
         ctx->saved_data["lengths"] = lengths.defined() ? c10::IValue(lengths) : c10::IValue();
         return {r.value, r.marginals};
@@ -561,7 +589,7 @@ class SoftSWAffineFunction : public torch::autograd::Function<SoftSWAffineFuncti
         if (gm.defined() && gm.numel() > 0) {
             Tensor G = prep_grad(gm, scores, "grad_posteriors");
             Tensor sf = scores.scalar_type() == torch::kFloat32 ? scores : scores.to(torch::kFloat32);
-            auto r = aff_backward_full_raw(sf, G, host_value(go), host_value(ge), host_value(temperature),
+            auto r = aff_backward_full_raw(FAM, sf, G, host_value(go), host_value(ge), host_value(temperature),
                                            lengths, s);
             grad_scores = have ? grad_scores + std::get<0>(r) : std::get<0>(r);
             if (ctx->needs_input_grad(1)) g_o = g_o + std::get<1>(r);
@@ -577,27 +605,30 @@ class SoftSWAffineFunction : public torch::autograd::Function<SoftSWAffineFuncti
     }
 };
 
-std::vector<Tensor> soft_sw_affine_cuda(Tensor scores, Tensor gap_open, Tensor gap_ext, Tensor temperature,
-                                        Tensor lengths) {
-    return SoftSWAffineFunction::apply(scores, gap_open, gap_ext, temperature, c10::optional<Tensor>(lengths));
+template <int FAM>
+std::vector<Tensor> soft_aff_cuda(Tensor scores, Tensor gap_open, Tensor gap_ext, Tensor temperature,
+                                  Tensor lengths) {
+    return AffFamilyFunction<FAM>::apply(scores, gap_open, gap_ext, temperature, c10::optional<Tensor>(lengths));
 }
 
-std::vector<Tensor> soft_sw_affine_float_cuda(Tensor scores, double gap_open, double gap_ext,
-                                              double temperature, c10::optional<Tensor> lengths) {
-    D2PB_CHECK_AFF_SCORES(scores);
+template <int FAM>
+std::vector<Tensor> soft_aff_float_cuda(Tensor scores, double gap_open, double gap_ext,
+                                        double temperature, c10::optional<Tensor> lengths) {
+    check_aff_scores(scores, FAM);
     const Shape s = checked_affine_shape(scores);
     c10::cuda::CUDAGuard guard(scores.device());
     Tensor len = resolve_lengths(lengths, s, scores.device());
     auto cpu = torch::TensorOptions().dtype(torch::kFloat32);
-    return SoftSWAffineFunction::apply(scores, torch::full({1}, (float)gap_open, cpu),
+    return AffFamilyFunction<FAM>::apply(scores, torch::full({1}, (float)gap_open, cpu),
                                        torch::full({1}, (float)gap_ext, cpu),
                                        torch::full({1}, (float)temperature, cpu),
                                        len.defined() ? c10::optional<Tensor>(len) : c10::nullopt);
 }
 
-std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor> soft_sw_affine_with_grads_cuda(
+template <int FAM>
+std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor> soft_aff_with_grads_cuda(
     Tensor scores, double gap_open, double gap_ext, double temperature, c10::optional<Tensor> lengths) {
-    D2PB_CHECK_AFF_SCORES(scores);
+    check_aff_scores(scores, FAM);
     const Shape s = checked_affine_shape(scores);
     c10::cuda::CUDAGuard guard(scores.device());
     Tensor len = resolve_lengths(lengths, s, scores.device());
@@ -605,11 +636,12 @@ std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor> soft_sw_affine_with_grads_cud
     po.host = (float)gap_open;
     pe.host = (float)gap_ext;
     pT.host = (float)temperature;
-    AffFwd r = aff_forward(scores, po, pe, pT, len, s, true);
+    AffFwd r = aff_forward(FAM, scores, po, pe, pT, len, s, true);
     return {r.value, r.marginals, r.dparams[0].clone(), r.dparams[1].clone(), r.dparams[2].clone()};
 }
 
-Tensor soft_sw_affine_hvp_cuda(Tensor scores, Tensor tangent, double gap_open, double gap_ext,
+template <int FAM>
+Tensor soft_aff_hvp_cuda(Tensor scores, Tensor tangent, double gap_open, double gap_ext,
                                double temperature, c10::optional<Tensor> lengths) {
     D2PB_CHECK_INPUT(scores);
     D2PB_CHECK_INPUT(tangent);
@@ -620,10 +652,11 @@ Tensor soft_sw_affine_hvp_cuda(Tensor scores, Tensor tangent, double gap_open, d
     const Shape s = checked_affine_shape(scores);
     c10::cuda::CUDAGuard guard(scores.device());
     Tensor len = resolve_lengths(lengths, s, scores.device());
-    return aff_hvp_raw(scores, tangent, (float)gap_open, (float)gap_ext, (float)temperature, len, s);
+    return aff_hvp_raw(FAM, scores, tangent, (float)gap_open, (float)gap_ext, (float)temperature, len, s);
 }
 
-Tensor soft_sw_affine_param_jacobian_cuda(Tensor scores, int64_t param_type, double gap_open,
+template <int FAM>
+Tensor soft_aff_param_jacobian_cuda(Tensor scores, int64_t param_type, double gap_open,
                                           double gap_ext, double temperature,
                                           c10::optional<Tensor> lengths) {
     D2PB_CHECK_INPUT(scores);
@@ -632,10 +665,11 @@ Tensor soft_sw_affine_param_jacobian_cuda(Tensor scores, int64_t param_type, dou
     const Shape s = checked_affine_shape(scores);
     c10::cuda::CUDAGuard guard(scores.device());
     Tensor len = resolve_lengths(lengths, s, scores.device());
-    return aff_jac_raw(scores, (int)param_type, (float)gap_open, (float)gap_ext, (float)temperature, len, s);
+    return aff_jac_raw(FAM, scores, (int)param_type, (float)gap_open, (float)gap_ext, (float)temperature, len, s);
 }
 
-std::tuple<Tensor, Tensor, Tensor, Tensor> soft_sw_affine_backward_full_cuda(
+template <int FAM>
+std::tuple<Tensor, Tensor, Tensor, Tensor> soft_aff_backward_full_cuda(
     Tensor scores, Tensor grad_alignment, double gap_open, double gap_ext, double temperature,
     c10::optional<Tensor> lengths) {
     D2PB_CHECK_INPUT(scores);
@@ -650,44 +684,43 @@ std::tuple<Tensor, Tensor, Tensor, Tensor> soft_sw_affine_backward_full_cuda(
     Tensor len = resolve_lengths(lengths, s, scores.device());
     Tensor G = grad_alignment.contiguous();
     if (G.scalar_type() != torch::kFloat32) G = G.to(torch::kFloat32);
-    return aff_backward_full_raw(scores, G, (float)gap_open, (float)gap_ext, (float)temperature, len, s);
+    return aff_backward_full_raw(FAM, scores, G, (float)gap_open, (float)gap_ext, (float)temperature, len, s);
 }
 
-// namespaced aliases (src/sw_affine/torch_cuda.cpp:820-911)
-std::vector<Tensor> sw_affine_forward_cuda(Tensor scores, double go, double ge, double temp,
-                                           c10::optional<Tensor> lengths) {
-    return soft_sw_affine_float_cuda(scores, go, ge, temp, lengths);
+// namespaced aliases (src/sw_affine/torch_cuda.cpp:820-911; src/nw_affine/torch_cuda.cpp:700-785)
+template <int FAM>
+std::vector<Tensor> aff_forward_alias(Tensor scores, double go, double ge, double temp,
+                                      c10::optional<Tensor> lengths) {
+    return soft_aff_float_cuda<FAM>(scores, go, ge, temp, lengths);
 }
-std::vector<Tensor> sw_affine_forward_t_cuda(Tensor scores, Tensor go, Tensor ge, Tensor temp, Tensor lengths) {
-    return soft_sw_affine_cuda(scores, go, ge, temp, lengths);
+template <int FAM>
+std::vector<Tensor> aff_forward_t_alias(Tensor scores, Tensor go, Tensor ge, Tensor temp, Tensor lengths) {
+    return soft_aff_cuda<FAM>(scores, go, ge, temp, lengths);
 }
-std::tuple<Tensor, Tensor, Tensor> sw_affine_value_grad_params_cuda(Tensor scores, double go, double ge,
-                                                                    double temp, c10::optional<Tensor> lengths) {
-    auto r = soft_sw_affine_with_grads_cuda(scores, go, ge, temp, lengths);
+template <int FAM>
+std::tuple<Tensor, Tensor, Tensor> aff_value_grad_params_alias(Tensor scores, double go, double ge, double temp,
+                                                               c10::optional<Tensor> lengths) {
+    auto r = soft_aff_with_grads_cuda<FAM>(scores, go, ge, temp, lengths);
     return {std::get<2>(r), std::get<3>(r), std::get<4>(r)};
 }
-std::tuple<Tensor, Tensor, Tensor, Tensor> sw_affine_marginals_backward_cuda(Tensor scores, Tensor g,
-                                                                             double go, double ge,
-                                                                             double temp,
-                                                                             c10::optional<Tensor> lengths) {
-    return soft_sw_affine_backward_full_cuda(scores, g, go, ge, temp, lengths);
+template <int FAM>
+std::tuple<Tensor, Tensor, Tensor, Tensor> aff_marginals_backward_alias(Tensor scores, Tensor g, double go, double ge,
+                                                                        double temp,
+                                                                        c10::optional<Tensor> lengths) {
+    return soft_aff_backward_full_cuda<FAM>(scores, g, go, ge, temp, lengths);
 }
-Tensor sw_affine_marginals_hvp_cuda(Tensor scores, Tensor v, double go, double ge, double temp,
-                                    c10::optional<Tensor> lengths) {
-    return soft_sw_affine_hvp_cuda(scores, v, go, ge, temp, lengths);
+template <int FAM>
+Tensor aff_marginals_hvp_alias(Tensor scores, Tensor v, double go, double ge, double temp,
+                               c10::optional<Tensor> lengths) {
+    return soft_aff_hvp_cuda<FAM>(scores, v, go, ge, temp, lengths);
 }
-Tensor sw_affine_marginals_grad_gap_open_cuda(Tensor scores, double go, double ge, double temp,
-                                              c10::optional<Tensor> lengths) {
-    return soft_sw_affine_param_jacobian_cuda(scores, 0, go, ge, temp, lengths);
+template <int FAM, int PT>
+Tensor aff_marginals_grad_alias(Tensor scores, double go, double ge, double temp, c10::optional<Tensor> lengths) {
+    return soft_aff_param_jacobian_cuda<FAM>(scores, PT, go, ge, temp, lengths);
 }
-Tensor sw_affine_marginals_grad_gap_ext_cuda(Tensor scores, double go, double ge, double temp,
-                                             c10::optional<Tensor> lengths) {
-    return soft_sw_affine_param_jacobian_cuda(scores, 1, go, ge, temp, lengths);
-}
-Tensor sw_affine_marginals_grad_temp_cuda(Tensor scores, double go, double ge, double temp,
-                                          c10::optional<Tensor> lengths) {
-    return soft_sw_affine_param_jacobian_cuda(scores, 2, go, ge, temp, lengths);
-}
+
+constexpr int kAff = D2P_FAMILY_AFFINE;
+constexpr int kNWAff = D2P_FAMILY_NW_AFFINE;
 
 }  // namespace
 
@@ -738,6 +771,21 @@ TORCH_LIBRARY_FRAGMENT(d2p, m) {
     m.def("sw_affine_marginals_grad_gap_open(Tensor scores, float gap_open, float gap_ext, float temp, Tensor? lengths) -> Tensor");
     m.def("sw_affine_marginals_grad_gap_ext(Tensor scores, float gap_open, float gap_ext, float temp, Tensor? lengths) -> Tensor");
     m.def("sw_affine_marginals_grad_temp(Tensor scores, float gap_open, float gap_ext, float temp, Tensor? lengths) -> Tensor");
+    // soft Needleman-Wunsch, affine gaps (src/nw_affine/registry.cpp:35-50)
+    m.def("soft_nw_affine(Tensor scores, Tensor gap_open, Tensor gap_ext, Tensor temperature, Tensor lengths) -> Tensor[]");
+    m.def("soft_nw_affine_float(Tensor scores, float gap_open, float gap_ext, float temperature, Tensor? lengths) -> Tensor[]");
+    m.def("soft_nw_affine_with_grads(Tensor scores, float gap_open, float gap_ext, float temperature, Tensor? lengths) -> (Tensor, Tensor, Tensor, Tensor, Tensor)");
+    m.def("soft_nw_affine_hvp(Tensor scores, Tensor tangent, float gap_open, float gap_ext, float temperature, Tensor? lengths) -> Tensor");
+    m.def("soft_nw_affine_param_jacobian(Tensor scores, int param_type, float gap_open, float gap_ext, float temperature, Tensor? lengths) -> Tensor");
+    m.def("soft_nw_affine_backward_full(Tensor scores, Tensor grad_alignment, float gap_open, float gap_ext, float temperature, Tensor? lengths) -> (Tensor, Tensor, Tensor, Tensor)");
+    m.def("nw_affine_forward(Tensor scores, float gap_open, float gap_ext, float temp, Tensor? lengths) -> Tensor[]");
+    m.def("nw_affine_forward_t(Tensor scores, Tensor gap_open, Tensor gap_ext, Tensor temp, Tensor lengths) -> Tensor[]");
+    m.def("nw_affine_value_grad_params(Tensor scores, float gap_open, float gap_ext, float temp, Tensor? lengths) -> (Tensor, Tensor, Tensor)");
+    m.def("nw_affine_marginals_backward(Tensor scores, Tensor grad_marginals, float gap_open, float gap_ext, float temp, Tensor? lengths) -> (Tensor, Tensor, Tensor, Tensor)");
+    m.def("nw_affine_marginals_hvp(Tensor scores, Tensor v, float gap_open, float gap_ext, float temp, Tensor? lengths) -> Tensor");
+    m.def("nw_affine_marginals_grad_gap_open(Tensor scores, float gap_open, float gap_ext, float temp, Tensor? lengths) -> Tensor");
+    m.def("nw_affine_marginals_grad_gap_ext(Tensor scores, float gap_open, float gap_ext, float temp, Tensor? lengths) -> Tensor");
+    m.def("nw_affine_marginals_grad_temp(Tensor scores, float gap_open, float gap_ext, float temp, Tensor? lengths) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(d2p, CUDA, m) {
@@ -767,20 +815,34 @@ TORCH_LIBRARY_IMPL(d2p, CUDA, m) {
     m.impl("nw_marginals_hvp", lin_marginals_hvp_alias<kNW>);
     m.impl("nw_marginals_grad_gap", lin_marginals_grad_gap_alias<kNW>);
     m.impl("nw_marginals_grad_temp", lin_marginals_grad_temp_alias<kNW>);
-    m.impl("soft_sw_affine", soft_sw_affine_cuda);
-    m.impl("soft_sw_affine_float", soft_sw_affine_float_cuda);
-    m.impl("soft_sw_affine_with_grads", soft_sw_affine_with_grads_cuda);
-    m.impl("soft_sw_affine_hvp", soft_sw_affine_hvp_cuda);
-    m.impl("soft_sw_affine_param_jacobian", soft_sw_affine_param_jacobian_cuda);
-    m.impl("soft_sw_affine_backward_full", soft_sw_affine_backward_full_cuda);
-    m.impl("sw_affine_forward", sw_affine_forward_cuda);
-    m.impl("sw_affine_forward_t", sw_affine_forward_t_cuda);
-    m.impl("sw_affine_value_grad_params", sw_affine_value_grad_params_cuda);
-    m.impl("sw_affine_marginals_backward", sw_affine_marginals_backward_cuda);
-    m.impl("sw_affine_marginals_hvp", sw_affine_marginals_hvp_cuda);
-    m.impl("sw_affine_marginals_grad_gap_open", sw_affine_marginals_grad_gap_open_cuda);
-    m.impl("sw_affine_marginals_grad_gap_ext", sw_affine_marginals_grad_gap_ext_cuda);
-    m.impl("sw_affine_marginals_grad_temp", sw_affine_marginals_grad_temp_cuda);
+    m.impl("soft_sw_affine", soft_aff_cuda<kAff>);
+    m.impl("soft_sw_affine_float", soft_aff_float_cuda<kAff>);
+    m.impl("soft_sw_affine_with_grads", soft_aff_with_grads_cuda<kAff>);
+    m.impl("soft_sw_affine_hvp", soft_aff_hvp_cuda<kAff>);
+    m.impl("soft_sw_affine_param_jacobian", soft_aff_param_jacobian_cuda<kAff>);
+    m.impl("soft_sw_affine_backward_full", soft_aff_backward_full_cuda<kAff>);
+    m.impl("sw_affine_forward", aff_forward_alias<kAff>);
+    m.impl("sw_affine_forward_t", aff_forward_t_alias<kAff>);
+    m.impl("sw_affine_value_grad_params", aff_value_grad_params_alias<kAff>);
+    m.impl("sw_affine_marginals_backward", aff_marginals_backward_alias<kAff>);
+    m.impl("sw_affine_marginals_hvp", aff_marginals_hvp_alias<kAff>);
+    m.impl("sw_affine_marginals_grad_gap_open", aff_marginals_grad_alias<kAff, 0>);
+    m.impl("sw_affine_marginals_grad_gap_ext", aff_marginals_grad_alias<kAff, 1>);
+    m.impl("sw_affine_marginals_grad_temp", aff_marginals_grad_alias<kAff, 2>);
+    m.impl("soft_nw_affine", soft_aff_cuda<kNWAff>);
+    m.impl("soft_nw_affine_float", soft_aff_float_cuda<kNWAff>);
+    m.impl("soft_nw_affine_with_grads", soft_aff_with_grads_cuda<kNWAff>);
+    m.impl("soft_nw_affine_hvp", soft_aff_hvp_cuda<kNWAff>);
+    m.impl("soft_nw_affine_param_jacobian", soft_aff_param_jacobian_cuda<kNWAff>);
+    m.impl("soft_nw_affine_backward_full", soft_aff_backward_full_cuda<kNWAff>);
+    m.impl("nw_affine_forward", aff_forward_alias<kNWAff>);
+    m.impl("nw_affine_forward_t", aff_forward_t_alias<kNWAff>);
+    m.impl("nw_affine_value_grad_params", aff_value_grad_params_alias<kNWAff>);
+    m.impl("nw_affine_marginals_backward", aff_marginals_backward_alias<kNWAff>);
+    m.impl("nw_affine_marginals_hvp", aff_marginals_hvp_alias<kNWAff>);
+    m.impl("nw_affine_marginals_grad_gap_open", aff_marginals_grad_alias<kNWAff, 0>);
+    m.impl("nw_affine_marginals_grad_gap_ext", aff_marginals_grad_alias<kNWAff, 1>);
+    m.impl("nw_affine_marginals_grad_temp", aff_marginals_grad_alias<kNWAff, 2>);
 }
 
 // No CPU kernels by design: CPU tensors get a clear error instead of a silent
@@ -802,7 +864,11 @@ TORCH_LIBRARY_IMPL(d2p, CPU, m) {
         "sw_affine_marginals_hvp", "sw_affine_marginals_grad_gap_open", "sw_affine_marginals_grad_gap_ext",
         "sw_affine_marginals_grad_temp", "soft_nw", "soft_nw_float", "soft_nw_with_grads", "soft_nw_hvp",
         "soft_nw_param_jacobian", "soft_nw_backward_full", "nw_forward", "nw_forward_t", "nw_value_grad_params",
-        "nw_marginals_backward", "nw_marginals_hvp", "nw_marginals_grad_gap", "nw_marginals_grad_temp"};
+        "nw_marginals_backward", "nw_marginals_hvp", "nw_marginals_grad_gap", "nw_marginals_grad_temp",
+        "soft_nw_affine", "soft_nw_affine_float", "soft_nw_affine_with_grads", "soft_nw_affine_hvp",
+        "soft_nw_affine_param_jacobian", "soft_nw_affine_backward_full", "nw_affine_forward", "nw_affine_forward_t",
+        "nw_affine_value_grad_params", "nw_affine_marginals_backward", "nw_affine_marginals_hvp",
+        "nw_affine_marginals_grad_gap_open", "nw_affine_marginals_grad_gap_ext", "nw_affine_marginals_grad_temp"};
     for (const char* name : kOps) m.impl(name, torch::CppFunction::makeFromBoxedFunction<&reject_cpu>());
 }
 
@@ -842,16 +908,16 @@ std::vector<Tensor> fwd_f_autograd(Tensor scores, double gap, double temperature
     }
     return soft_lin_float_cuda<FAM>(scores, gap, temperature, lengths);
 }
-template <const char* Name>
+template <const char* Name, int FAM>
 std::vector<Tensor> aff_fwd_t_autograd(Tensor scores, Tensor go, Tensor ge, Tensor temperature, Tensor lengths) {
     if (is_python_tensor(scores)) {
         static auto op = op_handle<AffForwardT>(Name);
         at::AutoDispatchBelowADInplaceOrView below;
         return op.call(scores, go, ge, temperature, lengths);
     }
-    return soft_sw_affine_cuda(scores, go, ge, temperature, lengths);
+    return soft_aff_cuda<FAM>(scores, go, ge, temperature, lengths);
 }
-template <const char* Name>
+template <const char* Name, int FAM>
 std::vector<Tensor> aff_fwd_f_autograd(Tensor scores, double go, double ge, double temperature,
                                        c10::optional<Tensor> lengths) {
     if (is_python_tensor(scores)) {
@@ -859,7 +925,7 @@ std::vector<Tensor> aff_fwd_f_autograd(Tensor scores, double go, double ge, doub
         at::AutoDispatchBelowADInplaceOrView below;
         return op.call(scores, go, ge, temperature, lengths);
     }
-    return soft_sw_affine_float_cuda(scores, go, ge, temperature, lengths);
+    return soft_aff_float_cuda<FAM>(scores, go, ge, temperature, lengths);
 }
 
 constexpr char kSoftSW[] = "d2p::soft_sw";
@@ -874,6 +940,10 @@ constexpr char kSoftNW[] = "d2p::soft_nw";
 constexpr char kSoftNWFloat[] = "d2p::soft_nw_float";
 constexpr char kNWForward[] = "d2p::nw_forward";
 constexpr char kNWForwardT[] = "d2p::nw_forward_t";
+constexpr char kSoftNWAffine[] = "d2p::soft_nw_affine";
+constexpr char kSoftNWAffineFloat[] = "d2p::soft_nw_affine_float";
+constexpr char kNWAffineForward[] = "d2p::nw_affine_forward";
+constexpr char kNWAffineForwardT[] = "d2p::nw_affine_forward_t";
 
 TORCH_LIBRARY_IMPL(d2p, AutogradCUDA, m) {
     m.impl("soft_sw", fwd_t_autograd<kSoftSW, kSW>);
@@ -884,8 +954,12 @@ TORCH_LIBRARY_IMPL(d2p, AutogradCUDA, m) {
     m.impl("soft_nw_float", fwd_f_autograd<kSoftNWFloat, kNW>);
     m.impl("nw_forward", fwd_f_autograd<kNWForward, kNW>);
     m.impl("nw_forward_t", fwd_t_autograd<kNWForwardT, kNW>);
-    m.impl("soft_sw_affine", aff_fwd_t_autograd<kSoftSWAffine>);
-    m.impl("soft_sw_affine_float", aff_fwd_f_autograd<kSoftSWAffineFloat>);
-    m.impl("sw_affine_forward", aff_fwd_f_autograd<kSWAffineForward>);
-    m.impl("sw_affine_forward_t", aff_fwd_t_autograd<kSWAffineForwardT>);
+    m.impl("soft_sw_affine", aff_fwd_t_autograd<kSoftSWAffine, kAff>);
+    m.impl("soft_sw_affine_float", aff_fwd_f_autograd<kSoftSWAffineFloat, kAff>);
+    m.impl("sw_affine_forward", aff_fwd_f_autograd<kSWAffineForward, kAff>);
+    m.impl("sw_affine_forward_t", aff_fwd_t_autograd<kSWAffineForwardT, kAff>);
+    m.impl("soft_nw_affine", aff_fwd_t_autograd<kSoftNWAffine, kNWAff>);
+    m.impl("soft_nw_affine_float", aff_fwd_f_autograd<kSoftNWAffineFloat, kNWAff>);
+    m.impl("nw_affine_forward", aff_fwd_f_autograd<kNWAffineForward, kNWAff>);
+    m.impl("nw_affine_forward_t", aff_fwd_t_autograd<kNWAffineForwardT, kNWAff>);
 }

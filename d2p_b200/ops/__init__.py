@@ -15,6 +15,10 @@ from .._ops import (  # noqa: F401
     soft_nw, soft_nw_float, soft_nw_with_grads, soft_nw_hvp, soft_nw_param_jacobian, soft_nw_backward_full,
     nw_forward, nw_forward_t, nw_value_grad_params, nw_marginals_backward, nw_marginals_hvp,
     nw_marginals_grad_gap, nw_marginals_grad_temp,
+    soft_nw_affine, soft_nw_affine_float, soft_nw_affine_with_grads, soft_nw_affine_hvp,
+    soft_nw_affine_param_jacobian, soft_nw_affine_backward_full, nw_affine_forward, nw_affine_forward_t,
+    nw_affine_value_grad_params, nw_affine_marginals_backward, nw_affine_marginals_hvp,
+    nw_affine_marginals_grad_gap_open, nw_affine_marginals_grad_gap_ext, nw_affine_marginals_grad_temp,
 )
 
 __all__ = [
@@ -31,4 +35,8 @@ __all__ = [
     "soft_nw", "soft_nw_float", "soft_nw_with_grads", "soft_nw_hvp", "soft_nw_param_jacobian",
     "soft_nw_backward_full", "nw_forward", "nw_forward_t", "nw_value_grad_params", "nw_marginals_backward",
     "nw_marginals_hvp", "nw_marginals_grad_gap", "nw_marginals_grad_temp",
+    "soft_nw_affine", "soft_nw_affine_float", "soft_nw_affine_with_grads", "soft_nw_affine_hvp",
+    "soft_nw_affine_param_jacobian", "soft_nw_affine_backward_full", "nw_affine_forward", "nw_affine_forward_t",
+    "nw_affine_value_grad_params", "nw_affine_marginals_backward", "nw_affine_marginals_hvp",
+    "nw_affine_marginals_grad_gap_open", "nw_affine_marginals_grad_gap_ext", "nw_affine_marginals_grad_temp",
 ]

@@ -50,6 +50,7 @@ extern "C" {
 #define D2P_FAMILY_LINEAR 0
 #define D2P_FAMILY_AFFINE 1
 #define D2P_FAMILY_NW 2 /* soft Needleman-Wunsch, linear gap (d2p_nw_*) */
+#define D2P_FAMILY_NW_AFFINE 3 /* soft Needleman-Wunsch, affine gaps (d2p_nw_affine_*) */
 
 #define D2P_OP_FORWARD_BACKWARD 0
 #define D2P_OP_HVP 1
@@ -228,6 +229,33 @@ D2P_API int d2p_nw_backward_full(const float* scores, const float* grad_marginal
                                  int L1, int L2, float gap, float temperature, float* grad_scores,
                                  float* grad_gap, float* grad_temperature, void* workspace,
                                  size_t workspace_bytes, void* stream);
+
+/* ---- soft Needleman-Wunsch with affine gaps (states M, I, D) ----
+ * M(0,0) = 0, I(i,0) = gap_open + (i-1) gap_ext, D(0,j) = gap_open + (j-1)
+ * gap_ext; S = the logsumexp of the three states at (L1, L2); marginal = the
+ * probability that the path visits M at (i, j).  fp32 scores.  Workspace from
+ * d2p_sw_workspace_bytes(D2P_FAMILY_NW_AFFINE, op, ...); param_type 0 =
+ * gap_open, 1 = gap_ext, 2 = temperature; the gradient outputs of
+ * forward_backward may be NULL.  They replace the reference's nw_affine
+ * launchers (src/nw_affine/kernels.cuh) behind its soft_nw_affine operators
+ * (src/nw_affine/torch_cuda.cpp, src/nw_affine/registry.cpp:35-50). */
+D2P_API int d2p_nw_affine_forward_backward(const float* scores, const int* lengths, int B, int L1, int L2,
+                                           float gap_open, float gap_ext, float temperature,
+                                           const float* gap_open_dev, const float* gap_ext_dev,
+                                           const float* temperature_dev, float* value, float* marginals,
+                                           float* grad_gap_open, float* grad_gap_ext, float* grad_temperature,
+                                           void* workspace, size_t workspace_bytes, void* stream);
+D2P_API int d2p_nw_affine_hvp(const float* scores, const float* tangent, const int* lengths, int B, int L1,
+                              int L2, float gap_open, float gap_ext, float temperature, float* hvp,
+                              void* workspace, size_t workspace_bytes, void* stream);
+D2P_API int d2p_nw_affine_param_jacobian(const float* scores, const int* lengths, int B, int L1, int L2,
+                                         int param_type, float gap_open, float gap_ext, float temperature,
+                                         float* jacobian, void* workspace, size_t workspace_bytes, void* stream);
+D2P_API int d2p_nw_affine_backward_full(const float* scores, const float* grad_marginals, const int* lengths,
+                                        int B, int L1, int L2, float gap_open, float gap_ext, float temperature,
+                                        float* grad_scores, float* grad_gap_open, float* grad_gap_ext,
+                                        float* grad_temperature, void* workspace, size_t workspace_bytes,
+                                        void* stream);
 
 /* Engine selection for the whole process (all devices): D2P_ENGINE_AUTO picks
  * per shape (the default, or what D2P_B200_ENGINE names at load: "plane",

@@ -78,6 +78,13 @@ SCHEMAS.update({
         SCHEMAS[name].replace("soft_sw", "soft_nw").replace("sw_", "nw_")
     for name in list(SCHEMAS) if "affine" not in name
 })
+# src/nw_affine/registry.cpp:35-50, verbatim: the affine soft Smith-Waterman
+# schemas under the Needleman-Wunsch names
+SCHEMAS.update({
+    name.replace("soft_sw", "soft_nw").replace("sw_", "nw_"):
+        SCHEMAS[name].replace("soft_sw", "soft_nw").replace("sw_", "nw_")
+    for name in list(SCHEMAS) if "affine" in name and "sw" in name
+})
 
 
 def _schema(name):
@@ -97,7 +104,8 @@ def _call_args(name, s, B):
     fl = (-2.0, -0.5, 1.0) if aff else (-1.0, 1.0)
     t = [s.new_tensor([v]) for v in fl]
     ln = torch.full((B, 2), 1, dtype=torch.int32, device=s.device)
-    if name in ("soft_sw", "sw_forward_t", "soft_sw_affine", "sw_affine_forward_t", "soft_nw", "nw_forward_t"):
+    if name in ("soft_sw", "sw_forward_t", "soft_sw_affine", "sw_affine_forward_t", "soft_nw", "nw_forward_t",
+                "soft_nw_affine", "nw_affine_forward_t"):
         return (s, *t, ln)
     if "hvp" in name or "backward" in name:
         return (s, torch.zeros_like(s), *fl, None)
@@ -119,7 +127,7 @@ LAYOUT = {
     "sw_affine_marginals_grad_gap_ext": "P", "sw_affine_marginals_grad_temp": "P",
 }
 LAYOUT.update({k.replace("soft_sw", "soft_nw").replace("sw_", "nw_"): v for k, v in list(LAYOUT.items())
-               if "affine" not in k})
+               if "sw" in k})
 
 
 @pytest.mark.parametrize("name", sorted(SCHEMAS))
@@ -139,7 +147,8 @@ def test_fake_kernels_give_the_reference_shapes(name):
 
 
 @pytest.mark.parametrize("name", ["soft_sw_float", "soft_sw_hvp", "soft_sw_affine_float", "sw_affine_marginals_hvp",
-                                  "soft_nw_float", "nw_marginals_backward"])
+                                  "soft_nw_float", "nw_marginals_backward", "soft_nw_affine_float",
+                                  "nw_affine_marginals_hvp"])
 def test_cpu_tensors_are_rejected(name):
     """No CPU kernel and no silent fallback: a CPU input raises, naming CUDA."""
     s = torch.randn(2, 4, 5)

@@ -269,7 +269,7 @@ def test_fake_shapes_match_real_outputs(d2p, cuda_device):
 
 
 @pytest.mark.parametrize("tensor_params", [False, True])
-@pytest.mark.parametrize("family", ["linear", "affine", "nw"])
+@pytest.mark.parametrize("family", ["linear", "affine", "nw", "nw_affine"])
 def test_compile_fullgraph_forward_backward(d2p, cuda_device, family, tensor_params):
     """torch.compile(fullgraph=True) traces the public API through the
     d2p_py:: custom ops and their autograd formulas: value, marginals and every
@@ -296,6 +296,9 @@ def test_compile_fullgraph_forward_backward(d2p, cuda_device, family, tensor_par
             r = d2p.soft_sw(s, gap=params[0], temperature=params[1])
         elif family == "nw":
             r = d2p.soft_nw(s, gap=params[0], temperature=params[1])
+            return r.score.sum() + (r.alignment * W).sum(), r.score, r.alignment
+        elif family == "nw_affine":
+            r = d2p.soft_nw_affine(s, gap_open=params[0], gap_ext=params[1], temperature=params[2])
             return r.score.sum() + (r.alignment * W).sum(), r.score, r.alignment
         else:
             r = d2p.soft_sw_affine(s, gap_open=params[0], gap_ext=params[1], temperature=params[2])
