@@ -524,3 +524,96 @@ def nw_affine_backward_full(scores, grad_alignment, lengths=None, gap_open=-2.0,
     gs = nw_affine_hvp(scores, G, lengths, gap_open, gap_ext, T, impl)
     js = [nw_affine_param_jacobian(scores, p, lengths, gap_open, gap_ext, T, impl) for p in (0, 1, 2)]
     return (gs,) + tuple(np.array([(G * j).sum()], dt) for j in js)
+
+
+# ----------------------------------------------------------------------------
+# soft DTW: dtw_oracle.c, or the reference's src/dtw/kernels_cpu.cpp;
+# op-level orchestration as src/dtw/torch_cpu.cpp (bandwidth < 0: no band)
+# ----------------------------------------------------------------------------
+_L = ctypes.c_int64
+
+
+def _dtw_call(impl, name_ref, name_oracle):
+    if impl == "ref":
+        return _lib("ref"), name_ref, _F
+    return _lib("oracle"), name_oracle + ("_f64" if impl == "f64" else "_f32"), (_D if impl == "f64" else _F)
+
+
+def dtw(costs, lengths=None, T=1.0, bandwidth=-1, impl="f32") -> dict:
+    """value, marginals (visit probabilities), grad_T (+ alpha) as soft_dtw_with_grads."""
+    dt = _dt(impl)
+    c = _arr(costs, dt)
+    B, L1, L2 = c.shape
+    ln = _lens(lengths, B, L1, L2)
+    A = (L1 + 1) * (L2 + 1)
+    alpha = np.zeros((B, A), dt)
+    beta = np.zeros((B, A), dt)
+    value = np.zeros(B, dt)
+    marg = np.zeros((B, L1, L2), dt)
+    gT = np.zeros(B, dt)
+    lib, name, R = _dtw_call(impl, "dtw_forward_cpu", "oracle_dtw_forward")
+    if impl == "ref":
+        _fn(lib, name, [_P] * 4 + [_I] * 3 + [_F, _L])(_ptr(c), _ptr(alpha), _ptr(value), _ptr(ln), B, L1, L2, T,
+                                                        bandwidth)
+        _fn(lib, "dtw_backward_cpu", [_P] * 7 + [_I] * 3 + [_F, _L])(
+            _ptr(alpha), _ptr(c), _ptr(value), _ptr(beta), _ptr(marg), _ptr(gT), _ptr(ln), B, L1, L2, T, bandwidth)
+    else:
+        _fn(lib, name, [_P, _P, _I, _I, _I, R, _L, _P, _P])(_ptr(c), _ptr(ln), B, L1, L2, T, bandwidth, _ptr(alpha),
+                                                           _ptr(value))
+        _fn(lib, name.replace("forward", "backward"), [_P, _P, _I, _I, _I, R, _L] + [_P] * 4)(
+            _ptr(c), _ptr(ln), B, L1, L2, T, bandwidth, _ptr(alpha), _ptr(beta), _ptr(marg), _ptr(gT))
+    return {"value": value, "marginals": marg, "grad_T": gT, "alpha": alpha}
+
+
+def dtw_hvp(costs, V, lengths=None, T=1.0, bandwidth=-1, impl="f32") -> np.ndarray:
+    dt = _dt(impl)
+    c = _arr(costs, dt)
+    v = _arr(V, dt)
+    B, L1, L2 = c.shape
+    ln = _lens(lengths, B, L1, L2)
+    base = dtw(c, ln, T, bandwidth, impl)
+    alpha, value = base["alpha"], base["value"]
+    A = (L1 + 1) * (L2 + 1)
+    w1, w2, w3 = (np.zeros((B, A), dt) for _ in range(3))
+    H = np.zeros((B, L1, L2), dt)
+    lib, name, R = _dtw_call(impl, "dtw_hvp_cpu", "oracle_dtw_hvp")
+    if impl == "ref":
+        dsc = np.zeros(B, dt)
+        _fn(lib, name, [_P] * 10 + [_I] * 3 + [_F, _L])(
+            _ptr(alpha), _ptr(c), _ptr(value), _ptr(v), _ptr(w1), _ptr(dsc), _ptr(w2), _ptr(w3), _ptr(H), _ptr(ln),
+            B, L1, L2, T, bandwidth)
+    else:
+        _fn(lib, name, [_P, _P, _P, _I, _I, _I, R, _L] + [_P] * 5)(
+            _ptr(c), _ptr(v), _ptr(ln), B, L1, L2, T, bandwidth, _ptr(alpha), _ptr(w1), _ptr(w2), _ptr(w3), _ptr(H))
+    return H
+
+
+def dtw_param_jacobian(costs, lengths=None, T=1.0, bandwidth=-1, impl="f32") -> np.ndarray:
+    """dP/dT, as soft_dtw_param_jacobian."""
+    dt = _dt(impl)
+    c = _arr(costs, dt)
+    B, L1, L2 = c.shape
+    ln = _lens(lengths, B, L1, L2)
+    base = dtw(c, ln, T, bandwidth, impl)
+    alpha, value = base["alpha"], base["value"]
+    A = (L1 + 1) * (L2 + 1)
+    w1, w2, w3 = (np.zeros((B, A), dt) for _ in range(3))
+    dP = np.zeros((B, L1, L2), dt)
+    lib, name, R = _dtw_call(impl, "dtw_param_grad_cpu", "oracle_dtw_param_grad")
+    if impl == "ref":
+        _fn(lib, name, [_P] * 8 + [_I] * 3 + [_F, _L])(
+            _ptr(alpha), _ptr(c), _ptr(value), _ptr(w1), _ptr(w2), _ptr(w3), _ptr(dP), _ptr(ln), B, L1, L2, T,
+            bandwidth)
+    else:
+        _fn(lib, name, [_P, _P, _I, _I, _I, R, _L] + [_P] * 5)(
+            _ptr(c), _ptr(ln), B, L1, L2, T, bandwidth, _ptr(alpha), _ptr(w1), _ptr(w2), _ptr(w3), _ptr(dP))
+    return dP
+
+
+def dtw_backward_full(costs, grad_alignment, lengths=None, T=1.0, bandwidth=-1, impl="f32"):
+    """(grad_costs, grad_T[1]) as soft_dtw_backward_full (src/dtw/torch_cpu.cpp)."""
+    dt = _dt(impl)
+    G = _arr(grad_alignment, dt)
+    gs = dtw_hvp(costs, G, lengths, T, bandwidth, impl)
+    j = dtw_param_jacobian(costs, lengths, T, bandwidth, impl)
+    return gs, np.array([(G * j).sum()], dt)

@@ -1,6 +1,6 @@
 """Generate the golden fixtures in tests/golden/ from the REFERENCE's own CPU
 kernels (src/sw/kernels_cpu.cpp, src/sw_affine/kernels_cpu.cpp,
-src/nw/kernels_cpu.cpp, src/nw_affine/kernels_cpu.cpp compiled from the reference sources into
+src/nw/kernels_cpu.cpp, src/nw_affine/kernels_cpu.cpp, src/dtw/kernels_cpu.cpp compiled from the reference sources into
 oracle/_ref/libref_sw_cpu.so by oracle/Makefile).
 
 Run in a container where the reference sources are present:
@@ -34,6 +34,13 @@ NW_CASES = [
 ]
 # the affine gap penalties of the Needleman-Wunsch edge cases
 NW_AFFINE = (-1.5, -0.4)
+
+# soft DTW (files named dtw_*): name, B, L1, L2, T, bandwidth (-1: none), lengths
+DTW_CASES = [
+    ("dtw_full", 3, 9, 12, 1.0, -1, None),
+    ("dtw_band", 5, 11, 8, 0.5, 2, [[11, 8], [0, 8], [11, 0], [7, 8], [11, 5]]),
+    ("dtw_sharp", 2, 10, 10, 0.1, 3, None),
+]
 
 
 def main():
@@ -85,6 +92,22 @@ def main():
                    gap_open=np.float32(go), gap_ext=np.float32(ge), lengths=ln)
         out.update(_nw_outputs(s, V, G, ln, gap, T))
         out.update(_nwa_outputs(s, V, G, ln, go, ge, T))
+        np.savez_compressed(os.path.join(HERE, name + ".npz"), **out)
+        print("wrote", name)
+    # soft DTW: non-negative costs, with and without a band, empty sequences
+    for name, B, L1, L2, T, bw, lens in DTW_CASES:
+        g = torch.Generator().manual_seed(zlib.crc32(name.encode()))
+        c = torch.rand(B, L1, L2, generator=g).numpy()
+        V = torch.randn(B, L1, L2, generator=g).numpy()
+        G = torch.randn(B, L1, L2, generator=g).numpy()
+        ln = np.array(lens, np.int32) if lens is not None else np.tile(np.array([[L1, L2]], np.int32), (B, 1))
+        out = dict(costs=c, tangent=V, grad_marginals=G, T=np.float32(T), bandwidth=np.int64(bw), lengths=ln)
+        r = oracle.dtw(c, ln, T, bw, "ref")
+        for k in ("value", "marginals", "grad_T"):
+            out["dtw_" + k] = r[k]
+        out["dtw_hvp"] = oracle.dtw_hvp(c, V, ln, T, bw, "ref")
+        out["dtw_jac"] = oracle.dtw_param_jacobian(c, ln, T, bw, "ref")
+        out["dtw_bf_costs"], out["dtw_bf_T"] = oracle.dtw_backward_full(c, G, ln, T, bw, "ref")
         np.savez_compressed(os.path.join(HERE, name + ".npz"), **out)
         print("wrote", name)
 

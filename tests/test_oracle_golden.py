@@ -12,8 +12,9 @@ import oracle
 
 ALL = sorted(glob.glob(os.path.join(os.path.dirname(__file__), "golden", "*.npz")))
 # Smith-Waterman fixtures; files named nw_* hold Needleman-Wunsch cases only
-GOLDEN = [p for p in ALL if not os.path.basename(p).startswith("nw_")]
+GOLDEN = [p for p in ALL if not os.path.basename(p).startswith(("nw_", "dtw_"))]
 NW_GOLDEN = [p for p in ALL if "nw_value" in np.load(p).files]
+DTW_GOLDEN = [p for p in ALL if "dtw_value" in np.load(p).files]
 
 
 def _load(path):
@@ -174,3 +175,28 @@ def test_nw_affine_restatement_matches_reference_golden(path):
             want = 0.0 if n == 0 else go + (n - 1) * ge
             assert abs(float(r64["value"][b]) - want) < 1e-9, (b, r64["value"][b], want)
             assert np.all(r64["marginals"][b] == 0)
+
+
+@pytest.mark.parametrize("path", DTW_GOLDEN, ids=[os.path.basename(p) for p in DTW_GOLDEN])
+def test_dtw_restatement_matches_reference_golden(path):
+    """dtw_oracle.c reproduces the reference's src/dtw/kernels_cpu.cpp bit for
+    bit, with and without a Sakoe-Chiba band and with empty sequences (whose
+    value stays at the +inf sentinel 1e30, as in the reference)."""
+    z = np.load(path)
+    c, ln, T, bw = z["costs"], z["lengths"], float(z["T"]), int(z["bandwidth"])
+    r = oracle.dtw(c, ln, T, bw, "f32")
+    for k in ("value", "marginals", "grad_T"):
+        _close(r[k], z["dtw_" + k], 0, 0, k)
+    _close(oracle.dtw_hvp(c, z["tangent"], ln, T, bw, "f32"), z["dtw_hvp"], 0, 0, "hvp")
+    _close(oracle.dtw_param_jacobian(c, ln, T, bw, "f32"), z["dtw_jac"], 0, 0, "jac")
+    bf = oracle.dtw_backward_full(c, z["grad_marginals"], ln, T, bw, "f32")
+    _close(bf[0], z["dtw_bf_costs"], 0, 0, "bf costs")
+    _close(bf[1], z["dtw_bf_T"], 1e-6, 1e-7, "bf T")
+    r64 = oracle.dtw(c, ln, T, bw, "f64")
+    fin = np.abs(z["dtw_value"]) < 1e29
+    _close(r64["value"][fin], z["dtw_value"][fin], 1e-5, 1e-5, "f64 value")
+    _close(r64["marginals"], z["dtw_marginals"], 1e-4, 1e-5, "f64 marginals")
+    # every warping path ends at (L1, L2): the marginals of the last cell are 1
+    for b, (l1, l2) in enumerate(ln):
+        if l1 > 0 and l2 > 0:
+            assert abs(r64["marginals"][b, l1 - 1, l2 - 1] - 1.0) < 1e-12
