@@ -1,6 +1,6 @@
 """d2p_b200 -- B200-native (sm_100a) soft Smith-Waterman operators, a drop-in for
 d2p's ``soft_sw`` / ``soft_sw_affine`` path, plus the soft Needleman-Wunsch
-operators (``soft_nw``, ``soft_nw_affine``).
+operators (``soft_nw``, ``soft_nw_affine``) and soft DTW (``soft_dtw``).
 
     import d2p_b200 as d2p
     result = d2p.soft_sw(scores, gap=-1.0, temperature=1.0)        # value [B], marginals [B,L1,L2]
@@ -16,6 +16,7 @@ from . import _pt2_ops  # the d2p_py:: custom ops torch.compile traces
 _ops._pt2_mod = _pt2_ops
 from .sw import SoftSW, SoftSWAffine, SWResult, soft_sw, soft_sw_affine
 from .nw import NWResult, SoftNW, SoftNWAffine, soft_nw, soft_nw_affine
+from .dtw import DTWResult, SoftDTW, soft_dtw
 from . import ops
 from .engine import engine_counts, set_engine, use_engine
 
@@ -40,6 +41,11 @@ soft_nw_affine_with_grads = _ops.soft_nw_affine_with_grads
 soft_nw_affine_hvp = _ops.soft_nw_affine_hvp
 soft_nw_affine_param_jacobian = _ops.soft_nw_affine_param_jacobian
 soft_nw_affine_backward_full = _ops.soft_nw_affine_backward_full
+soft_dtw_float = _ops.soft_dtw_float
+soft_dtw_with_grads = _ops.soft_dtw_with_grads
+soft_dtw_hvp = _ops.soft_dtw_hvp
+soft_dtw_param_jacobian = _ops.soft_dtw_param_jacobian
+soft_dtw_backward_full = _ops.soft_dtw_backward_full
 
 __version__ = "0.1.0"
 
@@ -51,5 +57,6 @@ __all__ = [
     "soft_nw", "NWResult", "SoftNW", "soft_nw_float", "soft_nw_with_grads", "soft_nw_hvp",
     "soft_nw_param_jacobian", "soft_nw_backward_full", "soft_nw_affine", "SoftNWAffine", "soft_nw_affine_float",
     "soft_nw_affine_with_grads", "soft_nw_affine_hvp", "soft_nw_affine_param_jacobian",
-    "soft_nw_affine_backward_full",
+    "soft_nw_affine_backward_full", "soft_dtw", "DTWResult", "SoftDTW", "soft_dtw_float", "soft_dtw_with_grads",
+    "soft_dtw_hvp", "soft_dtw_param_jacobian", "soft_dtw_backward_full",
 ]

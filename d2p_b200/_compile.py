@@ -1,5 +1,5 @@
-"""Fake-tensor (meta) shapes and autocast rules for the soft Smith-Waterman and
-soft Needleman-Wunsch ops.
+"""Fake-tensor (meta) shapes and autocast rules for the soft Smith-Waterman,
+soft Needleman-Wunsch and soft DTW ops.
 
 Mirrors d2p/_compile.py:18-250 (register_fake) and :857-901 (register_autocast)
 for the sw / sw_affine families.  Output shapes per op:
@@ -84,6 +84,13 @@ _OUTPUTS = {
     "nw_affine_marginals_grad_gap_open": _P,
     "nw_affine_marginals_grad_gap_ext": _P,
     "nw_affine_marginals_grad_temp": _P,
+    # soft DTW (d2p/_compile.py:371-415)
+    "soft_dtw": [_B, _P],
+    "soft_dtw_float": [_B, _P],
+    "soft_dtw_with_grads": (_B, _P, _B),
+    "soft_dtw_hvp": _P,
+    "soft_dtw_param_jacobian": _P,
+    "soft_dtw_backward_full": (_P, _ONE),
 }
 
 

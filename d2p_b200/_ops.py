@@ -1,8 +1,9 @@
 """Low-level operator access: loads the native libraries and wraps torch.ops.d2p.*.
 
 Mirrors d2p/_ops.py (loader :25-167, soft Smith-Waterman wrappers :170-210,
-soft Needleman-Wunsch wrappers :241-254) for the soft Smith-Waterman and soft
-Needleman-Wunsch (linear and affine gaps) operators.  The extension is in-tree (``_C.so`` next to this
+soft Needleman-Wunsch wrappers :241-254, soft DTW wrappers :217-222) for the
+soft Smith-Waterman, soft Needleman-Wunsch (linear and affine gaps) and soft
+DTW operators.  The extension is in-tree (``_C.so`` next to this
 file, linked to ``libd2p_b200.so``); there is no CPU kernel and no fallback:
 importing fails loudly when the extension is missing, and CPU tensors are
 rejected by the ops themselves.
@@ -182,6 +183,14 @@ nw_affine_marginals_grad_gap_open = _wrap("nw_affine_marginals_grad_gap_open")
 nw_affine_marginals_grad_gap_ext = _wrap("nw_affine_marginals_grad_gap_ext")
 nw_affine_marginals_grad_temp = _wrap("nw_affine_marginals_grad_temp")
 
+# soft DTW
+soft_dtw = _wrap("soft_dtw")
+soft_dtw_float = _wrap("soft_dtw_float")
+soft_dtw_with_grads = _wrap("soft_dtw_with_grads")
+soft_dtw_hvp = _wrap("soft_dtw_hvp")
+soft_dtw_param_jacobian = _wrap("soft_dtw_param_jacobian")
+soft_dtw_backward_full = _wrap("soft_dtw_backward_full")
+
 OP_NAMES = (
     "soft_sw", "soft_sw_float", "soft_sw_with_grads", "soft_sw_hvp", "soft_sw_param_jacobian",
     "soft_sw_backward_full", "sw_forward", "sw_forward_t", "sw_value_grad_params",
@@ -198,4 +207,6 @@ OP_NAMES = (
     "soft_nw_affine_param_jacobian", "soft_nw_affine_backward_full", "nw_affine_forward", "nw_affine_forward_t",
     "nw_affine_value_grad_params", "nw_affine_marginals_backward", "nw_affine_marginals_hvp",
     "nw_affine_marginals_grad_gap_open", "nw_affine_marginals_grad_gap_ext", "nw_affine_marginals_grad_temp",
+    "soft_dtw", "soft_dtw_float", "soft_dtw_with_grads", "soft_dtw_hvp", "soft_dtw_param_jacobian",
+    "soft_dtw_backward_full",
 )

@@ -1,7 +1,7 @@
 """PT2-safe custom ops (``d2p_py::*``) used while compiling or on fake tensors.
 
-Mirrors the soft Smith-Waterman and soft Needleman-Wunsch parts of
-d2p/_pt2_ops.py:72-660: each op wraps
+Mirrors the soft Smith-Waterman, soft Needleman-Wunsch and soft DTW parts of
+d2p/_pt2_ops.py:72-1010: each op wraps
 the dispatcher op, carries a fake implementation, and the differentiable ones
 (``soft_sw``, ``soft_sw_float``, affine analogues) register an autograd formula
 built from the saved marginals (value branch) and ``*_backward_full`` (marginal
@@ -324,3 +324,141 @@ def _make_affine_family(prefix: str):
 
 globals().update(_make_affine_family("soft_sw_affine"))
 globals().update(_make_affine_family("soft_nw_affine"))
+
+
+# --------------------------------------------------------------------------- soft DTW
+# (d2p/_pt2_ops.py:905-1010): the temperature is the one parameter; bandwidth
+# is an int (< 0: no band)
+@custom_op("d2p_py::soft_dtw_with_grads", mutates_args=())
+def soft_dtw_with_grads(costs: torch.Tensor, temperature: float, lengths: Optional[torch.Tensor],
+                        bandwidth: Optional[int]) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    v, m, gt = torch.ops.d2p.soft_dtw_with_grads(costs, temperature, lengths, bandwidth)
+    return v, m, gt
+
+
+@soft_dtw_with_grads.register_fake
+def _(costs, temperature, lengths, bandwidth):
+    return _like(costs, "B", "P", "B")
+
+
+@custom_op("d2p_py::soft_dtw_hvp", mutates_args=())
+def soft_dtw_hvp(costs: torch.Tensor, tangent: torch.Tensor, temperature: float, lengths: Optional[torch.Tensor],
+                 bandwidth: Optional[int]) -> torch.Tensor:
+    return torch.ops.d2p.soft_dtw_hvp(costs, tangent, temperature, lengths, bandwidth)
+
+
+@soft_dtw_hvp.register_fake
+def _(costs, tangent, temperature, lengths, bandwidth):
+    return _like(costs, "P")
+
+
+@custom_op("d2p_py::soft_dtw_param_jacobian", mutates_args=())
+def soft_dtw_param_jacobian(costs: torch.Tensor, temperature: float, lengths: Optional[torch.Tensor],
+                            bandwidth: Optional[int]) -> torch.Tensor:
+    return torch.ops.d2p.soft_dtw_param_jacobian(costs, temperature, lengths, bandwidth)
+
+
+@soft_dtw_param_jacobian.register_fake
+def _(costs, temperature, lengths, bandwidth):
+    return _like(costs, "P")
+
+
+@custom_op("d2p_py::soft_dtw_backward_full", mutates_args=())
+def soft_dtw_backward_full(costs: torch.Tensor, grad_alignment: torch.Tensor, temperature: float,
+                           lengths: Optional[torch.Tensor],
+                           bandwidth: Optional[int]) -> tuple[torch.Tensor, torch.Tensor]:
+    a, b = torch.ops.d2p.soft_dtw_backward_full(costs, grad_alignment, temperature, lengths, bandwidth)
+    return a, b
+
+
+@soft_dtw_backward_full.register_fake
+def _(costs, grad_alignment, temperature, lengths, bandwidth):
+    return _like(costs, "P", "1")
+
+
+@custom_op("d2p_py::soft_dtw", mutates_args=())
+def soft_dtw(costs: torch.Tensor, temperature: torch.Tensor, lengths: torch.Tensor,
+             bandwidth: int) -> tuple[torch.Tensor, torch.Tensor]:
+    v, m = torch.ops.d2p.soft_dtw(costs, temperature, lengths, bandwidth)
+    return v, m
+
+
+@soft_dtw.register_fake
+def _(costs, temperature, lengths, bandwidth):
+    return _like(costs, "B", "P")
+
+
+@custom_op("d2p_py::soft_dtw_grad_t", mutates_args=())
+def soft_dtw_grad_t(costs: torch.Tensor, temperature: torch.Tensor, lengths: torch.Tensor,
+                    bandwidth: int) -> torch.Tensor:
+    return torch.ops.d2p.soft_dtw_with_grads(costs, float(temperature), lengths, bandwidth)[2]
+
+
+@soft_dtw_grad_t.register_fake
+def _(costs, temperature, lengths, bandwidth):
+    return _like(costs, "B")
+
+
+@custom_op("d2p_py::soft_dtw_backward_full_t", mutates_args=())
+def soft_dtw_backward_full_t(costs: torch.Tensor, grad_alignment: torch.Tensor, temperature: torch.Tensor,
+                             lengths: torch.Tensor, bandwidth: int) -> tuple[torch.Tensor, torch.Tensor]:
+    a, b = torch.ops.d2p.soft_dtw_backward_full(costs, grad_alignment, float(temperature), lengths, bandwidth)
+    return a, b
+
+
+@soft_dtw_backward_full_t.register_fake
+def _(costs, grad_alignment, temperature, lengths, bandwidth):
+    return _like(costs, "P", "1")
+
+
+def _soft_dtw_setup(ctx, inputs, output):
+    costs, temperature, lengths, bandwidth = inputs
+    ctx.save_for_backward(costs, output[1], temperature.detach())
+    ctx.lengths, ctx.bandwidth = lengths, bandwidth
+
+
+def _soft_dtw_backward(ctx, grad_value, grad_marg):
+    costs, marg, temperature = ctx.saved_tensors
+    grad_costs = _expand_batch(grad_value, marg)
+    need_t = ctx.needs_input_grad[1]
+    g_t = None
+    if grad_value is not None and need_t:
+        g_t = _batch_dot(grad_value, soft_dtw_grad_t(costs, temperature, ctx.lengths, ctx.bandwidth))
+    if grad_marg is not None:
+        gc, gt = soft_dtw_backward_full_t(costs, grad_marg, temperature, ctx.lengths, ctx.bandwidth)
+        grad_costs = _add(grad_costs, gc)
+        g_t = _add(g_t, gt) if need_t else None
+    return grad_costs, g_t, None, None
+
+
+soft_dtw.register_autograd(_soft_dtw_backward, setup_context=_soft_dtw_setup)
+
+
+@custom_op("d2p_py::soft_dtw_float", mutates_args=())
+def soft_dtw_float(costs: torch.Tensor, temperature: float, lengths: Optional[torch.Tensor],
+                   bandwidth: Optional[int]) -> tuple[torch.Tensor, torch.Tensor]:
+    v, m = torch.ops.d2p.soft_dtw_float(costs, temperature, lengths, bandwidth)
+    return v, m
+
+
+@soft_dtw_float.register_fake
+def _(costs, temperature, lengths, bandwidth):
+    return _like(costs, "B", "P")
+
+
+def _soft_dtw_float_setup(ctx, inputs, output):
+    costs, temperature, lengths, bandwidth = inputs
+    ctx.save_for_backward(costs, output[1])
+    ctx.temperature, ctx.lengths, ctx.bandwidth = temperature, lengths, bandwidth
+
+
+def _soft_dtw_float_backward(ctx, grad_value, grad_marg):
+    costs, marg = ctx.saved_tensors
+    grad_costs = _expand_batch(grad_value, marg)
+    if grad_marg is not None:
+        gc, _ = soft_dtw_backward_full(costs, grad_marg, ctx.temperature, ctx.lengths, ctx.bandwidth)
+        grad_costs = _add(grad_costs, gc)
+    return grad_costs, None, None, None
+
+
+soft_dtw_float.register_autograd(_soft_dtw_float_backward, setup_context=_soft_dtw_float_setup)

@@ -164,9 +164,13 @@ const char* d2p_error_string(int code) {
 
 size_t d2p_sw_workspace_bytes(int family, int op, int B, int L1, int L2) {
     if (family != D2P_FAMILY_LINEAR && family != D2P_FAMILY_AFFINE && family != D2P_FAMILY_NW &&
-        family != D2P_FAMILY_NW_AFFINE)
+        family != D2P_FAMILY_NW_AFFINE && family != D2P_FAMILY_DTW)
         return (size_t)-1;
     if (!dims_ok(B, L1, L2)) return (size_t)-1;
+    if (family == D2P_FAMILY_DTW) {
+        if (op < D2P_OP_FORWARD_BACKWARD || op > D2P_OP_BACKWARD_FULL) return (size_t)-1;
+        return dtw_workspace_bytes(op, B, L1, L2);
+    }
     if (family == D2P_FAMILY_NW || family == D2P_FAMILY_NW_AFFINE) {
         if (op < D2P_OP_FORWARD_BACKWARD || op > D2P_OP_BACKWARD_FULL) return (size_t)-1;
         if (family == D2P_FAMILY_NW_AFFINE && 3LL * (L1 + 1LL) * (L2 + 1LL) > (long long)INT_MAX) return (size_t)-1;

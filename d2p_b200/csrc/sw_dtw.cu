@@ -1,0 +1,381 @@
+// sw_dtw.cu -- soft dynamic time warping with an optional Sakoe-Chiba band:
+// value, alignment marginals, dS/dT, the Hessian-vector product, the
+// temperature Jacobian dP/dT, and its contraction with a weight plane
+// (backward_full).
+//
+// Recurrence (src/dtw/kernels_cpu.cpp:58-128 restated, natural units):
+//   alpha[0,0] = 0, every other cell +inf until reached;
+//   alpha[i,j] = c_ij + softmin_T(alpha[i-1,j-1], alpha[i-1,j], alpha[i,j-1])
+//   for cells inside the band (|j - i L2 / L1| <= bandwidth, in the
+//   reference's float arithmetic; bandwidth < 0: no band); S = alpha[L1, L2]
+//   (+inf, the sentinel 1e30, when one sequence is empty).
+// softmin_T(v) = m - T ln sum exp((m - v_k) / T), m = min v, with normalised
+// weights w_k.  The reverse is the flow of the path distribution: beta[L1,L2] =
+// 1 and beta[c] = sum over the successors d of c of beta[d] w_c(d); the
+// marginal of (i, j) is beta[i, j] itself (every visited cell pays its cost).
+// dS/dT = -(the entropy of the path distribution): minus each visited cell's
+// choice entropy -sum w ln w weighted by beta, a sum of non-negative terms
+// (equal to the reference's sum beta (softmin - E[alpha]) / T).
+//
+// Tangents: the forward carries d alpha = V + sum w d alpha_k (along V) or
+// -entropy + sum w u_k (along T); the reverse carries d beta with
+// dw_c(d) = w_c(d) (E_d - t_c) / T, E_d = sum_k w_k(d) t_k (+ w_c(d) (a_c -
+// E[a](d)) / T^2 along T); the output is d beta
+// (src/dtw/kernels_cpu.cpp:236-534).
+//
+// Engine: one CTA per problem sweeps the anti-diagonals, threads striding
+// over a diagonal's cells, one barrier per diagonal; per-cell values live in
+// diagonal-major planes ([k][i]) in the workspace.  alpha and the forward
+// tangent are stored relative to an integer frame per diagonal (taken from
+// the diagonal's cell nearest the band's centre line), so options are formed
+// from small values plus exact frame differences.  Gather-form reverse, no
+// atomics; fp64 block sums.
+#include <math.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../../include/d2p_b200.h"
+#include "sw_common.cuh"
+#include "sw_internal.h"
+
+namespace d2pb {
+namespace dtw {
+
+constexpr int kThreads = 256;
+constexpr float kPInf = 1.0e30f;   // unreached cell, as the reference's sentinel
+constexpr float kFin = 0.5e30f;    // values below this are reached
+
+enum Plane : int { kA = 0, kWd, kWu, kWl, kB, kH, kF, kR, kNumPlanes };
+__host__ __device__ inline size_t plane_floats(int L1m, int L2m) {
+    return ((size_t)L1m + L2m + 1) * ((size_t)L1m + 1);
+}
+// MARG: alpha, weights, beta, entropy; tangents: + forward and reverse tangent
+__host__ __device__ inline int planes_for(int mode) { return mode == MODE_MARG ? kH + 1 : kNumPlanes; }
+__host__ __device__ inline size_t per_problem_bytes(int L1m, int L2m, int mode) {
+    const size_t b = (plane_floats(L1m, L2m) * planes_for(mode) + 2 * ((size_t)L1m + L2m + 1)) * sizeof(float);
+    return (b + 255) & ~(size_t)255;
+}
+
+struct Ctx {
+    float* p[kNumPlanes];
+    float* O;
+    float* D;
+    int stride;
+    __device__ float& at(int plane, int k, int i) const { return p[plane][(size_t)k * stride + i]; }
+};
+
+__device__ __forceinline__ double block_sum(double v, double* red) {
+    for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    double t = 0.0;
+    if (threadIdx.x < 32) {
+        t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0;
+        for (int o = 16; o >= 1; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    }
+    return t;   // valid in thread 0
+}
+
+// the reference's band test (src/dtw/kernels_cpu.cpp:23-29), float arithmetic
+__device__ __forceinline__ bool in_band(int i, int j, int L1, int L2, int bw) {
+    if (bw < 0 || L1 == 0 || L2 == 0) return true;
+    const float e = (float)((long long)i * L2) / (float)L1;
+    return fabsf((float)j - e) <= (float)bw;
+}
+
+// One CTA per problem.  MODE: MODE_MARG (value, marginals, dS/dT), MODE_HVP
+// (out = d marginals along p.tangent), MODE_PT (out = dP/dT; with dot_with,
+// dot_out[b] = sum dot_with * dP/dT).  p.gap2 carries nothing; the band is
+// p.parts (an int, < 0 for none).
+template <int MODE>
+__global__ void __launch_bounds__(kThreads) dtw_kernel(SwArgs p) {
+    __shared__ double red[32];
+    const int b = blockIdx.x;
+    const int L1m = p.L1, L2m = p.L2;
+    const int L1 = p.lengths ? min(max(p.lengths[2 * b], 0), L1m) : L1m;
+    const int L2 = p.lengths ? min(max(p.lengths[2 * b + 1], 0), L2m) : L2m;
+    const int bw = p.parts;
+    const float T = p.temp_dev ? __ldg(p.temp_dev) : p.temp;
+    const float iT = 1.f / T;
+    const size_t plane = (size_t)L1m * L2m;
+    const float* __restrict__ Cst = p.scores + (size_t)b * plane;
+    const float* __restrict__ V = MODE == MODE_HVP ? p.tangent + (size_t)b * plane : nullptr;
+    const float* __restrict__ Gw = p.dot_with ? p.dot_with + (size_t)b * plane : nullptr;
+    float* __restrict__ out = p.out ? p.out + (size_t)b * plane : nullptr;
+    Ctx C;
+    {
+        float* base = reinterpret_cast<float*>(reinterpret_cast<char*>(p.ws) + (size_t)b * per_problem_bytes(L1m, L2m, MODE));
+        const size_t pf = plane_floats(L1m, L2m);
+        for (int q = 0; q < kNumPlanes; ++q) C.p[q] = q < planes_for(MODE) ? base + (size_t)q * pf : nullptr;
+        C.O = base + pf * planes_for(MODE);
+        C.D = C.O + (L1m + L2m + 1);
+        C.stride = L1m + 1;
+    }
+    constexpr bool TAN = MODE != MODE_MARG;
+    const int K = L1 + L2;
+
+    if (out) {
+        for (size_t e = threadIdx.x; e < plane; e += blockDim.x) {
+            const int i = (int)(e / L2m), j = (int)(e - (size_t)i * L2m);
+            if (i >= L1 || j >= L2) out[e] = 0.f;
+        }
+    }
+
+    // ------------------------------------------------------------- forward
+    float O1 = 0.f, O2 = 0.f, D1 = 0.f, D2 = 0.f;
+    for (int k = 0; k <= K; ++k) {
+        float Ok = O1, Dk = D1;
+        if (k >= 2) {   // the previous diagonal's cell nearest the band's centre line
+            const int lo = max(0, k - 1 - L2), hi = min(L1, k - 1);
+            int im = K > 0 ? (int)(((long long)(k - 1) * L1 + K / 2) / K) : 0;
+            im = min(max(im, lo), hi);
+            const float a = C.at(kA, k - 1, im);
+            if (a < kFin) {
+                Ok = O1 + rintf(a);
+                if (TAN) Dk = D1 + rintf(C.at(kF, k - 1, im));
+            }
+        }
+        if (threadIdx.x == 0) {
+            C.O[k] = Ok;
+            C.D[k] = Dk;
+        }
+        const float dO1 = O1 - Ok, dO2 = O2 - Ok, dD1 = D1 - Dk, dD2 = D2 - Dk;   // exact
+        const int i0 = max(0, k - L2), i1 = min(L1, k);
+        for (int i = i0 + threadIdx.x; i <= i1; i += blockDim.x) {
+            const int j = k - i;
+            float a = kPInf, wd = 0.f, wu = 0.f, wl = 0.f, h = 0.f, f = 0.f;
+            if (k == 0) {
+                a = 0.f;
+            } else if (i >= 1 && j >= 1 && in_band(i, j, L1, L2, bw)) {
+                const size_t si = (size_t)(i - 1) * L2m + (j - 1);
+                const float vd = C.at(kA, k - 2, i - 1) + dO2, vu = C.at(kA, k - 1, i - 1) + dO1,
+                            vl = C.at(kA, k - 1, i) + dO1;
+                const float m = fminf(vd, fminf(vu, vl));
+                if (m < kFin) {
+                    const float ed = expf((m - vd) * iT), eu = expf((m - vu) * iT), el = expf((m - vl) * iT);
+                    const float sum = (ed + eu) + el;
+                    const float ls = logf(sum);
+                    const float is = 1.f / sum;
+                    wd = ed * is;
+                    wu = eu * is;
+                    wl = el * is;
+                    a = Cst[si] + fmaf(-T, ls, m);
+                    // the choice's entropy -sum w ln w = ln(sum) + sum w (v - m) / T
+                    h = ls + iT * fmaf(wd, vd - m, fmaf(wu, vu - m, wl * (vl - m)));
+                    if (TAN) {
+                        f = fmaf(wd, C.at(kF, k - 2, i - 1) + dD2,
+                                 fmaf(wu, C.at(kF, k - 1, i - 1) + dD1, wl * (C.at(kF, k - 1, i) + dD1)));
+                        if (MODE == MODE_HVP) f += V[si];
+                        if (MODE == MODE_PT) f -= h;
+                    }
+                }
+            }
+            C.at(kA, k, i) = a < kFin ? a : kPInf;
+            C.at(kWd, k, i) = wd;
+            C.at(kWu, k, i) = wu;
+            C.at(kWl, k, i) = wl;
+            C.at(kH, k, i) = h;
+            if (TAN) C.at(kF, k, i) = f;
+        }
+        __syncthreads();
+        O2 = O1;
+        O1 = Ok;
+        D2 = D1;
+        D1 = Dk;
+    }
+
+    // ------------------------------------------------------------- reverse
+    double sent = 0.0, sdot = 0.0;
+    for (int k = K; k >= 0; --k) {
+        const float Ok = C.O[k], Dk = C.D[k];
+        const float Ok1 = k + 1 <= K ? C.O[k + 1] : 0.f, Ok2 = k + 2 <= K ? C.O[k + 2] : 0.f;
+        const float Dk1 = k + 1 <= K ? C.D[k + 1] : 0.f, Dk2 = k + 2 <= K ? C.D[k + 2] : 0.f;
+        const int i0 = max(0, k - L2), i1 = min(L1, k);
+        for (int i = i0 + threadIdx.x; i <= i1; i += blockDim.x) {
+            const int j = k - i;
+            float be = k == K ? 1.f : 0.f, tb = 0.f;
+            const float tc = TAN ? C.at(kF, k, i) : 0.f;
+            const float ac = C.at(kA, k, i);
+            // successor d of this cell by its option with weight plane pw;
+            // dO, dD: the successor's frames minus this cell's (exact)
+            auto take = [&](int kd, int id, int pw, float dO, float dD) {
+                const float bd = C.at(kB, kd, id);
+                const float w = C.at(pw, kd, id);
+                be = fmaf(bd, w, be);
+                if (TAN) {
+                    const size_t sd = (size_t)(id - 1) * L2m + (kd - id - 1);
+                    // E_d - t_c: the successor's options' mean tangent minus this cell's
+                    float g = C.at(kF, kd, id) - tc + dD;
+                    if (MODE == MODE_HVP) g -= V[sd];
+                    float dw;
+                    if (MODE == MODE_PT) {
+                        const float hd = C.at(kH, kd, id);
+                        // a_c - E[a](d) = a_c - (alpha_d - c_d) - T h_d
+                        const float da = (ac - C.at(kA, kd, id)) + (Cst[sd] - dO) - T * hd;
+                        dw = w * fmaf(g + hd, iT, da * iT * iT);
+                    } else {
+                        dw = w * g * iT;
+                    }
+                    tb = fmaf(C.at(kR, kd, id), w, fmaf(bd, dw, tb));
+                }
+            };
+            // an unreached cell takes no flow (its successors give it weight 0);
+            // the end cell keeps its 1 even when unreached, as in the reference
+            if (ac < kFin) {
+                if (i + 1 <= L1 && j + 1 <= L2) take(k + 2, i + 1, kWd, Ok2 - Ok, Dk2 - Dk);
+                if (i + 1 <= L1 && j >= 1) take(k + 1, i + 1, kWu, Ok1 - Ok, Dk1 - Dk);
+                if (j + 1 <= L2 && i >= 1) take(k + 1, i, kWl, Ok1 - Ok, Dk1 - Dk);
+            }
+            C.at(kB, k, i) = be;
+            if (TAN) C.at(kR, k, i) = tb;
+            if (i >= 1 && j >= 1) {
+                const size_t si = (size_t)(i - 1) * L2m + (j - 1);
+                if (MODE == MODE_MARG) {
+                    if (out) out[si] = be;
+                    sent += (double)be * (double)C.at(kH, k, i);
+                } else {
+                    if (out) out[si] = tb;
+                    if (Gw) sdot += (double)Gw[si] * (double)tb;
+                }
+            }
+        }
+        __syncthreads();
+    }
+
+    if (MODE == MODE_MARG) {
+        const double th = block_sum(sent, red);
+        if (threadIdx.x == 0) {
+            const float aE = C.at(kA, K, L1);
+            if (p.value) p.value[b] = aE < kFin ? (float)((double)aE + (double)C.O[K]) : kPInf;
+            if (p.grad_T) p.grad_T[b] = (float)(-th);
+        }
+    } else if (p.dot_out) {
+        const double t = block_sum(sdot, red);
+        if (threadIdx.x == 0) p.dot_out[b] = (float)t;
+    }
+}
+
+}  // namespace dtw
+
+// ------------------------------------------------------------------ host side
+size_t dtw_workspace_bytes(int op, int B, int L1, int L2) {
+    const size_t fb = dtw::per_problem_bytes(L1, L2, op == D2P_OP_FORWARD_BACKWARD ? MODE_MARG : MODE_PT);
+    size_t n = (fb * (size_t)(B > 0 ? B : 1) + 255) & ~(size_t)255;
+    if (op == D2P_OP_BACKWARD_FULL) n += ((size_t)(B > 0 ? B : 1) * sizeof(float) + 255) & ~(size_t)255;
+    return n;
+}
+
+static int launch_dtw(const SwArgs& a, cudaStream_t st) {
+    if (a.B == 0) return 0;
+    switch (a.mode) {
+        case MODE_MARG: dtw::dtw_kernel<MODE_MARG><<<a.B, dtw::kThreads, 0, st>>>(a); break;
+        case MODE_HVP: dtw::dtw_kernel<MODE_HVP><<<a.B, dtw::kThreads, 0, st>>>(a); break;
+        case MODE_PT: dtw::dtw_kernel<MODE_PT><<<a.B, dtw::kThreads, 0, st>>>(a); break;
+        default: return kErrInvalid;
+    }
+    return (int)cudaGetLastError();
+}
+
+}  // namespace d2pb
+
+using namespace d2pb;
+
+// ---------------------------------------------------------------- C ABI
+extern "C" {
+
+static bool dtw_dims_ok(int B, int L1, int L2) {
+    if (B < 0 || L1 < 0 || L2 < 0) return false;
+    return (long long)(L1 + 1) * (long long)(L2 + 1) <= 2147483647LL;
+}
+
+static SwArgs dtw_args(const float* costs, const int* lengths, int B, int L1, int L2, float T, int bandwidth,
+                       void* ws) {
+    SwArgs a{};
+    a.scores = costs;
+    a.lengths = lengths;
+    a.B = B;
+    a.L1 = L1;
+    a.L2 = L2;
+    a.temp = T;
+    a.parts = bandwidth < 0 ? -1 : bandwidth;
+    a.ws = (float*)ws;
+    return a;
+}
+
+int d2p_dtw_forward_backward(const float* costs, const int* lengths, int B, int L1, int L2, float temperature,
+                             const float* temperature_dev, int bandwidth, float* value, float* marginals,
+                             float* grad_temperature, void* workspace, size_t workspace_bytes, void* stream) {
+    if (!dtw_dims_ok(B, L1, L2)) return D2P_ERR_TOO_LARGE;
+    if (B == 0) return D2P_OK;
+    if (!costs || !value || !marginals) return D2P_ERR_INVALID_ARGUMENT;
+    if (!workspace || workspace_bytes < dtw_workspace_bytes(D2P_OP_FORWARD_BACKWARD, B, L1, L2))
+        return D2P_ERR_WORKSPACE_TOO_SMALL;
+    SwArgs a = dtw_args(costs, lengths, B, L1, L2, temperature, bandwidth, workspace);
+    a.temp_dev = temperature_dev;
+    a.mode = MODE_MARG;
+    a.value = value;
+    a.out = marginals;
+    a.grad_T = grad_temperature;
+    return launch_dtw(a, (cudaStream_t)stream);
+}
+
+int d2p_dtw_hvp(const float* costs, const float* tangent, const int* lengths, int B, int L1, int L2,
+                float temperature, int bandwidth, float* hvp, void* workspace, size_t workspace_bytes,
+                void* stream) {
+    if (!dtw_dims_ok(B, L1, L2)) return D2P_ERR_TOO_LARGE;
+    if (B == 0) return D2P_OK;
+    if (!costs || !tangent || !hvp) return D2P_ERR_INVALID_ARGUMENT;
+    if (!workspace || workspace_bytes < dtw_workspace_bytes(D2P_OP_HVP, B, L1, L2)) return D2P_ERR_WORKSPACE_TOO_SMALL;
+    SwArgs a = dtw_args(costs, lengths, B, L1, L2, temperature, bandwidth, workspace);
+    a.mode = MODE_HVP;
+    a.tangent = tangent;
+    a.out = hvp;
+    return launch_dtw(a, (cudaStream_t)stream);
+}
+
+int d2p_dtw_param_jacobian(const float* costs, const int* lengths, int B, int L1, int L2, float temperature,
+                           int bandwidth, float* jacobian, void* workspace, size_t workspace_bytes, void* stream) {
+    if (!dtw_dims_ok(B, L1, L2)) return D2P_ERR_TOO_LARGE;
+    if (B == 0) return D2P_OK;
+    if (!costs || !jacobian) return D2P_ERR_INVALID_ARGUMENT;
+    if (!workspace || workspace_bytes < dtw_workspace_bytes(D2P_OP_PARAM_JACOBIAN, B, L1, L2))
+        return D2P_ERR_WORKSPACE_TOO_SMALL;
+    SwArgs a = dtw_args(costs, lengths, B, L1, L2, temperature, bandwidth, workspace);
+    a.mode = MODE_PT;
+    a.out = jacobian;
+    return launch_dtw(a, (cudaStream_t)stream);
+}
+
+int d2p_dtw_backward_full(const float* costs, const float* grad_marginals, const int* lengths, int B, int L1, int L2,
+                          float temperature, int bandwidth, float* grad_costs, float* grad_temperature,
+                          void* workspace, size_t workspace_bytes, void* stream) {
+    if (!dtw_dims_ok(B, L1, L2)) return D2P_ERR_TOO_LARGE;
+    if (!grad_costs || !grad_temperature) return D2P_ERR_INVALID_ARGUMENT;
+    cudaStream_t st = (cudaStream_t)stream;
+    if (B == 0) return (int)cudaMemsetAsync(grad_temperature, 0, sizeof(float), st);
+    if (!costs || !grad_marginals) return D2P_ERR_INVALID_ARGUMENT;
+    if (!workspace || workspace_bytes < dtw_workspace_bytes(D2P_OP_BACKWARD_FULL, B, L1, L2))
+        return D2P_ERR_WORKSPACE_TOO_SMALL;
+    // grad_costs = H . grad_marginals (the Hessian of S is symmetric); grad_T
+    // = sum grad_marginals * dP/dT
+    const size_t area = dtw::per_problem_bytes(L1, L2, MODE_PT) * (size_t)B;
+    float* partials = (float*)((char*)workspace + ((area + 255) & ~(size_t)255));
+    SwArgs a = dtw_args(costs, lengths, B, L1, L2, temperature, bandwidth, workspace);
+    a.mode = MODE_HVP;
+    a.tangent = grad_marginals;
+    a.out = grad_costs;
+    int rc = launch_dtw(a, st);
+    if (rc) return rc;
+    a.tangent = nullptr;
+    a.out = nullptr;
+    a.dot_with = grad_marginals;
+    a.mode = MODE_PT;
+    a.dot_out = partials;
+    rc = launch_dtw(a, st);
+    if (rc) return rc;
+    return launch_sum_batches(partials, 1, B, grad_temperature, 0, st);
+}
+
+}  // extern "C"

@@ -99,7 +99,8 @@ struct SwArgs {
     int* redo;                          // [B] out: set for problems the kernel could not finish
     const int* only;                    // [B] in, optional: run only the problems whose entry is set
     const int* order;                   // [B] in, optional: problem of each CTA (largest first)
-    int parts;                          // CTAs per problem (1 unless a kernel spreads problems)
+    int parts;                          // CTAs per problem (1 unless a kernel spreads problems);
+                                        //   soft DTW: the Sakoe-Chiba bandwidth (< 0: no band)
     int* sync;                          // [B][kSyncBytes / 4], zeroed: cross-CTA words of each problem
 };
 
@@ -146,6 +147,8 @@ int launch_nw(const SwArgs& a, cudaStream_t st);
 // a.mode MODE_MARG, MODE_HVP, MODE_PGAP (open), MODE_PGE (ext), MODE_PT
 size_t nwa_workspace_bytes(int op, int B, int L1, int L2);
 int launch_nwa(const SwArgs& a, cudaStream_t st);
+// soft DTW (sw_dtw.cu): workspace of one operator
+size_t dtw_workspace_bytes(int op, int B, int L1, int L2);
 // engine counters of the current device (cumulative, read synchronously):
 // problems the plane engine computed [linear, affine], and problems the
 // log-domain kernel recomputed after a linear-domain kernel flagged them

@@ -1,12 +1,12 @@
 // torch_bindings.cpp -- the reference's dispatcher surface (torch.ops.d2p.*) for the
-// soft Smith-Waterman family and the soft Needleman-Wunsch operators (linear and
-// affine gaps),
+// soft Smith-Waterman family, the soft Needleman-Wunsch operators (linear and
+// affine gaps) and soft DTW,
 // implemented on top of the C ABI in
 // include/d2p_b200.h (libd2p_b200.so).
 //
 // Schemas are the reference's, verbatim (src/sw/registry.cpp:30-44,
 // src/sw_affine/registry.cpp:27-42, src/nw/registry.cpp:35-49,
-// src/nw_affine/registry.cpp:35-50), so code written against d2p's ops binds
+// src/nw_affine/registry.cpp:35-50, src/dtw/registry.cpp:35-40), so code written against d2p's ops binds
 // unchanged.  CUDA and AutogradCUDA keys are registered exactly as the reference
 // does (src/sw/torch_cuda.cpp:857-883, src/sw_affine/torch_cuda.cpp:914-948);
 // there is no CPU kernel and no fallback: CPU tensors are rejected with the
@@ -722,6 +722,211 @@ Tensor aff_marginals_grad_alias(Tensor scores, double go, double ge, double temp
 constexpr int kAff = D2P_FAMILY_AFFINE;
 constexpr int kNWAff = D2P_FAMILY_NW_AFFINE;
 
+// =============================================================================
+// soft DTW (reference SoftDTWCUDAFunction and bindings, src/dtw/torch_cuda.cpp:140-600)
+// =============================================================================
+// the reference's bandwidth range check (src/dtw/torch_cuda.cpp:73-80)
+int checked_dtw_bandwidth(int64_t bandwidth) {
+    TORCH_CHECK(bandwidth >= std::numeric_limits<int>::min() && bandwidth <= std::numeric_limits<int>::max(),
+                "DTW bandwidth is out of CUDA int range: ", bandwidth);
+    return static_cast<int>(bandwidth);
+}
+
+Shape checked_dtw_shape(const Tensor& costs) {
+    TORCH_CHECK(costs.dim() == 3, "costs must be 3D (B, L1, L2)");
+    return checked_shape(costs);
+}
+
+struct DtwFwd {
+    Tensor value, marginals, dT;   // dT [B]: dS/dT (undefined if not requested)
+};
+
+DtwFwd dtw_forward(const Tensor& costs, const Param& T, const Tensor& lengths, const Shape& s, int bw,
+                   bool want_T) {
+    auto opt = costs.options();
+    DtwFwd r;
+    r.value = torch::empty({s.B}, opt);
+    r.marginals = torch::empty({s.B, s.L1, s.L2}, opt);
+    if (want_T) r.dT = torch::empty({s.B}, opt);
+    size_t wb = 0;
+    Tensor ws = workspace(D2P_FAMILY_DTW, D2P_OP_FORWARD_BACKWARD, s, costs.device(), &wb);
+    check_rc(d2p_dtw_forward_backward(costs.data_ptr<float>(), len_ptr(lengths), s.B, s.L1, s.L2, T.host, T.dev, bw,
+                                      r.value.data_ptr<float>(), r.marginals.data_ptr<float>(),
+                                      want_T ? r.dT.data_ptr<float>() : nullptr, ws.data_ptr(), wb, cur_stream()),
+             "d2p_dtw_forward_backward");
+    return r;
+}
+
+Tensor dtw_hvp_raw(const Tensor& costs, const Tensor& tangent, float T, const Tensor& lengths, const Shape& s,
+                   int bw) {
+    Tensor H = torch::empty({s.B, s.L1, s.L2}, costs.options());
+    size_t wb = 0;
+    Tensor ws = workspace(D2P_FAMILY_DTW, D2P_OP_HVP, s, costs.device(), &wb);
+    check_rc(d2p_dtw_hvp(costs.data_ptr<float>(), tangent.data_ptr<float>(), len_ptr(lengths), s.B, s.L1, s.L2, T,
+                         bw, H.data_ptr<float>(), ws.data_ptr(), wb, cur_stream()),
+             "d2p_dtw_hvp");
+    return H;
+}
+
+Tensor dtw_jac_raw(const Tensor& costs, float T, const Tensor& lengths, const Shape& s, int bw) {
+    Tensor J = torch::empty({s.B, s.L1, s.L2}, costs.options());
+    size_t wb = 0;
+    Tensor ws = workspace(D2P_FAMILY_DTW, D2P_OP_PARAM_JACOBIAN, s, costs.device(), &wb);
+    check_rc(d2p_dtw_param_jacobian(costs.data_ptr<float>(), len_ptr(lengths), s.B, s.L1, s.L2, T, bw,
+                                    J.data_ptr<float>(), ws.data_ptr(), wb, cur_stream()),
+             "d2p_dtw_param_jacobian");
+    return J;
+}
+
+std::tuple<Tensor, Tensor> dtw_backward_full_raw(const Tensor& costs, const Tensor& G, float T,
+                                                 const Tensor& lengths, const Shape& s, int bw) {
+    auto opt = costs.options();
+    Tensor gc = torch::empty({s.B, s.L1, s.L2}, opt);
+    Tensor gT = torch::empty({1}, opt);
+    size_t wb = 0;
+    Tensor ws = workspace(D2P_FAMILY_DTW, D2P_OP_BACKWARD_FULL, s, costs.device(), &wb);
+    check_rc(d2p_dtw_backward_full(costs.data_ptr<float>(), G.data_ptr<float>(), len_ptr(lengths), s.B, s.L1, s.L2,
+                                   T, bw, gc.data_ptr<float>(), gT.data_ptr<float>(), ws.data_ptr(), wb,
+                                   cur_stream()),
+             "d2p_dtw_backward_full");
+    return {gc, gT};
+}
+
+// outputs (cost [B], alignment [B,L1,L2]); backward: (grad costs, grad T [1],
+// none for lengths and bandwidth)
+class SoftDTWFunction : public torch::autograd::Function<SoftDTWFunction> {
+   public:
+    static tensor_list forward(AutogradContext* ctx, Tensor costs, Tensor temperature,
+                               c10::optional<Tensor> lengths_opt, int64_t bandwidth) {
+        Tensor lengths = lengths_opt.has_value() ? *lengths_opt : Tensor();
+        ctx->set_materialize_grads(false);
+        D2PB_CHECK_INPUT(costs);
+        const Shape s = checked_dtw_shape(costs);
+        c10::cuda::CUDAGuard guard(costs.device());
+        const int bw = checked_dtw_bandwidth(bandwidth);
+        Param pT = read_param(temperature, costs, "temperature");
+        if (lengths.defined()) validate_lengths(lengths, s, costs.device());
+        DtwFwd r = dtw_forward(costs, pT, lengths, s, bw, temperature.requires_grad());
+        ctx->save_for_backward({costs, r.marginals, r.dT, temperature});
+        ctx->saved_data["lengths"] = lengths.defined() ? c10::IValue(lengths) : c10::IValue();
+        ctx->saved_data["bandwidth"] = static_cast<int64_t>(bw);
+        return {r.value, r.marginals};
+    }
+
+    static tensor_list backward(AutogradContext* ctx, tensor_list grad_outputs) {
+        auto saved = ctx->get_saved_variables();
+        Tensor costs = saved[0], marginals = saved[1], dT = saved[2], temperature = saved[3];
+        Tensor lengths;
+        if (!ctx->saved_data["lengths"].isNone()) lengths = ctx->saved_data["lengths"].toTensor();
+        const int bw = static_cast<int>(ctx->saved_data["bandwidth"].toInt());
+        const Shape s = checked_dtw_shape(costs);
+        c10::cuda::CUDAGuard guard(costs.device());
+        auto opt = costs.options();
+        Tensor gv = grad_outputs[0], gm = grad_outputs[1];
+        Tensor grad_costs;
+        Tensor grad_T = ctx->needs_input_grad(1) ? torch::zeros({1}, opt) : Tensor();
+        bool have = false;
+        if (gv.defined() && gv.numel() > 0) {
+            Tensor g = gv.to(torch::kFloat32).contiguous();
+            if (g.device() != costs.device()) g = g.to(costs.device());
+            grad_costs = torch::empty({s.B, s.L1, s.L2}, opt);
+            const bool param = dT.defined();
+            Tensor gp = param ? torch::empty({1}, opt) : Tensor();
+            check_rc(d2p_sw_value_backward_lengths(g.data_ptr<float>(), marginals.data_ptr<float>(),
+                                                   lengths.defined() ? lengths.data_ptr<int>() : nullptr,
+                                                   param ? dT.data_ptr<float>() : nullptr, param ? 1 : 0, s.B,
+                                                   s.L1, s.L2, grad_costs.data_ptr<float>(),
+                                                   param ? gp.data_ptr<float>() : nullptr, cur_stream()),
+                     "d2p_sw_value_backward_lengths");
+            if (param) grad_T = gp;
+            have = true;
+        }
+        if (gm.defined() && gm.numel() > 0) {
+            Tensor G = prep_grad(gm, costs, "grad_posteriors");
+            auto r = dtw_backward_full_raw(costs, G, host_value(temperature), lengths, s, bw);
+            grad_costs = have ? grad_costs + std::get<0>(r) : std::get<0>(r);
+            if (ctx->needs_input_grad(1)) grad_T = grad_T + std::get<1>(r);
+            have = true;
+        }
+        if (!have) grad_costs = torch::zeros({s.B, s.L1, s.L2}, opt);
+        if (!ctx->needs_input_grad(1)) grad_T = Tensor();
+        return {grad_costs, grad_T, Tensor(), Tensor()};
+    }
+};
+
+std::vector<Tensor> soft_dtw_cuda(Tensor costs, Tensor temperature, Tensor lengths, int64_t bandwidth) {
+    return SoftDTWFunction::apply(costs, temperature, c10::optional<Tensor>(lengths), bandwidth);
+}
+
+std::vector<Tensor> soft_dtw_float_cuda(Tensor costs, double temperature, c10::optional<Tensor> lengths,
+                                        c10::optional<int64_t> bandwidth) {
+    D2PB_CHECK_INPUT(costs);
+    const Shape s = checked_dtw_shape(costs);
+    c10::cuda::CUDAGuard guard(costs.device());
+    Tensor len = resolve_lengths(lengths, s, costs.device());
+    auto cpu = torch::TensorOptions().dtype(torch::kFloat32);
+    return SoftDTWFunction::apply(costs, torch::full({1}, (float)temperature, cpu),
+                                  len.defined() ? c10::optional<Tensor>(len) : c10::nullopt,
+                                  bandwidth.has_value() ? *bandwidth : -1);
+}
+
+std::tuple<Tensor, Tensor, Tensor> soft_dtw_with_grads_cuda(Tensor costs, double temperature,
+                                                            c10::optional<Tensor> lengths,
+                                                            c10::optional<int64_t> bandwidth) {
+    D2PB_CHECK_INPUT(costs);
+    const Shape s = checked_dtw_shape(costs);
+    c10::cuda::CUDAGuard guard(costs.device());
+    Tensor len = resolve_lengths(lengths, s, costs.device());
+    Param pT;
+    pT.host = (float)temperature;
+    DtwFwd r = dtw_forward(costs, pT, len, s, checked_dtw_bandwidth(bandwidth.has_value() ? *bandwidth : -1), true);
+    return {r.value, r.marginals, r.dT};
+}
+
+Tensor soft_dtw_hvp_cuda(Tensor costs, Tensor tangent, double temperature, c10::optional<Tensor> lengths,
+                         c10::optional<int64_t> bandwidth) {
+    D2PB_CHECK_INPUT(costs);
+    D2PB_CHECK_INPUT(tangent);
+    TORCH_CHECK(costs.dim() == 3, "costs must be 3D");
+    TORCH_CHECK(tangent.sizes() == costs.sizes(), "tangent must have same shape as costs");
+    TORCH_CHECK(tangent.device() == costs.device(), "tangent must be on same device as costs, got ",
+                tangent.device(), " vs ", costs.device());
+    const Shape s = checked_dtw_shape(costs);
+    c10::cuda::CUDAGuard guard(costs.device());
+    Tensor len = resolve_lengths(lengths, s, costs.device());
+    return dtw_hvp_raw(costs, tangent, (float)temperature, len, s,
+                       checked_dtw_bandwidth(bandwidth.has_value() ? *bandwidth : -1));
+}
+
+Tensor soft_dtw_param_jacobian_cuda(Tensor costs, double temperature, c10::optional<Tensor> lengths,
+                                    c10::optional<int64_t> bandwidth) {
+    D2PB_CHECK_INPUT(costs);
+    TORCH_CHECK(costs.dim() == 3, "costs must be 3D");
+    const Shape s = checked_dtw_shape(costs);
+    c10::cuda::CUDAGuard guard(costs.device());
+    Tensor len = resolve_lengths(lengths, s, costs.device());
+    return dtw_jac_raw(costs, (float)temperature, len, s,
+                       checked_dtw_bandwidth(bandwidth.has_value() ? *bandwidth : -1));
+}
+
+std::tuple<Tensor, Tensor> soft_dtw_backward_full_cuda(Tensor costs, Tensor grad_alignment, double temperature,
+                                                       c10::optional<Tensor> lengths,
+                                                       c10::optional<int64_t> bandwidth) {
+    D2PB_CHECK_INPUT(costs);
+    TORCH_CHECK(costs.dim() == 3, "costs must be 3D (B, L1, L2)");
+    TORCH_CHECK(grad_alignment.sizes() == costs.sizes(), "grad_alignment must have same shape as costs");
+    TORCH_CHECK(grad_alignment.is_cuda(), "grad_alignment must be a CUDA tensor");
+    TORCH_CHECK(grad_alignment.device() == costs.device(), "grad_alignment must be on same device as costs, got ",
+                grad_alignment.device(), " vs ", costs.device());
+    const Shape s = checked_dtw_shape(costs);
+    c10::cuda::CUDAGuard guard(costs.device());
+    Tensor len = resolve_lengths(lengths, s, costs.device());
+    Tensor G = grad_alignment.contiguous();
+    if (G.scalar_type() != torch::kFloat32) G = G.to(torch::kFloat32);
+    return dtw_backward_full_raw(costs, G, (float)temperature, len, s,
+                                 checked_dtw_bandwidth(bandwidth.has_value() ? *bandwidth : -1));
+}
+
 }  // namespace
 
 // =============================================================================
@@ -786,6 +991,13 @@ TORCH_LIBRARY_FRAGMENT(d2p, m) {
     m.def("nw_affine_marginals_grad_gap_open(Tensor scores, float gap_open, float gap_ext, float temp, Tensor? lengths) -> Tensor");
     m.def("nw_affine_marginals_grad_gap_ext(Tensor scores, float gap_open, float gap_ext, float temp, Tensor? lengths) -> Tensor");
     m.def("nw_affine_marginals_grad_temp(Tensor scores, float gap_open, float gap_ext, float temp, Tensor? lengths) -> Tensor");
+    // soft DTW (src/dtw/registry.cpp:35-40)
+    m.def("soft_dtw(Tensor costs, Tensor temperature, Tensor lengths, int bandwidth) -> Tensor[]");
+    m.def("soft_dtw_float(Tensor costs, float temperature, Tensor? lengths, int? bandwidth) -> Tensor[]");
+    m.def("soft_dtw_with_grads(Tensor costs, float temperature, Tensor? lengths, int? bandwidth) -> (Tensor, Tensor, Tensor)");
+    m.def("soft_dtw_hvp(Tensor costs, Tensor tangent, float temperature, Tensor? lengths, int? bandwidth) -> Tensor");
+    m.def("soft_dtw_param_jacobian(Tensor costs, float temperature, Tensor? lengths, int? bandwidth) -> Tensor");
+    m.def("soft_dtw_backward_full(Tensor costs, Tensor grad_alignment, float temperature, Tensor? lengths, int? bandwidth) -> (Tensor, Tensor)");
 }
 
 TORCH_LIBRARY_IMPL(d2p, CUDA, m) {
@@ -843,6 +1055,12 @@ TORCH_LIBRARY_IMPL(d2p, CUDA, m) {
     m.impl("nw_affine_marginals_grad_gap_open", aff_marginals_grad_alias<kNWAff, 0>);
     m.impl("nw_affine_marginals_grad_gap_ext", aff_marginals_grad_alias<kNWAff, 1>);
     m.impl("nw_affine_marginals_grad_temp", aff_marginals_grad_alias<kNWAff, 2>);
+    m.impl("soft_dtw", soft_dtw_cuda);
+    m.impl("soft_dtw_float", soft_dtw_float_cuda);
+    m.impl("soft_dtw_with_grads", soft_dtw_with_grads_cuda);
+    m.impl("soft_dtw_hvp", soft_dtw_hvp_cuda);
+    m.impl("soft_dtw_param_jacobian", soft_dtw_param_jacobian_cuda);
+    m.impl("soft_dtw_backward_full", soft_dtw_backward_full_cuda);
 }
 
 // No CPU kernels by design: CPU tensors get a clear error instead of a silent
@@ -868,7 +1086,9 @@ TORCH_LIBRARY_IMPL(d2p, CPU, m) {
         "soft_nw_affine", "soft_nw_affine_float", "soft_nw_affine_with_grads", "soft_nw_affine_hvp",
         "soft_nw_affine_param_jacobian", "soft_nw_affine_backward_full", "nw_affine_forward", "nw_affine_forward_t",
         "nw_affine_value_grad_params", "nw_affine_marginals_backward", "nw_affine_marginals_hvp",
-        "nw_affine_marginals_grad_gap_open", "nw_affine_marginals_grad_gap_ext", "nw_affine_marginals_grad_temp"};
+        "nw_affine_marginals_grad_gap_open", "nw_affine_marginals_grad_gap_ext", "nw_affine_marginals_grad_temp",
+        "soft_dtw", "soft_dtw_float", "soft_dtw_with_grads", "soft_dtw_hvp", "soft_dtw_param_jacobian",
+        "soft_dtw_backward_full"};
     for (const char* name : kOps) m.impl(name, torch::CppFunction::makeFromBoxedFunction<&reject_cpu>());
 }
 
@@ -889,6 +1109,26 @@ using ForwardT = std::vector<Tensor>(Tensor, Tensor, Tensor, Tensor);
 using ForwardF = std::vector<Tensor>(Tensor, double, double, c10::optional<Tensor>);
 using AffForwardT = std::vector<Tensor>(Tensor, Tensor, Tensor, Tensor, Tensor);
 using AffForwardF = std::vector<Tensor>(Tensor, double, double, double, c10::optional<Tensor>);
+using DtwForwardT = std::vector<Tensor>(Tensor, Tensor, Tensor, int64_t);
+using DtwForwardF = std::vector<Tensor>(Tensor, double, c10::optional<Tensor>, c10::optional<int64_t>);
+
+std::vector<Tensor> dtw_fwd_t_autograd(Tensor costs, Tensor temperature, Tensor lengths, int64_t bandwidth) {
+    if (is_python_tensor(costs)) {
+        static auto op = op_handle<DtwForwardT>("d2p::soft_dtw");
+        at::AutoDispatchBelowADInplaceOrView below;
+        return op.call(costs, temperature, lengths, bandwidth);
+    }
+    return soft_dtw_cuda(costs, temperature, lengths, bandwidth);
+}
+std::vector<Tensor> dtw_fwd_f_autograd(Tensor costs, double temperature, c10::optional<Tensor> lengths,
+                                       c10::optional<int64_t> bandwidth) {
+    if (is_python_tensor(costs)) {
+        static auto op = op_handle<DtwForwardF>("d2p::soft_dtw_float");
+        at::AutoDispatchBelowADInplaceOrView below;
+        return op.call(costs, temperature, lengths, bandwidth);
+    }
+    return soft_dtw_float_cuda(costs, temperature, lengths, bandwidth);
+}
 
 template <const char* Name, int FAM>
 std::vector<Tensor> fwd_t_autograd(Tensor scores, Tensor gap, Tensor temperature, Tensor lengths) {
@@ -962,4 +1202,6 @@ TORCH_LIBRARY_IMPL(d2p, AutogradCUDA, m) {
     m.impl("soft_nw_affine_float", aff_fwd_f_autograd<kSoftNWAffineFloat, kNWAff>);
     m.impl("nw_affine_forward", aff_fwd_f_autograd<kNWAffineForward, kNWAff>);
     m.impl("nw_affine_forward_t", aff_fwd_t_autograd<kNWAffineForwardT, kNWAff>);
+    m.impl("soft_dtw", dtw_fwd_t_autograd);
+    m.impl("soft_dtw_float", dtw_fwd_f_autograd);
 }

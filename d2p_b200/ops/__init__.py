@@ -19,6 +19,7 @@ from .._ops import (  # noqa: F401
     soft_nw_affine_param_jacobian, soft_nw_affine_backward_full, nw_affine_forward, nw_affine_forward_t,
     nw_affine_value_grad_params, nw_affine_marginals_backward, nw_affine_marginals_hvp,
     nw_affine_marginals_grad_gap_open, nw_affine_marginals_grad_gap_ext, nw_affine_marginals_grad_temp,
+    soft_dtw, soft_dtw_float, soft_dtw_with_grads, soft_dtw_hvp, soft_dtw_param_jacobian, soft_dtw_backward_full,
 )
 
 __all__ = [
@@ -39,4 +40,6 @@ __all__ = [
     "soft_nw_affine_param_jacobian", "soft_nw_affine_backward_full", "nw_affine_forward", "nw_affine_forward_t",
     "nw_affine_value_grad_params", "nw_affine_marginals_backward", "nw_affine_marginals_hvp",
     "nw_affine_marginals_grad_gap_open", "nw_affine_marginals_grad_gap_ext", "nw_affine_marginals_grad_temp",
+    "soft_dtw", "soft_dtw_float", "soft_dtw_with_grads", "soft_dtw_hvp", "soft_dtw_param_jacobian",
+    "soft_dtw_backward_full",
 ]

@@ -51,6 +51,7 @@ extern "C" {
 #define D2P_FAMILY_AFFINE 1
 #define D2P_FAMILY_NW 2 /* soft Needleman-Wunsch, linear gap (d2p_nw_*) */
 #define D2P_FAMILY_NW_AFFINE 3 /* soft Needleman-Wunsch, affine gaps (d2p_nw_affine_*) */
+#define D2P_FAMILY_DTW 4 /* soft dynamic time warping (d2p_dtw_*) */
 
 #define D2P_OP_FORWARD_BACKWARD 0
 #define D2P_OP_HVP 1
@@ -256,6 +257,30 @@ D2P_API int d2p_nw_affine_backward_full(const float* scores, const float* grad_m
                                         float* grad_scores, float* grad_gap_open, float* grad_gap_ext,
                                         float* grad_temperature, void* workspace, size_t workspace_bytes,
                                         void* stream);
+
+/* ---- soft dynamic time warping (softmin over the three predecessors) ----
+ * alpha[0,0] = 0; alpha[i,j] = costs[i,j] + softmin_T of the three
+ * predecessors for cells inside the Sakoe-Chiba band |j - i L2 / L1| <=
+ * bandwidth (bandwidth < 0: no band); S = alpha[L1, L2] (the sentinel 1e30
+ * when a sequence is empty or the end cannot be reached); marginal = the
+ * probability that the warping path visits (i, j).  fp32 costs; lengths may
+ * be NULL (full lengths).  Workspace from
+ * d2p_sw_workspace_bytes(D2P_FAMILY_DTW, op, ...).  They replace the
+ * reference's dtw launchers (src/dtw/kernels.cuh) behind its soft_dtw
+ * operators (src/dtw/torch_cuda.cpp, src/dtw/registry.cpp:35-40). */
+D2P_API int d2p_dtw_forward_backward(const float* costs, const int* lengths, int B, int L1, int L2,
+                                     float temperature, const float* temperature_dev, int bandwidth, float* value,
+                                     float* marginals, float* grad_temperature, void* workspace,
+                                     size_t workspace_bytes, void* stream);
+D2P_API int d2p_dtw_hvp(const float* costs, const float* tangent, const int* lengths, int B, int L1, int L2,
+                        float temperature, int bandwidth, float* hvp, void* workspace, size_t workspace_bytes,
+                        void* stream);
+D2P_API int d2p_dtw_param_jacobian(const float* costs, const int* lengths, int B, int L1, int L2, float temperature,
+                                   int bandwidth, float* jacobian, void* workspace, size_t workspace_bytes,
+                                   void* stream);
+D2P_API int d2p_dtw_backward_full(const float* costs, const float* grad_marginals, const int* lengths, int B, int L1,
+                                  int L2, float temperature, int bandwidth, float* grad_costs,
+                                  float* grad_temperature, void* workspace, size_t workspace_bytes, void* stream);
 
 /* Engine selection for the whole process (all devices): D2P_ENGINE_AUTO picks
  * per shape (the default, or what D2P_B200_ENGINE names at load: "plane",

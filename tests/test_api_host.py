@@ -85,6 +85,19 @@ SCHEMAS.update({
         SCHEMAS[name].replace("soft_sw", "soft_nw").replace("sw_", "nw_")
     for name in list(SCHEMAS) if "affine" in name and "sw" in name
 })
+# src/dtw/registry.cpp:35-40, verbatim
+SCHEMAS.update({
+    "soft_dtw": "soft_dtw(Tensor costs, Tensor temperature, Tensor lengths, int bandwidth) -> Tensor[]",
+    "soft_dtw_float": "soft_dtw_float(Tensor costs, float temperature, Tensor? lengths, int? bandwidth) -> Tensor[]",
+    "soft_dtw_with_grads": "soft_dtw_with_grads(Tensor costs, float temperature, Tensor? lengths, int? bandwidth) -> "
+                           "(Tensor, Tensor, Tensor)",
+    "soft_dtw_hvp": "soft_dtw_hvp(Tensor costs, Tensor tangent, float temperature, Tensor? lengths, int? bandwidth) "
+                    "-> Tensor",
+    "soft_dtw_param_jacobian": "soft_dtw_param_jacobian(Tensor costs, float temperature, Tensor? lengths, "
+                               "int? bandwidth) -> Tensor",
+    "soft_dtw_backward_full": "soft_dtw_backward_full(Tensor costs, Tensor grad_alignment, float temperature, "
+                              "Tensor? lengths, int? bandwidth) -> (Tensor, Tensor)",
+})
 
 
 def _schema(name):
@@ -100,6 +113,13 @@ def test_every_reference_schema_is_registered_verbatim():
 
 def _call_args(name, s, B):
     """Arguments of op `name` for scores `s` (float parameters, full lengths)."""
+    if "dtw" in name:
+        ln = torch.full((B, 2), 1, dtype=torch.int32, device=s.device)
+        if name == "soft_dtw":
+            return (s, s.new_tensor([1.0]), ln, -1)
+        if "hvp" in name or "backward" in name:
+            return (s, torch.zeros_like(s), 1.0, None, None)
+        return (s, 1.0, None, None)
     aff = "affine" in name
     fl = (-2.0, -0.5, 1.0) if aff else (-1.0, 1.0)
     t = [s.new_tensor([v]) for v in fl]
@@ -128,6 +148,8 @@ LAYOUT = {
 }
 LAYOUT.update({k.replace("soft_sw", "soft_nw").replace("sw_", "nw_"): v for k, v in list(LAYOUT.items())
                if "sw" in k})
+LAYOUT.update({"soft_dtw": "BP", "soft_dtw_float": "BP", "soft_dtw_with_grads": "BPB", "soft_dtw_hvp": "P",
+               "soft_dtw_param_jacobian": "P", "soft_dtw_backward_full": "P1"})
 
 
 @pytest.mark.parametrize("name", sorted(SCHEMAS))
@@ -148,7 +170,7 @@ def test_fake_kernels_give_the_reference_shapes(name):
 
 @pytest.mark.parametrize("name", ["soft_sw_float", "soft_sw_hvp", "soft_sw_affine_float", "sw_affine_marginals_hvp",
                                   "soft_nw_float", "nw_marginals_backward", "soft_nw_affine_float",
-                                  "nw_affine_marginals_hvp"])
+                                  "nw_affine_marginals_hvp", "soft_dtw_float", "soft_dtw_backward_full"])
 def test_cpu_tensors_are_rejected(name):
     """No CPU kernel and no silent fallback: a CPU input raises, naming CUDA."""
     s = torch.randn(2, 4, 5)
