@@ -126,7 +126,8 @@ int launch_lin_fast(const SwArgs& a, size_t ws_bytes, cudaStream_t st);
 // 16-byte units go through padded copies in the workspace); returns -1 when
 // the shape or arguments are not covered
 size_t lin_strip_workspace_bytes(int B, int L1, int L2);
-int launch_lin_strip(const SwArgs& a, size_t ws_bytes, cudaStream_t st);
+// nw: soft Needleman-Wunsch instead of Smith-Waterman (value + marginals)
+int launch_lin_strip(const SwArgs& a, size_t ws_bytes, cudaStream_t st, bool nw = false);
 // affine-gap linear-domain fast path (sw_affine_fast.cu): value + marginals
 // without parameter gradients, fp32 or bf16 scores (bf16 widened into the
 // workspace first); returns -1 when the shape or arguments are not covered

@@ -24,6 +24,10 @@
 // dw_k = w_k (dv_k - d alpha) / T (+ w_k (E[v] - v_k) / T^2 along T), and the
 // marginal's tangent d beta w_diag + beta dw_diag (src/nw/kernels_cpu.cpp:278-642).
 //
+// Value + marginals without parameter gradients run on the column-sweep strip
+// kernel (sw_strip.cu, its NW form) for problems of at most 512 rows; this
+// engine takes the rest and recomputes whatever the strip kernel flags.
+//
 // Engine.  One CTA per problem sweeps the anti-diagonals (k = i + j), the
 // threads striding over the cells of a diagonal, with one barrier per
 // diagonal.  Per-cell values live in diagonal-major planes in the workspace
@@ -101,6 +105,7 @@ template <int MODE>
 __global__ void __launch_bounds__(kThreads) nw_kernel(SwArgs p) {
     __shared__ double red[32];
     const int b = blockIdx.x;
+    if (p.only && !p.only[b]) return;   // a fix-up launch: only the problems the strip kernel flagged
     const int L1m = p.L1, L2m = p.L2;
     const int L1 = p.lengths ? min(max(p.lengths[2 * b], 0), L1m) : L1m;
     const int L2 = p.lengths ? min(max(p.lengths[2 * b + 1], 0), L2m) : L2m;
@@ -299,10 +304,21 @@ __global__ void __launch_bounds__(kThreads) nw_kernel(SwArgs p) {
 }  // namespace nw
 
 // ------------------------------------------------------------------ host side
+static size_t a256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+// value + marginals: the engine's planes or the strip kernel's workspace,
+// whichever is larger, then the strip kernel's flags and CTA order (B ints each)
+static size_t nw_fb_area(int B, int L1, int L2) {
+    size_t n = a256(nw::per_problem_bytes(L1, L2, MODE_MARG) * (size_t)(B > 0 ? B : 1));
+    const size_t sf = lin_strip_workspace_bytes(B, L1, L2);
+    return n > sf ? n : a256(sf);
+}
+
 size_t nw_workspace_bytes(int op, int B, int L1, int L2) {
-    const size_t fb = nw::per_problem_bytes(L1, L2, op == D2P_OP_FORWARD_BACKWARD ? MODE_MARG : MODE_PT);
-    size_t n = (fb * (size_t)(B > 0 ? B : 1) + 255) & ~(size_t)255;
-    if (op == D2P_OP_BACKWARD_FULL) n += ((size_t)2 * (B > 0 ? B : 1) * sizeof(float) + 255) & ~(size_t)255;
+    const size_t nb = (size_t)(B > 0 ? B : 1);
+    if (op == D2P_OP_FORWARD_BACKWARD) return nw_fb_area(B, L1, L2) + 2 * a256(nb * sizeof(int));
+    size_t n = a256(nw::per_problem_bytes(L1, L2, MODE_PT) * nb);
+    if (op == D2P_OP_BACKWARD_FULL) n += a256((size_t)2 * nb * sizeof(float));
     return n;
 }
 
@@ -361,7 +377,29 @@ int d2p_nw_forward_backward(const float* scores, const int* lengths, int B, int 
     a.out = marginals;
     a.grad_gap = grad_gap;
     a.grad_T = grad_temperature;
-    return launch_nw(a, (cudaStream_t)stream);
+    cudaStream_t st = (cudaStream_t)stream;
+    if (!grad_gap && !grad_temperature) {
+        // value + marginals: the column-sweep strip kernel (problems of at most
+        // 512 rows); the engine recomputes only the problems it flags
+        const size_t area = nw_fb_area(B, L1, L2);
+        int* flags = (int*)((char*)workspace + area);
+        int* order = (int*)((char*)flags + a256((size_t)B * sizeof(int)));
+        a.redo = flags;
+        if (lengths) {
+            const int ro = launch_lin_order(lengths, B, L1, L2, order, st);
+            if (ro == D2P_OK) a.order = order;
+            else if (ro != -1) return ro;
+        }
+        const int rc = launch_lin_strip(a, area, st, true);
+        a.order = nullptr;
+        a.redo = nullptr;
+        if (rc == D2P_OK) {
+            a.only = flags;
+            return launch_nw(a, st);
+        }
+        if (rc != -1) return rc;
+    }
+    return launch_nw(a, st);
 }
 
 int d2p_nw_hvp(const float* scores, const float* tangent, const int* lengths, int B, int L1, int L2, float gap,

@@ -105,6 +105,7 @@ struct Hand {                          // handoffs between the warps of a set, b
 struct Meet {                          // the reverse's values at the cut, per row block
     float B[kWR], PB[kWR];
     float Q[32];
+    float b0;                          // NW, row block 0: B of the boundary row 0 (lane 0's frame)
 };
 
 // The warps' tiles come last, so that a CTA of W warps per direction
@@ -222,6 +223,7 @@ struct Args {
 struct Prob {
     float c, gl, G, G2;
     int L1, L2, nv;     // nv: rows of this lane inside the problem (0..4)
+    int rend;           // NW: the end row's place in this lane's strip (0..3), -1 when another lane holds it
 };
 
 __device__ __forceinline__ void prob_init(const Args& A, int b, int w, int lane, Prob& p) {
@@ -234,6 +236,8 @@ __device__ __forceinline__ void prob_init(const Args& A, int b, int w, int lane,
     p.L1 = A.lengths ? min(max(A.lengths[2 * b], 0), A.L1v) : A.L1v;
     p.L2 = A.lengths ? min(max(A.lengths[2 * b + 1], 0), A.L2v) : A.L2v;
     p.nv = min(max(p.L1 - kWR * w - kR * lane, 0), kR);
+    const int er = p.L1 - 1 - kWR * w - kR * lane;   // the end row (0-based) relative to this strip
+    p.rend = (er >= 0 && er < kR) ? er : -1;
 }
 
 // Constants of one lane for one block (forward): from its frame E, its upper
@@ -274,22 +278,27 @@ struct RevK {
     float Min;          // G^(4 (32-l)) 2^(Qin - Q): the row below the warp into this lane's first row
 };
 
-__device__ __forceinline__ void rev_consts(const Prob& p, float Q, float Qin, bool below, int lane, RevK& k) {
+// lv: the last lane with rows of the problem (31 when the warp is full).  Lanes
+// below it hold zeros in frame 0; NW frames can lie far below 0, and a
+// conversion factor from such a lane would overflow (inf x 0), so NW passes lv
+// and takes nothing from them.
+__device__ __forceinline__ void rev_consts(const Prob& p, float Q, float Qin, bool below, int lane, RevK& k,
+                                           int lv = 31) {
     float q1 = __shfl_down_sync(kAll, Q, 1);
     const float q2 = __shfl_down_sync(kAll, Q, 2), q4 = __shfl_down_sync(kAll, Q, 4);
     const float q8 = __shfl_down_sync(kAll, Q, 8), q16 = __shfl_down_sync(kAll, Q, 16);
     if (lane == 31) q1 = Qin;
-    const bool has1 = lane <= 30 || below;
+    const bool has1 = lane + 1 <= lv || (lane == 31 && below);
     k.fsq = ex2f(-Q);
     const float d1 = q1 - Q;
     k.m1 = has1 ? ex2f(d1) : 0.f;
 #pragma unroll
     for (int r = 0; r < kR; ++r) k.Gm[r] = has1 ? ex2f(fmaf((float)(kR - r), p.gl, d1)) : 0.f;
-    k.M[0] = lane <= 30 ? ex2f(fmaf(4.f, p.gl, d1)) : 0.f;
-    k.M[1] = lane <= 29 ? ex2f(fmaf(8.f, p.gl, q2 - Q)) : 0.f;
-    k.M[2] = lane <= 27 ? ex2f(fmaf(16.f, p.gl, q4 - Q)) : 0.f;
-    k.M[3] = lane <= 23 ? ex2f(fmaf(32.f, p.gl, q8 - Q)) : 0.f;
-    k.M[4] = lane <= 15 ? ex2f(fmaf(64.f, p.gl, q16 - Q)) : 0.f;
+    k.M[0] = lane + 1 <= lv ? ex2f(fmaf(4.f, p.gl, d1)) : 0.f;
+    k.M[1] = lane + 2 <= lv ? ex2f(fmaf(8.f, p.gl, q2 - Q)) : 0.f;
+    k.M[2] = lane + 4 <= lv ? ex2f(fmaf(16.f, p.gl, q4 - Q)) : 0.f;
+    k.M[3] = lane + 8 <= lv ? ex2f(fmaf(32.f, p.gl, q8 - Q)) : 0.f;
+    k.M[4] = lane + 16 <= lv ? ex2f(fmaf(64.f, p.gl, q16 - Q)) : 0.f;
     k.Min = below ? ex2f(fmaf((float)(kR * (32 - lane)), p.gl, Qin - Q)) : 0.f;
 }
 
@@ -346,16 +355,17 @@ __device__ __forceinline__ float fwd_column(const Prob& p, const FwdK& k, float 
 // Qin), pbn: P B of that row at column j+1 (lane 31, already in its frame).  w
 // is replaced by the marginals (before the frame factor).  MASK: cells outside
 // the problem are 0 (B, and so P B, and the marginals).
-template <bool MASK>
+template <bool MASK, bool NW>
 __device__ __forceinline__ void rev_column(const Prob& p, const RevK& k, float (&Bv)[kR], float (&PB)[kR],
                                            const float (&P)[kR], float (&w)[kR], float bin, float pbn, int nvc,
-                                           int lane) {
+                                           int lane, int onerow, float k1 = 1.f, float k2 = 1.f) {
     float pbd = __shfl_down_sync(kAll, PB[0], 1) * k.m1;   // lane l+1's top row, column j+1
     if (lane == 31) pbd = pbn;
     float cc[kR];
 #pragma unroll
     for (int r = 0; r < kR; ++r) {
-        const float one = (!MASK || r < nvc) ? k.fsq : 0.f;
+        // SW: a path may end at any cell; NW: only at the end cell (onerow of this lane)
+        const float one = NW ? (r == onerow ? k.fsq : 0.f) : ((!MASK || r < nvc) ? k.fsq : 0.f);
         cc[r] = fmaf(p.G, Bv[r], one + (r + 1 < kR ? PB[r + 1] : pbd));
     }
     // suffix of the strip: cc[r] <- sum_{q >= r} G^(q-r) cc[q]
@@ -377,9 +387,26 @@ __device__ __forceinline__ void rev_column(const Prob& p, const RevK& k, float (
         const float b = fmaf(k.Gm[r], yn, cc[r]);
         Bv[r] = b;
         PB[r] = P[r] * b;
-        const float m = b * w[r];
+        const float m = NW ? (b * k1) * (w[r] * k2) : b * w[r];
         w[r] = (!MASK || r < nvc) ? m : 0.f;
     }
+}
+
+// NW: log2 C(n + 4, 4), the growth of the number of paths over the first four
+// columns next to an edge n rows away (the frames at the grid's edges start
+// half a block ahead, so that the first block's combinatorial growth stays
+// inside the frame window)
+__device__ __forceinline__ float nw_lead(int n) {
+    const float f = (float)(n + 1) * (float)(n + 2) * (float)(n + 3) * (float)(n + 4) * (1.f / 24.f);
+    return log2f(f);
+}
+// NW frame steps may reach this (the edges' combinatorial growth); marginals
+// are then formed as (b 2^xa) (w 2^(x - xa)) so that b w cannot overflow
+constexpr int kJMaxNW = 90;
+__device__ __forceinline__ void split_scale(float x, float& k1, float& k2) {
+    const float xa = fminf(fmaxf(floorf(0.5f * x), -126.f), 126.f);
+    k1 = ex2f(xa);
+    k2 = ex2f(fminf(fmaxf(x - xa, -126.f), 126.f));
 }
 
 // Largest value of the strip -> the frame step J (new frame E + J) and 2^-J.
@@ -455,6 +482,7 @@ __device__ __forceinline__ void put_partial(CtaSmem& S, int slot, float base, do
 
 // S = log2(1 + sum of the partials of slots o .. o + n - 1), as integer +
 // fraction; false when not finite
+template <bool NW>
 __device__ __forceinline__ bool partition(const CtaSmem& S, int o, int n, float& Sint, float& Sfrac) {
     float m = -3.0e38f;
     for (int g = 0; g < 3; ++g)
@@ -462,7 +490,7 @@ __device__ __forceinline__ bool partition(const CtaSmem& S, int o, int n, float&
     double tot = 0.0;
     for (int g = 0; g < 3; ++g)
         for (int v = o; v < o + n; ++v) tot = fma(S.psum[g * kMaxW + v], ld::p2d(S.pbase[g * kMaxW + v] - m), tot);
-    tot += ld::p2d(-m);   // alpha[0,0] = 0 adds 1
+    if (!NW) tot += ld::p2d(-m);   // SW: alpha[0,0] = 0 adds 1 (the empty path)
     const int hi = __double2hiint(tot);
     const int ef = (hi >> 20) & 0x7ff;
     Sint = (float)(ef - 1023 + (int)m);
@@ -511,12 +539,14 @@ struct FwdState {
     float ab;
     int jmax;
     float Qn;           // phase 2: the reverse's frame of the block
+    float endz, endE;   // NW: Z of the end cell (in the lane that holds it) and its frame
+    int nf;             // NW: a marginal came out non-finite
 };
 
 // One forward block bk.  Phase 1 (!P2): keeps w and adds the block's Z to the
 // partition.  Phase 2: forms the marginals from the kept B, writes them over
 // the block's scores in shared memory and stores that tile.
-template <bool MASK, bool P2>
+template <bool MASK, bool P2, bool NW>
 __device__ __forceinline__ void fwd_block(const Sweep& sw, const Prob& p, FwdState& st, int bk, float Sint,
                                           float Sfrac) {
     CtaSmem& S = *sw.S;
@@ -541,13 +571,24 @@ __device__ __forceinline__ void fwd_block(const Sweep& sw, const Prob& p, FwdSta
     if (sw.above) {
         ring::wait_flag(&S.progF[sw.s - 1], bk + 1, err);
         Ein = Hup.fe[slot];
+    } else if (NW) {   // NW, warp 0: the boundary row 0 (Z_0j = G^j) is the row above
+        Ein = rintf((float)(kBC * bk) * p.gl);
     }
     if (sw.below && bk >= kHB) ring::wait_flag(&S.consF[sw.s + 1], bk - kHB + 1, err);   // ring space
     FwdK K;
-    fwd_consts(p, st.E, Ein, sw.above, lane, K);
-    float kE = 0.f;
+    fwd_consts(p, st.E, Ein, sw.above || NW, lane, K);
+    if (NW) K.fs = 0.f;   // no path starts inside the grid
+    float kE = 0.f, k1 = 1.f, k2 = 1.f;
     if (P2) {   // marginals = B w 2^(Q + E - S)
-        kE = ex2f((st.Qn + st.E - Sint) - Sfrac);
+        const float x = (st.Qn + st.E - Sint) - Sfrac;
+        if (NW) {
+            split_scale(x, k1, k2);
+            kE = 1.f;
+        } else {
+            // (clamped: a lane with no cells of the problem has B w = 0, and 0 x
+            // inf would be NaN)
+            kE = fminf(ex2f(x), 3.0e38f);
+        }
         if (bk + 1 < nT) st.Qn = sw.pfr[32 * (bk + 1)];
     }
     float gs = 0.f;
@@ -578,15 +619,27 @@ __device__ __forceinline__ void fwd_block(const Sweep& sw, const Prob& p, FwdSta
         for (int c = 0; c < kQC; ++c) {
             const int j = j0 + c;
             const int nvc = MASK ? (j < p.L2 ? p.nv : 0) : kR;
-            const float yin = sw.above ? Hup.fv[slot][kQC * q + c] : 0.f;
+            const float yin = sw.above ? Hup.fv[slot][kQC * q + c]
+                                       : (NW ? ex2f(fmaf((float)(j + 1), p.gl, -Ein)) : 0.f);
             float wv[kR];
             const float y = fwd_column<MASK>(p, K, st.z, st.dc, P[c], yin, nvc, lane, wv, gs);
+            if (NW && !P2 && j == p.L2 - 1 && p.rend >= 0) {   // the end cell: the partition when no cut crosses
+                st.endz = p.rend == 0 ? st.z[0] : p.rend == 1 ? st.z[1] : p.rend == 2 ? st.z[2] : st.z[3];
+                st.endE = st.E;
+            }
             if (sw.below && lane == 31) Hme.fv[slot][kQC * q + c] = y;
             if (!P2) {
                 sw.kp[32 * j] = f4(wv[0], wv[1], wv[2], wv[3]);
             } else {
                 const float4 bv = kr[32 * c + lane];
-                mu[c] = f4(bv.x * wv[0], bv.y * wv[1], bv.z * wv[2], bv.w * wv[3]);
+                if (NW) {
+                    mu[c] = f4((bv.x * k1) * (wv[0] * k2), (bv.y * k1) * (wv[1] * k2), (bv.z * k1) * (wv[2] * k2),
+                               (bv.w * k1) * (wv[3] * k2));
+                    const float t = (mu[c].x + mu[c].y) + (mu[c].z + mu[c].w);
+                    if (!(fabsf(t) <= 3.0e38f)) st.nf = 1;
+                } else {
+                    mu[c] = f4(bv.x * wv[0], bv.y * wv[1], bv.z * wv[2], bv.w * wv[3]);
+                }
             }
         }
         if (P2) {
@@ -616,7 +669,7 @@ __device__ __forceinline__ void fwd_block(const Sweep& sw, const Prob& p, FwdSta
     }
 }
 
-template <bool MASK>
+template <bool MASK, bool NW>
 __device__ void run_fwd(const Sweep& sw, const Args& A) {
     CtaSmem& S = *sw.S;
     const int lane = sw.lane, w = sw.w, nT = sw.nT, nL = sw.nL;
@@ -634,11 +687,28 @@ __device__ void run_fwd(const Sweep& sw, const Args& A) {
     st.acc = 0.0;
     st.jmax = 0;
     st.Qn = 0.f;
+    st.endz = 0.f;
+    st.endE = -3.0e38f;
+    st.nf = 0;
+    if (NW && p.nv > 0) {
+        // the boundary column 0: Z_i0 = G^i for this strip's rows, and Z of the
+        // row above the strip as the first column's diagonal predecessor
+        const int i0 = kWR * w + kR * lane + 1;   // the strip's first row (1-based)
+        st.E = rintf(fmaf((float)i0, p.gl, nw_lead(i0)));
+#pragma unroll
+        for (int r = 0; r < kR; ++r) st.z[r] = r < p.nv ? ex2f(fmaf((float)(i0 + r), p.gl, -st.E)) : 0.f;
+        st.dc = ex2f(fmaf((float)(i0 - 1), p.gl, -st.E));
+    }
 
-    for (int bk = 0; bk < nL; ++bk) fwd_block<MASK, false>(sw, p, st, bk, 0.f, 0.f);
+    for (int bk = 0; bk < nL; ++bk) fwd_block<MASK, false, NW>(sw, p, st, bk, 0.f, 0.f);
 
     // the cut
-    put_partial(S, sw.s, st.ab, st.acc, lane);
+    if (NW) {   // every column left of the cut (nL == nT): the partition is the end cell's Z
+        const bool e = nL == nT && p.rend >= 0;
+        put_partial(S, sw.s, e ? st.endE : -3.0e38f, e ? (double)st.endz : 0.0, lane);
+    } else {
+        put_partial(S, sw.s, st.ab, st.acc, lane);
+    }
     prob_barrier(sw.pbar, 0, sw.err, lane);   // phase 1 done: every partial and the reverse's values at the cut are in
     if (nL < nT) {   // the moves across the cut: Z_{i,m} (G B_{i,m+1} + P_{i+1,m+1} B_{i+1,m+1})
         const Meet& M = S.meet[sw.s];
@@ -658,12 +728,19 @@ __device__ void run_fwd(const Sweep& sw, const Args& A) {
 #pragma unroll
         for (int r = 0; r < kR; ++r)
             s1 = fmaf(st.z[r], fmaf(p.G, M.B[kR * lane + r], r + 1 < kR ? M.PB[kR * lane + r + 1] : 0.f), s1);
-        const double cr = (double)s1 + (double)(st.z[kR - 1] * pn) * ld::p2d(Qb - Ql);
+        double cr = (double)s1 + (double)(st.z[kR - 1] * pn) * ld::p2d(Qb - Ql);
+        if (NW && w == 0 && lane == 0) {
+            // the moves out of the boundary row 0 at the cut column m: Z_0m = G^m,
+            // to (0, m+1) and to (1, m+1)
+            const float x = fmaf((float)(kBC * nL), p.gl, -st.E);   // log2 of G^m in this lane's frame
+            const float xi = floorf(x);
+            cr += (double)(fmaf(p.G, M.b0, M.PB[0]) * ex2f(x - xi)) * ld::p2d(xi);
+        }
         put_partial(S, 2 * kMaxW + sw.s, st.E + Ql, cr, lane);
     }
     prob_barrier(sw.pbar, 1, sw.err, lane);
     float Sint, Sfrac;
-    const bool fin = partition(S, sw.o, sw.Wp, Sint, Sfrac);
+    const bool fin = partition<NW>(S, sw.o, sw.Wp, Sint, Sfrac);
     if (w == 0 && lane == 0 && A.value) A.value[sw.b] = (Sint + Sfrac) / p.c;
 
     if (nL < nT) {
@@ -674,10 +751,11 @@ __device__ void run_fwd(const Sweep& sw, const Args& A) {
         }
         st.Qn = sw.pfr[32 * nL];
     }
-    for (int bk = nL; bk < nT; ++bk) fwd_block<MASK, true>(sw, p, st, bk, Sint, Sfrac);
+    for (int bk = nL; bk < nT; ++bk) fwd_block<MASK, true, NW>(sw, p, st, bk, Sint, Sfrac);
 
-    const bool bad = __any_sync(kAll, st.jmax > ld::kJMax);
-    if (lane == 0 && (bad || !fin)) atomicOr(sw.err, bad ? 4 : 8);
+    const bool bad = __any_sync(kAll, st.jmax > (NW ? kJMaxNW : ld::kJMax));
+    const bool nf = NW && __any_sync(kAll, st.nf != 0);
+    if (lane == 0 && (bad || !fin || nf)) atomicOr(sw.err, bad ? 4 : 8);
 }
 
 // ------------------------------------------------------------------ reverse
@@ -689,12 +767,14 @@ struct RevState {
     float ab;
     int jmax;
     float En;           // phase 2: the forward's frame of the block
+    float b0;           // NW, warp 0 lane 0: B of the boundary row 0 at the current column
+    int nf;             // NW: a marginal came out non-finite
 };
 
 // One reverse block bk (ordinal rb).  Phase 1 (!P2): keeps B and adds the
 // block's P B to the partition.  Phase 2: forms the marginals from the kept w,
 // over the block's scores, and stores them.
-template <bool MASK, bool P2>
+template <bool MASK, bool P2, bool NW>
 __device__ __forceinline__ void rev_block(const Sweep& sw, const Prob& p, RevState& st, int rb, float Sint,
                                           float Sfrac) {
     CtaSmem& S = *sw.S;
@@ -715,6 +795,7 @@ __device__ __forceinline__ void rev_block(const Sweep& sw, const Prob& p, RevSta
             st.PB[r] *= inv;
         }
         st.pbin *= inv;
+        if (NW) st.b0 *= inv;
         st.Q += J;
         if (!P2) ld::acc_rebase(st.acc, st.ab, st.Q);
     }
@@ -725,10 +806,16 @@ __device__ __forceinline__ void rev_block(const Sweep& sw, const Prob& p, RevSta
     }
     if (sw.above && rb >= kHB) ring::wait_flag(&S.consR[sw.s - 1], rb - kHB + 1, err);   // ring space
     RevK K;
-    rev_consts(p, st.Q, Qin, sw.below, lane, K);
-    float kE = 0.f;
+    rev_consts(p, st.Q, Qin, sw.below, lane, K, NW ? min(31, (p.L1 - 1 - kWR * sw.w) / kR) : 31);
+    float kE = 0.f, k1 = 1.f, k2 = 1.f;
     if (P2) {   // marginals = B w 2^(Q + E - S)
-        kE = ex2f((st.Q + st.En - Sint) - Sfrac);
+        const float x = (st.Q + st.En - Sint) - Sfrac;
+        if (NW) {
+            split_scale(x, k1, k2);
+            kE = 1.f;
+        } else {
+            kE = fminf(ex2f(x), 3.0e38f);
+        }
         if (bk > 0) st.En = sw.pfr[32 * (bk - 1)];
     }
     float gs = 0.f;
@@ -771,7 +858,17 @@ __device__ __forceinline__ void rev_block(const Sweep& sw, const Prob& p, RevSta
             } else {
                 wk[0] = wk[1] = wk[2] = wk[3] = 0.f;
             }
-            rev_column<MASK>(p, K, st.Bv, st.PB, P[c], wk, bin, pbn, nvc, lane);
+            const float pbprev = st.PB[0];
+            rev_column<MASK, NW>(p, K, st.Bv, st.PB, P[c], wk, bin, pbn, nvc, lane,
+                                 (NW && j == p.L2 - 1) ? p.rend : -1, k1, k2);
+            if (NW && P2) {
+                const float t = (wk[0] + wk[1]) + (wk[2] + wk[3]);
+                if (!(fabsf(t) <= 3.0e38f)) st.nf = 1;
+            }
+            // NW, warp 0 (lane 0's value is used): B of the boundary row 0 at this
+            // column, from row 1 here (down) and one column right (diagonal), and
+            // row 0 one column right
+            if (NW && !P2 && sw.w == 0) st.b0 = fmaf(p.G, st.b0 + st.Bv[0], pbprev);
             if (sw.above && lane == 0) {
                 Hme.rv[slot][cb] = st.Bv[0];
                 Hme.rp[slot][cb] = st.PB[0];
@@ -812,7 +909,7 @@ __device__ __forceinline__ void rev_block(const Sweep& sw, const Prob& p, RevSta
     }
 }
 
-template <bool MASK>
+template <bool MASK, bool NW>
 __device__ void run_rev(const Sweep& sw, const Args& A) {
     CtaSmem& S = *sw.S;
     const int lane = sw.lane, w = sw.w, nT = sw.nT, nL = sw.nL;
@@ -830,8 +927,18 @@ __device__ void run_rev(const Sweep& sw, const Args& A) {
     st.acc = 0.0;
     st.jmax = 0;
     st.En = 0.f;
+    st.b0 = 0.f;
+    st.nf = 0;
+    if (NW && p.nv > 0) {
+        // NW weights scale like G^(rows below): at the right edge B_iL2 = G^(L1 - i).
+        // Start each lane's frame there (and half a block ahead), so that lanes
+        // far above the end row do not begin as zeros that no frame step can
+        // bring back.
+        const int ilast = kWR * w + kR * lane + p.nv;   // the strip's last row inside the problem (1-based)
+        st.Q = rintf(fmaf((float)(p.L1 - ilast), p.gl, nw_lead(p.L1 - ilast)));
+    }
 
-    for (int rb = 0; rb < nT - nL; ++rb) rev_block<MASK, false>(sw, p, st, rb, 0.f, 0.f);
+    for (int rb = 0; rb < nT - nL; ++rb) rev_block<MASK, false, NW>(sw, p, st, rb, 0.f, 0.f);
 
     // the cut: B and P B at its right column (zero when nothing is right of it)
     Meet& M = S.meet[sw.s];
@@ -841,21 +948,24 @@ __device__ void run_rev(const Sweep& sw, const Args& A) {
         M.PB[kR * lane + r] = st.PB[r];
     }
     M.Q[lane] = st.Q;
-    put_partial(S, kMaxW + sw.s, st.ab, st.acc, lane);
+    if (NW && sw.w == 0 && lane == 0) M.b0 = st.b0;
+    // NW: no path starts right of the cut, nothing to add there
+    put_partial(S, kMaxW + sw.s, NW ? -3.0e38f : st.ab, NW ? 0.0 : st.acc, lane);
     prob_barrier(sw.pbar, 0, sw.err, lane);
     prob_barrier(sw.pbar, 1, sw.err, lane);   // the forward warps have added the moves across the cut
     float Sint, Sfrac;
-    partition(S, sw.o, sw.Wp, Sint, Sfrac);
+    partition<NW>(S, sw.o, sw.Wp, Sint, Sfrac);
 
     if (lane == 0) {   // the kept w of the last block left of the cut: group 1, then group 0
         load_kept(sw, 0, nL - 1, 1);
         load_kept(sw, 1, nL - 1, 0);
     }
     st.En = sw.pfr[32 * (nL - 1)];
-    for (int rb = nT - nL; rb < nT; ++rb) rev_block<MASK, true>(sw, p, st, rb, Sint, Sfrac);
+    for (int rb = nT - nL; rb < nT; ++rb) rev_block<MASK, true, NW>(sw, p, st, rb, Sint, Sfrac);
 
-    const bool bad = __any_sync(kAll, st.jmax > ld::kJMax);
-    if (lane == 0 && bad) atomicOr(sw.err, 4);
+    const bool bad = __any_sync(kAll, st.jmax > (NW ? kJMaxNW : ld::kJMax));
+    const bool nf = NW && __any_sync(kAll, st.nf != 0);
+    if (lane == 0 && (bad || nf)) atomicOr(sw.err, bad ? 4 : 8);
 }
 
 // rows and columns of problem b inside the padded shape
@@ -869,6 +979,10 @@ __device__ __forceinline__ void prob_shape(const Args& A, int b, int& L1, int& L
 // and the table gives each slot's problem and row block; a problem holds
 // max(Wact, 1) consecutive slots, and the last of them also writes the zeros
 // of the padded plane's row blocks past them.
+// NW: soft Needleman-Wunsch (global alignment): no start term, the boundary row
+// and column of gaps, the end cell's weight, the partition from the crossing
+// terms alone.
+template <bool NW>
 __global__ void __launch_bounds__(64 * kMaxW, 2) lin_strip_kernel(const __grid_constant__ CUtensorMap tmS,
                                                                 const __grid_constant__ CUtensorMap tmO,
                                                                 const Args A) {
@@ -977,14 +1091,14 @@ __global__ void __launch_bounds__(64 * kMaxW, 2) lin_strip_kernel(const __grid_c
             const bool mask = L1 < kWR * (w + 1) || L2 % kBC != 0;
             if (fwd) {
                 if (mask)
-                    run_fwd<true>(sw, A);
+                    run_fwd<true, NW>(sw, A);
                 else
-                    run_fwd<false>(sw, A);
+                    run_fwd<false, NW>(sw, A);
             } else {
                 if (mask)
-                    run_rev<true>(sw, A);
+                    run_rev<true, NW>(sw, A);
                 else
-                    run_rev<false>(sw, A);
+                    run_rev<false, NW>(sw, A);
             }
         }
         if (lane == 0) tma_store_wait0();
@@ -997,7 +1111,11 @@ __global__ void __launch_bounds__(64 * kMaxW, 2) lin_strip_kernel(const __grid_c
             const int b = e >> 2;
             int L1, L2;
             prob_shape(A, b, L1, L2);
-            if ((L1 == 0 || L2 == 0) && A.value && S.err[o] == 0) A.value[b] = 0.f;
+            if ((L1 == 0 || L2 == 0) && A.value && S.err[o] == 0) {
+                // SW: the empty path; NW: the one all-gap path
+                const float g = A.gap_dev ? *A.gap_dev : A.gap;
+                A.value[b] = NW ? (float)(L1 + L2) * g : 0.f;
+            }
             if (A.redo) A.redo[b] = S.err[o];
         }
     }
@@ -1144,7 +1262,7 @@ size_t lin_strip_workspace_bytes(int B, int L1, int L2) {
     return strip_main_bytes(B, L1, L2) + strip_pack_bytes(B);
 }
 
-int launch_lin_strip(const SwArgs& a, size_t ws_bytes, cudaStream_t st) {
+int launch_lin_strip(const SwArgs& a, size_t ws_bytes, cudaStream_t st, bool nw) {
     if (a.mode != MODE_MARG || !a.redo || a.grad_gap || a.grad_T || !a.out || !a.scores) return -1;
     if (engine_forced_plane() || engine_forced_pipeline()) return -1;
     if (!strip_shape_ok(a.L1, a.L2)) return -1;
@@ -1170,8 +1288,13 @@ int launch_lin_strip(const SwArgs& a, size_t ws_bytes, cudaStream_t st) {
     static DeviceSetup setup;
     int nsm = 0;
     const int se = device_setup(setup, dev, [] {
-        return (int)cudaFuncSetAttribute(strip::lin_strip_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)strip::smem_bytes_for(strip::kMaxW));
+        const int bytes = (int)strip::smem_bytes_for(strip::kMaxW);
+        cudaError_t e = cudaFuncSetAttribute(strip::lin_strip_kernel<false>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(strip::lin_strip_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     bytes);
+        return (int)e;
     }, &nsm);
     if (se != 0) return se;
     strip::Args A;
@@ -1207,9 +1330,14 @@ int launch_lin_strip(const SwArgs& a, size_t ws_bytes, cudaStream_t st) {
         if (pe != cudaSuccess) return (int)pe;
         A.pack = tab;
         A.order = nullptr;
-        strip::lin_strip_kernel<<<a.B, 64 * strip::kMaxW, strip::smem_bytes_for(strip::kMaxW), st>>>(tmS, tmO, A);
+        if (nw)
+            strip::lin_strip_kernel<true><<<a.B, 64 * strip::kMaxW, strip::smem_bytes_for(strip::kMaxW), st>>>(tmS, tmO, A);
+        else
+            strip::lin_strip_kernel<false><<<a.B, 64 * strip::kMaxW, strip::smem_bytes_for(strip::kMaxW), st>>>(tmS, tmO, A);
+    } else if (nw) {
+        strip::lin_strip_kernel<true><<<a.B, 64 * W, strip::smem_bytes_for(W), st>>>(tmS, tmO, A);
     } else {
-        strip::lin_strip_kernel<<<a.B, 64 * W, strip::smem_bytes_for(W), st>>>(tmS, tmO, A);
+        strip::lin_strip_kernel<false><<<a.B, 64 * W, strip::smem_bytes_for(W), st>>>(tmS, tmO, A);
     }
     cudaError_t e2 = cudaGetLastError();
     if (e2 != cudaSuccess || !repack) return (int)e2;

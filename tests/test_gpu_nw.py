@@ -57,9 +57,10 @@ def test_value_marginals_param_grads(d2p, cuda_device, B, L1, L2, gap, T, ragged
     check("nw marginals", m, r64["marginals"], r32["marginals"])
     check("nw grad_gap", gg, r64["grad_gap"], r32["grad_gap"])
     check("nw grad_T", gt, r64["grad_T"], r32["grad_T"])
-    # the float op gives the same value and marginals, bit for bit
+    # the float op (value + marginals only: the strip kernel) against the oracle too
     v2, m2 = d2p.soft_nw_float(s0.to(cuda_device), gap, T, lnd)
-    assert torch.equal(v, v2) and torch.equal(m, m2)
+    check("nw value (strip)", v2, r64["value"], r32["value"])
+    check("nw marginals (strip)", m2, r64["marginals"], r32["marginals"])
 
 
 @pytest.mark.parametrize("B,L1,L2,gap,T,ragged,seed", CASES)
@@ -157,3 +158,40 @@ def test_nw_value_is_global(d2p, cuda_device):
     ln = torch.tensor([[0, L2]], dtype=torch.int32)
     v0, m0 = d2p.soft_nw_float(s0.to(cuda_device), gap, T, ln.to(cuda_device))
     assert abs(float(v0[0]) - L2 * gap) < 1e-6 and float(m0.abs().max()) == 0.0
+
+
+# value + marginals on the column-sweep strip kernel (problems of at most 512
+# rows): full, ragged (packed several per CTA), odd widths (padded copies),
+# one row, and a cut that a single column block does not reach
+STRIP = [  # (B, L1, L2, gap, T, ragged, seed)
+    (4, 512, 512, -1.0, 1.0, False, 20),
+    (6, 512, 300, -0.5, 0.5, True, 21),
+    (3, 100, 57, -1.0, 1.0, False, 22),
+    (3, 1, 64, -1.0, 1.0, False, 23),
+    (5, 200, 8, -1.0, 0.7, True, 24),
+    (2, 128, 1000, -1.0, 1.0, False, 25),
+]
+
+
+@pytest.mark.parametrize("B,L1,L2,gap,T,ragged,seed", STRIP)
+def test_strip_kernel_nw(d2p, cuda_device, B, L1, L2, gap, T, ragged, seed):
+    """soft_nw_float on the strip kernel against the oracle, padding exactly
+    zero, and its own result: the general engine (use_engine("plane")) rounds
+    differently."""
+    s0 = scores(B, L1, L2, seed=seed)
+    ln, lnd = _lengths(B, L1, L2, ragged, seed, cuda_device)
+    v, m = d2p.soft_nw_float(s0.to(cuda_device), gap, T, lnd)
+    r64 = oracle.nw_linear(s0.numpy(), ln, gap, T, "f64")
+    r32 = oracle.nw_linear(s0.numpy(), ln, gap, T, "f32")
+    check("nw strip value", v, r64["value"], r32["value"])
+    check("nw strip marginals", m, r64["marginals"], r32["marginals"])
+    if ln is not None:
+        mc = m.cpu()
+        for b, (l1, l2) in enumerate(ln.tolist()):
+            assert torch.count_nonzero(mc[b, l1:, :]) == 0 and torch.count_nonzero(mc[b, :, l2:]) == 0
+    with d2p.use_engine("plane"):
+        ve, me = d2p.soft_nw_float(s0.to(cuda_device), gap, T, lnd)
+    full = [b for b in range(B) if ln is None or (ln[b, 0] > 1 and ln[b, 1] > 1)]
+    assert any(not torch.equal(m[b], me[b]) for b in full), "the strip kernel did not run"
+    v2, m2 = d2p.soft_nw_float(s0.to(cuda_device), gap, T, lnd)
+    assert torch.equal(v, v2) and torch.equal(m, m2)
