@@ -20,6 +20,11 @@ region.
 ranks (rank r takes the contiguous slice ``shard_bounds(B, N, r)`` of one
 globally seeded batch), timed the same way: the fixed-total-work curve.
 ``hvp`` times the Hessian-vector product over the same batch (linear family).
+``--config nw2`` / ``nwa2`` / ``dtw2`` run soft Needleman-Wunsch (linear and
+affine gaps) and soft DTW at config 2's shape (the same step through
+``soft_nw`` / ``soft_nw_affine`` / ``soft_dtw``); their reference leg is the
+reference's own CPU kernels of that family (value + marginals, whose marginals
+are the gradient of value.sum()).
 The MUFU roofline denominator is measured in the same run (``d2p_mufu_probe``,
 an ex2.approx throughput kernel).
 ``--impl reference`` times the reference's own CPU operators (oracle/_ref, built
@@ -56,6 +61,13 @@ CONFIGS = {
                dtype="bf16", desc="soft_sw_affine [64,1024,1024] bf16 -> fp32, open -2, ext -0.5, T 1"),
     "c5": dict(family="linear", B=32, L1=4096, L2=4096, gap=-1.0, T=1.0, scale=0.5, lengths=False,
                dtype="f32", desc="soft_sw [32,4096,4096] fp32 0.5*N(0,1), gap -1, T 1"),
+    # soft Needleman-Wunsch at config 2's shape (a widening of the path, not a BASELINE config)
+    "nw2": dict(family="nw", B=256, L1=512, L2=512, gap=-1.0, T=1.0, scale=1.0, lengths=False,
+                dtype="f32", desc="soft_nw [256,512,512] fp32, gap -1, T 1, no masks"),
+    "nwa2": dict(family="nw_affine", B=256, L1=512, L2=512, gap=(-2.0, -0.5), T=1.0, scale=1.0, lengths=False,
+                 dtype="f32", desc="soft_nw_affine [256,512,512] fp32, open -2, ext -0.5, T 1, no masks"),
+    "dtw2": dict(family="dtw", B=256, L1=512, L2=512, gap=None, T=1.0, scale=1.0, lengths=False,
+                 dtype="f32", desc="soft_dtw [256,512,512] fp32 N(0,1) costs, T 1, no band, no masks"),
 }
 
 # Algorithmic cost per valid cell (a fixed convention from the log-domain algorithm,
@@ -64,7 +76,9 @@ CONFIGS = {
 #     MUFU 10 (forward LSE 4 ex2 + 1 lg2, reverse 1 ex2 beta_init + 4 ex2 weights);
 #     affine: 22 MUFU.
 #   value backward kernel: read marginals 4 B + write grad 4 B.
-MUFU_PER_CELL = {"linear": 10, "affine": 22}
+#   soft NW: as linear; affine NW: 21 (three 3-way LSEs forward, nine weights reverse);
+#   soft DTW: 7 (one 3-way softmin forward, three weights reverse).
+MUFU_PER_CELL = {"linear": 10, "affine": 22, "nw": 10, "nw_affine": 21, "dtw": 7}
 MUFU_PER_SM_CLK = 16
 
 
@@ -250,15 +264,21 @@ def run_ours(args, cfg):
     len_dev = lengths.to(dev) if lengths is not None else None
     vals_all = torch.empty(world * cfg["B"], device=dev)
 
-    def fwd(scores):
+    def fwd(scores, ln):
         if fam == "linear":
-            return d2p.soft_sw(scores, gap=gap, temperature=T, lengths=len_dev)
-        return d2p.soft_sw_affine(scores, gap_open=gap[0], gap_ext=gap[1], temperature=T, lengths=len_dev)
+            return d2p.soft_sw(scores, gap=gap, temperature=T, lengths=ln)
+        if fam == "nw":
+            return d2p.soft_nw(scores, gap=gap, temperature=T, lengths=ln)
+        if fam == "nw_affine":
+            return d2p.soft_nw_affine(scores, gap_open=gap[0], gap_ext=gap[1], temperature=T, lengths=ln)
+        if fam == "dtw":
+            return d2p.soft_dtw(scores, temperature=T, lengths=ln)
+        return d2p.soft_sw_affine(scores, gap_open=gap[0], gap_ext=gap[1], temperature=T, lengths=ln)
 
     def step(scores):
-        res = fwd(scores)
-        (grad,) = torch.autograd.grad(res.value.sum(), scores)
-        v = res.value.detach()
+        res = fwd(scores, len_dev)
+        (grad,) = torch.autograd.grad(res[0].sum(), scores)
+        v = res[0].detach()
         if world > 1:  # rank r owns problems [r*B, (r+1)*B) of the global batch
             vals_all.copy_(gather_values(v, world * cfg["B"]))
         return v, grad
@@ -298,6 +318,12 @@ def run_ours(args, cfg):
             # the op the forward calls when the gap parameters and T need no gradient
             if fam == "linear":
                 return torch.ops.d2p.soft_sw_float(s_dev, gap, T, len_dev)
+            if fam == "nw":
+                return torch.ops.d2p.soft_nw_float(s_dev, gap, T, len_dev)
+            if fam == "nw_affine":
+                return torch.ops.d2p.soft_nw_affine_float(s_dev, gap[0], gap[1], T, len_dev)
+            if fam == "dtw":
+                return torch.ops.d2p.soft_dtw_float(s_dev, T, len_dev, None)
             return torch.ops.d2p.soft_sw_affine_float(s_dev, gap[0], gap[1], T, len_dev)
         for _ in range(2):
             kern()
@@ -382,12 +408,9 @@ def run_ours(args, cfg):
         vals_g = torch.empty(cfg["B"], device=dev)
 
         def strong_step():
-            if fam == "linear":
-                res = d2p.soft_sw(sh_dev, gap=gap, temperature=T, lengths=sh_len)
-            else:
-                res = d2p.soft_sw_affine(sh_dev, gap_open=gap[0], gap_ext=gap[1], temperature=T, lengths=sh_len)
-            torch.autograd.grad(res.value.sum(), sh_dev)
-            vals_g.copy_(gather_values(res.value.detach(), cfg["B"]))
+            res = fwd(sh_dev, sh_len)
+            torch.autograd.grad(res[0].sum(), sh_dev)
+            vals_g.copy_(gather_values(res[0].detach(), cfg["B"]))
 
         for _ in range(args.warmup):
             strong_step()
@@ -440,8 +463,9 @@ def run_ours(args, cfg):
     roofline = {
         "bound": bound, "achieved": round(achieved, 4), "peak": round(peak, 4), "unit": unit,
         "frac": round(achieved / peak, 4), "traffic": traffic,
-        "kernel": dom.split("(")[0].split("<")[0] + " (value+marginals: d2p_sw" +
-                  ("" if fam == "linear" else "_affine") + "_forward_backward)",
+        "kernel": dom.split("(")[0].split("<")[0] + " (value+marginals: " +
+                  {"linear": "d2p_sw", "affine": "d2p_sw_affine", "nw": "d2p_nw",
+                   "nw_affine": "d2p_nw_affine", "dtw": "d2p_dtw"}[fam] + "_forward_backward)",
         "kernel_ms": round(k_ms, 4), "time_bound_ms": round(max(t_hbm, t_mufu) * 1e3, 4),
         "hbm_gbs_achieved": round(k_bytes / k_s / 1e9, 2), "hbm_peak_gbs": hbm_gbs,
         "mufu_tops_achieved": round(k_mufu / k_s / 1e12, 3), "mufu_peak_tops": round(mufu_peak / 1e12, 3),
@@ -567,7 +591,7 @@ def _ref_cpu(cfg, steps: int, warmup: int, budget_s: float):
     torch.set_num_threads(ncores)
     s_all, ln_all = _ref_inputs(cfg)
     kind = "reference"
-    if os.path.exists(REF_OPS):
+    if os.path.exists(REF_OPS) and cfg["family"] in ("linear", "affine"):
         torch.ops.load_library(REF_OPS)
         step = lambda s, ln: _ref_fwd_bwd(cfg, s, ln)  # noqa: E731
         path = "torch.ops.d2p (reference CPU operators) + value.sum().backward()"
@@ -581,6 +605,13 @@ def _ref_cpu(cfg, steps: int, warmup: int, budget_s: float):
             lnp = None if ln is None else ln.numpy()
             if cfg["family"] == "linear":
                 return oracle.sw_linear(s.numpy(), lnp, cfg["gap"], cfg["T"], impl)
+            # NW / DTW: value + marginals; d value.sum() / d scores is the marginals
+            if cfg["family"] == "nw":
+                return oracle.nw_linear(s.numpy(), lnp, cfg["gap"], cfg["T"], impl)
+            if cfg["family"] == "nw_affine":
+                return oracle.nw_affine(s.numpy(), lnp, cfg["gap"][0], cfg["gap"][1], cfg["T"], impl)
+            if cfg["family"] == "dtw":
+                return oracle.dtw(s.numpy(), lnp, cfg["T"], -1, impl)
             return oracle.sw_affine(s.numpy(), lnp, cfg["gap"][0], cfg["gap"][1], cfg["T"], impl)
         path = f"CPU kernels ({impl}) through ctypes"
     nb = min(cfg["B"], max(1, ncores))
@@ -611,8 +642,8 @@ def _ref_cuda(cfg, budget_s: float):
     from the full batch until one step fits budget_s).  None when unavailable."""
     import torch
 
-    if not (torch.cuda.is_available() and os.path.exists(REF_CUDA_OPS)):
-        return None
+    if cfg["family"] not in ("linear", "affine") or not (torch.cuda.is_available() and os.path.exists(REF_CUDA_OPS)):
+        return None  # the operator build holds the reference's SW and affine SW CUDA operators only
     torch.ops.load_library(REF_CUDA_OPS)
     s_all, ln_all = _ref_inputs(cfg)
     dev = torch.device("cuda", 0)
