@@ -85,12 +85,28 @@ __device__ __forceinline__ bool in_band(int i, int j, int L1, int L2, int bw) {
     return fabsf((float)j - e) <= (float)bw;
 }
 
+// Rings: the last three diagonals of alpha (and the forward tangent) during
+// the forward, and of beta (and the reverse tangent) during the reverse, sit
+// in shared memory ([3][L1m + 1] floats each) when they fit, so the sweep reads
+// its neighbours at shared-memory latency; the planes in the workspace still
+// receive what the reverse reads back (weights, entropies; for the tangent
+// modes alpha and the forward tangent).  When the rings do not fit, each ring is its
+// quantity's plane.  The global loads of a diagonal (costs, direction, the
+// successors' weights) are issued one diagonal ahead, before the barrier.
+constexpr int kPF = 2;                          // cells per thread prefetched (diagonals of <= 512 cells)
+constexpr size_t kMaxRingBytes = 200 * 1024;    // dynamic shared memory cap of the rings
+__host__ __device__ inline int rings_for(int mode) { return mode == MODE_MARG ? 2 : 4; }
+__host__ __device__ inline size_t ring_bytes(int L1m, int mode) {
+    return (size_t)rings_for(mode) * 3 * ((size_t)L1m + 1) * sizeof(float);
+}
+
 // One CTA per problem.  MODE: MODE_MARG (value, marginals, dS/dT), MODE_HVP
 // (out = d marginals along p.tangent), MODE_PT (out = dP/dT; with dot_with,
 // dot_out[b] = sum dot_with * dP/dT).  p.gap2 carries nothing; the band is
 // p.parts (an int, < 0 for none).
 template <int MODE>
 __global__ void __launch_bounds__(kThreads) dtw_kernel(SwArgs p) {
+    extern __shared__ float ring_smem[];
     __shared__ double red[32];
     const int b = blockIdx.x;
     const int L1m = p.L1, L2m = p.L2;
@@ -115,43 +131,70 @@ __global__ void __launch_bounds__(kThreads) dtw_kernel(SwArgs p) {
     }
     constexpr bool TAN = MODE != MODE_MARG;
     const int K = L1 + L2;
+    const int tid = threadIdx.x;
+    // rings in shared memory (the launch gives them their bytes) or in the planes
+    const bool smR = ring_bytes(L1m, MODE) <= kMaxRingBytes;
+    const int S = L1m + 1;
+    float* const rgA = ring_smem;
+    float* const rgB = ring_smem + 3 * S;
+    float* const rgF = ring_smem + 6 * S;   // TAN only
+    float* const rgR = ring_smem + 9 * S;   // TAN only
+    auto row = [&](float* rg, int pl, int k) -> float* {
+        return smR ? rg + (k % 3) * S : C.p[pl] + (size_t)k * C.stride;
+    };
 
-    if (out) {
-        for (size_t e = threadIdx.x; e < plane; e += blockDim.x) {
-            const int i = (int)(e / L2m), j = (int)(e - (size_t)i * L2m);
-            if (i >= L1 || j >= L2) out[e] = 0.f;
-        }
+    if (out && (L1 < L1m || L2 < L2m)) {   // zeros outside the problem
+        for (int i = 0; i < L1m; ++i)
+            for (int j = (i < L1 ? L2 : 0) + (int)threadIdx.x; j < L2m; j += blockDim.x) out[(size_t)i * L2m + j] = 0.f;
     }
 
     // ------------------------------------------------------------- forward
+    // costs (and direction) of this thread's first kPF cells of diagonal k
+    float pc[kPF], pv[kPF];
+    auto fetch_fwd = [&](int k, float* c, float* v) {
+        const int i0 = max(0, k - L2), i1 = min(L1, k);
+#pragma unroll
+        for (int r = 0; r < kPF; ++r) {
+            const int i = i0 + tid + r * kThreads, j = k - i;
+            const bool ok = i <= i1 && i >= 1 && j >= 1;
+            const size_t si = ok ? (size_t)(i - 1) * L2m + (j - 1) : 0;
+            c[r] = ok ? __ldg(Cst + si) : 0.f;
+            if (MODE == MODE_HVP) v[r] = ok ? __ldg(V + si) : 0.f;
+        }
+    };
+    fetch_fwd(0, pc, pv);
     float O1 = 0.f, O2 = 0.f, D1 = 0.f, D2 = 0.f;
     for (int k = 0; k <= K; ++k) {
+        float* const a0 = row(rgA, kA, k);
+        const float* const a1 = row(rgA, kA, max(k - 1, 0));
+        const float* const a2 = row(rgA, kA, max(k - 2, 0));
+        float* const f0 = TAN ? row(rgF, kF, k) : nullptr;
+        const float* const f1 = TAN ? row(rgF, kF, max(k - 1, 0)) : nullptr;
+        const float* const f2 = TAN ? row(rgF, kF, max(k - 2, 0)) : nullptr;
         float Ok = O1, Dk = D1;
         if (k >= 2) {   // the previous diagonal's cell nearest the band's centre line
             const int lo = max(0, k - 1 - L2), hi = min(L1, k - 1);
             int im = K > 0 ? (int)(((long long)(k - 1) * L1 + K / 2) / K) : 0;
             im = min(max(im, lo), hi);
-            const float a = C.at(kA, k - 1, im);
+            const float a = a1[im];
             if (a < kFin) {
                 Ok = O1 + rintf(a);
-                if (TAN) Dk = D1 + rintf(C.at(kF, k - 1, im));
+                if (TAN) Dk = D1 + rintf(f1[im]);
             }
         }
-        if (threadIdx.x == 0) {
+        if (tid == 0) {
             C.O[k] = Ok;
             C.D[k] = Dk;
         }
         const float dO1 = O1 - Ok, dO2 = O2 - Ok, dD1 = D1 - Dk, dD2 = D2 - Dk;   // exact
         const int i0 = max(0, k - L2), i1 = min(L1, k);
-        for (int i = i0 + threadIdx.x; i <= i1; i += blockDim.x) {
+        auto cell = [&](int i, float cst, float vv) {
             const int j = k - i;
             float a = kPInf, wd = 0.f, wu = 0.f, wl = 0.f, h = 0.f, f = 0.f;
             if (k == 0) {
                 a = 0.f;
             } else if (i >= 1 && j >= 1 && in_band(i, j, L1, L2, bw)) {
-                const size_t si = (size_t)(i - 1) * L2m + (j - 1);
-                const float vd = C.at(kA, k - 2, i - 1) + dO2, vu = C.at(kA, k - 1, i - 1) + dO1,
-                            vl = C.at(kA, k - 1, i) + dO1;
+                const float vd = a2[i - 1] + dO2, vu = a1[i - 1] + dO1, vl = a1[i] + dO1;
                 const float m = fminf(vd, fminf(vu, vl));
                 if (m < kFin) {
                     const float ed = expf((m - vd) * iT), eu = expf((m - vu) * iT), el = expf((m - vl) * iT);
@@ -161,65 +204,154 @@ __global__ void __launch_bounds__(kThreads) dtw_kernel(SwArgs p) {
                     wd = ed * is;
                     wu = eu * is;
                     wl = el * is;
-                    a = Cst[si] + fmaf(-T, ls, m);
+                    a = cst + fmaf(-T, ls, m);
                     // the choice's entropy -sum w ln w = ln(sum) + sum w (v - m) / T
                     h = ls + iT * fmaf(wd, vd - m, fmaf(wu, vu - m, wl * (vl - m)));
                     if (TAN) {
-                        f = fmaf(wd, C.at(kF, k - 2, i - 1) + dD2,
-                                 fmaf(wu, C.at(kF, k - 1, i - 1) + dD1, wl * (C.at(kF, k - 1, i) + dD1)));
-                        if (MODE == MODE_HVP) f += V[si];
+                        f = fmaf(wd, f2[i - 1] + dD2, fmaf(wu, f1[i - 1] + dD1, wl * (f1[i] + dD1)));
+                        if (MODE == MODE_HVP) f += vv;
                         if (MODE == MODE_PT) f -= h;
                     }
                 }
             }
-            C.at(kA, k, i) = a < kFin ? a : kPInf;
+            const float as = a < kFin ? a : kPInf;
+            a0[i] = as;
+            if (smR && TAN) C.at(kA, k, i) = as;   // the tangent reverses read alpha back
             C.at(kWd, k, i) = wd;
             C.at(kWu, k, i) = wu;
             C.at(kWl, k, i) = wl;
             C.at(kH, k, i) = h;
-            if (TAN) C.at(kF, k, i) = f;
+            if (TAN) {
+                f0[i] = f;
+                if (smR) C.at(kF, k, i) = f;
+            }
+        };
+#pragma unroll
+        for (int r = 0; r < kPF; ++r) {
+            const int i = i0 + tid + r * kThreads;
+            if (i <= i1) cell(i, pc[r], pv[r]);
         }
-        __syncthreads();
+        for (int i = i0 + tid + kPF * kThreads; i <= i1; i += kThreads) {
+            const int j = k - i;
+            const bool ok = i >= 1 && j >= 1;
+            const size_t si = ok ? (size_t)(i - 1) * L2m + (j - 1) : 0;
+            cell(i, ok ? __ldg(Cst + si) : 0.f, MODE == MODE_HVP && ok ? __ldg(V + si) : 0.f);
+        }
+        if (k < K) {
+            float nc[kPF], nv[kPF];
+            fetch_fwd(k + 1, nc, nv);
+            __syncthreads();
+#pragma unroll
+            for (int r = 0; r < kPF; ++r) {
+                pc[r] = nc[r];
+                pv[r] = nv[r];
+            }
+        } else {
+            __syncthreads();
+        }
         O2 = O1;
         O1 = Ok;
         D2 = D1;
         D1 = Dk;
     }
+    const float aE = row(rgA, kA, K)[L1];   // read before any reverse write (separate rings)
 
     // ------------------------------------------------------------- reverse
+    // this thread's first kPF cells of diagonal k: entropy and the three
+    // weights its successors give it (MODE_MARG)
+    float ph[kPF], pd[kPF], pu[kPF], pl[kPF];
+    auto fetch_rev = [&](int k, float* h, float* wd, float* wu, float* wl) {
+        const int i0 = max(0, k - L2), i1 = min(L1, k);
+#pragma unroll
+        for (int r = 0; r < kPF; ++r) {
+            const int i = i0 + tid + r * kThreads, j = k - i;
+            const bool ok = i <= i1;
+            h[r] = ok && i >= 1 && j >= 1 ? C.at(kH, k, i) : 0.f;
+            wd[r] = ok && i + 1 <= L1 && j + 1 <= L2 ? C.at(kWd, k + 2, i + 1) : 0.f;
+            wu[r] = ok && i + 1 <= L1 && j >= 1 ? C.at(kWu, k + 1, i + 1) : 0.f;
+            wl[r] = ok && j + 1 <= L2 && i >= 1 ? C.at(kWl, k + 1, i) : 0.f;
+        }
+    };
+    if (MODE == MODE_MARG) fetch_rev(K, ph, pd, pu, pl);
     double sent = 0.0, sdot = 0.0;
     for (int k = K; k >= 0; --k) {
         const float Ok = C.O[k], Dk = C.D[k];
         const float Ok1 = k + 1 <= K ? C.O[k + 1] : 0.f, Ok2 = k + 2 <= K ? C.O[k + 2] : 0.f;
         const float Dk1 = k + 1 <= K ? C.D[k + 1] : 0.f, Dk2 = k + 2 <= K ? C.D[k + 2] : 0.f;
+        float* const b0 = row(rgB, kB, k);
+        const float* const b1 = row(rgB, kB, min(k + 1, K));
+        const float* const b2 = row(rgB, kB, min(k + 2, K));
+        float* const r0 = TAN ? row(rgR, kR, k) : nullptr;
+        const float* const r1 = TAN ? row(rgR, kR, min(k + 1, K)) : nullptr;
+        const float* const r2 = TAN ? row(rgR, kR, min(k + 2, K)) : nullptr;
         const int i0 = max(0, k - L2), i1 = min(L1, k);
-        for (int i = i0 + threadIdx.x; i <= i1; i += blockDim.x) {
+        if (MODE == MODE_MARG) {
+            // An unreached cell gets weight 0 from each successor, so its flow
+            // is 0 without a test; the end cell keeps its 1, as in the reference.
+            auto cell = [&](int i, float h, float wd, float wu, float wl) {
+                const int j = k - i;
+                float be = k == K ? 1.f : 0.f;
+                if (i + 1 <= L1 && j + 1 <= L2) be = fmaf(b2[i + 1], wd, be);
+                if (i + 1 <= L1 && j >= 1) be = fmaf(b1[i + 1], wu, be);
+                if (j + 1 <= L2 && i >= 1) be = fmaf(b1[i], wl, be);
+                b0[i] = be;
+                if (i >= 1 && j >= 1) {
+                    if (out) out[(size_t)(i - 1) * L2m + (j - 1)] = be;
+                    sent += (double)be * (double)h;
+                }
+            };
+#pragma unroll
+            for (int r = 0; r < kPF; ++r) {
+                const int i = i0 + tid + r * kThreads;
+                if (i <= i1) cell(i, ph[r], pd[r], pu[r], pl[r]);
+            }
+            for (int i = i0 + tid + kPF * kThreads; i <= i1; i += kThreads) {
+                const int j = k - i;
+                cell(i, i >= 1 && j >= 1 ? C.at(kH, k, i) : 0.f,
+                     i + 1 <= L1 && j + 1 <= L2 ? C.at(kWd, k + 2, i + 1) : 0.f,
+                     i + 1 <= L1 && j >= 1 ? C.at(kWu, k + 1, i + 1) : 0.f,
+                     j + 1 <= L2 && i >= 1 ? C.at(kWl, k + 1, i) : 0.f);
+            }
+            if (k > 0) {
+                float nh[kPF], nd[kPF], nu[kPF], nl[kPF];
+                fetch_rev(k - 1, nh, nd, nu, nl);
+                __syncthreads();
+#pragma unroll
+                for (int r = 0; r < kPF; ++r) {
+                    ph[r] = nh[r];
+                    pd[r] = nd[r];
+                    pu[r] = nu[r];
+                    pl[r] = nl[r];
+                }
+            } else {
+                __syncthreads();
+            }
+        } else {
+        for (int i = i0 + tid; i <= i1; i += blockDim.x) {
             const int j = k - i;
             float be = k == K ? 1.f : 0.f, tb = 0.f;
-            const float tc = TAN ? C.at(kF, k, i) : 0.f;
+            const float tc = C.at(kF, k, i);
             const float ac = C.at(kA, k, i);
             // successor d of this cell by its option with weight plane pw;
             // dO, dD: the successor's frames minus this cell's (exact)
             auto take = [&](int kd, int id, int pw, float dO, float dD) {
-                const float bd = C.at(kB, kd, id);
+                const float bd = (kd == k + 1 ? b1 : b2)[id];
                 const float w = C.at(pw, kd, id);
                 be = fmaf(bd, w, be);
-                if (TAN) {
-                    const size_t sd = (size_t)(id - 1) * L2m + (kd - id - 1);
-                    // E_d - t_c: the successor's options' mean tangent minus this cell's
-                    float g = C.at(kF, kd, id) - tc + dD;
-                    if (MODE == MODE_HVP) g -= V[sd];
-                    float dw;
-                    if (MODE == MODE_PT) {
-                        const float hd = C.at(kH, kd, id);
-                        // a_c - E[a](d) = a_c - (alpha_d - c_d) - T h_d
-                        const float da = (ac - C.at(kA, kd, id)) + (Cst[sd] - dO) - T * hd;
-                        dw = w * fmaf(g + hd, iT, da * iT * iT);
-                    } else {
-                        dw = w * g * iT;
-                    }
-                    tb = fmaf(C.at(kR, kd, id), w, fmaf(bd, dw, tb));
+                const size_t sd = (size_t)(id - 1) * L2m + (kd - id - 1);
+                // E_d - t_c: the successor's options' mean tangent minus this cell's
+                float g = C.at(kF, kd, id) - tc + dD;
+                if (MODE == MODE_HVP) g -= V[sd];
+                float dw;
+                if (MODE == MODE_PT) {
+                    const float hd = C.at(kH, kd, id);
+                    // a_c - E[a](d) = a_c - (alpha_d - c_d) - T h_d
+                    const float da = (ac - C.at(kA, kd, id)) + (Cst[sd] - dO) - T * hd;
+                    dw = w * fmaf(g + hd, iT, da * iT * iT);
+                } else {
+                    dw = w * g * iT;
                 }
+                tb = fmaf((kd == k + 1 ? r1 : r2)[id], w, fmaf(bd, dw, tb));
             };
             // an unreached cell takes no flow (its successors give it weight 0);
             // the end cell keeps its 1 even when unreached, as in the reference
@@ -228,32 +360,27 @@ __global__ void __launch_bounds__(kThreads) dtw_kernel(SwArgs p) {
                 if (i + 1 <= L1 && j >= 1) take(k + 1, i + 1, kWu, Ok1 - Ok, Dk1 - Dk);
                 if (j + 1 <= L2 && i >= 1) take(k + 1, i, kWl, Ok1 - Ok, Dk1 - Dk);
             }
-            C.at(kB, k, i) = be;
-            if (TAN) C.at(kR, k, i) = tb;
+            b0[i] = be;
+            r0[i] = tb;
             if (i >= 1 && j >= 1) {
                 const size_t si = (size_t)(i - 1) * L2m + (j - 1);
-                if (MODE == MODE_MARG) {
-                    if (out) out[si] = be;
-                    sent += (double)be * (double)C.at(kH, k, i);
-                } else {
-                    if (out) out[si] = tb;
-                    if (Gw) sdot += (double)Gw[si] * (double)tb;
-                }
+                if (out) out[si] = tb;
+                if (Gw) sdot += (double)Gw[si] * (double)tb;
             }
         }
         __syncthreads();
+        }
     }
 
     if (MODE == MODE_MARG) {
         const double th = block_sum(sent, red);
-        if (threadIdx.x == 0) {
-            const float aE = C.at(kA, K, L1);
+        if (tid == 0) {
             if (p.value) p.value[b] = aE < kFin ? (float)((double)aE + (double)C.O[K]) : kPInf;
             if (p.grad_T) p.grad_T[b] = (float)(-th);
         }
     } else if (p.dot_out) {
         const double t = block_sum(sdot, red);
-        if (threadIdx.x == 0) p.dot_out[b] = (float)t;
+        if (tid == 0) p.dot_out[b] = (float)t;
     }
 }
 
@@ -269,10 +396,26 @@ size_t dtw_workspace_bytes(int op, int B, int L1, int L2) {
 
 static int launch_dtw(const SwArgs& a, cudaStream_t st) {
     if (a.B == 0) return 0;
+    static DeviceSetup setup;
+    int dev = 0, sms = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return (int)e;
+    int rc = device_setup(setup, dev, [] {
+        const int cap = (int)dtw::kMaxRingBytes;
+        cudaError_t r = cudaFuncSetAttribute(dtw::dtw_kernel<MODE_MARG>, cudaFuncAttributeMaxDynamicSharedMemorySize, cap);
+        if (r == cudaSuccess)
+            r = cudaFuncSetAttribute(dtw::dtw_kernel<MODE_HVP>, cudaFuncAttributeMaxDynamicSharedMemorySize, cap);
+        if (r == cudaSuccess)
+            r = cudaFuncSetAttribute(dtw::dtw_kernel<MODE_PT>, cudaFuncAttributeMaxDynamicSharedMemorySize, cap);
+        return (int)r;
+    }, &sms);
+    if (rc) return rc;
+    const size_t rb = dtw::ring_bytes(a.L1, a.mode);
+    const size_t smem = rb <= dtw::kMaxRingBytes ? rb : 0;   // else the rings are the planes
     switch (a.mode) {
-        case MODE_MARG: dtw::dtw_kernel<MODE_MARG><<<a.B, dtw::kThreads, 0, st>>>(a); break;
-        case MODE_HVP: dtw::dtw_kernel<MODE_HVP><<<a.B, dtw::kThreads, 0, st>>>(a); break;
-        case MODE_PT: dtw::dtw_kernel<MODE_PT><<<a.B, dtw::kThreads, 0, st>>>(a); break;
+        case MODE_MARG: dtw::dtw_kernel<MODE_MARG><<<a.B, dtw::kThreads, smem, st>>>(a); break;
+        case MODE_HVP: dtw::dtw_kernel<MODE_HVP><<<a.B, dtw::kThreads, smem, st>>>(a); break;
+        case MODE_PT: dtw::dtw_kernel<MODE_PT><<<a.B, dtw::kThreads, smem, st>>>(a); break;
         default: return kErrInvalid;
     }
     return (int)cudaGetLastError();

@@ -90,6 +90,21 @@ __device__ __forceinline__ double block_sum(double v, double* red) {
     return t;   // valid in thread 0
 }
 
+// Rings: the last three diagonals of alpha (and the forward tangent) during
+// the forward, and of beta (and the reverse tangent) during the reverse, sit
+// in shared memory ([3][L1m + 1] floats each) when they fit, so the sweep reads
+// its neighbours at shared-memory latency; the planes still receive what the
+// reverse reads back (weights and entropies; the forward tangent; alpha and
+// E[v] for MODE_PT).  When the rings do not fit, each ring is its quantity's
+// plane.  The scores (and direction) of a diagonal are loaded one diagonal
+// ahead, before the barrier.
+constexpr int kPF = 2;                          // cells per thread prefetched (diagonals of <= 512 cells)
+constexpr size_t kMaxRingBytes = 200 * 1024;    // dynamic shared memory cap of the rings
+__host__ __device__ inline int rings_for(int mode) { return mode == MODE_MARG ? 2 : 4; }
+__host__ __device__ inline size_t ring_bytes(int L1m, int mode) {
+    return (size_t)rings_for(mode) * 3 * ((size_t)L1m + 1) * sizeof(float);
+}
+
 // One CTA per problem.  MODE: MODE_MARG (value, marginals, dS/dgap, dS/dT),
 // MODE_HVP (out = d marginals along p.tangent), MODE_PGAP / MODE_PT (out =
 // dP/dtheta; with dot_with, dot_out[b] = sum dot_with * dP/dtheta).
@@ -103,6 +118,7 @@ __device__ __forceinline__ double block_sum(double v, double* red) {
 // the same way.
 template <int MODE>
 __global__ void __launch_bounds__(kThreads) nw_kernel(SwArgs p) {
+    extern __shared__ float ring_smem[];
     __shared__ double red[32];
     const int b = blockIdx.x;
     if (p.only && !p.only[b]) return;   // a fix-up launch: only the problems the strip kernel flagged
@@ -130,49 +146,79 @@ __global__ void __launch_bounds__(kThreads) nw_kernel(SwArgs p) {
     // the forward tangent (dalpha, or U) and the reverse tangent (dbeta, or W)
     const int kF = kT1, kR = kT2, kEv = kT3;
     const int K = L1 + L2;   // the end cell's diagonal
+    const int tid = threadIdx.x;
+    const bool smR = ring_bytes(L1m, MODE) <= kMaxRingBytes;
+    const int RS = L1m + 1;
+    // row of diagonal k of ring rg (alpha 0, beta 1, forward tangent 2,
+    // reverse tangent 3), or of its plane pl when the rings are the planes
+    auto row = [&](int rg, int pl, int k) -> float* {
+        return smR ? ring_smem + (size_t)(3 * rg + k % 3) * RS : C.p[pl] + (size_t)k * C.stride;
+    };
 
     // padding of the output: zeros outside the problem
-    if (out) {
-        for (size_t e = threadIdx.x; e < plane; e += blockDim.x) {
-            const int i = (int)(e / L2m), j = (int)(e - (size_t)i * L2m);
-            if (i >= L1 || j >= L2) out[e] = 0.f;
-        }
+    if (out && (L1 < L1m || L2 < L2m)) {   // zeros outside the problem
+        for (int i = 0; i < L1m; ++i)
+            for (int j = (i < L1 ? L2 : 0) + (int)threadIdx.x; j < L2m; j += blockDim.x) out[(size_t)i * L2m + j] = 0.f;
     }
 
     // ------------------------------------------------------------- forward
+    float pc[kPF], pv[kPF];   // scores (and direction) of this thread's first kPF cells of a diagonal
+    auto fetch_fwd = [&](int k, float* c, float* v) {
+        const int i0 = max(0, k - L2), i1 = min(L1, k);
+#pragma unroll
+        for (int r = 0; r < kPF; ++r) {
+            const int i = i0 + tid + r * kThreads, j = k - i;
+            const bool ok = i <= i1 && i >= 1 && j >= 1;
+            const size_t si = ok ? (size_t)(i - 1) * L2m + (j - 1) : 0;
+            c[r] = ok ? __ldg(S + si) : 0.f;
+            if (MODE == MODE_HVP) v[r] = ok ? __ldg(V + si) : 0.f;
+        }
+    };
+    fetch_fwd(0, pc, pv);
     float O1 = 0.f, O2 = 0.f, D1 = 0.f, D2 = 0.f;   // frames of diagonals k-1, k-2
     for (int k = 0; k <= K; ++k) {
+        float* const a0 = row(0, kA, k);
+        const float* const a1 = row(0, kA, max(k - 1, 0));
+        const float* const a2 = row(0, kA, max(k - 2, 0));
+        float* const f0 = TAN ? row(2, kF, k) : nullptr;
+        const float* const f1 = TAN ? row(2, kF, max(k - 1, 0)) : nullptr;
+        const float* const f2 = TAN ? row(2, kF, max(k - 2, 0)) : nullptr;
         float Ok = 0.f, Dk = 0.f;
         if (k >= 2) {   // from the previous diagonal's middle cell (the same value in every thread)
             const int im = (max(0, k - 1 - L2) + min(L1, k - 1)) >> 1;
-            Ok = O1 + rintf(C.at(kA, k - 1, im));
-            if (TAN) Dk = D1 + rintf(C.at(kF, k - 1, im));
+            Ok = O1 + rintf(a1[im]);
+            if (TAN) Dk = D1 + rintf(f1[im]);
         }
-        if (threadIdx.x == 0) {
+        if (tid == 0) {
             C.O[k] = Ok;
             C.D[k] = Dk;
         }
         const float dO1 = O1 - Ok, dO2 = O2 - Ok, dD1 = D1 - Dk, dD2 = D2 - Dk;   // exact
-        const int i0 = max(0, k - L2), i1 = min(L1, k);
-        for (int i = i0 + threadIdx.x; i <= i1; i += blockDim.x) {
+        auto putA = [&](int i, float v) {
+            a0[i] = v;
+            if (smR && MODE == MODE_PT) C.at(kA, k, i) = v;
+        };
+        auto putF = [&](int i, float v) {
+            f0[i] = v;
+            if (smR) C.at(kF, k, i) = v;
+        };
+        auto cell = [&](int i, float sc, float vv) {
             const int j = k - i;
             if (i == 0 || j == 0) {   // boundary: alpha = k gap; the gap tangent is k
-                C.at(kA, k, i) = fmaf((float)k, gap, -Ok);
-                if (TAN) C.at(kF, k, i) = (MODE == MODE_PGAP ? (float)k : 0.f) - Dk;
-                continue;
+                putA(i, fmaf((float)k, gap, -Ok));
+                if (TAN) putF(i, (MODE == MODE_PGAP ? (float)k : 0.f) - Dk);
+                return;
             }
-            const size_t si = (size_t)(i - 1) * L2m + (j - 1);
-            const float sc = S[si];
-            const float vd = C.at(kA, k - 2, i - 1) + (sc + dO2);
-            const float vu = C.at(kA, k - 1, i - 1) + (gap + dO1);
-            const float vl = C.at(kA, k - 1, i) + (gap + dO1);
+            const float vd = a2[i - 1] + (sc + dO2);
+            const float vu = a1[i - 1] + (gap + dO1);
+            const float vl = a1[i] + (gap + dO1);
             const float m = fmaxf(vd, fmaxf(vu, vl));
             const float ed = expf((vd - m) * iT), eu = expf((vu - m) * iT), el = expf((vl - m) * iT);
             const float sum = (ed + eu) + el;
             const float a = fmaf(T, logf(sum), m);
             const float is = 1.f / sum;
             const float wd = ed * is, wu = eu * is, wl = el * is;
-            C.at(kA, k, i) = a;
+            putA(i, a);
             C.at(kWd, k, i) = wd;
             C.at(kWu, k, i) = wu;
             C.at(kWl, k, i) = wl;
@@ -183,9 +229,8 @@ __global__ void __launch_bounds__(kThreads) nw_kernel(SwArgs p) {
             }
             if (TAN) {
                 // tangents of the three options, in this diagonal's frame
-                float td = C.at(kF, k - 2, i - 1) + dD2, tu = C.at(kF, k - 1, i - 1) + dD1,
-                      tl = C.at(kF, k - 1, i) + dD1;
-                if (MODE == MODE_HVP) td += V[si];
+                float td = f2[i - 1] + dD2, tu = f1[i - 1] + dD1, tl = f1[i] + dD1;
+                if (MODE == MODE_HVP) td += vv;
                 if (MODE == MODE_PGAP) {
                     tu += 1.f;
                     tl += 1.f;
@@ -196,15 +241,39 @@ __global__ void __launch_bounds__(kThreads) nw_kernel(SwArgs p) {
                     C.at(kEv, k, i) = ev;
                     f = fmaf(a - ev, iT, f);
                 }
-                C.at(kF, k, i) = f;
+                putF(i, f);
             }
+        };
+        const int i0 = max(0, k - L2), i1 = min(L1, k);
+#pragma unroll
+        for (int r = 0; r < kPF; ++r) {
+            const int i = i0 + tid + r * kThreads;
+            if (i <= i1) cell(i, pc[r], pv[r]);
         }
-        __syncthreads();
+        for (int i = i0 + tid + kPF * kThreads; i <= i1; i += kThreads) {
+            const int j = k - i;
+            const bool ok = i >= 1 && j >= 1;
+            const size_t si = ok ? (size_t)(i - 1) * L2m + (j - 1) : 0;
+            cell(i, ok ? __ldg(S + si) : 0.f, MODE == MODE_HVP && ok ? __ldg(V + si) : 0.f);
+        }
+        if (k < K) {
+            float nc[kPF], nv[kPF];
+            fetch_fwd(k + 1, nc, nv);
+            __syncthreads();
+#pragma unroll
+            for (int r = 0; r < kPF; ++r) {
+                pc[r] = nc[r];
+                pv[r] = nv[r];
+            }
+        } else {
+            __syncthreads();
+        }
         O2 = O1;
         O1 = Ok;
         D2 = D1;
         D1 = Dk;
     }
+    const float aEnd = row(0, kA, K)[L1];   // read before any reverse write (separate rings)
 
     // ------------------------------------------------------------- reverse
     double sgap = 0.0, sent = 0.0, sdot = 0.0;
@@ -213,13 +282,19 @@ __global__ void __launch_bounds__(kThreads) nw_kernel(SwArgs p) {
         const float Ok1 = k + 1 <= K ? C.O[k + 1] : 0.f, Ok2 = k + 2 <= K ? C.O[k + 2] : 0.f;
         const float Dk1 = k + 1 <= K ? C.D[k + 1] : 0.f, Dk2 = k + 2 <= K ? C.D[k + 2] : 0.f;
         const float Om2 = k >= 2 ? C.O[k - 2] : 0.f, Dm2 = k >= 2 ? C.D[k - 2] : 0.f;
+        float* const b0 = row(1, kB, k);
+        const float* const b1 = row(1, kB, min(k + 1, K));
+        const float* const b2 = row(1, kB, min(k + 2, K));
+        float* const r0 = TAN ? row(3, kR, k) : nullptr;
+        const float* const r1 = TAN ? row(3, kR, min(k + 1, K)) : nullptr;
+        const float* const r2 = TAN ? row(3, kR, min(k + 2, K)) : nullptr;
         const int i0 = max(0, k - L2), i1 = min(L1, k);
-        for (int i = i0 + threadIdx.x; i <= i1; i += blockDim.x) {
+        for (int i = i0 + tid; i <= i1; i += blockDim.x) {
             const int j = k - i;
             const bool interior = i >= 1 && j >= 1;
             float be = 0.f, tb = 0.f;
             const float fc = TAN ? C.at(kF, k, i) : 0.f;
-            const float ac = C.at(kA, k, i);
+            const float ac = MODE == MODE_PT ? C.at(kA, k, i) : 0.f;
             if (k == K) {
                 be = 1.f;   // the end cell (L1, L2); its tangent is 0
             } else {
@@ -227,7 +302,7 @@ __global__ void __launch_bounds__(kThreads) nw_kernel(SwArgs p) {
                 // its up option (if j >= 1), (i, j+1) by its left option (if i >= 1)
                 auto take = [&](int kd, int id, int opt, int si_d, float dO, float dD) {
                     // dO, dD: this cell's frames minus the successor's (exact)
-                    const float bd = C.at(kB, kd, id);
+                    const float bd = (kd == k + 1 ? b1 : b2)[id];
                     const float w = C.at(opt, kd, id);
                     be = fmaf(bd, w, be);
                     if (TAN) {
@@ -243,15 +318,15 @@ __global__ void __launch_bounds__(kThreads) nw_kernel(SwArgs p) {
                             const float v = ac + ((opt == kWd ? S[si_d] : gap) + dO);
                             dw = fmaf(w * (C.at(kEv, kd, id) - v), iT * iT, dw);
                         }
-                        tb = fmaf(C.at(kR, kd, id), w, fmaf(bd, dw, tb));
+                        tb = fmaf((kd == k + 1 ? r1 : r2)[id], w, fmaf(bd, dw, tb));
                     }
                 };
                 if (i + 1 <= L1 && j + 1 <= L2) take(k + 2, i + 1, kWd, i * L2m + j, Ok - Ok2, Dk - Dk2);
                 if (i + 1 <= L1 && j >= 1) take(k + 1, i + 1, kWu, 0, Ok - Ok1, Dk - Dk1);
                 if (j + 1 <= L2 && i >= 1) take(k + 1, i, kWl, 0, Ok - Ok1, Dk - Dk1);
             }
-            C.at(kB, k, i) = be;
-            if (TAN) C.at(kR, k, i) = tb;
+            b0[i] = be;
+            if (TAN) r0[i] = tb;
             if (MODE == MODE_MARG && !interior) sgap += (double)be * (double)k;   // a path ending at (i, 0) or (0, j) takes k more gaps
             if (interior) {
                 const size_t si = (size_t)(i - 1) * L2m + (j - 1);
@@ -290,7 +365,7 @@ __global__ void __launch_bounds__(kThreads) nw_kernel(SwArgs p) {
         const double tgap = block_sum(sgap, red);
         const double tent = block_sum(sent, red);
         if (threadIdx.x == 0) {
-            const double Sv = (double)C.at(kA, K, L1) + (double)C.O[K];
+            const double Sv = (double)aEnd + (double)C.O[K];
             if (p.value) p.value[b] = (float)Sv;
             if (p.grad_gap) p.grad_gap[b] = (float)tgap;
             if (p.grad_T) p.grad_T[b] = (float)tent;
@@ -324,11 +399,27 @@ size_t nw_workspace_bytes(int op, int B, int L1, int L2) {
 
 int launch_nw(const SwArgs& a, cudaStream_t st) {
     if (a.B == 0) return 0;
+    static DeviceSetup setup;
+    int dev = 0, sms = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return (int)e;
+    int rc = device_setup(setup, dev, [] {
+        const int cap = (int)nw::kMaxRingBytes;
+        const void* ks[] = {(const void*)nw::nw_kernel<MODE_MARG>, (const void*)nw::nw_kernel<MODE_HVP>,
+                            (const void*)nw::nw_kernel<MODE_PGAP>, (const void*)nw::nw_kernel<MODE_PT>};
+        cudaError_t r = cudaSuccess;
+        for (const void* k : ks)
+            if (r == cudaSuccess) r = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, cap);
+        return (int)r;
+    }, &sms);
+    if (rc) return rc;
+    const size_t rb = nw::ring_bytes(a.L1, a.mode);
+    const size_t smem = rb <= nw::kMaxRingBytes ? rb : 0;   // else the rings are the planes
     switch (a.mode) {
-        case MODE_MARG: nw::nw_kernel<MODE_MARG><<<a.B, nw::kThreads, 0, st>>>(a); break;
-        case MODE_HVP: nw::nw_kernel<MODE_HVP><<<a.B, nw::kThreads, 0, st>>>(a); break;
-        case MODE_PGAP: nw::nw_kernel<MODE_PGAP><<<a.B, nw::kThreads, 0, st>>>(a); break;
-        case MODE_PT: nw::nw_kernel<MODE_PT><<<a.B, nw::kThreads, 0, st>>>(a); break;
+        case MODE_MARG: nw::nw_kernel<MODE_MARG><<<a.B, nw::kThreads, smem, st>>>(a); break;
+        case MODE_HVP: nw::nw_kernel<MODE_HVP><<<a.B, nw::kThreads, smem, st>>>(a); break;
+        case MODE_PGAP: nw::nw_kernel<MODE_PGAP><<<a.B, nw::kThreads, smem, st>>>(a); break;
+        case MODE_PT: nw::nw_kernel<MODE_PT><<<a.B, nw::kThreads, smem, st>>>(a); break;
         default: return kErrInvalid;
     }
     return (int)cudaGetLastError();

@@ -108,12 +108,39 @@ __device__ __forceinline__ float lse3w(float v1, float v2, float v3, float T, fl
     return fmaf(T, ls, m);
 }
 
+// Rings: the last three diagonals of the three alphas (and forward tangents)
+// during the forward, and of the three betas (and reverse tangents) during the
+// reverse, sit in shared memory ([3][L1m + 1] floats each) when they fit, so
+// the sweep reads its neighbours at shared-memory latency; the planes in the
+// workspace still receive what the reverse reads back (the weights; for the
+// tangent modes the alphas and the forward tangents).  When the rings do not
+// fit, each ring is its quantity's plane.  The scores (and direction) of a
+// diagonal, and in MODE_MARG the weights its reverse reads, are loaded one
+// diagonal ahead, before the barrier.
+constexpr int kPF = 2;                          // forward: cells per thread prefetched (diagonals of <= 512 cells)
+constexpr int kPFR = 2;                         // reverse (18 weights a cell): diagonals of <= 512 cells
+constexpr size_t kMaxRingBytes = 200 * 1024;    // dynamic shared memory cap of the rings
+__host__ __device__ inline int rings_for(int mode) { return mode == MODE_MARG ? 6 : 12; }
+__host__ __device__ inline size_t ring_bytes(int L1m, int mode) {
+    return (size_t)rings_for(mode) * 3 * ((size_t)L1m + 1) * sizeof(float);
+}
+// ring ids: alphas 0..2, betas 3..5, forward tangents 6..8, reverse tangents 9..11
+enum Ring : int { rAM = 0, rBM = 3, rFM = 6, rRM = 9 };
+
+// the weights one cell's reverse reads (MODE_MARG): those its successors give
+// its states (M at (i+1, j+1), I at (i+1, j), D at (i, j+1)) and its own
+struct RevIn {
+    float sm[3], si[3], sd[3];
+    float om[3], oi[3], od[3];
+};
+
 // One CTA per problem.  MODE: MODE_MARG (value, marginals, the three
 // parameter gradients), MODE_HVP (out = d marginals along p.tangent),
 // MODE_PGAP / MODE_PGE / MODE_PT (out = dP/d(open, ext, T); with dot_with,
 // dot_out[b] = sum dot_with * dP).
 template <int MODE>
 __global__ void __launch_bounds__(kThreads) nwa_kernel(SwArgs p) {
+    extern __shared__ float ring_smem[];
     __shared__ double red[32];
     const int b = blockIdx.x;
     const int L1m = p.L1, L2m = p.L2;
@@ -142,67 +169,114 @@ __global__ void __launch_bounds__(kThreads) nwa_kernel(SwArgs p) {
     constexpr float xI1 = MODE == MODE_PGAP ? 1.f : 0.f, xI2 = MODE == MODE_PGE ? 1.f : 0.f, xI3 = xI1;
     constexpr float xD1 = xI1, xD2 = xI1, xD3 = xI2;
     const int K = L1 + L2;
+    const int tid = threadIdx.x;
+    const bool smR = ring_bytes(L1m, MODE) <= kMaxRingBytes;
+    const int RS = L1m + 1;
+    // row of diagonal k of ring rg (its plane pl when the rings are the planes)
+    auto row = [&](int rg, int pl, int k) -> float* {
+        return smR ? ring_smem + (size_t)(3 * rg + k % 3) * RS : C.p[pl] + (size_t)k * C.stride;
+    };
 
-    if (out) {   // zeros outside the problem
-        for (size_t e = threadIdx.x; e < plane; e += blockDim.x) {
-            const int i = (int)(e / L2m), j = (int)(e - (size_t)i * L2m);
-            if (i >= L1 || j >= L2) out[e] = 0.f;
-        }
+    if (out && (L1 < L1m || L2 < L2m)) {   // zeros outside the problem
+        for (int i = 0; i < L1m; ++i)
+            for (int j = (i < L1 ? L2 : 0) + (int)threadIdx.x; j < L2m; j += blockDim.x) out[(size_t)i * L2m + j] = 0.f;
     }
 
     // ------------------------------------------------------------- forward
+    float pc[kPF], pv[kPF];   // scores (and direction) of this thread's first kPF cells of a diagonal
+    auto fetch_fwd = [&](int k, float* c, float* v) {
+        const int i0 = max(0, k - L2), i1 = min(L1, k);
+#pragma unroll
+        for (int r = 0; r < kPF; ++r) {
+            const int i = i0 + tid + r * kThreads, j = k - i;
+            const bool ok = i <= i1 && i >= 1 && j >= 1;
+            const size_t si = ok ? (size_t)(i - 1) * L2m + (j - 1) : 0;
+            c[r] = ok ? __ldg(S + si) : 0.f;
+            if (MODE == MODE_HVP) v[r] = ok ? __ldg(V + si) : 0.f;
+        }
+    };
+    fetch_fwd(0, pc, pv);
     float O1 = 0.f, O2 = 0.f, D1 = 0.f, D2 = 0.f;
     for (int k = 0; k <= K; ++k) {
+        const int k1 = max(k - 1, 0), k2 = max(k - 2, 0);
+        float* const aM0 = row(rAM, kAM, k);
+        float* const aI0 = row(rAM + 1, kAI, k);
+        float* const aD0 = row(rAM + 2, kAD, k);
+        const float* const aM1 = row(rAM, kAM, k1);
+        const float* const aI1 = row(rAM + 1, kAI, k1);
+        const float* const aD1 = row(rAM + 2, kAD, k1);
+        const float* const aM2 = row(rAM, kAM, k2);
+        const float* const aI2 = row(rAM + 1, kAI, k2);
+        const float* const aD2 = row(rAM + 2, kAD, k2);
+        float* const fM0 = TAN ? row(rFM, kFM, k) : nullptr;
+        float* const fI0 = TAN ? row(rFM + 1, kFI, k) : nullptr;
+        float* const fD0 = TAN ? row(rFM + 2, kFD, k) : nullptr;
+        const float* const fM1 = TAN ? row(rFM, kFM, k1) : nullptr;
+        const float* const fI1 = TAN ? row(rFM + 1, kFI, k1) : nullptr;
+        const float* const fD1 = TAN ? row(rFM + 2, kFD, k1) : nullptr;
+        const float* const fM2 = TAN ? row(rFM, kFM, k2) : nullptr;
+        const float* const fI2 = TAN ? row(rFM + 1, kFI, k2) : nullptr;
+        const float* const fD2 = TAN ? row(rFM + 2, kFD, k2) : nullptr;
         float Ok = 0.f, Dk = 0.f;
         if (k >= 1) {   // from the previous diagonal's middle cell: its largest state
             const int im = (max(0, k - 1 - L2) + min(L1, k - 1)) >> 1;
-            float a = C.at(kAM, k - 1, im), x = a;
+            float x = aM1[im];
             int st = 0;
-            if (C.at(kAI, k - 1, im) > x) x = C.at(kAI, k - 1, im), st = 1;
-            if (C.at(kAD, k - 1, im) > x) x = C.at(kAD, k - 1, im), st = 2;
+            if (aI1[im] > x) x = aI1[im], st = 1;
+            if (aD1[im] > x) x = aD1[im], st = 2;
             Ok = O1 + rintf(x);
-            if (TAN) Dk = D1 + rintf(C.at(kFM + st, k - 1, im));
+            if (TAN) Dk = D1 + rintf((st == 0 ? fM1 : st == 1 ? fI1 : fD1)[im]);
         }
-        if (threadIdx.x == 0) {
+        if (tid == 0) {
             C.O[k] = Ok;
             C.D[k] = Dk;
         }
         const float dO1 = O1 - Ok, dO2 = O2 - Ok, dD1 = D1 - Dk, dD2 = D2 - Dk;   // exact
-        const int i0 = max(0, k - L2), i1 = min(L1, k);
-        for (int i = i0 + threadIdx.x; i <= i1; i += blockDim.x) {
+        // the alphas (rings; the planes too where the tangent reverses read them)
+        auto putA = [&](int i, float vM, float vI, float vD) {
+            aM0[i] = vM;
+            aI0[i] = vI;
+            aD0[i] = vD;
+            if (smR && TAN) {
+                C.at(kAM, k, i) = vM;
+                C.at(kAI, k, i) = vI;
+                C.at(kAD, k, i) = vD;
+            }
+        };
+        auto putF = [&](int i, float vM, float vI, float vD) {
+            fM0[i] = vM;
+            fI0[i] = vI;
+            fD0[i] = vD;
+            if (smR) {
+                C.at(kFM, k, i) = vM;
+                C.at(kFI, k, i) = vI;
+                C.at(kFD, k, i) = vD;
+            }
+        };
+        auto cell = [&](int i, float sc, float vv) {
             const int j = k - i;
             if (i == 0 || j == 0) {   // boundary states
-                C.at(kAM, k, i) = k == 0 ? 0.f : kNInf;
-                C.at(kAI, k, i) = (j == 0 && i >= 1) ? fmaf((float)(i - 1), ge, go) - Ok : kNInf;
-                C.at(kAD, k, i) = (i == 0 && j >= 1) ? fmaf((float)(j - 1), ge, go) - Ok : kNInf;
+                putA(i, k == 0 ? 0.f : kNInf, (j == 0 && i >= 1) ? fmaf((float)(i - 1), ge, go) - Ok : kNInf,
+                     (i == 0 && j >= 1) ? fmaf((float)(j - 1), ge, go) - Ok : kNInf);
                 if (TAN) {
                     const float lead = MODE == MODE_PGAP ? 1.f : MODE == MODE_PGE ? (float)(k - 1) : 0.f;
-                    C.at(kFM, k, i) = -Dk;
-                    C.at(kFI, k, i) = ((j == 0 && i >= 1) ? lead : 0.f) - Dk;
-                    C.at(kFD, k, i) = ((i == 0 && j >= 1) ? lead : 0.f) - Dk;
+                    putF(i, -Dk, ((j == 0 && i >= 1) ? lead : 0.f) - Dk, ((i == 0 && j >= 1) ? lead : 0.f) - Dk);
                 }
-                continue;
+                return;
             }
-            const size_t si = (size_t)(i - 1) * L2m + (j - 1);
-            const float sc = S[si];
             // M from (i-1, j-1)
-            const float m1 = C.at(kAM, k - 2, i - 1) + dO2, m2 = C.at(kAI, k - 2, i - 1) + dO2,
-                        m3 = C.at(kAD, k - 2, i - 1) + dO2;
+            const float m1 = aM2[i - 1] + dO2, m2 = aI2[i - 1] + dO2, m3 = aD2[i - 1] + dO2;
             float wm1, wm2, wm3, hM;
             const float aM = sc + lse3w(m1, m2, m3, T, iT, wm1, wm2, wm3, MODE == MODE_PT ? &hM : nullptr);
             // I from (i-1, j)
-            const float u1 = C.at(kAM, k - 1, i - 1) + (go + dO1), u2 = C.at(kAI, k - 1, i - 1) + (ge + dO1),
-                        u3 = C.at(kAD, k - 1, i - 1) + (go + dO1);
+            const float u1 = aM1[i - 1] + (go + dO1), u2 = aI1[i - 1] + (ge + dO1), u3 = aD1[i - 1] + (go + dO1);
             float wi1, wi2, wi3, hI;
             const float aI = lse3w(u1, u2, u3, T, iT, wi1, wi2, wi3, MODE == MODE_PT ? &hI : nullptr);
             // D from (i, j-1)
-            const float l1 = C.at(kAM, k - 1, i) + (go + dO1), l2 = C.at(kAI, k - 1, i) + (go + dO1),
-                        l3 = C.at(kAD, k - 1, i) + (ge + dO1);
+            const float l1 = aM1[i] + (go + dO1), l2 = aI1[i] + (go + dO1), l3 = aD1[i] + (ge + dO1);
             float wd1, wd2, wd3, hD;
             const float aD = lse3w(l1, l2, l3, T, iT, wd1, wd2, wd3, MODE == MODE_PT ? &hD : nullptr);
-            C.at(kAM, k, i) = aM;
-            C.at(kAI, k, i) = aI;
-            C.at(kAD, k, i) = aD;
+            putA(i, aM, aI, aD);
             C.at(kWM1, k, i) = wm1;
             C.at(kWM2, k, i) = wm2;
             C.at(kWM3, k, i) = wm3;
@@ -213,91 +287,209 @@ __global__ void __launch_bounds__(kThreads) nwa_kernel(SwArgs p) {
             C.at(kWD2, k, i) = wd2;
             C.at(kWD3, k, i) = wd3;
             if (TAN) {
-                float fM = fmaf(wm1, C.at(kFM, k - 2, i - 1) + dD2,
-                                fmaf(wm2, C.at(kFI, k - 2, i - 1) + dD2, wm3 * (C.at(kFD, k - 2, i - 1) + dD2)));
-                float fI = fmaf(wi1, C.at(kFM, k - 1, i - 1) + (xI1 + dD1),
-                                fmaf(wi2, C.at(kFI, k - 1, i - 1) + (xI2 + dD1),
-                                     wi3 * (C.at(kFD, k - 1, i - 1) + (xI3 + dD1))));
-                float fD = fmaf(wd1, C.at(kFM, k - 1, i) + (xD1 + dD1),
-                                fmaf(wd2, C.at(kFI, k - 1, i) + (xD2 + dD1), wd3 * (C.at(kFD, k - 1, i) + (xD3 + dD1))));
-                if (MODE == MODE_HVP) fM += V[si];
+                float fM = fmaf(wm1, fM2[i - 1] + dD2, fmaf(wm2, fI2[i - 1] + dD2, wm3 * (fD2[i - 1] + dD2)));
+                float fI = fmaf(wi1, fM1[i - 1] + (xI1 + dD1),
+                                fmaf(wi2, fI1[i - 1] + (xI2 + dD1), wi3 * (fD1[i - 1] + (xI3 + dD1))));
+                float fD = fmaf(wd1, fM1[i] + (xD1 + dD1), fmaf(wd2, fI1[i] + (xD2 + dD1), wd3 * (fD1[i] + (xD3 + dD1))));
+                if (MODE == MODE_HVP) fM += vv;
                 if (MODE == MODE_PT) {   // + the choice's entropy (d LSE_T / dT at fixed options)
                     fM += hM;
                     fI += hI;
                     fD += hD;
                 }
-                C.at(kFM, k, i) = fM;
-                C.at(kFI, k, i) = fI;
-                C.at(kFD, k, i) = fD;
+                putF(i, fM, fI, fD);
             }
+        };
+        const int i0 = max(0, k - L2), i1 = min(L1, k);
+#pragma unroll
+        for (int r = 0; r < kPF; ++r) {
+            const int i = i0 + tid + r * kThreads;
+            if (i <= i1) cell(i, pc[r], pv[r]);
         }
-        __syncthreads();
+        for (int i = i0 + tid + kPF * kThreads; i <= i1; i += kThreads) {
+            const int j = k - i;
+            const bool ok = i >= 1 && j >= 1;
+            const size_t si = ok ? (size_t)(i - 1) * L2m + (j - 1) : 0;
+            cell(i, ok ? __ldg(S + si) : 0.f, MODE == MODE_HVP && ok ? __ldg(V + si) : 0.f);
+        }
+        if (k < K) {
+            float nc[kPF], nv[kPF];
+            fetch_fwd(k + 1, nc, nv);
+            __syncthreads();
+#pragma unroll
+            for (int r = 0; r < kPF; ++r) {
+                pc[r] = nc[r];
+                pv[r] = nv[r];
+            }
+        } else {
+            __syncthreads();
+        }
         O2 = O1;
         O1 = Ok;
         D2 = D1;
         D1 = Dk;
     }
 
-    // the final choice among the end cell's states
+    // the final choice among the end cell's states (rings read before any reverse write)
+    const float eM = row(rAM, kAM, K)[L1], eI = row(rAM + 1, kAI, K)[L1], eD = row(rAM + 2, kAD, K)[L1];
     float fw1, fw2, fw3, fh;
-    const float aEnd = lse3w(C.at(kAM, K, L1), C.at(kAI, K, L1), C.at(kAD, K, L1), T, iT, fw1, fw2, fw3, &fh);
+    const float aEnd = lse3w(eM, eI, eD, T, iT, fw1, fw2, fw3, &fh);
     float fr1 = 0.f, fr2 = 0.f, fr3 = 0.f;   // the final weights' tangents
     if (TAN) {
-        const float t1 = C.at(kFM, K, L1), t2 = C.at(kFI, K, L1), t3 = C.at(kFD, K, L1);
+        const float t1 = row(rFM, kFM, K)[L1], t2 = row(rFM + 1, kFI, K)[L1], t3 = row(rFM + 2, kFD, K)[L1];
         const float E = fmaf(fw1, t1, fmaf(fw2, t2, fw3 * t3));
         fr1 = fw1 * (t1 - E) * iT;
         fr2 = fw2 * (t2 - E) * iT;
         fr3 = fw3 * (t3 - E) * iT;
         if (MODE == MODE_PT) {
-            const float a1 = C.at(kAM, K, L1), a2 = C.at(kAI, K, L1), a3 = C.at(kAD, K, L1);
-            const float Ev = fmaf(fw1, a1, fmaf(fw2, a2, fw3 * a3));
+            const float Ev = fmaf(fw1, eM, fmaf(fw2, eI, fw3 * eD));
             const float iT2 = iT * iT;
-            fr1 = fmaf(fw1 * (Ev - a1), iT2, fr1);
-            fr2 = fmaf(fw2 * (Ev - a2), iT2, fr2);
-            fr3 = fmaf(fw3 * (Ev - a3), iT2, fr3);
+            fr1 = fmaf(fw1 * (Ev - eM), iT2, fr1);
+            fr2 = fmaf(fw2 * (Ev - eI), iT2, fr2);
+            fr3 = fmaf(fw3 * (Ev - eD), iT2, fr3);
         }
     }
 
     // ------------------------------------------------------------- reverse
+    RevIn pre[kPFR];
+    auto fetch_one = [&](int k, int i, RevIn& q) {
+        const int j = k - i;
+        const bool okM = i + 1 <= L1 && j + 1 <= L2, okI = i + 1 <= L1 && j >= 1, okD = j + 1 <= L2 && i >= 1;
+        const bool own = i >= 1 && j >= 1;
+#pragma unroll
+        for (int s = 0; s < 3; ++s) {
+            q.sm[s] = okM ? C.at(kWM1 + s, k + 2, i + 1) : 0.f;
+            q.si[s] = okI ? C.at(kWI1 + s, k + 1, i + 1) : 0.f;
+            q.sd[s] = okD ? C.at(kWD1 + s, k + 1, i) : 0.f;
+            q.om[s] = own ? C.at(kWM1 + s, k, i) : 0.f;
+            q.oi[s] = own ? C.at(kWI1 + s, k, i) : 0.f;
+            q.od[s] = own ? C.at(kWD1 + s, k, i) : 0.f;
+        }
+    };
+    auto fetch_rev = [&](int k, RevIn* q) {
+        const int i0 = max(0, k - L2), i1 = min(L1, k);
+#pragma unroll
+        for (int r = 0; r < kPFR; ++r) {
+            const int i = i0 + tid + r * kThreads;
+            if (i <= i1) fetch_one(k, i, q[r]);
+        }
+    };
+    if (MODE == MODE_MARG) fetch_rev(K, pre);
     double sopen = 0.0, sext = 0.0, sent = 0.0, sdot = 0.0;
     for (int k = K; k >= 0; --k) {
+        const int k1 = min(k + 1, K), k2 = min(k + 2, K);
+        float* const bM0 = row(rBM, kBM, k);
+        float* const bI0 = row(rBM + 1, kBI, k);
+        float* const bD0 = row(rBM + 2, kBD, k);
+        const float* const bM2 = row(rBM, kBM, k2);     // M successors lie on diagonal k + 2
+        const float* const bI1 = row(rBM + 1, kBI, k1);
+        const float* const bD1 = row(rBM + 2, kBD, k1);
         const int i0 = max(0, k - L2), i1 = min(L1, k);
-        for (int i = i0 + threadIdx.x; i <= i1; i += blockDim.x) {
-            const int j = k - i;
-            const bool interior = i >= 1 && j >= 1;
-            float bM = 0.f, bI = 0.f, bD = 0.f, rM = 0.f, rI = 0.f, rD = 0.f;
-            if (k == K) {
-                bM = fw1;
-                bI = fw2;
-                bD = fw3;
-                rM = fr1;
-                rI = fr2;
-                rD = fr3;
+        if (MODE == MODE_MARG) {
+            auto ent = [](const float* w) {   // a state's choice entropy -sum w ln w
+                float h = 0.f;
+#pragma unroll
+                for (int q = 0; q < 3; ++q)
+                    if (w[q] > 0.f) h = fmaf(-w[q], logf(w[q]), h);
+                return h;
+            };
+            auto cell = [&](int i, const RevIn& q) {
+                const int j = k - i;
+                float bM = 0.f, bI = 0.f, bD = 0.f;
+                if (k == K) {
+                    bM = fw1;
+                    bI = fw2;
+                    bD = fw3;
+                }
+                if (i + 1 <= L1 && j + 1 <= L2) {
+                    const float by = bM2[i + 1];
+                    bM = fmaf(by, q.sm[0], bM);
+                    bI = fmaf(by, q.sm[1], bI);
+                    bD = fmaf(by, q.sm[2], bD);
+                }
+                if (i + 1 <= L1 && j >= 1) {
+                    const float by = bI1[i + 1];
+                    bM = fmaf(by, q.si[0], bM);
+                    bI = fmaf(by, q.si[1], bI);
+                    bD = fmaf(by, q.si[2], bD);
+                }
+                if (j + 1 <= L2 && i >= 1) {
+                    const float by = bD1[i];
+                    bM = fmaf(by, q.sd[0], bM);
+                    bI = fmaf(by, q.sd[1], bI);
+                    bD = fmaf(by, q.sd[2], bD);
+                }
+                bM0[i] = bM;
+                bI0[i] = bI;
+                bD0[i] = bD;
+                if (i >= 1 && j >= 1) {
+                    if (out) out[(size_t)(i - 1) * L2m + (j - 1)] = bM;
+                    sopen += (double)bI * (double)(q.oi[0] + q.oi[2]) + (double)bD * (double)(q.od[0] + q.od[1]);
+                    sext += (double)bI * (double)q.oi[1] + (double)bD * (double)q.od[2];
+                    sent += (double)bM * (double)ent(q.om) + (double)bI * (double)ent(q.oi) +
+                            (double)bD * (double)ent(q.od);
+                } else if (k >= 1) {   // leading gaps of the boundary states
+                    const float bb = i >= 1 ? bI : bD;
+                    sopen += (double)bb;
+                    sext += (double)bb * (double)(k - 1);
+                }
+            };
+#pragma unroll
+            for (int r = 0; r < kPFR; ++r) {
+                const int i = i0 + tid + r * kThreads;
+                if (i <= i1) cell(i, pre[r]);
             }
-            // this cell's states as options: their tangents (a shift common
-            // to the three cancels in u - E) and, along T, their values
-            float t1 = 0.f, t2 = 0.f, t3 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-            if (TAN) {
-                t1 = C.at(kFM, k, i);
-                t2 = C.at(kFI, k, i);
-                t3 = C.at(kFD, k, i);
+            for (int i = i0 + tid + kPFR * kThreads; i <= i1; i += kThreads) {
+                RevIn q;
+                fetch_one(k, i, q);
+                cell(i, q);
             }
-            if (MODE == MODE_PT) {
-                a1 = C.at(kAM, k, i);
-                a2 = C.at(kAI, k, i);
-                a3 = C.at(kAD, k, i);
+            if (k > 0) {
+                RevIn nxt[kPFR];
+                fetch_rev(k - 1, nxt);
+                __syncthreads();
+#pragma unroll
+                for (int r = 0; r < kPFR; ++r) pre[r] = nxt[r];
+            } else {
+                __syncthreads();
             }
-            // successor state Y at d takes this cell's states with weights w1..w3;
-            // x1..x3: the options' direct parameter derivatives, g1..g3 their gap terms
-            auto take = [&](int kd, int id, int pb, int pr, int pw, float x1, float x2, float x3, float g1,
-                            float g2, float g3) {
-                const float by = C.at(pb, kd, id);
-                const float w1 = C.at(pw, kd, id), w2 = C.at(pw + 1, kd, id), w3 = C.at(pw + 2, kd, id);
-                bM = fmaf(by, w1, bM);
-                bI = fmaf(by, w2, bI);
-                bD = fmaf(by, w3, bD);
-                if (TAN) {
-                    const float ry = C.at(pr, kd, id);
+        } else {
+            float* const rM0 = row(rRM, kRM, k);
+            float* const rI0 = row(rRM + 1, kRI, k);
+            float* const rD0 = row(rRM + 2, kRD, k);
+            const float* const rM2 = row(rRM, kRM, k2);
+            const float* const rI1 = row(rRM + 1, kRI, k1);
+            const float* const rD1 = row(rRM + 2, kRD, k1);
+            for (int i = i0 + tid; i <= i1; i += blockDim.x) {
+                const int j = k - i;
+                const bool interior = i >= 1 && j >= 1;
+                float bM = 0.f, bI = 0.f, bD = 0.f, rM = 0.f, rI = 0.f, rD = 0.f;
+                if (k == K) {
+                    bM = fw1;
+                    bI = fw2;
+                    bD = fw3;
+                    rM = fr1;
+                    rI = fr2;
+                    rD = fr3;
+                }
+                // this cell's states as options: their tangents (a shift common
+                // to the three cancels in u - E) and, along T, their values
+                const float t1 = C.at(kFM, k, i), t2 = C.at(kFI, k, i), t3 = C.at(kFD, k, i);
+                float a1 = 0.f, a2 = 0.f, a3 = 0.f;
+                if (MODE == MODE_PT) {
+                    a1 = C.at(kAM, k, i);
+                    a2 = C.at(kAI, k, i);
+                    a3 = C.at(kAD, k, i);
+                }
+                // successor state Y at d (beta by, its tangent ry) takes this
+                // cell's states with weights w1..w3; x1..x3: the options' direct
+                // parameter derivatives, g1..g3 their gap terms
+                auto take = [&](int kd, int id, float by, float ry, int pw, float x1, float x2, float x3, float g1,
+                                float g2, float g3) {
+                    const float w1 = C.at(pw, kd, id), w2 = C.at(pw + 1, kd, id), w3 = C.at(pw + 2, kd, id);
+                    bM = fmaf(by, w1, bM);
+                    bI = fmaf(by, w2, bI);
+                    bD = fmaf(by, w3, bD);
                     const float u1 = t1 + x1, u2 = t2 + x2, u3 = t3 + x3;
                     const float E = fmaf(w1, u1, fmaf(w2, u2, w3 * u3));
                     float e1 = w1 * (u1 - E) * iT, e2 = w2 * (u2 - E) * iT, e3 = w3 * (u3 - E) * iT;
@@ -312,56 +504,32 @@ __global__ void __launch_bounds__(kThreads) nwa_kernel(SwArgs p) {
                     rM = fmaf(ry, w1, fmaf(by, e1, rM));
                     rI = fmaf(ry, w2, fmaf(by, e2, rI));
                     rD = fmaf(ry, w3, fmaf(by, e3, rD));
-                }
-            };
-            if (i + 1 <= L1 && j + 1 <= L2) take(k + 2, i + 1, kBM, kRM, kWM1, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f);
-            if (i + 1 <= L1 && j >= 1) take(k + 1, i + 1, kBI, kRI, kWI1, xI1, xI2, xI3, go, ge, go);
-            if (j + 1 <= L2 && i >= 1) take(k + 1, i, kBD, kRD, kWD1, xD1, xD2, xD3, go, go, ge);
-            C.at(kBM, k, i) = bM;
-            C.at(kBI, k, i) = bI;
-            C.at(kBD, k, i) = bD;
-            if (TAN) {
-                C.at(kRM, k, i) = rM;
-                C.at(kRI, k, i) = rI;
-                C.at(kRD, k, i) = rD;
-            }
-            if (interior) {
-                const size_t si = (size_t)(i - 1) * L2m + (j - 1);
-                if (MODE == MODE_MARG) {
-                    if (out) out[si] = bM;
-                    const float wi1 = C.at(kWI1, k, i), wi2 = C.at(kWI2, k, i), wi3 = C.at(kWI3, k, i);
-                    const float wd1 = C.at(kWD1, k, i), wd2 = C.at(kWD2, k, i), wd3 = C.at(kWD3, k, i);
-                    sopen += (double)bI * (double)(wi1 + wi3) + (double)bD * (double)(wd1 + wd2);
-                    sext += (double)bI * (double)wi2 + (double)bD * (double)wd3;
-                    // each visited state's choice entropy -sum w ln w
-                    auto ent = [&](int pw) {
-                        float h = 0.f;
-                        for (int q = 0; q < 3; ++q) {
-                            const float w = C.at(pw + q, k, i);
-                            if (w > 0.f) h = fmaf(-w, logf(w), h);
-                        }
-                        return h;
-                    };
-                    sent += (double)bM * (double)ent(kWM1) + (double)bI * (double)ent(kWI1) +
-                            (double)bD * (double)ent(kWD1);
-                } else {
+                };
+                if (i + 1 <= L1 && j + 1 <= L2)
+                    take(k + 2, i + 1, bM2[i + 1], rM2[i + 1], kWM1, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f);
+                if (i + 1 <= L1 && j >= 1) take(k + 1, i + 1, bI1[i + 1], rI1[i + 1], kWI1, xI1, xI2, xI3, go, ge, go);
+                if (j + 1 <= L2 && i >= 1) take(k + 1, i, bD1[i], rD1[i], kWD1, xD1, xD2, xD3, go, go, ge);
+                bM0[i] = bM;
+                bI0[i] = bI;
+                bD0[i] = bD;
+                rM0[i] = rM;
+                rI0[i] = rI;
+                rD0[i] = rD;
+                if (interior) {
+                    const size_t si = (size_t)(i - 1) * L2m + (j - 1);
                     if (out) out[si] = rM;
                     if (Gw) sdot += (double)Gw[si] * (double)rM;
                 }
-            } else if (MODE == MODE_MARG && k >= 1) {   // leading gaps of the boundary states
-                const float bb = i >= 1 ? bI : bD;
-                sopen += (double)bb;
-                sext += (double)bb * (double)(k - 1);
             }
+            __syncthreads();
         }
-        __syncthreads();
     }
 
     if (MODE == MODE_MARG) {
         const double to = block_sum(sopen, red);
         const double te = block_sum(sext, red);
         const double th = block_sum(sent, red);
-        if (threadIdx.x == 0) {
+        if (tid == 0) {
             if (p.value) p.value[b] = (float)((double)aEnd + (double)C.O[K]);
             if (p.grad_gap) p.grad_gap[b] = (float)to;
             if (p.grad_gap2) p.grad_gap2[b] = (float)te;
@@ -369,7 +537,7 @@ __global__ void __launch_bounds__(kThreads) nwa_kernel(SwArgs p) {
         }
     } else if (p.dot_out) {
         const double t = block_sum(sdot, red);
-        if (threadIdx.x == 0) p.dot_out[b] = (float)t;
+        if (tid == 0) p.dot_out[b] = (float)t;
     }
 }
 
@@ -385,12 +553,29 @@ size_t nwa_workspace_bytes(int op, int B, int L1, int L2) {
 
 int launch_nwa(const SwArgs& a, cudaStream_t st) {
     if (a.B == 0) return 0;
+    static DeviceSetup setup;
+    int dev = 0, sms = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return (int)e;
+    int rc = device_setup(setup, dev, [] {
+        const int cap = (int)nwa::kMaxRingBytes;
+        const void* ks[] = {(const void*)nwa::nwa_kernel<MODE_MARG>, (const void*)nwa::nwa_kernel<MODE_HVP>,
+                            (const void*)nwa::nwa_kernel<MODE_PGAP>, (const void*)nwa::nwa_kernel<MODE_PGE>,
+                            (const void*)nwa::nwa_kernel<MODE_PT>};
+        cudaError_t r = cudaSuccess;
+        for (const void* k : ks)
+            if (r == cudaSuccess) r = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, cap);
+        return (int)r;
+    }, &sms);
+    if (rc) return rc;
+    const size_t rb = nwa::ring_bytes(a.L1, a.mode);
+    const size_t smem = rb <= nwa::kMaxRingBytes ? rb : 0;   // else the rings are the planes
     switch (a.mode) {
-        case MODE_MARG: nwa::nwa_kernel<MODE_MARG><<<a.B, nwa::kThreads, 0, st>>>(a); break;
-        case MODE_HVP: nwa::nwa_kernel<MODE_HVP><<<a.B, nwa::kThreads, 0, st>>>(a); break;
-        case MODE_PGAP: nwa::nwa_kernel<MODE_PGAP><<<a.B, nwa::kThreads, 0, st>>>(a); break;
-        case MODE_PGE: nwa::nwa_kernel<MODE_PGE><<<a.B, nwa::kThreads, 0, st>>>(a); break;
-        case MODE_PT: nwa::nwa_kernel<MODE_PT><<<a.B, nwa::kThreads, 0, st>>>(a); break;
+        case MODE_MARG: nwa::nwa_kernel<MODE_MARG><<<a.B, nwa::kThreads, smem, st>>>(a); break;
+        case MODE_HVP: nwa::nwa_kernel<MODE_HVP><<<a.B, nwa::kThreads, smem, st>>>(a); break;
+        case MODE_PGAP: nwa::nwa_kernel<MODE_PGAP><<<a.B, nwa::kThreads, smem, st>>>(a); break;
+        case MODE_PGE: nwa::nwa_kernel<MODE_PGE><<<a.B, nwa::kThreads, smem, st>>>(a); break;
+        case MODE_PT: nwa::nwa_kernel<MODE_PT><<<a.B, nwa::kThreads, smem, st>>>(a); break;
         default: return kErrInvalid;
     }
     return (int)cudaGetLastError();
