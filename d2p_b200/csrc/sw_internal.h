@@ -150,6 +150,11 @@ size_t nwa_workspace_bytes(int op, int B, int L1, int L2);
 int launch_nwa(const SwArgs& a, cudaStream_t st);
 // soft DTW (sw_dtw.cu): workspace of one operator
 size_t dtw_workspace_bytes(int op, int B, int L1, int L2);
+// soft DTW value pass in wavefront form (sw_dtw_wave.cu): its workspace, and
+// the launch (MODE_MARG, a.redo a zeroed flag per problem; -1: shape not
+// covered, nothing launched)
+size_t dtw_wave_area(int B, int L1, int L2);
+int launch_dtw_wave(const SwArgs& a, cudaStream_t st);
 // engine counters of the current device (cumulative, read synchronously):
 // problems the plane engine computed [linear, affine], and problems the
 // log-domain kernel recomputed after a linear-domain kernel flagged them

@@ -168,3 +168,48 @@ def test_compile_fullgraph(d2p, cuda_device):
         torch.testing.assert_close(mc, me, rtol=0, atol=0)
         for a, b in zip(gc, ge):
             torch.testing.assert_close(a, b, rtol=1e-5, atol=1e-6)
+
+
+def _kernel_names(fn):
+    from torch.profiler import ProfilerActivity, profile
+
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        torch.ones(1, device="cuda").add_(1)   # a torch launch first (a session's first launches can go unrecorded)
+        torch.cuda.synchronize()
+        fn()
+        torch.cuda.synchronize()
+    return [e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA]
+
+
+WAVE_CASES = [
+    # (B, L1, L2, T, bandwidth, ragged, seed): more row-blocks than the CTA has
+    # warps, widths that are not multiples of 4 or 16, one column, a band
+    (3, 512, 512, 1.0, -1, False, 11),
+    (3, 300, 701, 0.5, 60, True, 12),
+    (2, 33, 1, 1.0, -1, False, 13),
+    (2, 1000, 64, 0.25, -1, True, 14),
+]
+WAVE_IDS = [f"{c[0]}x{c[1]}x{c[2]}-T{c[3]}-bw{c[4]}{'-ragged' if c[5] else ''}" for c in WAVE_CASES]
+
+
+@pytest.mark.parametrize("B,L1,L2,T,bw,ragged,seed", WAVE_CASES, ids=WAVE_IDS)
+def test_wavefront_value_pass(d2p, cuda_device, B, L1, L2, T, bw, ragged, seed):
+    """The value pass in row-block wavefront form (dtw_wave_kernel) against the
+    oracle, and repeatable bit for bit.  An empty sequence in the ragged cases
+    is flagged by it and recomputed by the diagonal engine."""
+    c0 = costs(B, L1, L2, seed)
+    ln = _lengths(B, L1, L2, ragged, seed)
+    lnd = torch.from_numpy(ln).to(cuda_device)
+    cd = c0.to(cuda_device)
+    names = _kernel_names(lambda: d2p.soft_dtw_with_grads(cd, T, lnd, bw))
+    assert any("dtw_wave_kernel" in n for n in names), names
+    v, m, gt = d2p.soft_dtw_with_grads(cd, T, lnd, bw)
+    r64 = oracle.dtw(c0.numpy(), ln, T, bw, "f64")
+    r32 = oracle.dtw(c0.numpy(), ln, T, bw, "f32")
+    fin = _finite(r64["value"], v)
+    check("dtw value", v[torch.from_numpy(fin).to(cuda_device)], r64["value"][fin], r32["value"][fin])
+    check("dtw marginals", m, r64["marginals"], r32["marginals"])
+    check("dtw grad_T", gt, r64["grad_T"], r32["grad_T"])
+    v2, m2, gt2 = d2p.soft_dtw_with_grads(cd, T, lnd, bw)
+    assert torch.equal(v, v2) and torch.equal(m, m2) and torch.equal(gt, gt2)
