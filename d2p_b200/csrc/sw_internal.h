@@ -148,6 +148,11 @@ int launch_nw(const SwArgs& a, cudaStream_t st);
 // a.mode MODE_MARG, MODE_HVP, MODE_PGAP (open), MODE_PGE (ext), MODE_PT
 size_t nwa_workspace_bytes(int op, int B, int L1, int L2);
 int launch_nwa(const SwArgs& a, cudaStream_t st);
+// affine NW value pass in wavefront form (sw_nw_affine_wave.cu): its
+// workspace, and the launch (MODE_MARG, a.redo a zeroed flag per problem; -1:
+// shape not covered, nothing launched)
+size_t nwa_wave_area(int B, int L1, int L2);
+int launch_nwa_wave(const SwArgs& a, cudaStream_t st);
 // soft DTW (sw_dtw.cu): workspace of one operator
 size_t dtw_workspace_bytes(int op, int B, int L1, int L2);
 // soft DTW value pass in wavefront form (sw_dtw_wave.cu): its workspace, and

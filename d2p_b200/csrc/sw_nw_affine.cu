@@ -143,6 +143,7 @@ __global__ void __launch_bounds__(kThreads) nwa_kernel(SwArgs p) {
     extern __shared__ float ring_smem[];
     __shared__ double red[32];
     const int b = blockIdx.x;
+    if (p.only && !p.only[b]) return;   // a fix-up launch: only the problems the wavefront kernel flagged
     const int L1m = p.L1, L2m = p.L2;
     const int L1 = p.lengths ? min(max(p.lengths[2 * b], 0), L1m) : L1m;
     const int L2 = p.lengths ? min(max(p.lengths[2 * b + 1], 0), L2m) : L2m;
@@ -547,6 +548,11 @@ __global__ void __launch_bounds__(kThreads) nwa_kernel(SwArgs p) {
 size_t nwa_workspace_bytes(int op, int B, int L1, int L2) {
     const size_t fb = nwa::per_problem_bytes(L1, L2, op == D2P_OP_FORWARD_BACKWARD ? MODE_MARG : MODE_PT);
     size_t n = (fb * (size_t)(B > 0 ? B : 1) + 255) & ~(size_t)255;
+    if (op == D2P_OP_FORWARD_BACKWARD) {   // the wavefront pass shares the area; + one flag per problem
+        const size_t w = nwa_wave_area(B, L1, L2);
+        if (w > n) n = w;
+        n += ((size_t)(B > 0 ? B : 1) * sizeof(int) + 255) & ~(size_t)255;
+    }
     if (op == D2P_OP_BACKWARD_FULL) n += ((size_t)3 * (B > 0 ? B : 1) * sizeof(float) + 255) & ~(size_t)255;
     return n;
 }
@@ -629,7 +635,19 @@ int d2p_nw_affine_forward_backward(const float* scores, const int* lengths, int 
     a.grad_gap = grad_gap_open;
     a.grad_gap2 = grad_gap_ext;
     a.grad_T = grad_temperature;
-    return launch_nwa(a, (cudaStream_t)stream);
+    cudaStream_t st = (cudaStream_t)stream;
+    // the wavefront pass; the engine recomputes the problems it flags
+    const size_t eng = (nwa::per_problem_bytes(L1, L2, MODE_MARG) * (size_t)B + 255) & ~(size_t)255;
+    const size_t wav = nwa_wave_area(B, L1, L2);
+    int* flags = (int*)((char*)workspace + (eng > wav ? eng : wav));
+    int rc = (int)cudaMemsetAsync(flags, 0, (size_t)B * sizeof(int), st);
+    if (rc) return rc;
+    SwArgs w = a;
+    w.redo = flags;
+    rc = launch_nwa_wave(w, st);
+    if (rc == 0) a.only = flags;
+    else if (rc != -1) return rc;
+    return launch_nwa(a, st);
 }
 
 int d2p_nw_affine_hvp(const float* scores, const float* tangent, const int* lengths, int B, int L1, int L2,

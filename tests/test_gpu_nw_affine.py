@@ -168,3 +168,48 @@ def test_empty_problems_are_all_gap_paths(d2p, cuda_device):
     assert np.allclose(g_o.cpu().numpy(), (n > 0).astype(float), atol=1e-6)
     assert np.allclose(g_e.cpu().numpy(), np.maximum(n - 1, 0), atol=1e-6)
     assert np.allclose(g_t.cpu().numpy(), 0.0, atol=1e-6)
+
+
+def _kernel_names(fn):
+    from torch.profiler import ProfilerActivity, profile
+
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        torch.ones(1, device="cuda").add_(1)   # a torch launch first (a session's first launches can go unrecorded)
+        torch.cuda.synchronize()
+        fn()
+        torch.cuda.synchronize()
+    return [e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA]
+
+
+WAVE_CASES = [
+    # (B, L1, L2, gap_open, gap_ext, T, ragged, seed): more row-blocks than the
+    # CTA has warps, widths that are not multiples of 4 or 16, one column, a
+    # ragged batch with an empty problem, low temperature
+    (3, 512, 512, -2.0, -0.5, 1.0, False, 21),
+    (3, 300, 701, -1.5, -0.3, 0.5, True, 22),
+    (2, 33, 1, -2.0, -0.5, 1.0, False, 23),
+    (2, 1000, 64, -2.0, -0.5, 0.25, True, 24),
+]
+WAVE_IDS = [f"{c[0]}x{c[1]}x{c[2]}-T{c[5]}{'-ragged' if c[6] else ''}" for c in WAVE_CASES]
+
+
+@pytest.mark.parametrize("B,L1,L2,go,ge,T,ragged,seed", WAVE_CASES, ids=WAVE_IDS)
+def test_wavefront_value_pass(d2p, cuda_device, B, L1, L2, go, ge, T, ragged, seed):
+    """The value pass in row-block wavefront form (nwa_wave_kernel) against the
+    oracle -- value, marginals and the three parameter gradients (leading gaps
+    of row 0 and column 0 included) -- and repeatable bit for bit.  An empty
+    problem is flagged by it and recomputed by the diagonal engine."""
+    s0 = scores(B, L1, L2, seed=seed)
+    ln, lnd = _lengths(B, L1, L2, ragged, seed, cuda_device)
+    sd = s0.to(cuda_device)
+    names = _kernel_names(lambda: d2p.soft_nw_affine_with_grads(sd, go, ge, T, lnd))
+    assert any("nwa_wave_kernel" in n for n in names), names
+    out = d2p.soft_nw_affine_with_grads(sd, go, ge, T, lnd)
+    r64 = oracle.nw_affine(s0.numpy(), ln, go, ge, T, "f64")
+    r32 = oracle.nw_affine(s0.numpy(), ln, go, ge, T, "f32")
+    for name, x, key in zip(("value", "marginals", "grad_open", "grad_ext", "grad_T"), out,
+                            ("value", "marginals", "grad_open", "grad_ext", "grad_T")):
+        check("nwa " + name, x, r64[key], r32[key])
+    again = d2p.soft_nw_affine_with_grads(sd, go, ge, T, lnd)
+    assert all(torch.equal(a, b) for a, b in zip(out, again))
