@@ -66,6 +66,10 @@ CONFIGS = {
                 dtype="f32", desc="soft_nw [256,512,512] fp32, gap -1, T 1, no masks"),
     "nwa2": dict(family="nw_affine", B=256, L1=512, L2=512, gap=(-2.0, -0.5), T=1.0, scale=1.0, lengths=False,
                  dtype="f32", desc="soft_nw_affine [256,512,512] fp32, open -2, ext -0.5, T 1, no masks"),
+    # soft SW of scores built from bf16 embeddings on the tensor cores (score producer + DP)
+    "emb2": dict(family="embed", B=256, L1=512, L2=512, D=128, gap=-1.0, T=1.0, scale=1.0, lengths=False,
+                 dtype="bf16", desc="soft_sw_embed: bf16 embeddings [256,512,128] x [256,512,128] -> scores "
+                                    "[256,512,512], gap -1, T 1"),
     "dtw2": dict(family="dtw", B=256, L1=512, L2=512, gap=None, T=1.0, scale=1.0, lengths=False,
                  dtype="f32", desc="soft_dtw [256,512,512] fp32 N(0,1) costs, T 1, no band, no masks"),
 }
@@ -547,6 +551,128 @@ def run_ours(args, cfg):
 
 
 # ----------------------------------------------------------------------------
+# soft SW from embeddings (score producer on tcgen05 + the strip kernel)
+# ----------------------------------------------------------------------------
+def run_embed(args, cfg):
+    """One step = soft_sw_embed (scores = x y^T on the tensor cores, soft SW of
+    them) + value.sum().backward() down to the embeddings.  Single process; the
+    producer kernel is also timed alone against the measured bf16 and HBM peaks."""
+    import torch
+
+    import d2p_b200 as d2p
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    B, L1, L2, D = cfg["B"], cfg["L1"], cfg["L2"], cfg["D"]
+    g = torch.Generator().manual_seed(0)
+    x_host = (torch.randn(B, L1, D, generator=g) / D ** 0.25).to(torch.bfloat16)
+    y_host = (torch.randn(B, L2, D, generator=g) / D ** 0.25).to(torch.bfloat16)
+    x = x_host.to(dev).requires_grad_(True)
+    y = y_host.to(dev).requires_grad_(True)
+    gap, T = cfg["gap"], cfg["T"]
+
+    def step(xa, ya):
+        res = d2p.soft_sw_embed(xa, ya, gap=gap, temperature=T)
+        gx, gy = torch.autograd.grad(res.value.sum(), (xa, ya))
+        return res.value.detach(), gx, gy
+
+    for _ in range(args.warmup):
+        step(x, y)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(0)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    clocks.mark_start()
+    e0.record()
+    for _ in range(args.steps):
+        step(x, y)
+    e1.record()
+    torch.cuda.synchronize()
+    clocks.mark_end()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+
+    # the producer alone (same stream, CUDA events)
+    with torch.no_grad():
+        xd, yd = x.detach(), y.detach()
+        for _ in range(3):
+            torch.ops.d2p_b200.embed_scores(xd, yd, 1.0)
+        torch.cuda.synchronize()
+        p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        nk = max(3, args.steps)
+        p0.record()
+        for _ in range(nk):
+            torch.ops.d2p_b200.embed_scores(xd, yd, 1.0)
+        p1.record()
+        torch.cuda.synchronize()
+        p_ms = p0.elapsed_time(p1) / nk
+
+    step_kernels = profile_kernels(lambda: step(x, y))
+    ours = {n.replace("void ", "", 1): v for n, v in step_kernels.items() if "d2pb::" in n or "embed_scores" in n}
+    launches = sum(v[0] for v in ours.values())
+
+    # end to end: the embeddings from pinned host memory every step, the values back
+    xp, yp = x_host.pin_memory(), y_host.pin_memory()
+    v_host = torch.empty(B, pin_memory=True)
+
+    def e2e_step():
+        xa = xp.to(dev, non_blocking=True).requires_grad_(True)
+        ya = yp.to(dev, non_blocking=True).requires_grad_(True)
+        v, _, _ = step(xa, ya)
+        v_host.copy_(v, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    x0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    x1.record()
+    torch.cuda.synchronize()
+    e2e_ms = x0.elapsed_time(x1) / args.steps
+
+    cells = B * L1 * L2
+    hbm_gbs, _, peak_src = load_peaks()
+    try:
+        bf16_peak = float(json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["bf16_tflops"])
+    except Exception:
+        bf16_peak = 1590.0
+    flops = 2.0 * B * L1 * L2 * D
+    wbytes = 4.0 * cells + 2.0 * B * (L1 + L2) * D   # scores written, embeddings read
+    t_tensor = flops / (bf16_peak * 1e12)
+    t_hbm = wbytes / (hbm_gbs * 1e9)
+    bound = "hbm" if t_hbm >= t_tensor else "tensor"
+    p_s = p_ms * 1e-3
+    producer = {
+        "kernel": "d2pb::emb::embed_scores_kernel (tcgen05.mma kind::f16, TMA, TMEM; d2p_embed_scores)",
+        "kernel_ms": round(p_ms, 4), "bound": bound,
+        "achieved": round(wbytes / p_s / 1e9, 2) if bound == "hbm" else round(flops / p_s / 1e12, 2),
+        "peak": hbm_gbs if bound == "hbm" else bf16_peak, "unit": "GB/s" if bound == "hbm" else "TFLOP/s",
+        "frac": round((t_hbm if bound == "hbm" else t_tensor) / p_s, 4),
+        "tflops": round(flops / p_s / 1e12, 2), "gbs": round(wbytes / p_s / 1e9, 2),
+        "peak_source": f"MEASURED_PEAKS.json ({peak_src}): hbm_gbs and bf16_tflops (burst)",
+    }
+    line = {
+        "metric": "soft_sw_embed fwd+bwd GCUPS (DP cells/s), scores built from bf16 embeddings on the tensor cores",
+        "value": round(cells / (ms * 1e-3) / 1e9, 3), "unit": "GCUPS", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16-in/f32", "data": "synthetic (seeded N(0,1)/D^0.25 embeddings)",
+        "config": {"workload": f"{args.config}: {cfg['desc']}", "B": B, "L1": L1, "L2": L2, "D": D,
+                   "step": "soft_sw_embed (value + marginals) + value.sum().backward() to x and y",
+                   "l2": "scores (268 MB) and marginals larger than L2"},
+        "e2e": {"value": round(cells / (e2e_ms * 1e-3) / 1e9, 3), "unit": "GCUPS",
+                "h2d_bytes_per_step": int(x_host.numel() * 2 + y_host.numel() * 2), "d2h_bytes_per_step": B * 4,
+                "ms_per_step": round(e2e_ms, 4)},
+        "gpu_launches": args.steps * launches,
+        "step_kernels": {n.split("(")[0]: v[0] for n, v in ours.items()},
+        "producer": producer,
+        "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------
 # reference CPU (oracle/_ref = the reference's own CPU kernels)
 # ----------------------------------------------------------------------------
 REF_OPS = os.path.join(ROOT, "oracle", "_ref", "libref_sw_ops.so")
@@ -744,7 +870,11 @@ def main():
         cfg["B"] = args.batch
         cfg["desc"] = cfg["desc"] + f" (batch overridden to {args.batch})"
     if args.impl == "reference":
+        if cfg["family"] == "embed":   # the reference has no embedding operator: einsum + its CPU soft_sw
+            cfg = dict(cfg, family="linear")
         run_reference(args, cfg)
+    elif cfg["family"] == "embed":
+        run_embed(args, cfg)
     else:
         run_ours(args, cfg)
 

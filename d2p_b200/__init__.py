@@ -17,6 +17,7 @@ _ops._pt2_mod = _pt2_ops
 from .sw import SoftSW, SoftSWAffine, SWResult, soft_sw, soft_sw_affine
 from .nw import NWResult, SoftNW, SoftNWAffine, soft_nw, soft_nw_affine
 from .dtw import DTWResult, SoftDTW, soft_dtw
+from .embed import embed_scores, soft_sw_embed
 from . import ops
 from .engine import engine_counts, set_engine, use_engine
 
@@ -50,7 +51,7 @@ soft_dtw_backward_full = _ops.soft_dtw_backward_full
 __version__ = "0.1.0"
 
 __all__ = [
-    "soft_sw", "soft_sw_affine", "SWResult", "SoftSW", "SoftSWAffine", "ops",
+    "soft_sw", "soft_sw_affine", "SWResult", "SoftSW", "SoftSWAffine", "ops", "embed_scores", "soft_sw_embed",
     "soft_sw_float", "soft_sw_with_grads", "soft_sw_hvp", "soft_sw_param_jacobian", "soft_sw_backward_full",
     "soft_sw_affine_float", "soft_sw_affine_with_grads", "soft_sw_affine_hvp", "soft_sw_affine_param_jacobian",
     "soft_sw_affine_backward_full", "engine_counts", "set_engine", "use_engine",

@@ -932,6 +932,36 @@ std::tuple<Tensor, Tensor> soft_dtw_backward_full_cuda(Tensor costs, Tensor grad
 // =============================================================================
 // schemas (verbatim from the reference registries) and implementations
 // =============================================================================
+// =============================================================================
+// score producer (no reference operator: its examples build the score plane
+// with an einsum, docs/examples.md:9-23): scores = scale * x y^T on tcgen05
+// =============================================================================
+Tensor embed_scores_cuda(const Tensor& x, const Tensor& y, double scale) {
+    TORCH_CHECK(x.is_cuda() && y.is_cuda(), "embed_scores: x and y must be CUDA tensors");
+    TORCH_CHECK(x.scalar_type() == at::kBFloat16 && y.scalar_type() == at::kBFloat16,
+                "embed_scores: x and y must be bfloat16");
+    TORCH_CHECK(x.dim() == 3 && y.dim() == 3, "embed_scores: x must be [B, L1, D] and y [B, L2, D]");
+    TORCH_CHECK(x.size(0) == y.size(0) && x.size(2) == y.size(2), "embed_scores: x and y must share B and D");
+    TORCH_CHECK(x.device() == y.device(), "embed_scores: x and y must be on the same device");
+    const c10::cuda::CUDAGuard guard(x.device());
+    const Tensor xc = x.contiguous(), yc = y.contiguous();
+    const int64_t B = x.size(0), L1 = x.size(1), L2 = y.size(1), D = x.size(2);
+    TORCH_CHECK(B <= 65535 && L1 <= std::numeric_limits<int>::max() && L2 <= std::numeric_limits<int>::max(),
+                "embed_scores: sizes out of range");
+    Tensor out = torch::empty({B, L1, L2}, x.options().dtype(at::kFloat));
+    check_rc(d2p_embed_scores(xc.data_ptr(), yc.data_ptr(), (int)B, (int)L1, (int)L2, (int)D, (float)scale,
+                              out.data_ptr<float>(), nullptr, cur_stream()),
+             "d2p_embed_scores");
+    return out;
+}
+
+TORCH_LIBRARY_FRAGMENT(d2p_b200, m) {
+    m.def("embed_scores(Tensor x, Tensor y, float scale) -> Tensor");
+}
+TORCH_LIBRARY_IMPL(d2p_b200, CUDA, m) {
+    m.impl("embed_scores", embed_scores_cuda);
+}
+
 TORCH_LIBRARY_FRAGMENT(d2p, m) {
     // src/sw/registry.cpp:30-44
     m.def("soft_sw(Tensor scores, Tensor gap, Tensor temperature, Tensor lengths) -> Tensor[]");

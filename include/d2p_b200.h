@@ -282,6 +282,19 @@ D2P_API int d2p_dtw_backward_full(const float* costs, const float* grad_marginal
                                   int L2, float temperature, int bandwidth, float* grad_costs,
                                   float* grad_temperature, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Score producer: scores[b] = scale * x[b] y[b]^T for bf16 embeddings x [B, L1,
+ * D] and y [B, L2, D] (contiguous, 16-byte aligned), fp32 scores [B, L1, L2],
+ * on the tcgen05 tensor cores.  D a multiple of 64, at most 256 (pad the
+ * embeddings with zeros: a zero column adds nothing to a dot product).
+ * status (optional, device int): incremented for each output tile whose copy
+ * or product did not arrive within the kernel's bounded waits (the tile is
+ * then computed on the CUDA cores; nothing is wrong with its values).  No
+ * operator of the reference corresponds: it takes the score plane as input
+ * (d2p/sw.py:247) and its examples build it with an einsum of embeddings
+ * (docs/examples.md:9-23). */
+D2P_API int d2p_embed_scores(const void* x, const void* y, int B, int L1, int L2, int D, float scale, float* scores,
+                             int* status, void* stream);
+
 /* Engine selection for the whole process (all devices): D2P_ENGINE_AUTO picks
  * per shape (the default, or what D2P_B200_ENGINE names at load: "plane",
  * "pipeline"); D2P_ENGINE_PLANE runs the general plane engine for every
