@@ -612,22 +612,45 @@ def run_embed(args, cfg):
     ours = {n.replace("void ", "", 1): v for n, v in step_kernels.items() if "d2pb::" in n or "embed_scores" in n}
     launches = sum(v[0] for v in ours.values())
 
-    # end to end: the embeddings from pinned host memory every step, the values back
+    # end to end: every step's embeddings copied from pinned host memory, its
+    # values back; as in an input pipeline, step k+1's copy runs on a copy
+    # stream while step k computes (two device buffers), all inside the timed region
     xp, yp = x_host.pin_memory(), y_host.pin_memory()
     v_host = torch.empty(B, pin_memory=True)
+    bx = [torch.empty_like(x.detach()), torch.empty_like(x.detach())]
+    by = [torch.empty_like(y.detach()), torch.empty_like(y.detach())]
+    main = torch.cuda.current_stream(dev)
+    cstream = torch.cuda.Stream(device=dev)
+    freed = [torch.cuda.Event(), torch.cuda.Event()]
+    loaded = [torch.cuda.Event(), torch.cuda.Event()]
 
-    def e2e_step():
-        xa = xp.to(dev, non_blocking=True).requires_grad_(True)
-        ya = yp.to(dev, non_blocking=True).requires_grad_(True)
-        v, _, _ = step(xa, ya)
-        v_host.copy_(v, non_blocking=True)
+    def issue_copy(i):
+        cstream.wait_event(freed[i])
+        with torch.cuda.stream(cstream):
+            bx[i].copy_(xp, non_blocking=True)
+            by[i].copy_(yp, non_blocking=True)
+        loaded[i].record(cstream)
 
-    e2e_step()
+    def e2e_run(n):
+        for i in range(2):
+            freed[i].record(main)
+        issue_copy(0)
+        for k in range(n):
+            i = k % 2
+            if k + 1 < n:
+                issue_copy(1 - i)
+            main.wait_event(loaded[i])
+            v, _, _ = step(bx[i].requires_grad_(True), by[i].requires_grad_(True))
+            v_host.copy_(v, non_blocking=True)
+            bx[i].requires_grad_(False)
+            by[i].requires_grad_(False)
+            freed[i].record(main)
+
+    e2e_run(2)
     torch.cuda.synchronize()
     x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     x0.record()
-    for _ in range(args.steps):
-        e2e_step()
+    e2e_run(args.steps)
     x1.record()
     torch.cuda.synchronize()
     e2e_ms = x0.elapsed_time(x1) / args.steps

@@ -229,6 +229,22 @@ __global__ void __launch_bounds__(kThreads) embed_scores_kernel(const __grid_con
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTile) : "memory");
 }
 
+// G[b] = bf16(scale * g[b] * P[b]): the gradient of the scores for a loss
+// that reaches only the values, in the operand type of the embeddings'
+// gradient GEMMs (8 elements per thread: 32 bytes read, 16 written)
+__global__ void grad_scores_bf16_kernel(const float* __restrict__ P, const float* __restrict__ g, float scale,
+                                        size_t plane, size_t n8, __nv_bfloat16* __restrict__ G) {
+    for (size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x; e < n8; e += (size_t)gridDim.x * blockDim.x) {
+        const size_t i = e * 8;
+        const float s = scale * __ldg(g + i / plane);
+        const float4 a = __ldcs(reinterpret_cast<const float4*>(P + i));
+        const float4 c = __ldcs(reinterpret_cast<const float4*>(P + i + 4));
+        __nv_bfloat162 o[4] = {__floats2bfloat162_rn(s * a.x, s * a.y), __floats2bfloat162_rn(s * a.z, s * a.w),
+                               __floats2bfloat162_rn(s * c.x, s * c.y), __floats2bfloat162_rn(s * c.z, s * c.w)};
+        *reinterpret_cast<uint4*>(G + i) = *reinterpret_cast<uint4*>(o);
+    }
+}
+
 }  // namespace emb
 
 namespace {
@@ -304,6 +320,28 @@ int d2p_embed_scores(const void* x, const void* y, int B, int L1, int L2, int D,
     const dim3 grid((L2 + emb::kTile - 1) / emb::kTile, (L1 + emb::kTile - 1) / emb::kTile, B);
     emb::embed_scores_kernel<<<grid, emb::kThreads, emb::smem_bytes(D), (cudaStream_t)stream>>>(
         tmX, tmY, tmS, tma_out, (const __nv_bfloat16*)x, (const __nv_bfloat16*)y, scores, L1, L2, D, scale, status);
+    return (int)cudaGetLastError();
+}
+
+int d2p_embed_grad_scores(const float* marginals, const float* grad_value, int B, int L1, int L2, float scale,
+                          void* grad_scores_bf16, void* stream) {
+    if (B < 0 || L1 < 0 || L2 < 0) return D2P_ERR_INVALID_ARGUMENT;
+    const size_t plane = (size_t)L1 * L2, n = plane * (size_t)B;
+    if (n == 0) return D2P_OK;
+    if (!marginals || !grad_value || !grad_scores_bf16) return D2P_ERR_INVALID_ARGUMENT;
+    if (plane % 8 != 0 || (((uintptr_t)marginals | (uintptr_t)grad_scores_bf16) & 15)) return D2P_ERR_INVALID_ARGUMENT;
+    static DeviceSetup setup;
+    int dev = 0, sms = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return (int)e;
+    int rc = device_setup(setup, dev, [] { return 0; }, &sms);
+    if (rc) return rc;
+    const size_t n8 = n / 8;
+    const int threads = 256;
+    const size_t want = (n8 + threads - 1) / threads;
+    const int blocks = (int)(want < (size_t)sms * 16 ? want : (size_t)sms * 16);
+    emb::grad_scores_bf16_kernel<<<blocks, threads, 0, (cudaStream_t)stream>>>(
+        marginals, grad_value, scale, plane, n8, (__nv_bfloat16*)grad_scores_bf16);
     return (int)cudaGetLastError();
 }
 

@@ -955,11 +955,28 @@ Tensor embed_scores_cuda(const Tensor& x, const Tensor& y, double scale) {
     return out;
 }
 
+// bf16(scale * grad_value[b] * marginals[b]): the scores' gradient of a loss of the values
+Tensor embed_grad_scores_cuda(const Tensor& marginals, const Tensor& grad_value, double scale) {
+    TORCH_CHECK(marginals.is_cuda() && marginals.scalar_type() == at::kFloat && marginals.dim() == 3,
+                "embed_grad_scores: marginals must be a [B, L1, L2] fp32 CUDA tensor");
+    TORCH_CHECK(grad_value.is_cuda() && grad_value.scalar_type() == at::kFloat && grad_value.numel() == marginals.size(0),
+                "embed_grad_scores: grad_value must be a [B] fp32 CUDA tensor");
+    const c10::cuda::CUDAGuard guard(marginals.device());
+    const Tensor P = marginals.contiguous(), g = grad_value.contiguous();
+    Tensor out = torch::empty(P.sizes(), P.options().dtype(at::kBFloat16));
+    check_rc(d2p_embed_grad_scores(P.data_ptr<float>(), g.data_ptr<float>(), (int)P.size(0), (int)P.size(1),
+                                   (int)P.size(2), (float)scale, out.data_ptr(), cur_stream()),
+             "d2p_embed_grad_scores");
+    return out;
+}
+
 TORCH_LIBRARY_FRAGMENT(d2p_b200, m) {
     m.def("embed_scores(Tensor x, Tensor y, float scale) -> Tensor");
+    m.def("embed_grad_scores(Tensor marginals, Tensor grad_value, float scale) -> Tensor");
 }
 TORCH_LIBRARY_IMPL(d2p_b200, CUDA, m) {
     m.impl("embed_scores", embed_scores_cuda);
+    m.impl("embed_grad_scores", embed_grad_scores_cuda);
 }
 
 TORCH_LIBRARY_FRAGMENT(d2p, m) {

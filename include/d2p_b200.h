@@ -294,6 +294,12 @@ D2P_API int d2p_dtw_backward_full(const float* costs, const float* grad_marginal
  * (docs/examples.md:9-23). */
 D2P_API int d2p_embed_scores(const void* x, const void* y, int B, int L1, int L2, int D, float scale, float* scores,
                              int* status, void* stream);
+/* The scores' gradient for a loss of the values only, in bf16 for the
+ * embeddings' gradient GEMMs: grad_scores[b] = bf16(scale * grad_value[b] *
+ * marginals[b]) (L1 * L2 a multiple of 8; 16-byte aligned planes).  No
+ * reference counterpart (see d2p_embed_scores). */
+D2P_API int d2p_embed_grad_scores(const float* marginals, const float* grad_value, int B, int L1, int L2, float scale,
+                                  void* grad_scores_bf16, void* stream);
 
 /* Engine selection for the whole process (all devices): D2P_ENGINE_AUTO picks
  * per shape (the default, or what D2P_B200_ENGINE names at load: "plane",

@@ -137,3 +137,36 @@ def test_embed_kernel_runs(d2p, cuda_device):
         torch.cuda.synchronize()
     names = [e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA]
     assert any("embed_scores_kernel" in n for n in names), names
+
+
+def test_soft_sw_embed_marginal_loss(d2p, cuda_device):
+    """A loss of the values and of the marginals: dL/dscores = g P + H W (the
+    Hessian-vector product along the marginals' weights W, from backward_full),
+    then the embeddings' GEMMs; against fp64 (oracle HVP) at the bf16 tolerance."""
+    B, L1, L2, D, gap, T = 2, 64, 80, 64, -1.0, 1.0
+    x = embeddings(B, L1, D, 8).to(cuda_device).requires_grad_(True)
+    y = embeddings(B, L2, D, 9).to(cuda_device).requires_grad_(True)
+    g = torch.Generator().manual_seed(10)
+    W = torch.randn(B, L1, L2, generator=g)
+    res = d2p.soft_sw_embed(x, y, gap=gap, temperature=T)
+    (res.value.sum() + (res.marginals * W.to(cuda_device)).sum()).backward()
+    s64 = torch.bmm(x.detach().cpu().double(), y.detach().cpu().double().transpose(1, 2)).numpy()
+    P = oracle.sw_linear(s64, None, gap, T, "f64")["marginals"]
+    HW = oracle.sw_linear_hvp(s64, W.double().numpy(), None, gap, T, "f64")
+    G = torch.from_numpy(P + HW)
+    gx_ref = torch.bmm(G, y.detach().cpu().double())
+    gy_ref = torch.bmm(G.transpose(1, 2), x.detach().cpu().double())
+    for name, got, want in (("grad_x", x.grad, gx_ref), ("grad_y", y.grad, gy_ref)):
+        err = (got.double().cpu() - want).abs()
+        assert torch.all(err <= 1e-2 * want.abs() + 1e-2 * want.abs().max()), (name, float(err.max()))
+
+
+def test_embed_grad_scores_op(d2p, cuda_device):
+    g = torch.Generator().manual_seed(11)
+    P = torch.rand(3, 40, 56, generator=g)
+    gv = torch.randn(3, generator=g)
+    G = d2p.embed_scores.__globals__["torch"].ops.d2p_b200.embed_grad_scores(P.to(cuda_device),
+                                                                             gv.to(cuda_device), 0.5)
+    assert G.dtype == torch.bfloat16
+    want = (0.5 * gv[:, None, None] * P).to(torch.bfloat16)
+    assert torch.equal(G.cpu(), want)
