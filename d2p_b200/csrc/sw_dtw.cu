@@ -388,15 +388,22 @@ __global__ void __launch_bounds__(kThreads) dtw_kernel(SwArgs p) {
 }  // namespace dtw
 
 // ------------------------------------------------------------------ host side
-size_t dtw_workspace_bytes(int op, int B, int L1, int L2) {
+// the area the engine and the wavefront passes of one operator share
+static size_t dtw_area(int op, int B, int L1, int L2) {
     const size_t fb = dtw::per_problem_bytes(L1, L2, op == D2P_OP_FORWARD_BACKWARD ? MODE_MARG : MODE_PT);
     size_t n = (fb * (size_t)(B > 0 ? B : 1) + 255) & ~(size_t)255;
-    if (op == D2P_OP_FORWARD_BACKWARD) {   // the wavefront pass shares the area; + one flag per problem
-        const size_t w = dtw_wave_area(B, L1, L2);
-        if (w > n) n = w;
-        n += ((size_t)(B > 0 ? B : 1) * sizeof(int) + 255) & ~(size_t)255;
-    }
-    if (op == D2P_OP_BACKWARD_FULL) n += ((size_t)(B > 0 ? B : 1) * sizeof(float) + 255) & ~(size_t)255;
+    size_t w = 0;
+    if (op == D2P_OP_FORWARD_BACKWARD) w = dtw_wave_area(B, L1, L2);
+    if (op == D2P_OP_HVP || op == D2P_OP_BACKWARD_FULL) w = dtw_wave_hvp_area(B, L1, L2);
+    return w > n ? w : n;
+}
+static size_t dtw_vec_bytes(int B) { return ((size_t)(B > 0 ? B : 1) * 4 + 255) & ~(size_t)255; }
+
+// [shared area][partials (backward_full)][a flag per problem (wavefront passes)]
+size_t dtw_workspace_bytes(int op, int B, int L1, int L2) {
+    size_t n = dtw_area(op, B, L1, L2);
+    if (op == D2P_OP_BACKWARD_FULL) n += dtw_vec_bytes(B);
+    if (op != D2P_OP_PARAM_JACOBIAN) n += dtw_vec_bytes(B);
     return n;
 }
 
@@ -469,9 +476,7 @@ int d2p_dtw_forward_backward(const float* costs, const int* lengths, int B, int 
     a.grad_T = grad_temperature;
     cudaStream_t st = (cudaStream_t)stream;
     // the wavefront pass; the engine recomputes the problems it flags
-    const size_t eng = (dtw::per_problem_bytes(L1, L2, MODE_MARG) * (size_t)B + 255) & ~(size_t)255;
-    const size_t wav = dtw_wave_area(B, L1, L2);
-    int* flags = (int*)((char*)workspace + (eng > wav ? eng : wav));
+    int* flags = (int*)((char*)workspace + dtw_area(D2P_OP_FORWARD_BACKWARD, B, L1, L2));
     int rc = (int)cudaMemsetAsync(flags, 0, (size_t)B * sizeof(int), st);
     if (rc) return rc;
     SwArgs w = a;
@@ -493,7 +498,17 @@ int d2p_dtw_hvp(const float* costs, const float* tangent, const int* lengths, in
     a.mode = MODE_HVP;
     a.tangent = tangent;
     a.out = hvp;
-    return launch_dtw(a, (cudaStream_t)stream);
+    cudaStream_t st = (cudaStream_t)stream;
+    // the wavefront pass; the engine recomputes the problems it flags
+    int* flags = (int*)((char*)workspace + dtw_area(D2P_OP_HVP, B, L1, L2));
+    int rc = (int)cudaMemsetAsync(flags, 0, (size_t)B * sizeof(int), st);
+    if (rc) return rc;
+    SwArgs w = a;
+    w.redo = flags;
+    rc = launch_dtw_wave_hvp(w, st);
+    if (rc == 0) a.only = flags;
+    else if (rc != -1) return rc;
+    return launch_dtw(a, st);
 }
 
 int d2p_dtw_param_jacobian(const float* costs, const int* lengths, int B, int L1, int L2, float temperature,
@@ -519,16 +534,26 @@ int d2p_dtw_backward_full(const float* costs, const float* grad_marginals, const
     if (!costs || !grad_marginals) return D2P_ERR_INVALID_ARGUMENT;
     if (!workspace || workspace_bytes < dtw_workspace_bytes(D2P_OP_BACKWARD_FULL, B, L1, L2))
         return D2P_ERR_WORKSPACE_TOO_SMALL;
-    // grad_costs = H . grad_marginals (the Hessian of S is symmetric); grad_T
-    // = sum grad_marginals * dP/dT
-    const size_t area = dtw::per_problem_bytes(L1, L2, MODE_PT) * (size_t)B;
-    float* partials = (float*)((char*)workspace + ((area + 255) & ~(size_t)255));
+    // grad_costs = H . grad_marginals (the Hessian of S is symmetric; the
+    // wavefront sweep, the engine for the problems it flags); grad_T = sum
+    // grad_marginals * dP/dT (the engine's dot sweep)
+    const size_t area = dtw_area(D2P_OP_BACKWARD_FULL, B, L1, L2);
+    float* partials = (float*)((char*)workspace + area);
+    int* flags = (int*)((char*)workspace + area + dtw_vec_bytes(B));
     SwArgs a = dtw_args(costs, lengths, B, L1, L2, temperature, bandwidth, workspace);
     a.mode = MODE_HVP;
     a.tangent = grad_marginals;
     a.out = grad_costs;
-    int rc = launch_dtw(a, st);
+    int rc = (int)cudaMemsetAsync(flags, 0, (size_t)B * sizeof(int), st);
     if (rc) return rc;
+    SwArgs w = a;
+    w.redo = flags;
+    rc = launch_dtw_wave_hvp(w, st);
+    if (rc == 0) a.only = flags;
+    else if (rc != -1) return rc;
+    rc = launch_dtw(a, st);
+    if (rc) return rc;
+    a.only = nullptr;
     a.tangent = nullptr;
     a.out = nullptr;
     a.dot_with = grad_marginals;

@@ -316,10 +316,316 @@ __global__ void __launch_bounds__(kThreads, 2) dtw_wave_kernel(SwArgs p) {
     }
 }
 
+
+// ============================================================================
+// The Hessian-vector product H V = d(marginals)/d(costs) . V in the same form.
+// The forward carries each cell's tangent along V, f = sum_k w_k f_k + V_c
+// (framed per step like alpha, frame D_t), and stores (w_d, w_u, w_l, f) and
+// V per cell.  The reverse carries beta and its tangent r: a cell d hands each
+// predecessor k the flow b_d w_k and r_d w_k + b_d w_k (f_d - V_d - f_k + D_d -
+// D_k) / T, the difference of tangents formed per successor as in the
+// reference (src/dtw/kernels_cpu.cpp:236-420 restated as flows): it reads its
+// predecessors' forward tangents itself (its own prefetched slot for the left
+// one, lane l-1's by shuffle for the upper two, the row-block above's for lane
+// 0); the predecessor's r is the sum of what it receives.
+// ============================================================================
+__host__ __device__ inline size_t hvp_problem_bytes(int L1m, int L2m) {
+    const size_t nr = (size_t)nrb_of(L1m) * row_elems(L2m);
+    const size_t sl = plane_floats(L1m, L2m);   // slots [rb][t][lane]
+    return ring::align_up(sl * sizeof(float4), 256) + ring::align_up(sl * sizeof(float), 256) +
+           2 * ring::align_up(nr * sizeof(float4), 256) + ring::align_up((size_t)nrb_of(L1m) * steps_of(L2m) * 4, 256);
+}
+
+__global__ void __launch_bounds__(kThreads, 2) dtw_wave_hvp_kernel(SwArgs p) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    CtaSmem& sm = *reinterpret_cast<CtaSmem*>(smem_raw);
+    const int b = blockIdx.x;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int L1m = p.L1, L2m = p.L2;
+    const int L1 = p.lengths ? min(max(p.lengths[2 * b], 0), L1m) : L1m;
+    const int L2 = p.lengths ? min(max(p.lengths[2 * b + 1], 0), L2m) : L2m;
+    if (L1 == 0 || L2 == 0) {
+        if (tid == 0) p.redo[b] = 1;
+        return;
+    }
+    const int bw = p.parts;
+    const float T = p.temp_dev ? __ldg(p.temp_dev) : p.temp;
+    const float iT = 1.f / T;
+    const size_t plane = (size_t)L1m * L2m;
+    const float* __restrict__ Cst = p.scores + (size_t)b * plane;
+    const float* __restrict__ Vin = p.tangent + (size_t)b * plane;
+    float* __restrict__ out = p.out + (size_t)b * plane;
+    const int TP = steps_of(L2m);
+    char* base = reinterpret_cast<char*>(p.ws) + (size_t)b * hvp_problem_bytes(L1m, L2m);
+    const size_t sl = plane_floats(L1m, L2m);
+    float4* const Wp = reinterpret_cast<float4*>(base);                                   // (w_d, w_u, w_l, f)
+    float* const Vp = reinterpret_cast<float*>(base + ring::align_up(sl * sizeof(float4), 256));
+    const size_t nr = (size_t)nrb_of(L1m) * row_elems(L2m);
+    float4* const bnd = reinterpret_cast<float4*>(reinterpret_cast<char*>(Vp) + ring::align_up(sl * sizeof(float), 256));
+    float4* const bbr = bnd + ring::align_up(nr * sizeof(float4), 256) / sizeof(float4);
+    float* const Dst = reinterpret_cast<float*>(bbr + ring::align_up(nr * sizeof(float4), 256) / sizeof(float4));
+    const int nRB = nrb_of(L1);
+    const int nst = (L2 + 31 + kCW - 1) / kCW;
+    WarpSmem& ws = sm.w[warp];
+    __shared__ float4 binF[kW][kCW];   // forward: the row above (alpha - O, O, f - D, D)
+    __shared__ float4 bbinR[kW][kCW];  // reverse: flows from the row below (flow, q, p, -)
+
+    if (tid < kW) {
+        sm.progF[tid] = -1;
+        sm.progR[tid] = -1;
+    }
+    if (tid == 0) sm.err = 0;
+    if (L1 < L1m || L2 < L2m) {
+        for (int i = 0; i < L1m; ++i)
+            for (int j = (i < L1 ? L2 : 0) + tid; j < L2m; j += kThreads) out[(size_t)i * L2m + j] = 0.f;
+    }
+    __syncthreads();
+    const float ratio = (float)L1 / (float)(L1 + L2);
+
+    // ------------------------------------------------------------- forward
+    for (int rb = warp; rb < nRB; rb += kW) {
+        const int i = 32 * rb + lane + 1;
+        const bool rowok = i <= L1;
+        const float ei = (float)((long long)i * L2) / (float)L1;
+        const size_t poff = (size_t)rb * TP * 32 + lane;
+        const float* vrow = Vin + (size_t)(rowok ? i - 1 : 0) * L2m;
+        auto load_chunk = [&](int c) {
+            const int col = c * kCW + (lane & 15);
+            const bool cin = col < L2;
+#pragma unroll 4
+            for (int q = 0; q < 16; ++q) {
+                const int r = (lane >> 4) + 2 * q;
+                const bool ok = cin && 32 * rb + r < L1;
+                const float* g = ok ? Cst + (size_t)(32 * rb + r) * L2m + col : Cst;
+                cp_async4_zfill(&ws.ring[r * kRW + (col & (kRW - 1))], g, ok ? 4 : 0);
+            }
+            ring::cp_async_commit();
+        };
+        load_chunk(0);
+        float prev = kPInf, upPrev = (rb == 0 && lane == 0) ? 0.f : kPInf, dprev = 0.f, O = 0.f;
+        float prevF = 0.f, upPrevF = 0.f, ddprev = 0.f, Dfr = 0.f;
+        int lstar = 0;
+        const int prodKey = (rb - 1) << 16;
+        const float4* bin_g = bnd + (size_t)(rb > 0 ? rb - 1 : 0) * row_elems(L2m);
+        float4* bout = bnd + (size_t)rb * row_elems(L2m);
+        for (int c = 0; c < nst; ++c) {
+            ring::cp_async_wait0();
+            __syncwarp();
+            load_chunk(c + 1);
+            if (rb > 0) {
+                ring::wait_flag(&sm.progF[(rb - 1) % kW], prodKey | min(c + 3, nst), &sm.err);
+                if (lane < kCW) {
+                    const int jj = c * kCW + lane + 1;
+                    binF[warp][lane] = jj <= L2 ? __ldcg(bin_g + jj) : make_float4(kPInf, 0.f, 0.f, 0.f);
+                }
+                __syncwarp();
+            }
+#pragma unroll 2
+            for (int q = 0; q < kCW; ++q) {
+                const int t = c * kCW + q;
+                const float an = __shfl_sync(kAll, prev, lstar), anF = __shfl_sync(kAll, prevF, lstar);
+                const float d = an < kFin ? rintf(an) : 0.f;
+                const float dd = an < kFin ? rintf(anF) : 0.f;
+                float up = __shfl_up_sync(kAll, prev, 1), upF = __shfl_up_sync(kAll, prevF, 1);
+                if (lane == 0) {
+                    if (rb == 0) {
+                        up = kPInf;
+                        upF = 0.f;
+                    } else {
+                        const float4 bv = binF[warp][q];
+                        up = bv.x < kFin ? bv.x + (bv.y - O) : kPInf;
+                        upF = bv.x < kFin ? bv.z + (bv.w - Dfr) : 0.f;
+                    }
+                }
+                const float dg = upPrev < kFin ? upPrev - dprev : kPInf;
+                const float dgF = upPrevF - ddprev;
+                const float lf = prev, lfF = prevF;
+                const int j = t - lane + 1;
+                const bool live = rowok && j >= 1 && j <= L2;
+                const bool act = live && (bw < 0 || fabsf((float)j - ei) <= (float)bw);
+                const float vv = live ? __ldg(vrow + (j - 1)) : 0.f;
+                float a = kPInf, wd = 0.f, wu = 0.f, wl = 0.f, f = 0.f;
+                if (act) {
+                    const float m = fminf(dg, fminf(up, lf));
+                    if (m < kFin) {
+                        const float cst = ws.ring[lane * kRW + ((t - lane) & (kRW - 1))];
+                        const float ed = expf((m - dg) * iT), eu = expf((m - up) * iT), el = expf((m - lf) * iT);
+                        const float sum = (ed + eu) + el;
+                        const float ls = logf(sum);
+                        const float is = 1.f / sum;
+                        wd = ed * is;
+                        wu = eu * is;
+                        wl = el * is;
+                        a = cst + fmaf(-T, ls, m);
+                        f = fmaf(wd, dgF, fmaf(wu, upF, wl * lfF)) + vv;
+                    }
+                }
+                const bool reached = a < kFin;
+                const float o = reached ? a - d : kPInf;
+                const float oF = reached ? f - dd : 0.f;
+                const size_t pi = poff + (size_t)t * 32;
+                Wp[pi] = make_float4(wd, wu, wl, oF);
+                Vp[pi] = vv;
+                if (lane == 31 && live) bout[j] = make_float4(o, O + d, oF, Dfr + dd);
+                if (lane == 0) Dst[(size_t)rb * TP + t] = Dfr + dd;
+                upPrev = up;
+                upPrevF = upF;
+                dprev = d;
+                ddprev = dd;
+                prev = o;
+                prevF = oF;
+                O += d;
+                Dfr += dd;
+                const int lo = max(0, t - L2 + 1), hi = min(min(t, 31), L1 - 1 - 32 * rb);
+                int lc = 16;
+                if (bw >= 0) lc = (int)rintf((float)(32 * rb + t + 2) * ratio) - (32 * rb + 1);
+                lstar = lo <= hi ? min(max(lc, lo), hi) : 0;
+            }
+            if (lane == 31) ring::st_release(&sm.progF[warp], (rb << 16) | (c + 1));
+        }
+        ring::cp_async_wait0();
+        __syncwarp();
+    }
+    __syncthreads();
+
+    // ------------------------------------------------------------- reverse
+    for (int n = warp; n < nRB; n += kW) {
+        const int rb = nRB - 1 - n;
+        const int i = 32 * rb + lane + 1;
+        const bool rowok = i <= L1;
+        const size_t poff = (size_t)rb * TP * 32 + lane;
+        const float* Drb = Dst + (size_t)rb * TP;
+        const float* Dup = Dst + (size_t)(rb > 0 ? rb - 1 : 0) * TP;
+        const float4* Wup = Wp + (size_t)(rb > 0 ? rb - 1 : 0) * TP * 32 + 31;   // the row above: lane 31
+        const int T0 = L2 + 30;
+        float4 wbuf[kPD];
+        float vbuf[kPD];
+#pragma unroll
+        for (int s = 0; s < kPD; ++s) {
+            const size_t pi = poff + (size_t)max(T0 - s, 0) * 32;
+            wbuf[s] = Wp[pi];
+            vbuf[s] = Vp[pi];
+        }
+        float Lf = 0.f, Lq = 0.f;   // from the right successor (own previous step)
+        float Df = 0.f, Dq = 0.f;   // the diagonal message of the previous step
+        float Xf = 0.f, Xq = 0.f;   // this step's message to lane l-1
+        const bool below = rb + 1 < nRB;
+        const int prodKey = (n - 1) << 16;
+        const float4* bb_in = bbr + (size_t)rb * row_elems(L2m);
+        float4* bb_out = bbr + (size_t)(rb > 0 ? rb - 1 : 0) * row_elems(L2m);
+        for (int c = 0; c < nst; ++c) {
+            if (below) {
+                ring::wait_flag(&sm.progR[(n - 1) % kW], prodKey | min(c + 3, nst), &sm.err);
+                if (lane < kCW) {
+                    const int jj = L2 - (c * kCW + lane);
+                    bbinR[warp][lane] = jj >= 1 ? __ldcg(bb_in + jj) : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+            }
+            __syncwarp();
+#pragma unroll
+            for (int q = 0; q < kCW; ++q) {
+                const int s = c * kCW + q;
+                const int t = T0 - s;
+                if (t < 0) break;
+                const float4 wv = wbuf[q % kPD];
+                const float vc = vbuf[q % kPD];
+                // the predecessors' forward tangents (their frames): left = this lane's
+                // step t-1; up / diagonal = lane l-1's steps t-1 / t-2 (prefetched there),
+                // for lane 0 the row-block above's last row at its steps t+31 / t+30
+                const float fl = wbuf[(q + 1) % kPD].w;
+                float fu = __shfl_up_sync(kAll, fl, 1);
+                float fd = __shfl_up_sync(kAll, wbuf[(q + 2) % kPD].w, 1);
+                const float fua = Wup[(size_t)min(t + 31, TP - 1) * 32].w, fda = Wup[(size_t)min(t + 30, TP - 1) * 32].w;
+                {
+                    const size_t pi = poff + (size_t)max(t - kPD, 0) * 32;
+                    wbuf[q % kPD] = Wp[pi];
+                    vbuf[q % kPD] = Vp[pi];
+                }
+                float xf = __shfl_down_sync(kAll, Xf, 1), xq = __shfl_down_sync(kAll, Xq, 1);
+                if (lane == 31) {
+                    const float4 bv = below ? bbinR[warp][q] : make_float4(0.f, 0.f, 0.f, 0.f);
+                    xf = bv.x;
+                    xq = bv.y;
+                }
+                const int j = t - lane + 1;
+                const bool live = rowok && j >= 1 && j <= L2;
+                const float seed = (i == L1 && j == L2) ? 1.f : 0.f;
+                float beta = 0.f, r = 0.f;
+                if (live) {
+                    beta = (seed + Lf) + xf;
+                    r = Lq + xq;
+                }
+                const float Dt = __ldg(Drb + t);
+                const float Dl = __ldg(Drb + max(t - 1, 0));
+                const float Dd = __ldg(Drb + max(t - 2, 0));
+                const float Dua = __ldg(Dup + min(t + 31, TP - 1)), Dda = __ldg(Dup + min(t + 30, TP - 1));
+                const bool top = lane == 0 && rb > 0;
+                float Du = Dl, Ddg = Dd;
+                if (top) {
+                    fu = fua;
+                    fd = fda;
+                    Du = Dua;
+                    Ddg = Dda;
+                }
+                // to predecessor k with weight w: r w + b w (f - V - f_k + D - D_k) / T
+                const float bT = beta * iT;
+                const float e = wv.w - vc;
+                Lf = beta * wv.z;
+                Lq = fmaf(r, wv.z, bT * wv.z * ((e - fl) + (Dt - Dl)));
+                Xf = fmaf(beta, wv.y, Df);
+                Xq = fmaf(r, wv.y, bT * wv.y * ((e - fu) + (Dt - Du))) + Dq;
+                Df = beta * wv.x;
+                Dq = fmaf(r, wv.x, bT * wv.x * ((e - fd) + (Dt - Ddg)));
+                if (live) ws.ring[lane * kRW + ((t - lane) & (kRW - 1))] = r;
+                if (lane == 0 && rb > 0 && live) bb_out[j] = make_float4(Xf, Xq, 0.f, 0.f);
+                if ((t & (kCW - 1)) == 0) {
+                    __syncwarp();
+                    const int col = t + (lane & 15);
+                    if (col < L2) {
+#pragma unroll 4
+                        for (int r2 = 0; r2 < 16; ++r2) {
+                            const int rr = (lane >> 4) + 2 * r2;
+                            if (32 * rb + rr < L1) out[(size_t)(32 * rb + rr) * L2m + col] = ws.ring[rr * kRW + (col & (kRW - 1))];
+                        }
+                    }
+                    __syncwarp();
+                }
+            }
+            if (lane == 0) ring::st_release(&sm.progR[warp], (n << 16) | (c + 1));
+        }
+    }
+    __syncthreads();
+    if (tid == 0 && sm.err) p.redo[b] = 1;
+}
+
 }  // namespace dtww
 
 size_t dtw_wave_area(int B, int L1, int L2) {
     return ring::align_up(dtww::per_problem_bytes(L1, L2) * (size_t)(B > 0 ? B : 1), 256);
+}
+
+size_t dtw_wave_hvp_area(int B, int L1, int L2) {
+    return ring::align_up(dtww::hvp_problem_bytes(L1, L2) * (size_t)(B > 0 ? B : 1), 256);
+}
+
+// H V of every problem (a.tangent = V, a.out = H V, a.redo a zeroed flag per
+// problem).  Returns -1 when the shape is not covered (nothing launched).
+int launch_dtw_wave_hvp(const SwArgs& a, cudaStream_t st) {
+    if (!a.redo || !a.out || !a.tangent || a.L1 > dtww::kMaxL1 || a.L2 > dtww::kMaxL2 || a.L1 < 1 || a.L2 < 1)
+        return -1;
+    if (a.B == 0) return 0;
+    static DeviceSetup setup;
+    int dev = 0, sms = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return (int)e;
+    const size_t smem = sizeof(dtww::CtaSmem);
+    int rc = device_setup(setup, dev, [smem] {
+        return (int)cudaFuncSetAttribute(dtww::dtw_wave_hvp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    }, &sms);
+    if (rc) return rc;
+    dtww::dtw_wave_hvp_kernel<<<a.B, dtww::kThreads, smem, st>>>(a);
+    return (int)cudaGetLastError();
 }
 
 // Value + marginals + dS/dT of every problem (a.mode == MODE_MARG, a.redo set

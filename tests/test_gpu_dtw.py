@@ -213,3 +213,27 @@ def test_wavefront_value_pass(d2p, cuda_device, B, L1, L2, T, bw, ragged, seed):
     check("dtw grad_T", gt, r64["grad_T"], r32["grad_T"])
     v2, m2, gt2 = d2p.soft_dtw_with_grads(cd, T, lnd, bw)
     assert torch.equal(v, v2) and torch.equal(m, m2) and torch.equal(gt, gt2)
+
+
+@pytest.mark.parametrize("B,L1,L2,T,bw,ragged,seed", WAVE_CASES, ids=WAVE_IDS)
+def test_wavefront_hvp_backward_full(d2p, cuda_device, B, L1, L2, T, bw, ragged, seed):
+    """The Hessian-vector product in wavefront form (dtw_wave_hvp_kernel), and
+    backward_full's cost gradient through it, against the oracle; repeatable bit
+    for bit."""
+    c0 = costs(B, L1, L2, seed)
+    g = torch.Generator().manual_seed(seed + 300)
+    V = torch.randn(B, L1, L2, generator=g)
+    ln = _lengths(B, L1, L2, ragged, seed)
+    lnd = torch.from_numpy(ln).to(cuda_device)
+    cd, Vd = c0.to(cuda_device), V.to(cuda_device)
+    names = _kernel_names(lambda: d2p.soft_dtw_hvp(cd, Vd, T, lnd, bw))
+    assert any("dtw_wave_hvp_kernel" in n for n in names), names
+    H = d2p.soft_dtw_hvp(cd, Vd, T, lnd, bw)
+    check("dtw wave hvp", H, oracle.dtw_hvp(c0.numpy(), V.numpy(), ln, T, bw, "f64"),
+          oracle.dtw_hvp(c0.numpy(), V.numpy(), ln, T, bw, "f32"))
+    assert torch.equal(H, d2p.soft_dtw_hvp(cd, Vd, T, lnd, bw))
+    gc, gt = d2p.soft_dtw_backward_full(cd, Vd, T, lnd, bw)
+    r64 = oracle.dtw_backward_full(c0.numpy(), V.numpy(), ln, T, bw, "f64")
+    r32 = oracle.dtw_backward_full(c0.numpy(), V.numpy(), ln, T, bw, "f32")
+    check("dtw wave backward_full costs", gc, r64[0], r32[0])
+    check("dtw wave backward_full T", gt, r64[1], r32[1])
