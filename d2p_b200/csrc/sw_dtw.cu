@@ -394,7 +394,7 @@ static size_t dtw_area(int op, int B, int L1, int L2) {
     size_t n = (fb * (size_t)(B > 0 ? B : 1) + 255) & ~(size_t)255;
     size_t w = 0;
     if (op == D2P_OP_FORWARD_BACKWARD) w = dtw_wave_area(B, L1, L2);
-    if (op == D2P_OP_HVP || op == D2P_OP_BACKWARD_FULL) w = dtw_wave_hvp_area(B, L1, L2);
+    if (op != D2P_OP_FORWARD_BACKWARD) w = dtw_wave_tan_area(B, L1, L2);
     return w > n ? w : n;
 }
 static size_t dtw_vec_bytes(int B) { return ((size_t)(B > 0 ? B : 1) * 4 + 255) & ~(size_t)255; }
@@ -403,8 +403,7 @@ static size_t dtw_vec_bytes(int B) { return ((size_t)(B > 0 ? B : 1) * 4 + 255) 
 size_t dtw_workspace_bytes(int op, int B, int L1, int L2) {
     size_t n = dtw_area(op, B, L1, L2);
     if (op == D2P_OP_BACKWARD_FULL) n += dtw_vec_bytes(B);
-    if (op != D2P_OP_PARAM_JACOBIAN) n += dtw_vec_bytes(B);
-    return n;
+    return n + dtw_vec_bytes(B);
 }
 
 static int launch_dtw(const SwArgs& a, cudaStream_t st) {
@@ -505,7 +504,7 @@ int d2p_dtw_hvp(const float* costs, const float* tangent, const int* lengths, in
     if (rc) return rc;
     SwArgs w = a;
     w.redo = flags;
-    rc = launch_dtw_wave_hvp(w, st);
+    rc = launch_dtw_wave_tan(w, st);
     if (rc == 0) a.only = flags;
     else if (rc != -1) return rc;
     return launch_dtw(a, st);
@@ -521,7 +520,17 @@ int d2p_dtw_param_jacobian(const float* costs, const int* lengths, int B, int L1
     SwArgs a = dtw_args(costs, lengths, B, L1, L2, temperature, bandwidth, workspace);
     a.mode = MODE_PT;
     a.out = jacobian;
-    return launch_dtw(a, (cudaStream_t)stream);
+    cudaStream_t st = (cudaStream_t)stream;
+    // the wavefront pass; the engine recomputes the problems it flags
+    int* flags = (int*)((char*)workspace + dtw_area(D2P_OP_PARAM_JACOBIAN, B, L1, L2));
+    int rc = (int)cudaMemsetAsync(flags, 0, (size_t)B * sizeof(int), st);
+    if (rc) return rc;
+    SwArgs w = a;
+    w.redo = flags;
+    rc = launch_dtw_wave_tan(w, st);
+    if (rc == 0) a.only = flags;
+    else if (rc != -1) return rc;
+    return launch_dtw(a, st);
 }
 
 int d2p_dtw_backward_full(const float* costs, const float* grad_marginals, const int* lengths, int B, int L1, int L2,
@@ -534,9 +543,9 @@ int d2p_dtw_backward_full(const float* costs, const float* grad_marginals, const
     if (!costs || !grad_marginals) return D2P_ERR_INVALID_ARGUMENT;
     if (!workspace || workspace_bytes < dtw_workspace_bytes(D2P_OP_BACKWARD_FULL, B, L1, L2))
         return D2P_ERR_WORKSPACE_TOO_SMALL;
-    // grad_costs = H . grad_marginals (the Hessian of S is symmetric; the
-    // wavefront sweep, the engine for the problems it flags); grad_T = sum
-    // grad_marginals * dP/dT (the engine's dot sweep)
+    // grad_costs = H . grad_marginals (the Hessian of S is symmetric); grad_T
+    // = sum grad_marginals * dP/dT: two wavefront sweeps, the engine for the
+    // problems they flag
     const size_t area = dtw_area(D2P_OP_BACKWARD_FULL, B, L1, L2);
     float* partials = (float*)((char*)workspace + area);
     int* flags = (int*)((char*)workspace + area + dtw_vec_bytes(B));
@@ -548,17 +557,23 @@ int d2p_dtw_backward_full(const float* costs, const float* grad_marginals, const
     if (rc) return rc;
     SwArgs w = a;
     w.redo = flags;
-    rc = launch_dtw_wave_hvp(w, st);
+    rc = launch_dtw_wave_tan(w, st);
     if (rc == 0) a.only = flags;
     else if (rc != -1) return rc;
     rc = launch_dtw(a, st);
     if (rc) return rc;
-    a.only = nullptr;
     a.tangent = nullptr;
     a.out = nullptr;
     a.dot_with = grad_marginals;
     a.mode = MODE_PT;
     a.dot_out = partials;
+    w = a;
+    w.only = nullptr;
+    w.redo = flags;
+    rc = launch_dtw_wave_tan(w, st);
+    if (rc == 0) a.only = flags;
+    else if (rc != -1) return rc;
+    else a.only = nullptr;
     rc = launch_dtw(a, st);
     if (rc) return rc;
     return launch_sum_batches(partials, 1, B, grad_temperature, 0, st);

@@ -332,11 +332,14 @@ __global__ void __launch_bounds__(kThreads, 2) dtw_wave_kernel(SwArgs p) {
 __host__ __device__ inline size_t hvp_problem_bytes(int L1m, int L2m) {
     const size_t nr = (size_t)nrb_of(L1m) * row_elems(L2m);
     const size_t sl = plane_floats(L1m, L2m);   // slots [rb][t][lane]
-    return ring::align_up(sl * sizeof(float4), 256) + ring::align_up(sl * sizeof(float), 256) +
-           2 * ring::align_up(nr * sizeof(float4), 256) + ring::align_up((size_t)nrb_of(L1m) * steps_of(L2m) * 4, 256);
+    return 2 * ring::align_up(sl * sizeof(float4), 256) + 2 * ring::align_up(nr * sizeof(float4), 256) +
+           2 * ring::align_up((size_t)nrb_of(L1m) * steps_of(L2m) * 4, 256);
 }
 
-__global__ void __launch_bounds__(kThreads, 2) dtw_wave_hvp_kernel(SwArgs p) {
+// MODE_HVP: out = H p.tangent.  MODE_PT: out = dP/dT (if p.out), and with
+// p.dot_with, dot_out[b] = sum dot_with * dP/dT.
+template <int MODE>
+__global__ void __launch_bounds__(kThreads, 2) dtw_wave_tan_kernel(SwArgs p) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     CtaSmem& sm = *reinterpret_cast<CtaSmem*>(smem_raw);
     const int b = blockIdx.x;
@@ -353,17 +356,20 @@ __global__ void __launch_bounds__(kThreads, 2) dtw_wave_hvp_kernel(SwArgs p) {
     const float iT = 1.f / T;
     const size_t plane = (size_t)L1m * L2m;
     const float* __restrict__ Cst = p.scores + (size_t)b * plane;
-    const float* __restrict__ Vin = p.tangent + (size_t)b * plane;
-    float* __restrict__ out = p.out + (size_t)b * plane;
+    const float* __restrict__ Vin = MODE == MODE_HVP ? p.tangent + (size_t)b * plane : nullptr;
+    float* __restrict__ out = p.out ? p.out + (size_t)b * plane : nullptr;
+    const float* __restrict__ Gw = p.dot_with ? p.dot_with + (size_t)b * plane : nullptr;
     const int TP = steps_of(L2m);
     char* base = reinterpret_cast<char*>(p.ws) + (size_t)b * hvp_problem_bytes(L1m, L2m);
     const size_t sl = plane_floats(L1m, L2m);
-    float4* const Wp = reinterpret_cast<float4*>(base);                                   // (w_d, w_u, w_l, f)
-    float* const Vp = reinterpret_cast<float*>(base + ring::align_up(sl * sizeof(float4), 256));
+    float4* const Wp = reinterpret_cast<float4*>(base);   // (w_d, w_u, w_l, f)
+    // HVP: (V, -, -, -); PT: (alpha - O, h, alpha - O - cost, -), alpha 0 where unreached
+    float4* const Xp = Wp + ring::align_up(sl * sizeof(float4), 256) / sizeof(float4);
     const size_t nr = (size_t)nrb_of(L1m) * row_elems(L2m);
-    float4* const bnd = reinterpret_cast<float4*>(reinterpret_cast<char*>(Vp) + ring::align_up(sl * sizeof(float), 256));
+    float4* const bnd = Xp + ring::align_up(sl * sizeof(float4), 256) / sizeof(float4);
     float4* const bbr = bnd + ring::align_up(nr * sizeof(float4), 256) / sizeof(float4);
     float* const Dst = reinterpret_cast<float*>(bbr + ring::align_up(nr * sizeof(float4), 256) / sizeof(float4));
+    float* const Ost = Dst + ring::align_up((size_t)nrb_of(L1m) * TP * 4, 256) / 4;   // alpha's frames
     const int nRB = nrb_of(L1);
     const int nst = (L2 + 31 + kCW - 1) / kCW;
     WarpSmem& ws = sm.w[warp];
@@ -375,7 +381,7 @@ __global__ void __launch_bounds__(kThreads, 2) dtw_wave_hvp_kernel(SwArgs p) {
         sm.progR[tid] = -1;
     }
     if (tid == 0) sm.err = 0;
-    if (L1 < L1m || L2 < L2m) {
+    if (out && (L1 < L1m || L2 < L2m)) {   // zeros outside the problem (no plane: only the dot is wanted)
         for (int i = 0; i < L1m; ++i)
             for (int j = (i < L1 ? L2 : 0) + tid; j < L2m; j += kThreads) out[(size_t)i * L2m + j] = 0.f;
     }
@@ -388,7 +394,7 @@ __global__ void __launch_bounds__(kThreads, 2) dtw_wave_hvp_kernel(SwArgs p) {
         const bool rowok = i <= L1;
         const float ei = (float)((long long)i * L2) / (float)L1;
         const size_t poff = (size_t)rb * TP * 32 + lane;
-        const float* vrow = Vin + (size_t)(rowok ? i - 1 : 0) * L2m;
+        const float* vrow = MODE == MODE_HVP ? Vin + (size_t)(rowok ? i - 1 : 0) * L2m : nullptr;
         auto load_chunk = [&](int c) {
             const int col = c * kCW + (lane & 15);
             const bool cin = col < L2;
@@ -443,12 +449,12 @@ __global__ void __launch_bounds__(kThreads, 2) dtw_wave_hvp_kernel(SwArgs p) {
                 const int j = t - lane + 1;
                 const bool live = rowok && j >= 1 && j <= L2;
                 const bool act = live && (bw < 0 || fabsf((float)j - ei) <= (float)bw);
-                const float vv = live ? __ldg(vrow + (j - 1)) : 0.f;
-                float a = kPInf, wd = 0.f, wu = 0.f, wl = 0.f, f = 0.f;
+                const float vv = MODE == MODE_HVP && live ? __ldg(vrow + (j - 1)) : 0.f;
+                float a = kPInf, wd = 0.f, wu = 0.f, wl = 0.f, f = 0.f, h = 0.f, cst = 0.f;
                 if (act) {
                     const float m = fminf(dg, fminf(up, lf));
                     if (m < kFin) {
-                        const float cst = ws.ring[lane * kRW + ((t - lane) & (kRW - 1))];
+                        cst = ws.ring[lane * kRW + ((t - lane) & (kRW - 1))];
                         const float ed = expf((m - dg) * iT), eu = expf((m - up) * iT), el = expf((m - lf) * iT);
                         const float sum = (ed + eu) + el;
                         const float ls = logf(sum);
@@ -457,7 +463,13 @@ __global__ void __launch_bounds__(kThreads, 2) dtw_wave_hvp_kernel(SwArgs p) {
                         wu = eu * is;
                         wl = el * is;
                         a = cst + fmaf(-T, ls, m);
-                        f = fmaf(wd, dgF, fmaf(wu, upF, wl * lfF)) + vv;
+                        f = fmaf(wd, dgF, fmaf(wu, upF, wl * lfF));
+                        if (MODE == MODE_HVP) {
+                            f += vv;
+                        } else {   // along T: minus the choice's entropy
+                            h = ls + iT * fmaf(wd, dg - m, fmaf(wu, up - m, wl * (lf - m)));
+                            f -= h;
+                        }
                     }
                 }
                 const bool reached = a < kFin;
@@ -465,9 +477,13 @@ __global__ void __launch_bounds__(kThreads, 2) dtw_wave_hvp_kernel(SwArgs p) {
                 const float oF = reached ? f - dd : 0.f;
                 const size_t pi = poff + (size_t)t * 32;
                 Wp[pi] = make_float4(wd, wu, wl, oF);
-                Vp[pi] = vv;
+                if (MODE == MODE_HVP) Xp[pi] = make_float4(vv, 0.f, 0.f, 0.f);
+                else Xp[pi] = reached ? make_float4(o, h, o - cst, 0.f) : make_float4(0.f, 0.f, 0.f, 0.f);
                 if (lane == 31 && live) bout[j] = make_float4(o, O + d, oF, Dfr + dd);
-                if (lane == 0) Dst[(size_t)rb * TP + t] = Dfr + dd;
+                if (lane == 0) {
+                    Dst[(size_t)rb * TP + t] = Dfr + dd;
+                    Ost[(size_t)rb * TP + t] = O + d;
+                }
                 upPrev = up;
                 upPrevF = upF;
                 dprev = d;
@@ -489,22 +505,27 @@ __global__ void __launch_bounds__(kThreads, 2) dtw_wave_hvp_kernel(SwArgs p) {
     __syncthreads();
 
     // ------------------------------------------------------------- reverse
+    constexpr int kPT = 4;   // steps loaded ahead (a divisor of kCW: slot q % kPT is step s % kPT)
+    double sdot = 0.0;
     for (int n = warp; n < nRB; n += kW) {
         const int rb = nRB - 1 - n;
         const int i = 32 * rb + lane + 1;
         const bool rowok = i <= L1;
         const size_t poff = (size_t)rb * TP * 32 + lane;
+        const size_t rup = (size_t)(rb > 0 ? rb - 1 : 0);
         const float* Drb = Dst + (size_t)rb * TP;
-        const float* Dup = Dst + (size_t)(rb > 0 ? rb - 1 : 0) * TP;
-        const float4* Wup = Wp + (size_t)(rb > 0 ? rb - 1 : 0) * TP * 32 + 31;   // the row above: lane 31
+        const float* Dup = Dst + rup * TP;
+        const float* Orb = Ost + (size_t)rb * TP;
+        const float* Oup = Ost + rup * TP;
+        const float4* Wup = Wp + rup * TP * 32 + 31;   // the row above: lane 31
+        const float4* Xup = Xp + rup * TP * 32 + 31;
         const int T0 = L2 + 30;
-        float4 wbuf[kPD];
-        float vbuf[kPD];
+        float4 wbuf[kPT], xbuf[kPT];
 #pragma unroll
-        for (int s = 0; s < kPD; ++s) {
+        for (int s = 0; s < kPT; ++s) {
             const size_t pi = poff + (size_t)max(T0 - s, 0) * 32;
             wbuf[s] = Wp[pi];
-            vbuf[s] = Vp[pi];
+            xbuf[s] = Xp[pi];
         }
         float Lf = 0.f, Lq = 0.f;   // from the right successor (own previous step)
         float Df = 0.f, Dq = 0.f;   // the diagonal message of the previous step
@@ -512,7 +533,7 @@ __global__ void __launch_bounds__(kThreads, 2) dtw_wave_hvp_kernel(SwArgs p) {
         const bool below = rb + 1 < nRB;
         const int prodKey = (n - 1) << 16;
         const float4* bb_in = bbr + (size_t)rb * row_elems(L2m);
-        float4* bb_out = bbr + (size_t)(rb > 0 ? rb - 1 : 0) * row_elems(L2m);
+        float4* bb_out = bbr + rup * row_elems(L2m);
         for (int c = 0; c < nst; ++c) {
             if (below) {
                 ring::wait_flag(&sm.progR[(n - 1) % kW], prodKey | min(c + 3, nst), &sm.err);
@@ -527,19 +548,29 @@ __global__ void __launch_bounds__(kThreads, 2) dtw_wave_hvp_kernel(SwArgs p) {
                 const int s = c * kCW + q;
                 const int t = T0 - s;
                 if (t < 0) break;
-                const float4 wv = wbuf[q % kPD];
-                const float vc = vbuf[q % kPD];
-                // the predecessors' forward tangents (their frames): left = this lane's
-                // step t-1; up / diagonal = lane l-1's steps t-1 / t-2 (prefetched there),
-                // for lane 0 the row-block above's last row at its steps t+31 / t+30
-                const float fl = wbuf[(q + 1) % kPD].w;
+                const float4 wv = wbuf[q % kPT];
+                const float4 xv = xbuf[q % kPT];
+                // the predecessors' forward tangents (and along T their alphas), in
+                // their frames: left = this lane's step t-1; up / diagonal = lane
+                // l-1's steps t-1 / t-2 (in flight there), for lane 0 the row-block
+                // above's last row at its steps t+31 / t+30
+                const float fl = wbuf[(q + 1) % kPT].w;
                 float fu = __shfl_up_sync(kAll, fl, 1);
-                float fd = __shfl_up_sync(kAll, wbuf[(q + 2) % kPD].w, 1);
-                const float fua = Wup[(size_t)min(t + 31, TP - 1) * 32].w, fda = Wup[(size_t)min(t + 30, TP - 1) * 32].w;
+                float fd = __shfl_up_sync(kAll, wbuf[(q + 2) % kPT].w, 1);
+                const int su = min(t + 31, TP - 1), sd = min(t + 30, TP - 1);
+                const float fua = Wup[(size_t)su * 32].w, fda = Wup[(size_t)sd * 32].w;
+                float al = 0.f, au = 0.f, ad = 0.f, aua = 0.f, ada = 0.f;
+                if (MODE == MODE_PT) {
+                    al = xbuf[(q + 1) % kPT].x;
+                    au = __shfl_up_sync(kAll, al, 1);
+                    ad = __shfl_up_sync(kAll, xbuf[(q + 2) % kPT].x, 1);
+                    aua = Xup[(size_t)su * 32].x;
+                    ada = Xup[(size_t)sd * 32].x;
+                }
                 {
-                    const size_t pi = poff + (size_t)max(t - kPD, 0) * 32;
-                    wbuf[q % kPD] = Wp[pi];
-                    vbuf[q % kPD] = Vp[pi];
+                    const size_t pi = poff + (size_t)max(t - kPT, 0) * 32;
+                    wbuf[q % kPT] = Wp[pi];
+                    xbuf[q % kPT] = Xp[pi];
                 }
                 float xf = __shfl_down_sync(kAll, Xf, 1), xq = __shfl_down_sync(kAll, Xq, 1);
                 if (lane == 31) {
@@ -558,24 +589,47 @@ __global__ void __launch_bounds__(kThreads, 2) dtw_wave_hvp_kernel(SwArgs p) {
                 const float Dt = __ldg(Drb + t);
                 const float Dl = __ldg(Drb + max(t - 1, 0));
                 const float Dd = __ldg(Drb + max(t - 2, 0));
-                const float Dua = __ldg(Dup + min(t + 31, TP - 1)), Dda = __ldg(Dup + min(t + 30, TP - 1));
+                const float Dua = __ldg(Dup + su), Dda = __ldg(Dup + sd);
+                float Ot = 0.f, Ol = 0.f, Od = 0.f, Oua = 0.f, Oda = 0.f;
+                if (MODE == MODE_PT) {
+                    Ot = __ldg(Orb + t);
+                    Ol = __ldg(Orb + max(t - 1, 0));
+                    Od = __ldg(Orb + max(t - 2, 0));
+                    Oua = __ldg(Oup + su);
+                    Oda = __ldg(Oup + sd);
+                }
                 const bool top = lane == 0 && rb > 0;
-                float Du = Dl, Ddg = Dd;
+                float Du = Dl, Ddg = Dd, Ou = Ol, Odg = Od;
                 if (top) {
                     fu = fua;
                     fd = fda;
+                    au = aua;
+                    ad = ada;
                     Du = Dua;
                     Ddg = Dda;
+                    Ou = Oua;
+                    Odg = Oda;
                 }
-                // to predecessor k with weight w: r w + b w (f - V - f_k + D - D_k) / T
-                const float bT = beta * iT;
-                const float e = wv.w - vc;
+                // to predecessor k with weight w: r w + b dw, with
+                //   HVP: dw = w (f - V - f_k + D - D_k) / T
+                //   PT:  dw = w ((f - f_k + D - D_k + h) / T + (a_k - s + O_k - O - T h) / T^2)
+                auto msg = [&](float w, float fk, float Dk, float ak, float Ok) {
+                    float dw;
+                    if (MODE == MODE_HVP) {
+                        dw = w * (((wv.w - xv.x) - fk) + (Dt - Dk)) * iT;
+                    } else {
+                        const float g = (wv.w - fk) + (Dt - Dk);
+                        const float da = (ak - xv.z) + (Ok - Ot) - T * xv.y;
+                        dw = w * fmaf(g + xv.y, iT, da * iT * iT);
+                    }
+                    return fmaf(r, w, beta * dw);
+                };
                 Lf = beta * wv.z;
-                Lq = fmaf(r, wv.z, bT * wv.z * ((e - fl) + (Dt - Dl)));
+                Lq = msg(wv.z, fl, Dl, al, Ol);
                 Xf = fmaf(beta, wv.y, Df);
-                Xq = fmaf(r, wv.y, bT * wv.y * ((e - fu) + (Dt - Du))) + Dq;
+                Xq = msg(wv.y, fu, Du, au, Ou) + Dq;
                 Df = beta * wv.x;
-                Dq = fmaf(r, wv.x, bT * wv.x * ((e - fd) + (Dt - Ddg)));
+                Dq = msg(wv.x, fd, Ddg, ad, Odg);
                 if (live) ws.ring[lane * kRW + ((t - lane) & (kRW - 1))] = r;
                 if (lane == 0 && rb > 0 && live) bb_out[j] = make_float4(Xf, Xq, 0.f, 0.f);
                 if ((t & (kCW - 1)) == 0) {
@@ -585,7 +639,12 @@ __global__ void __launch_bounds__(kThreads, 2) dtw_wave_hvp_kernel(SwArgs p) {
 #pragma unroll 4
                         for (int r2 = 0; r2 < 16; ++r2) {
                             const int rr = (lane >> 4) + 2 * r2;
-                            if (32 * rb + rr < L1) out[(size_t)(32 * rb + rr) * L2m + col] = ws.ring[rr * kRW + (col & (kRW - 1))];
+                            if (32 * rb + rr < L1) {
+                                const float hv = ws.ring[rr * kRW + (col & (kRW - 1))];
+                                const size_t gi = (size_t)(32 * rb + rr) * L2m + col;
+                                if (out) out[gi] = hv;
+                                if (Gw) sdot += (double)__ldg(Gw + gi) * (double)hv;
+                            }
                         }
                     }
                     __syncwarp();
@@ -594,8 +653,17 @@ __global__ void __launch_bounds__(kThreads, 2) dtw_wave_hvp_kernel(SwArgs p) {
             if (lane == 0) ring::st_release(&sm.progR[warp], (n << 16) | (c + 1));
         }
     }
+    for (int o = 16; o >= 1; o >>= 1) sdot += __shfl_xor_sync(kAll, sdot, o);
+    if (lane == 0) sm.red[warp] = sdot;
     __syncthreads();
-    if (tid == 0 && sm.err) p.redo[b] = 1;
+    if (tid == 0) {
+        if (p.dot_out) {
+            double th = 0.0;
+            for (int w = 0; w < kW; ++w) th += sm.red[w];
+            p.dot_out[b] = (float)th;
+        }
+        if (sm.err) p.redo[b] = 1;
+    }
 }
 
 }  // namespace dtww
@@ -604,15 +672,19 @@ size_t dtw_wave_area(int B, int L1, int L2) {
     return ring::align_up(dtww::per_problem_bytes(L1, L2) * (size_t)(B > 0 ? B : 1), 256);
 }
 
-size_t dtw_wave_hvp_area(int B, int L1, int L2) {
+size_t dtw_wave_tan_area(int B, int L1, int L2) {
     return ring::align_up(dtww::hvp_problem_bytes(L1, L2) * (size_t)(B > 0 ? B : 1), 256);
 }
 
-// H V of every problem (a.tangent = V, a.out = H V, a.redo a zeroed flag per
-// problem).  Returns -1 when the shape is not covered (nothing launched).
-int launch_dtw_wave_hvp(const SwArgs& a, cudaStream_t st) {
-    if (!a.redo || !a.out || !a.tangent || a.L1 > dtww::kMaxL1 || a.L2 > dtww::kMaxL2 || a.L1 < 1 || a.L2 < 1)
-        return -1;
+// a.mode MODE_HVP: H V of every problem (a.tangent = V, a.out = H V);
+// MODE_PT: dP/dT (a.out, optional) and dot_out[b] = sum dot_with * dP/dT (with
+// a.dot_with).  a.redo a zeroed flag per problem.  Returns -1 when the shape is
+// not covered (nothing launched).
+int launch_dtw_wave_tan(const SwArgs& a, cudaStream_t st) {
+    if (!a.redo || a.L1 > dtww::kMaxL1 || a.L2 > dtww::kMaxL2 || a.L1 < 1 || a.L2 < 1) return -1;
+    if (a.mode == MODE_HVP && (!a.out || !a.tangent)) return -1;
+    if (a.mode == MODE_PT && !a.out && !(a.dot_with && a.dot_out)) return -1;
+    if (a.mode != MODE_HVP && a.mode != MODE_PT) return -1;
     if (a.B == 0) return 0;
     static DeviceSetup setup;
     int dev = 0, sms = 0;
@@ -620,11 +692,16 @@ int launch_dtw_wave_hvp(const SwArgs& a, cudaStream_t st) {
     if (e != cudaSuccess) return (int)e;
     const size_t smem = sizeof(dtww::CtaSmem);
     int rc = device_setup(setup, dev, [smem] {
-        return (int)cudaFuncSetAttribute(dtww::dtw_wave_hvp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem);
+        cudaError_t r = cudaFuncSetAttribute(dtww::dtw_wave_tan_kernel<MODE_HVP>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (r == cudaSuccess)
+            r = cudaFuncSetAttribute(dtww::dtw_wave_tan_kernel<MODE_PT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)smem);
+        return (int)r;
     }, &sms);
     if (rc) return rc;
-    dtww::dtw_wave_hvp_kernel<<<a.B, dtww::kThreads, smem, st>>>(a);
+    if (a.mode == MODE_HVP) dtww::dtw_wave_tan_kernel<MODE_HVP><<<a.B, dtww::kThreads, smem, st>>>(a);
+    else dtww::dtw_wave_tan_kernel<MODE_PT><<<a.B, dtww::kThreads, smem, st>>>(a);
     return (int)cudaGetLastError();
 }
 

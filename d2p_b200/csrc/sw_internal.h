@@ -160,8 +160,8 @@ size_t dtw_workspace_bytes(int op, int B, int L1, int L2);
 // covered, nothing launched)
 size_t dtw_wave_area(int B, int L1, int L2);
 int launch_dtw_wave(const SwArgs& a, cudaStream_t st);
-size_t dtw_wave_hvp_area(int B, int L1, int L2);
-int launch_dtw_wave_hvp(const SwArgs& a, cudaStream_t st);
+size_t dtw_wave_tan_area(int B, int L1, int L2);
+int launch_dtw_wave_tan(const SwArgs& a, cudaStream_t st);
 // engine counters of the current device (cumulative, read synchronously):
 // problems the plane engine computed [linear, affine], and problems the
 // log-domain kernel recomputed after a linear-domain kernel flagged them

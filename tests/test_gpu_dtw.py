@@ -217,9 +217,9 @@ def test_wavefront_value_pass(d2p, cuda_device, B, L1, L2, T, bw, ragged, seed):
 
 @pytest.mark.parametrize("B,L1,L2,T,bw,ragged,seed", WAVE_CASES, ids=WAVE_IDS)
 def test_wavefront_hvp_backward_full(d2p, cuda_device, B, L1, L2, T, bw, ragged, seed):
-    """The Hessian-vector product in wavefront form (dtw_wave_hvp_kernel), and
-    backward_full's cost gradient through it, against the oracle; repeatable bit
-    for bit."""
+    """The Hessian-vector product and dP/dT in wavefront form
+    (dtw_wave_tan_kernel<HVP / PT>), and backward_full through both, against the
+    oracle; repeatable bit for bit."""
     c0 = costs(B, L1, L2, seed)
     g = torch.Generator().manual_seed(seed + 300)
     V = torch.randn(B, L1, L2, generator=g)
@@ -227,7 +227,7 @@ def test_wavefront_hvp_backward_full(d2p, cuda_device, B, L1, L2, T, bw, ragged,
     lnd = torch.from_numpy(ln).to(cuda_device)
     cd, Vd = c0.to(cuda_device), V.to(cuda_device)
     names = _kernel_names(lambda: d2p.soft_dtw_hvp(cd, Vd, T, lnd, bw))
-    assert any("dtw_wave_hvp_kernel" in n for n in names), names
+    assert any("dtw_wave_tan_kernel" in n for n in names), names
     H = d2p.soft_dtw_hvp(cd, Vd, T, lnd, bw)
     check("dtw wave hvp", H, oracle.dtw_hvp(c0.numpy(), V.numpy(), ln, T, bw, "f64"),
           oracle.dtw_hvp(c0.numpy(), V.numpy(), ln, T, bw, "f32"))
@@ -237,3 +237,7 @@ def test_wavefront_hvp_backward_full(d2p, cuda_device, B, L1, L2, T, bw, ragged,
     r32 = oracle.dtw_backward_full(c0.numpy(), V.numpy(), ln, T, bw, "f32")
     check("dtw wave backward_full costs", gc, r64[0], r32[0])
     check("dtw wave backward_full T", gt, r64[1], r32[1])
+    J = d2p.soft_dtw_param_jacobian(cd, T, lnd, bw)
+    check("dtw wave jacobian", J, oracle.dtw_param_jacobian(c0.numpy(), ln, T, bw, "f64"),
+          oracle.dtw_param_jacobian(c0.numpy(), ln, T, bw, "f32"))
+    assert torch.equal(J, d2p.soft_dtw_param_jacobian(cd, T, lnd, bw))
