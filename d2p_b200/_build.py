@@ -29,7 +29,7 @@ NVCC = os.path.join(CUDA_HOME, "bin", "nvcc")
 CXX = "/usr/bin/g++" if os.path.exists("/usr/bin/g++") else "g++"
 
 CU_SOURCES = ["sw_plane.cu", "sw_wavefront.cu", "sw_linear.cu", "sw_affine_fast.cu", "sw_tangent.cu",
-              "sw_affine_tangent.cu", "sw_strip.cu", "sw_nw.cu", "sw_nw_affine.cu", "sw_nw_affine_wave.cu", "sw_dtw.cu", "sw_dtw_wave.cu", "sw_embed.cu", "sw_elementwise.cu", "sw_capi.cu", "sw_noalloc.cu", "sw_selftest.cu"]
+              "sw_affine_tangent.cu", "sw_strip.cu", "sw_nw.cu", "sw_nw_wave_tan.cu", "sw_nw_affine.cu", "sw_nw_affine_wave.cu", "sw_dtw.cu", "sw_dtw_wave.cu", "sw_embed.cu", "sw_elementwise.cu", "sw_capi.cu", "sw_noalloc.cu", "sw_selftest.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -161,6 +161,9 @@ size_t dtw_workspace_bytes(int op, int B, int L1, int L2);
 size_t dtw_wave_area(int B, int L1, int L2);
 int launch_dtw_wave(const SwArgs& a, cudaStream_t st);
 size_t dtw_wave_tan_area(int B, int L1, int L2);
+// soft NW tangent operators in wavefront form (sw_nw_wave_tan.cu)
+size_t nw_wave_tan_area(int B, int L1, int L2);
+int launch_nw_wave_tan(const SwArgs& a, cudaStream_t st);
 int launch_dtw_wave_tan(const SwArgs& a, cudaStream_t st);
 // engine counters of the current device (cumulative, read synchronously):
 // problems the plane engine computed [linear, affine], and problems the

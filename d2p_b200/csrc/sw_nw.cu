@@ -389,12 +389,33 @@ static size_t nw_fb_area(int B, int L1, int L2) {
     return n > sf ? n : a256(sf);
 }
 
+// the area the engine and the wavefront tangent passes share
+static size_t nw_tan_area(int B, int L1, int L2) {
+    const size_t nb = (size_t)(B > 0 ? B : 1);
+    const size_t e = a256(nw::per_problem_bytes(L1, L2, MODE_PT) * nb), w = nw_wave_tan_area(B, L1, L2);
+    return e > w ? e : w;
+}
+
+// tangent ops: [shared area][partials (backward_full)][a flag per problem]
 size_t nw_workspace_bytes(int op, int B, int L1, int L2) {
     const size_t nb = (size_t)(B > 0 ? B : 1);
     if (op == D2P_OP_FORWARD_BACKWARD) return nw_fb_area(B, L1, L2) + 2 * a256(nb * sizeof(int));
-    size_t n = a256(nw::per_problem_bytes(L1, L2, MODE_PT) * nb);
+    size_t n = nw_tan_area(B, L1, L2);
     if (op == D2P_OP_BACKWARD_FULL) n += a256((size_t)2 * nb * sizeof(float));
-    return n;
+    return n + a256(nb * sizeof(int));
+}
+
+// one tangent sweep: the wavefront form, then the engine for the problems it
+// flags (all of them when the wavefront form does not take the shape)
+static int nw_tan_sweep(SwArgs a, int* flags, cudaStream_t st) {
+    int rc = (int)cudaMemsetAsync(flags, 0, (size_t)a.B * sizeof(int), st);
+    if (rc) return rc;
+    SwArgs w = a;
+    w.redo = flags;
+    rc = launch_nw_wave_tan(w, st);
+    if (rc == 0) a.only = flags;
+    else if (rc != -1) return rc;
+    return launch_nw(a, st);
 }
 
 int launch_nw(const SwArgs& a, cudaStream_t st) {
@@ -503,7 +524,8 @@ int d2p_nw_hvp(const float* scores, const float* tangent, const int* lengths, in
     a.mode = MODE_HVP;
     a.tangent = tangent;
     a.out = hvp;
-    return launch_nw(a, (cudaStream_t)stream);
+    int* flags = (int*)((char*)workspace + nw_tan_area(B, L1, L2));
+    return nw_tan_sweep(a, flags, (cudaStream_t)stream);
 }
 
 int d2p_nw_param_jacobian(const float* scores, const int* lengths, int B, int L1, int L2, int param_type,
@@ -518,7 +540,8 @@ int d2p_nw_param_jacobian(const float* scores, const int* lengths, int B, int L1
     SwArgs a = nw_args(scores, lengths, B, L1, L2, gap, temperature, workspace);
     a.mode = param_type == 0 ? MODE_PGAP : MODE_PT;
     a.out = jacobian;
-    return launch_nw(a, (cudaStream_t)stream);
+    int* flags = (int*)((char*)workspace + nw_tan_area(B, L1, L2));
+    return nw_tan_sweep(a, flags, (cudaStream_t)stream);
 }
 
 int d2p_nw_backward_full(const float* scores, const float* grad_marginals, const int* lengths, int B, int L1,
@@ -537,13 +560,14 @@ int d2p_nw_backward_full(const float* scores, const float* grad_marginals, const
         return D2P_ERR_WORKSPACE_TOO_SMALL;
     // grad_scores = H . grad_marginals (the Hessian of S is symmetric);
     // grad_gap / grad_T = sum grad_marginals * dP/dgap, dP/dT
-    const size_t area = nw::per_problem_bytes(L1, L2, MODE_PT) * (size_t)B;
-    float* partials = (float*)((char*)workspace + ((area + 255) & ~(size_t)255));
+    const size_t area = nw_tan_area(B, L1, L2);
+    float* partials = (float*)((char*)workspace + area);
+    int* flags = (int*)((char*)workspace + area + a256((size_t)2 * B * sizeof(float)));
     SwArgs a = nw_args(scores, lengths, B, L1, L2, gap, temperature, workspace);
     a.mode = MODE_HVP;
     a.tangent = grad_marginals;
     a.out = grad_scores;
-    int rc = launch_nw(a, st);
+    int rc = nw_tan_sweep(a, flags, st);
     if (rc) return rc;
     a.tangent = nullptr;
     a.out = nullptr;
@@ -553,7 +577,7 @@ int d2p_nw_backward_full(const float* scores, const float* grad_marginals, const
     for (int q = 0; q < 2; ++q) {
         a.mode = modes[q];
         a.dot_out = partials + (size_t)q * B;
-        rc = launch_nw(a, st);
+        rc = nw_tan_sweep(a, flags, st);
         if (rc) return rc;
         rc = launch_sum_batches(partials + (size_t)q * B, 1, B, outs[q], 0, st);
         if (rc) return rc;

@@ -195,3 +195,54 @@ def test_strip_kernel_nw(d2p, cuda_device, B, L1, L2, gap, T, ragged, seed):
     assert any(not torch.equal(m[b], me[b]) for b in full), "the strip kernel did not run"
     v2, m2 = d2p.soft_nw_float(s0.to(cuda_device), gap, T, lnd)
     assert torch.equal(v, v2) and torch.equal(m, m2)
+
+
+def _tan_kernel_names(fn):
+    from torch.profiler import ProfilerActivity, profile
+
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        torch.ones(1, device="cuda").add_(1)   # a torch launch first (a session's first launches can go unrecorded)
+        torch.cuda.synchronize()
+        fn()
+        torch.cuda.synchronize()
+    return [e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA]
+
+
+WAVE_TAN_CASES = [
+    # (B, L1, L2, gap, T, ragged, seed): more row-blocks than the CTA has warps,
+    # widths that are not multiples of 4 or 16, one column, ragged with an empty problem
+    (3, 512, 512, -1.0, 1.0, False, 31),
+    (3, 300, 701, -0.5, 0.5, True, 32),
+    (2, 33, 1, -1.0, 1.0, False, 33),
+    (2, 1000, 64, -1.0, 0.25, True, 34),
+]
+
+
+@pytest.mark.parametrize("B,L1,L2,gap,T,ragged,seed", WAVE_TAN_CASES,
+                         ids=[f"{c[0]}x{c[1]}x{c[2]}-T{c[4]}{'-ragged' if c[5] else ''}" for c in WAVE_TAN_CASES])
+def test_wavefront_tangents(d2p, cuda_device, B, L1, L2, gap, T, ragged, seed):
+    """The tangent operators in wavefront form (nw_wave_tan_kernel<HVP / PGAP /
+    PT>): HVP, both Jacobians and backward_full against the oracle, each
+    repeatable bit for bit."""
+    s0 = scores(B, L1, L2, seed=seed)
+    V = scores(B, L1, L2, seed=seed + 100)
+    ln, lnd = _lengths(B, L1, L2, ragged, seed, cuda_device)
+    sd, Vd = s0.to(cuda_device), V.to(cuda_device)
+    names = _tan_kernel_names(lambda: d2p.soft_nw_hvp(sd, Vd, gap, T, lnd))
+    assert any("nw_wave_tan_kernel" in n for n in names), names
+    H = d2p.soft_nw_hvp(sd, Vd, gap, T, lnd)
+    check("nw wave hvp", H, oracle.nw_linear_hvp(s0.numpy(), V.numpy(), ln, gap, T, "f64"),
+          oracle.nw_linear_hvp(s0.numpy(), V.numpy(), ln, gap, T, "f32"))
+    assert torch.equal(H, d2p.soft_nw_hvp(sd, Vd, gap, T, lnd))
+    for pt in (0, 1):
+        J = d2p.soft_nw_param_jacobian(sd, pt, gap, T, lnd)
+        check(f"nw wave jacobian {pt}", J, oracle.nw_linear_param_jacobian(s0.numpy(), pt, ln, gap, T, "f64"),
+              oracle.nw_linear_param_jacobian(s0.numpy(), pt, ln, gap, T, "f32"))
+        assert torch.equal(J, d2p.soft_nw_param_jacobian(sd, pt, gap, T, lnd))
+    gs, gg, gt = d2p.soft_nw_backward_full(sd, Vd, gap, T, lnd)
+    r64 = oracle.nw_linear_backward_full(s0.numpy(), V.numpy(), ln, gap, T, "f64")
+    r32 = oracle.nw_linear_backward_full(s0.numpy(), V.numpy(), ln, gap, T, "f32")
+    check("nw wave backward_full scores", gs, r64[0], r32[0])
+    check("nw wave backward_full gap", gg, r64[1], r32[1])
+    check("nw wave backward_full T", gt, r64[2], r32[2])
