@@ -244,6 +244,12 @@ __global__ void grad_scores_bf16_kernel(const float* __restrict__ P, const float
         *reinterpret_cast<uint4*>(G + i) = *reinterpret_cast<uint4*>(o);
     }
 }
+// the same, one element per thread (planes that are not whole 8-element units)
+__global__ void grad_scores_bf16_scalar_kernel(const float* __restrict__ P, const float* __restrict__ g, float scale,
+                                               size_t plane, size_t n, __nv_bfloat16* __restrict__ G) {
+    for (size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (size_t)gridDim.x * blockDim.x)
+        G[e] = __float2bfloat16_rn(scale * __ldg(g + e / plane) * __ldcs(P + e));
+}
 
 }  // namespace emb
 
@@ -329,19 +335,23 @@ int d2p_embed_grad_scores(const float* marginals, const float* grad_value, int B
     const size_t plane = (size_t)L1 * L2, n = plane * (size_t)B;
     if (n == 0) return D2P_OK;
     if (!marginals || !grad_value || !grad_scores_bf16) return D2P_ERR_INVALID_ARGUMENT;
-    if (plane % 8 != 0 || (((uintptr_t)marginals | (uintptr_t)grad_scores_bf16) & 15)) return D2P_ERR_INVALID_ARGUMENT;
     static DeviceSetup setup;
     int dev = 0, sms = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return (int)e;
     int rc = device_setup(setup, dev, [] { return 0; }, &sms);
     if (rc) return rc;
-    const size_t n8 = n / 8;
     const int threads = 256;
-    const size_t want = (n8 + threads - 1) / threads;
+    const bool vec = plane % 8 == 0 && ((((uintptr_t)marginals | (uintptr_t)grad_scores_bf16) & 15) == 0);
+    const size_t units = vec ? n / 8 : n;
+    const size_t want = (units + threads - 1) / threads;
     const int blocks = (int)(want < (size_t)sms * 16 ? want : (size_t)sms * 16);
-    emb::grad_scores_bf16_kernel<<<blocks, threads, 0, (cudaStream_t)stream>>>(
-        marginals, grad_value, scale, plane, n8, (__nv_bfloat16*)grad_scores_bf16);
+    if (vec)
+        emb::grad_scores_bf16_kernel<<<blocks, threads, 0, (cudaStream_t)stream>>>(
+            marginals, grad_value, scale, plane, units, (__nv_bfloat16*)grad_scores_bf16);
+    else
+        emb::grad_scores_bf16_scalar_kernel<<<blocks, threads, 0, (cudaStream_t)stream>>>(
+            marginals, grad_value, scale, plane, units, (__nv_bfloat16*)grad_scores_bf16);
     return (int)cudaGetLastError();
 }
 

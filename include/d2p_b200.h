@@ -296,8 +296,9 @@ D2P_API int d2p_embed_scores(const void* x, const void* y, int B, int L1, int L2
                              int* status, void* stream);
 /* The scores' gradient for a loss of the values only, in bf16 for the
  * embeddings' gradient GEMMs: grad_scores[b] = bf16(scale * grad_value[b] *
- * marginals[b]) (L1 * L2 a multiple of 8; 16-byte aligned planes).  No
- * reference counterpart (see d2p_embed_scores). */
+ * marginals[b]) (any size; 8 elements per thread when L1 * L2 is a multiple
+ * of 8 and both planes are 16-byte aligned).  No reference counterpart (see
+ * d2p_embed_scores). */
 D2P_API int d2p_embed_grad_scores(const float* marginals, const float* grad_value, int B, int L1, int L2, float scale,
                                   void* grad_scores_bf16, void* stream);
 

@@ -161,12 +161,27 @@ def test_soft_sw_embed_marginal_loss(d2p, cuda_device):
         assert torch.all(err <= 1e-2 * want.abs() + 1e-2 * want.abs().max()), (name, float(err.max()))
 
 
-def test_embed_grad_scores_op(d2p, cuda_device):
+@pytest.mark.parametrize("L1,L2", [(40, 56), (37, 51)], ids=["whole-8", "odd"])
+def test_embed_grad_scores_op(d2p, cuda_device, L1, L2):
     g = torch.Generator().manual_seed(11)
-    P = torch.rand(3, 40, 56, generator=g)
+    P = torch.rand(3, L1, L2, generator=g)
     gv = torch.randn(3, generator=g)
-    G = d2p.embed_scores.__globals__["torch"].ops.d2p_b200.embed_grad_scores(P.to(cuda_device),
-                                                                             gv.to(cuda_device), 0.5)
+    G = torch.ops.d2p_b200.embed_grad_scores(P.to(cuda_device), gv.to(cuda_device), 0.5)
     assert G.dtype == torch.bfloat16
     want = (0.5 * gv[:, None, None] * P).to(torch.bfloat16)
     assert torch.equal(G.cpu(), want)
+
+
+def test_soft_sw_embed_odd_shape_backward(d2p, cuda_device):
+    """Planes that are not whole 8-element units, D that is padded (40 -> 64)."""
+    B, L1, L2, D = 2, 37, 51, 40
+    x = embeddings(B, L1, D, 12).to(cuda_device).requires_grad_(True)
+    y = embeddings(B, L2, D, 13).to(cuda_device).requires_grad_(True)
+    res = d2p.soft_sw_embed(x, y, gap=-1.0, temperature=1.0)
+    res.value.sum().backward()
+    s64 = torch.bmm(x.detach().cpu().double(), y.detach().cpu().double().transpose(1, 2)).numpy()
+    P = torch.from_numpy(oracle.sw_linear(s64, None, -1.0, 1.0, "f64")["marginals"])
+    for name, got, want in (("grad_x", x.grad, torch.bmm(P, y.detach().cpu().double())),
+                            ("grad_y", y.grad, torch.bmm(P.transpose(1, 2), x.detach().cpu().double()))):
+        err = (got.double().cpu() - want).abs()
+        assert torch.all(err <= 1e-2 * want.abs() + 1e-2 * want.abs().max()), (name, float(err.max()))
