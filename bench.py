@@ -19,7 +19,8 @@ region.
 ``strong`` (N > 1) is the same step with the config's batch split across the
 ranks (rank r takes the contiguous slice ``shard_bounds(B, N, r)`` of one
 globally seeded batch), timed the same way: the fixed-total-work curve.
-``hvp`` times the Hessian-vector product over the same batch (linear family).
+``hvp`` times the Hessian-vector product over the same batch (every family
+but affine SW).
 ``--config nw2`` / ``nwa2`` / ``dtw2`` run soft Needleman-Wunsch (linear and
 affine gaps) and soft DTW at config 2's shape (the same step through
 ``soft_nw`` / ``soft_nw_affine`` / ``soft_dtw``); their reference leg is the
@@ -482,11 +483,17 @@ def run_ours(args, cfg):
 
     # ---------------- Hessian-vector product (BASELINE config 5 reports it) ----------------
     hvp = None
-    if fam == "linear" and not args.no_hvp:
+    if fam in ("linear", "nw", "nw_affine", "dtw") and not args.no_hvp:
         gv = torch.Generator().manual_seed(2 + 1000 * rank)
         v_dev = torch.randn(s_host.shape, generator=gv).to(dev)
         with torch.no_grad():
             def hvp_step():
+                if fam == "nw":
+                    return torch.ops.d2p.soft_nw_hvp(s_dev, v_dev, gap, T, len_dev)
+                if fam == "nw_affine":
+                    return torch.ops.d2p.soft_nw_affine_hvp(s_dev, v_dev, gap[0], gap[1], T, len_dev)
+                if fam == "dtw":
+                    return torch.ops.d2p.soft_dtw_hvp(s_dev, v_dev, T, len_dev, None)
                 return torch.ops.d2p.soft_sw_hvp(s_dev, v_dev, gap, T, len_dev)
             for _ in range(2):
                 hvp_step()
@@ -502,10 +509,14 @@ def run_ours(args, cfg):
         if world > 1:
             dist.all_reduce(th, op=dist.ReduceOp.MAX)
         h_ms = float(th.item())
-        # convention: 12 B (scores, V, H) and 10 MUFU per valid cell
-        h_bound = max(12.0 * cells / (hbm_gbs * 1e9), 10.0 * cells / mufu_peak)
+        # convention: 12 B (scores, V, H) and the family's MUFU count per valid cell
+        h_bound = max(12.0 * cells / (hbm_gbs * 1e9), MUFU_PER_CELL[fam] * cells / mufu_peak)
+        h_kernel = {"linear": "ltan::lin_tan_kernel (d2p_sw_hvp)",
+                    "nw": "nwt::nw_wave_tan_kernel<HVP> (d2p_nw_hvp)",
+                    "nw_affine": "nwa::nwa_kernel<HVP> (d2p_nw_affine_hvp)",
+                    "dtw": "dtww::dtw_wave_tan_kernel<HVP> (d2p_dtw_hvp)"}[fam]
         hvp = {"value": round(total_cells / (h_ms * 1e-3) / 1e9, 3), "unit": "GCUPS", "ms_per_step": round(h_ms, 4),
-               "kernel": "ltan::lin_tan_kernel (d2p_sw_hvp)", "time_bound_ms": round(h_bound * 1e3, 4),
+               "kernel": h_kernel, "time_bound_ms": round(h_bound * 1e3, 4),
                "frac": round(h_bound / (h_ms * 1e-3), 4),
                # fwd + bwd step and one HVP over the same cells, timed as above
                "combined": {"value": round(total_cells / ((ms_max + h_ms) * 1e-3) / 1e9, 3), "unit": "GCUPS",
@@ -884,7 +895,7 @@ def main():
     ap.add_argument("--ref-cuda-seconds", type=float, default=5.0)
     ap.add_argument("--batch", type=int, default=0, help="override the per-rank batch (profiling on a small case)")
     ap.add_argument("--no-hvp", action="store_true",
-                    help="skip the Hessian-vector product leg (timed by default for the linear family)")
+                    help="skip the Hessian-vector product leg (timed by default for every family but affine SW)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -395,6 +395,11 @@ __global__ void __launch_bounds__(kThreads, 2) dtw_wave_tan_kernel(SwArgs p) {
         const float ei = (float)((long long)i * L2) / (float)L1;
         const size_t poff = (size_t)rb * TP * 32 + lane;
         const float* vrow = MODE == MODE_HVP ? Vin + (size_t)(rowok ? i - 1 : 0) * L2m : nullptr;
+        // V of this lane's column, two steps ahead (steps t and t + 1 in flight)
+        auto vload = [&](int jj) {
+            return MODE == MODE_HVP && rowok && jj >= 1 && jj <= L2 ? __ldg(vrow + (jj - 1)) : 0.f;
+        };
+        float vcur = vload(1 - lane), vnext = vload(2 - lane);
         auto load_chunk = [&](int c) {
             const int col = c * kCW + (lane & 15);
             const bool cin = col < L2;
@@ -449,7 +454,9 @@ __global__ void __launch_bounds__(kThreads, 2) dtw_wave_tan_kernel(SwArgs p) {
                 const int j = t - lane + 1;
                 const bool live = rowok && j >= 1 && j <= L2;
                 const bool act = live && (bw < 0 || fabsf((float)j - ei) <= (float)bw);
-                const float vv = MODE == MODE_HVP && live ? __ldg(vrow + (j - 1)) : 0.f;
+                const float vv = live ? vcur : 0.f;
+                vcur = vnext;
+                vnext = vload(j + 2);
                 float a = kPInf, wd = 0.f, wu = 0.f, wl = 0.f, f = 0.f, h = 0.f, cst = 0.f;
                 if (act) {
                     const float m = fminf(dg, fminf(up, lf));
@@ -505,6 +512,7 @@ __global__ void __launch_bounds__(kThreads, 2) dtw_wave_tan_kernel(SwArgs p) {
     __syncthreads();
 
     // ------------------------------------------------------------- reverse
+    constexpr bool XPT = MODE == MODE_PT;
     constexpr int kPT = 4;   // steps loaded ahead (a divisor of kCW: slot q % kPT is step s % kPT)
     double sdot = 0.0;
     for (int n = warp; n < nRB; n += kW) {
@@ -527,6 +535,15 @@ __global__ void __launch_bounds__(kThreads, 2) dtw_wave_tan_kernel(SwArgs p) {
             wbuf[s] = Wp[pi];
             xbuf[s] = Xp[pi];
         }
+        float upf[kPT], upa[kPT];   // the row above's lane-31 tangent (and alpha) at steps T0 + 30 - s
+#pragma unroll
+        for (int s = 0; s < kPT; ++s) {
+            const size_t ss = (size_t)min(T0 + 30 - s, TP - 1) * 32;
+            upf[s] = Wup[ss].w;
+            upa[s] = XPT ? Xup[ss].x : 0.f;
+        }
+        float fuaC = Wup[(size_t)min(T0 + 31, TP - 1) * 32].w;
+        float auaC = XPT ? Xup[(size_t)min(T0 + 31, TP - 1) * 32].x : 0.f;
         float Lf = 0.f, Lq = 0.f;   // from the right successor (own previous step)
         float Df = 0.f, Dq = 0.f;   // the diagonal message of the previous step
         float Xf = 0.f, Xq = 0.f;   // this step's message to lane l-1
@@ -558,14 +575,21 @@ __global__ void __launch_bounds__(kThreads, 2) dtw_wave_tan_kernel(SwArgs p) {
                 float fu = __shfl_up_sync(kAll, fl, 1);
                 float fd = __shfl_up_sync(kAll, wbuf[(q + 2) % kPT].w, 1);
                 const int su = min(t + 31, TP - 1), sd = min(t + 30, TP - 1);
-                const float fua = Wup[(size_t)su * 32].w, fda = Wup[(size_t)sd * 32].w;
-                float al = 0.f, au = 0.f, ad = 0.f, aua = 0.f, ada = 0.f;
+                // the row above's lane 31 at steps t + 31 / t + 30, loaded kPT steps ahead
+                const float fda = upf[q % kPT], fua = fuaC;
+                const float ada = upa[q % kPT], aua = auaC;
+                fuaC = fda;
+                auaC = ada;
+                {
+                    const size_t ss = (size_t)max(min(t - kPT + 30, TP - 1), 0) * 32;
+                    upf[q % kPT] = Wup[ss].w;
+                    if (XPT) upa[q % kPT] = Xup[ss].x;
+                }
+                float al = 0.f, au = 0.f, ad = 0.f;
                 if (MODE == MODE_PT) {
                     al = xbuf[(q + 1) % kPT].x;
                     au = __shfl_up_sync(kAll, al, 1);
                     ad = __shfl_up_sync(kAll, xbuf[(q + 2) % kPT].x, 1);
-                    aua = Xup[(size_t)su * 32].x;
-                    ada = Xup[(size_t)sd * 32].x;
                 }
                 {
                     const size_t pi = poff + (size_t)max(t - kPT, 0) * 32;

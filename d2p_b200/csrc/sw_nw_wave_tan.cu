@@ -134,6 +134,9 @@ __global__ void __launch_bounds__(kThreads, 2) nw_wave_tan_kernel(SwArgs p) {
         const bool rowok = i <= L1;
         const size_t poff = (size_t)rb * TP * 32 + lane;
         const float* vrow = HV ? Vin + (size_t)(rowok ? i - 1 : 0) * L2m : nullptr;
+        // V of this lane's column, two steps ahead (steps t and t + 1 in flight)
+        auto vload = [&](int jj) { return HV && rowok && jj >= 1 && jj <= L2 ? __ldg(vrow + (jj - 1)) : 0.f; };
+        float vcur = vload(1 - lane), vnext = vload(2 - lane);
         const int hiRow = min(31, L1 - 1 - 32 * rb);
         auto load_chunk = [&](int c) {
             const int col = c * kCW + (lane & 15);
@@ -200,7 +203,7 @@ __global__ void __launch_bounds__(kThreads, 2) nw_wave_tan_kernel(SwArgs p) {
                 float4 wq = make_float4(0.f, 0.f, 0.f, 0.f), xq = wq;
                 if (live) {
                     const float sc = ws.ring[lane * kRW + ((t - lane) & (kRW - 1))];
-                    const float vv = HV ? __ldg(vrow + (j - 1)) : 0.f;
+                    const float vv = vcur;
                     const float vd = dg + sc, vu = up + gap, vl = lf + gap;
                     const float m = fmaxf(vd, fmaxf(vu, vl));
                     const float ed = expf((vd - m) * iT), eu = expf((vu - m) * iT), el = expf((vl - m) * iT);
@@ -226,6 +229,8 @@ __global__ void __launch_bounds__(kThreads, 2) nw_wave_tan_kernel(SwArgs p) {
                     if (HV) xq.x = vv;
                     if (PT) xq = make_float4(o, ev - d, sc, 0.f);
                 }
+                vcur = vnext;
+                vnext = vload(j + 2);
                 const size_t pi = poff + (size_t)t * 32;
                 Wp[pi] = wq;
                 if (!PG) Xp[pi] = xq;
@@ -255,6 +260,7 @@ __global__ void __launch_bounds__(kThreads, 2) nw_wave_tan_kernel(SwArgs p) {
     __syncthreads();
 
     // ------------------------------------------------------------- reverse
+    constexpr bool XPT = PT;
     double sdot = 0.0;
     for (int n = warp; n < nRB; n += kW) {
         const int rb = nRB - 1 - n;
@@ -276,6 +282,15 @@ __global__ void __launch_bounds__(kThreads, 2) nw_wave_tan_kernel(SwArgs p) {
             wbuf[s] = Wp[pi];
             xbuf[s] = PG ? make_float4(0.f, 0.f, 0.f, 0.f) : Xp[pi];
         }
+        float upf[kPT], upa[kPT];   // the row above's lane-31 tangent (and alpha) at steps T0 + 30 - s
+#pragma unroll
+        for (int s = 0; s < kPT; ++s) {
+            const size_t ss = (size_t)min(T0 + 30 - s, TP - 1) * 32;
+            upf[s] = Wup[ss].w;
+            upa[s] = XPT ? Xup[ss].x : 0.f;
+        }
+        float fuaC = Wup[(size_t)min(T0 + 31, TP - 1) * 32].w;
+        float auaC = XPT ? Xup[(size_t)min(T0 + 31, TP - 1) * 32].x : 0.f;
         float Lf = 0.f, Lq = 0.f, Df = 0.f, Dq = 0.f, Xf = 0.f, Xq = 0.f;
         const bool below = rb + 1 < nRB;
         const int prodKey = (n - 1) << 16;
@@ -301,14 +316,21 @@ __global__ void __launch_bounds__(kThreads, 2) nw_wave_tan_kernel(SwArgs p) {
                 float fu = __shfl_up_sync(kAll, fl0, 1);
                 float fd = __shfl_up_sync(kAll, wbuf[(q + 2) % kPT].w, 1);
                 const int su = min(t + 31, TP - 1), sd = min(t + 30, TP - 1);
-                const float fua = Wup[(size_t)su * 32].w, fda = Wup[(size_t)sd * 32].w;
-                float al = 0.f, au = 0.f, ad = 0.f, aua = 0.f, ada = 0.f;
+                // the row above's lane 31 at steps t + 31 / t + 30, loaded kPT steps ahead
+                const float fda = upf[q % kPT], fua = fuaC;
+                const float ada = upa[q % kPT], aua = auaC;
+                fuaC = fda;
+                auaC = ada;
+                {
+                    const size_t ss = (size_t)max(min(t - kPT + 30, TP - 1), 0) * 32;
+                    upf[q % kPT] = Wup[ss].w;
+                    if (XPT) upa[q % kPT] = Xup[ss].x;
+                }
+                float al = 0.f, au = 0.f, ad = 0.f;
                 if (PT) {
                     al = xbuf[(q + 1) % kPT].x;
                     au = __shfl_up_sync(kAll, al, 1);
                     ad = __shfl_up_sync(kAll, xbuf[(q + 2) % kPT].x, 1);
-                    aua = Xup[(size_t)su * 32].x;
-                    ada = Xup[(size_t)sd * 32].x;
                 }
                 {
                     const size_t pi = poff + (size_t)max(t - kPT, 0) * 32;
