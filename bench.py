@@ -26,6 +26,10 @@ affine gaps) and soft DTW at config 2's shape (the same step through
 ``soft_nw`` / ``soft_nw_affine`` / ``soft_dtw``); their reference leg is the
 reference's own CPU kernels of that family (value + marginals, whose marginals
 are the gradient of value.sum()).
+``--config emb2`` runs soft SW of scores built from bf16 embeddings on the
+tensor cores (``soft_sw_embed``: the tcgen05 score producer, then the DP) with
+the gradient down to the embeddings; its line adds a ``producer`` object (the
+producer kernel alone against the measured HBM and bf16 peaks).
 The MUFU roofline denominator is measured in the same run (``d2p_mufu_probe``,
 an ex2.approx throughput kernel).
 ``--impl reference`` times the reference's own CPU operators (oracle/_ref, built
