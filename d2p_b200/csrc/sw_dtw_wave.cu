@@ -55,6 +55,7 @@
 namespace d2pb {
 namespace dtww {
 
+using ring::cp_async4_zfill;
 using ring::kAll;
 
 constexpr int kW = 8;                 // warps per CTA
@@ -90,11 +91,6 @@ __host__ __device__ inline size_t per_problem_bytes(int L1m, int L2m) {
     const size_t nr = (size_t)nrb_of(L1m) * row_elems(L2m);
     return ring::align_up(4 * plane_floats(L1m, L2m) * sizeof(float), 256) + ring::align_up(nr * sizeof(float2), 256) +
            ring::align_up(nr * sizeof(float), 256);
-}
-
-__device__ __forceinline__ void cp_async4_zfill(float* smem, const float* gmem, int src_bytes) {
-    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(s), "l"(gmem), "r"(src_bytes));
 }
 
 __global__ void __launch_bounds__(kThreads, 2) dtw_wave_kernel(SwArgs p) {

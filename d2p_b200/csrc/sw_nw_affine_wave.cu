@@ -56,6 +56,7 @@
 namespace d2pb {
 namespace nwaw {
 
+using ring::cp_async4_zfill;
 using ring::kAll;
 
 constexpr int kW = 8;                 // warps per CTA
@@ -89,11 +90,6 @@ __host__ __device__ inline size_t row_elems(int L2m) { return (size_t)L2m + kCW 
 __host__ __device__ inline size_t per_problem_bytes(int L1m, int L2m) {
     const size_t nr = (size_t)nrb_of(L1m) * row_elems(L2m);
     return ring::align_up(3 * slots_of(L1m, L2m) * sizeof(float4), 256) + 2 * ring::align_up(nr * sizeof(float4), 256);
-}
-
-__device__ __forceinline__ void cp_async4_zfill(float* smem, const float* gmem, int src_bytes) {
-    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(s), "l"(gmem), "r"(src_bytes));
 }
 
 // normalised weights of three options; returns the LSE (m + T ln sum), and

@@ -42,6 +42,7 @@
 namespace d2pb {
 namespace nwt {
 
+using ring::cp_async4_zfill;
 using ring::kAll;
 
 constexpr int kW = 8;
@@ -74,11 +75,6 @@ __host__ __device__ inline size_t per_problem_bytes(int L1m, int L2m) {
     const size_t sl = slots_of(L1m, L2m), nr = (size_t)nrb_of(L1m) * row_elems(L2m);
     return 2 * ring::align_up(sl * sizeof(float4), 256) + 2 * ring::align_up(nr * sizeof(float4), 256) +
            2 * ring::align_up((size_t)nrb_of(L1m) * steps_of(L2m) * 4, 256);
-}
-
-__device__ __forceinline__ void cp_async4_zfill(float* smem, const float* gmem, int src_bytes) {
-    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(s), "l"(gmem), "r"(src_bytes));
 }
 
 template <int MODE>

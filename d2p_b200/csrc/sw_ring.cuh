@@ -30,6 +30,11 @@ __device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
     const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(s), "l"(gmem));
 }
+// 4 bytes, or zeros when src_bytes is 0 (gmem must still be a valid address)
+__device__ __forceinline__ void cp_async4_zfill(float* smem, const float* gmem, int src_bytes) {
+    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(s), "l"(gmem), "r"(src_bytes));
+}
 // bring a 128-byte line into L2 ahead of a cp.async that will read it
 __device__ __forceinline__ void prefetch_l2(const void* gmem) {
     asm volatile("prefetch.global.L2 [%0];\n" ::"l"(gmem));
