@@ -576,7 +576,11 @@ def run_embed(args, cfg):
 
     import d2p_b200 as d2p
 
-    dev = torch.device("cuda", 0)
+    # one process per GPU when launched by torchrun: each rank times its own
+    # copy of the workload (no collective); rank 0 prints its line
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    rank = int(os.environ.get("RANK", "0"))
+    dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     B, L1, L2, D = cfg["B"], cfg["L1"], cfg["L2"], cfg["D"]
     g = torch.Generator().manual_seed(0)
@@ -594,7 +598,7 @@ def run_embed(args, cfg):
     for _ in range(args.warmup):
         step(x, y)
     torch.cuda.synchronize()
-    clocks = ClockSampler(0)
+    clocks = ClockSampler(local)
     clocks.start()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
@@ -707,7 +711,8 @@ def run_embed(args, cfg):
         "producer": producer,
         "clocks": clk,
     }
-    print(json.dumps(line), flush=True)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
 
 
 # ----------------------------------------------------------------------------
