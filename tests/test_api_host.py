@@ -298,3 +298,39 @@ def test_public_api_on_fake_tensors_uses_the_custom_ops():
         assert ra.marginals.shape == (2, 5, 6)
         gs, gg, gt = d2p.soft_sw_backward_full(s, s, -1.0, 1.0, None)
         assert gs.shape == (2, 5, 6) and gg.shape == (1,) and gt.shape == (1,)
+
+
+# ---------------------------------------------------------------- score producer
+def test_embed_scores_validation():
+    """embed_scores / soft_sw_embed check dtype, shapes and D before any launch."""
+    x = torch.zeros(2, 5, 16, dtype=torch.bfloat16)
+    with pytest.raises(TypeError, match="bfloat16"):
+        d2p.embed_scores(x.float(), x)
+    with pytest.raises(ValueError, match="same B and D"):
+        d2p.embed_scores(x, torch.zeros(3, 5, 16, dtype=torch.bfloat16))
+    with pytest.raises(ValueError, match="same B and D"):
+        d2p.embed_scores(x, torch.zeros(2, 5, 8, dtype=torch.bfloat16))
+    with pytest.raises(ValueError, match="exceeds 256"):
+        big = torch.zeros(1, 2, 320, dtype=torch.bfloat16)
+        d2p.embed_scores(big, big)
+    with pytest.raises(ValueError):
+        d2p.soft_sw_embed(x, x, temperature=0.0)
+    assert "embed_scores" in d2p.__all__ and "soft_sw_embed" in d2p.__all__
+
+
+def test_embed_scores_fake_shape():
+    """Under FakeTensorMode the producer op gives [B, L1, L2] fp32 (its register_fake)."""
+    from torch._subclasses.fake_tensor import FakeTensorMode
+
+    with FakeTensorMode() as mode:
+        x = mode.from_tensor(torch.empty(2, 5, 64, dtype=torch.bfloat16))
+        y = mode.from_tensor(torch.empty(2, 7, 64, dtype=torch.bfloat16))
+        s = torch.ops.d2p_b200.embed_scores(x, y, 1.0)
+    assert tuple(s.shape) == (2, 5, 7) and s.dtype == torch.float32
+
+
+def test_embed_scores_cpu_rejected():
+    """No CPU producer and no silent fallback."""
+    x = torch.zeros(1, 4, 64, dtype=torch.bfloat16)
+    with pytest.raises((RuntimeError, NotImplementedError)):
+        torch.ops.d2p_b200.embed_scores(x, x, 1.0)
